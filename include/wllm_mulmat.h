@@ -1,0 +1,196 @@
+/*
+ * wllm_mulmat — C ABI of the B200 quantized MUL_MAT library.
+ *
+ * Drop-in for one op of paulrobello/webllm: ggml MUL_MAT with a GGUF
+ * quantized src0 (Q4_K, Q6_K, Q8_0) and f32 src1/dst. The ABI mirrors the
+ * JSEP operator-plugin seam the ggml backend calls per graph node
+ * (src/inference/jsep/index.ts:1-21,129-305): seven callbacks
+ * alloc/free/write/read/clear/run_op/sync over integer buffer handles, and
+ * the same per-op descriptor words (src/inference/jsep/ops/matmul.ts:22-41).
+ *
+ * Conventions
+ *  - Status codes (src/inference/jsep/index.ts:31-33, jsep/README.md):
+ *      WLLM_STATUS_OK (0), WLLM_STATUS_NOT_IMPLEMENTED (1: op or type not
+ *      handled here, the caller falls back), WLLM_STATUS_FAILED (-1: bad
+ *      arguments, validation failure or CUDA error; wllm_last_error() has
+ *      the message). No C++ exception crosses this boundary.
+ *  - Every call is ordered on the library's single CUDA stream for the
+ *    bound device (one process or one host thread per GPU). The library
+ *    guards its state with a mutex; calls from several host threads are
+ *    serialised, not concurrent.
+ *  - Buffers are owned by the library (handles >= 1, never 0). Host
+ *    pointers passed in are owned by the caller and only used during the
+ *    call.
+ */
+#ifndef WLLM_MULMAT_H
+#define WLLM_MULMAT_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Exported with default visibility even when the library is built with
+ * -fvisibility=hidden. */
+#if defined(__GNUC__)
+#pragma GCC visibility push(default)
+#endif
+
+#define WLLM_STATUS_OK 0
+#define WLLM_STATUS_NOT_IMPLEMENTED 1
+#define WLLM_STATUS_FAILED (-1)
+
+/* ggml_op / ggml_type ids (jsep/index.ts:45, ggml-wasm.ts:8-25). */
+#define WLLM_GGML_OP_MUL_MAT 29
+#define WLLM_TYPE_F32 0
+#define WLLM_TYPE_F16 1
+#define WLLM_TYPE_Q4_0 2
+#define WLLM_TYPE_Q8_0 8
+#define WLLM_TYPE_Q4_K 12
+#define WLLM_TYPE_Q6_K 14
+
+/* Descriptor geometry (matmul.ts:22-41): [op, n_src, dst block, src blocks...],
+ * each block = buf_handle, offset, type, ne[4] lo, ne[4] hi, nb[4] lo, nb[4] hi.
+ * The hi halves carry the upper 32 bits of ne/nb (large vocab projections
+ * exceed 2^31 bytes). `offset` is one unsigned 32-bit word. */
+#define WLLM_TENSOR_BLOCK_I32 19
+#define WLLM_DESC_HEADER_I32 2
+
+/* Per-callback invocation counters (jsep/index.ts:92-105, JsepCounters)
+ * plus the library's device-memory accounting. */
+typedef struct wllm_counters {
+    uint64_t alloc, free, write, read, clear, run_op, sync;
+    uint64_t kernels_launched;   /* kernels this library launched */
+    uint64_t bytes_live;         /* bytes held by live handles */
+    uint64_t bytes_reserved;     /* bytes held from cudaMalloc incl. free lists */
+} wllm_counters;
+
+/* Bind the library to a CUDA device and create its stream. Replaces
+ * installJsepCallbacks(module, device) (jsep/index.ts:129). Calling it again
+ * for the same device is a no-op; for another device it fails. */
+int32_t wllm_init(int32_t device);
+
+/* Release every buffer, the stream and cached scratch. Replaces
+ * destroyJsepCallbacks (jsep/index.ts:400-413). */
+int32_t wllm_shutdown(void);
+
+/* jsepAlloc(size) -> handle >= 1 (jsep/index.ts:163-166,
+ * GpuDataManager.alloc gpu-data-manager.ts:65-103). Memory comes from
+ * cudaMalloc through a size-class free list; size must be > 0. */
+int32_t wllm_alloc(uint64_t size, int32_t* out_handle);
+
+/* jsepFree(handle): idempotent, unknown handles are a no-op
+ * (gpu-data-manager.ts:105-116). */
+int32_t wllm_free(int32_t handle);
+
+/* jsepWrite(h, off, ptr, size) (jsep/index.ts:173-228,
+ * GpuDataManager.write gpu-data-manager.ts:128-142): stream-ordered after
+ * every earlier call; the host buffer may be reused when the call returns. */
+int32_t wllm_write(int32_t handle, uint64_t offset, const void* host_src, uint64_t size);
+
+/* jsepRead(h, off, ptr, size) (jsep/index.ts:230-254, readAsync
+ * gpu-data-manager.ts:144-170): waits for every earlier call, then copies. */
+int32_t wllm_read(int32_t handle, uint64_t offset, void* host_dst, uint64_t size);
+
+/* Non-blocking readback, begin/poll/finish/cancel
+ * (webgpu-bridge.cpp:353-370, backend_tensor_get_async_*). poll returns
+ * 1 when ready, 0 while pending, -1 on error. */
+int32_t wllm_read_async_begin(int32_t handle, uint64_t offset, uint64_t size, int32_t* out_request);
+int32_t wllm_read_async_poll(int32_t request);
+int32_t wllm_read_async_finish(int32_t request, void* host_dst, uint64_t size);
+int32_t wllm_read_async_cancel(int32_t request);
+
+/* jsepClear(h, value, off, size) (jsep/index.ts:256-268): byte fill. */
+int32_t wllm_clear(int32_t handle, int32_t value, uint64_t offset, uint64_t size);
+
+/* jsepRunOp(descriptorPtr, descriptorWords, opParamsPtr, opParamsLen)
+ * (jsep/index.ts:270-300) -> dispatchMatmul (matmul.ts:555-1000).
+ * Enqueues the op and returns. op != MUL_MAT, or src0 of a type this
+ * library does not compute, returns WLLM_STATUS_NOT_IMPLEMENTED; shape,
+ * stride, range or handle violations return WLLM_STATUS_FAILED. dst may
+ * share a buffer with a source; overlapping byte ranges are computed into
+ * library scratch and copied back (matmul.ts:675-958 divert path). */
+int32_t wllm_run_op(const int32_t* desc, int32_t desc_words,
+                    const void* op_params, int32_t op_params_len);
+
+/* Several independent MUL_MAT descriptors in one kernel launch (for example
+ * the q/k/v projections of a layer, which read the same src1). No
+ * descriptor's dst may overlap another's sources. Extension of the
+ * jsepRunOp seam: ggml's graph_compute sees such sibling nodes together. */
+int32_t wllm_run_ops(const int32_t* const* descs, const int32_t* desc_words, int32_t n_ops);
+
+/* jsepSync() (jsep/index.ts:302-305): waits for all enqueued work and
+ * reports any asynchronous CUDA error. */
+int32_t wllm_sync(void);
+
+/* Copy the last error message (NUL-terminated, truncated to len). Returns
+ * the full message length. */
+int32_t wllm_last_error(char* buf, int32_t len);
+
+/* Counter snapshot (JsepCounters, jsep/index.ts:92-105). */
+int32_t wllm_get_counters(wllm_counters* out);
+
+/* Device address and capacity of a buffer handle, for hosts that drive the
+ * device-pointer entry points below on library-owned memory. */
+int32_t wllm_buffer_device_ptr(int32_t handle, void** out_ptr, uint64_t* out_size);
+
+/* Device-pointer MUL_MAT on a caller-chosen stream (NULL = the library
+ * stream): y[m + y_stride*n] = sum_k W[m,k] * x[k + x_stride*n] with W
+ * given as M rows of w_row_bytes raw GGUF blocks. Same math as
+ * wllm_run_op; used by the row-sharded multi-GPU path, where each rank
+ * passes its own row slice. The pointers must be device memory of the
+ * bound device; the library checks alignment, not extents. */
+int32_t wllm_mul_mat(int32_t src0_type, const void* w, int64_t w_row_bytes,
+                     const float* x, int64_t x_stride,
+                     float* y, int64_t y_stride,
+                     int32_t M, int32_t K, int32_t N, void* stream);
+
+/* One device-pointer MUL_MAT for wllm_mul_mat_batch. */
+typedef struct wllm_mulmat_args {
+    int32_t src0_type;
+    int32_t M, K, N;
+    const void* w;
+    int64_t w_row_bytes;
+    const float* x;
+    int64_t x_stride;  /* floats between activation vectors */
+    float* y;
+    int64_t y_stride;  /* floats between output vectors */
+} wllm_mulmat_args;
+
+/* Up to 16 independent device-pointer MUL_MATs in one kernel launch on
+ * `stream` (NULL = the library stream). */
+int32_t wllm_mul_mat_batch(const wllm_mulmat_args* ops, int32_t n_ops, void* stream);
+
+/* The library's CUDA stream (a cudaStream_t), so a host can order its own
+ * work (collectives, events) with the library's. */
+int32_t wllm_get_stream(void** out_stream);
+
+/* Record the run_op/run_ops calls made between begin and end into a CUDA
+ * graph instead of executing them, then replay the whole sequence with one
+ * launch per token (the graph_compute of a fixed decode graph,
+ * webgpu-bridge.cpp:317-320). Buffer writes, reads, clears and syncs are
+ * rejected while recording. Replays read the buffers' current contents. */
+int32_t wllm_graph_begin(void);
+int32_t wllm_graph_end(int32_t* out_graph);
+int32_t wllm_graph_launch(int32_t graph);
+int32_t wllm_graph_destroy(int32_t graph);
+
+/* Device dequantization of n elements (n a multiple of the block size) of
+ * raw GGUF blocks to f32. Replaces the libllama oracle shim
+ * webllm_dequantize_q4_K (webgpu-bridge.cpp:692-708) on the device, for
+ * Q4_K, Q6_K and Q8_0. Returns -1 on bad arguments. */
+int32_t wllm_dequantize(int32_t type, const void* src, float* dst, int64_t n, void* stream);
+
+/* Library build/version string. */
+const char* wllm_version(void);
+
+#if defined(__GNUC__)
+#pragma GCC visibility pop
+#endif
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,263 @@
+"""GPU parity tests: the CUDA MUL_MAT through the C ABI against the oracle.
+
+Bar (from the path's contract): dequantization bit-exact; GEMV max relative
+error <= 1e-3, rel = max|y - r| / max|r| with r the oracle's f64-accumulated
+dequant-then-dot. Cases follow the reference's golden tests
+(tests/jsep-matmul-golden.test.ts, smoke-test/p2-v2-spike.src.ts) and add
+odd shapes, batches, broadcast, aliasing and error paths.
+"""
+from __future__ import annotations
+
+import zlib
+
+import numpy as np
+import pytest
+
+from oracle import oracle as O
+from webllm_b200 import jsep, synth
+
+pytestmark = pytest.mark.gpu
+
+GEMV_TOL = 1e-3
+
+
+def upload(rt, arr) -> int:
+    a = np.ascontiguousarray(arr)
+    h = rt.data_manager.alloc(a.nbytes)
+    rt.data_manager.write(h, 0, a)
+    return h
+
+
+def run_mul_mat(rt, qtype, w, x, *, check_status=True):
+    """dst = MUL_MAT(w, x) through jsepRunOp-style descriptors; returns (N, M)."""
+    M = w.shape[0]
+    N, K = x.shape
+    h0, h1 = upload(rt, w), upload(rt, x)
+    hd = rt.data_manager.alloc(4 * M * N)
+    desc = jsep.JsepOpDescriptor(jsep.GGML_OP_MUL_MAT, 2, jsep.meta_for(hd, jsep.GGML_TYPE_F32, (M, N, 1, 1)),
+                                 [jsep.meta_for(h0, qtype, (K, M, 1, 1)), jsep.meta_for(h1, jsep.GGML_TYPE_F32, (K, N, 1, 1))])
+    st = jsep.dispatch_matmul(rt, desc)
+    if check_status:
+        assert st == jsep.STATUS_OK, jsep.last_error()
+    rt.encoder_batcher.flush()
+    out = rt.data_manager.read(hd, 0, 4 * M * N).view(np.float32).reshape(N, M)
+    for h in (h0, h1, hd):
+        rt.data_manager.free(h)
+    return out
+
+
+def test_q4k_kat(runtime, golden):
+    """tests/jsep-matmul-golden.test.ts:521-600 (single Q4_K super-block)."""
+    z = golden("q4k_kat.npz")
+    got = run_mul_mat(runtime, jsep.GGML_TYPE_Q4_K, z["block"].reshape(1, 144), z["src1"].reshape(1, 256))
+    assert abs(float(got[0, 0]) - float(z["dst"][0, 0])) < float(z["tol"])
+    r = O.mul_mat_f64(O.TYPE_Q4_K, z["block"].reshape(1, 144), z["src1"].reshape(1, 256))
+    assert O.rel_error(got, r) <= GEMV_TOL
+
+
+def test_q4k_synth_64x2048(runtime, golden):
+    """buildSyntheticQ4KMatrix M=64 K=2048 N=6 (p2-v2-spike.src.ts:287-360)."""
+    z = golden("q4k_synth_64x2048.npz")
+    got = run_mul_mat(runtime, jsep.GGML_TYPE_Q4_K, z["weights"], z["src1"])
+    assert O.rel_error(got, z["dst_f64"]) <= GEMV_TOL
+    assert np.all(np.isfinite(got))
+
+
+@pytest.mark.parametrize("qtype,name", [(jsep.GGML_TYPE_Q4_K, "q4_k"), (jsep.GGML_TYPE_Q6_K, "q6_k"),
+                                        (jsep.GGML_TYPE_Q8_0, "q8_0")])
+def test_device_dequant_bit_exact(runtime, golden, qtype, name):
+    z = golden("gguf_blocks.npz")
+    raw = z[f"{name}_raw"]
+    be, _ = jsep.BLOCK_GEOMETRY[qtype]
+    n = raw.shape[0] * be
+    hs = upload(runtime, raw)
+    hd = runtime.data_manager.alloc(4 * n)
+    ps, _ = runtime.data_manager.get(hs)
+    pd, _ = runtime.data_manager.get(hd)
+    jsep.dequantize_device(qtype, ps, pd, n)
+    runtime.encoder_batcher.flush()
+    got = runtime.data_manager.read(hd, 0, 4 * n).view(np.float32)
+    assert np.array_equal(got.view(np.uint32), z[f"{name}_dequant"].view(np.uint32))
+    # and against the oracle on synthetic blocks of the bench distribution
+    rng = np.random.default_rng(qtype)
+    w = synth.weights(rng, qtype, 16, 1024)
+    hs2 = upload(runtime, w)
+    hd2 = runtime.data_manager.alloc(4 * 16 * 1024)
+    jsep.dequantize_device(qtype, runtime.data_manager.get(hs2)[0], runtime.data_manager.get(hd2)[0], 16 * 1024)
+    got2 = runtime.data_manager.read(hd2, 0, 4 * 16 * 1024).view(np.float32).reshape(16, 1024)
+    ref2 = O.dequantize_matrix(qtype, w, 1024)
+    assert np.array_equal(got2.view(np.uint32), ref2.view(np.uint32))
+    for h in (hs, hd, hs2, hd2):
+        runtime.data_manager.free(h)
+
+
+SHAPES = [(1, 256, 1), (7, 512, 1), (33, 768, 2), (257, 1024, 3), (64, 2048, 5), (96, 3072, 8), (40, 2304, 13)]
+
+
+@pytest.mark.parametrize("qtype", [jsep.GGML_TYPE_Q4_K, jsep.GGML_TYPE_Q6_K, jsep.GGML_TYPE_Q8_0])
+@pytest.mark.parametrize("M,K,N", SHAPES)
+def test_gemv_random_shapes(runtime, qtype, M, K, N):
+    be, _ = jsep.BLOCK_GEOMETRY[qtype]
+    if K % be:
+        pytest.skip("K not a multiple of the block")
+    rng = np.random.default_rng(M * 7919 + K * 31 + N + qtype)
+    w = synth.weights(rng, qtype, M, K)
+    x = synth.activations(rng, N, K)
+    got = run_mul_mat(runtime, qtype, w, x)
+    r = O.mul_mat_f64(qtype, w, x)
+    assert O.rel_error(got, r) <= GEMV_TOL
+
+
+@pytest.mark.parametrize("name,qtype,M,K", synth.LLAMA32_3B_LAYER)
+def test_llama32_3b_layer_shapes(runtime, name, qtype, M, K):
+    rng = np.random.default_rng(zlib.crc32(name.encode()))
+    w = synth.weights(rng, qtype, M, K)
+    x = synth.activations(rng, 1, K)
+    got = run_mul_mat(runtime, qtype, w, x)
+    assert O.rel_error(got, O.mul_mat_f64(qtype, w, x)) <= GEMV_TOL
+
+
+def test_single_gemv_4096(runtime):
+    """The 4096x4096 Q4_K single-GEMV workload, batch 1."""
+    rng = np.random.default_rng(1)
+    w = synth.q4_k_blocks(rng, 4096, 4096)
+    x = synth.activations(rng, 1, 4096)
+    got = run_mul_mat(runtime, jsep.GGML_TYPE_Q4_K, w, x)
+    assert O.rel_error(got, O.mul_mat_f64(O.TYPE_Q4_K, w, x)) <= GEMV_TOL
+
+
+def test_scaling_by_two_is_exact_and_deterministic(runtime):
+    """Size-independent properties at a full layer size: doubling x doubles y
+    bit-exactly (power-of-two scaling commutes with every rounding), and two
+    runs are bit-identical."""
+    rng = np.random.default_rng(5)
+    w = synth.q4_k_blocks(rng, 8192, 3072)
+    x = synth.activations(rng, 1, 3072)
+    a = run_mul_mat(runtime, jsep.GGML_TYPE_Q4_K, w, x)
+    b = run_mul_mat(runtime, jsep.GGML_TYPE_Q4_K, w, x)
+    c = run_mul_mat(runtime, jsep.GGML_TYPE_Q4_K, w, 2 * x)
+    assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
+    assert np.array_equal((2 * a).view(np.uint32), c.view(np.uint32))
+
+
+def test_batched_broadcast_and_strides(runtime):
+    """ne2 = 4 activation batches sharing 2 weight batches (r2 = 2, the GQA
+    broadcast of matmul.ts:594-611) with padded src1/dst row strides."""
+    rng = np.random.default_rng(11)
+    qtype, M, K, N, B0, B1 = jsep.GGML_TYPE_Q4_K, 48, 512, 3, 2, 4
+    w = synth.weights(rng, qtype, M * B0, K).reshape(B0, M, -1)
+    xpad, ypad = K + 8, M + 4
+    x = np.zeros((B1, N, xpad), np.float32)
+    x[:, :, :K] = rng.standard_normal((B1, N, K), dtype=np.float32)
+    h0, h1 = upload(runtime, w), upload(runtime, x)
+    hd = runtime.data_manager.alloc(4 * B1 * N * ypad)
+    runtime.data_manager.clear(hd, 0, 0, 4 * B1 * N * ypad)
+    rb = synth.row_bytes(qtype, K)
+    src0 = jsep.JsepTensorMeta(h0, 0, qtype, (K, M, B0, 1), (144, rb, rb * M, rb * M * B0))
+    src1 = jsep.JsepTensorMeta(h1, 0, 0, (K, N, B1, 1), (4, 4 * xpad, 4 * xpad * N, 4 * xpad * N * B1))
+    dst = jsep.JsepTensorMeta(hd, 0, 0, (M, N, B1, 1), (4, 4 * ypad, 4 * ypad * N, 4 * ypad * N * B1))
+    assert jsep.dispatch_matmul(runtime, jsep.JsepOpDescriptor(29, 2, dst, [src0, src1])) == 0, jsep.last_error()
+    got = runtime.data_manager.read(hd, 0, 4 * B1 * N * ypad).view(np.float32).reshape(B1, N, ypad)
+    for b in range(B1):
+        r = O.mul_mat_f64(qtype, w[b // 2], x[b, :, :K])
+        assert O.rel_error(got[b, :, :M], r) <= GEMV_TOL
+        assert np.all(got[b, :, M:] == 0)
+
+
+def test_dst_aliases_src1_buffer(runtime):
+    """dst and src1 in one buffer: disjoint ranges run in place, overlapping
+    ranges take the divert path (matmul.ts:675-958)."""
+    rng = np.random.default_rng(12)
+    qtype, M, K, N = jsep.GGML_TYPE_Q6_K, 256, 256, 2
+    w = synth.weights(rng, qtype, M, K)
+    x = synth.activations(rng, N, K)
+    r = O.mul_mat_f64(qtype, w, x)
+    h0 = upload(runtime, w)
+    for dst_off in (4 * N * K, 0):  # disjoint, then overlapping (dst over src1)
+        hb = runtime.data_manager.alloc(4 * N * K + 4 * M * N)
+        runtime.data_manager.write(hb, 0, x)
+        desc = jsep.JsepOpDescriptor(29, 2, jsep.meta_for(hb, 0, (M, N, 1, 1), offset=dst_off),
+                                     [jsep.meta_for(h0, qtype, (K, M, 1, 1)), jsep.meta_for(hb, 0, (K, N, 1, 1))])
+        assert jsep.dispatch_matmul(runtime, desc) == 0, jsep.last_error()
+        got = runtime.data_manager.read(hb, dst_off, 4 * M * N).view(np.float32).reshape(N, M)
+        assert O.rel_error(got, r) <= GEMV_TOL, dst_off
+        runtime.data_manager.free(hb)
+    runtime.data_manager.free(h0)
+
+
+def test_run_ops_grouped_qkv(runtime):
+    """q/k/v of one layer (two Q4_K, one Q6_K) in a single launch."""
+    rng = np.random.default_rng(13)
+    x = synth.activations(rng, 1, 3072)
+    hx = upload(runtime, x)
+    specs = [(jsep.GGML_TYPE_Q4_K, 3072), (jsep.GGML_TYPE_Q4_K, 1024), (jsep.GGML_TYPE_Q6_K, 1024)]
+    ws, hs, descs = [], [], []
+    for qtype, M in specs:
+        w = synth.weights(rng, qtype, M, 3072)
+        h0, hd = upload(runtime, w), runtime.data_manager.alloc(4 * M)
+        ws.append(w)
+        hs.append((h0, hd))
+        descs.append(jsep.JsepOpDescriptor(29, 2, jsep.meta_for(hd, 0, (M, 1, 1, 1)),
+                                           [jsep.meta_for(h0, qtype, (3072, M, 1, 1)), jsep.meta_for(hx, 0, (3072, 1, 1, 1))]))
+    k0 = runtime.counters()["kernels_launched"]
+    assert runtime.run_ops(descs) == 0, jsep.last_error()
+    assert runtime.counters()["kernels_launched"] == k0 + 1
+    for (qtype, M), w, (h0, hd) in zip(specs, ws, hs):
+        got = runtime.data_manager.read(hd, 0, 4 * M).view(np.float32).reshape(1, M)
+        assert O.rel_error(got, O.mul_mat_f64(qtype, w, x)) <= GEMV_TOL
+
+
+def test_status_codes(runtime):
+    """NOT_IMPLEMENTED for other ops/types (caller falls back), FAILED with a
+    message for shape, stride, range and handle violations."""
+    dm = runtime.data_manager
+    h0, h1, hd = dm.alloc(144 * 4), dm.alloc(4 * 256), dm.alloc(16)
+    good_src0 = jsep.meta_for(h0, jsep.GGML_TYPE_Q4_K, (256, 4, 1, 1))
+    src1 = jsep.meta_for(h1, 0, (256, 1, 1, 1))
+    dst = jsep.meta_for(hd, 0, (4, 1, 1, 1))
+
+    def st(desc):
+        return jsep.dispatch_matmul(runtime, desc)
+
+    assert st(jsep.JsepOpDescriptor(jsep.GGML_OP_RMS_NORM, 1, dst, [src1])) == jsep.STATUS_NOT_IMPLEMENTED
+    f16 = jsep.meta_for(h0, jsep.GGML_TYPE_F16, (256, 1, 1, 1))
+    assert st(jsep.JsepOpDescriptor(29, 2, dst, [f16, src1])) == jsep.STATUS_NOT_IMPLEMENTED
+    assert st(jsep.JsepOpDescriptor(29, 2, dst, [good_src0, src1])) == jsep.STATUS_OK
+    bad_shape = jsep.meta_for(hd, 0, (3, 1, 1, 1))
+    assert st(jsep.JsepOpDescriptor(29, 2, bad_shape, [good_src0, src1])) == jsep.STATUS_FAILED
+    assert "shape mismatch" in jsep.last_error()
+    too_long = jsep.meta_for(h0, jsep.GGML_TYPE_Q4_K, (256, 5, 1, 1))  # 5 rows in a 4-row buffer
+    assert st(jsep.JsepOpDescriptor(29, 2, jsep.meta_for(hd, 0, (5, 1, 1, 1)), [too_long, src1])) == jsep.STATUS_FAILED
+    assert "past" in jsep.last_error()
+    dead = jsep.meta_for(9999, jsep.GGML_TYPE_Q4_K, (256, 4, 1, 1))
+    assert st(jsep.JsepOpDescriptor(29, 2, dst, [dead, src1])) == jsep.STATUS_FAILED
+    assert "invalid handle" in jsep.last_error()
+    bad_src1 = jsep.meta_for(h1, jsep.GGML_TYPE_F16, (256, 1, 1, 1))
+    assert st(jsep.JsepOpDescriptor(29, 2, dst, [good_src0, bad_src1])) == jsep.STATUS_FAILED
+    one_src = jsep.JsepOpDescriptor(29, 1, dst, [good_src0])
+    assert st(one_src) == jsep.STATUS_FAILED
+    assert "expected 2 srcs" in jsep.last_error()
+    for h in (h0, h1, hd):
+        dm.free(h)
+    dm.free(h0)  # idempotent
+    rt_sync = runtime.lib.wllm_sync()
+    assert rt_sync == jsep.STATUS_OK
+
+
+def test_buffers_roundtrip_clear_and_async_read(runtime):
+    dm = runtime.data_manager
+    h = dm.alloc(1 << 20)
+    data = np.arange(1 << 18, dtype=np.uint32)
+    dm.write(h, 0, data)
+    assert np.array_equal(dm.read(h, 0, 1 << 20).view(np.uint32), data)
+    dm.clear(h, 0xAB, 4096, 100)
+    back = dm.read(h, 4096, 100)
+    assert np.all(back == 0xAB)
+    req = dm.read_async(h, 0, 4096)
+    for _ in range(100000):
+        if req.poll():
+            break
+    assert np.array_equal(req.finish().view(np.uint32), data[:1024])
+    c = runtime.counters()
+    assert c["alloc"] >= 1 and c["write"] >= 1 and c["read"] >= 2
+    dm.free(h)

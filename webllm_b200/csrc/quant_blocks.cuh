@@ -1,0 +1,87 @@
+// Device-side decoding of GGUF quant blocks (Q4_K, Q6_K, Q8_0).
+//
+// Block layouts (bytes):
+//   Q4_K (256 elements, 144 B): f16 d @0, f16 dmin @2, scales[12] @4,
+//        qs[128] @16. Pair p (0..3) owns qs[32p..32p+31]; the low nibble of
+//        qs[32p+l] is element 64p+l (sub-block 2p), the high nibble element
+//        64p+32+l (sub-block 2p+1). y = d*sc*q - dmin*m with (sc, m) the
+//        6-bit pair unpacked as in src/inference/jsep/ops/matmul.ts:408-424.
+//   Q6_K (256 elements, 210 B): ql[128] @0, qh[64] @128, int8 scales[16]
+//        @192, f16 d @208. y = d*scales[e/16]*(q6 - 32).
+//   Q8_0 (32 elements, 34 B): f16 d @0, int8 qs[32] @2. y = d*q.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+namespace wllm {
+
+__device__ __forceinline__ float f16_bits_to_f32(uint32_t bits16) {
+    return __half2float(__ushort_as_half(static_cast<unsigned short>(bits16 & 0xffffu)));
+}
+
+__device__ __forceinline__ uint32_t ldg_u32(const uint8_t* p) {
+    return __ldg(reinterpret_cast<const unsigned int*>(p));
+}
+__device__ __forceinline__ uint32_t ldg_u16(const uint8_t* p) {
+    return __ldg(reinterpret_cast<const unsigned short*>(p));
+}
+
+// Byte i (0..11) of the Q4_K scales, held as three little-endian words.
+__device__ __forceinline__ uint32_t q4k_sbyte(const uint32_t s[3], int i) {
+    return (s[i >> 2] >> (8 * (i & 3))) & 0xffu;
+}
+
+// (sc, m) of sub-block j (0..7): get_scale_min_k4 semantics
+// (matmul.ts:408-424, p2-v2-spike.src.ts:1037-1055).
+__device__ __forceinline__ void q4k_scale_min(const uint32_t s[3], int j, int& sc, int& m) {
+    if (j < 4) {
+        sc = static_cast<int>(q4k_sbyte(s, j) & 63u);
+        m = static_cast<int>(q4k_sbyte(s, j + 4) & 63u);
+    } else {
+        sc = static_cast<int>((q4k_sbyte(s, j + 4) & 0xFu) | ((q4k_sbyte(s, j - 4) >> 6) << 4));
+        m = static_cast<int>((q4k_sbyte(s, j + 4) >> 4) | ((q4k_sbyte(s, j) >> 6) << 4));
+    }
+}
+
+// Exact dequantization of element e (0..255) of a Q4_K block.
+__device__ __forceinline__ float q4k_dequant_elem(const uint8_t* blk, int e) {
+    const uint32_t dm = ldg_u16(blk) | (ldg_u16(blk + 2) << 16);
+    const float d = f16_bits_to_f32(dm), dmin = f16_bits_to_f32(dm >> 16);
+    uint32_t s[3];
+    s[0] = ldg_u16(blk + 4) | (ldg_u16(blk + 6) << 16);
+    s[1] = ldg_u16(blk + 8) | (ldg_u16(blk + 10) << 16);
+    s[2] = ldg_u16(blk + 12) | (ldg_u16(blk + 14) << 16);
+    const int p = e >> 6, within = e & 63, l = within & 31;
+    const int j = 2 * p + (within >= 32 ? 1 : 0);
+    int sc, m;
+    q4k_scale_min(s, j, sc, m);
+    const uint32_t byte = blk[16 + 32 * p + l];
+    const uint32_t q = within < 32 ? (byte & 0xFu) : (byte >> 4);
+    // d*sc, dmin*m and (d*sc)*q are exact in f32 (<= 24 significant bits);
+    // the subtraction is the single rounding, as in the oracle.
+    return __fsub_rn(__fmul_rn(__fmul_rn(d, static_cast<float>(sc)), static_cast<float>(q)),
+                     __fmul_rn(dmin, static_cast<float>(m)));
+}
+
+// Exact dequantization of element e (0..255) of a Q6_K block.
+__device__ __forceinline__ float q6k_dequant_elem(const uint8_t* blk, int e) {
+    const int h = e >> 7, r = e & 127, quarter = r >> 5, l = r & 31;
+    const uint32_t ql = blk[64 * h + (quarter & 1) * 32 + l];
+    const uint32_t qh = blk[128 + 32 * h + l];
+    const uint32_t lo = (quarter < 2) ? (ql & 0xFu) : (ql >> 4);
+    const uint32_t hi = (qh >> (2 * quarter)) & 3u;
+    const int q = static_cast<int>(lo | (hi << 4)) - 32;
+    const int sc = static_cast<int8_t>(blk[192 + (e >> 4)]);
+    const float d = f16_bits_to_f32(ldg_u16(blk + 208));
+    return __fmul_rn(__fmul_rn(d, static_cast<float>(sc)), static_cast<float>(q));
+}
+
+// Exact dequantization of element e (0..31) of a Q8_0 block.
+__device__ __forceinline__ float q8_0_dequant_elem(const uint8_t* blk, int e) {
+    const float d = f16_bits_to_f32(ldg_u16(blk));
+    const int q = static_cast<int8_t>(blk[2 + e]);
+    return __fmul_rn(d, static_cast<float>(q));
+}
+
+}  // namespace wllm

@@ -1,0 +1,63 @@
+// Internal interface between the C-ABI runtime (runtime.cpp) and the CUDA
+// kernels (*.cu). Not part of the public ABI.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace wllm {
+
+// GGUF block geometry (src/models/gguf-parser.ts:273-294).
+constexpr int kTypeF32 = 0;
+constexpr int kTypeQ8_0 = 8;
+constexpr int kTypeQ4_K = 12;
+constexpr int kTypeQ6_K = 14;
+
+inline int block_elems(int type) {
+    switch (type) {
+        case kTypeQ8_0: return 32;
+        case kTypeQ4_K: return 256;
+        case kTypeQ6_K: return 256;
+        case kTypeF32: return 1;
+        default: return 0;
+    }
+}
+inline int block_bytes(int type) {
+    switch (type) {
+        case kTypeQ8_0: return 34;
+        case kTypeQ4_K: return 144;
+        case kTypeQ6_K: return 210;
+        case kTypeF32: return 4;
+        default: return 0;
+    }
+}
+
+// One MUL_MAT node in device terms. Rows of W are raw GGUF blocks.
+// y[m, n, b2, b3] = sum_k W[m, k, b2/r2, b3/r3] * x[k, n, b2, b3].
+struct MulMatOp {
+    const uint8_t* w;
+    const float* x;
+    float* y;
+    int64_t w_nb1, w_nb2, w_nb3;  // bytes
+    int64_t x_nb1, x_nb2, x_nb3;  // bytes
+    int64_t y_nb1, y_nb2, y_nb3;  // bytes
+    int32_t type, M, K, N;
+    int32_t ne2, ne3;             // batch dims of x / y
+    int32_t r2, r3;               // broadcast factors x.ne2/w.ne2, x.ne3/w.ne3
+};
+
+constexpr int kMaxOpsPerLaunch = 16;
+
+// Checks alignment/shape preconditions the kernels rely on. Returns an
+// empty string when the op can be launched, else the reason.
+const char* check_mulmat_op(const MulMatOp& op);
+
+// Enqueue n_ops independent MUL_MAT ops (1 <= n_ops <= kMaxOpsPerLaunch)
+// on `stream`. Returns the number of kernels launched (>= 1) or a negative
+// cudaError_t on launch failure.
+int launch_mulmat(const MulMatOp* ops, int n_ops, cudaStream_t stream);
+
+// Device dequantization of n elements to f32 (bit-exact with the oracle).
+int launch_dequantize(int type, const void* src, float* dst, int64_t n, cudaStream_t stream);
+
+}  // namespace wllm
