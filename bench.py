@@ -138,29 +138,39 @@ class ClockSampler:
 # ------------------------------------------------------------------ CPU arms
 
 
-def cpu_sample(layers_budget_s: float, threads: int | None = None):
-    """Time the oracle's f32 dequant-then-dot on whole layers of the sweep
-    until about `layers_budget_s` seconds have passed. Returns (GB/s, cores,
-    sample description)."""
-    from oracle import oracle as O
+CPU_DISTINCT_LAYERS = 8  # 513 MB of weights: larger than any host's last-level cache
+
+
+def cpu_layers(n: int):
+    """n distinct synthetic layers of the sweep: [[(type, w, x, bytes) x7] x n]."""
     from webllm_b200 import synth
 
     rng = np.random.default_rng(1234)
-    mats = []
-    for name, t, M, K in synth.LLAMA32_3B_LAYER:
-        mats.append((t, synth.weights(rng, t, M, K), synth.activations(rng, 1, K), synth.algorithmic_bytes(t, M, K, 1)))
+    return [[(t, synth.weights(rng, t, M, K), synth.activations(rng, 1, K), synth.algorithmic_bytes(t, M, K, 1))
+             for _, t, M, K in synth.LLAMA32_3B_LAYER] for _ in range(n)]
+
+
+def cpu_sample(layers_budget_s: float, threads: int | None = None):
+    """Time the oracle's f32 dequant-then-dot on whole layers of the sweep,
+    cycling through 8 distinct layers so the weights stream from DRAM, until
+    about `layers_budget_s` seconds have passed. Returns (GB/s, cores,
+    sample description)."""
+    from oracle import oracle as O
+
+    layers = cpu_layers(CPU_DISTINCT_LAYERS)
     cores = O.max_threads() if threads is None else threads
-    O.mul_mat_f32(mats[0][0], mats[0][1][:8], mats[0][2], threads=cores)  # warm up threads
+    O.mul_mat_f32(layers[0][0][0], layers[0][0][1][:8], layers[0][0][2], threads=cores)  # start the thread pool
     done_bytes, t0, n_layers = 0, time.perf_counter(), 0
     while True:
-        for t, w, x, b in mats:
+        for t, w, x, b in layers[n_layers % len(layers)]:
             O.mul_mat_f32(t, w, x, threads=cores)
             done_bytes += b
         n_layers += 1
         el = time.perf_counter() - t0
         if el >= layers_budget_s:
             break
-    return done_bytes / el / 1e9, cores, f"{n_layers} layer(s) of the sweep (7 GEMVs each, {done_bytes/1e6:.0f} MB) in {el:.1f} s"
+    return done_bytes / el / 1e9, cores, (f"{n_layers} layers of the sweep (7 GEMVs each, cycling over "
+                                          f"{len(layers)} distinct layers = 513 MB), {done_bytes/1e6:.0f} MB in {el:.1f} s")
 
 
 def run_reference(args, rank: int):
@@ -170,14 +180,14 @@ def run_reference(args, rank: int):
     from webllm_b200 import synth
 
     cores = O.max_threads()
-    rng = np.random.default_rng(1234)
-    mats = [(t, synth.weights(rng, t, M, K), synth.activations(rng, 1, K), synth.algorithmic_bytes(t, M, K, 1))
-            for _, t, M, K in synth.LLAMA32_3B_LAYER]
-    layer_bytes = sum(m[3] for m in mats)
+    layers = cpu_layers(CPU_DISTINCT_LAYERS)
+    layer_bytes = sum(m[3] for m in layers[0])
+    counter = [0]
 
     def one_step():
-        for t, w, x, _ in mats:
+        for t, w, x, _ in layers[counter[0] % len(layers)]:
             O.mul_mat_f32(t, w, x, threads=cores)
+        counter[0] += 1
 
     for _ in range(args.warmup):
         one_step()
@@ -186,8 +196,9 @@ def run_reference(args, rank: int):
         one_step()
     el = time.perf_counter() - t0
     gbs = layer_bytes * args.steps / el / 1e9
-    sample = (f"each step: 1 of the 28 layers (7 GEMVs, {layer_bytes/1e6:.1f} MB of algorithmic bytes); "
-              f"f32 dequant-then-dot oracle (the reference's llama.cpp CPU kernels are not vendored)")
+    sample = (f"each step: 1 of the 28 layers (7 GEMVs, {layer_bytes/1e6:.1f} MB of algorithmic bytes), cycling "
+              f"over {len(layers)} distinct layers (513 MB) so weights stream from DRAM; f32 dequant-then-dot "
+              f"oracle (the reference's llama.cpp CPU kernels are not vendored in the reference repository)")
     line = {
         "impl": "reference", "metric": METRIC, "value": round(gbs, 3), "unit": "GB/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(el / args.steps * 1e3, 3),

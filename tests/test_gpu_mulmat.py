@@ -117,6 +117,30 @@ def test_llama32_3b_layer_shapes(runtime, name, qtype, M, K):
     assert O.rel_error(got, O.mul_mat_f64(qtype, w, x)) <= GEMV_TOL
 
 
+@pytest.mark.parametrize("name,qtype,M,K", synth.GEMMA2_2B_SHAPES[:2] + [synth.GEMMA2_2B_SHAPES[3]])
+@pytest.mark.parametrize("N", [1, 2])
+def test_gemma2_q8_0_shapes(runtime, name, qtype, M, K, N):
+    rng = np.random.default_rng(zlib.crc32(name.encode()) + N)
+    w = synth.weights(rng, qtype, M, K)
+    x = synth.activations(rng, N, K)
+    got = run_mul_mat(runtime, qtype, w, x)
+    assert O.rel_error(got, O.mul_mat_f64(qtype, w, x)) <= GEMV_TOL
+
+
+@pytest.mark.parametrize("qtype", [jsep.GGML_TYPE_Q4_K, jsep.GGML_TYPE_Q6_K, jsep.GGML_TYPE_Q8_0])
+def test_streaming_edge_shapes(runtime, qtype):
+    """Shapes around the streaming kernel's unit/segment boundaries: rows not
+    a multiple of the 8-row unit, K spanning several segments, a row count
+    far below the SM count and one above it."""
+    for M, K in ((1, 256), (9, 4096), (15, 12288), (1000, 2560), (2051, 512)):
+        rng = np.random.default_rng(M * 31 + K + qtype)
+        w = synth.weights(rng, qtype, M, K)
+        for N in (1, 2):
+            x = synth.activations(rng, N, K)
+            got = run_mul_mat(runtime, qtype, w, x)
+            assert O.rel_error(got, O.mul_mat_f64(qtype, w, x)) <= GEMV_TOL, (M, K, N)
+
+
 def test_single_gemv_4096(runtime):
     """The 4096x4096 Q4_K single-GEMV workload, batch 1."""
     rng = np.random.default_rng(1)

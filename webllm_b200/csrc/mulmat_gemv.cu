@@ -241,7 +241,13 @@ const char* check_mulmat_op(const MulMatOp& op) {
     return nullptr;
 }
 
-int launch_mulmat(const MulMatOp* ops, int n_ops, cudaStream_t stream) {
+int launch_mulmat(const MulMatOp* ops, int n_ops, cudaStream_t stream, int num_sms) {
+    if (n_ops >= 1 && n_ops <= kMaxOpsPerLaunch && stream_supported(ops, n_ops))
+        return launch_stream(ops, n_ops, stream, num_sms);
+    return launch_mulmat_general(ops, n_ops, stream);
+}
+
+int launch_mulmat_general(const MulMatOp* ops, int n_ops, cudaStream_t stream) {
     if (n_ops < 1 || n_ops > kMaxOpsPerLaunch) return -static_cast<int>(cudaErrorInvalidValue);
     OpList L;
     L.n_ops = n_ops;

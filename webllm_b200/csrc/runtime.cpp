@@ -42,6 +42,7 @@ struct AsyncRead {
 struct State {
     std::mutex mu;
     int device = -1;
+    int num_sms = 148;
     cudaStream_t stream = nullptr;
     std::unordered_map<int32_t, Buffer> live;
     std::map<uint64_t, std::vector<void*>> free_lists;  // cap -> blocks
@@ -293,7 +294,7 @@ void* get_scratch(State& s, uint64_t bytes) {
 }
 
 int32_t launch(State& s, const MulMatOp* ops, int n, cudaStream_t stream) {
-    const int rc = wllm::launch_mulmat(ops, n, stream);
+    const int rc = wllm::launch_mulmat(ops, n, stream, s.num_sms);
     if (rc < 0) return cuda_fail(s, static_cast<cudaError_t>(-rc), "MUL_MAT launch");
     if (s.capturing) s.captured_kernels += static_cast<uint64_t>(rc);
     else s.counters.kernels_launched += static_cast<uint64_t>(rc);
@@ -319,6 +320,8 @@ int32_t wllm_init(int32_t device) {
     if (e != cudaSuccess) return cuda_fail(s, e, "cudaSetDevice");
     e = cudaStreamCreateWithFlags(&s.stream, cudaStreamNonBlocking);
     if (e != cudaSuccess) return cuda_fail(s, e, "cudaStreamCreate");
+    int sms = 0;
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) == cudaSuccess && sms > 0) s.num_sms = sms;
     s.device = device;
     return WLLM_STATUS_OK;
 }
@@ -612,6 +615,8 @@ int32_t wllm_sync(void) {
     if (e != cudaSuccess) return cuda_fail(s, e, "wllm_sync");
     e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(s, e, "wllm_sync (pending error)");
+    const unsigned kerr = wllm::read_and_clear_stream_error();
+    if (kerr) return fail(s, "wllm_sync: a kernel gave up waiting on a pipeline barrier (code 0x%x)", kerr);
     return WLLM_STATUS_OK;
 }
 

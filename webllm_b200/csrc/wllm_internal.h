@@ -55,7 +55,16 @@ const char* check_mulmat_op(const MulMatOp& op);
 // Enqueue n_ops independent MUL_MAT ops (1 <= n_ops <= kMaxOpsPerLaunch)
 // on `stream`. Returns the number of kernels launched (>= 1) or a negative
 // cudaError_t on launch failure.
-int launch_mulmat(const MulMatOp* ops, int n_ops, cudaStream_t stream);
+int launch_mulmat(const MulMatOp* ops, int n_ops, cudaStream_t stream, int num_sms);
+// The general kernel only (every shape; used by tests to compare paths).
+int launch_mulmat_general(const MulMatOp* ops, int n_ops, cudaStream_t stream);
+
+// Streaming decode kernel (mulmat_stream.cu): ne2 = ne3 = 1, N <= 2,
+// K % 256 == 0, K <= 16384, 16-byte aligned activations (and Q4_K rows).
+bool stream_supported(const MulMatOp* ops, int n_ops);
+int launch_stream(const MulMatOp* ops, int n_ops, cudaStream_t stream, int num_sms);
+// Error code recorded by a bounded wait that timed out (0 = none); clears it.
+unsigned read_and_clear_stream_error();
 
 // Device dequantization of n elements to f32 (bit-exact with the oracle).
 int launch_dequantize(int type, const void* src, float* dst, int64_t n, cudaStream_t stream);
