@@ -141,6 +141,21 @@ def test_streaming_edge_shapes(runtime, qtype):
             assert O.rel_error(got, O.mul_mat_f64(qtype, w, x)) <= GEMV_TOL, (M, K, N)
 
 
+@pytest.mark.parametrize("scale", [1e-6, 1.0, 3e5])
+def test_activation_magnitudes(runtime, scale):
+    """Activations far outside N(0,1), including values beyond the f16 range
+    (the tensor-core path rescales each vector by a power of two)."""
+    rng = np.random.default_rng(int(scale * 1e6) % 2**31)
+    for qtype in (jsep.GGML_TYPE_Q4_K, jsep.GGML_TYPE_Q6_K, jsep.GGML_TYPE_Q8_0):
+        w = synth.weights(rng, qtype, 64, 2048)
+        for N in (1, 2):
+            x = (synth.activations(rng, N, 2048) * scale).astype(np.float32)
+            x[0, 5] = 0.0
+            got = run_mul_mat(runtime, qtype, w, x)
+            assert np.all(np.isfinite(got))
+            assert O.rel_error(got, O.mul_mat_f64(qtype, w, x)) <= GEMV_TOL, (qtype, N, scale)
+
+
 def test_single_gemv_4096(runtime):
     """The 4096x4096 Q4_K single-GEMV workload, batch 1."""
     rng = np.random.default_rng(1)

@@ -1,35 +1,42 @@
 // Decode-regime quantized MUL_MAT (N = 1 or 2 activation vectors): a
 // persistent, warp-specialised streaming GEMV over raw GGUF blocks.
 //
-// Data movement. The weight matrix is cut into units of 8 rows; each unit's
-// rows are cut into segments of at most 2304 bytes. One producer warp moves
-// every (row, segment) piece HBM -> shared memory with one bulk async copy
-// (cp.async.bulk, completion counted on an mbarrier), through a ring of
-// stages, with an evict-first L2 policy because each weight byte is read
-// exactly once. The copy window is the piece rounded out to 16-byte
-// boundaries, so Q6_K (210 B) and Q8_0 (34 B) blocks, which are not
-// 16-byte aligned, stream exactly like Q4_K. Eight consumer warps decode
-// from shared memory.
+// Data movement. The weight matrix is cut into units of 16 rows; each
+// unit's rows are cut into segments of at most 8 Q4_K / 5 Q6_K / 32 Q8_0
+// blocks. One producer warp moves every (row, segment) piece HBM -> shared
+// memory with one bulk async copy (cp.async.bulk, completion counted on an
+// mbarrier) through a ring of stages, with an evict-first L2 policy (each
+// weight byte is read exactly once). The copy window is the piece rounded
+// out to 16-byte boundaries, so Q6_K (210 B) and Q8_0 (34 B) blocks, which
+// are not 16-byte aligned, stream exactly like Q4_K. Eight consumer warps
+// compute from shared memory.
 //
-// Consumer mapping. Lanes 8j..8j+7 work on row 4q+j of the unit; lane
-// chunk c = lane%8 owns 32 elements of a 256-element block (Q4_K, Q6_K) or
-// one whole 32-element block (Q8_0). The activation chunk a lane needs is
-// the same for the four rows of a quad and for both quads of the unit, so it
-// is loaded from shared memory once per block and kept in registers.
+// Q4_K on tensor cores (mma.sync m16n8k16, f16 in, f32 accumulate). A unit
+// is one 16-row MMA tile. A 4-bit quant enters the MMA as the exact f16
+// subnormal q * 2^-24 (one LOP3 per two quants: low nibble pairs are
+// (v & 0x000F000F), high nibbles (v & 0x00F000F0) = 16 q * 2^-24). The
+// activations are the B operand, split into two f16 limbs hi = f16(x s),
+// lo = f16(x s - hi) (s a power of two per vector keeps x s inside f16
+// range), so 22 bits of x take part and every product is exact; the MMA
+// sums them in f32. Each 32-element sub-block is its own accumulator chain
+// of two k16 MMAs; the chain result is scaled in f32 by d*sc (decoded once
+// per stage into a shared table) and the min term dmin*m*sum(x) is
+// subtracted in f32. The k order inside an MMA is a fixed permutation
+// shared by A and B: lane group c holds quant bytes 4c..4c+3.
 //
-// Arithmetic. A 4- or 6-bit quant q is turned into the float 1 + q/128 with
-// one byte permute (the byte 0x80|q becomes bits 16..23 of 0x3F800000);
-// S = sum (1 + q/128) x is accumulated with packed FFMA2 and the quant sum
-// is recovered as 128 (S - X), X = sum x over the same elements (computed
-// once per block and lane). This keeps the weight unpack at ~1.3 integer
-// ops per weight. Scales, mins and d are applied per sub-block in f32.
+// Q6_K and Q8_0 on CUDA cores. Lanes 8j..8j+7 work on row 4q+j (q = 0..3);
+// lane chunk c = lane%8 owns 32 elements of a 256-element block (Q6_K) or
+// one 32-element block (Q8_0); the lane's activation chunk stays in
+// registers for the unit's four quads. A 6-bit quant becomes the float
+// 1 + q/128 with one byte permute (0x80|q placed in bits 16..23 of
+// 0x3F800000), S = sum (1 + q/128) x runs on packed FFMA2, and the quant
+// sum is recovered as 128 (S - X) with X = sum x over the same elements.
 //
-// Launch. Programmatic dependent launch: every CTA triggers its dependents
-// at entry, the producer streams weights (never written by a preceding
-// kernel) immediately, and the consumers execute griddepcontrol.wait before
-// reading activations or writing outputs. So the next MUL_MAT's weight
-// stream overlaps this one's tail. Every mbarrier wait is bounded; on
-// timeout the kernel records an error code and returns.
+// Launch. Programmatic dependent launch: CTAs trigger their dependents at
+// entry; the producer streams weights (never written by a preceding kernel)
+// immediately; consumers execute griddepcontrol.wait before reading
+// activations or writing outputs. Every mbarrier wait is bounded; on timeout
+// the CTA records an error code and drains without further waiting.
 #include <cuda_fp16.h>
 #include <stdint.h>
 
@@ -42,16 +49,19 @@ __device__ unsigned int g_stream_error = 0;
 
 namespace {
 
-constexpr int kCW = 8;                       // consumer warps
-constexpr int kThreads = 32 * (kCW + 1);     // + one producer warp
-constexpr int kRows = 8;                     // rows per unit
-constexpr int kPieceCap = 2304;              // max bytes of one row segment
-constexpr int kPieceStride = kPieceCap + 32; // + window rounding slack
+constexpr int kCW = 8;                        // consumer warps
+constexpr int kThreads = 32 * (kCW + 1);      // + one producer warp
+constexpr int kRows = 16;                     // rows per unit (one MMA m-tile)
+constexpr int kPieceStride = 1296;            // bytes per row piece (== 16 mod 128: conflict-free rows)
 constexpr int kStageBytes = kRows * kPieceStride;
-constexpr int kMaxStages = 6;
+constexpr int kMaxStages = 8;
 constexpr int kMaxNT = 2;
+constexpr int kQ4kSegBlocks = 8;              // 1152 B
+constexpr int kQ6kSegBlocks = 5;              // 1050 B (+ window slack)
+constexpr int kQ80SegBlocks = 32;             // 1088 B, whole 8-block groups
+constexpr int kTabBytes = kRows * kQ4kSegBlocks * 4 * 16;  // Q4_K scale table, one buffer
 constexpr uint32_t kSpinLimit = 1u << 22;
-constexpr int kSmemBudget = 110 * 1024;      // leaves room for a second CTA per SM
+constexpr int kSmemBudget = 200 * 1024;
 
 struct SOp {
     const uint8_t* w;
@@ -69,7 +79,7 @@ struct SList {
     int32_t n_ops;
     int32_t total_units;
     int32_t stages;
-    int32_t x_floats;  // shared-memory floats reserved for activations
+    int32_t x_bytes;  // shared-memory bytes reserved for staged activations
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -133,6 +143,15 @@ __device__ __forceinline__ void consumers_sync() {
     asm volatile("bar.sync 1, %0;" ::"n"(kCW * 32) : "memory");
 }
 
+__device__ __forceinline__ void mma_f16(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                        uint32_t b0, uint32_t b1, const float (&c)[4]) {
+    asm(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%10,%11,%12,%13};"
+        : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(c[0]), "f"(c[1]), "f"(c[2]), "f"(c[3]));
+}
+
 __device__ __forceinline__ int block_elems_of(int type) { return type == kTypeQ8_0 ? 32 : 256; }
 __device__ __forceinline__ int block_bytes_of(int type) {
     return type == kTypeQ4_K ? 144 : (type == kTypeQ6_K ? 210 : 34);
@@ -144,14 +163,10 @@ __device__ __forceinline__ float unit_q(uint32_t w) {
     return __uint_as_float(__byte_perm(w, 0x3F000000u, 0x7044u | (k << 8)));
 }
 
-// Element offset (within the block group) of float4 f of lane chunk c.
-// Activations are staged as xs4[group][f][c] so that the 8 chunks of one
-// LDS.128 phase are 8 consecutive float4 (no bank conflicts).
+// Element offset (within its 256-element group) of float4 f of lane chunk c,
+// for the CUDA-core formats. Activations are staged as xs4[group][f][c] so
+// the 8 chunks of one LDS.128 phase are 8 consecutive float4.
 __device__ __forceinline__ int chunk_elem(int type, int c, int f) {
-    if (type == kTypeQ4_K) {
-        const int p = c >> 1, h = c & 1;
-        return 64 * p + 16 * h + (f < 4 ? 4 * f : 32 + 4 * (f - 4));
-    }
     if (type == kTypeQ6_K) {
         const int h = c >> 2, l0 = 8 * (c & 3), t = f >> 1;
         return 128 * h + 32 * t + l0 + 4 * (f & 1);
@@ -159,69 +174,38 @@ __device__ __forceinline__ int chunk_elem(int type, int c, int f) {
     return 32 * c + 4 * f;  // Q8_0: lane chunk c is block c of the group
 }
 
-// 16-byte (or smaller-aligned) loads from shared memory of raw block bytes.
+// 4 bytes at any 2-byte-aligned shared address.
 __device__ __forceinline__ uint32_t lds_u32_any(const uint8_t* p) {
     const uint32_t mis = static_cast<uint32_t>(reinterpret_cast<uintptr_t>(p) & 3);
-    const uint32_t* q = reinterpret_cast<const uint32_t*>(p - mis);  // keeps the shared-space provenance
+    const uint32_t* q = reinterpret_cast<const uint32_t*>(p - mis);
     return __funnelshift_r(q[0], q[1], mis * 8);
 }
 __device__ __forceinline__ uint32_t lds_u16(const uint8_t* p) { return *reinterpret_cast<const uint16_t*>(p); }
 
-template <int NT>
-struct Acc {
-    float v[2][NT];  // [quad][token]
-};
+// ---------------------------------------------------------------- Q4_K (tensor cores)
 
-// ---- per-format item computations (one lane, one row, one block) ----
-
-template <int NT>
-__device__ __forceinline__ void item_q4_k(const uint8_t* blk, int c, const float4 (&xr)[NT][8], const float (&xs)[NT][2],
-                                          float (&acc)[NT]) {
+// Scale table entry for (row, block, pair p): d*sc*2^24 (low sub-block),
+// d*sc*2^20 (high sub-block; its quants enter as 16 q), dmin*m low, high.
+__device__ __forceinline__ void q4k_decode_scales(const uint8_t* blk, float4* out /* [4] */) {
     const uint4 hdr = *reinterpret_cast<const uint4*>(blk);
-    const uint4 qv = *reinterpret_cast<const uint4*>(blk + 16 + 16 * c);
-    const int p = c >> 1;
-    // packed 6-bit scales/mins (get_scale_min_k4): words of bytes sc0..3, m0..3, sc4..7, m4..7
     const uint32_t s0 = hdr.y, s1 = hdr.z, s2 = hdr.w;
-    uint32_t scw, mw;
-    if (p < 2) {
-        scw = s0 & 0x3F3F3F3Fu;
-        mw = s1 & 0x3F3F3F3Fu;
-    } else {
-        scw = (s2 & 0x0F0F0F0Fu) | ((s0 >> 2) & 0x30303030u);
-        mw = ((s2 >> 4) & 0x0F0F0F0Fu) | ((s1 >> 2) & 0x30303030u);
-    }
-    const int sh = 16 * (p & 1);  // byte pair (2p, 2p+1) within the word
+    const uint32_t sc_lo4 = s0 & 0x3F3F3F3Fu, m_lo4 = s1 & 0x3F3F3F3Fu;
+    const uint32_t sc_hi4 = (s2 & 0x0F0F0F0Fu) | ((s0 >> 2) & 0x30303030u);
+    const uint32_t m_hi4 = ((s2 >> 4) & 0x0F0F0F0Fu) | ((s1 >> 2) & 0x30303030u);
     const float d = f16_bits_to_f32(hdr.x), dmin = f16_bits_to_f32(hdr.x >> 16);
-    const float sc_lo = static_cast<float>((scw >> sh) & 0xFFu), sc_hi = static_cast<float>((scw >> (sh + 8)) & 0xFFu);
-    const float m_lo = static_cast<float>((mw >> sh) & 0xFFu), m_hi = static_cast<float>((mw >> (sh + 8)) & 0xFFu);
-    const float a_lo = 128.f * d * sc_lo, a_hi = 128.f * d * sc_hi;
-    const float b_lo = a_lo + dmin * m_lo, b_hi = a_hi + dmin * m_hi;
-    const uint32_t w4[4] = {qv.x, qv.y, qv.z, qv.w};
-    float2 slo[NT], shi[NT];
+    const float d24 = d * 16777216.f, d20 = d * 1048576.f;
 #pragma unroll
-    for (int n = 0; n < NT; ++n) slo[n] = shi[n] = make_float2(0.f, 0.f);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const uint32_t lo = (w4[i] & 0x0F0F0F0Fu) | 0x80808080u;
-        const uint32_t hi = ((w4[i] >> 4) & 0x0F0F0F0Fu) | 0x80808080u;
-        const float2 l01 = make_float2(unit_q<0>(lo), unit_q<1>(lo)), l23 = make_float2(unit_q<2>(lo), unit_q<3>(lo));
-        const float2 h01 = make_float2(unit_q<0>(hi), unit_q<1>(hi)), h23 = make_float2(unit_q<2>(hi), unit_q<3>(hi));
-#pragma unroll
-        for (int n = 0; n < NT; ++n) {
-            const float4 xl = xr[n][i], xh = xr[n][4 + i];
-            slo[n] = __ffma2_rn(l01, make_float2(xl.x, xl.y), slo[n]);
-            slo[n] = __ffma2_rn(l23, make_float2(xl.z, xl.w), slo[n]);
-            shi[n] = __ffma2_rn(h01, make_float2(xh.x, xh.y), shi[n]);
-            shi[n] = __ffma2_rn(h23, make_float2(xh.z, xh.w), shi[n]);
-        }
-    }
-#pragma unroll
-    for (int n = 0; n < NT; ++n) {
-        const float S_lo = slo[n].x + slo[n].y, S_hi = shi[n].x + shi[n].y;
-        // sum (d sc q - dmin m) x = a (S - X) - dmin m X = a S - b X
-        acc[n] += a_lo * S_lo - b_lo * xs[n][0] + a_hi * S_hi - b_hi * xs[n][1];
+    for (int p = 0; p < 4; ++p) {
+        const uint32_t scw = p < 2 ? sc_lo4 : sc_hi4, mw = p < 2 ? m_lo4 : m_hi4;
+        const int sh = 16 * (p & 1);
+        out[p] = make_float4(d24 * static_cast<float>((scw >> sh) & 0xFFu),
+                             d20 * static_cast<float>((scw >> (sh + 8)) & 0xFFu),
+                             dmin * static_cast<float>((mw >> sh) & 0xFFu),
+                             dmin * static_cast<float>((mw >> (sh + 8)) & 0xFFu));
     }
 }
+
+// ---------------------------------------------------------------- Q6_K / Q8_0 (CUDA cores)
 
 template <int NT>
 __device__ __forceinline__ void item_q6_k(const uint8_t* blk, int c, const float4 (&xr)[NT][8], const float (&xq)[NT][4],
@@ -265,7 +249,7 @@ __device__ __forceinline__ void item_q6_k(const uint8_t* blk, int c, const float
         float r = 0.f;
 #pragma unroll
         for (int t = 0; t < 4; ++t) {
-            // sum d sc (q6 - 32) x = a (S - X) - 32/128 a X = a S - (5/4) a X
+            // sum d sc (q6 - 32) x = a (S - X) - 32/128 a X = a (S - (5/4) X)
             r += a[t] * ((s[t][n].x + s[t][n].y) - 1.25f * xq[n][t]);
         }
         acc[n] += r;
@@ -275,13 +259,20 @@ __device__ __forceinline__ void item_q6_k(const uint8_t* blk, int c, const float
 template <int NT>
 __device__ __forceinline__ void item_q8_0(const uint8_t* blk, const float4 (&xr)[NT][8], float (&acc)[NT]) {
     const float d = f16_bits_to_f32(lds_u16(blk));
+    // the 32 quant bytes at blk+2 (2-byte aligned): 9 aligned words, then funnel shifts
+    const uint8_t* q = blk + 2;
+    const uint32_t mis = static_cast<uint32_t>(reinterpret_cast<uintptr_t>(q) & 3);
+    const uint32_t* wp = reinterpret_cast<const uint32_t*>(q - mis);
+    uint32_t wv[9];
+#pragma unroll
+    for (int i = 0; i < 9; ++i) wv[i] = wp[i];
     float2 s[NT];
 #pragma unroll
     for (int n = 0; n < NT; ++n) s[n] = make_float2(0.f, 0.f);
 #pragma unroll
     for (int f = 0; f < 8; ++f) {
-        const uint32_t w = lds_u32_any(blk + 2 + 4 * f) ^ 0x80808080u;  // biased to u = q + 128
-        // 2^23 + u exactly, then subtract 2^23 + 128 -> q
+        const uint32_t w = __funnelshift_r(wv[f], wv[f + 1], mis * 8) ^ 0x80808080u;  // u = q + 128
+        // 2^23 + u exactly, minus 2^23 + 128 -> q
         const float q0 = __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7440u)) - 8388736.f;
         const float q1 = __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7441u)) - 8388736.f;
         const float q2 = __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7442u)) - 8388736.f;
@@ -297,14 +288,36 @@ __device__ __forceinline__ void item_q8_0(const uint8_t* blk, const float4 (&xr)
     for (int n = 0; n < NT; ++n) acc[n] += d * (s[n].x + s[n].y);
 }
 
+// f16 limbs of v: hi = f16(v), lo = f16(v - hi).
+__device__ __forceinline__ void limbs(float v, __half& hi, __half& lo) {
+    hi = __float2half_rn(v);
+    lo = __float2half_rn(v - __half2float(hi));
+}
+
+__device__ __forceinline__ uint32_t pack_h2(__half a, __half b) {
+    return static_cast<uint32_t>(__half_as_ushort(a)) | (static_cast<uint32_t>(__half_as_ushort(b)) << 16);
+}
+
+// Power of two s with max|x s| in [2^14, 2^15) (1 when max is 0 or not finite).
+__device__ __forceinline__ float limb_scale(float maxabs) {
+    const uint32_t bits = __float_as_uint(maxabs);
+    const int e = static_cast<int>((bits >> 23) & 0xFF);
+    if (maxabs == 0.f || e == 0xFF) return 1.f;
+    int se = 14 - (e - 127) + 127;  // exponent field of 2^(14 - e)
+    se = se < 1 ? 1 : (se > 254 ? 254 : se);
+    return __uint_as_float(static_cast<uint32_t>(se) << 23);
+}
+
 template <int NT>
-__global__ void __launch_bounds__(kThreads, 2) stream_gemv_kernel(const __grid_constant__ SList L) {
+__global__ void __launch_bounds__(kThreads, 1) stream_gemv_kernel(const __grid_constant__ SList L) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int S = L.stages;
     uint8_t* stages = smem;
-    float4* xs4 = reinterpret_cast<float4*>(smem + S * kStageBytes);
-    float* red = reinterpret_cast<float*>(smem + S * kStageBytes + 4 * L.x_floats);  // [2][kCW][kRows][NT]
-    uint64_t* full = reinterpret_cast<uint64_t*>(red + 2 * kCW * kRows * NT);
+    uint8_t* xsm = smem + S * kStageBytes;                                 // staged activations
+    float4* tab = reinterpret_cast<float4*>(xsm + L.x_bytes);              // [2][16 rows][8 blocks][4]
+    float* red = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(tab) + 2 * kTabBytes);  // [2][kCW][16][NT]
+    float* xscale = red + 2 * kCW * kRows * NT;                            // [NT] 1/s per vector
+    uint64_t* full = reinterpret_cast<uint64_t*>(xscale + 2 * kMaxNT);
     uint64_t* empty = full + kMaxStages;
     volatile int* poisoned = reinterpret_cast<volatile int*>(empty + kMaxStages);
 
@@ -333,21 +346,22 @@ __global__ void __launch_bounds__(kThreads, 2) stream_gemv_kernel(const __grid_c
                 const int nblocks = op.K / block_elems_of(op.type);
                 const int r0 = (u - op.unit_begin) * kRows;
                 const int nrows = min(kRows, op.M - r0);
+                const uint8_t* wrow0 = op.w + static_cast<int64_t>(r0) * op.w_nb1;
                 for (int sg = 0; sg < op.nseg; ++sg, ++it) {
                     const int s = it % S;
                     if (!mbar_wait(&empty[s], ((it / S) & 1) ^ 1, 1u, poisoned)) return;
                     const int b0 = sg * op.seg_blocks;
-                    const int nb = min(op.seg_blocks, nblocks - b0);
+                    const int nbytes = min(op.seg_blocks, nblocks - b0) * bb;
                     uint32_t total = 0;
                     for (int r = 0; r < nrows; ++r) {
-                        const uintptr_t g = reinterpret_cast<uintptr_t>(op.w + (r0 + r) * op.w_nb1 + b0 * bb);
-                        total += static_cast<uint32_t>(((g + nb * bb + 15) & ~uintptr_t(15)) - (g & ~uintptr_t(15)));
+                        const uintptr_t g = reinterpret_cast<uintptr_t>(wrow0 + r * op.w_nb1 + b0 * bb);
+                        total += static_cast<uint32_t>(((g + nbytes + 15) & ~uintptr_t(15)) - (g & ~uintptr_t(15)));
                     }
                     mbar_arrive_expect_tx(&full[s], total);
                     for (int r = 0; r < nrows; ++r) {
-                        const uintptr_t g = reinterpret_cast<uintptr_t>(op.w + (r0 + r) * op.w_nb1 + b0 * bb);
+                        const uintptr_t g = reinterpret_cast<uintptr_t>(wrow0 + r * op.w_nb1 + b0 * bb);
                         const uintptr_t ga = g & ~uintptr_t(15);
-                        const uint32_t bytes = static_cast<uint32_t>(((g + nb * bb + 15) & ~uintptr_t(15)) - ga);
+                        const uint32_t bytes = static_cast<uint32_t>(((g + nbytes + 15) & ~uintptr_t(15)) - ga);
                         bulk_g2s(stages + s * kStageBytes + r * kPieceStride, reinterpret_cast<const void*>(ga), bytes,
                                  &full[s], policy);
                     }
@@ -361,121 +375,231 @@ __global__ void __launch_bounds__(kThreads, 2) stream_gemv_kernel(const __grid_c
     asm volatile("griddepcontrol.wait;" ::: "memory");
     const int ct = threadIdx.x - 32;  // 0..255
     const int cw = warp - 1;          // 0..7
-    const int j = lane >> 3, c = lane & 7;
     uint32_t it = 0;
     int oi = 0, staged = -1;
-    int rb = 0;  // reduction buffer parity
+    int rb = 0, tb = 0;
     for (int u = blockIdx.x; u < L.total_units; u += gridDim.x) {
         while (oi + 1 < L.n_ops && u >= L.op[oi + 1].unit_begin) ++oi;
         const SOp& op = L.op[oi];
-        // (re)stage activations when the op's x or layout changes
-        if (staged < 0 || L.op[staged].x != op.x || L.op[staged].type != op.type || L.op[staged].K != op.K ||
-            L.op[staged].N != op.N || L.op[staged].x_nb1 != op.x_nb1) {
+        const int N = op.N;
+        const int K = op.K;
+        const bool tc = op.type == kTypeQ4_K;
+        // ---- (re)stage activations when the op's x or layout changes ----
+        if (staged < 0 || L.op[staged].x != op.x || L.op[staged].type != op.type || L.op[staged].K != K ||
+            L.op[staged].N != N || L.op[staged].x_nb1 != op.x_nb1) {
             consumers_sync();
-            const int groups = op.K / 256;  // 256-element block groups
-            const int per_tok = groups * 64;
-            for (int idx = ct; idx < per_tok * op.N; idx += kCW * 32) {
-                const int n = idx / per_tok, r = idx % per_tok;
-                const int g = r >> 6, f = (r >> 3) & 7, cc = r & 7;
-                const float* xp = reinterpret_cast<const float*>(reinterpret_cast<const uint8_t*>(op.x) + n * op.x_nb1);
-                xs4[idx] = __ldg(reinterpret_cast<const float4*>(xp + g * 256 + chunk_elem(op.type, cc, f)));
+            if (tc) {
+                // per-vector power-of-two scale: warp n finds max|x_n|
+                if (cw < N) {
+                    const float* xp = reinterpret_cast<const float*>(reinterpret_cast<const uint8_t*>(op.x) + cw * op.x_nb1);
+                    float mx = 0.f;
+                    for (int k = lane * 4; k < K; k += 128) {
+                        const float4 v = __ldg(reinterpret_cast<const float4*>(xp + k));
+                        mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+                    }
+#pragma unroll
+                    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+                    if (lane == 0) {
+                        const float sc = limb_scale(mx);
+                        xscale[cw] = sc;
+                        xscale[kMaxNT + cw] = 1.f / sc;
+                    }
+                }
+                consumers_sync();
+                // B fragments: entry e = ((b*4 + p)*2 + j)*2 + h, lanes 0..8N-1
+                uint2* xB = reinterpret_cast<uint2*>(xsm);
+                const int lanes = 8 * N;
+                const int entries = (K / 256) * 16;
+                for (int idx = ct; idx < entries * lanes; idx += kCW * 32) {
+                    const int Lc = idx % lanes, e = idx / lanes;
+                    const int h = e & 1, jj = (e >> 1) & 1, p = (e >> 2) & 3, b = e >> 4;
+                    const int gp = Lc >> 2, cp = Lc & 3, t = gp >> 1, limb = gp & 1;
+                    const float* xp = reinterpret_cast<const float*>(reinterpret_cast<const uint8_t*>(op.x) + t * op.x_nb1) +
+                                      b * 256 + 64 * p + 32 * h + 16 * jj + 4 * cp;
+                    const float4 v = __ldg(reinterpret_cast<const float4*>(xp));
+                    const float sc = xscale[t];
+                    __half h0, l0, h1, l1, h2, l2, h3, l3;
+                    limbs(v.x * sc, h0, l0);
+                    limbs(v.y * sc, h1, l1);
+                    limbs(v.z * sc, h2, l2);
+                    limbs(v.w * sc, h3, l3);
+                    // b0 = (k 2c, 2c+1) <- elements (4c, 4c+2); b1 = (2c+8, 2c+9) <- (4c+1, 4c+3)
+                    xB[idx] = limb == 0 ? make_uint2(pack_h2(h0, h2), pack_h2(h1, h3))
+                                        : make_uint2(pack_h2(l0, l2), pack_h2(l1, l3));
+                }
+                // sub-block sums of x (unscaled f32) for the min term
+                float* Xs = reinterpret_cast<float*>(xsm + entries * lanes * 8);
+                const int nsub = K / 32;
+                for (int idx = ct; idx < nsub * N; idx += kCW * 32) {
+                    const int t = idx / nsub, sbk = idx % nsub;
+                    const float* xp = reinterpret_cast<const float*>(reinterpret_cast<const uint8_t*>(op.x) + t * op.x_nb1) +
+                                      32 * sbk;
+                    float a = 0.f;
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) {
+                        const float4 v = __ldg(reinterpret_cast<const float4*>(xp + 4 * i));
+                        a += (v.x + v.y) + (v.z + v.w);
+                    }
+                    Xs[idx] = a;
+                }
+            } else {
+                float4* xs4 = reinterpret_cast<float4*>(xsm);
+                const int per_tok = (K / 256) * 64;
+                for (int idx = ct; idx < per_tok * N; idx += kCW * 32) {
+                    const int n = idx / per_tok, r = idx % per_tok;
+                    const int g = r >> 6, f = (r >> 3) & 7, cc = r & 7;
+                    const float* xp = reinterpret_cast<const float*>(reinterpret_cast<const uint8_t*>(op.x) + n * op.x_nb1);
+                    xs4[idx] = __ldg(reinterpret_cast<const float4*>(xp + g * 256 + chunk_elem(op.type, cc, f)));
+                }
             }
             consumers_sync();
             staged = oi;
         }
         const int bb = block_bytes_of(op.type);
-        const int nblocks = op.K / block_elems_of(op.type);
+        const int nblocks = K / block_elems_of(op.type);
         const int r0 = (u - op.unit_begin) * kRows;
-        const int groups_per_tok = op.K / 256;
-        float acc[2][NT];
-#pragma unroll
-        for (int q = 0; q < 2; ++q)
-#pragma unroll
-            for (int n = 0; n < NT; ++n) acc[q][n] = 0.f;
+        const uint32_t wlo = static_cast<uint32_t>(reinterpret_cast<uintptr_t>(op.w + static_cast<int64_t>(r0) * op.w_nb1));
+        const uint32_t nb1lo = static_cast<uint32_t>(op.w_nb1);
 
-        for (int sg = 0; sg < op.nseg; ++sg, ++it) {
-            const int s = it % S;
-            mbar_wait(&full[s], (it / S) & 1, 2u, poisoned);
-            const int b0 = sg * op.seg_blocks;
-            const int nb = min(op.seg_blocks, nblocks - b0);
-            const uint8_t* stage = stages + s * kStageBytes;
-            // block groups of this segment (Q8_0: 8 blocks per group)
-            const int gpb = op.type == kTypeQ8_0 ? 8 : 1;
-            const int g0 = b0 / gpb;
-            const int ngroups = (nb + gpb - 1) / gpb;
-            for (int gi = cw; gi < ngroups; gi += kCW) {
-                const int g = g0 + gi;
-                float4 xr[NT][8];
-#pragma unroll
-                for (int n = 0; n < NT; ++n)
-#pragma unroll
-                    for (int f = 0; f < 8; ++f) xr[n][f] = xs4[(n * groups_per_tok + g) * 64 + f * 8 + c];
-                if (op.type == kTypeQ8_0) {
-                    const int blk = g * 8 + c;  // this lane's Q8_0 block
-                    if (blk < b0 + nb) {
-#pragma unroll
-                        for (int q = 0; q < 2; ++q) {
-                            const int r = 4 * q + j;
-                            const uintptr_t gaddr = reinterpret_cast<uintptr_t>(op.w + (r0 + r) * op.w_nb1 + b0 * bb);
-                            const uint8_t* base = stage + r * kPieceStride + (gaddr & 15);
-                            item_q8_0<NT>(base + (blk - b0) * 34, xr, acc[q]);
-                        }
+        if (tc) {
+            // ================= Q4_K, tensor cores =================
+            const int g = lane >> 2, c = lane & 3;
+            const int lanes = 8 * N;
+            const uint2* xB = reinterpret_cast<const uint2*>(xsm);
+            const float* Xs = reinterpret_cast<const float*>(xsm + (K / 256) * 16 * lanes * 8);
+            const int nsub = K / 32;
+            float accm_g = 0.f, accm_g8 = 0.f;  // sum A * (D_hi + D_lo), in units of x*s
+            float accn_g = 0.f, accn_g8 = 0.f;  // sum dmin*m*X (unscaled)
+            for (int sg = 0; sg < op.nseg; ++sg, ++it) {
+                const int s = it % S;
+                mbar_wait(&full[s], (it / S) & 1, 2u, poisoned);
+                const int b0 = sg * op.seg_blocks;
+                const int nb = min(op.seg_blocks, nblocks - b0);
+                const uint8_t* stage = stages + s * kStageBytes;
+                float4* tbuf = tab + tb * (kRows * kQ4kSegBlocks * 4);
+                // scale table: one thread per (row, block)
+                if (ct < kRows * nb) {
+                    const int r = ct & 15, bl = ct >> 4;
+                    q4k_decode_scales(stage + r * kPieceStride + bl * 144, tbuf + (r * kQ4kSegBlocks + bl) * 4);
+                }
+                consumers_sync();
+                const float zero4[4] = {0.f, 0.f, 0.f, 0.f};
+                for (int item = cw; item < nb * 4; item += kCW) {
+                    const int bl = item >> 2, p = item & 3;
+                    const int bg = b0 + bl;
+                    const uint8_t* rq = stage + g * kPieceStride + bl * 144 + 16 + 32 * p + 4 * c;
+                    const uint32_t vg0 = *reinterpret_cast<const uint32_t*>(rq);
+                    const uint32_t vg1 = *reinterpret_cast<const uint32_t*>(rq + 16);
+                    const uint32_t vh0 = *reinterpret_cast<const uint32_t*>(rq + 8 * kPieceStride);
+                    const uint32_t vh1 = *reinterpret_cast<const uint32_t*>(rq + 8 * kPieceStride + 16);
+                    const uint2* xe = xB + ((bg * 4 + p) * 4) * lanes;  // entries (j, h) = 0..3
+                    uint2 bl0 = make_uint2(0u, 0u), bl1 = bl0, bh0 = bl0, bh1 = bl0;
+                    if (lane < lanes) {
+                        bl0 = xe[0 * lanes + lane];  // j=0, lo
+                        bh0 = xe[1 * lanes + lane];  // j=0, hi
+                        bl1 = xe[2 * lanes + lane];  // j=1, lo
+                        bh1 = xe[3 * lanes + lane];  // j=1, hi
                     }
-                } else if (op.type == kTypeQ4_K) {
-                    float xs[NT][2];
-#pragma unroll
-                    for (int n = 0; n < NT; ++n) {
-                        float a = 0.f, b = 0.f;
-#pragma unroll
-                        for (int f = 0; f < 4; ++f) {
-                            a += (xr[n][f].x + xr[n][f].y) + (xr[n][f].z + xr[n][f].w);
-                            b += (xr[n][4 + f].x + xr[n][4 + f].y) + (xr[n][4 + f].z + xr[n][4 + f].w);
-                        }
-                        xs[n][0] = a;
-                        xs[n][1] = b;
+                    const uint32_t vg0s = vg0 >> 8, vg1s = vg1 >> 8, vh0s = vh0 >> 8, vh1s = vh1 >> 8;
+                    float dlo[4], dhi[4];
+                    mma_f16(dlo, vg0 & 0x000F000Fu, vh0 & 0x000F000Fu, vg0s & 0x000F000Fu, vh0s & 0x000F000Fu, bl0.x,
+                            bl0.y, zero4);
+                    mma_f16(dlo, vg1 & 0x000F000Fu, vh1 & 0x000F000Fu, vg1s & 0x000F000Fu, vh1s & 0x000F000Fu, bl1.x,
+                            bl1.y, dlo);
+                    mma_f16(dhi, vg0 & 0x00F000F0u, vh0 & 0x00F000F0u, vg0s & 0x00F000F0u, vh0s & 0x00F000F0u, bh0.x,
+                            bh0.y, zero4);
+                    mma_f16(dhi, vg1 & 0x00F000F0u, vh1 & 0x00F000F0u, vg1s & 0x00F000F0u, vh1s & 0x00F000F0u, bh1.x,
+                            bh1.y, dhi);
+                    const float4 sg_ = tbuf[(g * kQ4kSegBlocks + bl) * 4 + p];
+                    const float4 sg8 = tbuf[((g + 8) * kQ4kSegBlocks + bl) * 4 + p];
+                    float xlo = 0.f, xhi = 0.f;
+                    if (c < N) {
+                        xlo = Xs[c * nsub + bg * 8 + 2 * p];
+                        xhi = Xs[c * nsub + bg * 8 + 2 * p + 1];
                     }
+                    accm_g += sg_.x * (dlo[0] + dlo[1]) + sg_.y * (dhi[0] + dhi[1]);
+                    accm_g8 += sg8.x * (dlo[2] + dlo[3]) + sg8.y * (dhi[2] + dhi[3]);
+                    accn_g += sg_.z * xlo + sg_.w * xhi;
+                    accn_g8 += sg8.z * xlo + sg8.w * xhi;
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&empty[s]);
+                tb ^= 1;
+            }
+            if (c < N) {
+                const float inv = xscale[kMaxNT + c];
+                red[((rb * kCW + cw) * kRows + g) * NT + c] = accm_g * inv - accn_g;
+                red[((rb * kCW + cw) * kRows + g + 8) * NT + c] = accm_g8 * inv - accn_g8;
+            }
+        } else {
+            // ================= Q6_K / Q8_0, CUDA cores =================
+            const int j = lane >> 3, c = lane & 7;
+            const int K256 = K / 256;
+            const float4* xs4 = reinterpret_cast<const float4*>(xsm);
+            float acc[4][NT];
 #pragma unroll
-                    for (int q = 0; q < 2; ++q) {
-                        const int r = 4 * q + j;
-                        const uintptr_t gaddr = reinterpret_cast<uintptr_t>(op.w + (r0 + r) * op.w_nb1 + b0 * bb);
-                        const uint8_t* base = stage + r * kPieceStride + (gaddr & 15);
-                        item_q4_k<NT>(base + (g - b0) * 144, c, xr, xs, acc[q]);
-                    }
-                } else {
-                    float xq[NT][4];
+            for (int q = 0; q < 4; ++q)
+#pragma unroll
+                for (int n = 0; n < NT; ++n) acc[q][n] = 0.f;
+            for (int sg = 0; sg < op.nseg; ++sg, ++it) {
+                const int s = it % S;
+                mbar_wait(&full[s], (it / S) & 1, 2u, poisoned);
+                const int b0 = sg * op.seg_blocks;
+                const int nb = min(op.seg_blocks, nblocks - b0);
+                const uint8_t* stage = stages + s * kStageBytes;
+                const uint32_t glo = wlo + static_cast<uint32_t>(b0 * bb);
+                const uint8_t* base[4];
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const int r = 4 * q + j;
+                    base[q] = stage + r * kPieceStride + ((glo + static_cast<uint32_t>(r) * nb1lo) & 15u);
+                }
+                const int gpb = op.type == kTypeQ8_0 ? 8 : 1;
+                const int g0 = b0 / gpb;
+                const int ngroups = (nb + gpb - 1) / gpb;
+                for (int gi = cw; gi < ngroups; gi += kCW) {
+                    const int g = g0 + gi;
+                    float4 xr[NT][8];
 #pragma unroll
                     for (int n = 0; n < NT; ++n)
 #pragma unroll
-                        for (int t = 0; t < 4; ++t)
-                            xq[n][t] = (xr[n][2 * t].x + xr[n][2 * t].y) + (xr[n][2 * t].z + xr[n][2 * t].w) +
-                                       (xr[n][2 * t + 1].x + xr[n][2 * t + 1].y) +
-                                       (xr[n][2 * t + 1].z + xr[n][2 * t + 1].w);
+                        for (int f = 0; f < 8; ++f) xr[n][f] = xs4[(n * K256 + g) * 64 + f * 8 + c];
+                    if (op.type == kTypeQ8_0) {
+                        const int blk = g * 8 + c;
+                        if (blk < b0 + nb) {
 #pragma unroll
-                    for (int q = 0; q < 2; ++q) {
-                        const int r = 4 * q + j;
-                        const uintptr_t gaddr = reinterpret_cast<uintptr_t>(op.w + (r0 + r) * op.w_nb1 + b0 * bb);
-                        const uint8_t* base = stage + r * kPieceStride + (gaddr & 15);
-                        item_q6_k<NT>(base + (g - b0) * 210, c, xr, xq, acc[q]);
+                            for (int q = 0; q < 4; ++q) item_q8_0<NT>(base[q] + (blk - b0) * 34, xr, acc[q]);
+                        }
+                    } else {
+                        float xq[NT][4];
+#pragma unroll
+                        for (int n = 0; n < NT; ++n)
+#pragma unroll
+                            for (int t = 0; t < 4; ++t)
+                                xq[n][t] = (xr[n][2 * t].x + xr[n][2 * t].y) + (xr[n][2 * t].z + xr[n][2 * t].w) +
+                                           (xr[n][2 * t + 1].x + xr[n][2 * t + 1].y) +
+                                           (xr[n][2 * t + 1].z + xr[n][2 * t + 1].w);
+#pragma unroll
+                        for (int q = 0; q < 4; ++q) item_q6_k<NT>(base[q] + (g - b0) * 210, c, xr, xq, acc[q]);
                     }
                 }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&empty[s]);
             }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&empty[s]);
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+#pragma unroll
+                for (int n = 0; n < NT; ++n) {
+                    float v = acc[q][n];
+                    v += __shfl_xor_sync(0xffffffffu, v, 1);
+                    v += __shfl_xor_sync(0xffffffffu, v, 2);
+                    v += __shfl_xor_sync(0xffffffffu, v, 4);
+                    if (c == 0) red[((rb * kCW + cw) * kRows + 4 * q + j) * NT + n] = v;
+                }
         }
-        // ---- reduce: 8 lanes of a row, then the 8 consumer warps ----
-#pragma unroll
-        for (int q = 0; q < 2; ++q)
-#pragma unroll
-            for (int n = 0; n < NT; ++n) {
-                float v = acc[q][n];
-                v += __shfl_xor_sync(0xffffffffu, v, 1);
-                v += __shfl_xor_sync(0xffffffffu, v, 2);
-                v += __shfl_xor_sync(0xffffffffu, v, 4);
-                if (c == 0) red[((rb * kCW + cw) * kRows + 4 * q + j) * NT + n] = v;
-            }
         consumers_sync();
-        if (ct < kRows * op.N && ct < kRows * NT) {
-            const int r = ct / op.N, n = ct % op.N;
+        if (ct < kRows * N) {
+            const int r = ct / N, n = ct % N;
             if (r0 + r < op.M) {
                 float v = 0.f;
 #pragma unroll
@@ -487,10 +611,9 @@ __global__ void __launch_bounds__(kThreads, 2) stream_gemv_kernel(const __grid_c
     }
 }
 
-template <int NT>
-size_t smem_bytes(int stages, int x_floats) {
-    return static_cast<size_t>(stages) * kStageBytes + 4ull * x_floats + 4ull * 2 * kCW * kRows * NT +
-           16ull * kMaxStages + 16;
+size_t smem_bytes(int stages, int x_bytes) {
+    return static_cast<size_t>(stages) * kStageBytes + static_cast<size_t>(x_bytes) + 2ull * kTabBytes +
+           4ull * 2 * kCW * kRows * kMaxNT + 4ull * 2 * kMaxNT + 16ull * kMaxStages + 16;
 }
 
 }  // namespace
@@ -505,7 +628,7 @@ bool stream_supported(const MulMatOp* ops, int n_ops) {
         if (o.K % 256 != 0) return false;  // whole 256-element groups (Q8_0 too)
         if (o.K > 16384) return false;
         if (o.type == kTypeQ4_K && ((reinterpret_cast<uintptr_t>(o.w) | static_cast<uintptr_t>(o.w_nb1)) & 15))
-            return false;  // 16-byte header/quant loads from shared memory
+            return false;  // 16-byte header loads from shared memory
         if ((reinterpret_cast<uintptr_t>(o.x) | static_cast<uintptr_t>(o.x_nb1)) & 15) return false;
     }
     return true;
@@ -514,7 +637,7 @@ bool stream_supported(const MulMatOp* ops, int n_ops) {
 int launch_stream(const MulMatOp* ops, int n_ops, cudaStream_t stream, int num_sms) {
     SList L{};
     L.n_ops = n_ops;
-    int units = 0, max_n = 1, x_floats = 0;
+    int units = 0, max_n = 1, x_bytes = 0;
     for (int i = 0; i < n_ops; ++i) {
         const MulMatOp& o = ops[i];
         SOp& s = L.op[i];
@@ -529,29 +652,29 @@ int launch_stream(const MulMatOp* ops, int n_ops, cudaStream_t stream, int num_s
         s.K = o.K;
         s.N = o.N;
         s.unit_begin = units;
-        const int bb = block_bytes(o.type), be = block_elems(o.type);
-        const int nblocks = o.K / be;
-        int max_blocks = kPieceCap / bb;
-        if (o.type == kTypeQ8_0) max_blocks = max_blocks / 8 * 8;  // whole 8-block groups per segment
-        const int nseg = (nblocks + max_blocks - 1) / max_blocks;
+        const int nblocks = o.K / block_elems(o.type);
+        const int cap = o.type == kTypeQ4_K ? kQ4kSegBlocks : (o.type == kTypeQ6_K ? kQ6kSegBlocks : kQ80SegBlocks);
+        const int nseg = (nblocks + cap - 1) / cap;
         int seg = (nblocks + nseg - 1) / nseg;
         if (o.type == kTypeQ8_0) seg = (seg + 7) / 8 * 8;
         s.seg_blocks = seg;
         s.nseg = (nblocks + seg - 1) / seg;
         units += (o.M + kRows - 1) / kRows;
         max_n = o.N > max_n ? o.N : max_n;
-        x_floats = (o.K * o.N > x_floats) ? o.K * o.N : x_floats;
+        const int xb = o.type == kTypeQ4_K ? (o.K / 256) * 16 * 8 * o.N * 8 + (o.K / 32) * o.N * 4 : 4 * o.K * o.N;
+        x_bytes = xb > x_bytes ? xb : x_bytes;
     }
+    x_bytes = (x_bytes + 15) / 16 * 16;
     L.total_units = units;
-    L.x_floats = x_floats;
-    const int NT = max_n <= 1 ? 1 : 2;
-    const size_t fixed = (NT == 1 ? smem_bytes<1>(0, x_floats) : smem_bytes<2>(0, x_floats));
-    int stages = static_cast<int>((static_cast<size_t>(kSmemBudget) - fixed) / kStageBytes);
-    if (fixed > static_cast<size_t>(kSmemBudget)) stages = 0;
+    L.x_bytes = x_bytes;
+    const size_t fixed = smem_bytes(0, x_bytes);
+    int stages = fixed >= static_cast<size_t>(kSmemBudget)
+                     ? 0
+                     : static_cast<int>((static_cast<size_t>(kSmemBudget) - fixed) / kStageBytes);
     stages = stages > kMaxStages ? kMaxStages : stages;
     if (stages < 2) stages = 2;
     L.stages = stages;
-    const size_t smem = NT == 1 ? smem_bytes<1>(stages, x_floats) : smem_bytes<2>(stages, x_floats);
+    const size_t smem = smem_bytes(stages, x_bytes);
     if (smem > 227 * 1024) return -static_cast<int>(cudaErrorInvalidValue);
     const int grid = units < num_sms ? units : num_sms;
 
@@ -566,7 +689,7 @@ int launch_stream(const MulMatOp* ops, int n_ops, cudaStream_t stream, int num_s
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     cudaError_t e;
-    if (NT == 1) {
+    if (max_n <= 1) {
         static bool configured = false;
         if (!configured) {
             cudaFuncSetAttribute(stream_gemv_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
