@@ -60,8 +60,8 @@ constexpr int kQ4kSegBlocks = 8;              // 1152 B
 constexpr int kQ6kSegBlocks = 5;              // 1050 B (+ window slack)
 constexpr int kQ80SegBlocks = 32;             // 1088 B, whole 8-block groups
 constexpr int kTabBytes = kRows * kQ4kSegBlocks * 4 * 16;  // Q4_K scale table, one buffer
-constexpr uint32_t kSpinLimit = 1u << 22;
-constexpr int kSmemBudget = 200 * 1024;
+constexpr uint32_t kSpinLimit = 1u << 16;    // polls of up to ~0.1 ms each
+constexpr int kSmemBudget = 112 * 1024;       // two CTAs per SM: this launch and the next (PDL)
 
 struct SOp {
     const uint8_t* w;
@@ -90,14 +90,16 @@ __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
 }
 
+// try_wait with a suspend-time hint: the thread sleeps (up to ~0.1 ms) until
+// the phase completes instead of spinning on issue slots.
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}"
         : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(parity)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(100000u)
         : "memory");
     return ok != 0;
 }
@@ -309,7 +311,7 @@ __device__ __forceinline__ float limb_scale(float maxabs) {
 }
 
 template <int NT>
-__global__ void __launch_bounds__(kThreads, 1) stream_gemv_kernel(const __grid_constant__ SList L) {
+__global__ void __maxnreg__(112) stream_gemv_kernel(const __grid_constant__ SList L) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int S = L.stages;
     uint8_t* stages = smem;
@@ -334,38 +336,35 @@ __global__ void __launch_bounds__(kThreads, 1) stream_gemv_kernel(const __grid_c
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
     if (warp == 0) {
-        // ---------------- producer ----------------
-        if (lane == 0) {
-            const uint64_t policy = evict_first_policy();
-            uint32_t it = 0;
-            int oi = 0;
-            for (int u = blockIdx.x; u < L.total_units; u += gridDim.x) {
-                while (oi + 1 < L.n_ops && u >= L.op[oi + 1].unit_begin) ++oi;
-                const SOp& op = L.op[oi];
-                const int bb = block_bytes_of(op.type);
-                const int nblocks = op.K / block_elems_of(op.type);
-                const int r0 = (u - op.unit_begin) * kRows;
-                const int nrows = min(kRows, op.M - r0);
-                const uint8_t* wrow0 = op.w + static_cast<int64_t>(r0) * op.w_nb1;
-                for (int sg = 0; sg < op.nseg; ++sg, ++it) {
-                    const int s = it % S;
-                    if (!mbar_wait(&empty[s], ((it / S) & 1) ^ 1, 1u, poisoned)) return;
-                    const int b0 = sg * op.seg_blocks;
-                    const int nbytes = min(op.seg_blocks, nblocks - b0) * bb;
-                    uint32_t total = 0;
-                    for (int r = 0; r < nrows; ++r) {
-                        const uintptr_t g = reinterpret_cast<uintptr_t>(wrow0 + r * op.w_nb1 + b0 * bb);
-                        total += static_cast<uint32_t>(((g + nbytes + 15) & ~uintptr_t(15)) - (g & ~uintptr_t(15)));
-                    }
-                    mbar_arrive_expect_tx(&full[s], total);
-                    for (int r = 0; r < nrows; ++r) {
-                        const uintptr_t g = reinterpret_cast<uintptr_t>(wrow0 + r * op.w_nb1 + b0 * bb);
-                        const uintptr_t ga = g & ~uintptr_t(15);
-                        const uint32_t bytes = static_cast<uint32_t>(((g + nbytes + 15) & ~uintptr_t(15)) - ga);
-                        bulk_g2s(stages + s * kStageBytes + r * kPieceStride, reinterpret_cast<const void*>(ga), bytes,
-                                 &full[s], policy);
-                    }
-                }
+        // ---------------- producer: lane r issues row r's copy ----------------
+        const uint64_t policy = evict_first_policy();
+        uint32_t it = 0;
+        int oi = 0;
+        for (int u = blockIdx.x; u < L.total_units; u += gridDim.x) {
+            while (oi + 1 < L.n_ops && u >= L.op[oi + 1].unit_begin) ++oi;
+            const SOp& op = L.op[oi];
+            const int bb = block_bytes_of(op.type);
+            const int nblocks = op.K / block_elems_of(op.type);
+            const int r0 = (u - op.unit_begin) * kRows;
+            const int nrows = min(kRows, op.M - r0);
+            const bool active = lane < nrows;
+            const uintptr_t grow = reinterpret_cast<uintptr_t>(op.w + static_cast<int64_t>(r0 + (active ? lane : 0)) * op.w_nb1);
+            for (int sg = 0; sg < op.nseg; ++sg, ++it) {
+                const int s = it % S;
+                int ok = 1;
+                if (lane == 0) ok = mbar_wait(&empty[s], ((it / S) & 1) ^ 1, 1u, poisoned);
+                if (!__shfl_sync(0xffffffffu, ok, 0)) return;
+                const int b0 = sg * op.seg_blocks;
+                const int nbytes = min(op.seg_blocks, nblocks - b0) * bb;
+                const uintptr_t g = grow + static_cast<uintptr_t>(b0 * bb);
+                const uintptr_t ga = g & ~uintptr_t(15);
+                const uint32_t bytes = active ? static_cast<uint32_t>(((g + nbytes + 15) & ~uintptr_t(15)) - ga) : 0u;
+                const uint32_t total = __reduce_add_sync(0xffffffffu, bytes);
+                if (lane == 0) mbar_arrive_expect_tx(&full[s], total);
+                __syncwarp();
+                if (active)
+                    bulk_g2s(stages + s * kStageBytes + lane * kPieceStride, reinterpret_cast<const void*>(ga), bytes,
+                             &full[s], policy);
             }
         }
         return;
@@ -388,68 +387,106 @@ __global__ void __launch_bounds__(kThreads, 1) stream_gemv_kernel(const __grid_c
         if (staged < 0 || L.op[staged].x != op.x || L.op[staged].type != op.type || L.op[staged].K != K ||
             L.op[staged].N != N || L.op[staged].x_nb1 != op.x_nb1) {
             consumers_sync();
+            const uint8_t* xb = reinterpret_cast<const uint8_t*>(op.x);
+            const int per_tok4 = K / 4;           // float4 per vector (a multiple of 64)
+            const int total4 = per_tok4 * N;
+            constexpr int kBatch = 4;             // float4 loads in flight per thread
             if (tc) {
-                // per-vector power-of-two scale: warp n finds max|x_n|
-                if (cw < N) {
-                    const float* xp = reinterpret_cast<const float*>(reinterpret_cast<const uint8_t*>(op.x) + cw * op.x_nb1);
-                    float mx = 0.f;
-                    for (int k = lane * 4; k < K; k += 128) {
-                        const float4 v = __ldg(reinterpret_cast<const float4*>(xp + k));
-                        mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+                // pass 1: per-vector max|x| -> power-of-two scale s (loads batched)
+                float mx[kMaxNT] = {0.f, 0.f};
+                for (int base = 0; base < total4; base += kBatch * kCW * 32) {
+                    float4 v[kBatch];
+#pragma unroll
+                    for (int i = 0; i < kBatch; ++i) {
+                        const int idx = base + i * kCW * 32 + ct;
+                        if (idx < total4)
+                            v[i] = __ldg(reinterpret_cast<const float4*>(xb + (idx / per_tok4) * op.x_nb1) + idx % per_tok4);
                     }
 #pragma unroll
-                    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-                    if (lane == 0) {
-                        const float sc = limb_scale(mx);
-                        xscale[cw] = sc;
-                        xscale[kMaxNT + cw] = 1.f / sc;
+                    for (int i = 0; i < kBatch; ++i) {
+                        const int idx = base + i * kCW * 32 + ct;
+                        if (idx < total4) {
+                            const float m = fmaxf(fmaxf(fabsf(v[i].x), fabsf(v[i].y)), fmaxf(fabsf(v[i].z), fabsf(v[i].w)));
+                            if (idx < per_tok4) mx[0] = fmaxf(mx[0], m);
+                            else mx[1] = fmaxf(mx[1], m);
+                        }
                     }
+                }
+#pragma unroll
+                for (int n = 0; n < kMaxNT; ++n) {
+#pragma unroll
+                    for (int o = 16; o > 0; o >>= 1) mx[n] = fmaxf(mx[n], __shfl_xor_sync(0xffffffffu, mx[n], o));
+                    if (lane == 0) red[n * kCW + cw] = mx[n];
                 }
                 consumers_sync();
-                // B fragments: entry e = ((b*4 + p)*2 + j)*2 + h, lanes 0..8N-1
+                if (ct < N) {
+                    float m = 0.f;
+#pragma unroll
+                    for (int w2 = 0; w2 < kCW; ++w2) m = fmaxf(m, red[ct * kCW + w2]);
+                    const float sc = limb_scale(m);
+                    xscale[ct] = sc;
+                    xscale[kMaxNT + ct] = 1.f / sc;
+                }
+                consumers_sync();
+                // pass 2 (L1-resident reload): f16 limbs in B-fragment order, entry
+                // e = ((b*4 + p)*2 + j)*2 + h, lanes 0..8N-1, and the sub-block sums
+                // X of the unscaled x for the min term (8 consecutive lanes hold one
+                // 32-element sub-block).
                 uint2* xB = reinterpret_cast<uint2*>(xsm);
                 const int lanes = 8 * N;
-                const int entries = (K / 256) * 16;
-                for (int idx = ct; idx < entries * lanes; idx += kCW * 32) {
-                    const int Lc = idx % lanes, e = idx / lanes;
-                    const int h = e & 1, jj = (e >> 1) & 1, p = (e >> 2) & 3, b = e >> 4;
-                    const int gp = Lc >> 2, cp = Lc & 3, t = gp >> 1, limb = gp & 1;
-                    const float* xp = reinterpret_cast<const float*>(reinterpret_cast<const uint8_t*>(op.x) + t * op.x_nb1) +
-                                      b * 256 + 64 * p + 32 * h + 16 * jj + 4 * cp;
-                    const float4 v = __ldg(reinterpret_cast<const float4*>(xp));
-                    const float sc = xscale[t];
-                    __half h0, l0, h1, l1, h2, l2, h3, l3;
-                    limbs(v.x * sc, h0, l0);
-                    limbs(v.y * sc, h1, l1);
-                    limbs(v.z * sc, h2, l2);
-                    limbs(v.w * sc, h3, l3);
-                    // b0 = (k 2c, 2c+1) <- elements (4c, 4c+2); b1 = (2c+8, 2c+9) <- (4c+1, 4c+3)
-                    xB[idx] = limb == 0 ? make_uint2(pack_h2(h0, h2), pack_h2(h1, h3))
-                                        : make_uint2(pack_h2(l0, l2), pack_h2(l1, l3));
-                }
-                // sub-block sums of x (unscaled f32) for the min term
-                float* Xs = reinterpret_cast<float*>(xsm + entries * lanes * 8);
-                const int nsub = K / 32;
-                for (int idx = ct; idx < nsub * N; idx += kCW * 32) {
-                    const int t = idx / nsub, sbk = idx % nsub;
-                    const float* xp = reinterpret_cast<const float*>(reinterpret_cast<const uint8_t*>(op.x) + t * op.x_nb1) +
-                                      32 * sbk;
-                    float a = 0.f;
+                float* Xs = reinterpret_cast<float*>(xsm + (K / 256) * 16 * lanes * 8);
+                for (int base = 0; base < total4; base += kBatch * kCW * 32) {
+                    float4 v[kBatch];
 #pragma unroll
-                    for (int i = 0; i < 8; ++i) {
-                        const float4 v = __ldg(reinterpret_cast<const float4*>(xp + 4 * i));
-                        a += (v.x + v.y) + (v.z + v.w);
+                    for (int i = 0; i < kBatch; ++i) {
+                        const int idx = base + i * kCW * 32 + ct;
+                        if (idx < total4)
+                            v[i] = __ldg(reinterpret_cast<const float4*>(xb + (idx / per_tok4) * op.x_nb1) + idx % per_tok4);
                     }
-                    Xs[idx] = a;
+#pragma unroll
+                    for (int i = 0; i < kBatch; ++i) {
+                        const int idx = base + i * kCW * 32 + ct;
+                        if (idx < total4) {  // warp-uniform: total4 is a multiple of 64
+                            const int t = idx / per_tok4, k = 4 * (idx % per_tok4);
+                            const int b = k >> 8, r = k & 255, p = r >> 6, h = (r >> 5) & 1, jj = (r >> 4) & 1;
+                            const int cp = (r >> 2) & 3;
+                            const int e = ((b * 4 + p) * 2 + jj) * 2 + h;
+                            const float sc = xscale[t];
+                            __half h0, l0, h1, l1, h2, l2, h3, l3;
+                            limbs(v[i].x * sc, h0, l0);
+                            limbs(v[i].y * sc, h1, l1);
+                            limbs(v[i].z * sc, h2, l2);
+                            limbs(v[i].w * sc, h3, l3);
+                            // b0 = (k 2c, 2c+1) <- elements (4c, 4c+2); b1 = (2c+8, 2c+9) <- (4c+1, 4c+3)
+                            xB[e * lanes + 4 * (2 * t) + cp] = make_uint2(pack_h2(h0, h2), pack_h2(h1, h3));
+                            xB[e * lanes + 4 * (2 * t + 1) + cp] = make_uint2(pack_h2(l0, l2), pack_h2(l1, l3));
+                            float a = (v[i].x + v[i].y) + (v[i].z + v[i].w);
+                            a += __shfl_xor_sync(0xffffffffu, a, 1);
+                            a += __shfl_xor_sync(0xffffffffu, a, 2);
+                            a += __shfl_xor_sync(0xffffffffu, a, 4);
+                            if ((ct & 7) == 0) Xs[t * (K / 32) + (k >> 5)] = a;
+                        }
+                    }
                 }
             } else {
                 float4* xs4 = reinterpret_cast<float4*>(xsm);
-                const int per_tok = (K / 256) * 64;
-                for (int idx = ct; idx < per_tok * N; idx += kCW * 32) {
-                    const int n = idx / per_tok, r = idx % per_tok;
-                    const int g = r >> 6, f = (r >> 3) & 7, cc = r & 7;
-                    const float* xp = reinterpret_cast<const float*>(reinterpret_cast<const uint8_t*>(op.x) + n * op.x_nb1);
-                    xs4[idx] = __ldg(reinterpret_cast<const float4*>(xp + g * 256 + chunk_elem(op.type, cc, f)));
+                for (int base = 0; base < total4; base += kBatch * kCW * 32) {
+                    float4 v[kBatch];
+#pragma unroll
+                    for (int i = 0; i < kBatch; ++i) {
+                        const int idx = base + i * kCW * 32 + ct;
+                        if (idx < total4) {
+                            const int n = idx / per_tok4, r = idx % per_tok4;
+                            const int g = r >> 6, f = (r >> 3) & 7, cc = r & 7;
+                            v[i] = __ldg(reinterpret_cast<const float4*>(
+                                reinterpret_cast<const float*>(xb + n * op.x_nb1) + g * 256 + chunk_elem(op.type, cc, f)));
+                        }
+                    }
+#pragma unroll
+                    for (int i = 0; i < kBatch; ++i) {
+                        const int idx = base + i * kCW * 32 + ct;
+                        if (idx < total4) xs4[idx] = v[i];
+                    }
                 }
             }
             consumers_sync();
