@@ -240,6 +240,7 @@ def test_run_ops_grouped_qkv(runtime):
                                            [jsep.meta_for(h0, qtype, (3072, M, 1, 1)), jsep.meta_for(hx, 0, (3072, 1, 1, 1))]))
     k0 = runtime.counters()["kernels_launched"]
     assert runtime.run_ops(descs) == 0, jsep.last_error()
+    # one kernel launch for all three
     assert runtime.counters()["kernels_launched"] == k0 + 1
     for (qtype, M), w, (h0, hd) in zip(specs, ws, hs):
         got = runtime.data_manager.read(hd, 0, 4 * M).view(np.float32).reshape(1, M)

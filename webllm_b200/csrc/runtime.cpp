@@ -49,7 +49,7 @@ struct State {
     int32_t next_handle = 1;
     wllm_counters counters{};
     std::string last_error;
-    void* scratch = nullptr;
+    void* scratch = nullptr;  // divert target for aliased dst
     uint64_t scratch_cap = 0;
     std::unordered_map<int32_t, AsyncRead> reads;
     int32_t next_request = 1;
