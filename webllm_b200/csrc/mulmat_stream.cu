@@ -236,9 +236,12 @@ __device__ __forceinline__ float limb_scale(float maxabs) {
     return __uint_as_float(static_cast<uint32_t>(se) << 23);
 }
 
-// Scale-table entry for (row, block, pair p): d*sc*2^24 (low sub-block),
-// d*sc*2^20 (high sub-block, whose quants enter as 16 q), dmin*m low, high.
-__device__ __forceinline__ void q4k_decode_scales(const uint8_t* blk, float4* out /* [4] */) {
+// Scale-table entries of one (row, block), pair p at out[16 p]: d*sc*2^24
+// (low sub-block), d*sc*2^20 (high sub-block, whose quants enter as 16 q),
+// dmin*m low, high. The table of a stage is [block][pair][16 rows], so the
+// 16 rows a decoding half-warp writes and the 8 rows an MMA quad-row group
+// reads are consecutive float4 (no bank conflicts).
+__device__ __forceinline__ void q4k_decode_scales(const uint8_t* blk, float4* out) {
     const uint4 hdr = *reinterpret_cast<const uint4*>(blk);
     const uint32_t s0 = hdr.y, s1 = hdr.z, s2 = hdr.w;
     const uint32_t sc_lo4 = s0 & 0x3F3F3F3Fu, m_lo4 = s1 & 0x3F3F3F3Fu;
@@ -254,14 +257,14 @@ __device__ __forceinline__ void q4k_decode_scales(const uint8_t* blk, float4* ou
     for (int p = 0; p < 4; ++p) {
         const uint32_t scw = p < 2 ? sc_lo4 : sc_hi4, mw = p < 2 ? m_lo4 : m_hi4;
         const uint32_t b = 2 * (p & 1);  // bytes b, b+1 of the word: sub-blocks 2p, 2p+1
-        out[p] = make_float4(d24 * byte_f(scw, 0x7440u | b), d20 * byte_f(scw, 0x7440u | (b + 1)),
+        out[16 * p] = make_float4(d24 * byte_f(scw, 0x7440u | b), d20 * byte_f(scw, 0x7440u | (b + 1)),
                              dmin * byte_f(mw, 0x7440u | b), dmin * byte_f(mw, 0x7440u | (b + 1)));
     }
 }
 
 // Q4_K: one pair p (64 elements) of one block for rows g, g+8 of the unit.
 // Returns (sum A*(D_hi+D_lo) row g, same row g+8, sum dmin*m*X row g, row g+8).
-__device__ __forceinline__ float4 q4_pair(const uint8_t* blk_g, int row8, const float4* tab_g, int tab8,
+__device__ __forceinline__ float4 q4_pair(const uint8_t* blk_g, int row8, const float4* tab_g,
                                           const uint2* xe, const float* xs, int p, int c, int lane, int lanes,
                                           bool has_tok) {
     const uint8_t* rq = blk_g + 16 + 32 * p + 4 * c;
@@ -274,7 +277,7 @@ __device__ __forceinline__ float4 q4_pair(const uint8_t* blk_g, int row8, const 
     const uint2* xp = xe + p * 4 * lanes;
     const uint2 bl0 = act ? xp[0 * lanes] : z, bh0 = act ? xp[1 * lanes] : z;
     const uint2 bl1 = act ? xp[2 * lanes] : z, bh1 = act ? xp[3 * lanes] : z;
-    const float4 sg = tab_g[p], sg8 = tab_g[tab8 + p];
+    const float4 sg = tab_g[16 * p], sg8 = tab_g[16 * p + 8];
     const float xlo = has_tok ? xs[2 * p] : 0.f, xhi = has_tok ? xs[2 * p + 1] : 0.f;
     const float zero4[4] = {0.f, 0.f, 0.f, 0.f};
     const uint32_t vg0s = vg0 >> 8, vg1s = vg1 >> 8, vh0s = vh0 >> 8, vh1s = vh1 >> 8;
@@ -421,7 +424,7 @@ __device__ __forceinline__ void stage_activations(const OpInfo& op, uint8_t* xsm
             const float4* xv = reinterpret_cast<const float4*>(xb + t * op.x_nb1);
             // pass 1: max|x| (loads from L2, batched)
             float mx = 0.f;
-            for (int i0 = 0; i0 < kXF4; i0 += kB) {
+            for (int i0 = 0; i0 < kXF4 && i0 * kCW * 32 < per4; i0 += kB) {
                 float4 v[kB];
 #pragma unroll
                 for (int i = 0; i < kB; ++i) {
@@ -441,7 +444,7 @@ __device__ __forceinline__ void stage_activations(const OpInfo& op, uint8_t* xsm
             for (int w = 0; w < kCW; ++w) m = fmaxf(m, wred[w]);
             const float sc = limb_scale(m);
             // pass 2 (L1-resident reload): limbs in B-fragment order and sub-block sums
-            for (int i0 = 0; i0 < kXF4; i0 += kB) {
+            for (int i0 = 0; i0 < kXF4 && i0 * kCW * 32 < per4; i0 += kB) {
               float4 v[kB];
 #pragma unroll
               for (int i = 0; i < kB; ++i) {
@@ -481,7 +484,7 @@ __device__ __forceinline__ void stage_activations(const OpInfo& op, uint8_t* xsm
         constexpr int kB = 8;  // float4 loads in flight per thread
         for (int t = 0; t < N; ++t) {
             const float* xf = reinterpret_cast<const float*>(xb + t * op.x_nb1);
-            for (int i0 = 0; i0 < kXF4; i0 += kB) {
+            for (int i0 = 0; i0 < kXF4 && i0 * kCW * 32 < per4; i0 += kB) {
                 float4 v[kB];
 #pragma unroll
                 for (int i = 0; i < kB; ++i) {
@@ -509,7 +512,7 @@ __global__ void __maxnreg__(112) stream_gemv_kernel(const __grid_constant__ SLis
     const int SB = L.stage_bytes;
     const int TB = L.tab_blocks;                                      // table blocks per stage
     uint8_t* stages = smem;
-    float4* tabs = reinterpret_cast<float4*>(smem + S * SB);           // [S][16][TB][4]
+    float4* tabs = reinterpret_cast<float4*>(smem + S * SB);           // [S][TB][4][16]
     uint8_t* xsm = reinterpret_cast<uint8_t*>(tabs) + S * kRows * TB * 64;
     float* ubuf = reinterpret_cast<float*>(xsm + L.x_bytes);          // [kUnitSlots][kCW][16][NT]
     int* ucnt = reinterpret_cast<int*>(ubuf + kUnitSlots * kCW * kRows * NT);
@@ -617,7 +620,7 @@ __global__ void __maxnreg__(112) stream_gemv_kernel(const __grid_constant__ SLis
                 float4* tab = tabs + s * kRows * TB * 4;
                 for (int e = lane; e < kRows * nb; e += 32) {
                     const int r = e & 15, bl = e >> 4;
-                    q4k_decode_scales(stage + r * op.wbox + bl * 144, tab + (r * TB + bl) * 4);
+                    q4k_decode_scales(stage + r * op.wbox + bl * 144, tab + bl * 64 + r);
                 }
             }
             __syncwarp();
@@ -668,17 +671,17 @@ __global__ void __maxnreg__(112) stream_gemv_kernel(const __grid_constant__ SLis
                 const int nb = min(op.seg_blocks, nblocks - b0);
                 const uint8_t* stage = stages + s * SB;
                 const float4* tab = tabs + s * kRows * TB * 4;
-                const int row8 = 8 * op.wbox, tab8 = 8 * TB * 4;
+                const int row8 = 8 * op.wbox;
                 for (int i = (cw - static_cast<int>(item_base % kCW) + kCW) % kCW; i < nb; i += kCW) {
                     const int bg = b0 + i;
                     const uint8_t* blk_g = stage + g * op.wbox + i * 144;
-                    const float4* tab_g = tab + (g * TB + i) * 4;
+                    const float4* tab_g = tab + i * 64 + g;
                     const uint2* xe = xB + (bg * 16) * lanes + (lane < lanes ? lane : 0);
                     const float* xs = Xs + bg * 8;
-                    const float4 r0v = q4_pair(blk_g, row8, tab_g, tab8, xe, xs, 0, c, lane, lanes, has_tok);
-                    const float4 r1v = q4_pair(blk_g, row8, tab_g, tab8, xe, xs, 1, c, lane, lanes, has_tok);
-                    const float4 r2v = q4_pair(blk_g, row8, tab_g, tab8, xe, xs, 2, c, lane, lanes, has_tok);
-                    const float4 r3v = q4_pair(blk_g, row8, tab_g, tab8, xe, xs, 3, c, lane, lanes, has_tok);
+                    const float4 r0v = q4_pair(blk_g, row8, tab_g, xe, xs, 0, c, lane, lanes, has_tok);
+                    const float4 r1v = q4_pair(blk_g, row8, tab_g, xe, xs, 1, c, lane, lanes, has_tok);
+                    const float4 r2v = q4_pair(blk_g, row8, tab_g, xe, xs, 2, c, lane, lanes, has_tok);
+                    const float4 r3v = q4_pair(blk_g, row8, tab_g, xe, xs, 3, c, lane, lanes, has_tok);
                     accm_g += (r0v.x + r1v.x) + (r2v.x + r3v.x);
                     accm_g8 += (r0v.y + r1v.y) + (r2v.y + r3v.y);
                     accn_g += (r0v.z + r1v.z) + (r2v.z + r3v.z);
