@@ -3,35 +3,33 @@
 //
 // Data movement. The weight matrix is cut into units of 16 rows (one MMA
 // tile); each unit's rows into segments of at most 9 Q4_K / 6 Q6_K / 32 Q8_0
-// blocks. Warp 0 (producer) moves each (unit, segment) into a ring of shared
+// blocks. Warp 0 (copy warp) moves each (unit, segment) into a ring of shared
 // memory stages with ONE 2D tensor-map TMA copy (16 rows x the segment,
 // rounded out to 16-byte columns; evict-first L2 policy, each weight byte is
-// read once). Under load a box takes ~2 us to land, so a CTA keeps several
-// stages in flight and two CTAs share an SM: ~140 KB of weights in flight per
-// SM, enough to run HBM at full rate while the consumers wait for the
-// activations of a dependent launch. Row layouts whose stride is not a
-// multiple of 16 bytes (Q6_K with an odd number of 256-blocks per 8) fall back
-// to one bulk copy per row. When a Q4_K stage lands the producer decodes its
-// 6-bit scales and mins into a float table and releases the stage through a
-// `ready` mbarrier. Eight consumer warps take work items (one block of a unit,
-// all 16 rows) round-robin from the CTA's item sequence without CTA-wide
-// barriers; the per-warp partial sums of a unit meet in shared memory and the
-// warp that finishes the unit last writes it out (fixed summation order, so
-// results are deterministic).
+// read once). Row layouts whose stride is not a multiple of 16 bytes fall back
+// to one bulk copy per row. The other warps (consumers) take work items (one
+// block of a unit, all 16 rows) round-robin from the CTA's item sequence
+// without CTA-wide barriers; the per-warp partial sums of a unit meet in
+// shared memory and the warp that finishes the unit last writes it out (fixed
+// summation order, so results are deterministic).
 //
-// Activations. After griddepcontrol.wait each CTA loads x with one L2 round
-// trip and builds its shared-memory image: for Q4_K the tensor-core B
-// fragments (two f16 limbs hi = f16(x s), lo = f16(x s - hi), s a power of two
-// per vector so x s stays inside f16 range) and the sub-block sums of x; for
-// Q6_K/Q8_0 a bank-conflict-free permutation of x.
-//
-// Q4_K runs on tensor cores (mma.sync m16n8k16, f16 x f16 -> f32). A 4-bit
-// quant enters as the exact f16 subnormal q * 2^-24 (one LOP3 per two quants:
-// low nibbles (v & 0x000F000F), high nibbles (v & 0x00F000F0) = 16 q * 2^-24),
-// so every product is exact and 22 bits of x take part. Each 32-element
-// sub-block is its own accumulator chain of two k16 MMAs, scaled in f32 by
-// d*sc from the table; the min term dmin*m*sum(x) is subtracted in f32. The k
-// order inside an MMA is a fixed permutation shared by A and B.
+// Q4_K runs on integer tensor cores (mma.sync m16n8k32, u8 x s8 -> s32):
+//  - weights: ldmatrix hands each lane the bytes of its fragment; the low
+//    nibbles (v & 0x0F0F0F0F, sub-block 2p) and the high nibbles kept in place
+//    (v & 0xF0F0F0F0 = 16 q, sub-block 2p+1) are the A operands, one LOP each
+//    per four quants;
+//  - activations: per 256-element block and vector, x = (l0 + l1/128) / s with
+//    s = 127 / max|x| and int8 limbs l0 = rint(x s), l1 = rint(128 (x s - l0))
+//    (|error| <= max|x| / 32512); the two limbs of each vector are two B
+//    columns, so the MMA's eight columns hold up to four vectors;
+//  - each 32-element sub-block is one MMA; its s32 result is scaled by the
+//    sub-block's 6-bit scale in integer (16 sc for low-nibble sub-blocks, whose
+//    quants entered unscaled), accumulated exactly over the block, then
+//    converted once: y += d / (16 s) * (acc_l0 + acc_l1 / 128);
+//  - the min term dmin * m * sum(x) uses exact f32 sub-block sums of x, split
+//    over the four lanes of an MMA row group and summed once per unit.
+// Each consumer warp decodes the scales of its own item into a small
+// double-buffered table in shared memory (no cross-warp hand-off).
 //
 // Q6_K and Q8_0 run on CUDA cores: lanes 8j..8j+7 take row 4q+j (q = 0..3),
 // lane chunk c = lane%8 owns 32 elements of a 256-element block (Q6_K) or one
@@ -40,7 +38,7 @@
 // runs on packed FFMA2 and the quant sum is 128 (S - X), X = sum x.
 //
 // Launch: programmatic dependent launch. CTAs trigger their dependents at
-// entry; the producer streams weights (never written by a preceding kernel)
+// entry; the copy warp streams weights (never written by a preceding kernel)
 // at once; consumers execute griddepcontrol.wait before reading activations or
 // writing outputs. Every mbarrier wait is bounded; on timeout the CTA records
 // an error code for the host and stops waiting, so it still ends.
@@ -59,13 +57,14 @@ __device__ unsigned int g_stream_error = 0;
 namespace {
 
 constexpr int kCW = 8;                        // consumer warps
-constexpr int kThreads = 32 * (kCW + 2);      // + copy warp + hand-off warp
+constexpr int kThreads = 32 * (kCW + 1);      // + copy warp
 constexpr int kRows = 16;                     // rows per unit (one MMA m-tile)
 constexpr int kQ4kSegBlocks = 9;              // <= 1296 B per row and stage
 constexpr int kQ6kSegBlocks = 6;              // <= 1260 B (+ 16-byte window slack)
 constexpr int kQ80SegBlocks = 32;             // 1088 B, whole 8-block groups
 constexpr int kMaxStages = 8;
 constexpr int kUnitSlots = kMaxStages + 2;    // units a CTA can have in flight, plus margin
+constexpr int kXPad = 16;                     // bytes after each int8 activation column (ldmatrix banks)
 constexpr int kMaxNT = 2;
 constexpr int kXF4 = 16;                      // float4 of x per consumer thread: K <= 16384
 constexpr uint32_t kSpinLimit = 1u << 26;     // polls before a wait gives up (well over a second)
@@ -91,7 +90,7 @@ struct SList {
     int32_t total_units;
     int32_t stages;
     int32_t stage_bytes;  // 16 rows x the largest wbox
-    int32_t tab_blocks;   // Q4_K scale-table blocks per stage (0: no Q4_K op)
+    int32_t has_q4k;      // a Q4_K op is present: per-warp scale tables are reserved
     int32_t x_bytes;      // shared-memory bytes reserved for the activation image
 };
 
@@ -121,19 +120,46 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 // Bounded wait. If the phase does not complete in time the CTA is poisoned:
 // an error code is recorded for the host and every later wait of the CTA
 // returns at once, so all threads run to the end (results are garbage, the
-// error is reported by wllm_sync).
+// error is reported by wllm_sync). The poison flag is read once per 256
+// polls: every poll is a shared-memory operation, and polls of many warps
+// were measured to slow the copy warp's own barrier and TMA operations.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned code, volatile int* poisoned) {
     for (uint32_t i = 0; i < kSpinLimit; ++i) {
         if (mbar_try_wait(bar, parity)) return true;
-        if (*poisoned) return false;
+        if ((i & 255u) == 255u && *poisoned) return false;
     }
     *poisoned = 1;
     atomicOr(&g_stream_error, code);
     return false;
 }
 
-__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+// Warp-wide wait of a consumer warp: lane 0 polls, backing off with a short
+// sleep between polls; then every lane observes the completed phase itself
+// (one poll that succeeds at once), which orders the landed copy's bytes
+// before its reads.
+__device__ __forceinline__ void mbar_wait_warp(uint64_t* bar, uint32_t parity, unsigned code, volatile int* poisoned,
+                                               int lane) {
+    int ok = 1;
+    if (lane == 0) {
+        ok = 0;
+        for (uint32_t i = 0; i < kSpinLimit; ++i) {
+            if (mbar_try_wait(bar, parity)) {
+                ok = 1;
+                break;
+            }
+            if ((i & 255u) == 255u && *poisoned) break;
+            __nanosleep(32);
+        }
+        if (!ok && !*poisoned) {
+            *poisoned = 1;
+            atomicOr(&g_stream_error, code);
+        }
+    }
+    if (__shfl_sync(0xffffffffu, ok, 0)) (void)mbar_try_wait(bar, parity);
+}
+
+__device__ __forceinline__ void mbar_arrive_cnt(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
 }
 
 __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
@@ -169,12 +195,22 @@ __device__ __forceinline__ void consumers_sync() {
     asm volatile("bar.sync 1, %0;" ::"n"(kCW * 32) : "memory");
 }
 
-__device__ __forceinline__ void mma_f16(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
-                                        uint32_t b0, uint32_t b1, const float (&c)[4]) {
-    asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-        "{%10,%11,%12,%13};"
-        : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
-        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(c[0]), "f"(c[1]), "f"(c[2]), "f"(c[3]));
+// Four 8x8 b16 matrices from shared memory; lane l supplies the row address
+// for row l%8 of matrix l/8 and receives, of each matrix, bytes 4(l%4)..+3 of
+// row l/4.
+__device__ __forceinline__ void ldmatrix_x4(uint32_t (&r)[4], const void* row_addr) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(smem_u32(row_addr)));
+}
+
+// D = A (16x32 u8, row) * B (32x8 s8, col), s32 accumulate from zero.
+__device__ __forceinline__ void imma_u8s8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                          uint32_t b0, uint32_t b1) {
+    asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%10,%10,%10,%10};"
+        : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
 }
 
 __host__ __device__ __forceinline__ int seg_cap(int type) {
@@ -186,9 +222,18 @@ __device__ __forceinline__ int block_bytes_of(int type) {
 }
 
 // Byte layout of the shared-memory activation image.
-__host__ __device__ __forceinline__ int img_xb_bytes(int K, int N) { return (K / 256) * 16 * 8 * N * 8; }
+//  Q4_K: int8 limb columns [2N][K + kXPad] (column 2t + l = limb l of vector
+//        t), then f32 d-factors [N][K/256] (max|x| / (127 * 16) per block),
+//        then exact f32 sub-block sums [N][K/32].
+//  Q6_K / Q8_0: f32 x permuted per lane chunk, [N][K/256][8 f][8 c] float4.
+__host__ __device__ __forceinline__ int img_col_bytes(int K) { return K + kXPad; }
+__host__ __device__ __forceinline__ int img_inv_off(int K, int N) { return 2 * N * img_col_bytes(K); }
+// (16-byte aligned: the sums are read as float2)
+__host__ __device__ __forceinline__ int img_sum_off(int K, int N) {
+    return (img_inv_off(K, N) + 4 * N * (K / 256) + 15) & ~15;
+}
 __host__ __device__ __forceinline__ int img_bytes(int type, int K, int N) {
-    if (type == kTypeQ4_K) return img_xb_bytes(K, N) + N * (K / 32) * 4 + 16;  // B frags, sub-block sums, 1/s
+    if (type == kTypeQ4_K) return img_sum_off(K, N) + 4 * N * (K / 32);
     return 4 * K * N;
 }
 
@@ -216,79 +261,46 @@ __device__ __forceinline__ uint32_t lds_u32_any(const uint8_t* p) {
 }
 __device__ __forceinline__ uint32_t lds_u16(const uint8_t* p) { return *reinterpret_cast<const uint16_t*>(p); }
 
-// f16 limbs of v: hi = f16(v), lo = f16(v - hi).
-__device__ __forceinline__ void limbs(float v, __half& hi, __half& lo) {
-    hi = __float2half_rn(v);
-    lo = __float2half_rn(v - __half2float(hi));
-}
+// Scales of one Q4_K item (16 rows of one block) as the MMA lanes use them.
+struct Q4Tab {
+    int4 sc[2][kRows];    // [half h][row]: sub-blocks 4h..4h+3; 16 sc for even (low-nibble) ones
+    float2 mn[4][kRows];  // [pair c][row]: dmin*m of sub-blocks 2c, 2c+1
+    float d[kRows];
+};
 
-__device__ __forceinline__ uint32_t pack_h2(__half a, __half b) {
-    return static_cast<uint32_t>(__half_as_ushort(a)) | (static_cast<uint32_t>(__half_as_ushort(b)) << 16);
-}
-
-// Power of two s with max|x s| in [2^14, 2^15) (1 when max is 0 or not finite).
-__device__ __forceinline__ float limb_scale(float maxabs) {
-    const uint32_t bits = __float_as_uint(maxabs);
-    const int e = static_cast<int>((bits >> 23) & 0xFF);
-    if (maxabs == 0.f || e == 0xFF) return 1.f;
-    int se = 14 - (e - 127) + 127;  // exponent field of 2^(14 - e)
-    se = se < 1 ? 1 : (se > 254 ? 254 : se);
-    return __uint_as_float(static_cast<uint32_t>(se) << 23);
-}
-
-// Scale-table entries of one (row, block), pair p at out[16 p]: d*sc*2^24
-// (low sub-block), d*sc*2^20 (high sub-block, whose quants enter as 16 q),
-// dmin*m low, high. The table of a stage is [block][pair][16 rows], so the
-// 16 rows a decoding half-warp writes and the 8 rows an MMA quad-row group
-// reads are consecutive float4 (no bank conflicts).
-__device__ __forceinline__ void q4k_decode_scales(const uint8_t* blk, float4* out) {
+// Lane (row r = lane%16, half h = lane/16) decodes sub-blocks 4h..4h+3 of
+// row r's block header into the table (get_scale_min_k4 semantics,
+// src/inference/jsep/ops/matmul.ts:408-424): for j < 4 sc = s[j]&63,
+// m = s[j+4]&63; for j >= 4 sc = (s[j+4]&15) | (s[j-4]>>6)<<4,
+// m = (s[j+4]>>4) | (s[j]>>6)<<4, done four sub-blocks at a time on bytes.
+__device__ __forceinline__ void q4k_decode_item(const uint8_t* blk, int r, int h, Q4Tab& T) {
     const uint4 hdr = *reinterpret_cast<const uint4*>(blk);
-    const uint32_t s0 = hdr.y, s1 = hdr.z, s2 = hdr.w;
-    const uint32_t sc_lo4 = s0 & 0x3F3F3F3Fu, m_lo4 = s1 & 0x3F3F3F3Fu;
-    const uint32_t sc_hi4 = (s2 & 0x0F0F0F0Fu) | ((s0 >> 2) & 0x30303030u);
-    const uint32_t m_hi4 = ((s2 >> 4) & 0x0F0F0F0Fu) | ((s1 >> 2) & 0x30303030u);
     const float d = f16_bits_to_f32(hdr.x), dmin = f16_bits_to_f32(hdr.x >> 16);
-    const float d24 = d * 16777216.f, d20 = d * 1048576.f;
-    // byte -> float on the FP32 pipe: 0x4B0000bb is 2^23 + bb exactly
-    auto byte_f = [](uint32_t w, uint32_t sel) {
-        return __uint_as_float(__byte_perm(w, 0x4B000000u, sel)) - 8388608.f;
-    };
-#pragma unroll
-    for (int p = 0; p < 4; ++p) {
-        const uint32_t scw = p < 2 ? sc_lo4 : sc_hi4, mw = p < 2 ? m_lo4 : m_hi4;
-        const uint32_t b = 2 * (p & 1);  // bytes b, b+1 of the word: sub-blocks 2p, 2p+1
-        out[16 * p] = make_float4(d24 * byte_f(scw, 0x7440u | b), d20 * byte_f(scw, 0x7440u | (b + 1)),
-                             dmin * byte_f(mw, 0x7440u | b), dmin * byte_f(mw, 0x7440u | (b + 1)));
-    }
+    const uint32_t w1 = hdr.y, w2 = hdr.z, w3 = hdr.w;
+    const uint32_t sa = h ? w3 : w1, sb = h ? (w1 >> 2) : w1;
+    const uint32_t ma = h ? (w3 >> 4) : w2, mb = h ? (w2 >> 2) : w2;
+    const uint32_t scw = (sa & 0x0F0F0F0Fu) | (sb & 0x30303030u);
+    const uint32_t mw = (ma & 0x0F0F0F0Fu) | (mb & 0x30303030u);
+    T.sc[h][r] = make_int4(static_cast<int>(__byte_perm(scw, 0, 0x4440)) << 4,
+                           static_cast<int>(__byte_perm(scw, 0, 0x4441)),
+                           static_cast<int>(__byte_perm(scw, 0, 0x4442)) << 4,
+                           static_cast<int>(__byte_perm(scw, 0, 0x4443)));
+    // dmin*m exactly rounded: (2^23 + m) dmin - 2^23 dmin in one FMA (both
+    // products exact: dmin has at most 11 significant bits)
+    const float dm23 = dmin * 8388608.f;
+    const float m0 = fmaf(__uint_as_float(__byte_perm(mw, 0x4B000000u, 0x7440u)), dmin, -dm23);
+    const float m1 = fmaf(__uint_as_float(__byte_perm(mw, 0x4B000000u, 0x7441u)), dmin, -dm23);
+    const float m2 = fmaf(__uint_as_float(__byte_perm(mw, 0x4B000000u, 0x7442u)), dmin, -dm23);
+    const float m3 = fmaf(__uint_as_float(__byte_perm(mw, 0x4B000000u, 0x7443u)), dmin, -dm23);
+    T.mn[2 * h][r] = make_float2(m0, m1);
+    T.mn[2 * h + 1][r] = make_float2(m2, m3);
+    if (h == 0) T.d[r] = d;
 }
 
-// Q4_K: one pair p (64 elements) of one block for rows g, g+8 of the unit.
-// Returns (sum A*(D_hi+D_lo) row g, same row g+8, sum dmin*m*X row g, row g+8).
-__device__ __forceinline__ float4 q4_pair(const uint8_t* blk_g, int row8, const float4* tab_g,
-                                          const uint2* xe, const float* xs, int p, int c, int lane, int lanes,
-                                          bool has_tok) {
-    const uint8_t* rq = blk_g + 16 + 32 * p + 4 * c;
-    const uint32_t vg0 = *reinterpret_cast<const uint32_t*>(rq);
-    const uint32_t vg1 = *reinterpret_cast<const uint32_t*>(rq + 16);
-    const uint32_t vh0 = *reinterpret_cast<const uint32_t*>(rq + row8);
-    const uint32_t vh1 = *reinterpret_cast<const uint32_t*>(rq + row8 + 16);
-    const uint2 z = make_uint2(0u, 0u);
-    const bool act = lane < lanes;
-    const uint2* xp = xe + p * 4 * lanes;
-    const uint2 bl0 = act ? xp[0 * lanes] : z, bh0 = act ? xp[1 * lanes] : z;
-    const uint2 bl1 = act ? xp[2 * lanes] : z, bh1 = act ? xp[3 * lanes] : z;
-    const float4 sg = tab_g[16 * p], sg8 = tab_g[16 * p + 8];
-    const float xlo = has_tok ? xs[2 * p] : 0.f, xhi = has_tok ? xs[2 * p + 1] : 0.f;
-    const float zero4[4] = {0.f, 0.f, 0.f, 0.f};
-    const uint32_t vg0s = vg0 >> 8, vg1s = vg1 >> 8, vh0s = vh0 >> 8, vh1s = vh1 >> 8;
-    float dlo[4], dhi[4];
-    mma_f16(dlo, vg0 & 0x000F000Fu, vh0 & 0x000F000Fu, vg0s & 0x000F000Fu, vh0s & 0x000F000Fu, bl0.x, bl0.y, zero4);
-    mma_f16(dhi, vg0 & 0x00F000F0u, vh0 & 0x00F000F0u, vg0s & 0x00F000F0u, vh0s & 0x00F000F0u, bh0.x, bh0.y, zero4);
-    mma_f16(dlo, vg1 & 0x000F000Fu, vh1 & 0x000F000Fu, vg1s & 0x000F000Fu, vh1s & 0x000F000Fu, bl1.x, bl1.y, dlo);
-    mma_f16(dhi, vg1 & 0x00F000F0u, vh1 & 0x00F000F0u, vg1s & 0x00F000F0u, vh1s & 0x00F000F0u, bh1.x, bh1.y, dhi);
-    return make_float4(sg.x * (dlo[0] + dlo[1]) + sg.y * (dhi[0] + dhi[1]),
-                       sg8.x * (dlo[2] + dlo[3]) + sg8.y * (dhi[2] + dhi[3]), sg.z * xlo + sg.w * xhi,
-                       sg8.z * xlo + sg8.w * xhi);
+// Low bytes of four ints -> one word.
+__device__ __forceinline__ uint32_t pack_b4(int a, int b, int c, int d) {
+    return __byte_perm(__byte_perm(static_cast<uint32_t>(a), static_cast<uint32_t>(b), 0x0040u),
+                       __byte_perm(static_cast<uint32_t>(c), static_cast<uint32_t>(d), 0x0040u), 0x5410u);
 }
 
 template <int NT>
@@ -410,75 +422,60 @@ struct SeqCursor {
 };
 
 // Builds the activation image of `op` in shared memory (all consumer threads;
-// one L2 round trip per vector). `wred` holds kCW floats.
-__device__ __forceinline__ void stage_activations(const OpInfo& op, uint8_t* xsm, float* wred, int ct, int lane, int cw) {
+// one L2 round trip per vector).
+__device__ __forceinline__ void stage_activations(const OpInfo& op, uint8_t* xsm, int ct, int lane, int cw) {
     const int K = op.K, N = op.N, per4 = K / 4;
     const uint8_t* xb = reinterpret_cast<const uint8_t*>(op.x);
     if (op.type == kTypeQ4_K) {
-        const int lanes = 8 * N;
-        uint2* xB = reinterpret_cast<uint2*>(xsm);
-        float* Xs = reinterpret_cast<float*>(xsm + img_xb_bytes(K, N));
-        float* inv = reinterpret_cast<float*>(xsm + img_bytes(kTypeQ4_K, K, N) - 16);
-        constexpr int kB = 4;  // float4 loads in flight per thread
-        for (int t = 0; t < N; ++t) {
-            const float4* xv = reinterpret_cast<const float4*>(xb + t * op.x_nb1);
-            // pass 1: max|x| (loads from L2, batched)
-            float mx = 0.f;
-            for (int i0 = 0; i0 < kXF4 && i0 * kCW * 32 < per4; i0 += kB) {
-                float4 v[kB];
+        // one warp per (vector, 256-block); lane covers elements 8 lane .. 8 lane + 7
+        const int nblk = K / 256, XS = img_col_bytes(K);
+        float* dfac = reinterpret_cast<float*>(xsm + img_inv_off(K, N));
+        float* Xs = reinterpret_cast<float*>(xsm + img_sum_off(K, N));
+        constexpr int kB = 4;  // (vector, block) items per warp with loads in flight together
+        for (int tb0 = cw; tb0 < N * nblk; tb0 += kB * kCW) {
+            float4 v[kB][2];
 #pragma unroll
-                for (int i = 0; i < kB; ++i) {
-                    const int f = (i0 + i) * kCW * 32 + ct;
-                    v[i] = f < per4 ? __ldg(xv + f) : make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int q = 0; q < kB; ++q) {
+                const int tb = tb0 + q * kCW;
+                if (tb < N * nblk) {  // warp-uniform
+                    const int t = tb / nblk, b = tb - t * nblk;
+                    const float4* xv = reinterpret_cast<const float4*>(xb + t * op.x_nb1) + b * 64 + 2 * lane;
+                    v[q][0] = __ldg(xv);
+                    v[q][1] = __ldg(xv + 1);
                 }
-#pragma unroll
-                for (int i = 0; i < kB; ++i)
-                    mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v[i].x), fabsf(v[i].y)), fmaxf(fabsf(v[i].z), fabsf(v[i].w))));
             }
 #pragma unroll
-            for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-            if (lane == 0) wred[cw] = mx;
-            consumers_sync();
-            float m = 0.f;
+            for (int q = 0; q < kB; ++q) {
+                const int tb = tb0 + q * kCW;
+                if (tb >= N * nblk) break;
+                const int t = tb / nblk, b = tb - t * nblk;
+                const float e[8] = {v[q][0].x, v[q][0].y, v[q][0].z, v[q][0].w,
+                                    v[q][1].x, v[q][1].y, v[q][1].z, v[q][1].w};
+                float mx = 0.f;
 #pragma unroll
-            for (int w = 0; w < kCW; ++w) m = fmaxf(m, wred[w]);
-            const float sc = limb_scale(m);
-            // pass 2 (L1-resident reload): limbs in B-fragment order and sub-block sums
-            for (int i0 = 0; i0 < kXF4 && i0 * kCW * 32 < per4; i0 += kB) {
-              float4 v[kB];
+                for (int k = 0; k < 8; ++k) mx = fmaxf(mx, fabsf(e[k]));
 #pragma unroll
-              for (int i = 0; i < kB; ++i) {
-                  const int f = (i0 + i) * kCW * 32 + ct;
-                  v[i] = f < per4 ? __ldg(xv + f) : make_float4(0.f, 0.f, 0.f, 0.f);
-              }
+                for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+                const float sc = mx > 0.f ? 127.f / mx : 0.f;
+                int l0[8], l1[8];
 #pragma unroll
-              for (int ii = 0; ii < kB; ++ii) {
-                const int f = (i0 + ii) * kCW * 32 + ct;
-                const int i = ii;
-                if (f < per4) {  // warp-uniform: per4 is a multiple of 64
-                    const int k = 4 * f;
-                    const int b = k >> 8, r = k & 255, p = r >> 6, h = (r >> 5) & 1, jj = (r >> 4) & 1;
-                    const int cp = (r >> 2) & 3;
-                    const int e = ((b * 4 + p) * 2 + jj) * 2 + h;
-                    __half h0, l0, h1, l1, h2, l2, h3, l3;
-                    limbs(v[i].x * sc, h0, l0);
-                    limbs(v[i].y * sc, h1, l1);
-                    limbs(v[i].z * sc, h2, l2);
-                    limbs(v[i].w * sc, h3, l3);
-                    // b0 = (k 2c, 2c+1) <- elements (4c, 4c+2); b1 = (2c+8, 2c+9) <- (4c+1, 4c+3)
-                    xB[e * lanes + 4 * (2 * t) + cp] = make_uint2(pack_h2(h0, h2), pack_h2(h1, h3));
-                    xB[e * lanes + 4 * (2 * t + 1) + cp] = make_uint2(pack_h2(l0, l2), pack_h2(l1, l3));
-                    float a = (v[i].x + v[i].y) + (v[i].z + v[i].w);
-                    a += __shfl_xor_sync(0xffffffffu, a, 1);
-                    a += __shfl_xor_sync(0xffffffffu, a, 2);
-                    a += __shfl_xor_sync(0xffffffffu, a, 4);
-                    if ((ct & 7) == 0) Xs[t * (K / 32) + (k >> 5)] = a;
+                for (int k = 0; k < 8; ++k) {
+                    l0[k] = __float2int_rn(e[k] * sc);  // |l0| <= 127
+                    l1[k] = __float2int_rn(fmaf(e[k], sc, -static_cast<float>(l0[k])) * 128.f);  // |l1| <= 64
                 }
-              }
+                uint8_t* c0 = xsm + (2 * t) * XS + b * 256 + 8 * lane;
+                *reinterpret_cast<uint2*>(c0) =
+                    make_uint2(pack_b4(l0[0], l0[1], l0[2], l0[3]), pack_b4(l0[4], l0[5], l0[6], l0[7]));
+                *reinterpret_cast<uint2*>(c0 + XS) =
+                    make_uint2(pack_b4(l1[0], l1[1], l1[2], l1[3]), pack_b4(l1[4], l1[5], l1[6], l1[7]));
+                float a = ((e[0] + e[1]) + (e[2] + e[3])) + ((e[4] + e[5]) + (e[6] + e[7]));
+                a += __shfl_xor_sync(0xffffffffu, a, 1);
+                a += __shfl_xor_sync(0xffffffffu, a, 2);
+                if ((lane & 3) == 0) Xs[t * (K / 32) + b * 8 + (lane >> 2)] = a;
+                if (lane == 0) dfac[t * nblk + b] = mx * (1.f / 2032.f);  // 1 / (16 s)
             }
-            if (ct == 0) inv[t] = 1.f / sc;
-            consumers_sync();  // wred is reused by the next vector
         }
+        consumers_sync();
     } else {
         float4* xs4 = reinterpret_cast<float4*>(xsm);
         constexpr int kB = 8;  // float4 loads in flight per thread
@@ -506,21 +503,19 @@ __device__ __forceinline__ void stage_activations(const OpInfo& op, uint8_t* xsm
 }
 
 template <int NT>
-__global__ void __maxnreg__(112) stream_gemv_kernel(const __grid_constant__ SList L) {
+__global__ void __launch_bounds__(kThreads, 1) stream_gemv_kernel(const __grid_constant__ SList L) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int S = L.stages;
     const int SB = L.stage_bytes;
-    const int TB = L.tab_blocks;                                      // table blocks per stage
     uint8_t* stages = smem;
-    float4* tabs = reinterpret_cast<float4*>(smem + S * SB);           // [S][TB][4][16]
-    uint8_t* xsm = reinterpret_cast<uint8_t*>(tabs) + S * kRows * TB * 64;
-    float* ubuf = reinterpret_cast<float*>(xsm + L.x_bytes);          // [kUnitSlots][kCW][16][NT]
+    uint8_t* xsm = smem + S * SB;
+    Q4Tab* tabs = reinterpret_cast<Q4Tab*>(xsm + L.x_bytes);                 // [kCW][2] when has_q4k
+    float* ubuf = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(tabs) +
+                                           (L.has_q4k ? kCW * 2 * sizeof(Q4Tab) : 0));  // [kUnitSlots][kCW][16][NT]
     int* ucnt = reinterpret_cast<int*>(ubuf + kUnitSlots * kCW * kRows * NT);
-    float* wred = reinterpret_cast<float*>(ucnt + kUnitSlots);        // [kCW]
-    uint64_t* full = reinterpret_cast<uint64_t*>(wred + kCW);
+    uint64_t* full = reinterpret_cast<uint64_t*>(ucnt + kUnitSlots + 2);  // 8-byte aligned: kUnitSlots + 2 is even
     uint64_t* empty = full + kMaxStages;
-    uint64_t* ready = empty + kMaxStages;
-    volatile int* poisoned = reinterpret_cast<volatile int*>(ready + kMaxStages);
+    volatile int* poisoned = reinterpret_cast<volatile int*>(empty + kMaxStages);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     for (int i = threadIdx.x; i < kUnitSlots; i += kThreads) ucnt[i] = 0;
@@ -528,7 +523,6 @@ __global__ void __maxnreg__(112) stream_gemv_kernel(const __grid_constant__ SLis
         for (int s = 0; s < S; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], kCW);
-            mbar_init(&ready[s], 1);
         }
         *poisoned = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -563,79 +557,73 @@ __global__ void __maxnreg__(112) stream_gemv_kernel(const __grid_constant__ SLis
 
     if (warp == 0) {
         // ---------------- copy warp: waits only for released slots ----------------
+        // The op's fields live in registers and are reloaded only when the op
+        // changes: every shared-memory access here competes with the
+        // consumers' traffic.
         const uint64_t policy = evict_first_policy();
-        SeqCursor ci;
-        ci.start(T);
-        for (uint32_t issued = 0; !ci.done(T); ++issued, ci.next(T)) {
-            const int s = issued % S;
-            int ok = 0;
-            if (lane == 0) ok = mbar_wait(&empty[s], ((issued / S) & 1) ^ 1, 1u, poisoned);
-            if (!__shfl_sync(0xffffffffu, ok, 0)) break;
-            {
-                const OpInfo& op = T.op[ci.oi];
-                const int bb = block_bytes_of(op.type);
-                const int r0 = (ci.u - op.unit_begin) * kRows;
-                const int b0 = ci.sg * op.seg_blocks;
+        const int n_ops = T.n_ops, total = T.total_units;
+        int u = blockIdx.x, oi = 0;
+        while (oi + 1 < n_ops && u >= T.op[oi + 1].unit_begin) ++oi;
+        int s = 0;
+        uint32_t phase = 1;  // the first pass finds every slot free
+        for (; u < total; u += gridDim.x) {
+            while (oi + 1 < n_ops && u >= T.op[oi + 1].unit_begin) ++oi;
+            const OpInfo& op = T.op[oi];
+            const int bb = block_bytes_of(op.type), nseg = op.nseg, seg_blocks = op.seg_blocks, wbox = op.wbox;
+            const int r0 = (u - op.unit_begin) * kRows;
+            const bool tma = op.use_tma != 0;
+            const CUtensorMap* tm = &L.op[oi].tmap;
+            const int nblocks = op.K / block_elems_of(op.type), nrows = min(kRows, op.M - r0);
+            const uint8_t* wrow = op.w + static_cast<int64_t>(r0 + (lane < nrows ? lane : 0)) * op.w_nb1;
+            bool stop = false;
+            for (int sg = 0; sg < nseg; ++sg) {
+                int ok = 0;
+                if (lane == 0) ok = mbar_wait(&empty[s], phase, 1u, poisoned);
+                if (!__shfl_sync(0xffffffffu, ok, 0)) {
+                    stop = true;
+                    break;
+                }
+                const int b0 = sg * seg_blocks;
                 uint8_t* dst = stages + s * SB;
-                if (op.use_tma) {
+                if (tma) {
                     // one box: 16 rows x wbox bytes from the 16-byte-aligned column at
                     // or below the segment start (rows past M and columns past the row
                     // end read as zeros)
                     if (lane == 0) {
-                        mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(kRows * op.wbox));
-                        tma_2d_g2s(dst, &L.op[ci.oi].tmap, ((b0 * bb) & ~15) / 8, r0, &full[s], policy);
+                        mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(kRows * wbox));
+                        tma_2d_g2s(dst, tm, ((b0 * bb) & ~15) / 8, r0, &full[s], policy);
                     }
                 } else {
                     // one bulk copy per row: the row's segment rounded out to 16 bytes
-                    const int nblocks = op.K / block_elems_of(op.type);
-                    const int nrows = min(kRows, op.M - r0);
                     const bool active = lane < nrows;
-                    const int nbytes = min(op.seg_blocks, nblocks - b0) * bb;
-                    const uintptr_t g = reinterpret_cast<uintptr_t>(
-                        op.w + static_cast<int64_t>(r0 + (active ? lane : 0)) * op.w_nb1 + b0 * bb);
+                    const int nbytes = min(seg_blocks, nblocks - b0) * bb;
+                    const uintptr_t g = reinterpret_cast<uintptr_t>(wrow + b0 * bb);
                     const uintptr_t ga = g & ~uintptr_t(15);
                     const uint32_t bytes = active ? static_cast<uint32_t>(((g + nbytes + 15) & ~uintptr_t(15)) - ga) : 0u;
-                    const uint32_t total = __reduce_add_sync(0xffffffffu, bytes);
-                    if (lane == 0) mbar_arrive_expect_tx(&full[s], total);
+                    const uint32_t sum = __reduce_add_sync(0xffffffffu, bytes);
+                    if (lane == 0) mbar_arrive_expect_tx(&full[s], sum);
                     __syncwarp();
-                    if (active) bulk_g2s(dst + lane * op.wbox, reinterpret_cast<const void*>(ga), bytes, &full[s], policy);
+                    if (active) bulk_g2s(dst + lane * wbox, reinterpret_cast<const void*>(ga), bytes, &full[s], policy);
+                }
+                if (++s == S) {
+                    s = 0;
+                    phase ^= 1u;
                 }
             }
-        }
-        return;
-    }
-    if (warp == 1) {
-        // ---------------- hand-off warp: waits for landed stages, decodes Q4_K scales ----------------
-        SeqCursor cd;
-        cd.start(T);
-        for (uint32_t decoded = 0; !cd.done(T); ++decoded, cd.next(T)) {
-            const int s = decoded % S;
-            int ok = 0;
-            if (lane == 0) ok = mbar_wait(&full[s], (decoded / S) & 1, 1u, poisoned);
-            if (!__shfl_sync(0xffffffffu, ok, 0)) break;
-            const OpInfo& op = T.op[cd.oi];
-            if (op.type == kTypeQ4_K) {
-                const int nb = min(op.seg_blocks, op.K / 256 - cd.sg * op.seg_blocks);
-                const uint8_t* stage = stages + s * SB;
-                float4* tab = tabs + s * kRows * TB * 4;
-                for (int e = lane; e < kRows * nb; e += 32) {
-                    const int r = e & 15, bl = e >> 4;
-                    q4k_decode_scales(stage + r * op.wbox + bl * 144, tab + bl * 64 + r);
-                }
-            }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&ready[s]);
+            if (stop) break;
         }
         return;
     }
 
     // ---------------- consumers ----------------
     asm volatile("griddepcontrol.wait;" ::: "memory");
-    const int ct = threadIdx.x - 64;  // 0..255
-    const int cw = warp - 2;          // 0..7
-    uint32_t seq = 0;                 // stage sequence number
+    const int ct = threadIdx.x - 32;  // 0 .. 32 kCW - 1
+    const int cw = warp - 1;          // 0 .. kCW - 1
+    int cslot = 0;                    // stage slot of the current segment
+    uint32_t cphase = 0;              // its full-barrier parity
     uint32_t item_base = 0;           // items of the CTA's sequence before the current segment
     int staged = -1, uslot = 0;
+    uint32_t tsel = 0;                // Q4_K table buffer of the next item
     SeqCursor cur;
     cur.start(T);
     while (!cur.done(T)) {
@@ -647,7 +635,7 @@ __global__ void __maxnreg__(112) stream_gemv_kernel(const __grid_constant__ SLis
             T.op[staged].x_nb1 != op.x_nb1 || (T.op[staged].type == kTypeQ4_K) != (op.type == kTypeQ4_K) ||
             (op.type != kTypeQ4_K && T.op[staged].type != op.type)) {
             consumers_sync();  // nobody still reads the previous image
-            stage_activations(op, xsm, wred, ct, lane, cw);
+            stage_activations(op, xsm, ct, lane, cw);
             staged = oi;
         }
         const int bb = block_bytes_of(op.type);
@@ -657,44 +645,105 @@ __global__ void __maxnreg__(112) stream_gemv_kernel(const __grid_constant__ SLis
         float* ub = ubuf + (uslot * kCW + cw) * kRows * NT;
 
         if (op.type == kTypeQ4_K) {
-            // ================= Q4_K, tensor cores =================
+            // ================= Q4_K, integer tensor cores =================
             const int g = lane >> 2, c = lane & 3;
-            const int lanes = 8 * N;
-            const bool has_tok = c < N;
-            const uint2* xB = reinterpret_cast<const uint2*>(xsm);
-            const float* Xs = reinterpret_cast<const float*>(xsm + img_xb_bytes(K, N)) + (has_tok ? c : 0) * (K / 32);
-            float accm_g = 0.f, accm_g8 = 0.f, accn_g = 0.f, accn_g8 = 0.f;
-            for (int sg = 0; sg < op.nseg; ++sg, ++seq) {
-                const int s = seq % S;
-                mbar_wait(&ready[s], (seq / S) & 1, 2u, poisoned);
+            const int XS = img_col_bytes(K);
+            // ldmatrix row addresses: weights (matrix m = lane/8: rows 0-7 / 8-15 of
+            // the 16-byte chunk 0 / 1 of a pair), activations (row = limb column,
+            // clamped to the 2N real ones; chunk m of the pair's 64 elements)
+            const int wrow = (lane & 7) + 8 * ((lane >> 3) & 1), wchunk = lane >> 4;
+            const int wlane = wrow * op.wbox + 16 + 16 * wchunk;
+            const uint8_t* xlane = xsm + ((lane & 7) % (2 * N)) * XS + 16 * (lane >> 3);
+            const float* dfac = reinterpret_cast<const float*>(xsm + img_inv_off(K, N)) + (c < N ? c : 0) * (K / 256);
+            const float2* Xs2 = reinterpret_cast<const float2*>(xsm + img_sum_off(K, N));
+            Q4Tab* mytab = tabs + 2 * cw;
+            float yg = 0.f, yh = 0.f;              // vector c, rows g and g + 8
+            float mg[NT], mh[NT];                  // min-term partials (sub-blocks 2c, 2c+1), per vector
+#pragma unroll
+            for (int t = 0; t < NT; ++t) mg[t] = mh[t] = 0.f;
+            for (int sg = 0; sg < op.nseg; ++sg) {
                 const int b0 = sg * op.seg_blocks;
                 const int nb = min(op.seg_blocks, nblocks - b0);
-                const uint8_t* stage = stages + s * SB;
-                const float4* tab = tabs + s * kRows * TB * 4;
-                const int row8 = 8 * op.wbox;
-                for (int i = (cw - static_cast<int>(item_base % kCW) + kCW) % kCW; i < nb; i += kCW) {
+                // this warp's first item of the segment; a warp without one neither
+                // waits for nor releases the stage (the warp with item 0 releases it
+                // for them)
+                const int i0 = (cw - static_cast<int>(item_base % kCW) + kCW) % kCW;
+                if (i0 >= nb) {
+                    item_base += nb;
+                    if (++cslot == S) {
+                        cslot = 0;
+                        cphase ^= 1u;
+                    }
+                    continue;
+                }
+                mbar_wait_warp(&full[cslot], cphase, 2u, poisoned, lane);
+                const uint8_t* stage = stages + cslot * SB;
+                for (int i = i0; i < nb; i += kCW) {
                     const int bg = b0 + i;
-                    const uint8_t* blk_g = stage + g * op.wbox + i * 144;
-                    const float4* tab_g = tab + i * 64 + g;
-                    const uint2* xe = xB + (bg * 16) * lanes + (lane < lanes ? lane : 0);
-                    const float* xs = Xs + bg * 8;
-                    const float4 r0v = q4_pair(blk_g, row8, tab_g, xe, xs, 0, c, lane, lanes, has_tok);
-                    const float4 r1v = q4_pair(blk_g, row8, tab_g, xe, xs, 1, c, lane, lanes, has_tok);
-                    const float4 r2v = q4_pair(blk_g, row8, tab_g, xe, xs, 2, c, lane, lanes, has_tok);
-                    const float4 r3v = q4_pair(blk_g, row8, tab_g, xe, xs, 3, c, lane, lanes, has_tok);
-                    accm_g += (r0v.x + r1v.x) + (r2v.x + r3v.x);
-                    accm_g8 += (r0v.y + r1v.y) + (r2v.y + r3v.y);
-                    accn_g += (r0v.z + r1v.z) + (r2v.z + r3v.z);
-                    accn_g8 += (r0v.w + r1v.w) + (r2v.w + r3v.w);
+                    Q4Tab& tb = mytab[tsel];
+                    tsel ^= 1u;
+                    q4k_decode_item(stage + (lane & 15) * op.wbox + i * 144, lane & 15, lane >> 4, tb);
+                    __syncwarp();
+                    const int4 sg0 = tb.sc[0][g], sg1 = tb.sc[1][g], sh0 = tb.sc[0][g + 8], sh1 = tb.sc[1][g + 8];
+                    const int scg[8] = {sg0.x, sg0.y, sg0.z, sg0.w, sg1.x, sg1.y, sg1.z, sg1.w};
+                    const int sch[8] = {sh0.x, sh0.y, sh0.z, sh0.w, sh1.x, sh1.y, sh1.z, sh1.w};
+                    const uint8_t* wp = stage + wlane + i * 144;
+                    const uint8_t* xp = xlane + bg * 256;
+                    int a0 = 0, a1 = 0, a2 = 0, a3 = 0;  // (g, limb 0), (g, limb 1), (g+8, l0), (g+8, l1)
+#pragma unroll
+                    for (int p = 0; p < 4; ++p) {
+                        uint32_t w[4], xb[4];
+                        ldmatrix_x4(w, wp + 32 * p);
+                        ldmatrix_x4(xb, xp + 64 * p);
+                        int dl[4], dh[4];
+                        imma_u8s8(dl, w[0] & 0x0F0F0F0Fu, w[1] & 0x0F0F0F0Fu, w[2] & 0x0F0F0F0Fu, w[3] & 0x0F0F0F0Fu,
+                                  xb[0], xb[1]);
+                        imma_u8s8(dh, w[0] & 0xF0F0F0F0u, w[1] & 0xF0F0F0F0u, w[2] & 0xF0F0F0F0u, w[3] & 0xF0F0F0F0u,
+                                  xb[2], xb[3]);
+                        a0 += scg[2 * p] * dl[0] + scg[2 * p + 1] * dh[0];
+                        a1 += scg[2 * p] * dl[1] + scg[2 * p + 1] * dh[1];
+                        a2 += sch[2 * p] * dl[2] + sch[2 * p + 1] * dh[2];
+                        a3 += sch[2 * p] * dl[3] + sch[2 * p + 1] * dh[3];
+                    }
+                    const float xf = dfac[bg];
+                    yg = fmaf(fmaf(static_cast<float>(a1), 0.0078125f, static_cast<float>(a0)), tb.d[g] * xf, yg);
+                    yh = fmaf(fmaf(static_cast<float>(a3), 0.0078125f, static_cast<float>(a2)), tb.d[g + 8] * xf, yh);
+                    const float2 mng = tb.mn[c][g], mnh = tb.mn[c][g + 8];
+#pragma unroll
+                    for (int t = 0; t < NT; ++t) {
+                        if (t < N) {
+                            const float2 xs = Xs2[t * (K / 64) + bg * 4 + c];
+                            mg[t] = fmaf(mng.x, xs.x, fmaf(mng.y, xs.y, mg[t]));
+                            mh[t] = fmaf(mnh.x, xs.x, fmaf(mnh.y, xs.y, mh[t]));
+                        }
+                    }
                 }
                 item_base += nb;
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&empty[s]);
+                if (lane == 0) mbar_arrive_cnt(&empty[cslot], i0 == 0 ? 1u + kCW - min(nb, kCW) : 1u);
+                if (++cslot == S) {
+                    cslot = 0;
+                    cphase ^= 1u;
+                }
             }
-            if (has_tok) {
-                const float inv = reinterpret_cast<const float*>(xsm + img_bytes(kTypeQ4_K, K, N) - 16)[c];
-                ub[g * NT + c] = accm_g * inv - accn_g;
-                ub[(g + 8) * NT + c] = accm_g8 * inv - accn_g8;
+            // min term: sum the four sub-block pairs of the row group, then lane c
+            // (vector c) subtracts its vector's total
+            float og = yg, oh = yh;
+#pragma unroll
+            for (int t = 0; t < NT; ++t) {
+                float vg = mg[t], vh = mh[t];
+                vg += __shfl_xor_sync(0xffffffffu, vg, 1);
+                vh += __shfl_xor_sync(0xffffffffu, vh, 1);
+                vg += __shfl_xor_sync(0xffffffffu, vg, 2);
+                vh += __shfl_xor_sync(0xffffffffu, vh, 2);
+                if (c == t) {
+                    og -= vg;
+                    oh -= vh;
+                }
+            }
+            if (c < N) {
+                ub[g * NT + c] = og;
+                ub[(g + 8) * NT + c] = oh;
             }
         } else {
             // ================= Q6_K / Q8_0, CUDA cores =================
@@ -709,12 +758,22 @@ __global__ void __maxnreg__(112) stream_gemv_kernel(const __grid_constant__ SLis
             for (int q = 0; q < 4; ++q)
 #pragma unroll
                 for (int n = 0; n < NT; ++n) acc[q][n] = 0.f;
-            for (int sg = 0; sg < op.nseg; ++sg, ++seq) {
-                const int s = seq % S;
-                mbar_wait(&ready[s], (seq / S) & 1, 2u, poisoned);
+            for (int sg = 0; sg < op.nseg; ++sg) {
                 const int b0 = sg * op.seg_blocks;
                 const int nb = min(op.seg_blocks, nblocks - b0);
-                const uint8_t* stage = stages + s * SB;
+                const int gpb = q8 ? 8 : 1;
+                const int ngroups = (nb + gpb - 1) / gpb;
+                const int g0 = (cw - static_cast<int>(item_base % kCW) + kCW) % kCW;
+                if (g0 >= ngroups) {  // no item here: the warp with item 0 releases the stage
+                    item_base += ngroups;
+                    if (++cslot == S) {
+                        cslot = 0;
+                        cphase ^= 1u;
+                    }
+                    continue;
+                }
+                mbar_wait_warp(&full[cslot], cphase, 2u, poisoned, lane);
+                const uint8_t* stage = stages + cslot * SB;
                 const uint32_t glo = wlo + static_cast<uint32_t>(b0 * bb);
                 const uint8_t* base[4];
 #pragma unroll
@@ -723,9 +782,7 @@ __global__ void __maxnreg__(112) stream_gemv_kernel(const __grid_constant__ SLis
                     // each row's copy window starts at its segment start rounded down to 16 bytes
                     base[q] = stage + r * op.wbox + ((glo + static_cast<uint32_t>(r) * nb1lo) & 15u);
                 }
-                const int gpb = q8 ? 8 : 1;
-                const int ngroups = (nb + gpb - 1) / gpb;
-                for (int gi = (cw - static_cast<int>(item_base % kCW) + kCW) % kCW; gi < ngroups; gi += kCW) {
+                for (int gi = g0; gi < ngroups; gi += kCW) {
                     const int gg = b0 / gpb + gi;  // 256-element group index
                     float4 xr[NT][8];
 #pragma unroll
@@ -755,7 +812,11 @@ __global__ void __maxnreg__(112) stream_gemv_kernel(const __grid_constant__ SLis
                 }
                 item_base += ngroups;
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&empty[s]);
+                if (lane == 0) mbar_arrive_cnt(&empty[cslot], g0 == 0 ? 1u + kCW - min(ngroups, kCW) : 1u);
+                if (++cslot == S) {
+                    cslot = 0;
+                    cphase ^= 1u;
+                }
             }
 #pragma unroll
             for (int q = 0; q < 4; ++q)
@@ -801,10 +862,10 @@ __global__ void __maxnreg__(112) stream_gemv_kernel(const __grid_constant__ SLis
     }
 }
 
-size_t smem_bytes(int stages, int stage_bytes, int tab_blocks, int x_bytes, int nt) {
-    return static_cast<size_t>(stages) * (static_cast<size_t>(stage_bytes) + kRows * tab_blocks * 64) +
-           static_cast<size_t>(x_bytes) + 4ull * kUnitSlots * kCW * kRows * nt + 4ull * kUnitSlots + 4ull * kCW +
-           8ull * (3 * kMaxStages) + 16;
+size_t smem_bytes(int stages, int stage_bytes, int has_q4k, int x_bytes, int nt) {
+    return static_cast<size_t>(stages) * static_cast<size_t>(stage_bytes) + static_cast<size_t>(x_bytes) +
+           (has_q4k ? kCW * 2 * sizeof(Q4Tab) : 0) + 4ull * kUnitSlots * kCW * kRows * nt + 4ull * (kUnitSlots + 2) +
+           8ull * (2 * kMaxStages) + 16;
 }
 
 typedef CUresult (*TensorMapEncodeFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
@@ -864,7 +925,7 @@ bool stream_supported(const MulMatOp* ops, int n_ops) {
 int launch_stream(const MulMatOp* ops, int n_ops, cudaStream_t stream, int num_sms) {
     SList L{};
     L.n_ops = n_ops;
-    int units = 0, max_n = 1, x_bytes = 0, tab_blocks = 0, wmax = 0;
+    int units = 0, max_n = 1, x_bytes = 0, has_q4k = 0, wmax = 0;
     for (int i = 0; i < n_ops; ++i) {
         const MulMatOp& o = ops[i];
         SOp& s = L.op[i];
@@ -893,7 +954,7 @@ int launch_stream(const MulMatOp* ops, int n_ops, cudaStream_t stream, int num_s
         if (wbox % 32 == 0) wbox += 16;
         s.wbox = wbox;
         s.use_tma = encode_weight_map(s, nblocks * bb) ? 1 : 0;
-        if (o.type == kTypeQ4_K) tab_blocks = seg > tab_blocks ? seg : tab_blocks;
+        if (o.type == kTypeQ4_K) has_q4k = 1;
         wmax = wbox > wmax ? wbox : wmax;
         units += (o.M + kRows - 1) / kRows;
         max_n = o.N > max_n ? o.N : max_n;
@@ -903,17 +964,17 @@ int launch_stream(const MulMatOp* ops, int n_ops, cudaStream_t stream, int num_s
     L.total_units = units;
     L.x_bytes = x_bytes;
     L.stage_bytes = kRows * wmax;
-    L.tab_blocks = tab_blocks;
+    L.has_q4k = has_q4k;
     const int nt = max_n <= 1 ? 1 : 2;
-    const size_t fixed = smem_bytes(0, L.stage_bytes, tab_blocks, x_bytes, nt);
-    const size_t per_stage = smem_bytes(1, L.stage_bytes, tab_blocks, x_bytes, nt) - fixed;
+    const size_t fixed = smem_bytes(0, L.stage_bytes, has_q4k, x_bytes, nt);
+    const size_t per_stage = smem_bytes(1, L.stage_bytes, has_q4k, x_bytes, nt) - fixed;
     int stages = fixed >= static_cast<size_t>(kSmemBudget)
                      ? 0
                      : static_cast<int>((static_cast<size_t>(kSmemBudget) - fixed) / per_stage);
     stages = stages > kMaxStages ? kMaxStages : stages;
     if (stages < 2) stages = 2;
     L.stages = stages;
-    const size_t smem = smem_bytes(stages, L.stage_bytes, tab_blocks, x_bytes, nt);
+    const size_t smem = smem_bytes(stages, L.stage_bytes, has_q4k, x_bytes, nt);
     if (smem > 227 * 1024) return -static_cast<int>(cudaErrorInvalidValue);
     // CTAs per SM: two by default (~140 KB of weights in flight per SM, and a
     // finished CTA's slot goes to the next launch early); one via the
