@@ -90,7 +90,6 @@ struct SList {
     int32_t total_units;
     int32_t stages;
     int32_t stage_bytes;  // 16 rows x the largest wbox
-    int32_t has_q4k;      // a Q4_K op is present: per-warp scale tables are reserved
     int32_t x_bytes;      // shared-memory bytes reserved for the activation image
 };
 
@@ -204,6 +203,21 @@ __device__ __forceinline__ void ldmatrix_x4(uint32_t (&r)[4], const void* row_ad
                  : "r"(smem_u32(row_addr)));
 }
 
+__device__ __forceinline__ void ldmatrix_x4_at(uint32_t (&r)[4], uint32_t smem_addr) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(smem_addr));
+}
+
+// D += A (16x32 u8, row) * B (32x8 s8, col), s32.
+__device__ __forceinline__ void imma_u8s8_acc(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                              uint32_t b0, uint32_t b1) {
+    asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
 // D = A (16x32 u8, row) * B (32x8 s8, col), s32 accumulate from zero.
 __device__ __forceinline__ void imma_u8s8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                           uint32_t b0, uint32_t b1) {
@@ -261,40 +275,84 @@ __device__ __forceinline__ uint32_t lds_u32_any(const uint8_t* p) {
 }
 __device__ __forceinline__ uint32_t lds_u16(const uint8_t* p) { return *reinterpret_cast<const uint16_t*>(p); }
 
-// Scales of one Q4_K item (16 rows of one block) as the MMA lanes use them.
-struct Q4Tab {
-    int4 sc[2][kRows];    // [half h][row]: sub-blocks 4h..4h+3; 16 sc for even (low-nibble) ones
-    float2 mn[4][kRows];  // [pair c][row]: dmin*m of sub-blocks 2c, 2c+1
-    float d[kRows];
-};
-
-// Lane (row r = lane%16, half h = lane/16) decodes sub-blocks 4h..4h+3 of
-// row r's block header into the table (get_scale_min_k4 semantics,
-// src/inference/jsep/ops/matmul.ts:408-424): for j < 4 sc = s[j]&63,
-// m = s[j+4]&63; for j >= 4 sc = (s[j+4]&15) | (s[j-4]>>6)<<4,
-// m = (s[j+4]>>4) | (s[j]>>6)<<4, done four sub-blocks at a time on bytes.
-__device__ __forceinline__ void q4k_decode_item(const uint8_t* blk, int r, int h, Q4Tab& T) {
-    const uint4 hdr = *reinterpret_cast<const uint4*>(blk);
-    const float d = f16_bits_to_f32(hdr.x), dmin = f16_bits_to_f32(hdr.x >> 16);
-    const uint32_t w1 = hdr.y, w2 = hdr.z, w3 = hdr.w;
-    const uint32_t sa = h ? w3 : w1, sb = h ? (w1 >> 2) : w1;
-    const uint32_t ma = h ? (w3 >> 4) : w2, mb = h ? (w2 >> 2) : w2;
-    const uint32_t scw = (sa & 0x0F0F0F0Fu) | (sb & 0x30303030u);
-    const uint32_t mw = (ma & 0x0F0F0F0Fu) | (mb & 0x30303030u);
-    T.sc[h][r] = make_int4(static_cast<int>(__byte_perm(scw, 0, 0x4440)) << 4,
-                           static_cast<int>(__byte_perm(scw, 0, 0x4441)),
-                           static_cast<int>(__byte_perm(scw, 0, 0x4442)) << 4,
-                           static_cast<int>(__byte_perm(scw, 0, 0x4443)));
-    // dmin*m exactly rounded: (2^23 + m) dmin - 2^23 dmin in one FMA (both
-    // products exact: dmin has at most 11 significant bits)
+// Scales of the sub-blocks j = q NS + sl (q = 0 .. NCH-1) of one Q4_K block
+// header h (get_scale_min_k4 semantics, src/inference/jsep/ops/matmul.ts:408-424:
+// for j < 4 sc = s[j]&63, m = s[j+4]&63; for j >= 4 sc = (s[j+4]&15) |
+// (s[j-4]>>6)<<4, m = (s[j+4]>>4) | (s[j]>>6)<<4). sc comes out as an int,
+// times 16 for even (low-nibble) sub-blocks, whose quants enter the MMA
+// unscaled; m as dmin*m, exactly rounded: (2^23 + m) dmin - 2^23 dmin in one
+// FMA (both products exact: dmin has at most 11 significant bits).
+template <int NS, int NCH>
+__device__ __forceinline__ void q4k_slot_scales(const uint4 h, int sl, int (&sc)[NCH], float (&mdm)[NCH], float& d) {
+    d = f16_bits_to_f32(h.x);
+    const float dmin = f16_bits_to_f32(h.x >> 16);
     const float dm23 = dmin * 8388608.f;
-    const float m0 = fmaf(__uint_as_float(__byte_perm(mw, 0x4B000000u, 0x7440u)), dmin, -dm23);
-    const float m1 = fmaf(__uint_as_float(__byte_perm(mw, 0x4B000000u, 0x7441u)), dmin, -dm23);
-    const float m2 = fmaf(__uint_as_float(__byte_perm(mw, 0x4B000000u, 0x7442u)), dmin, -dm23);
-    const float m3 = fmaf(__uint_as_float(__byte_perm(mw, 0x4B000000u, 0x7443u)), dmin, -dm23);
-    T.mn[2 * h][r] = make_float2(m0, m1);
-    T.mn[2 * h + 1][r] = make_float2(m2, m3);
-    if (h == 0) T.d[r] = d;
+#pragma unroll
+    for (int q = 0; q < NCH; ++q) {
+        const int jj = q * NS + sl;
+        const uint32_t sel = 0x4440u + static_cast<uint32_t>(jj & 3);  // byte jj%4, zero-extended
+        uint32_t scv, mv;
+        if (q * NS < 4) {  // j < 4 (NS divides 4 and sl < NS)
+            scv = __byte_perm(h.y, 0u, sel) & 63u;
+            mv = __byte_perm(h.z, 0u, sel) & 63u;
+        } else {
+            const uint32_t b1 = __byte_perm(h.y, 0u, sel), b2 = __byte_perm(h.z, 0u, sel), b3 = __byte_perm(h.w, 0u, sel);
+            scv = (b3 & 15u) | ((b1 >> 2) & 0x30u);
+            mv = (b3 >> 4) | ((b2 >> 2) & 0x30u);
+        }
+        sc[q] = static_cast<int>(scv << ((jj & 1) ? 0 : 4));
+        mdm[q] = fmaf(__uint_as_float(0x4B000000u | mv), dmin, -dm23);
+    }
+}
+
+// One Q4_K item: 16 rows x one 256-element block, for NP = N rounded up to a
+// power of two. The MMA's 8 columns are NS = 4/NP sub-block slots x NP
+// vectors x 2 limbs (column 2 NP slot + 2 t + l). A sub-block's MMA reads the
+// activation rows of its own slot; every other B row is the zero row, so the
+// NS sub-blocks of a chain accumulate into one fragment without mixing, and
+// lane (g, c) ends up with its slot's sub-blocks (slot c / NP, vector c % NP)
+// of rows g and g+8: it scales only those, NCH = 8 / NS per row.
+template <int NP>
+__device__ __forceinline__ void q4k_item(const uint8_t* blk, int wbox, uint32_t wl, uint32_t xaddr, uint32_t xzero,
+                                         bool xv0, bool xv1, float xf, const float* xs, int g, int sl, float& yg,
+                                         float& yh) {
+    constexpr int NS = 4 / NP, NCH = 8 / NS;
+    const uint4 hg = *reinterpret_cast<const uint4*>(blk + g * wbox);
+    const uint4 hh = *reinterpret_cast<const uint4*>(blk + (g + 8) * wbox);
+    int scg[NCH], sch[NCH];
+    float mg[NCH], mh[NCH], dg, dh;
+    q4k_slot_scales<NS, NCH>(hg, sl, scg, mg, dg);
+    q4k_slot_scales<NS, NCH>(hh, sl, sch, mh, dh);
+    int D[NCH][4];
+#pragma unroll
+    for (int q = 0; q < NCH; ++q) D[q][0] = D[q][1] = D[q][2] = D[q][3] = 0;
+    const uint32_t wbase = smem_u32(blk) + wl;
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {
+        uint32_t w[4], x[4];
+        ldmatrix_x4_at(w, wbase + 32 * p);
+        ldmatrix_x4_at(x, ((p & 1) ? xv1 : xv0) ? xaddr + 64 * p : xzero);
+        imma_u8s8_acc(D[(2 * p) / NS], w[0] & 0x0F0F0F0Fu, w[1] & 0x0F0F0F0Fu, w[2] & 0x0F0F0F0Fu, w[3] & 0x0F0F0F0Fu,
+                      x[0], x[1]);
+        imma_u8s8_acc(D[(2 * p + 1) / NS], w[0] & 0xF0F0F0F0u, w[1] & 0xF0F0F0F0u, w[2] & 0xF0F0F0F0u,
+                      w[3] & 0xF0F0F0F0u, x[2], x[3]);
+    }
+    int a0 = 0, a1 = 0, a2 = 0, a3 = 0;  // (g, limb 0), (g, limb 1), (g+8, l0), (g+8, l1)
+#pragma unroll
+    for (int q = 0; q < NCH; ++q) {
+        a0 += scg[q] * D[q][0];
+        a1 += scg[q] * D[q][1];
+        a2 += sch[q] * D[q][2];
+        a3 += sch[q] * D[q][3];
+    }
+    yg = fmaf(fmaf(static_cast<float>(a1), 0.0078125f, static_cast<float>(a0)), dg * xf, yg);
+    yh = fmaf(fmaf(static_cast<float>(a3), 0.0078125f, static_cast<float>(a2)), dh * xf, yh);
+#pragma unroll
+    for (int q = 0; q < NCH; ++q) {
+        const float X = xs[q * NS + sl];
+        yg = fmaf(-mg[q], X, yg);
+        yh = fmaf(-mh[q], X, yh);
+    }
 }
 
 // Low bytes of four ints -> one word.
@@ -431,49 +489,52 @@ __device__ __forceinline__ void stage_activations(const OpInfo& op, uint8_t* xsm
         const int nblk = K / 256, XS = img_col_bytes(K);
         float* dfac = reinterpret_cast<float*>(xsm + img_inv_off(K, N));
         float* Xs = reinterpret_cast<float*>(xsm + img_sum_off(K, N));
-        constexpr int kB = 4;  // (vector, block) items per warp with loads in flight together
-        for (int tb0 = cw; tb0 < N * nblk; tb0 += kB * kCW) {
-            float4 v[kB][2];
-#pragma unroll
-            for (int q = 0; q < kB; ++q) {
-                const int tb = tb0 + q * kCW;
-                if (tb < N * nblk) {  // warp-uniform
-                    const int t = tb / nblk, b = tb - t * nblk;
-                    const float4* xv = reinterpret_cast<const float4*>(xb + t * op.x_nb1) + b * 64 + 2 * lane;
-                    v[q][0] = __ldg(xv);
-                    v[q][1] = __ldg(xv + 1);
-                }
+        // one (vector, block) per warp iteration, the next one's loads issued
+        // before this one's arithmetic
+        int tb = cw;
+        float4 n0 = make_float4(0.f, 0.f, 0.f, 0.f), n1 = n0;
+        if (tb < N * nblk) {
+            const int t = tb / nblk, b = tb - t * nblk;
+            const float4* xv = reinterpret_cast<const float4*>(xb + t * op.x_nb1) + b * 64 + 2 * lane;
+            n0 = __ldg(xv);
+            n1 = __ldg(xv + 1);
+        }
+        for (; tb < N * nblk; tb += kCW) {  // warp-uniform
+            const float4 v0 = n0, v1 = n1;
+            const int tn = tb + kCW;
+            if (tn < N * nblk) {
+                const int t = tn / nblk, b = tn - t * nblk;
+                const float4* xv = reinterpret_cast<const float4*>(xb + t * op.x_nb1) + b * 64 + 2 * lane;
+                n0 = __ldg(xv);
+                n1 = __ldg(xv + 1);
             }
+            const int t = tb / nblk, b = tb - t * nblk;
+            float mx = fmaxf(fmaxf(fmaxf(fabsf(v0.x), fabsf(v0.y)), fmaxf(fabsf(v0.z), fabsf(v0.w))),
+                             fmaxf(fmaxf(fabsf(v1.x), fabsf(v1.y)), fmaxf(fabsf(v1.z), fabsf(v1.w))));
 #pragma unroll
-            for (int q = 0; q < kB; ++q) {
-                const int tb = tb0 + q * kCW;
-                if (tb >= N * nblk) break;
-                const int t = tb / nblk, b = tb - t * nblk;
-                const float e[8] = {v[q][0].x, v[q][0].y, v[q][0].z, v[q][0].w,
-                                    v[q][1].x, v[q][1].y, v[q][1].z, v[q][1].w};
-                float mx = 0.f;
+            for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+            const float sc = mx > 0.f ? 127.f / mx : 0.f;
+            uint8_t* c0 = xsm + (2 * t) * XS + b * 256 + 8 * lane;
+            uint32_t p0[2], p1[2];
 #pragma unroll
-                for (int k = 0; k < 8; ++k) mx = fmaxf(mx, fabsf(e[k]));
-#pragma unroll
-                for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-                const float sc = mx > 0.f ? 127.f / mx : 0.f;
-                int l0[8], l1[8];
-#pragma unroll
-                for (int k = 0; k < 8; ++k) {
-                    l0[k] = __float2int_rn(e[k] * sc);  // |l0| <= 127
-                    l1[k] = __float2int_rn(fmaf(e[k], sc, -static_cast<float>(l0[k])) * 128.f);  // |l1| <= 64
-                }
-                uint8_t* c0 = xsm + (2 * t) * XS + b * 256 + 8 * lane;
-                *reinterpret_cast<uint2*>(c0) =
-                    make_uint2(pack_b4(l0[0], l0[1], l0[2], l0[3]), pack_b4(l0[4], l0[5], l0[6], l0[7]));
-                *reinterpret_cast<uint2*>(c0 + XS) =
-                    make_uint2(pack_b4(l1[0], l1[1], l1[2], l1[3]), pack_b4(l1[4], l1[5], l1[6], l1[7]));
-                float a = ((e[0] + e[1]) + (e[2] + e[3])) + ((e[4] + e[5]) + (e[6] + e[7]));
-                a += __shfl_xor_sync(0xffffffffu, a, 1);
-                a += __shfl_xor_sync(0xffffffffu, a, 2);
-                if ((lane & 3) == 0) Xs[t * (K / 32) + b * 8 + (lane >> 2)] = a;
-                if (lane == 0) dfac[t * nblk + b] = mx * (1.f / 2032.f);  // 1 / (16 s)
+            for (int h = 0; h < 2; ++h) {
+                const float4 v = h ? v1 : v0;
+                const int q0 = __float2int_rn(v.x * sc), q1 = __float2int_rn(v.y * sc);  // |l0| <= 127
+                const int q2 = __float2int_rn(v.z * sc), q3 = __float2int_rn(v.w * sc);
+                p0[h] = pack_b4(q0, q1, q2, q3);
+                // |l1| <= 64
+                p1[h] = pack_b4(__float2int_rn(fmaf(v.x, sc, -static_cast<float>(q0)) * 128.f),
+                                __float2int_rn(fmaf(v.y, sc, -static_cast<float>(q1)) * 128.f),
+                                __float2int_rn(fmaf(v.z, sc, -static_cast<float>(q2)) * 128.f),
+                                __float2int_rn(fmaf(v.w, sc, -static_cast<float>(q3)) * 128.f));
             }
+            *reinterpret_cast<uint2*>(c0) = make_uint2(p0[0], p0[1]);
+            *reinterpret_cast<uint2*>(c0 + XS) = make_uint2(p1[0], p1[1]);
+            float a = ((v0.x + v0.y) + (v0.z + v0.w)) + ((v1.x + v1.y) + (v1.z + v1.w));
+            a += __shfl_xor_sync(0xffffffffu, a, 1);
+            a += __shfl_xor_sync(0xffffffffu, a, 2);
+            if ((lane & 3) == 0) Xs[t * (K / 32) + b * 8 + (lane >> 2)] = a;
+            if (lane == 0) dfac[t * nblk + b] = mx * (1.f / 2032.f);  // 1 / (16 s)
         }
         consumers_sync();
     } else {
@@ -502,6 +563,78 @@ __device__ __forceinline__ void stage_activations(const OpInfo& op, uint8_t* xsm
     }
 }
 
+// Stage-ring position of the consumer warps.
+struct Ring {
+    uint8_t* stages;
+    uint64_t* full;
+    uint64_t* empty;
+    volatile int* poisoned;
+    int SB, S;
+    int slot;
+    uint32_t phase;
+    uint32_t item_base;  // items of the CTA's sequence before the current segment
+    __device__ __forceinline__ void advance() {
+        if (++slot == S) {
+            slot = 0;
+            phase ^= 1u;
+        }
+    }
+};
+
+// All segments of one Q4_K unit for this consumer warp; writes the warp's
+// partial sums of the unit's 16 rows (zeros where it had no item) to ub.
+template <int NP, int NT>
+__device__ __forceinline__ void q4k_unit(const OpInfo& op, Ring& R, const uint8_t* xsm, uint32_t xzero, int lane,
+                                         int cw, float* ub) {
+    constexpr int NS = 4 / NP;
+    const int K = op.K, N = op.N, XS = img_col_bytes(K), nblocks = K / 256;
+    const int g = lane >> 2, c = lane & 3, sl = c / NP, tk = c % NP;
+    // weights ldmatrix: matrix lane/8 = rows 0-7 / 8-15 of the pair's 16-byte chunk 0 / 1
+    const uint32_t wl = static_cast<uint32_t>(((lane & 7) + 8 * ((lane >> 3) & 1)) * op.wbox + 16 + 16 * (lane >> 4));
+    // activations ldmatrix: matrix mi = lane/8 (0, 1: b0, b1 of the low-nibble
+    // sub-block of a pair; 2, 3: of the high one), row rr = lane%8 = B column
+    const int mi = lane >> 3, rr = lane & 7;
+    const int slot_r = rr / (2 * NP), t_r = (rr >> 1) % NP, l_r = rr & 1;
+    const bool xv0 = t_r < N && slot_r == (mi >> 1) % NS;        // even pairs
+    const bool xv1 = t_r < N && slot_r == (2 + (mi >> 1)) % NS;  // odd pairs
+    const uint32_t xcol = smem_u32(xsm) + static_cast<uint32_t>((2 * t_r + l_r) * XS + 16 * mi);
+    const int tkc = tk < N ? tk : 0;
+    const float* dfac = reinterpret_cast<const float*>(xsm + img_inv_off(K, N)) + tkc * nblocks;
+    const float* Xs = reinterpret_cast<const float*>(xsm + img_sum_off(K, N)) + tkc * (K / 32);
+    float yg = 0.f, yh = 0.f;  // slot sl's part of vector tk, rows g and g + 8
+    for (int sg = 0; sg < op.nseg; ++sg) {
+        const int b0 = sg * op.seg_blocks;
+        const int nb = min(op.seg_blocks, nblocks - b0);
+        // this warp's first item of the segment; a warp without one neither
+        // waits for nor releases the stage (the warp with item 0 releases it
+        // for them)
+        const int i0 = (cw - static_cast<int>(R.item_base % kCW) + kCW) % kCW;
+        if (i0 < nb) {
+            mbar_wait_warp(&R.full[R.slot], R.phase, 2u, R.poisoned, lane);
+            const uint8_t* stage = R.stages + R.slot * R.SB;
+            for (int i = i0; i < nb; i += kCW) {
+                const int bg = b0 + i;
+                q4k_item<NP>(stage + i * 144, op.wbox, wl, xcol + bg * 256, xzero, xv0, xv1, dfac[bg], Xs + bg * 8, g,
+                             sl, yg, yh);
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cnt(&R.empty[R.slot], i0 == 0 ? 1u + kCW - min(nb, kCW) : 1u);
+        }
+        R.item_base += nb;
+        R.advance();
+    }
+    // sum the slots of each vector (lanes c with the same c % NP)
+#pragma unroll
+    for (int o = NP; o < 4; o <<= 1) {
+        yg += __shfl_xor_sync(0xffffffffu, yg, o);
+        yh += __shfl_xor_sync(0xffffffffu, yh, o);
+    }
+    if (sl == 0 && tk < N) {
+        ub[g * NT + tk] = yg;
+        ub[(g + 8) * NT + tk] = yh;
+    }
+}
+
 template <int NT>
 __global__ void __launch_bounds__(kThreads, 1) stream_gemv_kernel(const __grid_constant__ SList L) {
     extern __shared__ __align__(128) uint8_t smem[];
@@ -509,9 +642,8 @@ __global__ void __launch_bounds__(kThreads, 1) stream_gemv_kernel(const __grid_c
     const int SB = L.stage_bytes;
     uint8_t* stages = smem;
     uint8_t* xsm = smem + S * SB;
-    Q4Tab* tabs = reinterpret_cast<Q4Tab*>(xsm + L.x_bytes);                 // [kCW][2] when has_q4k
-    float* ubuf = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(tabs) +
-                                           (L.has_q4k ? kCW * 2 * sizeof(Q4Tab) : 0));  // [kUnitSlots][kCW][16][NT]
+    uint8_t* zrow = xsm + L.x_bytes;                                     // 16 zero bytes: the Q4_K MMA's empty B rows
+    float* ubuf = reinterpret_cast<float*>(zrow + 16);                   // [kUnitSlots][kCW][16][NT]
     int* ucnt = reinterpret_cast<int*>(ubuf + kUnitSlots * kCW * kRows * NT);
     uint64_t* full = reinterpret_cast<uint64_t*>(ucnt + kUnitSlots + 2);  // 8-byte aligned: kUnitSlots + 2 is even
     uint64_t* empty = full + kMaxStages;
@@ -519,6 +651,7 @@ __global__ void __launch_bounds__(kThreads, 1) stream_gemv_kernel(const __grid_c
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     for (int i = threadIdx.x; i < kUnitSlots; i += kThreads) ucnt[i] = 0;
+    if (threadIdx.x < 4) reinterpret_cast<uint32_t*>(zrow)[threadIdx.x] = 0u;
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; ++s) {
             mbar_init(&full[s], 1);
@@ -619,11 +752,8 @@ __global__ void __launch_bounds__(kThreads, 1) stream_gemv_kernel(const __grid_c
     asm volatile("griddepcontrol.wait;" ::: "memory");
     const int ct = threadIdx.x - 32;  // 0 .. 32 kCW - 1
     const int cw = warp - 1;          // 0 .. kCW - 1
-    int cslot = 0;                    // stage slot of the current segment
-    uint32_t cphase = 0;              // its full-barrier parity
-    uint32_t item_base = 0;           // items of the CTA's sequence before the current segment
+    Ring R{stages, full, empty, poisoned, SB, S, 0, 0u, 0u};
     int staged = -1, uslot = 0;
-    uint32_t tsel = 0;                // Q4_K table buffer of the next item
     SeqCursor cur;
     cur.start(T);
     while (!cur.done(T)) {
@@ -646,105 +776,10 @@ __global__ void __launch_bounds__(kThreads, 1) stream_gemv_kernel(const __grid_c
 
         if (op.type == kTypeQ4_K) {
             // ================= Q4_K, integer tensor cores =================
-            const int g = lane >> 2, c = lane & 3;
-            const int XS = img_col_bytes(K);
-            // ldmatrix row addresses: weights (matrix m = lane/8: rows 0-7 / 8-15 of
-            // the 16-byte chunk 0 / 1 of a pair), activations (row = limb column,
-            // clamped to the 2N real ones; chunk m of the pair's 64 elements)
-            const int wrow = (lane & 7) + 8 * ((lane >> 3) & 1), wchunk = lane >> 4;
-            const int wlane = wrow * op.wbox + 16 + 16 * wchunk;
-            const uint8_t* xlane = xsm + ((lane & 7) % (2 * N)) * XS + 16 * (lane >> 3);
-            const float* dfac = reinterpret_cast<const float*>(xsm + img_inv_off(K, N)) + (c < N ? c : 0) * (K / 256);
-            const float2* Xs2 = reinterpret_cast<const float2*>(xsm + img_sum_off(K, N));
-            Q4Tab* mytab = tabs + 2 * cw;
-            float yg = 0.f, yh = 0.f;              // vector c, rows g and g + 8
-            float mg[NT], mh[NT];                  // min-term partials (sub-blocks 2c, 2c+1), per vector
-#pragma unroll
-            for (int t = 0; t < NT; ++t) mg[t] = mh[t] = 0.f;
-            for (int sg = 0; sg < op.nseg; ++sg) {
-                const int b0 = sg * op.seg_blocks;
-                const int nb = min(op.seg_blocks, nblocks - b0);
-                // this warp's first item of the segment; a warp without one neither
-                // waits for nor releases the stage (the warp with item 0 releases it
-                // for them)
-                const int i0 = (cw - static_cast<int>(item_base % kCW) + kCW) % kCW;
-                if (i0 >= nb) {
-                    item_base += nb;
-                    if (++cslot == S) {
-                        cslot = 0;
-                        cphase ^= 1u;
-                    }
-                    continue;
-                }
-                mbar_wait_warp(&full[cslot], cphase, 2u, poisoned, lane);
-                const uint8_t* stage = stages + cslot * SB;
-                for (int i = i0; i < nb; i += kCW) {
-                    const int bg = b0 + i;
-                    Q4Tab& tb = mytab[tsel];
-                    tsel ^= 1u;
-                    q4k_decode_item(stage + (lane & 15) * op.wbox + i * 144, lane & 15, lane >> 4, tb);
-                    __syncwarp();
-                    const int4 sg0 = tb.sc[0][g], sg1 = tb.sc[1][g], sh0 = tb.sc[0][g + 8], sh1 = tb.sc[1][g + 8];
-                    const int scg[8] = {sg0.x, sg0.y, sg0.z, sg0.w, sg1.x, sg1.y, sg1.z, sg1.w};
-                    const int sch[8] = {sh0.x, sh0.y, sh0.z, sh0.w, sh1.x, sh1.y, sh1.z, sh1.w};
-                    const uint8_t* wp = stage + wlane + i * 144;
-                    const uint8_t* xp = xlane + bg * 256;
-                    int a0 = 0, a1 = 0, a2 = 0, a3 = 0;  // (g, limb 0), (g, limb 1), (g+8, l0), (g+8, l1)
-#pragma unroll
-                    for (int p = 0; p < 4; ++p) {
-                        uint32_t w[4], xb[4];
-                        ldmatrix_x4(w, wp + 32 * p);
-                        ldmatrix_x4(xb, xp + 64 * p);
-                        int dl[4], dh[4];
-                        imma_u8s8(dl, w[0] & 0x0F0F0F0Fu, w[1] & 0x0F0F0F0Fu, w[2] & 0x0F0F0F0Fu, w[3] & 0x0F0F0F0Fu,
-                                  xb[0], xb[1]);
-                        imma_u8s8(dh, w[0] & 0xF0F0F0F0u, w[1] & 0xF0F0F0F0u, w[2] & 0xF0F0F0F0u, w[3] & 0xF0F0F0F0u,
-                                  xb[2], xb[3]);
-                        a0 += scg[2 * p] * dl[0] + scg[2 * p + 1] * dh[0];
-                        a1 += scg[2 * p] * dl[1] + scg[2 * p + 1] * dh[1];
-                        a2 += sch[2 * p] * dl[2] + sch[2 * p + 1] * dh[2];
-                        a3 += sch[2 * p] * dl[3] + sch[2 * p + 1] * dh[3];
-                    }
-                    const float xf = dfac[bg];
-                    yg = fmaf(fmaf(static_cast<float>(a1), 0.0078125f, static_cast<float>(a0)), tb.d[g] * xf, yg);
-                    yh = fmaf(fmaf(static_cast<float>(a3), 0.0078125f, static_cast<float>(a2)), tb.d[g + 8] * xf, yh);
-                    const float2 mng = tb.mn[c][g], mnh = tb.mn[c][g + 8];
-#pragma unroll
-                    for (int t = 0; t < NT; ++t) {
-                        if (t < N) {
-                            const float2 xs = Xs2[t * (K / 64) + bg * 4 + c];
-                            mg[t] = fmaf(mng.x, xs.x, fmaf(mng.y, xs.y, mg[t]));
-                            mh[t] = fmaf(mnh.x, xs.x, fmaf(mnh.y, xs.y, mh[t]));
-                        }
-                    }
-                }
-                item_base += nb;
-                __syncwarp();
-                if (lane == 0) mbar_arrive_cnt(&empty[cslot], i0 == 0 ? 1u + kCW - min(nb, kCW) : 1u);
-                if (++cslot == S) {
-                    cslot = 0;
-                    cphase ^= 1u;
-                }
-            }
-            // min term: sum the four sub-block pairs of the row group, then lane c
-            // (vector c) subtracts its vector's total
-            float og = yg, oh = yh;
-#pragma unroll
-            for (int t = 0; t < NT; ++t) {
-                float vg = mg[t], vh = mh[t];
-                vg += __shfl_xor_sync(0xffffffffu, vg, 1);
-                vh += __shfl_xor_sync(0xffffffffu, vh, 1);
-                vg += __shfl_xor_sync(0xffffffffu, vg, 2);
-                vh += __shfl_xor_sync(0xffffffffu, vh, 2);
-                if (c == t) {
-                    og -= vg;
-                    oh -= vh;
-                }
-            }
-            if (c < N) {
-                ub[g * NT + c] = og;
-                ub[(g + 8) * NT + c] = oh;
-            }
+            if (NT == 1 || N == 1)
+                q4k_unit<1, NT>(op, R, xsm, smem_u32(zrow), lane, cw, ub);
+            else
+                q4k_unit<2, NT>(op, R, xsm, smem_u32(zrow), lane, cw, ub);
         } else {
             // ================= Q6_K / Q8_0, CUDA cores =================
             const int j = lane >> 3, c = lane & 7;
@@ -763,17 +798,14 @@ __global__ void __launch_bounds__(kThreads, 1) stream_gemv_kernel(const __grid_c
                 const int nb = min(op.seg_blocks, nblocks - b0);
                 const int gpb = q8 ? 8 : 1;
                 const int ngroups = (nb + gpb - 1) / gpb;
-                const int g0 = (cw - static_cast<int>(item_base % kCW) + kCW) % kCW;
+                const int g0 = (cw - static_cast<int>(R.item_base % kCW) + kCW) % kCW;
                 if (g0 >= ngroups) {  // no item here: the warp with item 0 releases the stage
-                    item_base += ngroups;
-                    if (++cslot == S) {
-                        cslot = 0;
-                        cphase ^= 1u;
-                    }
+                    R.item_base += ngroups;
+                    R.advance();
                     continue;
                 }
-                mbar_wait_warp(&full[cslot], cphase, 2u, poisoned, lane);
-                const uint8_t* stage = stages + cslot * SB;
+                mbar_wait_warp(&R.full[R.slot], R.phase, 2u, poisoned, lane);
+                const uint8_t* stage = stages + R.slot * SB;
                 const uint32_t glo = wlo + static_cast<uint32_t>(b0 * bb);
                 const uint8_t* base[4];
 #pragma unroll
@@ -810,13 +842,10 @@ __global__ void __launch_bounds__(kThreads, 1) stream_gemv_kernel(const __grid_c
                         for (int q = 0; q < 4; ++q) item_q6_k<NT>(base[q] + (gg - b0) * 210, c, xr, xq, acc[q]);
                     }
                 }
-                item_base += ngroups;
+                R.item_base += ngroups;
                 __syncwarp();
-                if (lane == 0) mbar_arrive_cnt(&empty[cslot], g0 == 0 ? 1u + kCW - min(ngroups, kCW) : 1u);
-                if (++cslot == S) {
-                    cslot = 0;
-                    cphase ^= 1u;
-                }
+                if (lane == 0) mbar_arrive_cnt(&R.empty[R.slot], g0 == 0 ? 1u + kCW - min(ngroups, kCW) : 1u);
+                R.advance();
             }
 #pragma unroll
             for (int q = 0; q < 4; ++q)
@@ -862,9 +891,9 @@ __global__ void __launch_bounds__(kThreads, 1) stream_gemv_kernel(const __grid_c
     }
 }
 
-size_t smem_bytes(int stages, int stage_bytes, int has_q4k, int x_bytes, int nt) {
+size_t smem_bytes(int stages, int stage_bytes, int x_bytes, int nt) {
     return static_cast<size_t>(stages) * static_cast<size_t>(stage_bytes) + static_cast<size_t>(x_bytes) +
-           (has_q4k ? kCW * 2 * sizeof(Q4Tab) : 0) + 4ull * kUnitSlots * kCW * kRows * nt + 4ull * (kUnitSlots + 2) +
+           16ull + 4ull * kUnitSlots * kCW * kRows * nt + 4ull * (kUnitSlots + 2) +
            8ull * (2 * kMaxStages) + 16;
 }
 
@@ -925,7 +954,7 @@ bool stream_supported(const MulMatOp* ops, int n_ops) {
 int launch_stream(const MulMatOp* ops, int n_ops, cudaStream_t stream, int num_sms) {
     SList L{};
     L.n_ops = n_ops;
-    int units = 0, max_n = 1, x_bytes = 0, has_q4k = 0, wmax = 0;
+    int units = 0, max_n = 1, x_bytes = 0, wmax = 0;
     for (int i = 0; i < n_ops; ++i) {
         const MulMatOp& o = ops[i];
         SOp& s = L.op[i];
@@ -954,7 +983,6 @@ int launch_stream(const MulMatOp* ops, int n_ops, cudaStream_t stream, int num_s
         if (wbox % 32 == 0) wbox += 16;
         s.wbox = wbox;
         s.use_tma = encode_weight_map(s, nblocks * bb) ? 1 : 0;
-        if (o.type == kTypeQ4_K) has_q4k = 1;
         wmax = wbox > wmax ? wbox : wmax;
         units += (o.M + kRows - 1) / kRows;
         max_n = o.N > max_n ? o.N : max_n;
@@ -964,17 +992,16 @@ int launch_stream(const MulMatOp* ops, int n_ops, cudaStream_t stream, int num_s
     L.total_units = units;
     L.x_bytes = x_bytes;
     L.stage_bytes = kRows * wmax;
-    L.has_q4k = has_q4k;
     const int nt = max_n <= 1 ? 1 : 2;
-    const size_t fixed = smem_bytes(0, L.stage_bytes, has_q4k, x_bytes, nt);
-    const size_t per_stage = smem_bytes(1, L.stage_bytes, has_q4k, x_bytes, nt) - fixed;
+    const size_t fixed = smem_bytes(0, L.stage_bytes, x_bytes, nt);
+    const size_t per_stage = smem_bytes(1, L.stage_bytes, x_bytes, nt) - fixed;
     int stages = fixed >= static_cast<size_t>(kSmemBudget)
                      ? 0
                      : static_cast<int>((static_cast<size_t>(kSmemBudget) - fixed) / per_stage);
     stages = stages > kMaxStages ? kMaxStages : stages;
     if (stages < 2) stages = 2;
     L.stages = stages;
-    const size_t smem = smem_bytes(stages, L.stage_bytes, has_q4k, x_bytes, nt);
+    const size_t smem = smem_bytes(stages, L.stage_bytes, x_bytes, nt);
     if (smem > 227 * 1024) return -static_cast<int>(cudaErrorInvalidValue);
     // CTAs per SM: two by default (~140 KB of weights in flight per SM, and a
     // finished CTA's slot goes to the next launch early); one via the
