@@ -59,11 +59,15 @@ namespace {
 constexpr int kCW = 8;                        // consumer warps
 constexpr int kThreads = 32 * (kCW + 1);      // + copy warp
 constexpr int kRows = 16;                     // rows per unit (one MMA m-tile)
-constexpr int kQ4kSegBlocks = 9;              // <= 1296 B per row and stage
+constexpr int kQ4kSegBlocks = 14;             // <= 2016 B per row and stage (a TMA box row is <= 2048 B)
 constexpr int kQ6kSegBlocks = 6;              // <= 1260 B (+ 16-byte window slack)
 constexpr int kQ80SegBlocks = 32;             // 1088 B, whole 8-block groups
 constexpr int kMaxStages = 8;
-constexpr int kUnitSlots = kMaxStages + 2;    // units a CTA can have in flight, plus margin
+constexpr int kRedDelay = 2;                  // a unit's partials are summed this many units later
+// Unit slots in flight: consumer warps drift apart by at most kMaxStages
+// stages (a stage is refilled only after every warp released it), so a slot
+// is summed before any warp writes it again.
+constexpr int kUnitSlots = kMaxStages + kRedDelay + 2;
 constexpr int kXPad = 16;                     // bytes after each int8 activation column (ldmatrix banks)
 constexpr int kMaxNT = 2;
 constexpr int kXF4 = 16;                      // float4 of x per consumer thread: K <= 16384
@@ -91,6 +95,7 @@ struct SList {
     int32_t stages;
     int32_t stage_bytes;  // 16 rows x the largest wbox
     int32_t x_bytes;      // shared-memory bytes reserved for the activation image
+    int32_t all_tma;      // every op is copied with its tensor map
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -116,6 +121,20 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     return ok != 0;
 }
 
+// Non-blocking test of a phase (cheaper than a potentially blocking try_wait
+// when the phase has already completed).
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
 // Bounded wait. If the phase does not complete in time the CTA is poisoned:
 // an error code is recorded for the host and every later wait of the CTA
 // returns at once, so all threads run to the end (results are garbage, the
@@ -123,6 +142,7 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 // polls: every poll is a shared-memory operation, and polls of many warps
 // were measured to slow the copy warp's own barrier and TMA operations.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned code, volatile int* poisoned) {
+    if (mbar_test_wait(bar, parity)) return true;
     for (uint32_t i = 0; i < kSpinLimit; ++i) {
         if (mbar_try_wait(bar, parity)) return true;
         if ((i & 255u) == 255u && *poisoned) return false;
@@ -563,6 +583,14 @@ __device__ __forceinline__ void stage_activations(const OpInfo& op, uint8_t* xsm
     }
 }
 
+// Where a unit's rows go; written and read by the unit's owner warp only.
+struct UnitMeta {
+    float* y;        // first output row of the unit, vector 0
+    int64_t y_nb1;   // bytes between vectors
+    int32_t rows;    // valid rows (<= 16)
+    int32_t n;       // vectors
+};
+
 // Stage-ring position of the consumer warps.
 struct Ring {
     uint8_t* stages;
@@ -581,26 +609,65 @@ struct Ring {
     }
 };
 
-// All segments of one Q4_K unit for this consumer warp; writes the warp's
-// partial sums of the unit's 16 rows (zeros where it had no item) to ub.
-template <int NP, int NT>
-__device__ __forceinline__ void q4k_unit(const OpInfo& op, Ring& R, const uint8_t* xsm, uint32_t xzero, int lane,
-                                         int cw, float* ub) {
+// Per-op constants of a consumer lane on the Q4_K path (see q4k_item).
+struct Q4Lane {
+    uint32_t wl;        // weights ldmatrix row offset in a stage
+    uint32_t xcol;      // activations ldmatrix row address (block 0, pair 0)
+    bool xv0, xv1;      // that row is real (not the zero row) for even / odd pairs
+    const float* dfac;  // d-factors of vector tk
+    const float* Xs;    // sub-block sums of vector tk
+    int sl, tk;         // slot and vector of the lane's accumulator columns
+};
+
+template <int NP>
+__device__ __forceinline__ Q4Lane q4k_lane(const OpInfo& op, const uint8_t* xsm, int lane) {
     constexpr int NS = 4 / NP;
     const int K = op.K, N = op.N, XS = img_col_bytes(K), nblocks = K / 256;
-    const int g = lane >> 2, c = lane & 3, sl = c / NP, tk = c % NP;
+    const int c = lane & 3;
+    Q4Lane q;
+    q.sl = c / NP;
+    q.tk = c % NP;
     // weights ldmatrix: matrix lane/8 = rows 0-7 / 8-15 of the pair's 16-byte chunk 0 / 1
-    const uint32_t wl = static_cast<uint32_t>(((lane & 7) + 8 * ((lane >> 3) & 1)) * op.wbox + 16 + 16 * (lane >> 4));
+    q.wl = static_cast<uint32_t>(((lane & 7) + 8 * ((lane >> 3) & 1)) * op.wbox + 16 + 16 * (lane >> 4));
     // activations ldmatrix: matrix mi = lane/8 (0, 1: b0, b1 of the low-nibble
     // sub-block of a pair; 2, 3: of the high one), row rr = lane%8 = B column
     const int mi = lane >> 3, rr = lane & 7;
     const int slot_r = rr / (2 * NP), t_r = (rr >> 1) % NP, l_r = rr & 1;
-    const bool xv0 = t_r < N && slot_r == (mi >> 1) % NS;        // even pairs
-    const bool xv1 = t_r < N && slot_r == (2 + (mi >> 1)) % NS;  // odd pairs
-    const uint32_t xcol = smem_u32(xsm) + static_cast<uint32_t>((2 * t_r + l_r) * XS + 16 * mi);
-    const int tkc = tk < N ? tk : 0;
-    const float* dfac = reinterpret_cast<const float*>(xsm + img_inv_off(K, N)) + tkc * nblocks;
-    const float* Xs = reinterpret_cast<const float*>(xsm + img_sum_off(K, N)) + tkc * (K / 32);
+    q.xv0 = t_r < N && slot_r == (mi >> 1) % NS;        // even pairs
+    q.xv1 = t_r < N && slot_r == (2 + (mi >> 1)) % NS;  // odd pairs
+    q.xcol = smem_u32(xsm) + static_cast<uint32_t>((2 * t_r + l_r) * XS + 16 * mi);
+    const int tkc = q.tk < N ? q.tk : 0;
+    q.dfac = reinterpret_cast<const float*>(xsm + img_inv_off(K, N)) + tkc * nblocks;
+    q.Xs = reinterpret_cast<const float*>(xsm + img_sum_off(K, N)) + tkc * (K / 32);
+    return q;
+}
+
+// Warp-wide bounded wait on an mbarrier phase (see ring_wait).
+__device__ __forceinline__ void ring_barrier_wait(uint64_t* bar, uint32_t parity, volatile int* poisoned, int lane) {
+    if (mbar_test_wait(bar, parity)) return;
+    mbar_wait_warp(bar, parity, 4u, poisoned, lane);
+}
+
+// Waits for the current stage of the ring (warp-wide): a non-blocking test
+// first, then lane 0 polls with a short back-off, then every lane observes
+// the completed phase itself (ordering the landed copy's bytes before its
+// reads).
+__device__ __forceinline__ void ring_wait(Ring& R, int lane) {
+    if (mbar_test_wait(&R.full[R.slot], R.phase)) return;
+    mbar_wait_warp(&R.full[R.slot], R.phase, 2u, R.poisoned, lane);
+}
+
+// All segments of one Q4_K unit for this consumer warp; writes the warp's
+// partial sums of the unit's 16 rows (zeros where it had no item) to ub.
+template <int NP, int NT>
+__device__ __forceinline__ void q4k_unit(const OpInfo& op, const Q4Lane& q, Ring& R, uint32_t xzero, int lane,
+                                         int cw, float* ub) {
+    const int N = op.N, nblocks = op.K / 256;
+    const int g = lane >> 2, sl = q.sl, tk = q.tk;
+    const uint32_t wl = q.wl, xcol = q.xcol;
+    const bool xv0 = q.xv0, xv1 = q.xv1;
+    const float* dfac = q.dfac;
+    const float* Xs = q.Xs;
     float yg = 0.f, yh = 0.f;  // slot sl's part of vector tk, rows g and g + 8
     for (int sg = 0; sg < op.nseg; ++sg) {
         const int b0 = sg * op.seg_blocks;
@@ -610,7 +677,7 @@ __device__ __forceinline__ void q4k_unit(const OpInfo& op, Ring& R, const uint8_
         // for them)
         const int i0 = (cw - static_cast<int>(R.item_base % kCW) + kCW) % kCW;
         if (i0 < nb) {
-            mbar_wait_warp(&R.full[R.slot], R.phase, 2u, R.poisoned, lane);
+            ring_wait(R, lane);
             const uint8_t* stage = R.stages + R.slot * R.SB;
             for (int i = i0; i < nb; i += kCW) {
                 const int bg = b0 + i;
@@ -644,19 +711,20 @@ __global__ void __launch_bounds__(kThreads, 1) stream_gemv_kernel(const __grid_c
     uint8_t* xsm = smem + S * SB;
     uint8_t* zrow = xsm + L.x_bytes;                                     // 16 zero bytes: the Q4_K MMA's empty B rows
     float* ubuf = reinterpret_cast<float*>(zrow + 16);                   // [kUnitSlots][kCW][16][NT]
-    int* ucnt = reinterpret_cast<int*>(ubuf + kUnitSlots * kCW * kRows * NT);
-    uint64_t* full = reinterpret_cast<uint64_t*>(ucnt + kUnitSlots + 2);  // 8-byte aligned: kUnitSlots + 2 is even
+    UnitMeta* umeta = reinterpret_cast<UnitMeta*>(ubuf + kUnitSlots * kCW * kRows * NT);  // [kUnitSlots]
+    uint64_t* ubar = reinterpret_cast<uint64_t*>(umeta + kUnitSlots);    // [kUnitSlots]: all warps' partials written
+    uint64_t* full = ubar + kUnitSlots;
     uint64_t* empty = full + kMaxStages;
     volatile int* poisoned = reinterpret_cast<volatile int*>(empty + kMaxStages);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    for (int i = threadIdx.x; i < kUnitSlots; i += kThreads) ucnt[i] = 0;
     if (threadIdx.x < 4) reinterpret_cast<uint32_t*>(zrow)[threadIdx.x] = 0u;
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], kCW);
         }
+        for (int s = 0; s < kUnitSlots; ++s) mbar_init(&ubar[s], kCW);
         *poisoned = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -688,8 +756,41 @@ __global__ void __launch_bounds__(kThreads, 1) stream_gemv_kernel(const __grid_c
     __syncthreads();
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
+    if (warp == 0 && L.all_tma) {
+        // ---------------- copy warp, tensor-map path: lane 0 alone ----------------
+        // One thread issues every box: a warp-wide loop (shuffles, reconvergence)
+        // was measured to double the time between two issues.
+        if (lane != 0) return;
+        const uint64_t policy = evict_first_policy();
+        const int n_ops = T.n_ops, total = T.total_units;
+        int u = blockIdx.x, oi = 0;
+        while (oi + 1 < n_ops && u >= T.op[oi + 1].unit_begin) ++oi;
+        int s = 0;
+        uint32_t phase = 1;  // the first pass finds every slot free
+        for (; u < total; u += gridDim.x) {
+            while (oi + 1 < n_ops && u >= T.op[oi + 1].unit_begin) ++oi;
+            const OpInfo& op = T.op[oi];
+            const int bb = block_bytes_of(op.type), nseg = op.nseg, step = op.seg_blocks * bb;
+            const uint32_t box = static_cast<uint32_t>(kRows * op.wbox);
+            const int r0 = (u - op.unit_begin) * kRows;
+            const CUtensorMap* tm = &L.op[oi].tmap;
+            for (int sg = 0, col = 0; sg < nseg; ++sg, col += step) {
+                if (!mbar_wait(&empty[s], phase, 1u, poisoned)) return;
+                // one box: 16 rows x wbox bytes from the 16-byte-aligned column at or
+                // below the segment start (rows past M and columns past the row end
+                // read as zeros)
+                mbar_arrive_expect_tx(&full[s], box);
+                tma_2d_g2s(stages + s * SB, tm, (col & ~15) / 8, r0, &full[s], policy);
+                if (++s == S) {
+                    s = 0;
+                    phase ^= 1u;
+                }
+            }
+        }
+        return;
+    }
     if (warp == 0) {
-        // ---------------- copy warp: waits only for released slots ----------------
+        // ---------------- copy warp, any op copied row by row ----------------
         // The op's fields live in registers and are reloaded only when the op
         // changes: every shared-memory access here competes with the
         // consumers' traffic.
@@ -753,33 +854,56 @@ __global__ void __launch_bounds__(kThreads, 1) stream_gemv_kernel(const __grid_c
     const int ct = threadIdx.x - 32;  // 0 .. 32 kCW - 1
     const int cw = warp - 1;          // 0 .. kCW - 1
     Ring R{stages, full, empty, poisoned, SB, S, 0, 0u, 0u};
-    int staged = -1, uslot = 0;
-    SeqCursor cur;
-    cur.start(T);
-    while (!cur.done(T)) {
-        const int oi = cur.oi;
+    const int n_ops = T.n_ops, total = T.total_units;
+    int staged = -1, oi = -1, useq = 0;
+    Q4Lane q4{};
+    // Sums the 8 warps' partials of this CTA's unit number j (fixed order:
+    // deterministic) and writes its rows; done by the unit's owner warp
+    // kRedDelay units later, when the other warps are normally long done.
+    auto reduce_unit = [&](int j) {
+        const int slot = j % kUnitSlots;
+        ring_barrier_wait(&ubar[slot], static_cast<uint32_t>(j / kUnitSlots) & 1u, poisoned, lane);
+        const UnitMeta m = umeta[slot];
+        if (lane < kRows * m.n) {
+            const int r = lane / m.n, n = lane - r * m.n;
+            const float* vb = ubuf + slot * kCW * kRows * NT + r * NT + n;
+            float v = 0.f;
+#pragma unroll
+            for (int w2 = 0; w2 < kCW; ++w2) v += vb[w2 * kRows * NT];
+            if (r < m.rows) *reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(m.y) + n * m.y_nb1 + 4 * r) = v;
+        }
+    };
+    for (int u = blockIdx.x; u < total; u += gridDim.x, ++useq) {
+        if (oi < 0 || (oi + 1 < n_ops && u >= T.op[oi + 1].unit_begin)) {
+            // ---- next op: activation image (re)built when x or its layout changes ----
+            do {
+                ++oi;
+            } while (oi + 1 < n_ops && u >= T.op[oi + 1].unit_begin);
+            const OpInfo& op = T.op[oi];
+            if (staged < 0 || T.op[staged].x != op.x || T.op[staged].K != op.K || T.op[staged].N != op.N ||
+                T.op[staged].x_nb1 != op.x_nb1 || (T.op[staged].type == kTypeQ4_K) != (op.type == kTypeQ4_K) ||
+                (op.type != kTypeQ4_K && T.op[staged].type != op.type)) {
+                consumers_sync();  // nobody still reads the previous image
+                stage_activations(op, xsm, ct, lane, cw);
+                staged = oi;
+            }
+            if (op.type == kTypeQ4_K) q4 = (NT == 1 || op.N == 1) ? q4k_lane<1>(op, xsm, lane) : q4k_lane<2>(op, xsm, lane);
+        }
         const OpInfo& op = T.op[oi];
         const int N = op.N, K = op.K;
-        // ---- activation image (re)built when the op's x or layout changes ----
-        if (staged < 0 || T.op[staged].x != op.x || T.op[staged].K != K || T.op[staged].N != N ||
-            T.op[staged].x_nb1 != op.x_nb1 || (T.op[staged].type == kTypeQ4_K) != (op.type == kTypeQ4_K) ||
-            (op.type != kTypeQ4_K && T.op[staged].type != op.type)) {
-            consumers_sync();  // nobody still reads the previous image
-            stage_activations(op, xsm, ct, lane, cw);
-            staged = oi;
-        }
         const int bb = block_bytes_of(op.type);
         const int nblocks = K / block_elems_of(op.type);
-        const int r0 = (cur.u - op.unit_begin) * kRows;
+        const int r0 = (u - op.unit_begin) * kRows;
+        const int uslot = useq % kUnitSlots;
         // this warp's partial sums of the unit: every warp writes all 16 rows
         float* ub = ubuf + (uslot * kCW + cw) * kRows * NT;
 
         if (op.type == kTypeQ4_K) {
             // ================= Q4_K, integer tensor cores =================
             if (NT == 1 || N == 1)
-                q4k_unit<1, NT>(op, R, xsm, smem_u32(zrow), lane, cw, ub);
+                q4k_unit<1, NT>(op, q4, R, smem_u32(zrow), lane, cw, ub);
             else
-                q4k_unit<2, NT>(op, R, xsm, smem_u32(zrow), lane, cw, ub);
+                q4k_unit<2, NT>(op, q4, R, smem_u32(zrow), lane, cw, ub);
         } else {
             // ================= Q6_K / Q8_0, CUDA cores =================
             const int j = lane >> 3, c = lane & 7;
@@ -804,7 +928,7 @@ __global__ void __launch_bounds__(kThreads, 1) stream_gemv_kernel(const __grid_c
                     R.advance();
                     continue;
                 }
-                mbar_wait_warp(&R.full[R.slot], R.phase, 2u, poisoned, lane);
+                ring_wait(R, lane);
                 const uint8_t* stage = stages + R.slot * SB;
                 const uint32_t glo = wlo + static_cast<uint32_t>(b0 * bb);
                 const uint8_t* base[4];
@@ -858,42 +982,27 @@ __global__ void __launch_bounds__(kThreads, 1) stream_gemv_kernel(const __grid_c
                     if (c == 0 && n < N) ub[(4 * q + j) * NT + n] = v;
                 }
         }
-        // ---- unit hand-off: the last of the 8 warps sums the partials and writes the unit ----
+        // ---- unit hand-off: publish this warp's partials; the owner sums them later ----
+        if (useq % kCW == cw && lane == 0) {
+            UnitMeta m;
+            m.y = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(op.y) + 4LL * r0);
+            m.y_nb1 = op.y_nb1;
+            m.rows = min(kRows, op.M - r0);
+            m.n = N;
+            umeta[uslot] = m;
+        }
         __syncwarp();
-        int last = 0;
-        if (lane == 0) {
-            __threadfence_block();
-            last = atomicAdd(&ucnt[uslot], 1) == kCW - 1;
-        }
-        last = __shfl_sync(0xffffffffu, last, 0);
-        if (last) {
-            __threadfence_block();
-            if (lane < kRows * N) {
-                // fixed summation order over the warps: results are deterministic
-                const int r = lane / N, n = lane % N;
-                const volatile float* vb = ubuf + uslot * kCW * kRows * NT + r * NT + n;
-                float v = 0.f;
-#pragma unroll
-                for (int w2 = 0; w2 < kCW; ++w2) v += vb[w2 * kRows * NT];
-                if (r0 + r < op.M)
-                    *reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(op.y) + n * op.y_nb1 + 4LL * (r0 + r)) = v;
-            }
-            __syncwarp();
-            if (lane == 0) {
-                __threadfence_block();
-                *reinterpret_cast<volatile int*>(&ucnt[uslot]) = 0;
-            }
-        }
-        uslot = uslot + 1 == kUnitSlots ? 0 : uslot + 1;
-        // advance to the next unit (the segment loop above consumed all of this unit's stages)
-        cur.sg = op.nseg - 1;
-        cur.next(T);
+        if (lane == 0) mbar_arrive_cnt(&ubar[uslot], 1u);  // release: the warp's partial writes precede it
+        if (useq >= kRedDelay && (useq - kRedDelay) % kCW == cw) reduce_unit(useq - kRedDelay);
     }
+    // the last kRedDelay units of the CTA
+    for (int j = useq - kRedDelay; j < useq; ++j)
+        if (j >= 0 && j % kCW == cw) reduce_unit(j);
 }
 
 size_t smem_bytes(int stages, int stage_bytes, int x_bytes, int nt) {
     return static_cast<size_t>(stages) * static_cast<size_t>(stage_bytes) + static_cast<size_t>(x_bytes) +
-           16ull + 4ull * kUnitSlots * kCW * kRows * nt + 4ull * (kUnitSlots + 2) +
+           16ull + 4ull * kUnitSlots * kCW * kRows * nt + sizeof(UnitMeta) * kUnitSlots + 8ull * kUnitSlots +
            8ull * (2 * kMaxStages) + 16;
 }
 
@@ -990,6 +1099,8 @@ int launch_stream(const MulMatOp* ops, int n_ops, cudaStream_t stream, int num_s
         x_bytes = xb > x_bytes ? xb : x_bytes;
     }
     L.total_units = units;
+    L.all_tma = 1;
+    for (int i = 0; i < n_ops; ++i) L.all_tma &= L.op[i].use_tma;
     L.x_bytes = x_bytes;
     L.stage_bytes = kRows * wmax;
     const int nt = max_n <= 1 ? 1 : 2;
