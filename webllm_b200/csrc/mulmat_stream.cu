@@ -509,52 +509,47 @@ __device__ __forceinline__ void stage_activations(const OpInfo& op, uint8_t* xsm
         const int nblk = K / 256, XS = img_col_bytes(K);
         float* dfac = reinterpret_cast<float*>(xsm + img_inv_off(K, N));
         float* Xs = reinterpret_cast<float*>(xsm + img_sum_off(K, N));
-        // one (vector, block) per warp iteration, the next one's loads issued
-        // before this one's arithmetic
-        int tb = cw;
-        float4 n0 = make_float4(0.f, 0.f, 0.f, 0.f), n1 = n0;
-        if (tb < N * nblk) {
-            const int t = tb / nblk, b = tb - t * nblk;
-            const float4* xv = reinterpret_cast<const float4*>(xb + t * op.x_nb1) + b * 64 + 2 * lane;
-            n0 = __ldg(xv);
-            n1 = __ldg(xv + 1);
-        }
-        for (; tb < N * nblk; tb += kCW) {  // warp-uniform
-            const float4 v0 = n0, v1 = n1;
-            const int tn = tb + kCW;
-            if (tn < N * nblk) {
-                const int t = tn / nblk, b = tn - t * nblk;
-                const float4* xv = reinterpret_cast<const float4*>(xb + t * op.x_nb1) + b * 64 + 2 * lane;
-                n0 = __ldg(xv);
-                n1 = __ldg(xv + 1);
-            }
-            const int t = tb / nblk, b = tb - t * nblk;
-            float mx = fmaxf(fmaxf(fmaxf(fabsf(v0.x), fabsf(v0.y)), fmaxf(fabsf(v0.z), fabsf(v0.w))),
-                             fmaxf(fmaxf(fabsf(v1.x), fabsf(v1.y)), fmaxf(fabsf(v1.z), fabsf(v1.w))));
+        // one (vector, block) per half-warp: lane h = lane%16 covers elements
+        // 16h .. 16h+15; all of a round's loads are issued before any arithmetic
+        const int hw = lane >> 4, h = lane & 15;
+        for (int tb = 2 * cw + hw; tb - hw < N * nblk; tb += 2 * kCW) {  // warp-uniform
+            const bool act = tb < N * nblk;
+            const int t = act ? tb / nblk : 0, b = act ? tb - t * nblk : 0;
+            const float4* xv = reinterpret_cast<const float4*>(xb + t * op.x_nb1) + b * 64 + 4 * h;
+            float4 v[4];
 #pragma unroll
-            for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+            for (int k = 0; k < 4; ++k) v[k] = act ? __ldg(xv + k) : make_float4(0.f, 0.f, 0.f, 0.f);
+            float mx = 0.f;
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+                mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v[k].x), fabsf(v[k].y)), fmaxf(fabsf(v[k].z), fabsf(v[k].w))));
+#pragma unroll
+            for (int o = 8; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));  // within the half
             const float sc = mx > 0.f ? 127.f / mx : 0.f;
-            uint8_t* c0 = xsm + (2 * t) * XS + b * 256 + 8 * lane;
-            uint32_t p0[2], p1[2];
+            uint32_t p0[4], p1[4];
 #pragma unroll
-            for (int h = 0; h < 2; ++h) {
-                const float4 v = h ? v1 : v0;
-                const int q0 = __float2int_rn(v.x * sc), q1 = __float2int_rn(v.y * sc);  // |l0| <= 127
-                const int q2 = __float2int_rn(v.z * sc), q3 = __float2int_rn(v.w * sc);
-                p0[h] = pack_b4(q0, q1, q2, q3);
+            for (int k = 0; k < 4; ++k) {
+                const float4 e = v[k];
+                const int q0 = __float2int_rn(e.x * sc), q1 = __float2int_rn(e.y * sc);  // |l0| <= 127
+                const int q2 = __float2int_rn(e.z * sc), q3 = __float2int_rn(e.w * sc);
+                p0[k] = pack_b4(q0, q1, q2, q3);
                 // |l1| <= 64
-                p1[h] = pack_b4(__float2int_rn(fmaf(v.x, sc, -static_cast<float>(q0)) * 128.f),
-                                __float2int_rn(fmaf(v.y, sc, -static_cast<float>(q1)) * 128.f),
-                                __float2int_rn(fmaf(v.z, sc, -static_cast<float>(q2)) * 128.f),
-                                __float2int_rn(fmaf(v.w, sc, -static_cast<float>(q3)) * 128.f));
+                p1[k] = pack_b4(__float2int_rn(fmaf(e.x, sc, -static_cast<float>(q0)) * 128.f),
+                                __float2int_rn(fmaf(e.y, sc, -static_cast<float>(q1)) * 128.f),
+                                __float2int_rn(fmaf(e.z, sc, -static_cast<float>(q2)) * 128.f),
+                                __float2int_rn(fmaf(e.w, sc, -static_cast<float>(q3)) * 128.f));
             }
-            *reinterpret_cast<uint2*>(c0) = make_uint2(p0[0], p0[1]);
-            *reinterpret_cast<uint2*>(c0 + XS) = make_uint2(p1[0], p1[1]);
-            float a = ((v0.x + v0.y) + (v0.z + v0.w)) + ((v1.x + v1.y) + (v1.z + v1.w));
-            a += __shfl_xor_sync(0xffffffffu, a, 1);
-            a += __shfl_xor_sync(0xffffffffu, a, 2);
-            if ((lane & 3) == 0) Xs[t * (K / 32) + b * 8 + (lane >> 2)] = a;
-            if (lane == 0) dfac[t * nblk + b] = mx * (1.f / 2032.f);  // 1 / (16 s)
+            float a = 0.f;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) a += (v[k].x + v[k].y) + (v[k].z + v[k].w);
+            a += __shfl_xor_sync(0xffffffffu, a, 1);  // a sub-block is two lanes
+            if (act) {
+                uint8_t* c0 = xsm + (2 * t) * XS + b * 256 + 16 * h;
+                *reinterpret_cast<uint4*>(c0) = make_uint4(p0[0], p0[1], p0[2], p0[3]);
+                *reinterpret_cast<uint4*>(c0 + XS) = make_uint4(p1[0], p1[1], p1[2], p1[3]);
+                if ((h & 1) == 0) Xs[t * (K / 32) + b * 8 + (h >> 1)] = a;
+                if (h == 0) dfac[t * nblk + b] = mx * (1.f / 2032.f);  // 1 / (16 s)
+            }
         }
         consumers_sync();
     } else {
