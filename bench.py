@@ -219,6 +219,7 @@ def run_b200(args, rank: int, world: int, local_rank: int):
 
     from webllm_b200 import jsep, synth
     from webllm_b200.build_ext import build
+    from webllm_b200.tp import row_shard
 
     build()
     dev = torch.device("cuda", local_rank)
@@ -238,20 +239,27 @@ def run_b200(args, rank: int, world: int, local_rank: int):
         for gi, (kin, mats) in enumerate(groups):
             x = torch.randn(1, kin, device=dev, generator=gen.manual_seed(10_000 * li + 10 * gi))
             lx.append(x)
-            gops, gys, gathers = [], [], []
+            gops, gys = [], []
+            # the group's row shards share one output buffer, so the group needs
+            # one all-gather (a decode layer's outputs are 4-32 KB: the gather
+            # is latency-bound, one call per group instead of one per matrix)
+            pads = [row_shard(M, world, rank).padded for (_, _, M, _) in mats]
+            ybuf = torch.zeros(1, sum(pads), device=dev)
+            offs = [sum(pads[:i]) for i in range(len(pads))]
             for mi, (name, t, M, K) in enumerate(mats):
-                assert M % world == 0
-                Mr = M // world
+                # this rank's contiguous row shard; every rank reserves `padded` rows
+                # in the gather buffer (the shapes here divide evenly at 1/2/4/8)
+                sh = row_shard(M, world, rank)
+                Mr = sh.count
                 gen.manual_seed(1_000_000 + 10_000 * li + 100 * gi + 10 * mi + rank)
                 w = synth.weights_torch(gen, t, Mr, K, dev)
-                y = torch.empty(1, Mr, device=dev)
+                y = ybuf[:, offs[mi]:offs[mi] + sh.padded]
                 lw.append(w)
                 gys.append(y)
-                gathers.append(torch.empty(world, Mr, device=dev) if world > 1 else None)
                 gops.append(jsep.MulMatArgs(t, Mr, K, 1, w.data_ptr(), synth.row_bytes(t, K), x.data_ptr(), K,
                                             y.data_ptr(), Mr))
-            ly.append(gys)
-            lg.append(gathers)
+            ly.append((ybuf, gys))
+            lg.append(torch.empty(world * ybuf.numel(), device=dev) if world > 1 else None)
             lops.append(gops)
         W.append(lw)
         X.append(lx)
@@ -266,8 +274,7 @@ def run_b200(args, rank: int, world: int, local_rank: int):
             for gi in range(len(groups)):
                 jsep.mul_mat_batch(ops[li][gi], stream_ptr)
                 if world > 1:
-                    for y, g in zip(Y[li][gi], G[li][gi]):
-                        dist.all_gather_into_tensor(g, y)
+                    dist.all_gather_into_tensor(G[li][gi], Y[li][gi][0].view(-1))
 
     # ---- warm-up, then capture the step as one CUDA graph
     s = torch.cuda.current_stream()
@@ -312,7 +319,8 @@ def run_b200(args, rank: int, world: int, local_rank: int):
     # ---- e2e: pinned host activations in, outputs out, every step
     flat_x = [x for lx in X for x in lx]
     x_host = [torch.randn_like(x, device="cpu").pin_memory() for x in flat_x]
-    outs = [g if g is not None else y for ly, lg in zip(Y, G) for gys, gg in zip(ly, lg) for y, g in zip(gys, gg)]
+    # every group's gathered output (or, at one GPU, its output buffer)
+    outs = [g if g is not None else yb[0] for ly, lg in zip(Y, G) for yb, g in zip(ly, lg)]
     y_host = [torch.empty_like(o, device="cpu").pin_memory() for o in outs]
     h2d = sum(t.numel() * 4 for t in x_host)
     d2h = sum(t.numel() * 4 for t in y_host) if rank == 0 else 0

@@ -129,7 +129,13 @@ def mul_mat_f32(qtype: int, w: np.ndarray, x: np.ndarray, threads: int | None = 
 
 
 def max_threads() -> int:
-    return int(lib().oracle_max_threads())
+    """Host cores this process may run on (the CPU affinity set). Not the
+    OpenMP default, which launchers such as torchrun cap with
+    OMP_NUM_THREADS=1; mul_mat_f32 passes its thread count explicitly."""
+    try:
+        return max(1, len(os.sched_getaffinity(0)))
+    except (AttributeError, OSError):
+        return int(lib().oracle_max_threads())
 
 
 def rel_error(y: np.ndarray, r: np.ndarray) -> float:
