@@ -1,0 +1,80 @@
+"""GPU parity tests of the prefill path: Q4_K MUL_MAT with N > 64 vectors runs
+as a tcgen05 tensor-core GEMM (f16 dequantized weights and activations, f32
+accumulation).
+
+Bar: max relative error <= 2e-2 (rel = max|y - r| / max|r|) against
+ - the oracle's f64 dequant-then-dot (small and ragged shapes), and
+ - a plain PyTorch fp32 reference (fp32 matmul of the device-dequantized
+   weights, bit-exact with the oracle's dequantization) for the
+   Llama-3-8B prefill shapes (N = 512 tokens).
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from oracle import oracle as O
+from webllm_b200 import jsep, synth
+
+from test_gpu_mulmat import run_mul_mat
+
+pytestmark = pytest.mark.gpu
+
+PREFILL_TOL = 2e-2
+
+
+def counters():
+    c = jsep.WllmCounters()
+    jsep.load_library().wllm_get_counters(c)
+    return c
+
+
+@pytest.mark.parametrize("M,K,N", [
+    (128, 256, 128),     # one tile, one block
+    (128, 512, 65),      # smallest prefill N, partial vector tile
+    (200, 768, 130),     # partial row tile and partial vector tile
+    (384, 2048, 256),
+])
+def test_prefill_matches_oracle(runtime, M, K, N):
+    rng = np.random.default_rng(1000 + M + K + N)
+    w = synth.weights(rng, O.TYPE_Q4_K, M, K)
+    x = synth.activations(rng, N, K)
+    k0 = counters().kernels_launched
+    y = run_mul_mat(runtime, O.TYPE_Q4_K, w, x)
+    assert counters().kernels_launched - k0 == 2, "expected the f16 pre-pass and the tensor-core GEMM"
+    r = O.mul_mat_f64(O.TYPE_Q4_K, w, x)
+    assert O.rel_error(y, r) <= PREFILL_TOL
+
+
+def test_prefill_activation_magnitudes(runtime):
+    rng = np.random.default_rng(7)
+    M, K, N = 256, 1024, 96
+    w = synth.weights(rng, O.TYPE_Q4_K, M, K)
+    for scale in (1e-3, 30.0):
+        x = (synth.activations(rng, N, K) * scale).astype(np.float32)
+        y = run_mul_mat(runtime, O.TYPE_Q4_K, w, x)
+        r = O.mul_mat_f64(O.TYPE_Q4_K, w, x)
+        assert O.rel_error(y, r) <= PREFILL_TOL, scale
+
+
+@pytest.mark.parametrize("M,K", [(4096, 4096), (1024, 4096), (14336, 4096), (4096, 14336)])
+def test_prefill_llama3_8b_shapes_vs_torch_fp32(runtime, M, K):
+    import torch
+
+    dev = torch.device("cuda", 0)
+    N = 512
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(M * 7 + K)
+    w = synth.weights_torch(gen, O.TYPE_Q4_K, M, K, dev)
+    x = torch.randn(N, K, device=dev, generator=gen)
+    y = torch.empty(N, M, device=dev)
+    torch.cuda.synchronize()  # the library runs on its own stream
+    stream = jsep.library_stream()
+    jsep.mul_mat_device(O.TYPE_Q4_K, w.data_ptr(), w.shape[1], x.data_ptr(), K, y.data_ptr(), M, M, K, N, stream)
+    wf = torch.empty(M, K, device=dev)
+    jsep.dequantize_device(O.TYPE_Q4_K, w.data_ptr(), wf.data_ptr(), M * K, stream)
+    runtime.jsep_sync()
+    torch.backends.cuda.matmul.allow_tf32 = False
+    ref = (x.double() @ wf.double().t()).float()  # [N, M]
+    rel = ((y - ref).abs().max() / ref.abs().max()).item()
+    assert rel <= PREFILL_TOL, rel

@@ -241,10 +241,36 @@ const char* check_mulmat_op(const MulMatOp& op) {
     return nullptr;
 }
 
-int launch_mulmat(const MulMatOp* ops, int n_ops, cudaStream_t stream, int num_sms) {
-    if (n_ops >= 1 && n_ops <= kMaxOpsPerLaunch && stream_supported(ops, n_ops))
-        return launch_stream(ops, n_ops, stream, num_sms);
-    return launch_mulmat_general(ops, n_ops, stream);
+size_t mulmat_workspace_bytes(const MulMatOp* ops, int n_ops) {
+    size_t need = 0;
+    for (int i = 0; i < n_ops; ++i)
+        if (prefill_supported(ops[i])) {
+            const size_t b = prefill_workspace_bytes(ops[i]);
+            need = b > need ? b : need;
+        }
+    return need;
+}
+
+int launch_mulmat(const MulMatOp* ops, int n_ops, cudaStream_t stream, int num_sms, void* workspace,
+                  size_t workspace_bytes) {
+    if (n_ops < 1 || n_ops > kMaxOpsPerLaunch) return -static_cast<int>(cudaErrorInvalidValue);
+    // prefill-sized ops run as tensor-core GEMMs, one launch each; the rest together
+    int launched = 0;
+    MulMatOp rest[kMaxOpsPerLaunch];
+    int n_rest = 0;
+    for (int i = 0; i < n_ops; ++i) {
+        if (prefill_supported(ops[i]) && workspace && workspace_bytes >= prefill_workspace_bytes(ops[i])) {
+            const int rc = launch_prefill(ops[i], workspace, workspace_bytes, stream);
+            if (rc < 0) return rc;
+            launched += rc;
+        } else {
+            rest[n_rest++] = ops[i];
+        }
+    }
+    if (n_rest == 0) return launched;
+    const int rc = stream_supported(rest, n_rest) ? launch_stream(rest, n_rest, stream, num_sms)
+                                                  : launch_mulmat_general(rest, n_rest, stream);
+    return rc < 0 ? rc : launched + rc;
 }
 
 int launch_mulmat_general(const MulMatOp* ops, int n_ops, cudaStream_t stream) {

@@ -1,0 +1,431 @@
+// Prefill-regime quantized MUL_MAT (N >= kPrefillMinN activation vectors, Q4_K
+// weights): a tcgen05 tensor-core GEMM that dequantizes the GGUF blocks to f16
+// in shared memory.
+//
+//   y[m + M n] = sum_k W[m, k] x[k + K n]   (ggml MUL_MAT, matmul.ts:10-17)
+//
+// One CTA computes a 128 (rows of W) x 128 (vectors) tile of y with the
+// accumulator in tensor memory (TMEM, 128 lanes x 128 f32 columns). K is
+// walked in chunks of 64; each chunk is one 128-byte-swizzled, K-major shared
+// memory tile per operand (the canonical UMMA layout: row r at
+// (r/8)*1024 + (r%8)*128 bytes, its 16-byte piece j at position j ^ (r%8)).
+//
+//  - warp 0 (TMA): per 256-element Q4_K block, one 2D box of the 128 rows'
+//    raw blocks (128 x 144 B) into a raw ring; per 64-chunk, one 2D box of the
+//    f16 activations (64 x 128, TMA 128B swizzle) straight into the B tile.
+//  - warps 2..9 (dequant, 256 threads): thread (row r = t%128, half h = t/128)
+//    turns the 32 quants of sub-block 2p+h of row r (chunk p of the block) into
+//    f16 d*sc*q - dmin*m (the quant enters as the exact f16 1024 + q, minus
+//    1024, then one f16 FMA) and stores them into the A tile.
+//  - warp 1 (MMA): TMEM allocation; one elected thread issues the 4 K=16
+//    tcgen05.mma (M=128, N=128, f16 x f16 -> f32) of each chunk and commits
+//    them to the chunk's "stage free" barrier.
+//  - epilogue (warps 2..9): tcgen05.ld of the accumulator (warp w reads TMEM
+//    lanes 32 (w%4) .. +31, i.e. rows), f32 stores to y.
+//
+// The activations are converted to f16 by a pre-pass (x_to_f16_kernel) into
+// library workspace: N x K x 2 bytes, read by every row tile from L2.
+//
+// Every mbarrier wait is bounded; on timeout the CTA records an error code
+// (read by wllm_sync), stops issuing work, and still releases its TMEM.
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+#include "quant_blocks.cuh"
+#include "wllm_internal.h"
+
+namespace wllm {
+
+__device__ unsigned int g_prefill_error = 0;
+
+namespace {
+
+constexpr int kTileM = 128;                      // rows of W per CTA (TMEM lanes)
+constexpr int kTileN = 128;                      // vectors per CTA (TMEM columns)
+constexpr int kChunkK = 64;                      // K per stage (one 128-byte swizzle atom of f16)
+constexpr int kStages = 4;
+constexpr int kRawSlots = 2;                     // raw Q4_K blocks in flight (each feeds 4 chunks)
+constexpr int kRawBytes = kTileM * 144;          // 18432
+constexpr int kABytes = kTileM * kChunkK * 2;    // 16384
+constexpr int kBBytes = kTileN * kChunkK * 2;    // 16384
+constexpr int kDqWarps = 8;
+constexpr int kThreads = 32 * (2 + kDqWarps);    // TMA warp, MMA warp, dequant/epilogue warps
+constexpr uint32_t kSpinLimit = 1u << 26;
+
+struct PrefillArgs {
+    CUtensorMap wmap;   // weights: [M rows][row_bytes / 8] uint64, box 18 x 128 (one block column)
+    CUtensorMap xmap;   // f16 activations: [N][K], box 64 x 128, 128-byte swizzle
+    float* y;
+    int64_t y_nb1;      // bytes between output vectors
+    int32_t M, K, N;
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ bool mbar_try(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Bounded wait; a timeout poisons the CTA (every later wait returns at once).
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned code, volatile int* poisoned) {
+    for (uint32_t i = 0; i < kSpinLimit; ++i) {
+        if (mbar_try(bar, parity)) return true;
+        if ((i & 255u) == 255u && *poisoned) return false;
+    }
+    *poisoned = 1;
+    atomicOr(&g_prefill_error, code);
+    return false;
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void tma_2d(void* dst, const CUtensorMap* tm, int x, int y, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            smem_u32(dst)),
+        "l"(tm), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// UMMA shared-memory descriptor: K-major, 128-byte swizzle, 8-row groups
+// 1024 bytes apart (SBO), version 1.
+__device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr) {
+    return static_cast<uint64_t>((saddr >> 4) & 0x3FFFu) | (1ull << 16) | (64ull << 32) | (1ull << 46) |
+           (2ull << 61);
+}
+// Instruction descriptor, kind::f16: f16 A and B (K-major), f32 accumulator,
+// M = 128, N = kTileN.
+constexpr uint32_t kIdesc = (1u << 4) | (static_cast<uint32_t>(kTileN >> 3) << 17) | (static_cast<uint32_t>(kTileM >> 4) << 24);
+
+__device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %5, %5, %5}, p;\n\t}"
+        :
+        : "r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(kIdesc), "r"(accumulate), "r"(0u)
+        : "memory");
+}
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+
+// 16 consecutive f32 columns of this warp's 32 TMEM lanes.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+    uint32_t r[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// (d*sc, dmin*m) of sub-block j of a Q4_K header (get_scale_min_k4,
+// src/inference/jsep/ops/matmul.ts:408-424).
+__device__ __forceinline__ void q4k_sub_scale(const uint4 h, int j, float& s, float& mn) {
+    const float d = f16_bits_to_f32(h.x), dmin = f16_bits_to_f32(h.x >> 16);
+    const uint32_t w[3] = {h.y, h.z, h.w};
+    int sc, m;
+    q4k_scale_min(w, j, sc, m);
+    s = d * static_cast<float>(sc);
+    mn = dmin * static_cast<float>(m);
+}
+
+__global__ void __launch_bounds__(kThreads, 1) prefill_q4k_kernel(const __grid_constant__ PrefillArgs P) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    // 1024-byte alignment for the swizzled tiles
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* A = smem;                                   // [kStages][kABytes]
+    uint8_t* B = A + kStages * kABytes;                  // [kStages][kBBytes]
+    uint8_t* raw = B + kStages * kBBytes;                // [kRawSlots][kRawBytes]
+    uint64_t* b_full = reinterpret_cast<uint64_t*>(raw + kRawSlots * kRawBytes);
+    uint64_t* a_full = b_full + kStages;
+    uint64_t* st_free = a_full + kStages;
+    uint64_t* raw_full = st_free + kStages;
+    uint64_t* raw_free = raw_full + kRawSlots;
+    uint64_t* acc_full = raw_free + kRawSlots;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
+    volatile int* poisoned = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int m0 = blockIdx.x * kTileM, n0 = blockIdx.y * kTileN;
+    const int nblk = P.K / 256, nchunk = nblk * 4;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(&b_full[s], 1);
+            mbar_init(&a_full[s], kDqWarps);
+            mbar_init(&st_free[s], 1);
+        }
+        for (int r = 0; r < kRawSlots; ++r) {
+            mbar_init(&raw_full[r], 1);
+            mbar_init(&raw_free[r], kDqWarps);
+        }
+        mbar_init(acc_full, 1);
+        *poisoned = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1) {
+        // TMEM: 128 columns x 128 lanes of f32 accumulator
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(kTileN));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        // ---------------- TMA producer ----------------
+        if (lane == 0) {
+            asm volatile("prefetch.tensormap [%0];" ::"l"(&P.wmap) : "memory");
+            asm volatile("prefetch.tensormap [%0];" ::"l"(&P.xmap) : "memory");
+            for (int q = 0; q < nchunk; ++q) {
+                const int kb = q >> 2, c = q & 3;
+                if (c == 0) {
+                    const int r = kb % kRawSlots;
+                    if (kb >= kRawSlots && !mbar_wait(&raw_free[r], ((kb / kRawSlots) - 1) & 1, 1u, poisoned)) break;
+                    mbar_expect_tx(&raw_full[r], kRawBytes);
+                    tma_2d(raw + r * kRawBytes, &P.wmap, kb * 18, m0, &raw_full[r]);
+                }
+                const int s = q % kStages;
+                if (q >= kStages && !mbar_wait(&st_free[s], ((q / kStages) - 1) & 1, 1u, poisoned)) break;
+                mbar_expect_tx(&b_full[s], kBBytes);
+                tma_2d(B + s * kBBytes, &P.xmap, q * kChunkK, n0, &b_full[s]);
+            }
+        }
+    } else if (warp == 1) {
+        // ---------------- MMA issuer ----------------
+        for (int q = 0; q < nchunk; ++q) {
+            const int s = q % kStages;
+            const uint32_t par = (q / kStages) & 1;
+            int ok = 1;
+            if (lane == 0) ok = mbar_wait(&b_full[s], par, 2u, poisoned) && mbar_wait(&a_full[s], par, 2u, poisoned);
+            ok = __shfl_sync(0xffffffffu, ok, 0);
+            if (!ok) break;
+            tc_fence_after();
+            if (lane == 0) {
+                const uint32_t a0 = smem_u32(A + s * kABytes), b0 = smem_u32(B + s * kBBytes);
+#pragma unroll
+                for (int ks = 0; ks < kChunkK / 16; ++ks)  // K = 16 per MMA: 32 bytes along the swizzled row
+                    umma_f16(tmem, umma_desc_sw128(a0 + 32 * ks), umma_desc_sw128(b0 + 32 * ks),
+                             (q > 0 || ks > 0) ? 1u : 0u);
+                umma_commit(&st_free[s]);  // the stage is free once these MMAs have read it
+                if (q == nchunk - 1) umma_commit(acc_full);
+            }
+            __syncwarp();
+        }
+    } else {
+        // ---------------- dequant (then epilogue) ----------------
+        const int t = threadIdx.x - 64;          // 0..255
+        const int r = t & (kTileM - 1), h = t >> 7;  // row of the tile, half of the chunk
+        const int dw = warp - 2;
+        float s_sc = 0.f, s_mn = 0.f;
+        for (int q = 0; q < nchunk; ++q) {
+            const int kb = q >> 2, p = q & 3, rs = kb % kRawSlots, s = q % kStages;
+            if (p == 0 && !mbar_wait(&raw_full[rs], (kb / kRawSlots) & 1, 3u, poisoned)) break;
+            if (q >= kStages && !mbar_wait(&st_free[s], ((q / kStages) - 1) & 1, 3u, poisoned)) break;
+            const uint8_t* blk = raw + rs * kRawBytes + r * 144;
+            const uint4 hdr = *reinterpret_cast<const uint4*>(blk);
+            q4k_sub_scale(hdr, 2 * p + h, s_sc, s_mn);
+            const __half2 sc2 = __float2half2_rn(s_sc), mn2 = __float2half2_rn(-s_mn);
+            const __half2 k1024 = __float2half2_rn(1024.f);
+            // the 32 bytes of pair p; this thread's quants are their low (h = 0) or
+            // high (h = 1) nibbles: elements 64p + 32h + l, l = 0..31
+            const uint4* qs = reinterpret_cast<const uint4*>(blk + 16 + 32 * p);
+            const uint4 v0 = qs[0], v1 = qs[1];
+            const uint32_t wv[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+            uint32_t out[16];  // 32 f16, element order l = 0..31
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const uint32_t nib = h ? ((wv[i] >> 4) & 0x0F0F0F0Fu) : (wv[i] & 0x0F0F0F0Fu);
+                // f16 1024 + q (exact) for bytes (0, 1) and (2, 3): 0x64 in each high byte
+                const uint32_t e01 = __byte_perm(nib, 0x00006464u, 0x5140u);
+                const uint32_t e23 = __byte_perm(nib, 0x00006464u, 0x5342u);
+                __half2 q01 = __hsub2(*reinterpret_cast<const __half2*>(&e01), k1024);
+                __half2 q23 = __hsub2(*reinterpret_cast<const __half2*>(&e23), k1024);
+                const __half2 w01 = __hfma2(q01, sc2, mn2), w23 = __hfma2(q23, sc2, mn2);
+                out[2 * i] = *reinterpret_cast<const uint32_t*>(&w01);
+                out[2 * i + 1] = *reinterpret_cast<const uint32_t*>(&w23);
+            }
+            // row r, k = 32h + l of this chunk: 16-byte pieces j = 4h .. 4h+3,
+            // stored at position j ^ (r % 8) of the row (128-byte swizzle)
+            uint8_t* arow = A + s * kABytes + (r >> 3) * 1024 + (r & 7) * 128;
+#pragma unroll
+            for (int jj = 0; jj < 4; ++jj) {
+                const int j = 4 * h + jj;
+                *reinterpret_cast<uint4*>(arow + ((j ^ (r & 7)) << 4)) =
+                    make_uint4(out[4 * jj], out[4 * jj + 1], out[4 * jj + 2], out[4 * jj + 3]);
+            }
+            // generic-proxy writes before the tensor core's (async proxy) reads
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(&a_full[s]);
+                if (p == 3) mbar_arrive(&raw_free[rs]);
+            }
+        }
+        // ---------------- epilogue ----------------
+        const bool ok = mbar_wait(acc_full, 0, 4u, poisoned);
+        tc_fence_after();
+        if (ok) {
+            const int quarter = warp & 3;              // TMEM lanes 32*quarter .. +31 = rows
+            const int col0 = (dw < 4) ? 0 : kTileN / 2;
+            const int row = m0 + 32 * quarter + lane;
+#pragma unroll 1
+            for (int cc = 0; cc < kTileN / 2; cc += 16) {
+                float v[16];
+                tmem_ld16(tmem + (static_cast<uint32_t>(32 * quarter) << 16) + static_cast<uint32_t>(col0 + cc), v);
+                if (row < P.M) {
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) {
+                        const int n = n0 + col0 + cc + i;
+                        if (n < P.N)
+                            *reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(P.y) + n * P.y_nb1 + 4LL * row) = v[i];
+                    }
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTileN));
+    }
+}
+
+// f32 activations [N][K] (vector stride x_nb1 bytes) -> contiguous f16 [N][K].
+__global__ void x_to_f16_kernel(const float* __restrict__ x, int64_t x_nb1, __half* __restrict__ x16, int K, int N) {
+    const int64_t total4 = static_cast<int64_t>(N) * (K / 4);
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total4;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t n = i / (K / 4), k4 = i - n * (K / 4);
+        const float4 v = *reinterpret_cast<const float4*>(reinterpret_cast<const uint8_t*>(x) + n * x_nb1 + 16 * k4);
+        __half2* o = reinterpret_cast<__half2*>(x16 + n * K + 4 * k4);
+        o[0] = __floats2half2_rn(v.x, v.y);
+        o[1] = __floats2half2_rn(v.z, v.w);
+    }
+}
+
+typedef CUresult (*EncodeFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                             const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                             CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeFn encoder() {
+    static EncodeFn fn = [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            p = nullptr;
+        cudaGetLastError();
+        return reinterpret_cast<EncodeFn>(p);
+    }();
+    return fn;
+}
+
+constexpr size_t kSmemBytes = 1024 /* alignment */ + kStages * (kABytes + kBBytes) + kRawSlots * kRawBytes +
+                              8 * (3 * kStages + 2 * kRawSlots + 1) + 16;
+
+}  // namespace
+
+bool prefill_supported(const MulMatOp& o) {
+    if (o.type != kTypeQ4_K || o.N < kPrefillMinN || o.ne2 != 1 || o.ne3 != 1) return false;
+    if (o.K % 256 != 0 || o.M < 1) return false;
+    const int64_t row_bytes = static_cast<int64_t>(o.K / 256) * 144;
+    if ((reinterpret_cast<uintptr_t>(o.w) | static_cast<uintptr_t>(o.w_nb1)) & 15) return false;  // TMA rows
+    if (o.w_nb1 < row_bytes) return false;
+    if ((reinterpret_cast<uintptr_t>(o.x) | static_cast<uintptr_t>(o.x_nb1)) & 15) return false;  // float4 reads
+    return encoder() != nullptr;
+}
+
+size_t prefill_workspace_bytes(const MulMatOp& o) { return static_cast<size_t>(o.N) * o.K * 2 + 256; }
+
+int launch_prefill(const MulMatOp& o, void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+    if (!prefill_supported(o)) return -static_cast<int>(cudaErrorInvalidValue);
+    if (!workspace || workspace_bytes < prefill_workspace_bytes(o) || (reinterpret_cast<uintptr_t>(workspace) & 255))
+        return -static_cast<int>(cudaErrorInvalidValue);
+    __half* x16 = static_cast<__half*>(workspace);
+    {
+        const int64_t total4 = static_cast<int64_t>(o.N) * (o.K / 4);
+        const int threads = 256;
+        const int64_t want = (total4 + threads - 1) / threads;
+        const int blocks = static_cast<int>(want < 4096 ? want : 4096);
+        x_to_f16_kernel<<<blocks, threads, 0, stream>>>(o.x, o.x_nb1, x16, o.K, o.N);
+        const cudaError_t e = cudaGetLastError();
+        if (e != cudaSuccess) return -static_cast<int>(e);
+    }
+    PrefillArgs P{};
+    const EncodeFn enc = encoder();
+    {
+        const cuuint64_t dims[2] = {static_cast<cuuint64_t>(o.K / 256) * 18, static_cast<cuuint64_t>(o.M)};
+        const cuuint64_t strides[1] = {static_cast<cuuint64_t>(o.w_nb1)};
+        const cuuint32_t box[2] = {18, kTileM};
+        const cuuint32_t es[2] = {1, 1};
+        if (enc(&P.wmap, CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, const_cast<uint8_t*>(o.w), dims, strides, box, es,
+                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return -static_cast<int>(cudaErrorInvalidValue);
+    }
+    {
+        const cuuint64_t dims[2] = {static_cast<cuuint64_t>(o.K), static_cast<cuuint64_t>(o.N)};
+        const cuuint64_t strides[1] = {static_cast<cuuint64_t>(o.K) * 2};
+        const cuuint32_t box[2] = {kChunkK, kTileN};
+        const cuuint32_t es[2] = {1, 1};
+        if (enc(&P.xmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, x16, dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return -static_cast<int>(cudaErrorInvalidValue);
+    }
+    P.y = o.y;
+    P.y_nb1 = o.y_nb1;
+    P.M = o.M;
+    P.K = o.K;
+    P.N = o.N;
+    static bool configured = false;
+    if (!configured) {
+        const cudaError_t e = cudaFuncSetAttribute(prefill_q4k_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                   static_cast<int>(kSmemBytes));
+        if (e != cudaSuccess) return -static_cast<int>(e);
+        configured = true;
+    }
+    const dim3 grid((o.M + kTileM - 1) / kTileM, (o.N + kTileN - 1) / kTileN);
+    prefill_q4k_kernel<<<grid, kThreads, kSmemBytes, stream>>>(P);
+    const cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? 2 : -static_cast<int>(e);
+}
+
+unsigned read_and_clear_prefill_error() {
+    unsigned v = 0;
+    if (cudaMemcpyFromSymbol(&v, g_prefill_error, sizeof(v)) != cudaSuccess) return 0xFFFFFFFFu;
+    if (v) {
+        const unsigned z = 0;
+        cudaMemcpyToSymbol(g_prefill_error, &z, sizeof(z));
+    }
+    return v;
+}
+
+}  // namespace wllm

@@ -217,12 +217,6 @@ __device__ __forceinline__ void consumers_sync() {
 // Four 8x8 b16 matrices from shared memory; lane l supplies the row address
 // for row l%8 of matrix l/8 and receives, of each matrix, bytes 4(l%4)..+3 of
 // row l/4.
-__device__ __forceinline__ void ldmatrix_x4(uint32_t (&r)[4], const void* row_addr) {
-    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
-                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-                 : "r"(smem_u32(row_addr)));
-}
-
 __device__ __forceinline__ void ldmatrix_x4_at(uint32_t (&r)[4], uint32_t smem_addr) {
     asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
                  : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
@@ -236,15 +230,6 @@ __device__ __forceinline__ void imma_u8s8_acc(int (&d)[4], uint32_t a0, uint32_t
         "{%0,%1,%2,%3};"
         : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-}
-
-// D = A (16x32 u8, row) * B (32x8 s8, col), s32 accumulate from zero.
-__device__ __forceinline__ void imma_u8s8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
-                                          uint32_t b0, uint32_t b1) {
-    asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-        "{%10,%10,%10,%10};"
-        : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
-        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
 }
 
 __host__ __device__ __forceinline__ int seg_cap(int type) {
@@ -462,7 +447,6 @@ __device__ __forceinline__ void item_q8_0(const uint8_t* blk, const float4 (&xr)
     for (int n = 0; n < NT; ++n) acc[n] += d * (s[n].x + s[n].y);
 }
 
-// Walks the (unit, segment) sequence of this CTA.
 // Per-op fields the kernel reads in its loops, copied from the parameter
 // block into shared memory at entry: the parameter block (with one tensor map
 // per op) is larger than the constant cache, and dynamically indexed reads of
@@ -481,23 +465,6 @@ struct OpTable {
     int32_t n_ops, total_units;
 };
 
-struct SeqCursor {
-    int u, sg, oi;
-    __device__ __forceinline__ void start(const OpTable& T) {
-        u = blockIdx.x;
-        sg = 0;
-        oi = 0;
-        while (oi + 1 < T.n_ops && u >= T.op[oi + 1].unit_begin) ++oi;
-    }
-    __device__ __forceinline__ bool done(const OpTable& T) const { return u >= T.total_units; }
-    __device__ __forceinline__ void next(const OpTable& T) {
-        if (++sg >= T.op[oi].nseg) {
-            sg = 0;
-            u += gridDim.x;
-            while (oi + 1 < T.n_ops && u >= T.op[oi + 1].unit_begin) ++oi;
-        }
-    }
-};
 
 // Builds the activation image of `op` in shared memory (all consumer threads;
 // one L2 round trip per vector).

@@ -51,6 +51,8 @@ struct State {
     std::string last_error;
     void* scratch = nullptr;  // divert target for aliased dst
     uint64_t scratch_cap = 0;
+    void* workspace = nullptr;  // kernel workspace (f16 activations of the prefill GEMM)
+    uint64_t workspace_cap = 0;
     std::unordered_map<int32_t, AsyncRead> reads;
     int32_t next_request = 1;
     bool capturing = false;
@@ -122,6 +124,9 @@ int32_t release_all(State& s) {
     if (s.scratch) cudaFree(s.scratch);
     s.scratch = nullptr;
     s.scratch_cap = 0;
+    if (s.workspace) cudaFree(s.workspace);
+    s.workspace = nullptr;
+    s.workspace_cap = 0;
     for (auto& kv : s.reads) {
         if (kv.second.done) cudaEventDestroy(kv.second.done);
         if (kv.second.pinned) cudaFreeHost(kv.second.pinned);
@@ -293,8 +298,34 @@ void* get_scratch(State& s, uint64_t bytes) {
     return s.scratch;
 }
 
+// Grows the kernel workspace to `bytes` (kept across calls; not while a graph
+// is being recorded, since that cannot allocate or wait).
+void* get_workspace(State& s, uint64_t bytes) {
+    if (s.workspace_cap >= bytes) return s.workspace;
+    if (s.capturing) return nullptr;
+    if (s.workspace) {
+        cudaStreamSynchronize(s.stream);
+        cudaFree(s.workspace);
+        s.counters.bytes_reserved -= s.workspace_cap;
+    }
+    s.workspace = nullptr;
+    s.workspace_cap = 0;
+    if (cudaMalloc(&s.workspace, bytes) != cudaSuccess) {
+        cudaGetLastError();
+        return nullptr;
+    }
+    s.workspace_cap = bytes;
+    s.counters.bytes_reserved += bytes;
+    return s.workspace;
+}
+
 int32_t launch(State& s, const MulMatOp* ops, int n, cudaStream_t stream) {
-    const int rc = wllm::launch_mulmat(ops, n, stream, s.num_sms);
+    const size_t need = wllm::mulmat_workspace_bytes(ops, n);
+    void* ws = need ? get_workspace(s, need) : nullptr;
+    if (need && !ws)
+        return fail(s, "MUL_MAT: cannot %s %llu bytes of kernel workspace",
+                    s.capturing ? "grow (while recording a graph) to" : "allocate", (unsigned long long)need);
+    const int rc = wllm::launch_mulmat(ops, n, stream, s.num_sms, ws, ws ? s.workspace_cap : 0);
     if (rc < 0) return cuda_fail(s, static_cast<cudaError_t>(-rc), "MUL_MAT launch");
     if (s.capturing) s.captured_kernels += static_cast<uint64_t>(rc);
     else s.counters.kernels_launched += static_cast<uint64_t>(rc);
@@ -615,7 +646,7 @@ int32_t wllm_sync(void) {
     if (e != cudaSuccess) return cuda_fail(s, e, "wllm_sync");
     e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(s, e, "wllm_sync (pending error)");
-    const unsigned kerr = wllm::read_and_clear_stream_error();
+    const unsigned kerr = wllm::read_and_clear_stream_error() | (wllm::read_and_clear_prefill_error() << 8);
     if (kerr) return fail(s, "wllm_sync: a kernel gave up waiting on a pipeline barrier (code 0x%x)", kerr);
     return WLLM_STATUS_OK;
 }

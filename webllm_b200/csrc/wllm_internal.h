@@ -55,7 +55,8 @@ const char* check_mulmat_op(const MulMatOp& op);
 // Enqueue n_ops independent MUL_MAT ops (1 <= n_ops <= kMaxOpsPerLaunch)
 // on `stream`. Returns the number of kernels launched (>= 1) or a negative
 // cudaError_t on launch failure.
-int launch_mulmat(const MulMatOp* ops, int n_ops, cudaStream_t stream, int num_sms);
+int launch_mulmat(const MulMatOp* ops, int n_ops, cudaStream_t stream, int num_sms, void* workspace = nullptr,
+                  size_t workspace_bytes = 0);
 // The general kernel only (every shape; used by tests to compare paths).
 int launch_mulmat_general(const MulMatOp* ops, int n_ops, cudaStream_t stream);
 
@@ -65,6 +66,20 @@ bool stream_supported(const MulMatOp* ops, int n_ops);
 int launch_stream(const MulMatOp* ops, int n_ops, cudaStream_t stream, int num_sms);
 // Error code recorded by a bounded wait that timed out (0 = none); clears it.
 unsigned read_and_clear_stream_error();
+
+// Prefill GEMM (mulmat_prefill.cu): Q4_K weights with N >= kPrefillMinN
+// vectors on tcgen05 tensor cores (f16 operands, f32 accumulation). The
+// activations are first converted to f16 into caller-provided workspace of
+// prefill_workspace_bytes(op) bytes (256-byte aligned). Returns the number of
+// kernels launched (2) or a negative cudaError_t.
+constexpr int kPrefillMinN = 65;
+bool prefill_supported(const MulMatOp& op);
+size_t prefill_workspace_bytes(const MulMatOp& op);
+int launch_prefill(const MulMatOp& op, void* workspace, size_t workspace_bytes, cudaStream_t stream);
+unsigned read_and_clear_prefill_error();
+
+// Workspace the launch of `ops` needs (0 if none).
+size_t mulmat_workspace_bytes(const MulMatOp* ops, int n_ops);
 
 // Device dequantization of n elements to f32 (bit-exact with the oracle).
 int launch_dequantize(int type, const void* src, float* dst, int64_t n, cudaStream_t stream);
