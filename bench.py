@@ -33,6 +33,7 @@ import subprocess
 import sys
 import tempfile
 import time
+import zlib
 
 REPO = os.path.dirname(os.path.abspath(__file__))
 if REPO not in sys.path:
@@ -54,6 +55,7 @@ def parse_args():
     ap.add_argument("--layers", type=int, default=28)
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU-baseline sample budget")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-prefill", action="store_true", help="skip the prefill GEMM measurement")
     return ap.parse_args()
 
 
@@ -64,6 +66,70 @@ def measured_peaks():
             d = json.load(f)
         return float(d["hbm_gbs"]), "measured"
     return FALLBACK_HBM_GBS, "fallback"
+
+
+def measured_tensor_peak():
+    """Dense bf16/f16 tensor peak in TFLOP/s: the burst figure (a GEMM timed
+    alone) from MEASURED_PEAKS.json, else the fallback."""
+    p = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        if "bf16_tflops" in d:
+            return float(d["bf16_tflops"]), "measured bf16_tflops (burst, cuBLAS)"
+    return 1590.0, "fallback (1.59 PFLOP/s burst)"
+
+
+def prefill_measure(dev, reps: int = 10, warmup: int = 3):
+    """Llama-3-8B prefill GEMMs (N = 512 tokens, Q4_K): each MUL_MAT is the
+    f16 pre-pass plus the tcgen05 GEMM. Two weight copies per shape (156 MB,
+    more than L2) alternate between replays. Returns the JSON object."""
+    import torch
+
+    from webllm_b200 import jsep, synth
+
+    N = 512
+    stream_ptr = jsep.library_stream()
+    lib_stream = torch.cuda.ExternalStream(stream_ptr)
+    gen = torch.Generator(device=dev)
+    shapes, per = [], []
+    for name, t, M, K in synth.LLAMA3_8B_PREFILL:
+        gen.manual_seed(zlib.crc32(name.encode()))
+        ws = [synth.weights_torch(gen, t, M, K, dev) for _ in range(2)]
+        x = torch.randn(N, K, device=dev, generator=gen)
+        y = torch.empty(N, M, device=dev)
+        shapes.append((name, t, M, K, ws, x, y))
+    torch.cuda.synchronize()
+
+    def run(copy: int, only=None):
+        for i, (name, t, M, K, ws, x, y) in enumerate(shapes):
+            if only is None or i == only:
+                jsep.mul_mat_device(t, ws[copy].data_ptr(), ws[copy].shape[1], x.data_ptr(), K, y.data_ptr(), M, M,
+                                    K, N, stream_ptr)
+
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    for i, (name, t, M, K, ws, x, y) in enumerate(shapes):
+        for w in range(warmup):
+            run(w & 1, i)
+        with torch.cuda.stream(lib_stream):
+            ev0.record()
+            for r in range(reps):
+                run(r & 1, i)
+            ev1.record()
+        ev1.synchronize()
+        ms = ev0.elapsed_time(ev1) / reps
+        per.append({"shape": f"{M}x{K}", "n": N, "us": round(ms * 1e3, 2),
+                    "tflops": round(2.0 * M * N * K / (ms * 1e-3) / 1e12, 1)})
+    total_flop = sum(2.0 * M * N * K for (_, _, M, K, _, _, _) in shapes)
+    total_us = sum(p["us"] for p in per)
+    tflops = total_flop / (total_us * 1e-6) / 1e12
+    peak, src = measured_tensor_peak()
+    return {"workload": "llama-3-8b prefill GEMMs (Q4_K 4096x4096, 1024x4096, 14336x4096, 4096x14336; 512 tokens)",
+            "value": round(tflops, 1), "unit": "TFLOP/s", "dtype": "f16 x f16 -> f32 (tcgen05)",
+            "per_shape": per,
+            "roofline": {"bound": "tensor", "achieved": round(tflops, 1), "peak": peak, "unit": "TFLOP/s",
+                         "frac": round(tflops / peak, 4), "peak_source": src,
+                         "note": "time includes the f32->f16 activation pre-pass of each MUL_MAT"}}
 
 
 def layer_groups():
@@ -352,6 +418,11 @@ def run_b200(args, rank: int, world: int, local_rank: int):
     if world == 1:
         jsep_e2e = jsep_path_e2e(args, layers)
 
+    # ---- prefill GEMMs (tensor cores), rank 0 at one GPU
+    prefill = None
+    if world == 1 and not args.no_prefill:
+        prefill = prefill_measure(dev)
+
     total_bytes = step_bytes(layers)
     gbs = total_bytes / (dev_ms * 1e-3) / 1e9
     peak, peak_src = measured_peaks()
@@ -383,6 +454,8 @@ def run_b200(args, rank: int, world: int, local_rank: int):
         }
         if jsep_e2e is not None:
             line["e2e_c_abi"] = jsep_e2e
+        if prefill is not None:
+            line["prefill"] = prefill
     if world > 1:
         del graph
         torch.cuda.synchronize()

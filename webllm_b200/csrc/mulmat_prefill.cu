@@ -6,20 +6,25 @@
 //
 // One CTA computes a 128 (rows of W) x 128 (vectors) tile of y with the
 // accumulator in tensor memory (TMEM, 128 lanes x 128 f32 columns). K is
-// walked in chunks of 64; each chunk is one 128-byte-swizzled, K-major shared
-// memory tile per operand (the canonical UMMA layout: row r at
-// (r/8)*1024 + (r%8)*128 bytes, its 16-byte piece j at position j ^ (r%8)).
+// walked in chunks of 64.
 //
 //  - warp 0 (TMA): per 256-element Q4_K block, one 2D box of the 128 rows'
 //    raw blocks (128 x 144 B) into a raw ring; per 64-chunk, one 2D box of the
-//    f16 activations (64 x 128, TMA 128B swizzle) straight into the B tile.
-//  - warps 2..9 (dequant, 256 threads): thread (row r = t%128, half h = t/128)
-//    turns the 32 quants of sub-block 2p+h of row r (chunk p of the block) into
-//    f16 d*sc*q - dmin*m (the quant enters as the exact f16 1024 + q, minus
-//    1024, then one f16 FMA) and stores them into the A tile.
+//    f16 activations (64 x 128, TMA 128-byte swizzle) into a B stage: the
+//    canonical K-major UMMA layout (vector n at (n/8)*1024 + (n%8)*128 bytes,
+//    its 16-byte piece j at position j ^ (n%8)).
+//  - warps 2..9 (dequant, 256 threads): warp w handles rows 32 (w%4) + lane
+//    (the TMEM lanes it may access) and half h = (w-2)/4 of each chunk: it turns
+//    the 32 quants of sub-block 2p+h (chunk p of the block) into f16
+//    d*sc*q - dmin*m (the quant enters as the exact f16 1024 + q, minus 1024,
+//    then one f16 FMA) and stores them with tcgen05.st straight into the A
+//    operand's TMEM columns (row = lane, two f16 per column). The weights thus
+//    never pass through shared memory, whose bandwidth the MMAs' B reads and
+//    the TMA writes need.
 //  - warp 1 (MMA): TMEM allocation; one elected thread issues the 4 K=16
-//    tcgen05.mma (M=128, N=128, f16 x f16 -> f32) of each chunk and commits
-//    them to the chunk's "stage free" barrier.
+//    tcgen05.mma (A from TMEM, B from shared memory; M=128, N=128,
+//    f16 x f16 -> f32) of each chunk and commits them to the chunk's "stage
+//    free" barrier.
 //  - epilogue (warps 2..9): tcgen05.ld of the accumulator (warp w reads TMEM
 //    lanes 32 (w%4) .. +31, i.e. rows), f32 stores to y.
 //
@@ -44,13 +49,17 @@ namespace {
 constexpr int kTileM = 128;                      // rows of W per CTA (TMEM lanes)
 constexpr int kTileN = 128;                      // vectors per CTA (TMEM columns)
 constexpr int kChunkK = 64;                      // K per stage (one 128-byte swizzle atom of f16)
-constexpr int kStages = 4;
+constexpr int kStages = 4;                       // B stages in smem, A stages in TMEM
 constexpr int kRawSlots = 2;                     // raw Q4_K blocks in flight (each feeds 4 chunks)
 constexpr int kRawBytes = kTileM * 144;          // 18432
-constexpr int kABytes = kTileM * kChunkK * 2;    // 16384
 constexpr int kBBytes = kTileN * kChunkK * 2;    // 16384
 constexpr int kDqWarps = 8;
 constexpr int kThreads = 32 * (2 + kDqWarps);    // TMA warp, MMA warp, dequant/epilogue warps
+constexpr int kACols = kChunkK / 2;              // TMEM columns of one A stage (two f16 per column)
+// accumulator (kTileN) + kStages A stages: 256 of the SM's 512 columns, so two
+// CTAs (about 103 KB of shared memory each) share an SM
+constexpr int kTmemCols = 256;
+static_assert(kTileN + kStages * kACols <= kTmemCols, "TMEM budget");
 constexpr uint32_t kSpinLimit = 1u << 26;
 
 struct PrefillArgs {
@@ -112,13 +121,24 @@ __device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr) {
 // M = 128, N = kTileN.
 constexpr uint32_t kIdesc = (1u << 4) | (static_cast<uint32_t>(kTileN >> 3) << 17) | (static_cast<uint32_t>(kTileM >> 4) << 24);
 
-__device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
+// D (TMEM) += A (TMEM, K-major) * B (shared memory descriptor).
+__device__ __forceinline__ void umma_f16_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t accumulate) {
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
         "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %5, %5, %5}, p;\n\t}"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, {%5, %5, %5, %5}, p;\n\t}"
         :
-        : "r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(kIdesc), "r"(accumulate), "r"(0u)
+        : "r"(tmem_d), "r"(tmem_a), "l"(bdesc), "r"(kIdesc), "r"(accumulate), "r"(0u)
+        : "memory");
+}
+
+// 16 consecutive 32-bit TMEM columns of this warp's 32 lanes.
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+            taddr),
+        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+        "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
         : "memory");
 }
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
@@ -141,23 +161,11 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
     for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-// (d*sc, dmin*m) of sub-block j of a Q4_K header (get_scale_min_k4,
-// src/inference/jsep/ops/matmul.ts:408-424).
-__device__ __forceinline__ void q4k_sub_scale(const uint4 h, int j, float& s, float& mn) {
-    const float d = f16_bits_to_f32(h.x), dmin = f16_bits_to_f32(h.x >> 16);
-    const uint32_t w[3] = {h.y, h.z, h.w};
-    int sc, m;
-    q4k_scale_min(w, j, sc, m);
-    s = d * static_cast<float>(sc);
-    mn = dmin * static_cast<float>(m);
-}
-
-__global__ void __launch_bounds__(kThreads, 1) prefill_q4k_kernel(const __grid_constant__ PrefillArgs P) {
+__global__ void __launch_bounds__(kThreads, 2) prefill_q4k_kernel(const __grid_constant__ PrefillArgs P) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     // 1024-byte alignment for the swizzled tiles
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t* A = smem;                                   // [kStages][kABytes]
-    uint8_t* B = A + kStages * kABytes;                  // [kStages][kBBytes]
+    uint8_t* B = smem;                                   // [kStages][kBBytes]
     uint8_t* raw = B + kStages * kBBytes;                // [kRawSlots][kRawBytes]
     uint64_t* b_full = reinterpret_cast<uint64_t*>(raw + kRawSlots * kRawBytes);
     uint64_t* a_full = b_full + kStages;
@@ -189,7 +197,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_q4k_kernel(const __grid_c
     if (warp == 1) {
         // TMEM: 128 columns x 128 lanes of f32 accumulator
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                     "r"(kTileN));
+                     "r"(kTmemCols));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
     }
     tc_fence_before();
@@ -227,11 +235,10 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_q4k_kernel(const __grid_c
             if (!ok) break;
             tc_fence_after();
             if (lane == 0) {
-                const uint32_t a0 = smem_u32(A + s * kABytes), b0 = smem_u32(B + s * kBBytes);
+                const uint32_t a0 = tmem + static_cast<uint32_t>(kTileN + s * kACols), b0 = smem_u32(B + s * kBBytes);
 #pragma unroll
-                for (int ks = 0; ks < kChunkK / 16; ++ks)  // K = 16 per MMA: 32 bytes along the swizzled row
-                    umma_f16(tmem, umma_desc_sw128(a0 + 32 * ks), umma_desc_sw128(b0 + 32 * ks),
-                             (q > 0 || ks > 0) ? 1u : 0u);
+                for (int ks = 0; ks < kChunkK / 16; ++ks)  // K = 16 per MMA: 8 TMEM columns of A, 32 bytes of B's row
+                    umma_f16_ts(tmem, a0 + 8 * ks, umma_desc_sw128(b0 + 32 * ks), (q > 0 || ks > 0) ? 1u : 0u);
                 umma_commit(&st_free[s]);  // the stage is free once these MMAs have read it
                 if (q == nchunk - 1) umma_commit(acc_full);
             }
@@ -239,59 +246,70 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_q4k_kernel(const __grid_c
         }
     } else {
         // ---------------- dequant (then epilogue) ----------------
-        const int t = threadIdx.x - 64;          // 0..255
-        const int r = t & (kTileM - 1), h = t >> 7;  // row of the tile, half of the chunk
+        const int quarter = warp & 3;                    // TMEM lanes this warp may access
+        const int r = 32 * quarter + lane, h = (warp - 2) >> 2;  // row of the tile, half of each chunk
         const int dw = warp - 2;
-        float s_sc = 0.f, s_mn = 0.f;
-        for (int q = 0; q < nchunk; ++q) {
-            const int kb = q >> 2, p = q & 3, rs = kb % kRawSlots, s = q % kStages;
-            if (p == 0 && !mbar_wait(&raw_full[rs], (kb / kRawSlots) & 1, 3u, poisoned)) break;
-            if (q >= kStages && !mbar_wait(&st_free[s], ((q / kStages) - 1) & 1, 3u, poisoned)) break;
+        const uint32_t trow = tmem + (static_cast<uint32_t>(32 * quarter) << 16);
+        const uint32_t sel_a = 0x4440u + static_cast<uint32_t>(h);      // byte h, zero-extended
+        const uint32_t sel_b = 0x4440u + 2u + static_cast<uint32_t>(h);  // byte 2 + h
+        const __half2 k1024 = __float2half2_rn(1024.f);
+        int q = 0;
+        bool stop = false;
+        for (int kb = 0; kb < nblk && !stop; ++kb) {
+            const int rs = kb % kRawSlots;
+            if (!mbar_wait(&raw_full[rs], (kb / kRawSlots) & 1, 3u, poisoned)) break;
             const uint8_t* blk = raw + rs * kRawBytes + r * 144;
+            // scales of this thread's sub-blocks j = 2p + h (p = 0..3), get_scale_min_k4
+            // (src/inference/jsep/ops/matmul.ts:408-424) on the bytes of the three scale words
             const uint4 hdr = *reinterpret_cast<const uint4*>(blk);
-            q4k_sub_scale(hdr, 2 * p + h, s_sc, s_mn);
-            const __half2 sc2 = __float2half2_rn(s_sc), mn2 = __float2half2_rn(-s_mn);
-            const __half2 k1024 = __float2half2_rn(1024.f);
-            // the 32 bytes of pair p; this thread's quants are their low (h = 0) or
-            // high (h = 1) nibbles: elements 64p + 32h + l, l = 0..31
-            const uint4* qs = reinterpret_cast<const uint4*>(blk + 16 + 32 * p);
-            const uint4 v0 = qs[0], v1 = qs[1];
-            const uint32_t wv[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
-            uint32_t out[16];  // 32 f16, element order l = 0..31
+            const float d = f16_bits_to_f32(hdr.x), dmin = f16_bits_to_f32(hdr.x >> 16);
+            const uint32_t w1a = __byte_perm(hdr.y, 0u, sel_a), w1b = __byte_perm(hdr.y, 0u, sel_b);
+            const uint32_t w2a = __byte_perm(hdr.z, 0u, sel_a), w2b = __byte_perm(hdr.z, 0u, sel_b);
+            const uint32_t w3a = __byte_perm(hdr.w, 0u, sel_a), w3b = __byte_perm(hdr.w, 0u, sel_b);
+            const uint32_t scv[4] = {w1a & 63u, w1b & 63u, (w3a & 15u) | ((w1a >> 6) << 4), (w3b & 15u) | ((w1b >> 6) << 4)};
+            const uint32_t mv[4] = {w2a & 63u, w2b & 63u, (w3a >> 4) | ((w2a >> 6) << 4), (w3b >> 4) | ((w2b >> 6) << 4)};
+            const uint4* qs = reinterpret_cast<const uint4*>(blk + 16);
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                const uint32_t nib = h ? ((wv[i] >> 4) & 0x0F0F0F0Fu) : (wv[i] & 0x0F0F0F0Fu);
-                // f16 1024 + q (exact) for bytes (0, 1) and (2, 3): 0x64 in each high byte
-                const uint32_t e01 = __byte_perm(nib, 0x00006464u, 0x5140u);
-                const uint32_t e23 = __byte_perm(nib, 0x00006464u, 0x5342u);
-                __half2 q01 = __hsub2(*reinterpret_cast<const __half2*>(&e01), k1024);
-                __half2 q23 = __hsub2(*reinterpret_cast<const __half2*>(&e23), k1024);
-                const __half2 w01 = __hfma2(q01, sc2, mn2), w23 = __hfma2(q23, sc2, mn2);
-                out[2 * i] = *reinterpret_cast<const uint32_t*>(&w01);
-                out[2 * i + 1] = *reinterpret_cast<const uint32_t*>(&w23);
-            }
-            // row r, k = 32h + l of this chunk: 16-byte pieces j = 4h .. 4h+3,
-            // stored at position j ^ (r % 8) of the row (128-byte swizzle)
-            uint8_t* arow = A + s * kABytes + (r >> 3) * 1024 + (r & 7) * 128;
+            for (int p = 0; p < 4; ++p, ++q) {
+                const int s = q % kStages;
+                if (q >= kStages && !mbar_wait(&st_free[s], ((q / kStages) - 1) & 1, 3u, poisoned)) {
+                    stop = true;
+                    break;
+                }
+                const __half2 sc2 = __float2half2_rn(d * static_cast<float>(scv[p]));
+                const __half2 mn2 = __float2half2_rn(-dmin * static_cast<float>(mv[p]));
+                // the 32 bytes of pair p; this thread's quants are their low (h = 0) or
+                // high (h = 1) nibbles: elements 64p + 32h + l, l = 0..31
+                const uint4 v0 = qs[2 * p], v1 = qs[2 * p + 1];
+                const uint32_t wv[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+                uint32_t out[16];  // 32 f16, element order l = 0..31
 #pragma unroll
-            for (int jj = 0; jj < 4; ++jj) {
-                const int j = 4 * h + jj;
-                *reinterpret_cast<uint4*>(arow + ((j ^ (r & 7)) << 4)) =
-                    make_uint4(out[4 * jj], out[4 * jj + 1], out[4 * jj + 2], out[4 * jj + 3]);
-            }
-            // generic-proxy writes before the tensor core's (async proxy) reads
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            __syncwarp();
-            if (lane == 0) {
-                mbar_arrive(&a_full[s]);
-                if (p == 3) mbar_arrive(&raw_free[rs]);
+                for (int i = 0; i < 8; ++i) {
+                    const uint32_t nib = (wv[i] >> (4 * h)) & 0x0F0F0F0Fu;
+                    // f16 1024 + q (exact) for bytes (0, 1) and (2, 3): 0x64 in each high byte
+                    const uint32_t e01 = __byte_perm(nib, 0x00006464u, 0x5140u);
+                    const uint32_t e23 = __byte_perm(nib, 0x00006464u, 0x5342u);
+                    const __half2 q01 = __hsub2(*reinterpret_cast<const __half2*>(&e01), k1024);
+                    const __half2 q23 = __hsub2(*reinterpret_cast<const __half2*>(&e23), k1024);
+                    const __half2 w01 = __hfma2(q01, sc2, mn2), w23 = __hfma2(q23, sc2, mn2);
+                    out[2 * i] = *reinterpret_cast<const uint32_t*>(&w01);
+                    out[2 * i + 1] = *reinterpret_cast<const uint32_t*>(&w23);
+                }
+                // k = 32h + l of this chunk: TMEM columns 16h .. 16h+15 of A stage s
+                tmem_st16(trow + static_cast<uint32_t>(kTileN + s * kACols + 16 * h), out);
+                asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) {
+                    mbar_arrive(&a_full[s]);
+                    if (p == 3) mbar_arrive(&raw_free[rs]);
+                }
             }
         }
         // ---------------- epilogue ----------------
         const bool ok = mbar_wait(acc_full, 0, 4u, poisoned);
         tc_fence_after();
         if (ok) {
-            const int quarter = warp & 3;              // TMEM lanes 32*quarter .. +31 = rows
             const int col0 = (dw < 4) ? 0 : kTileN / 2;
             const int row = m0 + 32 * quarter + lane;
 #pragma unroll 1
@@ -313,7 +331,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_q4k_kernel(const __grid_c
     __syncthreads();
     if (warp == 1) {
         tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTileN));
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
     }
 }
 
@@ -347,7 +365,7 @@ EncodeFn encoder() {
     return fn;
 }
 
-constexpr size_t kSmemBytes = 1024 /* alignment */ + kStages * (kABytes + kBBytes) + kRawSlots * kRawBytes +
+constexpr size_t kSmemBytes = 1024 /* alignment */ + kStages * kBBytes + kRawSlots * kRawBytes +
                               8 * (3 * kStages + 2 * kRawSlots + 1) + 16;
 
 }  // namespace
