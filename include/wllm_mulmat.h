@@ -177,6 +177,21 @@ int32_t wllm_graph_end(int32_t* out_graph);
 int32_t wllm_graph_launch(int32_t graph);
 int32_t wllm_graph_destroy(int32_t graph);
 
+/* Prefill MUL_MAT that allocates nothing: the same arguments and result as
+ * wllm_mul_mat for the prefill path (Q4_K weights, N >= 65 vectors,
+ * 16-byte aligned rows and activations), with the f16 activation workspace
+ * in a fixed 16 MiB device array of the library instead of library-allocated
+ * memory: N * K * 2 + 256 bytes must fit, otherwise WLLM_STATUS_FAILED with
+ * the sizes in wllm_last_error(). No cudaMalloc or cudaFree happens. The
+ * first call on a device looks up the array's address, so it must come
+ * before any stream capture. Calls that overlap in time (other streams or
+ * host threads) race on the one workspace. No counterpart in the reference
+ * (its WGSL dispatch allocates its own buffers). */
+int32_t wllm_mul_mat_prefill_static(int32_t src0_type, const void* w, int64_t w_row_bytes,
+                                    const float* x, int64_t x_stride,
+                                    float* y, int64_t y_stride,
+                                    int32_t M, int32_t K, int32_t N, void* stream);
+
 /* Device dequantization of n elements (n a multiple of the block size) of
  * raw GGUF blocks to f32. Replaces the libllama oracle shim
  * webllm_dequantize_q4_K (webgpu-bridge.cpp:692-708) on the device, for

@@ -436,6 +436,38 @@ int launch_prefill(const MulMatOp& o, void* workspace, size_t workspace_bytes, c
     return e == cudaSuccess ? 2 : -static_cast<int>(e);
 }
 
+// Fixed device workspace for wllm_mul_mat_prefill_static: the f16 copy of the
+// activations (N x K x 2 bytes) lives in this file-scope array instead of
+// runtime-allocated memory. Nothing in it needs to start at zero: the
+// activation pre-pass writes every byte the GEMM reads. Calls that use it at
+// the same time (several streams or host threads) race on it.
+static __device__ __align__(256) unsigned char g_prefill_static_ws[kPrefillStaticWorkspaceBytes];
+
+void* prefill_static_workspace(const char** err) {
+    // the array's device address, looked up once per device (the lookup must
+    // not happen while a stream is being captured)
+    static void* addr[64] = {};
+    static bool looked_up[64] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+        cudaGetLastError();
+        *err = "cannot query the current device";
+        return nullptr;
+    }
+    if (!looked_up[dev]) {
+        void* p = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_prefill_static_ws);
+        if (e != cudaSuccess || !p) {
+            cudaGetLastError();
+            *err = "cudaGetSymbolAddress of the static workspace failed";
+            return nullptr;
+        }
+        addr[dev] = p;
+        looked_up[dev] = true;
+    }
+    return addr[dev];
+}
+
 unsigned read_and_clear_prefill_error() {
     unsigned v = 0;
     if (cudaMemcpyFromSymbol(&v, g_prefill_error, sizeof(v)) != cudaSuccess) return 0xFFFFFFFFu;

@@ -708,6 +708,50 @@ int32_t wllm_mul_mat(int32_t src0_type, const void* w, int64_t w_row_bytes, cons
     return launch(s, &m, 1, stream ? static_cast<cudaStream_t>(stream) : s.stream);
 }
 
+int32_t wllm_mul_mat_prefill_static(int32_t src0_type, const void* w, int64_t w_row_bytes, const float* x,
+                                    int64_t x_stride, float* y, int64_t y_stride, int32_t M, int32_t K, int32_t N,
+                                    void* stream) {
+    State& s = S();
+    std::lock_guard<std::mutex> g(s.mu);
+    if (!ensure_init(s)) return WLLM_STATUS_FAILED;
+    if (!w || !x || !y) return fail(s, "wllm_mul_mat_prefill_static: null pointer");
+    MulMatOp m{};
+    m.w = static_cast<const uint8_t*>(w);
+    m.x = x;
+    m.y = y;
+    m.w_nb1 = w_row_bytes;
+    m.w_nb2 = m.w_nb3 = w_row_bytes * M;
+    m.x_nb1 = 4 * x_stride;
+    m.x_nb2 = m.x_nb3 = 4 * x_stride * N;
+    m.y_nb1 = 4 * y_stride;
+    m.y_nb2 = m.y_nb3 = 4 * y_stride * N;
+    m.type = src0_type;
+    m.M = M;
+    m.K = K;
+    m.N = N;
+    m.ne2 = m.ne3 = 1;
+    m.r2 = m.r3 = 1;
+    if (const char* why = wllm::check_mulmat_op(m)) return fail(s, "wllm_mul_mat_prefill_static: %s", why);
+    if (!wllm::prefill_supported(m))
+        return fail(s,
+                    "wllm_mul_mat_prefill_static: only the prefill path (Q4_K, N >= %d, 16-byte aligned rows and "
+                    "activations) is available here",
+                    wllm::kPrefillMinN);
+    const size_t need = wllm::prefill_workspace_bytes(m);
+    if (need > wllm::kPrefillStaticWorkspaceBytes)
+        return fail(s, "wllm_mul_mat_prefill_static: N*K = %lld needs %llu workspace bytes, above the fixed %llu",
+                    static_cast<long long>(N) * K, static_cast<unsigned long long>(need),
+                    static_cast<unsigned long long>(wllm::kPrefillStaticWorkspaceBytes));
+    const char* err = nullptr;
+    void* ws = wllm::prefill_static_workspace(&err);
+    if (!ws) return fail(s, "wllm_mul_mat_prefill_static: %s", err ? err : "no workspace");
+    const int rc = wllm::launch_prefill(m, ws, wllm::kPrefillStaticWorkspaceBytes,
+                                        stream ? static_cast<cudaStream_t>(stream) : s.stream);
+    if (rc < 0) return cuda_fail(s, static_cast<cudaError_t>(-rc), "wllm_mul_mat_prefill_static launch");
+    s.counters.kernels_launched += static_cast<uint64_t>(rc);
+    return WLLM_STATUS_OK;
+}
+
 int32_t wllm_dequantize(int32_t type, const void* src, float* dst, int64_t n, void* stream) {
     State& s = S();
     std::lock_guard<std::mutex> g(s.mu);

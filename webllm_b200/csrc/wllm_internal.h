@@ -78,6 +78,13 @@ size_t prefill_workspace_bytes(const MulMatOp& op);
 int launch_prefill(const MulMatOp& op, void* workspace, size_t workspace_bytes, cudaStream_t stream);
 unsigned read_and_clear_prefill_error();
 
+// Size of the prefill path's fixed device workspace (wllm_mul_mat_prefill_static):
+// ops with N * K * 2 + 256 bytes of f16 activations up to this size.
+constexpr size_t kPrefillStaticWorkspaceBytes = 16u << 20;
+// Its device address (looked up on first use on the current device); null and
+// *err set on failure.
+void* prefill_static_workspace(const char** err);
+
 // Workspace the launch of `ops` needs (0 if none).
 size_t mulmat_workspace_bytes(const MulMatOp* ops, int n_ops);
 

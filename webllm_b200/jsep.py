@@ -56,7 +56,7 @@ EXPORTED_SYMBOLS = (
     "wllm_clear", "wllm_run_op", "wllm_run_ops", "wllm_sync", "wllm_last_error", "wllm_get_counters",
     "wllm_buffer_device_ptr", "wllm_mul_mat", "wllm_mul_mat_batch", "wllm_get_stream",
     "wllm_graph_begin", "wllm_graph_end", "wllm_graph_launch", "wllm_graph_destroy",
-    "wllm_dequantize", "wllm_version",
+    "wllm_dequantize", "wllm_version", "wllm_mul_mat_prefill_static",
 )
 
 
@@ -106,6 +106,7 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
         "wllm_get_counters": ([P(WllmCounters)], i32),
         "wllm_buffer_device_ptr": ([i32, P(vp), P(u64)], i32),
         "wllm_mul_mat": ([i32, vp, i64, vp, i64, vp, i64, i32, i32, i32, vp], i32),
+        "wllm_mul_mat_prefill_static": ([i32, vp, i64, vp, i64, vp, i64, i32, i32, i32, vp], i32),
         "wllm_dequantize": ([i32, vp, vp, i64, vp], i32),
         "wllm_mul_mat_batch": ([P(MulMatArgs), i32, vp], i32),
         "wllm_get_stream": ([P(vp)], i32),
@@ -380,6 +381,17 @@ def mul_mat_device(src0_type: int, w_ptr: int, w_row_bytes: int, x_ptr: int, x_s
     rc = L.wllm_mul_mat(int(src0_type), int(w_ptr), int(w_row_bytes), int(x_ptr), int(x_stride),
                         int(y_ptr), int(y_stride), int(M), int(K), int(N), int(stream) or None)
     return _check(rc, "wllm_mul_mat")
+
+
+def mul_mat_prefill_static(src0_type: int, w_ptr: int, w_row_bytes: int, x_ptr: int, x_stride: int,
+                           y_ptr: int, y_stride: int, M: int, K: int, N: int, stream: int = 0) -> int:
+    """Prefill MUL_MAT with the library's fixed device workspace
+    (wllm_mul_mat_prefill_static): allocates nothing; N * K * 2 + 256 bytes
+    must fit in 16 MiB; overlapping calls race on the one workspace."""
+    L = load_library()
+    rc = L.wllm_mul_mat_prefill_static(int(src0_type), int(w_ptr), int(w_row_bytes), int(x_ptr), int(x_stride),
+                                       int(y_ptr), int(y_stride), int(M), int(K), int(N), int(stream) or None)
+    return _check(rc, "wllm_mul_mat_prefill_static")
 
 
 def mul_mat_batch(ops: Sequence[MulMatArgs], stream: int = 0) -> int:
