@@ -60,7 +60,7 @@ constexpr int kCW = 8;                        // consumer warps
 constexpr int kThreads = 32 * (kCW + 1);      // + copy warp
 constexpr int kRows = 16;                     // rows per unit (one MMA m-tile)
 constexpr int kQ4kSegBlocks = 14;             // <= 2016 B per row and stage (a TMA box row is <= 2048 B)
-constexpr int kQ6kSegBlocks = 6;              // <= 1260 B (+ 16-byte window slack)
+constexpr int kQ6kSegBlocks = 9;              // <= 1890 B (+ 16-byte window slack: a 1936 B box row)
 constexpr int kQ80SegBlocks = 32;             // 1088 B, whole 8-block groups
 constexpr int kMaxStages = 8;
 constexpr int kRedDelay = 2;                  // a unit's partials are summed this many units later
@@ -241,36 +241,28 @@ __device__ __forceinline__ int block_bytes_of(int type) {
 }
 
 // Byte layout of the shared-memory activation image.
-//  Q4_K: int8 limb columns [2N][K + kXPad] (column 2t + l = limb l of vector
-//        t), then f32 d-factors [N][K/256] (max|x| / (127 * 16) per block),
-//        then exact f32 sub-block sums [N][K/32].
-//  Q6_K / Q8_0: f32 x permuted per lane chunk, [N][K/256][8 f][8 c] float4.
+//  Q4_K and Q6_K (one shared image): int8 limb columns [2N][K + kXPad]
+//        (column 2t + l = limb l of vector t), then f32 d-factors [N][K/256]
+//        (max|x| / (127 * 16) per block), then exact f32 sums of x over
+//        32-element sub-blocks [N][K/32] (Q4_K) and over 16-element
+//        sub-blocks [N][K/16] (Q6_K).
+//  Q8_0: f32 x permuted per lane chunk, [N][K/256][8 f][8 c] float4.
+__host__ __device__ __forceinline__ bool limb_image(int type) { return type == kTypeQ4_K || type == kTypeQ6_K; }
 __host__ __device__ __forceinline__ int img_col_bytes(int K) { return K + kXPad; }
 __host__ __device__ __forceinline__ int img_inv_off(int K, int N) { return 2 * N * img_col_bytes(K); }
 // (16-byte aligned: the sums are read as float2)
 __host__ __device__ __forceinline__ int img_sum_off(int K, int N) {
     return (img_inv_off(K, N) + 4 * N * (K / 256) + 15) & ~15;
 }
+__host__ __device__ __forceinline__ int img_sum16_off(int K, int N) { return img_sum_off(K, N) + 4 * N * (K / 32); }
 __host__ __device__ __forceinline__ int img_bytes(int type, int K, int N) {
-    if (type == kTypeQ4_K) return img_sum_off(K, N) + 4 * N * (K / 32);
+    if (limb_image(type)) return img_sum16_off(K, N) + 4 * N * (K / 16);
     return 4 * K * N;
 }
 
-// 1 + q/128 for the byte 0x80|q in byte position k of w.
-template <int k>
-__device__ __forceinline__ float unit_q(uint32_t w) {
-    return __uint_as_float(__byte_perm(w, 0x3F000000u, 0x7044u | (k << 8)));
-}
-
 // Element offset (within its 256-element group) of float4 f of lane chunk c
-// (CUDA-core formats); the image is xs4[group][f][c].
-__device__ __forceinline__ int chunk_elem(int type, int c, int f) {
-    if (type == kTypeQ6_K) {
-        const int h = c >> 2, l0 = 8 * (c & 3), t = f >> 1;
-        return 128 * h + 32 * t + l0 + 4 * (f & 1);
-    }
-    return 32 * c + 4 * f;  // Q8_0: lane chunk c is block c of the group
-}
+// (Q8_0: lane chunk c is block c of the group); the image is xs4[group][f][c].
+__device__ __forceinline__ int chunk_elem(int c, int f) { return 32 * c + 4 * f; }
 
 // 4 bytes at any 2-byte-aligned shared address.
 __device__ __forceinline__ uint32_t lds_u32_any(const uint8_t* p) {
@@ -366,53 +358,84 @@ __device__ __forceinline__ uint32_t pack_b4(int a, int b, int c, int d) {
                        __byte_perm(static_cast<uint32_t>(c), static_cast<uint32_t>(d), 0x0040u), 0x5410u);
 }
 
-template <int NT>
-__device__ __forceinline__ void item_q6_k(const uint8_t* blk, int c, const float4 (&xr)[NT][8], const float (&xq)[NT][4],
-                                          float (&acc)[NT]) {
-    const int h = c >> 2, l0 = 8 * (c & 3);
-    const uint8_t* ql = blk + 64 * h + l0;
-    const uint8_t* qh = blk + 128 + 32 * h + l0;
-    const int8_t* sc = reinterpret_cast<const int8_t*>(blk + 192 + 8 * h + (l0 >> 4));
-    const float d = f16_bits_to_f32(lds_u16(blk + 208));
-    float a[4];
+// A operands of the four 32-element groups of one Q6_K half-block at one
+// fragment position: ql0 / ql1 hold four bytes of the half's low-quant
+// chunks 0 / 1 (ql[64h + l], ql[64h + 32 + l]), qh the four matching high-bit
+// bytes (qh[32h + l]). Group t holds the 6-bit quants (0..63) of elements
+// 128h + 32t + l: low nibble of chunk t&1 for t < 2, high nibble for t >= 2,
+// and bits 2t, 2t+1 of qh as bits 4, 5 (src/inference/jsep/ops/matmul.ts
+// leaves Q6_K to ggml; the layout is ggml's dequantize_row_q6_K). Each group
+// is one LOP3 (a & 0x0F) | (b & 0xF0) whose b carries nothing but the two
+// wanted bits in the high half of every byte.
+__device__ __forceinline__ void q6k_groups(uint32_t ql0, uint32_t ql1, uint32_t qh, uint32_t (&a)[4]) {
+    const uint32_t m = 0x0F0F0F0Fu;
+    const uint32_t qa = qh & 0x33333333u, qb = qh & 0xCCCCCCCCu;  // groups 0, 2 / 1, 3
+    a[0] = (ql0 & m) | ((qa << 4) & ~m);
+    a[1] = (ql1 & m) | ((qb << 2) & ~m);
+    a[2] = ((ql0 >> 4) & m) | (qa & ~m);
+    a[3] = ((ql1 >> 4) & m) | ((qb >> 2) & ~m);
+}
+
+// One Q6_K item: 16 rows x one 256-element block on integer tensor cores,
+// for NP = N rounded up to a power of two. Blocks are 210 bytes, so a block
+// sits at any even offset in shared memory: the A fragments come from aligned
+// 32-bit loads and a funnel shift (ldmatrix needs 16-byte rows). MMA i covers
+// elements 32i .. 32i+31, i.e. the 16-element sub-blocks 2i (k 0..15) and
+// 2i+1 (k 16..31). As for Q4_K, the 8 B columns are NS = 4/NP sub-block slots
+// x NP vectors x 2 limbs; sub-block j uses slot j % NS of chain j / NS, its
+// B rows are real only in its slot's columns, so NS sub-blocks share one
+// fragment without mixing. Lane (g, c) scales the chains' slot c / NP: the
+// sub-blocks j = q NS + sl of rows g and g + 8, with their int8 scales in
+// integer. The -32 offset of every quant is applied through the exact
+// 16-element sums of x: sum sc (q - 32) x = sum sc q x - 32 sum sc X.
+template <int NP>
+__device__ __forceinline__ void q6k_item(const uint8_t* pg, const uint8_t* ph, uint32_t xaddr, uint32_t xzero,
+                                         bool xv, float xf, const float* xs, int c, int sl, float& yg, float& yh) {
+    constexpr int NS = 4 / NP, NCH = 16 / NS, NCHH = NCH / 2;  // chains per half-block
+    // |D| <= 16 * 63 * 127 per sub-block; times |sc| <= 128, summed over the
+    // lane's 4 or 8 sub-blocks: well inside int32
+    int a0 = 0, a1 = 0, a2 = 0, a3 = 0;
+    float sg = 0.f, sh = 0.f;
 #pragma unroll
-    for (int t = 0; t < 4; ++t) a[t] = 128.f * d * static_cast<float>(sc[2 * t]);
-    float2 s[4][NT];
+    for (int h = 0; h < 2; ++h) {
+        int D[NCHH][4];
 #pragma unroll
-    for (int t = 0; t < 4; ++t)
+        for (int q = 0; q < NCHH; ++q) D[q][0] = D[q][1] = D[q][2] = D[q][3] = 0;
+        // fragment positions: 0 = row g k 4c.., 1 = row g+8 k 4c.., 2 = row g
+        // k 16+4c.., 3 = row g+8 k 16+4c..
+        uint32_t A[4][4];  // [position][group]
 #pragma unroll
-        for (int n = 0; n < NT; ++n) s[t][n] = make_float2(0.f, 0.f);
+        for (int r = 0; r < 4; ++r) {
+            const uint8_t* b = ((r & 1) ? ph : pg) + 4 * c + 16 * (r >> 1);
+            q6k_groups(lds_u32_any(b + 64 * h), lds_u32_any(b + 64 * h + 32), lds_u32_any(b + 128 + 32 * h), A[r]);
+        }
 #pragma unroll
-    for (int half = 0; half < 2; ++half) {
-        const uint32_t qa = lds_u32_any(ql + 4 * half), qb = lds_u32_any(ql + 32 + 4 * half);
-        const uint32_t hh = lds_u32_any(qh + 4 * half);
-        uint32_t t4[4];
-        t4[0] = (qa & 0x0F0F0F0Fu) | ((hh << 4) & 0x30303030u) | 0x80808080u;
-        t4[1] = (qb & 0x0F0F0F0Fu) | ((hh << 2) & 0x30303030u) | 0x80808080u;
-        t4[2] = ((qa >> 4) & 0x0F0F0F0Fu) | (hh & 0x30303030u) | 0x80808080u;
-        t4[3] = ((qb >> 4) & 0x0F0F0F0Fu) | ((hh >> 2) & 0x30303030u) | 0x80808080u;
+        for (int pp = 0; pp < 2; ++pp) {
+            const int p = 2 * h + pp;  // MMAs 2p, 2p+1 = groups 2pp, 2pp+1 of half h
+            uint32_t x[4];
+            ldmatrix_x4_at(x, xv ? xaddr + 64 * p : xzero);
+            imma_u8s8_acc(D[(4 * pp) / NS], A[0][2 * pp], A[1][2 * pp], A[2][2 * pp], A[3][2 * pp], x[0], x[1]);
+            imma_u8s8_acc(D[(4 * pp + 2) / NS], A[0][2 * pp + 1], A[1][2 * pp + 1], A[2][2 * pp + 1],
+                          A[3][2 * pp + 1], x[2], x[3]);
+        }
+        // chain q of this half holds sub-blocks (h NCHH + q) NS + slot
 #pragma unroll
-        for (int t = 0; t < 4; ++t) {
-            const float2 u01 = make_float2(unit_q<0>(t4[t]), unit_q<1>(t4[t]));
-            const float2 u23 = make_float2(unit_q<2>(t4[t]), unit_q<3>(t4[t]));
-#pragma unroll
-            for (int n = 0; n < NT; ++n) {
-                const float4 xv = xr[n][2 * t + half];
-                s[t][n] = __ffma2_rn(u01, make_float2(xv.x, xv.y), s[t][n]);
-                s[t][n] = __ffma2_rn(u23, make_float2(xv.z, xv.w), s[t][n]);
-            }
+        for (int q = 0; q < NCHH; ++q) {
+            const int j = (h * NCHH + q) * NS + sl;
+            const int scg = static_cast<int>(*reinterpret_cast<const int8_t*>(pg + 192 + j));
+            const int sch = static_cast<int>(*reinterpret_cast<const int8_t*>(ph + 192 + j));
+            a0 += scg * D[q][0];
+            a1 += scg * D[q][1];
+            a2 += sch * D[q][2];
+            a3 += sch * D[q][3];
+            const float X = xs[j];
+            sg = fmaf(static_cast<float>(scg), X, sg);
+            sh = fmaf(static_cast<float>(sch), X, sh);
         }
     }
-#pragma unroll
-    for (int n = 0; n < NT; ++n) {
-        float r = 0.f;
-#pragma unroll
-        for (int t = 0; t < 4; ++t) {
-            // sum d sc (q6 - 32) x = a (S - X) - 32/128 a X = a (S - (5/4) X)
-            r += a[t] * ((s[t][n].x + s[t][n].y) - 1.25f * xq[n][t]);
-        }
-        acc[n] += r;
-    }
+    const float dg = f16_bits_to_f32(lds_u16(pg + 208)), dh = f16_bits_to_f32(lds_u16(ph + 208));
+    yg = fmaf(dg, fmaf(fmaf(static_cast<float>(a1), 0.0078125f, static_cast<float>(a0)), xf, -32.f * sg), yg);
+    yh = fmaf(dh, fmaf(fmaf(static_cast<float>(a3), 0.0078125f, static_cast<float>(a2)), xf, -32.f * sh), yh);
 }
 
 template <int NT>
@@ -471,11 +494,11 @@ struct OpTable {
 __device__ __forceinline__ void stage_activations(const OpInfo& op, uint8_t* xsm, int ct, int lane, int cw) {
     const int K = op.K, N = op.N, per4 = K / 4;
     const uint8_t* xb = reinterpret_cast<const uint8_t*>(op.x);
-    if (op.type == kTypeQ4_K) {
-        // one warp per (vector, 256-block); lane covers elements 8 lane .. 8 lane + 7
+    if (limb_image(op.type)) {
         const int nblk = K / 256, XS = img_col_bytes(K);
         float* dfac = reinterpret_cast<float*>(xsm + img_inv_off(K, N));
         float* Xs = reinterpret_cast<float*>(xsm + img_sum_off(K, N));
+        float* X16 = reinterpret_cast<float*>(xsm + img_sum16_off(K, N));
         // one (vector, block) per half-warp: lane h = lane%16 covers elements
         // 16h .. 16h+15; all of a round's loads are issued before any arithmetic
         const int hw = lane >> 4, h = lane & 15;
@@ -506,14 +529,15 @@ __device__ __forceinline__ void stage_activations(const OpInfo& op, uint8_t* xsm
                                 __float2int_rn(fmaf(e.z, sc, -static_cast<float>(q2)) * 128.f),
                                 __float2int_rn(fmaf(e.w, sc, -static_cast<float>(q3)) * 128.f));
             }
-            float a = 0.f;
+            float a16 = 0.f;  // a lane's 16 elements: one Q6_K sub-block
 #pragma unroll
-            for (int k = 0; k < 4; ++k) a += (v[k].x + v[k].y) + (v[k].z + v[k].w);
-            a += __shfl_xor_sync(0xffffffffu, a, 1);  // a sub-block is two lanes
+            for (int k = 0; k < 4; ++k) a16 += (v[k].x + v[k].y) + (v[k].z + v[k].w);
+            const float a = a16 + __shfl_xor_sync(0xffffffffu, a16, 1);  // a Q4_K sub-block is two lanes
             if (act) {
                 uint8_t* c0 = xsm + (2 * t) * XS + b * 256 + 16 * h;
                 *reinterpret_cast<uint4*>(c0) = make_uint4(p0[0], p0[1], p0[2], p0[3]);
                 *reinterpret_cast<uint4*>(c0 + XS) = make_uint4(p1[0], p1[1], p1[2], p1[3]);
+                X16[t * (K / 16) + b * 16 + h] = a16;
                 if ((h & 1) == 0) Xs[t * (K / 32) + b * 8 + (h >> 1)] = a;
                 if (h == 0) dfac[t * nblk + b] = mx * (1.f / 2032.f);  // 1 / (16 s)
             }
@@ -531,7 +555,7 @@ __device__ __forceinline__ void stage_activations(const OpInfo& op, uint8_t* xsm
                     const int idx = (i0 + i) * kCW * 32 + ct;
                     if (idx < per4) {
                         const int g = idx >> 6, f = (idx >> 3) & 7, c = idx & 7;
-                        v[i] = __ldg(reinterpret_cast<const float4*>(xf + g * 256 + chunk_elem(op.type, c, f)));
+                        v[i] = __ldg(reinterpret_cast<const float4*>(xf + g * 256 + chunk_elem(c, f)));
                     }
                 }
 #pragma unroll
@@ -604,6 +628,35 @@ __device__ __forceinline__ Q4Lane q4k_lane(const OpInfo& op, const uint8_t* xsm,
     return q;
 }
 
+// Per-op constants of a consumer lane on the Q6_K path (see q6k_item).
+struct Q6Lane {
+    uint32_t xcol;      // activations ldmatrix row address (block 0, pair 0)
+    bool xv;            // that row is real (not the zero row)
+    const float* dfac;  // d-factors of vector tk
+    const float* X16;   // 16-element sub-block sums of vector tk
+    int sl, tk;         // slot and vector of the lane's accumulator columns
+};
+
+template <int NP>
+__device__ __forceinline__ Q6Lane q6k_lane(const OpInfo& op, const uint8_t* xsm, int lane) {
+    constexpr int NS = 4 / NP;
+    const int K = op.K, N = op.N, XS = img_col_bytes(K);
+    const int c = lane & 3;
+    Q6Lane q;
+    q.sl = c / NP;
+    q.tk = c % NP;
+    // matrix mi = lane/8 of a pair's ldmatrix is sub-block 4p + mi (k half
+    // mi&1 of MMA 2p + mi/2), slot mi % NS; row rr = lane%8 = B column
+    const int mi = lane >> 3, rr = lane & 7;
+    const int slot_r = rr / (2 * NP), t_r = (rr >> 1) % NP, l_r = rr & 1;
+    q.xv = t_r < N && slot_r == mi % NS;
+    q.xcol = smem_u32(xsm) + static_cast<uint32_t>((2 * t_r + l_r) * XS + 16 * mi);
+    const int tkc = q.tk < N ? q.tk : 0;
+    q.dfac = reinterpret_cast<const float*>(xsm + img_inv_off(K, N)) + tkc * (K / 256);
+    q.X16 = reinterpret_cast<const float*>(xsm + img_sum16_off(K, N)) + tkc * (K / 16);
+    return q;
+}
+
 // Warp-wide bounded wait on an mbarrier phase (see ring_wait).
 __device__ __forceinline__ void ring_barrier_wait(uint64_t* bar, uint32_t parity, volatile int* poisoned, int lane) {
     if (mbar_test_wait(bar, parity)) return;
@@ -653,6 +706,52 @@ __device__ __forceinline__ void q4k_unit(const OpInfo& op, const Q4Lane& q, Ring
         R.advance();
     }
     // sum the slots of each vector (lanes c with the same c % NP)
+#pragma unroll
+    for (int o = NP; o < 4; o <<= 1) {
+        yg += __shfl_xor_sync(0xffffffffu, yg, o);
+        yh += __shfl_xor_sync(0xffffffffu, yh, o);
+    }
+    if (sl == 0 && tk < N) {
+        ub[g * NT + tk] = yg;
+        ub[(g + 8) * NT + tk] = yh;
+    }
+}
+
+// All segments of one Q6_K unit for this consumer warp (see q4k_unit). Each
+// row's copy window starts at its segment start rounded down to 16 bytes;
+// glo is the low word of the unit's first row address.
+template <int NP, int NT>
+__device__ __forceinline__ void q6k_unit(const OpInfo& op, const Q6Lane& q, Ring& R, uint32_t xzero, uint32_t glo,
+                                         int lane, int cw, float* ub) {
+    const int N = op.N, nblocks = op.K / 256;
+    const int g = lane >> 2, c = lane & 3, sl = q.sl, tk = q.tk;
+    const uint32_t nb1 = static_cast<uint32_t>(op.w_nb1);
+    const uint32_t xcol = q.xcol;
+    const bool xv = q.xv;
+    const float* dfac = q.dfac;
+    const float* X16 = q.X16;
+    float yg = 0.f, yh = 0.f;
+    for (int sg = 0; sg < op.nseg; ++sg) {
+        const int b0 = sg * op.seg_blocks;
+        const int nb = min(op.seg_blocks, nblocks - b0);
+        const int i0 = (cw - static_cast<int>(R.item_base % kCW) + kCW) % kCW;
+        if (i0 < nb) {
+            ring_wait(R, lane);
+            const uint8_t* stage = R.stages + R.slot * R.SB;
+            const uint32_t gl = glo + static_cast<uint32_t>(b0 * 210);
+            const uint8_t* pg = stage + g * op.wbox + ((gl + static_cast<uint32_t>(g) * nb1) & 15u);
+            const uint8_t* ph = stage + (g + 8) * op.wbox + ((gl + static_cast<uint32_t>(g + 8) * nb1) & 15u);
+            for (int i = i0; i < nb; i += kCW) {
+                const int bg = b0 + i;
+                q6k_item<NP>(pg + i * 210, ph + i * 210, xcol + bg * 256, xzero, xv, 16.f * dfac[bg], X16 + bg * 16,
+                             c, sl, yg, yh);
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cnt(&R.empty[R.slot], i0 == 0 ? 1u + kCW - min(nb, kCW) : 1u);
+        }
+        R.item_base += nb;
+        R.advance();
+    }
 #pragma unroll
     for (int o = NP; o < 4; o <<= 1) {
         yg += __shfl_xor_sync(0xffffffffu, yg, o);
@@ -819,6 +918,7 @@ __global__ void __launch_bounds__(kThreads, 1) stream_gemv_kernel(const __grid_c
     const int n_ops = T.n_ops, total = T.total_units;
     int staged = -1, oi = -1, useq = 0;
     Q4Lane q4{};
+    Q6Lane q6{};
     // Sums the 8 warps' partials of this CTA's unit number j (fixed order:
     // deterministic) and writes its rows; done by the unit's owner warp
     // kRedDelay units later, when the other warps are normally long done.
@@ -843,13 +943,13 @@ __global__ void __launch_bounds__(kThreads, 1) stream_gemv_kernel(const __grid_c
             } while (oi + 1 < n_ops && u >= T.op[oi + 1].unit_begin);
             const OpInfo& op = T.op[oi];
             if (staged < 0 || T.op[staged].x != op.x || T.op[staged].K != op.K || T.op[staged].N != op.N ||
-                T.op[staged].x_nb1 != op.x_nb1 || (T.op[staged].type == kTypeQ4_K) != (op.type == kTypeQ4_K) ||
-                (op.type != kTypeQ4_K && T.op[staged].type != op.type)) {
+                T.op[staged].x_nb1 != op.x_nb1 || limb_image(T.op[staged].type) != limb_image(op.type)) {
                 consumers_sync();  // nobody still reads the previous image
                 stage_activations(op, xsm, ct, lane, cw);
                 staged = oi;
             }
             if (op.type == kTypeQ4_K) q4 = (NT == 1 || op.N == 1) ? q4k_lane<1>(op, xsm, lane) : q4k_lane<2>(op, xsm, lane);
+            if (op.type == kTypeQ6_K) q6 = (NT == 1 || op.N == 1) ? q6k_lane<1>(op, xsm, lane) : q6k_lane<2>(op, xsm, lane);
         }
         const OpInfo& op = T.op[oi];
         const int N = op.N, K = op.K;
@@ -866,14 +966,21 @@ __global__ void __launch_bounds__(kThreads, 1) stream_gemv_kernel(const __grid_c
                 q4k_unit<1, NT>(op, q4, R, smem_u32(zrow), lane, cw, ub);
             else
                 q4k_unit<2, NT>(op, q4, R, smem_u32(zrow), lane, cw, ub);
+        } else if (op.type == kTypeQ6_K) {
+            // ================= Q6_K, integer tensor cores =================
+            const uint32_t glo =
+                static_cast<uint32_t>(reinterpret_cast<uintptr_t>(op.w + static_cast<int64_t>(r0) * op.w_nb1));
+            if (NT == 1 || N == 1)
+                q6k_unit<1, NT>(op, q6, R, smem_u32(zrow), glo, lane, cw, ub);
+            else
+                q6k_unit<2, NT>(op, q6, R, smem_u32(zrow), glo, lane, cw, ub);
         } else {
-            // ================= Q6_K / Q8_0, CUDA cores =================
+            // ================= Q8_0, CUDA cores =================
             const int j = lane >> 3, c = lane & 7;
             const int K256 = K / 256;
             const float4* xs4 = reinterpret_cast<const float4*>(xsm);
             const uint32_t wlo = static_cast<uint32_t>(reinterpret_cast<uintptr_t>(op.w + static_cast<int64_t>(r0) * op.w_nb1));
             const uint32_t nb1lo = static_cast<uint32_t>(op.w_nb1);
-            const bool q8 = op.type == kTypeQ8_0;
             float acc[4][NT];
 #pragma unroll
             for (int q = 0; q < 4; ++q)
@@ -882,8 +989,7 @@ __global__ void __launch_bounds__(kThreads, 1) stream_gemv_kernel(const __grid_c
             for (int sg = 0; sg < op.nseg; ++sg) {
                 const int b0 = sg * op.seg_blocks;
                 const int nb = min(op.seg_blocks, nblocks - b0);
-                const int gpb = q8 ? 8 : 1;
-                const int ngroups = (nb + gpb - 1) / gpb;
+                const int ngroups = (nb + 7) / 8;  // 256-element groups of 8 blocks
                 const int g0 = (cw - static_cast<int>(R.item_base % kCW) + kCW) % kCW;
                 if (g0 >= ngroups) {  // no item here: the warp with item 0 releases the stage
                     R.item_base += ngroups;
@@ -901,7 +1007,7 @@ __global__ void __launch_bounds__(kThreads, 1) stream_gemv_kernel(const __grid_c
                     base[q] = stage + r * op.wbox + ((glo + static_cast<uint32_t>(r) * nb1lo) & 15u);
                 }
                 for (int gi = g0; gi < ngroups; gi += kCW) {
-                    const int gg = b0 / gpb + gi;  // 256-element group index
+                    const int gg = b0 / 8 + gi;  // 256-element group index
                     float4 xr[NT][8];
 #pragma unroll
                     for (int n = 0; n < NT; ++n) {
@@ -909,23 +1015,10 @@ __global__ void __launch_bounds__(kThreads, 1) stream_gemv_kernel(const __grid_c
 #pragma unroll
                         for (int f = 0; f < 8; ++f) xr[n][f] = xs4[(nn * K256 + gg) * 64 + f * 8 + c];
                     }
-                    if (q8) {
-                        const int blk = gg * 8 + c;
-                        if (blk < b0 + nb) {
+                    const int blk = gg * 8 + c;
+                    if (blk < b0 + nb) {
 #pragma unroll
-                            for (int q = 0; q < 4; ++q) item_q8_0<NT>(base[q] + (blk - b0) * 34, xr, acc[q]);
-                        }
-                    } else {
-                        float xq[NT][4];
-#pragma unroll
-                        for (int n = 0; n < NT; ++n)
-#pragma unroll
-                            for (int t = 0; t < 4; ++t)
-                                xq[n][t] = (xr[n][2 * t].x + xr[n][2 * t].y) + (xr[n][2 * t].z + xr[n][2 * t].w) +
-                                           (xr[n][2 * t + 1].x + xr[n][2 * t + 1].y) +
-                                           (xr[n][2 * t + 1].z + xr[n][2 * t + 1].w);
-#pragma unroll
-                        for (int q = 0; q < 4; ++q) item_q6_k<NT>(base[q] + (gg - b0) * 210, c, xr, xq, acc[q]);
+                        for (int q = 0; q < 4; ++q) item_q8_0<NT>(base[q] + (blk - b0) * 34, xr, acc[q]);
                     }
                 }
                 R.item_base += ngroups;
@@ -1017,6 +1110,8 @@ bool stream_supported(const MulMatOp* ops, int n_ops) {
         if (o.K > kXF4 * kCW * 32 * 4) return false;
         if (o.type == kTypeQ4_K && ((reinterpret_cast<uintptr_t>(o.w) | static_cast<uintptr_t>(o.w_nb1)) & 15))
             return false;  // 16-byte header loads from shared memory
+        if ((reinterpret_cast<uintptr_t>(o.w) | static_cast<uintptr_t>(o.w_nb1)) & 1)
+            return false;  // 2-byte f16 and word-pair loads from shared memory
         if ((reinterpret_cast<uintptr_t>(o.x) | static_cast<uintptr_t>(o.x_nb1)) & 15) return false;
     }
     return true;
