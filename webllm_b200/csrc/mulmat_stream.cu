@@ -2,40 +2,42 @@
 // persistent, warp-specialised streaming GEMV over raw GGUF blocks.
 //
 // Data movement. The weight matrix is cut into units of 16 rows (one MMA
-// tile); each unit's rows into segments of at most 9 Q4_K / 6 Q6_K / 32 Q8_0
-// blocks. Warp 0 (copy warp) moves each (unit, segment) into a ring of shared
-// memory stages with ONE 2D tensor-map TMA copy (16 rows x the segment,
-// rounded out to 16-byte columns; evict-first L2 policy, each weight byte is
-// read once). Row layouts whose stride is not a multiple of 16 bytes fall back
-// to one bulk copy per row. The other warps (consumers) take work items (one
-// block of a unit, all 16 rows) round-robin from the CTA's item sequence
-// without CTA-wide barriers; the per-warp partial sums of a unit meet in
-// shared memory and the warp that finishes the unit last writes it out (fixed
-// summation order, so results are deterministic).
+// tile); each unit's rows into segments of at most 14 Q4_K / 9 Q6_K / 32 Q8_0
+// blocks. Warp 0 (copy warp, lane 0) moves each (unit, segment) into a ring
+// of shared-memory stages with ONE 2D tensor-map TMA copy (16 rows x the
+// segment, rounded out to 16-byte columns; evict-first L2 policy, each
+// weight byte is read once). Row layouts whose stride is not a multiple of 16
+// bytes fall back to one bulk copy per row. A launch's first kPreStages boxes
+// go out at once; the rest wait until the activation image is staged.
 //
-// Q4_K runs on integer tensor cores (mma.sync m16n8k32, u8 x s8 -> s32):
-//  - weights: ldmatrix hands each lane the bytes of its fragment; the low
-//    nibbles (v & 0x0F0F0F0F, sub-block 2p) and the high nibbles kept in place
-//    (v & 0xF0F0F0F0 = 16 q, sub-block 2p+1) are the A operands, one LOP each
-//    per four quants;
+// Work split. The 8 consumer warps take work items (one block of a unit, all
+// 16 rows; at N = 1 two blocks at a time) round-robin from the CTA's item
+// sequence without CTA-wide barriers. Every warp writes its partial sums of a
+// unit to shared memory and arrives on the unit's barrier; the unit's owner
+// warp sums the 8 partials in a fixed order (results are deterministic)
+// kRedDelay units later, when the others are normally done, and writes the
+// rows.
+//
+// Q4_K and Q6_K run on integer tensor cores (mma.sync m16n8k32, u8 x s8 ->
+// s32):
 //  - activations: per 256-element block and vector, x = (l0 + l1/128) / s with
 //    s = 127 / max|x| and int8 limbs l0 = rint(x s), l1 = rint(128 (x s - l0))
 //    (|error| <= max|x| / 32512); the two limbs of each vector are two B
-//    columns, so the MMA's eight columns hold up to four vectors;
-//  - each 32-element sub-block is one MMA; its s32 result is scaled by the
-//    sub-block's 6-bit scale in integer (16 sc for low-nibble sub-blocks, whose
-//    quants entered unscaled), accumulated exactly over the block, then
-//    converted once: y += d / (16 s) * (acc_l0 + acc_l1 / 128);
-//  - the min term dmin * m * sum(x) uses exact f32 sub-block sums of x, split
-//    over the four lanes of an MMA row group and summed once per unit.
-// Each consumer warp decodes the scales of its own item into a small
-// double-buffered table in shared memory (no cross-warp hand-off).
-//
-// Q6_K and Q8_0 run on CUDA cores: lanes 8j..8j+7 take row 4q+j (q = 0..3),
-// lane chunk c = lane%8 owns 32 elements of a 256-element block (Q6_K) or one
-// 32-element block (Q8_0). A 6-bit quant becomes the float 1 + q/128 with one
-// byte permute (0x80|q in bits 16..23 of 0x3F800000); S = sum (1 + q/128) x
-// runs on packed FFMA2 and the quant sum is 128 (S - X), X = sum x.
+//    columns, so the MMA's eight columns hold sub-block slots x vectors x
+//    limbs, and a sub-block's MMA reads real B rows only in its own slot's
+//    columns: several sub-blocks share one accumulator without mixing;
+//  - Q4_K weights: ldmatrix hands each lane the bytes of its fragment; the
+//    low nibbles (v & 0x0F0F0F0F) and the high nibbles kept in place
+//    (v & 0xF0F0F0F0 = 16 q) are the A operands; 6-bit scales are applied in
+//    integer (16 sc for the low-nibble sub-blocks), the mins through exact
+//    f32 sums of x over 32-element sub-blocks;
+//  - Q6_K weights (210-byte blocks, 2-byte aligned in shared memory): A
+//    fragments come from aligned 32-bit loads and a funnel shift; one LOP3
+//    per group assembles the 6-bit quants from ql and qh; int8 scales are
+//    applied in integer, the -32 offset through exact sums of x over
+//    16-element sub-blocks.
+// Q8_0 runs on CUDA cores: lanes 8j..8j+7 take row 4q+j (q = 0..3), lane
+// chunk c = lane%8 owns one 32-element block of each 8-block group.
 //
 // Launch: programmatic dependent launch. CTAs trigger their dependents at
 // entry; the copy warp streams weights (never written by a preceding kernel)
@@ -45,7 +47,6 @@
 #include <cuda.h>  // CUtensorMap types only; the encoder is fetched with cudaGetDriverEntryPoint
 #include <cuda_fp16.h>
 #include <stdint.h>
-#include <stdlib.h>
 
 #include "quant_blocks.cuh"
 #include "wllm_internal.h"
@@ -70,6 +71,12 @@ constexpr int kRedDelay = 2;                  // a unit's partials are summed th
 constexpr int kUnitSlots = kMaxStages + kRedDelay + 2;
 constexpr int kXPad = 16;                     // bytes after each int8 activation column (ldmatrix banks)
 constexpr int kMaxNT = 2;
+// Boxes the copy warp issues before the consumers have staged the first
+// activation image: the activation loads wait behind whatever weight requests
+// are queued in the memory system, so a launch's first boxes are held back
+// until the image is built.
+constexpr int kPreStages = 2;
+static_assert((kCW & (kCW - 1)) == 0, "unit ownership rotates with a mask");
 constexpr int kXF4 = 16;                      // float4 of x per consumer thread: K <= 16384
 constexpr uint32_t kSpinLimit = 1u << 26;     // polls before a wait gives up (well over a second)
 constexpr int kSmemBudget = 200 * 1024;       // one CTA per SM, up to 8 stages in flight
@@ -309,46 +316,62 @@ __device__ __forceinline__ void q4k_slot_scales(const uint4 h, int sl, int (&sc)
 // NS sub-blocks of a chain accumulate into one fragment without mixing, and
 // lane (g, c) ends up with its slot's sub-blocks (slot c / NP, vector c % NP)
 // of rows g and g+8: it scales only those, NCH = 8 / NS per row.
-template <int NP>
-__device__ __forceinline__ void q4k_item(const uint8_t* blk, int wbox, uint32_t wl, uint32_t xaddr, uint32_t xzero,
-                                         bool xv0, bool xv1, float xf, const float* xs, int g, int sl, float& yg,
-                                         float& yh) {
+template <int NP, int NI>
+__device__ __forceinline__ void q4k_items(const uint8_t* blk, int wbox, uint32_t wl, uint32_t xaddr, uint32_t xzero,
+                                          bool xv0, bool xv1, const float* df, const float* xs, int g, int sl,
+                                          float& yg, float& yh) {
+    // NI items of one unit at once (blocks kCW apart): independent chains the
+    // scheduler interleaves
     constexpr int NS = 4 / NP, NCH = 8 / NS;
-    const uint4 hg = *reinterpret_cast<const uint4*>(blk + g * wbox);
-    const uint4 hh = *reinterpret_cast<const uint4*>(blk + (g + 8) * wbox);
-    int scg[NCH], sch[NCH];
-    float mg[NCH], mh[NCH], dg, dh;
-    q4k_slot_scales<NS, NCH>(hg, sl, scg, mg, dg);
-    q4k_slot_scales<NS, NCH>(hh, sl, sch, mh, dh);
-    int D[NCH][4];
+    constexpr int BS = kCW * 144;  // stage bytes between the items
+    constexpr int XS = kCW * 256;  // activation bytes between the items
+    int scg[NI][NCH], sch[NI][NCH];
+    float mg[NI][NCH], mh[NI][NCH], dg[NI], dh[NI];
 #pragma unroll
-    for (int q = 0; q < NCH; ++q) D[q][0] = D[q][1] = D[q][2] = D[q][3] = 0;
+    for (int k = 0; k < NI; ++k) {
+        const uint4 hg = *reinterpret_cast<const uint4*>(blk + k * BS + g * wbox);
+        const uint4 hh = *reinterpret_cast<const uint4*>(blk + k * BS + (g + 8) * wbox);
+        q4k_slot_scales<NS, NCH>(hg, sl, scg[k], mg[k], dg[k]);
+        q4k_slot_scales<NS, NCH>(hh, sl, sch[k], mh[k], dh[k]);
+    }
+    int D[NI][NCH][4];
+#pragma unroll
+    for (int k = 0; k < NI; ++k)
+#pragma unroll
+        for (int q = 0; q < NCH; ++q) D[k][q][0] = D[k][q][1] = D[k][q][2] = D[k][q][3] = 0;
     const uint32_t wbase = smem_u32(blk) + wl;
 #pragma unroll
     for (int p = 0; p < 4; ++p) {
-        uint32_t w[4], x[4];
-        ldmatrix_x4_at(w, wbase + 32 * p);
-        ldmatrix_x4_at(x, ((p & 1) ? xv1 : xv0) ? xaddr + 64 * p : xzero);
-        imma_u8s8_acc(D[(2 * p) / NS], w[0] & 0x0F0F0F0Fu, w[1] & 0x0F0F0F0Fu, w[2] & 0x0F0F0F0Fu, w[3] & 0x0F0F0F0Fu,
-                      x[0], x[1]);
-        imma_u8s8_acc(D[(2 * p + 1) / NS], w[0] & 0xF0F0F0F0u, w[1] & 0xF0F0F0F0u, w[2] & 0xF0F0F0F0u,
-                      w[3] & 0xF0F0F0F0u, x[2], x[3]);
-    }
-    int a0 = 0, a1 = 0, a2 = 0, a3 = 0;  // (g, limb 0), (g, limb 1), (g+8, l0), (g+8, l1)
 #pragma unroll
-    for (int q = 0; q < NCH; ++q) {
-        a0 += scg[q] * D[q][0];
-        a1 += scg[q] * D[q][1];
-        a2 += sch[q] * D[q][2];
-        a3 += sch[q] * D[q][3];
+        for (int k = 0; k < NI; ++k) {
+            uint32_t w[4], x[4];
+            ldmatrix_x4_at(w, wbase + k * BS + 32 * p);
+            ldmatrix_x4_at(x, ((p & 1) ? xv1 : xv0) ? xaddr + k * XS + 64 * p : xzero);
+            imma_u8s8_acc(D[k][(2 * p) / NS], w[0] & 0x0F0F0F0Fu, w[1] & 0x0F0F0F0Fu, w[2] & 0x0F0F0F0Fu,
+                          w[3] & 0x0F0F0F0Fu, x[0], x[1]);
+            imma_u8s8_acc(D[k][(2 * p + 1) / NS], w[0] & 0xF0F0F0F0u, w[1] & 0xF0F0F0F0u, w[2] & 0xF0F0F0F0u,
+                          w[3] & 0xF0F0F0F0u, x[2], x[3]);
+        }
     }
-    yg = fmaf(fmaf(static_cast<float>(a1), 0.0078125f, static_cast<float>(a0)), dg * xf, yg);
-    yh = fmaf(fmaf(static_cast<float>(a3), 0.0078125f, static_cast<float>(a2)), dh * xf, yh);
 #pragma unroll
-    for (int q = 0; q < NCH; ++q) {
-        const float X = xs[q * NS + sl];
-        yg = fmaf(-mg[q], X, yg);
-        yh = fmaf(-mh[q], X, yh);
+    for (int k = 0; k < NI; ++k) {
+        int a0 = 0, a1 = 0, a2 = 0, a3 = 0;  // (g, limb 0), (g, limb 1), (g+8, l0), (g+8, l1)
+#pragma unroll
+        for (int q = 0; q < NCH; ++q) {
+            a0 += scg[k][q] * D[k][q][0];
+            a1 += scg[k][q] * D[k][q][1];
+            a2 += sch[k][q] * D[k][q][2];
+            a3 += sch[k][q] * D[k][q][3];
+        }
+        const float xf = df[k * kCW];
+        yg = fmaf(fmaf(static_cast<float>(a1), 0.0078125f, static_cast<float>(a0)), dg[k] * xf, yg);
+        yh = fmaf(fmaf(static_cast<float>(a3), 0.0078125f, static_cast<float>(a2)), dh[k] * xf, yh);
+#pragma unroll
+        for (int q = 0; q < NCH; ++q) {
+            const float X = xs[k * kCW * 8 + q * NS + sl];
+            yg = fmaf(-mg[k][q], X, yg);
+            yh = fmaf(-mh[k][q], X, yh);
+        }
     }
 }
 
@@ -483,6 +506,32 @@ struct OpInfo {
     int32_t unit_begin, seg_blocks, nseg, wbox, use_tma;
 };
 
+// The current op's fields, held in registers by the consumer warps (the
+// shared-memory table is read only when the op changes).
+struct OpRegs {
+    const uint8_t* w;
+    float* y;
+    int64_t w_nb1, y_nb1;
+    int32_t type, M, K, N, unit_begin, seg_blocks, nseg, wbox;
+};
+
+__device__ __forceinline__ OpRegs op_regs(const OpInfo& o) {
+    OpRegs r;
+    r.w = o.w;
+    r.y = o.y;
+    r.w_nb1 = o.w_nb1;
+    r.y_nb1 = o.y_nb1;
+    r.type = o.type;
+    r.M = o.M;
+    r.K = o.K;
+    r.N = o.N;
+    r.unit_begin = o.unit_begin;
+    r.seg_blocks = o.seg_blocks;
+    r.nseg = o.nseg;
+    r.wbox = o.wbox;
+    return r;
+}
+
 struct OpTable {
     OpInfo op[kMaxOpsPerLaunch];
     int32_t n_ops, total_units;
@@ -499,47 +548,60 @@ __device__ __forceinline__ void stage_activations(const OpInfo& op, uint8_t* xsm
         float* dfac = reinterpret_cast<float*>(xsm + img_inv_off(K, N));
         float* Xs = reinterpret_cast<float*>(xsm + img_sum_off(K, N));
         float* X16 = reinterpret_cast<float*>(xsm + img_sum16_off(K, N));
-        // one (vector, block) per half-warp: lane h = lane%16 covers elements
-        // 16h .. 16h+15; all of a round's loads are issued before any arithmetic
-        const int hw = lane >> 4, h = lane & 15;
-        for (int tb = 2 * cw + hw; tb - hw < N * nblk; tb += 2 * kCW) {  // warp-uniform
-            const bool act = tb < N * nblk;
-            const int t = act ? tb / nblk : 0, b = act ? tb - t * nblk : 0;
-            const float4* xv = reinterpret_cast<const float4*>(xb + t * op.x_nb1) + b * 64 + 4 * h;
-            float4 v[4];
+        // one (vector, block) per half-warp and round: lane h = lane%16 covers
+        // elements 16h .. 16h+15. Two rounds' loads are issued before any
+        // arithmetic (K = 8192 at N = 1 is two rounds: one L2 round trip)
+        const int hw = lane >> 4, h = lane & 15, total = N * nblk;
+        for (int tb0 = 2 * cw + hw; tb0 - hw < total; tb0 += 4 * kCW) {  // warp-uniform
+            float4 v[2][4];
+            bool act[2];
+            int t[2], b[2];
 #pragma unroll
-            for (int k = 0; k < 4; ++k) v[k] = act ? __ldg(xv + k) : make_float4(0.f, 0.f, 0.f, 0.f);
-            float mx = 0.f;
+            for (int r = 0; r < 2; ++r) {
+                const int tb = tb0 + 2 * kCW * r;
+                act[r] = tb < total;
+                t[r] = act[r] ? tb / nblk : 0;
+                b[r] = act[r] ? tb - t[r] * nblk : 0;
+                const float4* xv = reinterpret_cast<const float4*>(xb + t[r] * op.x_nb1) + b[r] * 64 + 4 * h;
 #pragma unroll
-            for (int k = 0; k < 4; ++k)
-                mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v[k].x), fabsf(v[k].y)), fmaxf(fabsf(v[k].z), fabsf(v[k].w))));
-#pragma unroll
-            for (int o = 8; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));  // within the half
-            const float sc = mx > 0.f ? 127.f / mx : 0.f;
-            uint32_t p0[4], p1[4];
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                const float4 e = v[k];
-                const int q0 = __float2int_rn(e.x * sc), q1 = __float2int_rn(e.y * sc);  // |l0| <= 127
-                const int q2 = __float2int_rn(e.z * sc), q3 = __float2int_rn(e.w * sc);
-                p0[k] = pack_b4(q0, q1, q2, q3);
-                // |l1| <= 64
-                p1[k] = pack_b4(__float2int_rn(fmaf(e.x, sc, -static_cast<float>(q0)) * 128.f),
-                                __float2int_rn(fmaf(e.y, sc, -static_cast<float>(q1)) * 128.f),
-                                __float2int_rn(fmaf(e.z, sc, -static_cast<float>(q2)) * 128.f),
-                                __float2int_rn(fmaf(e.w, sc, -static_cast<float>(q3)) * 128.f));
+                for (int k = 0; k < 4; ++k) v[r][k] = act[r] ? __ldg(xv + k) : make_float4(0.f, 0.f, 0.f, 0.f);
             }
-            float a16 = 0.f;  // a lane's 16 elements: one Q6_K sub-block
 #pragma unroll
-            for (int k = 0; k < 4; ++k) a16 += (v[k].x + v[k].y) + (v[k].z + v[k].w);
-            const float a = a16 + __shfl_xor_sync(0xffffffffu, a16, 1);  // a Q4_K sub-block is two lanes
-            if (act) {
-                uint8_t* c0 = xsm + (2 * t) * XS + b * 256 + 16 * h;
-                *reinterpret_cast<uint4*>(c0) = make_uint4(p0[0], p0[1], p0[2], p0[3]);
-                *reinterpret_cast<uint4*>(c0 + XS) = make_uint4(p1[0], p1[1], p1[2], p1[3]);
-                X16[t * (K / 16) + b * 16 + h] = a16;
-                if ((h & 1) == 0) Xs[t * (K / 32) + b * 8 + (h >> 1)] = a;
-                if (h == 0) dfac[t * nblk + b] = mx * (1.f / 2032.f);  // 1 / (16 s)
+            for (int r = 0; r < 2; ++r) {
+                float mx = 0.f;
+#pragma unroll
+                for (int k = 0; k < 4; ++k)
+                    mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v[r][k].x), fabsf(v[r][k].y)),
+                                         fmaxf(fabsf(v[r][k].z), fabsf(v[r][k].w))));
+#pragma unroll
+                for (int o = 8; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));  // within the half
+                const float sc = mx > 0.f ? 127.f / mx : 0.f;
+                uint32_t p0[4], p1[4];
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    const float4 e = v[r][k];
+                    const int q0 = __float2int_rn(e.x * sc), q1 = __float2int_rn(e.y * sc);  // |l0| <= 127
+                    const int q2 = __float2int_rn(e.z * sc), q3 = __float2int_rn(e.w * sc);
+                    p0[k] = pack_b4(q0, q1, q2, q3);
+                    // |l1| <= 64
+                    p1[k] = pack_b4(__float2int_rn(fmaf(e.x, sc, -static_cast<float>(q0)) * 128.f),
+                                    __float2int_rn(fmaf(e.y, sc, -static_cast<float>(q1)) * 128.f),
+                                    __float2int_rn(fmaf(e.z, sc, -static_cast<float>(q2)) * 128.f),
+                                    __float2int_rn(fmaf(e.w, sc, -static_cast<float>(q3)) * 128.f));
+                }
+                float a16 = 0.f;  // a lane's 16 elements: one Q6_K sub-block
+#pragma unroll
+                for (int k = 0; k < 4; ++k) a16 += (v[r][k].x + v[r][k].y) + (v[r][k].z + v[r][k].w);
+                const float a = a16 + __shfl_xor_sync(0xffffffffu, a16, 1);  // a Q4_K sub-block is two lanes
+                if (act[r]) {
+                    const int tt = t[r], bb = b[r];
+                    uint8_t* c0 = xsm + (2 * tt) * XS + bb * 256 + 16 * h;
+                    *reinterpret_cast<uint4*>(c0) = make_uint4(p0[0], p0[1], p0[2], p0[3]);
+                    *reinterpret_cast<uint4*>(c0 + XS) = make_uint4(p1[0], p1[1], p1[2], p1[3]);
+                    X16[tt * (K / 16) + bb * 16 + h] = a16;
+                    if ((h & 1) == 0) Xs[tt * (K / 32) + bb * 8 + (h >> 1)] = a;
+                    if (h == 0) dfac[tt * nblk + bb] = mx * (1.f / 2032.f);  // 1 / (16 s)
+                }
             }
         }
         consumers_sync();
@@ -675,7 +737,7 @@ __device__ __forceinline__ void ring_wait(Ring& R, int lane) {
 // All segments of one Q4_K unit for this consumer warp; writes the warp's
 // partial sums of the unit's 16 rows (zeros where it had no item) to ub.
 template <int NP, int NT>
-__device__ __forceinline__ void q4k_unit(const OpInfo& op, const Q4Lane& q, Ring& R, uint32_t xzero, int lane,
+__device__ __forceinline__ void q4k_unit(const OpRegs& op, const Q4Lane& q, Ring& R, uint32_t xzero, int lane,
                                          int cw, float* ub) {
     const int N = op.N, nblocks = op.K / 256;
     const int g = lane >> 2, sl = q.sl, tk = q.tk;
@@ -694,10 +756,17 @@ __device__ __forceinline__ void q4k_unit(const OpInfo& op, const Q4Lane& q, Ring
         if (i0 < nb) {
             ring_wait(R, lane);
             const uint8_t* stage = R.stages + R.slot * R.SB;
-            for (int i = i0; i < nb; i += kCW) {
+            int i = i0;
+            // item pairs at N = 1 (at N = 2 the doubled accumulators would spill)
+            for (; NP == 1 && i + kCW < nb; i += 2 * kCW) {
                 const int bg = b0 + i;
-                q4k_item<NP>(stage + i * 144, op.wbox, wl, xcol + bg * 256, xzero, xv0, xv1, dfac[bg], Xs + bg * 8, g,
-                             sl, yg, yh);
+                q4k_items<NP, 2>(stage + i * 144, op.wbox, wl, xcol + bg * 256, xzero, xv0, xv1, dfac + bg,
+                                 Xs + bg * 8, g, sl, yg, yh);
+            }
+            for (; i < nb; i += kCW) {
+                const int bg = b0 + i;
+                q4k_items<NP, 1>(stage + i * 144, op.wbox, wl, xcol + bg * 256, xzero, xv0, xv1, dfac + bg,
+                                 Xs + bg * 8, g, sl, yg, yh);
             }
             __syncwarp();
             if (lane == 0) mbar_arrive_cnt(&R.empty[R.slot], i0 == 0 ? 1u + kCW - min(nb, kCW) : 1u);
@@ -721,7 +790,7 @@ __device__ __forceinline__ void q4k_unit(const OpInfo& op, const Q4Lane& q, Ring
 // row's copy window starts at its segment start rounded down to 16 bytes;
 // glo is the low word of the unit's first row address.
 template <int NP, int NT>
-__device__ __forceinline__ void q6k_unit(const OpInfo& op, const Q6Lane& q, Ring& R, uint32_t xzero, uint32_t glo,
+__device__ __forceinline__ void q6k_unit(const OpRegs& op, const Q6Lane& q, Ring& R, uint32_t xzero, uint32_t glo,
                                          int lane, int cw, float* ub) {
     const int N = op.N, nblocks = op.K / 256;
     const int g = lane >> 2, c = lane & 3, sl = q.sl, tk = q.tk;
@@ -776,7 +845,8 @@ __global__ void __launch_bounds__(kThreads, 1) stream_gemv_kernel(const __grid_c
     uint64_t* ubar = reinterpret_cast<uint64_t*>(umeta + kUnitSlots);    // [kUnitSlots]: all warps' partials written
     uint64_t* full = ubar + kUnitSlots;
     uint64_t* empty = full + kMaxStages;
-    volatile int* poisoned = reinterpret_cast<volatile int*>(empty + kMaxStages);
+    uint64_t* xready = empty + kMaxStages;  // the first activation image is staged
+    volatile int* poisoned = reinterpret_cast<volatile int*>(xready + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x < 4) reinterpret_cast<uint32_t*>(zrow)[threadIdx.x] = 0u;
@@ -786,6 +856,7 @@ __global__ void __launch_bounds__(kThreads, 1) stream_gemv_kernel(const __grid_c
             mbar_init(&empty[s], kCW);
         }
         for (int s = 0; s < kUnitSlots; ++s) mbar_init(&ubar[s], kCW);
+        mbar_init(xready, 1);
         *poisoned = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -826,7 +897,7 @@ __global__ void __launch_bounds__(kThreads, 1) stream_gemv_kernel(const __grid_c
         const int n_ops = T.n_ops, total = T.total_units;
         int u = blockIdx.x, oi = 0;
         while (oi + 1 < n_ops && u >= T.op[oi + 1].unit_begin) ++oi;
-        int s = 0;
+        int s = 0, issued = 0;
         uint32_t phase = 1;  // the first pass finds every slot free
         for (; u < total; u += gridDim.x) {
             while (oi + 1 < n_ops && u >= T.op[oi + 1].unit_begin) ++oi;
@@ -837,6 +908,7 @@ __global__ void __launch_bounds__(kThreads, 1) stream_gemv_kernel(const __grid_c
             const CUtensorMap* tm = &L.op[oi].tmap;
             for (int sg = 0, col = 0; sg < nseg; ++sg, col += step) {
                 if (!mbar_wait(&empty[s], phase, 1u, poisoned)) return;
+                if (issued++ == kPreStages && !mbar_wait(xready, 0u, 3u, poisoned)) return;
                 // one box: 16 rows x wbox bytes from the 16-byte-aligned column at or
                 // below the segment start (rows past M and columns past the row end
                 // read as zeros)
@@ -859,7 +931,7 @@ __global__ void __launch_bounds__(kThreads, 1) stream_gemv_kernel(const __grid_c
         const int n_ops = T.n_ops, total = T.total_units;
         int u = blockIdx.x, oi = 0;
         while (oi + 1 < n_ops && u >= T.op[oi + 1].unit_begin) ++oi;
-        int s = 0;
+        int s = 0, issued = 0;
         uint32_t phase = 1;  // the first pass finds every slot free
         for (; u < total; u += gridDim.x) {
             while (oi + 1 < n_ops && u >= T.op[oi + 1].unit_begin) ++oi;
@@ -873,7 +945,11 @@ __global__ void __launch_bounds__(kThreads, 1) stream_gemv_kernel(const __grid_c
             bool stop = false;
             for (int sg = 0; sg < nseg; ++sg) {
                 int ok = 0;
-                if (lane == 0) ok = mbar_wait(&empty[s], phase, 1u, poisoned);
+                if (lane == 0) {
+                    ok = mbar_wait(&empty[s], phase, 1u, poisoned);
+                    if (ok && issued == kPreStages) ok = mbar_wait(xready, 0u, 3u, poisoned);
+                }
+                ++issued;
                 if (!__shfl_sync(0xffffffffu, ok, 0)) {
                     stop = true;
                     break;
@@ -917,6 +993,9 @@ __global__ void __launch_bounds__(kThreads, 1) stream_gemv_kernel(const __grid_c
     Ring R{stages, full, empty, poisoned, SB, S, 0, 0u, 0u};
     const int n_ops = T.n_ops, total = T.total_units;
     int staged = -1, oi = -1, useq = 0;
+    int next_begin = -1;     // first unit of the next op
+    int uslot = 0, own = 0;  // useq % kUnitSlots, useq % kCW
+    OpRegs op{};
     Q4Lane q4{};
     Q6Lane q6{};
     // Sums the 8 warps' partials of this CTA's unit number j (fixed order:
@@ -936,27 +1015,28 @@ __global__ void __launch_bounds__(kThreads, 1) stream_gemv_kernel(const __grid_c
         }
     };
     for (int u = blockIdx.x; u < total; u += gridDim.x, ++useq) {
-        if (oi < 0 || (oi + 1 < n_ops && u >= T.op[oi + 1].unit_begin)) {
+        if (u >= next_begin) {
             // ---- next op: activation image (re)built when x or its layout changes ----
             do {
                 ++oi;
             } while (oi + 1 < n_ops && u >= T.op[oi + 1].unit_begin);
-            const OpInfo& op = T.op[oi];
-            if (staged < 0 || T.op[staged].x != op.x || T.op[staged].K != op.K || T.op[staged].N != op.N ||
-                T.op[staged].x_nb1 != op.x_nb1 || limb_image(T.op[staged].type) != limb_image(op.type)) {
+            const OpInfo& oo = T.op[oi];
+            if (staged < 0 || T.op[staged].x != oo.x || T.op[staged].K != oo.K || T.op[staged].N != oo.N ||
+                T.op[staged].x_nb1 != oo.x_nb1 || limb_image(T.op[staged].type) != limb_image(oo.type)) {
                 consumers_sync();  // nobody still reads the previous image
-                stage_activations(op, xsm, ct, lane, cw);
+                stage_activations(oo, xsm, ct, lane, cw);
+                if (ct == 0 && useq == 0) mbar_arrive_cnt(xready, 1u);  // the copy warp may go on
                 staged = oi;
             }
-            if (op.type == kTypeQ4_K) q4 = (NT == 1 || op.N == 1) ? q4k_lane<1>(op, xsm, lane) : q4k_lane<2>(op, xsm, lane);
-            if (op.type == kTypeQ6_K) q6 = (NT == 1 || op.N == 1) ? q6k_lane<1>(op, xsm, lane) : q6k_lane<2>(op, xsm, lane);
+            if (oo.type == kTypeQ4_K) q4 = (NT == 1 || oo.N == 1) ? q4k_lane<1>(oo, xsm, lane) : q4k_lane<2>(oo, xsm, lane);
+            if (oo.type == kTypeQ6_K) q6 = (NT == 1 || oo.N == 1) ? q6k_lane<1>(oo, xsm, lane) : q6k_lane<2>(oo, xsm, lane);
+            op = op_regs(oo);
+            next_begin = oi + 1 < n_ops ? T.op[oi + 1].unit_begin : total;
         }
-        const OpInfo& op = T.op[oi];
         const int N = op.N, K = op.K;
         const int bb = block_bytes_of(op.type);
         const int nblocks = K / block_elems_of(op.type);
         const int r0 = (u - op.unit_begin) * kRows;
-        const int uslot = useq % kUnitSlots;
         // this warp's partial sums of the unit: every warp writes all 16 rows
         float* ub = ubuf + (uslot * kCW + cw) * kRows * NT;
 
@@ -1038,7 +1118,7 @@ __global__ void __launch_bounds__(kThreads, 1) stream_gemv_kernel(const __grid_c
                 }
         }
         // ---- unit hand-off: publish this warp's partials; the owner sums them later ----
-        if (useq % kCW == cw && lane == 0) {
+        if (own == cw && lane == 0) {
             UnitMeta m;
             m.y = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(op.y) + 4LL * r0);
             m.y_nb1 = op.y_nb1;
@@ -1048,7 +1128,9 @@ __global__ void __launch_bounds__(kThreads, 1) stream_gemv_kernel(const __grid_c
         }
         __syncwarp();
         if (lane == 0) mbar_arrive_cnt(&ubar[uslot], 1u);  // release: the warp's partial writes precede it
-        if (useq >= kRedDelay && (useq - kRedDelay) % kCW == cw) reduce_unit(useq - kRedDelay);
+        if (useq >= kRedDelay && ((own - kRedDelay) & (kCW - 1)) == cw) reduce_unit(useq - kRedDelay);
+        if (++uslot == kUnitSlots) uslot = 0;
+        own = (own + 1) & (kCW - 1);
     }
     // the last kRedDelay units of the CTA
     for (int j = useq - kRedDelay; j < useq; ++j)
@@ -1058,7 +1140,7 @@ __global__ void __launch_bounds__(kThreads, 1) stream_gemv_kernel(const __grid_c
 size_t smem_bytes(int stages, int stage_bytes, int x_bytes, int nt) {
     return static_cast<size_t>(stages) * static_cast<size_t>(stage_bytes) + static_cast<size_t>(x_bytes) +
            16ull + 4ull * kUnitSlots * kCW * kRows * nt + sizeof(UnitMeta) * kUnitSlots + 8ull * kUnitSlots +
-           8ull * (2 * kMaxStages) + 16;
+           8ull * (2 * kMaxStages + 1) + 16;
 }
 
 typedef CUresult (*TensorMapEncodeFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
@@ -1171,16 +1253,8 @@ int launch_stream(const MulMatOp* ops, int n_ops, cudaStream_t stream, int num_s
     L.stages = stages;
     const size_t smem = smem_bytes(stages, L.stage_bytes, x_bytes, nt);
     if (smem > 227 * 1024) return -static_cast<int>(cudaErrorInvalidValue);
-    // CTAs per SM: two by default (~140 KB of weights in flight per SM, and a
-    // finished CTA's slot goes to the next launch early); one via the
-    // environment for experiments.
-    static const int ctas_per_sm = [] {
-        const char* e = getenv("WLLM_STREAM_CTAS_PER_SM");
-        const int v = e ? atoi(e) : 1;
-        return v == 2 ? 2 : 1;
-    }();
-    const int cap = ctas_per_sm * num_sms;
-    const int grid = units < cap ? units : cap;
+    // one CTA per SM: the ring needs most of its shared memory
+    const int grid = units < num_sms ? units : num_sms;
 
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -1221,3 +1295,4 @@ unsigned read_and_clear_stream_error() {
 }
 
 }  // namespace wllm
+
