@@ -43,6 +43,10 @@ import numpy as np  # noqa: E402
 
 METRIC = "quantized MUL_MAT GB/s & % HBM peak (decode); prefill TFLOPS; at 1/2/4/8 GPU"
 WORKLOAD = "llama-3.2-3b decode sweep (28 layers x 7 GEMVs, Q4_K/Q6_K x f32, batch 1)"
+# DRAM bytes (read + write) of one layer's four GEMV launches, summed from an
+# ncu capture of this workload (profiles/stream_gemv_llama32_3b_decode.md);
+# the algorithmic bytes are 64,139,264 per layer.
+NCU_DRAM_BYTES_PER_LAYER = 64_273_024
 FALLBACK_HBM_GBS = 6650.0
 
 
@@ -441,7 +445,9 @@ def run_b200(args, rank: int, world: int, local_rank: int):
                        "parallelism": f"tp{world} row-sharded" + (" + NCCL all-gather per group" if world > 1 else ""),
                        "launch": "4 grouped launches per layer, one CUDA graph per step"},
             "roofline": {"bound": "hbm", "achieved": round(gbs, 2), "peak": peak, "unit": "GB/s",
-                         "frac": round(gbs / peak, 4), "traffic": None,
+                         "frac": round(gbs / peak, 4),
+                         "traffic": NCU_DRAM_BYTES_PER_LAYER * layers if world == 1 else None,
+                         "traffic_note": "ncu dram__bytes_read.sum + dram__bytes_write.sum of the step's GEMV launches",
                          "peak_source": f"{peak_src} hbm_gbs (burst copy)",
                          "note": "achieved = step algorithmic bytes / step device time over all launches of the GEMV kernel"
                                  + (" (includes all-gathers)" if world > 1 else "")},
@@ -537,7 +543,8 @@ def jsep_path_e2e(args, layers: int):
         dm.free(h)
     return {"value": round(step_bytes(layers) / (ms * 1e-3) / 1e9, 2), "unit": "GB/s", "ms_per_step": round(ms, 4),
             "h2d_bytes_per_step": x_off, "d2h_bytes_per_step": y_off,
-            "path": "wllm_write(pageable host) -> wllm_graph_launch(112 recorded wllm_run_ops) -> wllm_read"}
+            "path": f"wllm_write(pageable host) -> wllm_graph_launch({layers * len(layer_groups())} recorded "
+                    "wllm_run_ops) -> wllm_read"}
 
 
 def main():
