@@ -136,6 +136,13 @@ def prefill_measure(dev, reps: int = 10, warmup: int = 3):
                          "note": "time includes the f32->f16 activation pre-pass of each MUL_MAT"}}
 
 
+class DevArray:
+    """A raw device pointer (library memory) as a torch tensor, zero copy."""
+
+    def __init__(self, ptr: int, n: int):
+        self.__cuda_array_interface__ = {"shape": (n,), "typestr": "<f4", "data": (ptr, False), "version": 3}
+
+
 def layer_groups():
     """[(input K, [(name, qtype, M, K), ...]), ...] for one layer."""
     from webllm_b200 import synth
@@ -302,49 +309,71 @@ def run_b200(args, rank: int, world: int, local_rank: int):
     layers = args.layers
     groups = layer_groups()
     gen = torch.Generator(device=dev)
+    # Row-sharded (world > 1): each group's rows from every rank land in one
+    # gathered buffer per rank, [world][group rows]. The GEMV writes this
+    # rank's rows into every rank's buffer over NVLink (peer memory opened
+    # with CUDA IPC); one bounded wait at the end of the step completes them.
+    tp = gview = None
+    gtot = [sum(row_shard(M, world, rank).padded for (_, _, M, _) in mats) for _, mats in groups]
+    per_layer = sum(world * g for g in gtot)
+    if world > 1:
+        g_ptr, g_handle = jsep.ipc_alloc(4 * per_layer * layers)
+        s_ptr, s_handle = jsep.ipc_alloc(4 * jsep.MAX_RANKS)
+        st_ptr, _ = jsep.ipc_alloc(16)
+        handles = [None] * world
+        dist.all_gather_object(handles, (g_handle, s_handle))
+        gbase = [g_ptr if r == rank else jsep.ipc_open(handles[r][0]) for r in range(world)]
+        sigs = [s_ptr if r == rank else jsep.ipc_open(handles[r][1]) for r in range(world)]
+        tp = jsep.tp_group(world, rank, sigs, st_ptr)
+        gview = torch.as_tensor(DevArray(g_ptr, per_layer * layers), device=dev)
     # ---- resident weights (row shard of every matrix), inputs, outputs
-    W, X, Y, G, ops = [], [], [], [], []
+    W, X, Y, ops, peer_outs = [], [], [], [], []
     for li in range(layers):
-        lw, lx, ly, lg, lops = [], [], [], [], []
+        lw, lx, ly, lops, louts = [], [], [], [], []
+        base = li * per_layer
         for gi, (kin, mats) in enumerate(groups):
             x = torch.randn(1, kin, device=dev, generator=gen.manual_seed(10_000 * li + 10 * gi))
             lx.append(x)
-            gops, gys = [], []
-            # the group's row shards share one output buffer, so the group needs
-            # one all-gather (a decode layer's outputs are 4-32 KB: the gather
-            # is latency-bound, one call per group instead of one per matrix)
             pads = [row_shard(M, world, rank).padded for (_, _, M, _) in mats]
-            ybuf = torch.zeros(1, sum(pads), device=dev)
             offs = [sum(pads[:i]) for i in range(len(pads))]
+            if world > 1:
+                out = gview[base:base + world * gtot[gi]].view(1, -1)  # the group's gathered rows
+            else:
+                out = torch.zeros(1, gtot[gi], device=dev)
+            gops, gouts = [], []
             for mi, (name, t, M, K) in enumerate(mats):
                 # this rank's contiguous row shard; every rank reserves `padded` rows
-                # in the gather buffer (the shapes here divide evenly at 1/2/4/8)
                 sh = row_shard(M, world, rank)
                 Mr = sh.count
                 gen.manual_seed(1_000_000 + 10_000 * li + 100 * gi + 10 * mi + rank)
                 w = synth.weights_torch(gen, t, Mr, K, dev)
-                y = ybuf[:, offs[mi]:offs[mi] + sh.padded]
                 lw.append(w)
-                gys.append(y)
+                col = rank * gtot[gi] + offs[mi]  # float offset of this rank's rows in the group's rows
                 gops.append(jsep.MulMatArgs(t, Mr, K, 1, w.data_ptr(), synth.row_bytes(t, K), x.data_ptr(), K,
-                                            y.data_ptr(), Mr))
-            ly.append((ybuf, gys))
-            lg.append(torch.empty(world * ybuf.numel(), device=dev) if world > 1 else None)
+                                            out.data_ptr() + 4 * col, Mr))
+                if world > 1:
+                    gouts.append([gbase[r] + 4 * (base + col) for r in range(world)])
+            ly.append(out)
             lops.append(gops)
+            louts.append(gouts)
+            base += world * gtot[gi]
         W.append(lw)
         X.append(lx)
         Y.append(ly)
-        G.append(lg)
         ops.append(lops)
+        peer_outs.append(louts)
     torch.cuda.synchronize()
-    launches_per_step = layers * len(groups)
+    launches_per_step = layers * len(groups) + (1 if world > 1 else 0)
 
     def step(stream_ptr: int):
         for li in range(layers):
             for gi in range(len(groups)):
-                jsep.mul_mat_batch(ops[li][gi], stream_ptr)
                 if world > 1:
-                    dist.all_gather_into_tensor(G[li][gi], Y[li][gi][0].view(-1))
+                    jsep.mul_mat_batch_tp(ops[li][gi], peer_outs[li][gi], tp, stream_ptr)
+                else:
+                    jsep.mul_mat_batch(ops[li][gi], stream_ptr)
+        if world > 1:
+            jsep.tp_wait(tp, stream_ptr)
 
     # ---- warm-up, then capture the step as one CUDA graph
     s = torch.cuda.current_stream()
@@ -389,8 +418,8 @@ def run_b200(args, rank: int, world: int, local_rank: int):
     # ---- e2e: pinned host activations in, outputs out, every step
     flat_x = [x for lx in X for x in lx]
     x_host = [torch.randn_like(x, device="cpu").pin_memory() for x in flat_x]
-    # every group's gathered output (or, at one GPU, its output buffer)
-    outs = [g if g is not None else yb[0] for ly, lg in zip(Y, G) for yb, g in zip(ly, lg)]
+    # every group's output (at N > 1 the gathered rows of all ranks)
+    outs = [o for ly in Y for o in ly]
     y_host = [torch.empty_like(o, device="cpu").pin_memory() for o in outs]
     h2d = sum(t.numel() * 4 for t in x_host)
     d2h = sum(t.numel() * 4 for t in y_host) if rank == 0 else 0
@@ -442,7 +471,8 @@ def run_b200(args, rank: int, world: int, local_rank: int):
             "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": {"workload": WORKLOAD, "layers": layers, "batch": 1, "bytes_per_step": total_bytes,
                        "l2": "inputs larger than L2 (1.80 GB of distinct weights per step), no flush",
-                       "parallelism": f"tp{world} row-sharded" + (" + NCCL all-gather per group" if world > 1 else ""),
+                       "parallelism": f"tp{world} row-sharded" + (" + NVLink peer-write gather fused into the GEMV"
+                                                                      if world > 1 else ""),
                        "launch": "4 grouped launches per layer, one CUDA graph per step"},
             "roofline": {"bound": "hbm", "achieved": round(gbs, 2), "peak": peak, "unit": "GB/s",
                          "frac": round(gbs / peak, 4),
@@ -450,7 +480,7 @@ def run_b200(args, rank: int, world: int, local_rank: int):
                          "traffic_note": "ncu dram__bytes_read.sum + dram__bytes_write.sum of the step's GEMV launches",
                          "peak_source": f"{peak_src} hbm_gbs (burst copy)",
                          "note": "achieved = step algorithmic bytes / step device time over all launches of the GEMV kernel"
-                                 + (" (includes all-gathers)" if world > 1 else "")},
+                                 + (" (includes the fused gather and its end-of-step wait)" if world > 1 else "")},
             "cpu_baseline": cpu,
             "e2e": {"value": round(total_bytes / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 4),
@@ -465,7 +495,14 @@ def run_b200(args, rank: int, world: int, local_rank: int):
     if world > 1:
         del graph
         torch.cuda.synchronize()
-        dist.barrier()
+        dist.barrier()  # no rank still writes into another's memory
+        for r in range(world):
+            if r != rank:
+                jsep.ipc_close(gbase[r])
+                jsep.ipc_close(sigs[r])
+        dist.barrier()  # every mapping closed before the owners free
+        for ptr in (g_ptr, s_ptr, st_ptr):
+            jsep.ipc_free(ptr)
         dist.destroy_process_group()
     if line is not None:
         print(json.dumps(line), flush=True)

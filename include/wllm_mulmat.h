@@ -163,6 +163,53 @@ typedef struct wllm_mulmat_args {
  * `stream` (NULL = the library stream). */
 int32_t wllm_mul_mat_batch(const wllm_mulmat_args* ops, int32_t n_ops, void* stream);
 
+/* ---- Row-sharded multi-GPU decode with the gather fused into the GEMV ----
+ * No counterpart in the reference, which runs on one browser GPU. The
+ * reference's op semantics (dst[m + M*n], matmul.ts:10-17) make output rows
+ * independent, so rank r computes a contiguous row slice of every weight. The
+ * GEMV's epilogue writes each finished row into every rank's gather buffer
+ * over NVLink (peer memory opened with CUDA IPC, plain stores), and the last
+ * CTA of the launch signals the peers. The next tensor-parallel launch on a
+ * rank (or wllm_tp_wait) waits, bounded, until every peer has signalled the
+ * previous one: no collective library call on the data path. */
+#define WLLM_MAX_RANKS 8
+#define WLLM_IPC_HANDLE_BYTES 64
+
+/* Peer-mappable device memory: its own cudaMalloc, zero-filled, with the
+ * 64-byte IPC handle another process on the node opens with wllm_ipc_open. */
+int32_t wllm_ipc_alloc(uint64_t size, void** out_ptr, void* out_handle);
+int32_t wllm_ipc_open(const void* handle, void** out_ptr);
+int32_t wllm_ipc_close(void* ptr);  /* a pointer from wllm_ipc_open */
+int32_t wllm_ipc_free(void* ptr);   /* a pointer from wllm_ipc_alloc */
+
+/* The ranks of one node. sig[r] is rank r's signal array (WLLM_MAX_RANKS
+ * uint32, wllm_ipc_alloc'd on rank r and opened on the others); state is this
+ * rank's private counter block (4 uint32, zeroed). Every rank issues the same
+ * sequence of tensor-parallel launches. */
+typedef struct wllm_tp_group {
+    int32_t world, rank;
+    uint32_t* sig[WLLM_MAX_RANKS];
+    uint32_t* state;
+} wllm_tp_group;
+
+/* Where every rank keeps this rank's rows of one op: y_rank[r] is rank r's
+ * copy (y_rank[rank] is the op's own y). */
+typedef struct wllm_tp_outputs {
+    float* y_rank[WLLM_MAX_RANKS];
+} wllm_tp_outputs;
+
+/* wllm_mul_mat_batch for one rank's row slices, each output row also written
+ * to y_rank[r] of every other rank r. Only the streaming decode shapes
+ * (N <= 2, K % 256 == 0, 16-byte aligned activations) are accepted;
+ * anything else returns WLLM_STATUS_FAILED. */
+int32_t wllm_mul_mat_batch_tp(const wllm_mulmat_args* ops, const wllm_tp_outputs* outs, int32_t n_ops,
+                              const wllm_tp_group* group, void* stream);
+
+/* Enqueues a wait (bounded) until every peer has signalled the rank's last
+ * tensor-parallel launch, so its gathered outputs are complete. A time-out
+ * is reported by the next wllm_sync. */
+int32_t wllm_tp_wait(const wllm_tp_group* group, void* stream);
+
 /* The library's CUDA stream (a cudaStream_t), so a host can order its own
  * work (collectives, events) with the library's. */
 int32_t wllm_get_stream(void** out_stream);

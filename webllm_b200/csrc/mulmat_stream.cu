@@ -93,6 +93,15 @@ struct SOp {
     int32_t nseg;
     int32_t wbox;                 // bytes per row in a stage (copy window, == 16 mod 32)
     int32_t use_tma;              // 1: one 2D tensor copy per stage; 0: one bulk copy per row
+    float* y_peer[kMaxRanks];     // row-sharded launch: this op's rows on rank r (own rank unused)
+};
+
+// Row-sharded launch: sig[r] is rank r's signal array, state this rank's
+// counters ([0] CTAs done with the launch, [1] launches done).
+struct TpSig {
+    int32_t world, rank;  // world 1: not row-sharded
+    uint32_t* sig[kMaxRanks];
+    uint32_t* state;
 };
 
 struct SList {
@@ -103,6 +112,7 @@ struct SList {
     int32_t stage_bytes;  // 16 rows x the largest wbox
     int32_t x_bytes;      // shared-memory bytes reserved for the activation image
     int32_t all_tma;      // every op is copied with its tensor map
+    TpSig tp;             // world > 1: every output row also goes to the other ranks
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -504,6 +514,7 @@ struct OpInfo {
     int64_t w_nb1, x_nb1, y_nb1;
     int32_t type, M, K, N;
     int32_t unit_begin, seg_blocks, nseg, wbox, use_tma;
+    float* y_peer[kMaxRanks];
 };
 
 // The current op's fields, held in registers by the consumer warps (the
@@ -637,6 +648,8 @@ struct UnitMeta {
     int64_t y_nb1;   // bytes between vectors
     int32_t rows;    // valid rows (<= 16)
     int32_t n;       // vectors
+    int32_t op;      // the unit's op (for the other ranks' copies)
+    int32_t r0;      // the unit's first row
 };
 
 // Stage-ring position of the consumer warps.
@@ -832,6 +845,37 @@ __device__ __forceinline__ void q6k_unit(const OpRegs& op, const Q6Lane& q, Ring
     }
 }
 
+// One thread: every other rank's count of this rank's sync points goes up by
+// one with a system-scope release reduction, which orders before it all that
+// this rank wrote earlier (all earlier kernels' row stores into other ranks'
+// memory, ordered before this thread by the stream or the dependency wait).
+__device__ void tp_signal_peers(uint32_t* const* sig, int world, int rank) {
+    for (int p = 0; p < world; ++p)
+        if (p != rank) asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(sig[p] + rank) : "memory");
+}
+
+// Bounded wait (one thread) until every other rank has signalled `seq`
+// sync points to this rank; false (and an error code) on time-out.
+__device__ bool tp_wait_peers(const uint32_t* const* sig, int world, int rank, uint32_t seq, volatile int* poisoned) {
+    for (int src = 0; src < world; ++src) {
+        if (src == rank) continue;
+        const uint32_t* f = sig[rank] + src;
+        uint32_t v;
+        uint32_t i = 0;
+        for (;; ++i) {
+            asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
+            if (static_cast<int32_t>(v - seq) >= 0) break;
+            if (i == kSpinLimit || (poisoned && *poisoned)) {
+                if (poisoned) *poisoned = 1;
+                atomicOr(&g_stream_error, 4u);
+                return false;
+            }
+            __nanosleep(64);
+        }
+    }
+    return true;
+}
+
 template <int NT>
 __global__ void __launch_bounds__(kThreads, 1) stream_gemv_kernel(const __grid_constant__ SList L) {
     extern __shared__ __align__(128) uint8_t smem[];
@@ -879,6 +923,7 @@ __global__ void __launch_bounds__(kThreads, 1) stream_gemv_kernel(const __grid_c
         d.nseg = o.nseg;
         d.wbox = o.wbox;
         d.use_tma = o.use_tma;
+        for (int r = 0; r < kMaxRanks; ++r) d.y_peer[r] = o.y_peer[r];
         if (o.use_tma) asm volatile("prefetch.tensormap [%0];" ::"l"(&o.tmap) : "memory");
     }
     if (threadIdx.x == 0) {
@@ -990,6 +1035,18 @@ __global__ void __launch_bounds__(kThreads, 1) stream_gemv_kernel(const __grid_c
     asm volatile("griddepcontrol.wait;" ::: "memory");
     const int ct = threadIdx.x - 32;  // 0 .. 32 kCW - 1
     const int cw = warp - 1;          // 0 .. kCW - 1
+    // Row-sharded: this launch is sync point `tp_seq` of the rank. CTA 0
+    // tells the other ranks that the rank's earlier launches are complete (the
+    // dependency wait above covers them), and every CTA waits until all ranks
+    // have reached this sync point, so their earlier rows have landed here
+    // before any activation is read (the first staging's barrier makes every
+    // consumer thread wait for thread 0).
+    uint32_t tp_seq = 0;
+    if (L.tp.world > 1 && ct == 0) {
+        tp_seq = *reinterpret_cast<volatile uint32_t*>(L.tp.state + 1);
+        if (blockIdx.x == 0) tp_signal_peers(L.tp.sig, L.tp.world, L.tp.rank);
+        tp_wait_peers(L.tp.sig, L.tp.world, L.tp.rank, tp_seq + 1u, poisoned);
+    }
     Ring R{stages, full, empty, poisoned, SB, S, 0, 0u, 0u};
     const int n_ops = T.n_ops, total = T.total_units;
     int staged = -1, oi = -1, useq = 0;
@@ -1011,7 +1068,15 @@ __global__ void __launch_bounds__(kThreads, 1) stream_gemv_kernel(const __grid_c
             float v = 0.f;
 #pragma unroll
             for (int w2 = 0; w2 < kCW; ++w2) v += vb[w2 * kRows * NT];
-            if (r < m.rows) *reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(m.y) + n * m.y_nb1 + 4 * r) = v;
+            if (r < m.rows) {
+                *reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(m.y) + n * m.y_nb1 + 4 * r) = v;
+                // row-sharded: the same row into every other rank's copy (NVLink stores)
+                for (int p = 0; p < L.tp.world; ++p) {
+                    float* yp = T.op[m.op].y_peer[p];
+                    if (p != L.tp.rank && yp)
+                        *reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(yp) + n * m.y_nb1 + 4LL * (m.r0 + r)) = v;
+                }
+            }
         }
     };
     for (int u = blockIdx.x; u < total; u += gridDim.x, ++useq) {
@@ -1124,6 +1189,8 @@ __global__ void __launch_bounds__(kThreads, 1) stream_gemv_kernel(const __grid_c
             m.y_nb1 = op.y_nb1;
             m.rows = min(kRows, op.M - r0);
             m.n = N;
+            m.op = oi;
+            m.r0 = r0;
             umeta[uslot] = m;
         }
         __syncwarp();
@@ -1135,6 +1202,26 @@ __global__ void __launch_bounds__(kThreads, 1) stream_gemv_kernel(const __grid_c
     // the last kRedDelay units of the CTA
     for (int j = useq - kRedDelay; j < useq; ++j)
         if (j >= 0 && j % kCW == cw) reduce_unit(j);
+    if (L.tp.world > 1 && ct == 0) {
+        // Row-sharded: the last CTA to finish counts the sync point (every CTA
+        // read the count at its start, before this).
+        const unsigned prev = atomicAdd(L.tp.state, 1u);
+        if (prev == gridDim.x - 1) {
+            L.tp.state[0] = 0u;
+            L.tp.state[1] = tp_seq + 1u;
+        }
+    }
+}
+
+// A sync point on its own: the rank's earlier row-sharded launches are
+// complete (stream order); after it every rank's rows are in place here.
+__global__ void tp_wait_kernel(const __grid_constant__ TpSig t) {
+    if (threadIdx.x == 0) {
+        const uint32_t seq = t.state[1];
+        tp_signal_peers(t.sig, t.world, t.rank);
+        tp_wait_peers(t.sig, t.world, t.rank, seq + 1u, nullptr);
+        t.state[1] = seq + 1u;
+    }
 }
 
 size_t smem_bytes(int stages, int stage_bytes, int x_bytes, int nt) {
@@ -1199,9 +1286,18 @@ bool stream_supported(const MulMatOp* ops, int n_ops) {
     return true;
 }
 
-int launch_stream(const MulMatOp* ops, int n_ops, cudaStream_t stream, int num_sms) {
+int launch_stream(const MulMatOp* ops, int n_ops, cudaStream_t stream, int num_sms, const TpLaunch* tp) {
     SList L{};
     L.n_ops = n_ops;
+    L.tp.world = 1;
+    if (tp) {
+        L.tp.world = tp->world;
+        L.tp.rank = tp->rank;
+        for (int r = 0; r < kMaxRanks; ++r) L.tp.sig[r] = tp->sig[r];
+        L.tp.state = tp->state;
+        for (int i = 0; i < n_ops; ++i)
+            for (int r = 0; r < kMaxRanks; ++r) L.op[i].y_peer[r] = r < tp->world ? tp->y_peer[i][r] : nullptr;
+    }
     int units = 0, max_n = 1, x_bytes = 0, wmax = 0;
     for (int i = 0; i < n_ops; ++i) {
         const MulMatOp& o = ops[i];
@@ -1281,6 +1377,17 @@ int launch_stream(const MulMatOp* ops, int n_ops, cudaStream_t stream, int num_s
     }
     e = ti == 0 ? cudaLaunchKernelEx(&cfg, stream_gemv_kernel<1>, L) : cudaLaunchKernelEx(&cfg, stream_gemv_kernel<2>, L);
     if (e == cudaSuccess) e = cudaGetLastError();
+    return e == cudaSuccess ? 1 : -static_cast<int>(e);
+}
+
+int launch_tp_wait(const TpLaunch& tp, cudaStream_t stream) {
+    TpSig t{};
+    t.world = tp.world;
+    t.rank = tp.rank;
+    for (int r = 0; r < kMaxRanks; ++r) t.sig[r] = tp.sig[r];
+    t.state = tp.state;
+    tp_wait_kernel<<<1, 32, 0, stream>>>(t);
+    const cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? 1 : -static_cast<int>(e);
 }
 

@@ -18,6 +18,7 @@
 #include <new>
 #include <string>
 #include <unordered_map>
+#include <unordered_set>
 #include <vector>
 
 #include "../../include/wllm_mulmat.h"
@@ -60,6 +61,8 @@ struct State {
     std::unordered_map<int32_t, cudaGraphExec_t> graphs;
     std::unordered_map<int32_t, uint64_t> graph_kernels;
     int32_t next_graph = 1;
+    std::unordered_set<void*> ipc_owned;   // wllm_ipc_alloc
+    std::unordered_set<void*> ipc_opened;  // wllm_ipc_open
 };
 
 State& S() {
@@ -135,6 +138,10 @@ int32_t release_all(State& s) {
     for (auto& kv : s.graphs) cudaGraphExecDestroy(kv.second);
     s.graphs.clear();
     s.graph_kernels.clear();
+    for (void* p : s.ipc_opened) cudaIpcCloseMemHandle(p);
+    s.ipc_opened.clear();
+    for (void* p : s.ipc_owned) cudaFree(p);
+    s.ipc_owned.clear();
     s.counters.bytes_live = 0;
     s.counters.bytes_reserved = 0;
     return WLLM_STATUS_OK;
@@ -329,6 +336,55 @@ int32_t launch(State& s, const MulMatOp* ops, int n, cudaStream_t stream) {
     if (rc < 0) return cuda_fail(s, static_cast<cudaError_t>(-rc), "MUL_MAT launch");
     if (s.capturing) s.captured_kernels += static_cast<uint64_t>(rc);
     else s.counters.kernels_launched += static_cast<uint64_t>(rc);
+    return WLLM_STATUS_OK;
+}
+
+// Converts and checks device-pointer ops; nonzero status (already reported)
+// on failure.
+int32_t ops_from_args(State& s, const char* what, const wllm_mulmat_args* ops, int32_t n_ops, MulMatOp* m) {
+    if (!ops || n_ops < 1 || n_ops > wllm::kMaxOpsPerLaunch)
+        return fail(s, "%s: n_ops=%d outside 1..%d", what, n_ops, wllm::kMaxOpsPerLaunch);
+    for (int i = 0; i < n_ops; ++i) {
+        const wllm_mulmat_args& a = ops[i];
+        if (a.src0_type != WLLM_TYPE_Q4_K && a.src0_type != WLLM_TYPE_Q6_K && a.src0_type != WLLM_TYPE_Q8_0)
+            return WLLM_STATUS_NOT_IMPLEMENTED;
+        if (!a.w || !a.x || !a.y) return fail(s, "%s: null pointer in op %d", what, i);
+        MulMatOp& o = m[i];
+        o = MulMatOp{};
+        o.w = static_cast<const uint8_t*>(a.w);
+        o.x = a.x;
+        o.y = a.y;
+        o.w_nb1 = a.w_row_bytes;
+        o.w_nb2 = o.w_nb3 = a.w_row_bytes * a.M;
+        o.x_nb1 = 4 * a.x_stride;
+        o.x_nb2 = o.x_nb3 = 4 * a.x_stride * a.N;
+        o.y_nb1 = 4 * a.y_stride;
+        o.y_nb2 = o.y_nb3 = 4 * a.y_stride * a.N;
+        o.type = a.src0_type;
+        o.M = a.M;
+        o.K = a.K;
+        o.N = a.N;
+        o.ne2 = o.ne3 = 1;
+        o.r2 = o.r3 = 1;
+        if (const char* why = wllm::check_mulmat_op(o)) return fail(s, "%s op %d: %s", what, i, why);
+    }
+    return WLLM_STATUS_OK;
+}
+
+// Checks a row-sharded group and copies it into the kernel's form.
+int32_t tp_from_group(State& s, const char* what, const wllm_tp_group* g, wllm::TpLaunch* t) {
+    if (!g) return fail(s, "%s: null group", what);
+    if (g->world < 2 || g->world > WLLM_MAX_RANKS || g->rank < 0 || g->rank >= g->world)
+        return fail(s, "%s: world=%d rank=%d (world must be 2..%d)", what, g->world, g->rank, WLLM_MAX_RANKS);
+    if (!g->state) return fail(s, "%s: null state", what);
+    *t = wllm::TpLaunch{};
+    t->world = g->world;
+    t->rank = g->rank;
+    t->state = g->state;
+    for (int r = 0; r < g->world; ++r) {
+        if (!g->sig[r]) return fail(s, "%s: null signal array of rank %d", what, r);
+        t->sig[r] = g->sig[r];
+    }
     return WLLM_STATUS_OK;
 }
 
@@ -771,34 +827,101 @@ int32_t wllm_mul_mat_batch(const wllm_mulmat_args* ops, int32_t n_ops, void* str
     State& s = S();
     std::lock_guard<std::mutex> g(s.mu);
     if (!ensure_init(s)) return WLLM_STATUS_FAILED;
-    if (!ops || n_ops < 1 || n_ops > wllm::kMaxOpsPerLaunch)
-        return fail(s, "wllm_mul_mat_batch: n_ops=%d outside 1..%d", n_ops, wllm::kMaxOpsPerLaunch);
     MulMatOp m[wllm::kMaxOpsPerLaunch];
-    for (int i = 0; i < n_ops; ++i) {
-        const wllm_mulmat_args& a = ops[i];
-        if (a.src0_type != WLLM_TYPE_Q4_K && a.src0_type != WLLM_TYPE_Q6_K && a.src0_type != WLLM_TYPE_Q8_0)
-            return WLLM_STATUS_NOT_IMPLEMENTED;
-        if (!a.w || !a.x || !a.y) return fail(s, "wllm_mul_mat_batch: null pointer in op %d", i);
-        MulMatOp& o = m[i];
-        o = MulMatOp{};
-        o.w = static_cast<const uint8_t*>(a.w);
-        o.x = a.x;
-        o.y = a.y;
-        o.w_nb1 = a.w_row_bytes;
-        o.w_nb2 = o.w_nb3 = a.w_row_bytes * a.M;
-        o.x_nb1 = 4 * a.x_stride;
-        o.x_nb2 = o.x_nb3 = 4 * a.x_stride * a.N;
-        o.y_nb1 = 4 * a.y_stride;
-        o.y_nb2 = o.y_nb3 = 4 * a.y_stride * a.N;
-        o.type = a.src0_type;
-        o.M = a.M;
-        o.K = a.K;
-        o.N = a.N;
-        o.ne2 = o.ne3 = 1;
-        o.r2 = o.r3 = 1;
-        if (const char* why = wllm::check_mulmat_op(o)) return fail(s, "wllm_mul_mat_batch op %d: %s", i, why);
-    }
+    if (const int32_t rc = ops_from_args(s, "wllm_mul_mat_batch", ops, n_ops, m)) return rc;
     return launch(s, m, n_ops, stream ? static_cast<cudaStream_t>(stream) : s.stream);
+}
+
+int32_t wllm_ipc_alloc(uint64_t size, void** out_ptr, void* out_handle) {
+    State& s = S();
+    std::lock_guard<std::mutex> g(s.mu);
+    if (!ensure_init(s)) return WLLM_STATUS_FAILED;
+    if (!out_ptr || !out_handle || size == 0) return fail(s, "wllm_ipc_alloc: null out or zero size");
+    if (s.capturing) return fail(s, "wllm_ipc_alloc: not while recording a graph");
+    void* p = nullptr;
+    cudaError_t e = cudaMalloc(&p, size);
+    if (e != cudaSuccess) return cuda_fail(s, e, "wllm_ipc_alloc cudaMalloc");
+    e = cudaMemset(p, 0, size);
+    cudaIpcMemHandle_t h;
+    if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, p);
+    if (e != cudaSuccess) {
+        cudaFree(p);
+        return cuda_fail(s, e, "wllm_ipc_alloc");
+    }
+    static_assert(sizeof(cudaIpcMemHandle_t) == WLLM_IPC_HANDLE_BYTES, "IPC handle size");
+    std::memcpy(out_handle, &h, sizeof(h));
+    s.ipc_owned.insert(p);
+    *out_ptr = p;
+    return WLLM_STATUS_OK;
+}
+
+int32_t wllm_ipc_open(const void* handle, void** out_ptr) {
+    State& s = S();
+    std::lock_guard<std::mutex> g(s.mu);
+    if (!ensure_init(s)) return WLLM_STATUS_FAILED;
+    if (!handle || !out_ptr) return fail(s, "wllm_ipc_open: null argument");
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, handle, sizeof(h));
+    void* p = nullptr;
+    const cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) return cuda_fail(s, e, "wllm_ipc_open");
+    s.ipc_opened.insert(p);
+    *out_ptr = p;
+    return WLLM_STATUS_OK;
+}
+
+int32_t wllm_ipc_close(void* ptr) {
+    State& s = S();
+    std::lock_guard<std::mutex> g(s.mu);
+    if (!s.ipc_opened.erase(ptr)) return fail(s, "wllm_ipc_close: %p was not opened here", ptr);
+    const cudaError_t e = cudaIpcCloseMemHandle(ptr);
+    return e == cudaSuccess ? WLLM_STATUS_OK : cuda_fail(s, e, "wllm_ipc_close");
+}
+
+int32_t wllm_ipc_free(void* ptr) {
+    State& s = S();
+    std::lock_guard<std::mutex> g(s.mu);
+    if (!s.ipc_owned.erase(ptr)) return fail(s, "wllm_ipc_free: %p was not allocated here", ptr);
+    const cudaError_t e = cudaFree(ptr);
+    return e == cudaSuccess ? WLLM_STATUS_OK : cuda_fail(s, e, "wllm_ipc_free");
+}
+
+int32_t wllm_mul_mat_batch_tp(const wllm_mulmat_args* ops, const wllm_tp_outputs* outs, int32_t n_ops,
+                              const wllm_tp_group* group, void* stream) {
+    State& s = S();
+    std::lock_guard<std::mutex> g(s.mu);
+    if (!ensure_init(s)) return WLLM_STATUS_FAILED;
+    const char* what = "wllm_mul_mat_batch_tp";
+    MulMatOp m[wllm::kMaxOpsPerLaunch];
+    if (const int32_t rc = ops_from_args(s, what, ops, n_ops, m)) return rc;
+    wllm::TpLaunch t;
+    if (const int32_t rc = tp_from_group(s, what, group, &t)) return rc;
+    if (!outs) return fail(s, "%s: null outputs", what);
+    for (int i = 0; i < n_ops; ++i)
+        for (int r = 0; r < t.world; ++r) {
+            if (r != t.rank && !outs[i].y_rank[r]) return fail(s, "%s: op %d has no output on rank %d", what, i, r);
+            t.y_peer[i][r] = r == t.rank ? nullptr : outs[i].y_rank[r];
+        }
+    if (!wllm::stream_supported(m, n_ops))
+        return fail(s, "%s: only decode shapes (N <= 2, K %% 256 == 0, 16-byte aligned x) are row-sharded", what);
+    const int rc = wllm::launch_stream(m, n_ops, stream ? static_cast<cudaStream_t>(stream) : s.stream, s.num_sms, &t);
+    if (rc < 0) return cuda_fail(s, static_cast<cudaError_t>(-rc), "wllm_mul_mat_batch_tp launch");
+    if (s.capturing) s.captured_kernels += static_cast<uint64_t>(rc);
+    else s.counters.kernels_launched += static_cast<uint64_t>(rc);
+    return WLLM_STATUS_OK;
+}
+
+int32_t wllm_tp_wait(const wllm_tp_group* group, void* stream) {
+    State& s = S();
+    std::lock_guard<std::mutex> g(s.mu);
+    if (!ensure_init(s)) return WLLM_STATUS_FAILED;
+    wllm::TpLaunch t;
+    if (const int32_t rc = tp_from_group(s, "wllm_tp_wait", group, &t)) return rc;
+    const int rc = wllm::launch_tp_wait(t, stream ? static_cast<cudaStream_t>(stream) : s.stream);
+    if (rc < 0) return cuda_fail(s, static_cast<cudaError_t>(-rc), "wllm_tp_wait launch");
+    if (s.capturing) s.captured_kernels += static_cast<uint64_t>(rc);
+    else s.counters.kernels_launched += static_cast<uint64_t>(rc);
+    return WLLM_STATUS_OK;
 }
 
 int32_t wllm_get_stream(void** out_stream) {

@@ -62,8 +62,21 @@ int launch_mulmat_general(const MulMatOp* ops, int n_ops, cudaStream_t stream);
 
 // Streaming decode kernel (mulmat_stream.cu): ne2 = ne3 = 1, N <= 2,
 // K % 256 == 0, K <= 16384, 16-byte aligned activations (and Q4_K rows).
+// Row-sharded launch: where the other ranks keep this rank's output rows and
+// the signal arrays (see wllm_mul_mat_batch_tp in wllm_mulmat.h).
+constexpr int kMaxRanks = 8;
+struct TpLaunch {
+    int32_t world, rank;
+    uint32_t* sig[kMaxRanks];                     // rank r's signal array
+    uint32_t* state;                              // this rank's counters: [0] CTAs done, [1] launches done
+    float* y_peer[kMaxOpsPerLaunch][kMaxRanks];  // op i's rows on rank r (own rank unused)
+};
+
 bool stream_supported(const MulMatOp* ops, int n_ops);
-int launch_stream(const MulMatOp* ops, int n_ops, cudaStream_t stream, int num_sms);
+int launch_stream(const MulMatOp* ops, int n_ops, cudaStream_t stream, int num_sms, const TpLaunch* tp = nullptr);
+// One-thread kernel that waits (bounded) for every peer's signal of the
+// rank's last row-sharded launch.
+int launch_tp_wait(const TpLaunch& tp, cudaStream_t stream);
 // Error code recorded by a bounded wait that timed out (0 = none); clears it.
 unsigned read_and_clear_stream_error();
 

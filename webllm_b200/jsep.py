@@ -57,7 +57,11 @@ EXPORTED_SYMBOLS = (
     "wllm_buffer_device_ptr", "wllm_mul_mat", "wllm_mul_mat_batch", "wllm_get_stream",
     "wllm_graph_begin", "wllm_graph_end", "wllm_graph_launch", "wllm_graph_destroy",
     "wllm_dequantize", "wllm_version", "wllm_mul_mat_prefill_static",
+    "wllm_ipc_alloc", "wllm_ipc_open", "wllm_ipc_close", "wllm_ipc_free", "wllm_mul_mat_batch_tp", "wllm_tp_wait",
 )
+
+MAX_RANKS = 8
+IPC_HANDLE_BYTES = 64
 
 
 class MulMatArgs(ctypes.Structure):
@@ -66,6 +70,17 @@ class MulMatArgs(ctypes.Structure):
                 ("N", ctypes.c_int32), ("w", ctypes.c_void_p), ("w_row_bytes", ctypes.c_int64),
                 ("x", ctypes.c_void_p), ("x_stride", ctypes.c_int64), ("y", ctypes.c_void_p),
                 ("y_stride", ctypes.c_int64)]
+
+
+class TpGroup(ctypes.Structure):
+    """wllm_tp_group (include/wllm_mulmat.h)."""
+    _fields_ = [("world", ctypes.c_int32), ("rank", ctypes.c_int32),
+                ("sig", ctypes.c_void_p * MAX_RANKS), ("state", ctypes.c_void_p)]
+
+
+class TpOutputs(ctypes.Structure):
+    """wllm_tp_outputs (include/wllm_mulmat.h)."""
+    _fields_ = [("y_rank", ctypes.c_void_p * MAX_RANKS)]
 
 
 class WllmCounters(ctypes.Structure):
@@ -109,6 +124,12 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
         "wllm_mul_mat_prefill_static": ([i32, vp, i64, vp, i64, vp, i64, i32, i32, i32, vp], i32),
         "wllm_dequantize": ([i32, vp, vp, i64, vp], i32),
         "wllm_mul_mat_batch": ([P(MulMatArgs), i32, vp], i32),
+        "wllm_ipc_alloc": ([u64, P(vp), vp], i32),
+        "wllm_ipc_open": ([vp, P(vp)], i32),
+        "wllm_ipc_close": ([vp], i32),
+        "wllm_ipc_free": ([vp], i32),
+        "wllm_mul_mat_batch_tp": ([P(MulMatArgs), P(TpOutputs), i32, P(TpGroup), vp], i32),
+        "wllm_tp_wait": ([P(TpGroup), vp], i32),
         "wllm_get_stream": ([P(vp)], i32),
         "wllm_graph_begin": ([], i32),
         "wllm_graph_end": ([P(i32)], i32),
@@ -399,6 +420,56 @@ def mul_mat_batch(ops: Sequence[MulMatArgs], stream: int = 0) -> int:
     L = load_library()
     arr = (MulMatArgs * len(ops))(*ops)
     return _check(L.wllm_mul_mat_batch(arr, len(ops), int(stream) or None), "wllm_mul_mat_batch")
+
+
+def ipc_alloc(size: int) -> tuple[int, bytes]:
+    """Peer-mappable zeroed device memory: (device pointer, 64-byte IPC handle)."""
+    p = ctypes.c_void_p(0)
+    h = ctypes.create_string_buffer(IPC_HANDLE_BYTES)
+    _check(load_library().wllm_ipc_alloc(int(size), ctypes.byref(p), h), "wllm_ipc_alloc")
+    return int(p.value), h.raw
+
+
+def ipc_open(handle: bytes) -> int:
+    """Maps another process's wllm_ipc_alloc memory; returns its device pointer here."""
+    p = ctypes.c_void_p(0)
+    buf = ctypes.create_string_buffer(bytes(handle), IPC_HANDLE_BYTES)
+    _check(load_library().wllm_ipc_open(buf, ctypes.byref(p)), "wllm_ipc_open")
+    return int(p.value)
+
+
+def ipc_close(ptr: int) -> None:
+    _check(load_library().wllm_ipc_close(int(ptr)), "wllm_ipc_close")
+
+
+def ipc_free(ptr: int) -> None:
+    _check(load_library().wllm_ipc_free(int(ptr)), "wllm_ipc_free")
+
+
+def tp_group(world: int, rank: int, sig_ptrs: Sequence[int], state_ptr: int) -> TpGroup:
+    g = TpGroup()
+    g.world, g.rank = int(world), int(rank)
+    for r, p in enumerate(sig_ptrs):
+        g.sig[r] = int(p)
+    g.state = int(state_ptr)
+    return g
+
+
+def mul_mat_batch_tp(ops: Sequence[MulMatArgs], outs: Sequence[Sequence[int]], group: TpGroup, stream: int = 0) -> int:
+    """Row-sharded MUL_MATs: op i's rows also go to outs[i][r] on every other rank r
+    (wllm_mul_mat_batch_tp)."""
+    arr = (MulMatArgs * len(ops))(*ops)
+    oa = (TpOutputs * len(ops))()
+    for i, ys in enumerate(outs):
+        for r, p in enumerate(ys):
+            oa[i].y_rank[r] = int(p)
+    return _check(load_library().wllm_mul_mat_batch_tp(arr, oa, len(ops), ctypes.byref(group), int(stream) or None),
+                  "wllm_mul_mat_batch_tp")
+
+
+def tp_wait(group: TpGroup, stream: int = 0) -> int:
+    """Waits (on the stream, bounded) for every peer's rows of the last row-sharded launch."""
+    return _check(load_library().wllm_tp_wait(ctypes.byref(group), int(stream) or None), "wllm_tp_wait")
 
 
 def library_stream() -> int:
