@@ -31,6 +31,11 @@
 // The activations are converted to f16 by a pre-pass (x_to_f16_kernel) into
 // library workspace: N x K x 2 bytes, read by every row tile from L2.
 //
+// Split K: grids far below two CTAs per SM (few row tiles) or with long K run
+// S splits of the K blocks per tile (grid z). Each split stores its f32 tile
+// in workspace; the tile's last split (a per-tile counter) sums the S tiles in
+// split order, so results do not depend on timing.
+//
 // Every mbarrier wait is bounded; on timeout the CTA records an error code
 // (read by wllm_sync), stops issuing work, and still releases its TMEM.
 #include <cuda.h>
@@ -68,6 +73,12 @@ struct PrefillArgs {
     float* y;
     int64_t y_nb1;      // bytes between output vectors
     int32_t M, K, N;
+    // split-K (splits > 1): CTA z of a tile covers K blocks [z kb_split, (z+1) kb_split),
+    // writes its f32 tile to partial[tile][z][col][row], and the tile's last CTA
+    // (counted in counters[tile], zero at launch) sums the splits in order
+    int32_t splits, kb_split;
+    float* partial;
+    unsigned* counters;
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -178,7 +189,8 @@ __global__ void __launch_bounds__(kThreads, 2) prefill_q4k_kernel(const __grid_c
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int m0 = blockIdx.x * kTileM, n0 = blockIdx.y * kTileN;
-    const int nblk = P.K / 256, nchunk = nblk * 4;
+    const int kb0 = blockIdx.z * P.kb_split;                          // first K block of this split
+    const int nblk = min(P.K / 256 - kb0, P.kb_split), nchunk = nblk * 4;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; ++s) {
@@ -216,12 +228,12 @@ __global__ void __launch_bounds__(kThreads, 2) prefill_q4k_kernel(const __grid_c
                     const int r = kb % kRawSlots;
                     if (kb >= kRawSlots && !mbar_wait(&raw_free[r], ((kb / kRawSlots) - 1) & 1, 1u, poisoned)) break;
                     mbar_expect_tx(&raw_full[r], kRawBytes);
-                    tma_2d(raw + r * kRawBytes, &P.wmap, kb * 18, m0, &raw_full[r]);
+                    tma_2d(raw + r * kRawBytes, &P.wmap, (kb0 + kb) * 18, m0, &raw_full[r]);
                 }
                 const int s = q % kStages;
                 if (q >= kStages && !mbar_wait(&st_free[s], ((q / kStages) - 1) & 1, 1u, poisoned)) break;
                 mbar_expect_tx(&b_full[s], kBBytes);
-                tma_2d(B + s * kBBytes, &P.xmap, q * kChunkK, n0, &b_full[s]);
+                tma_2d(B + s * kBBytes, &P.xmap, (4 * kb0 + q) * kChunkK, n0, &b_full[s]);
             }
         }
     } else if (warp == 1) {
@@ -309,20 +321,71 @@ __global__ void __launch_bounds__(kThreads, 2) prefill_q4k_kernel(const __grid_c
         // ---------------- epilogue ----------------
         const bool ok = mbar_wait(acc_full, 0, 4u, poisoned);
         tc_fence_after();
+        const int col0 = (dw < 4) ? 0 : kTileN / 2;
+        const int tr = 32 * quarter + lane, row = m0 + tr;
+        const int tile = blockIdx.y * gridDim.x + blockIdx.x;
+        float* part = P.partial + (static_cast<int64_t>(tile) * P.splits + blockIdx.z) * (kTileM * kTileN);
         if (ok) {
-            const int col0 = (dw < 4) ? 0 : kTileN / 2;
-            const int row = m0 + 32 * quarter + lane;
 #pragma unroll 1
             for (int cc = 0; cc < kTileN / 2; cc += 16) {
                 float v[16];
                 tmem_ld16(tmem + (static_cast<uint32_t>(32 * quarter) << 16) + static_cast<uint32_t>(col0 + cc), v);
-                if (row < P.M) {
+                if (P.splits > 1) {
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) part[(col0 + cc + i) * kTileM + tr] = v[i];  // [col][row]
+                } else if (row < P.M) {
 #pragma unroll
                     for (int i = 0; i < 16; ++i) {
                         const int n = n0 + col0 + cc + i;
                         if (n < P.N)
                             *reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(P.y) + n * P.y_nb1 + 4LL * row) = v[i];
                     }
+                }
+            }
+        }
+        if (P.splits > 1) {
+            // the tile's last split sums all of them in split order (deterministic)
+            __shared__ int last;
+            asm volatile("bar.sync 1, %0;" ::"n"(kDqWarps * 32) : "memory");
+            if (threadIdx.x == 64) {
+                __threadfence();  // this CTA's partial tile before the count
+                last = atomicAdd(P.counters + tile, 1u) == static_cast<unsigned>(P.splits - 1);
+                if (last) {
+                    P.counters[tile] = 0u;
+                    __threadfence();  // the other splits' partial tiles after the count
+                }
+            }
+            asm volatile("bar.sync 1, %0;" ::"n"(kDqWarps * 32) : "memory");
+            if (last) {
+                // thread t sums rows 4 (t % 32) .. +3 of columns t / 32 + 8 j (j < 16):
+                // 16 independent float4 loads per split in flight
+                const int t = threadIdx.x - 64, r4 = 4 * (t & 31), cb = t >> 5;
+                const float4* base =
+                    reinterpret_cast<const float4*>(P.partial + static_cast<int64_t>(tile) * P.splits * (kTileM * kTileN));
+                float4 acc[16];
+#pragma unroll
+                for (int j = 0; j < 16; ++j) acc[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+                for (int z = 0; z < P.splits; ++z) {
+                    float4 v[16];
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) v[j] = __ldcg(base + (z * kTileN + cb + 8 * j) * (kTileM / 4) + (r4 >> 2));
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        acc[j].x += v[j].x;
+                        acc[j].y += v[j].y;
+                        acc[j].z += v[j].z;
+                        acc[j].w += v[j].w;
+                    }
+                }
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                    const int n = n0 + cb + 8 * j, r = m0 + r4;
+                    if (n >= P.N) continue;
+                    float* yn = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(P.y) + n * P.y_nb1);
+                    const float a[4] = {acc[j].x, acc[j].y, acc[j].z, acc[j].w};
+#pragma unroll
+                    for (int i = 0; i < 4; ++i)
+                        if (r + i < P.M) yn[r + i] = a[i];
                 }
             }
         }
@@ -367,6 +430,37 @@ EncodeFn encoder() {
 
 constexpr size_t kSmemBytes = 1024 /* alignment */ + kStages * kBBytes + kRawSlots * kRawBytes +
                               8 * (3 * kStages + 2 * kRawSlots + 1) + 16;
+constexpr int kSlots = 2 * 148;  // CTAs resident at once (two per SM)
+constexpr int kMaxSplits = 8;
+
+// K splits per tile, only while the grid stays within one wave of resident
+// CTAs (a split grid past that adds partial-tile traffic without adding
+// parallelism): minimises the K blocks per CTA plus the final reduction
+// (about 0.65 K blocks' time per split summed).
+int plan_splits(const MulMatOp& o) {
+    const int tiles = ((o.M + kTileM - 1) / kTileM) * ((o.N + kTileN - 1) / kTileN);
+    const int nblk = o.K / 256;
+    int best = 1;
+    double best_cost = 1e30;
+    for (int S = 1; S <= kMaxSplits && S <= nblk && (S == 1 || tiles * S <= kSlots); ++S) {
+        const int kb = (nblk + S - 1) / S;
+        if (S > 1 && (nblk + kb - 1) / kb < S) continue;  // a split would be empty
+        const int waves = (tiles * S + kSlots - 1) / kSlots;
+        const double cost = static_cast<double>(waves) * kb + (S > 1 ? 0.65 * S : 0.0);
+        if (cost < best_cost - 1e-9) {
+            best_cost = cost;
+            best = S;
+        }
+    }
+    return best;
+}
+
+size_t x16_bytes(const MulMatOp& o) { return (static_cast<size_t>(o.N) * o.K * 2 + 255) & ~size_t(255); }
+size_t split_bytes(const MulMatOp& o, int splits) {
+    if (splits <= 1) return 0;
+    const size_t tiles = static_cast<size_t>((o.M + kTileM - 1) / kTileM) * ((o.N + kTileN - 1) / kTileN);
+    return tiles * splits * kTileM * kTileN * 4 + tiles * 4;
+}
 
 }  // namespace
 
@@ -380,12 +474,17 @@ bool prefill_supported(const MulMatOp& o) {
     return encoder() != nullptr;
 }
 
-size_t prefill_workspace_bytes(const MulMatOp& o) { return static_cast<size_t>(o.N) * o.K * 2 + 256; }
+size_t prefill_workspace_bytes(const MulMatOp& o) { return x16_bytes(o) + split_bytes(o, plan_splits(o)) + 256; }
+size_t prefill_min_workspace_bytes(const MulMatOp& o) { return x16_bytes(o) + 256; }
 
 int launch_prefill(const MulMatOp& o, void* workspace, size_t workspace_bytes, cudaStream_t stream) {
     if (!prefill_supported(o)) return -static_cast<int>(cudaErrorInvalidValue);
-    if (!workspace || workspace_bytes < prefill_workspace_bytes(o) || (reinterpret_cast<uintptr_t>(workspace) & 255))
+    if (!workspace || workspace_bytes < prefill_min_workspace_bytes(o) || (reinterpret_cast<uintptr_t>(workspace) & 255))
         return -static_cast<int>(cudaErrorInvalidValue);
+    // split K when the workspace holds the partial tiles (else one split)
+    int splits = plan_splits(o);
+    if (x16_bytes(o) + split_bytes(o, splits) > workspace_bytes) splits = 1;
+    const int nblk = o.K / 256, kb_split = (nblk + splits - 1) / splits;
     __half* x16 = static_cast<__half*>(workspace);
     {
         const int64_t total4 = static_cast<int64_t>(o.N) * (o.K / 4);
@@ -423,6 +522,16 @@ int launch_prefill(const MulMatOp& o, void* workspace, size_t workspace_bytes, c
     P.M = o.M;
     P.K = o.K;
     P.N = o.N;
+    P.splits = splits;
+    P.kb_split = kb_split;
+    int launched = 2;
+    if (splits > 1) {
+        const size_t tiles = static_cast<size_t>((o.M + kTileM - 1) / kTileM) * ((o.N + kTileN - 1) / kTileN);
+        P.partial = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + x16_bytes(o));
+        P.counters = reinterpret_cast<unsigned*>(P.partial + tiles * splits * kTileM * kTileN);
+        const cudaError_t e = cudaMemsetAsync(P.counters, 0, tiles * 4, stream);
+        if (e != cudaSuccess) return -static_cast<int>(e);
+    }
     static bool configured = false;
     if (!configured) {
         const cudaError_t e = cudaFuncSetAttribute(prefill_q4k_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -430,10 +539,10 @@ int launch_prefill(const MulMatOp& o, void* workspace, size_t workspace_bytes, c
         if (e != cudaSuccess) return -static_cast<int>(e);
         configured = true;
     }
-    const dim3 grid((o.M + kTileM - 1) / kTileM, (o.N + kTileN - 1) / kTileN);
+    const dim3 grid((o.M + kTileM - 1) / kTileM, (o.N + kTileN - 1) / kTileN, splits);
     prefill_q4k_kernel<<<grid, kThreads, kSmemBytes, stream>>>(P);
     const cudaError_t e = cudaGetLastError();
-    return e == cudaSuccess ? 2 : -static_cast<int>(e);
+    return e == cudaSuccess ? launched : -static_cast<int>(e);
 }
 
 // Fixed device workspace for wllm_mul_mat_prefill_static: the f16 copy of the

@@ -793,7 +793,7 @@ int32_t wllm_mul_mat_prefill_static(int32_t src0_type, const void* w, int64_t w_
                     "wllm_mul_mat_prefill_static: only the prefill path (Q4_K, N >= %d, 16-byte aligned rows and "
                     "activations) is available here",
                     wllm::kPrefillMinN);
-    const size_t need = wllm::prefill_workspace_bytes(m);
+    const size_t need = wllm::prefill_min_workspace_bytes(m);
     if (need > wllm::kPrefillStaticWorkspaceBytes)
         return fail(s, "wllm_mul_mat_prefill_static: N*K = %lld needs %llu workspace bytes, above the fixed %llu",
                     static_cast<long long>(N) * K, static_cast<unsigned long long>(need),

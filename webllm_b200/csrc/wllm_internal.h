@@ -88,6 +88,8 @@ unsigned read_and_clear_stream_error();
 constexpr int kPrefillMinN = 65;
 bool prefill_supported(const MulMatOp& op);
 size_t prefill_workspace_bytes(const MulMatOp& op);
+// The least workspace launch_prefill accepts (no K split).
+size_t prefill_min_workspace_bytes(const MulMatOp& op);
 int launch_prefill(const MulMatOp& op, void* workspace, size_t workspace_bytes, cudaStream_t stream);
 unsigned read_and_clear_prefill_error();
 
