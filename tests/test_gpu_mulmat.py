@@ -127,6 +127,19 @@ def test_gemma2_q8_0_shapes(runtime, name, qtype, M, K, N):
     assert O.rel_error(got, O.mul_mat_f64(qtype, w, x)) <= GEMV_TOL
 
 
+@pytest.mark.parametrize("name,M,K,N", [("ffn_up", 9216, 2304, 8), ("ffn_up", 9216, 2304, 64),
+                                         ("ffn_down", 2304, 9216, 16), ("attn_proxy", 2304, 2304, 32),
+                                         ("attn_proxy", 2304, 2304, 65), ("ragged", 200, 768, 3)])
+def test_q8_0_batched_decode(runtime, name, M, K, N):
+    """Several sequences decoding together (Gemma-2-2B Q8_0 shapes, batch up to
+    64 and one past it): the integer tensor-core batched GEMM, split K included."""
+    rng = np.random.default_rng(zlib.crc32(name.encode()) + N)
+    w = synth.weights(rng, jsep.GGML_TYPE_Q8_0, M, K)
+    x = synth.activations(rng, N, K)
+    got = run_mul_mat(runtime, jsep.GGML_TYPE_Q8_0, w, x)
+    assert O.rel_error(got, O.mul_mat_f64(jsep.GGML_TYPE_Q8_0, w, x)) <= GEMV_TOL
+
+
 @pytest.mark.parametrize("qtype", [jsep.GGML_TYPE_Q4_K, jsep.GGML_TYPE_Q6_K, jsep.GGML_TYPE_Q8_0])
 def test_streaming_edge_shapes(runtime, qtype):
     """Shapes around the streaming kernel's unit/segment boundaries: rows not

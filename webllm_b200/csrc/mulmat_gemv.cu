@@ -243,24 +243,30 @@ const char* check_mulmat_op(const MulMatOp& op) {
 
 size_t mulmat_workspace_bytes(const MulMatOp* ops, int n_ops) {
     size_t need = 0;
-    for (int i = 0; i < n_ops; ++i)
-        if (prefill_supported(ops[i])) {
-            const size_t b = prefill_workspace_bytes(ops[i]);
-            need = b > need ? b : need;
-        }
+    for (int i = 0; i < n_ops; ++i) {
+        size_t b = 0;
+        if (prefill_supported(ops[i])) b = prefill_workspace_bytes(ops[i]);
+        else if (batched_supported(ops[i])) b = batched_workspace_bytes(ops[i]);
+        need = b > need ? b : need;
+    }
     return need;
 }
 
 int launch_mulmat(const MulMatOp* ops, int n_ops, cudaStream_t stream, int num_sms, void* workspace,
                   size_t workspace_bytes) {
     if (n_ops < 1 || n_ops > kMaxOpsPerLaunch) return -static_cast<int>(cudaErrorInvalidValue);
-    // prefill-sized ops run as tensor-core GEMMs, one launch each; the rest together
+    // prefill-sized ops (Q4_K) and small batches (Q8_0) run as tensor-core GEMMs, one
+    // launch each; the rest together
     int launched = 0;
     MulMatOp rest[kMaxOpsPerLaunch];
     int n_rest = 0;
     for (int i = 0; i < n_ops; ++i) {
         if (prefill_supported(ops[i]) && workspace && workspace_bytes >= prefill_workspace_bytes(ops[i])) {
             const int rc = launch_prefill(ops[i], workspace, workspace_bytes, stream);
+            if (rc < 0) return rc;
+            launched += rc;
+        } else if (batched_supported(ops[i]) && workspace && workspace_bytes >= batched_workspace_bytes(ops[i])) {
+            const int rc = launch_batched(ops[i], workspace, workspace_bytes, stream);
             if (rc < 0) return rc;
             launched += rc;
         } else {

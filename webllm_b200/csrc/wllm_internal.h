@@ -93,6 +93,14 @@ size_t prefill_min_workspace_bytes(const MulMatOp& op);
 int launch_prefill(const MulMatOp& op, void* workspace, size_t workspace_bytes, cudaStream_t stream);
 unsigned read_and_clear_prefill_error();
 
+// Small-batch GEMM (mulmat_batched.cu): Q8_0 weights with N >= 3 vectors on
+// integer tensor cores; workspace holds the activation limbs (and split-K
+// partial tiles). Returns the number of kernels launched (2) or a negative
+// cudaError_t.
+bool batched_supported(const MulMatOp& op);
+size_t batched_workspace_bytes(const MulMatOp& op);
+int launch_batched(const MulMatOp& op, void* workspace, size_t workspace_bytes, cudaStream_t stream);
+
 // Size of the prefill path's fixed device workspace (wllm_mul_mat_prefill_static):
 // ops with N * K * 2 + 256 bytes of f16 activations up to this size.
 constexpr size_t kPrefillStaticWorkspaceBytes = 16u << 20;
