@@ -60,6 +60,7 @@ def parse_args():
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU-baseline sample budget")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-prefill", action="store_true", help="skip the prefill GEMM measurement")
+    ap.add_argument("--no-batched", action="store_true", help="skip the batched Q8_0 decode measurement")
     return ap.parse_args()
 
 
@@ -141,6 +142,54 @@ class DevArray:
 
     def __init__(self, ptr: int, n: int):
         self.__cuda_array_interface__ = {"shape": (n,), "typestr": "<f4", "data": (ptr, False), "version": 3}
+
+
+def batched_measure(dev, reps: int = 10, warmup: int = 3):
+    """Gemma-2-2B ffn_up (Q8_0 9216x2304) with 1..64 sequences decoding
+    together: N = 1, 2 run the streaming GEMV, N >= 3 the integer tensor-core
+    batched GEMM. 24 distinct weight copies (541 MB, over 4x the L2) rotate
+    between launches so every launch streams its weights from HBM. Returns
+    the JSON object."""
+    import torch
+
+    from webllm_b200 import jsep, synth
+
+    name, t, M, K = synth.GEMMA2_2B_SHAPES[0]
+    copies = 24
+    stream_ptr = jsep.library_stream()
+    lib_stream = torch.cuda.ExternalStream(stream_ptr)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(zlib.crc32(name.encode()))
+    ws = [synth.weights_torch(gen, t, M, K, dev) for _ in range(copies)]
+    per = []
+    hbm, _ = measured_peaks()
+    for N in (1, 8, 16, 32, 64):
+        x = torch.randn(N, K, device=dev, generator=gen)
+        y = torch.empty(N, M, device=dev)
+        torch.cuda.synchronize()
+
+        def run(i):
+            w = ws[i % copies]
+            jsep.mul_mat_device(t, w.data_ptr(), w.shape[1], x.data_ptr(), K, y.data_ptr(), M, M, K, N, stream_ptr)
+
+        for i in range(warmup):
+            run(i)
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(lib_stream):
+            ev0.record()
+            for i in range(reps * copies):
+                run(i)
+            ev1.record()
+        ev1.synchronize()
+        us = ev0.elapsed_time(ev1) * 1e3 / (reps * copies)
+        nbytes = synth.algorithmic_bytes(t, M, K, N)
+        per.append({"n": N, "us": round(us, 2), "gbs": round(nbytes / (us * 1e-6) / 1e9, 1),
+                    "hbm_frac": round(nbytes / (us * 1e-6) / 1e9 / hbm, 4),
+                    "tflops": round(2.0 * M * K * N / (us * 1e-6) / 1e12, 2)})
+    del ws
+    return {"workload": f"gemma-2-2b {name} Q8_0 {M}x{K}, N sequences decoding together",
+            "unit": "GB/s", "per_n": per,
+            "note": "N <= 2: streaming GEMV; N >= 3: integer tensor-core batched GEMM (x pre-pass included)"}
 
 
 def layer_groups():
@@ -451,10 +500,12 @@ def run_b200(args, rank: int, world: int, local_rank: int):
     if world == 1:
         jsep_e2e = jsep_path_e2e(args, layers)
 
-    # ---- prefill GEMMs (tensor cores), rank 0 at one GPU
-    prefill = None
+    # ---- prefill GEMMs (tensor cores) and batched decode, rank 0 at one GPU
+    prefill = batched = None
     if world == 1 and not args.no_prefill:
         prefill = prefill_measure(dev)
+    if world == 1 and not args.no_batched:
+        batched = batched_measure(dev)
 
     total_bytes = step_bytes(layers)
     gbs = total_bytes / (dev_ms * 1e-3) / 1e9
@@ -492,6 +543,8 @@ def run_b200(args, rank: int, world: int, local_rank: int):
             line["e2e_c_abi"] = jsep_e2e
         if prefill is not None:
             line["prefill"] = prefill
+        if batched is not None:
+            line["batched"] = batched
     if world > 1:
         del graph
         torch.cuda.synchronize()
