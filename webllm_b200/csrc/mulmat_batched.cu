@@ -17,11 +17,11 @@
 // Tiling: a CTA (4 warps) computes 64 rows x NV vectors (NV = 8 .. 64); warp w
 // rows 16 w .. 16 w + 15. K is walked in chunks of 256 (8 blocks): the chunk's
 // raw rows (64 x 272 B) and limbs (NV x 2 x 256 B) go to shared memory with
-// cp.async, double-buffered. Q8_0 blocks are 34 bytes, so a block sits at any
+// cp.async, 2 to 4 chunks in flight. Q8_0 blocks are 34 bytes, so a block sits at any
 // even offset: A fragments come from aligned 32-bit loads and a funnel shift;
 // B fragments from ldmatrix.
 //
-// Split K: grids below two CTAs per SM split the chunks S ways (grid z); each
+// Split K: grids below one wave of two CTAs per SM split the chunks S ways (grid z); each
 // split stores its tile in workspace and the tile's last split sums the S
 // tiles in split order (deterministic).
 #include <cuda_fp16.h>
@@ -59,6 +59,12 @@ struct BatchedArgs {
 template <int NV>
 __host__ __device__ constexpr int stage_bytes() {
     return kRowsB * kWRow + NV * 2 * kXRow + NV * 4;
+}
+// Pipeline depth: enough bytes in flight per SM (two CTAs) to cover the HBM
+// latency, within the shared memory of two CTAs.
+template <int NV>
+__host__ __device__ constexpr int stages_of() {
+    return NV <= 16 ? 4 : (NV == 32 ? 3 : 2);
 }
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -184,14 +190,18 @@ __global__ void __launch_bounds__(kThreadsB, 2) batched_q8_kernel(const __grid_c
 #pragma unroll
     for (int t = 0; t < NT; ++t) acc[t][0] = acc[t][1] = 0.f;
 
-    if (nch > 0) load(0, 0);
-    cp_async_commit();
-    for (int ch = 0; ch < nch; ++ch) {
-        if (ch + 1 < nch) load(ch + 1, (ch + 1) & 1);
+    constexpr int ST = stages_of<NV>();
+#pragma unroll
+    for (int sidx = 0; sidx < ST - 1; ++sidx) {
+        if (sidx < nch) load(sidx, sidx);
         cp_async_commit();
-        cp_async_wait<1>();  // chunk ch has landed
-        __syncthreads();
-        const uint8_t* sw = smem + (ch & 1) * SB;
+    }
+    for (int ch = 0; ch < nch; ++ch) {
+        cp_async_wait<ST - 2>();  // chunk ch has landed
+        __syncthreads();          // ... for every thread, and chunk ch - 1's buffer is free
+        if (ch + ST - 1 < nch) load(ch + ST - 1, (ch + ST - 1) % ST);
+        cp_async_commit();
+        const uint8_t* sw = smem + (ch % ST) * SB;
         const uint8_t* sx = sw + kRowsB * kWRow;
         const float* ss = reinterpret_cast<const float*>(sx + NV * 2 * kXRow);
         float is[NT];  // 1 / s of this lane's vector in each column tile
@@ -228,7 +238,6 @@ __global__ void __launch_bounds__(kThreadsB, 2) batched_q8_kernel(const __grid_c
                 }
             }
         }
-        __syncthreads();  // the buffer is refilled next iteration
     }
 
     // ---- outputs: lane (g, c) holds rows 16 warp + g (+8) of vector 4 t + c ----
@@ -281,7 +290,7 @@ void plan(const MulMatOp& o, int* nv, int* splits, int* cps) {
     *nv = pick_nv(o.N);
     const int tiles = ((o.M + kRowsB - 1) / kRowsB) * ((o.N + *nv - 1) / *nv);
     const int nchunks = o.K / kChunk;
-    int s = (kSlotsB + tiles - 1) / tiles;           // enough CTAs for two per SM
+    int s = kSlotsB / tiles;                         // at most one wave of two CTAs per SM
     s = s < kMaxSplitsB ? s : kMaxSplitsB;
     s = s < (nchunks + 1) / 2 ? s : (nchunks + 1) / 2;  // at least two chunks per split
     s = s > 1 ? s : 1;
@@ -304,7 +313,7 @@ size_t partial_bytes(const MulMatOp& o) {
 
 template <int NV>
 cudaError_t launch_nv(const BatchedArgs& P, dim3 grid, cudaStream_t stream) {
-    constexpr int smem = 2 * stage_bytes<NV>();
+    constexpr int smem = stages_of<NV>() * stage_bytes<NV>();
     static bool configured = false;
     if (!configured) {
         const cudaError_t e =
