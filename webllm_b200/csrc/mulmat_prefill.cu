@@ -4,29 +4,31 @@
 //
 //   y[m + M n] = sum_k W[m, k] x[k + K n]   (ggml MUL_MAT, matmul.ts:10-17)
 //
-// One CTA computes a 128 (rows of W) x 128 (vectors) tile of y with the
-// accumulator in tensor memory (TMEM, 128 lanes x 128 f32 columns). K is
-// walked in chunks of 64.
+// One CTA computes a 128 (rows of W) x 256 (vectors) tile of y with the
+// accumulator in tensor memory (TMEM, 128 lanes x 256 f32 columns): each
+// dequantized weight feeds 256 vectors, which keeps the dequantization (the
+// CUDA-core side) ahead of the MMAs. K is walked in chunks of 64.
 //
 //  - warp 0 (TMA): per 256-element Q4_K block, one 2D box of the 128 rows'
 //    raw blocks (128 x 144 B) into a raw ring; per 64-chunk, one 2D box of the
-//    f16 activations (64 x 128, TMA 128-byte swizzle) into a B stage: the
+//    f16 activations (64 x 256, TMA 128-byte swizzle) into a B stage: the
 //    canonical K-major UMMA layout (vector n at (n/8)*1024 + (n%8)*128 bytes,
 //    its 16-byte piece j at position j ^ (n%8)).
-//  - warps 2..9 (dequant, 256 threads): warp w handles rows 32 (w%4) + lane
-//    (the TMEM lanes it may access) and half h = (w-2)/4 of each chunk: it turns
-//    the 32 quants of sub-block 2p+h (chunk p of the block) into f16
+//  - warps 2..17 (dequant, 512 threads): warp w handles rows 32 (w%4) + lane
+//    (the TMEM lanes it may access) and quarter (w-2)/4 of each chunk: it turns
+//    16 quants of sub-block 2p+h (chunk p of the block) into f16
 //    d*sc*q - dmin*m (the quant enters as the exact f16 1024 + q, minus 1024,
 //    then one f16 FMA) and stores them with tcgen05.st straight into the A
 //    operand's TMEM columns (row = lane, two f16 per column). The weights thus
 //    never pass through shared memory, whose bandwidth the MMAs' B reads and
 //    the TMA writes need.
 //  - warp 1 (MMA): TMEM allocation; one elected thread issues the 4 K=16
-//    tcgen05.mma (A from TMEM, B from shared memory; M=128, N=128,
+//    tcgen05.mma (A from TMEM, B from shared memory; M=128, N=256,
 //    f16 x f16 -> f32) of each chunk and commits them to the chunk's "stage
 //    free" barrier.
-//  - epilogue (warps 2..9): tcgen05.ld of the accumulator (warp w reads TMEM
-//    lanes 32 (w%4) .. +31, i.e. rows), f32 stores to y.
+//  - epilogue (warps 2..17): tcgen05.ld of the accumulator (warp w reads TMEM
+//    lanes 32 (w%4) .. +31, i.e. rows, and a quarter of the columns), f32
+//    stores to y.
 //
 // The activations are converted to f16 by a pre-pass (x_to_f16_kernel) into
 // library workspace: N x K x 2 bytes, read by every row tile from L2.
@@ -52,18 +54,18 @@ __device__ unsigned int g_prefill_error = 0;
 namespace {
 
 constexpr int kTileM = 128;                      // rows of W per CTA (TMEM lanes)
-constexpr int kTileN = 128;                      // vectors per CTA (TMEM columns)
+constexpr int kTileN = 256;                      // vectors per CTA (TMEM columns)
 constexpr int kChunkK = 64;                      // K per stage (one 128-byte swizzle atom of f16)
 constexpr int kStages = 4;                       // B stages in smem, A stages in TMEM
 constexpr int kRawSlots = 2;                     // raw Q4_K blocks in flight (each feeds 4 chunks)
 constexpr int kRawBytes = kTileM * 144;          // 18432
-constexpr int kBBytes = kTileN * kChunkK * 2;    // 16384
-constexpr int kDqWarps = 8;
+constexpr int kBBytes = kTileN * kChunkK * 2;    // 32768
+constexpr int kDqWarps = 16;
 constexpr int kThreads = 32 * (2 + kDqWarps);    // TMA warp, MMA warp, dequant/epilogue warps
 constexpr int kACols = kChunkK / 2;              // TMEM columns of one A stage (two f16 per column)
-// accumulator (kTileN) + kStages A stages: 256 of the SM's 512 columns, so two
-// CTAs (about 103 KB of shared memory each) share an SM
-constexpr int kTmemCols = 256;
+// accumulator (kTileN) + kStages A stages = 384 columns, allocated as 512: one
+// CTA per SM (about 165 KB of shared memory)
+constexpr int kTmemCols = 512;
 static_assert(kTileN + kStages * kACols <= kTmemCols, "TMEM budget");
 constexpr uint32_t kSpinLimit = 1u << 26;
 
@@ -143,15 +145,13 @@ __device__ __forceinline__ void umma_f16_ts(uint32_t tmem_d, uint32_t tmem_a, ui
         : "memory");
 }
 
-// 16 consecutive 32-bit TMEM columns of this warp's 32 lanes.
-__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16]) {
-    asm volatile(
-        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
-            taddr),
-        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
-        "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
-        : "memory");
+// 8 consecutive 32-bit TMEM columns of this warp's 32 lanes.
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&v)[8]) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr), "r"(v[0]),
+                 "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
+                 : "memory");
 }
+
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
                  : "memory");
@@ -172,7 +172,7 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
     for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-__global__ void __launch_bounds__(kThreads, 2) prefill_q4k_kernel(const __grid_constant__ PrefillArgs P) {
+__global__ void __launch_bounds__(kThreads, 1) prefill_q4k_kernel(const __grid_constant__ PrefillArgs P) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     // 1024-byte alignment for the swizzled tiles
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -258,9 +258,10 @@ __global__ void __launch_bounds__(kThreads, 2) prefill_q4k_kernel(const __grid_c
         }
     } else {
         // ---------------- dequant (then epilogue) ----------------
-        const int quarter = warp & 3;                    // TMEM lanes this warp may access
-        const int r = 32 * quarter + lane, h = (warp - 2) >> 2;  // row of the tile, half of each chunk
+        const int quarter = warp & 3;  // TMEM lanes this warp may access
         const int dw = warp - 2;
+        const int part = dw >> 2;      // quarter of each chunk's K
+        const int r = 32 * quarter + lane, h = part >> 1, qq = part & 1;  // row; sub-block 2p + h, its half qq
         const uint32_t trow = tmem + (static_cast<uint32_t>(32 * quarter) << 16);
         const uint32_t sel_a = 0x4440u + static_cast<uint32_t>(h);      // byte h, zero-extended
         const uint32_t sel_b = 0x4440u + 2u + static_cast<uint32_t>(h);  // byte 2 + h
@@ -290,13 +291,13 @@ __global__ void __launch_bounds__(kThreads, 2) prefill_q4k_kernel(const __grid_c
                 }
                 const __half2 sc2 = __float2half2_rn(d * static_cast<float>(scv[p]));
                 const __half2 mn2 = __float2half2_rn(-dmin * static_cast<float>(mv[p]));
-                // the 32 bytes of pair p; this thread's quants are their low (h = 0) or
-                // high (h = 1) nibbles: elements 64p + 32h + l, l = 0..31
-                const uint4 v0 = qs[2 * p], v1 = qs[2 * p + 1];
-                const uint32_t wv[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
-                uint32_t out[16];  // 32 f16, element order l = 0..31
+                // bytes 16 qq .. 16 qq + 15 of pair p; this thread's quants are their low
+                // (h = 0) or high (h = 1) nibbles: elements 64p + 32h + 16qq + l, l = 0..15
+                const uint4 v0 = qs[2 * p + qq];
+                const uint32_t wv[4] = {v0.x, v0.y, v0.z, v0.w};
+                uint32_t out[8];  // 16 f16, element order l = 0..15
 #pragma unroll
-                for (int i = 0; i < 8; ++i) {
+                for (int i = 0; i < 4; ++i) {
                     const uint32_t nib = (wv[i] >> (4 * h)) & 0x0F0F0F0Fu;
                     // f16 1024 + q (exact) for bytes (0, 1) and (2, 3): 0x64 in each high byte
                     const uint32_t e01 = __byte_perm(nib, 0x00006464u, 0x5140u);
@@ -307,8 +308,8 @@ __global__ void __launch_bounds__(kThreads, 2) prefill_q4k_kernel(const __grid_c
                     out[2 * i] = *reinterpret_cast<const uint32_t*>(&w01);
                     out[2 * i + 1] = *reinterpret_cast<const uint32_t*>(&w23);
                 }
-                // k = 32h + l of this chunk: TMEM columns 16h .. 16h+15 of A stage s
-                tmem_st16(trow + static_cast<uint32_t>(kTileN + s * kACols + 16 * h), out);
+                // k = 32h + 16qq + l of this chunk: TMEM columns 16h + 8qq .. +7 of A stage s
+                tmem_st8(trow + static_cast<uint32_t>(kTileN + s * kACols + 16 * h + 8 * qq), out);
                 asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
                 tc_fence_before();
                 __syncwarp();
@@ -321,18 +322,18 @@ __global__ void __launch_bounds__(kThreads, 2) prefill_q4k_kernel(const __grid_c
         // ---------------- epilogue ----------------
         const bool ok = mbar_wait(acc_full, 0, 4u, poisoned);
         tc_fence_after();
-        const int col0 = (dw < 4) ? 0 : kTileN / 2;
+        const int col0 = part * (kTileN / 4);  // the 4 warps of a lane quarter split the columns
         const int tr = 32 * quarter + lane, row = m0 + tr;
         const int tile = blockIdx.y * gridDim.x + blockIdx.x;
-        float* part = P.partial + (static_cast<int64_t>(tile) * P.splits + blockIdx.z) * (kTileM * kTileN);
+        float* ptile = P.partial + (static_cast<int64_t>(tile) * P.splits + blockIdx.z) * (kTileM * kTileN);
         if (ok) {
 #pragma unroll 1
-            for (int cc = 0; cc < kTileN / 2; cc += 16) {
+            for (int cc = 0; cc < kTileN / 4; cc += 16) {
                 float v[16];
                 tmem_ld16(tmem + (static_cast<uint32_t>(32 * quarter) << 16) + static_cast<uint32_t>(col0 + cc), v);
                 if (P.splits > 1) {
 #pragma unroll
-                    for (int i = 0; i < 16; ++i) part[(col0 + cc + i) * kTileM + tr] = v[i];  // [col][row]
+                    for (int i = 0; i < 16; ++i) ptile[(col0 + cc + i) * kTileM + tr] = v[i];  // [col][row]
                 } else if (row < P.M) {
 #pragma unroll
                     for (int i = 0; i < 16; ++i) {
@@ -357,9 +358,10 @@ __global__ void __launch_bounds__(kThreads, 2) prefill_q4k_kernel(const __grid_c
             }
             asm volatile("bar.sync 1, %0;" ::"n"(kDqWarps * 32) : "memory");
             if (last) {
-                // thread t sums rows 4 (t % 32) .. +3 of columns t / 32 + 8 j (j < 16):
+                // thread t sums rows 4 (t % 32) .. +3 of columns t / 32 + 16 j (j < 16):
                 // 16 independent float4 loads per split in flight
                 const int t = threadIdx.x - 64, r4 = 4 * (t & 31), cb = t >> 5;
+                static_assert(kDqWarps * 32 / 32 * 16 == kTileN, "reduction covers the tile's columns");
                 const float4* base =
                     reinterpret_cast<const float4*>(P.partial + static_cast<int64_t>(tile) * P.splits * (kTileM * kTileN));
                 float4 acc[16];
@@ -368,7 +370,7 @@ __global__ void __launch_bounds__(kThreads, 2) prefill_q4k_kernel(const __grid_c
                 for (int z = 0; z < P.splits; ++z) {
                     float4 v[16];
 #pragma unroll
-                    for (int j = 0; j < 16; ++j) v[j] = __ldcg(base + (z * kTileN + cb + 8 * j) * (kTileM / 4) + (r4 >> 2));
+                    for (int j = 0; j < 16; ++j) v[j] = __ldcg(base + (z * kTileN + cb + 16 * j) * (kTileM / 4) + (r4 >> 2));
 #pragma unroll
                     for (int j = 0; j < 16; ++j) {
                         acc[j].x += v[j].x;
@@ -379,7 +381,7 @@ __global__ void __launch_bounds__(kThreads, 2) prefill_q4k_kernel(const __grid_c
                 }
 #pragma unroll
                 for (int j = 0; j < 16; ++j) {
-                    const int n = n0 + cb + 8 * j, r = m0 + r4;
+                    const int n = n0 + cb + 16 * j, r = m0 + r4;
                     if (n >= P.N) continue;
                     float* yn = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(P.y) + n * P.y_nb1);
                     const float a[4] = {acc[j].x, acc[j].y, acc[j].z, acc[j].w};
@@ -430,7 +432,7 @@ EncodeFn encoder() {
 
 constexpr size_t kSmemBytes = 1024 /* alignment */ + kStages * kBBytes + kRawSlots * kRawBytes +
                               8 * (3 * kStages + 2 * kRawSlots + 1) + 16;
-constexpr int kSlots = 2 * 148;  // CTAs resident at once (two per SM)
+constexpr int kSlots = 148;  // CTAs resident at once (one per SM)
 constexpr int kMaxSplits = 8;
 
 // K splits per tile, only while the grid stays within one wave of resident
