@@ -140,6 +140,31 @@ def test_q8_0_batched_decode(runtime, name, M, K, N):
     assert O.rel_error(got, O.mul_mat_f64(jsep.GGML_TYPE_Q8_0, w, x)) <= GEMV_TOL
 
 
+def test_qwen3_8b_output_projection_vs_torch_fp64(runtime):
+    """The largest decode GEMV of the sweeps: Qwen3-8B's 151936 x 4096 Q6_K output
+    projection (510 MB of weights) at N = 1, against a float64 matmul of the
+    device-dequantized weights (bit-exact with the oracle's dequantization)."""
+    import torch
+
+    dev = torch.device("cuda", 0)
+    M, K = 151936, 4096
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(8)
+    w = synth.weights_torch(gen, jsep.GGML_TYPE_Q6_K, M, K, dev)
+    x = torch.randn(1, K, device=dev, generator=gen)
+    y = torch.empty(1, M, device=dev)
+    torch.cuda.synchronize()  # the library runs on its own stream
+    stream = jsep.library_stream()
+    jsep.mul_mat_device(jsep.GGML_TYPE_Q6_K, w.data_ptr(), w.shape[1], x.data_ptr(), K, y.data_ptr(), M, M, K, 1,
+                        stream)
+    wf = torch.empty(M, K, device=dev)
+    jsep.dequantize_device(jsep.GGML_TYPE_Q6_K, w.data_ptr(), wf.data_ptr(), M * K, stream)
+    runtime.jsep_sync()
+    ref = (wf.double() @ x.double().t()).t()
+    rel = ((y.double() - ref).abs().max() / ref.abs().max()).item()
+    assert rel <= GEMV_TOL, rel
+
+
 @pytest.mark.parametrize("qtype", [jsep.GGML_TYPE_Q4_K, jsep.GGML_TYPE_Q6_K, jsep.GGML_TYPE_Q8_0])
 def test_streaming_edge_shapes(runtime, qtype):
     """Shapes around the streaming kernel's unit/segment boundaries: rows not
