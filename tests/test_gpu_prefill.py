@@ -78,3 +78,27 @@ def test_prefill_llama3_8b_shapes_vs_torch_fp32(runtime, M, K):
     ref = (x.double() @ wf.double().t()).float()  # [N, M]
     rel = ((y - ref).abs().max() / ref.abs().max()).item()
     assert rel <= PREFILL_TOL, rel
+
+
+@pytest.mark.parametrize("M,K,N", [(20480, 2048, 300), (14336, 4096, 200)])
+def test_prefill_large_grids_vs_torch_fp32(runtime, M, K, N):
+    """Grids of more than one wave of CTAs (320 and 224 tiles), with a partial
+    vector tile (N = 300 and 200), run twice in a row."""
+    import torch
+
+    dev = torch.device("cuda", 0)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(M + K + N)
+    w = synth.weights_torch(gen, O.TYPE_Q4_K, M, K, dev)
+    x = torch.randn(N, K, device=dev, generator=gen)
+    y = torch.empty(N, M, device=dev)
+    torch.cuda.synchronize()  # the library runs on its own stream
+    stream = jsep.library_stream()
+    for _ in range(2):
+        jsep.mul_mat_device(O.TYPE_Q4_K, w.data_ptr(), w.shape[1], x.data_ptr(), K, y.data_ptr(), M, M, K, N, stream)
+    wf = torch.empty(M, K, device=dev)
+    jsep.dequantize_device(O.TYPE_Q4_K, w.data_ptr(), wf.data_ptr(), M * K, stream)
+    runtime.jsep_sync()
+    ref = (x.double() @ wf.double().t()).float()
+    rel = ((y - ref).abs().max() / ref.abs().max()).item()
+    assert rel <= PREFILL_TOL, rel
