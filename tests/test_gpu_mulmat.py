@@ -140,6 +140,29 @@ def test_q8_0_batched_decode(runtime, name, M, K, N):
     assert O.rel_error(got, O.mul_mat_f64(jsep.GGML_TYPE_Q8_0, w, x)) <= GEMV_TOL
 
 
+@pytest.mark.parametrize("qtype,M,K", [(jsep.GGML_TYPE_Q4_K, 4096, 4096), (jsep.GGML_TYPE_Q4_K, 1024, 4096),
+                                       (jsep.GGML_TYPE_Q4_K, 12288, 4096), (jsep.GGML_TYPE_Q4_K, 4096, 12288)])
+def test_qwen3_8b_layer_shapes_vs_torch_fp64(runtime, qtype, M, K):
+    """Qwen3-8B decode (batch 1) layer shapes: q/o, k/v, gate/up, down."""
+    import torch
+
+    dev = torch.device("cuda", 0)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(M * 3 + K)
+    w = synth.weights_torch(gen, qtype, M, K, dev)
+    x = torch.randn(1, K, device=dev, generator=gen)
+    y = torch.empty(1, M, device=dev)
+    torch.cuda.synchronize()  # the library runs on its own stream
+    stream = jsep.library_stream()
+    jsep.mul_mat_device(qtype, w.data_ptr(), w.shape[1], x.data_ptr(), K, y.data_ptr(), M, M, K, 1, stream)
+    wf = torch.empty(M, K, device=dev)
+    jsep.dequantize_device(qtype, w.data_ptr(), wf.data_ptr(), M * K, stream)
+    runtime.jsep_sync()
+    ref = (wf.double() @ x.double().t()).t()
+    rel = ((y.double() - ref).abs().max() / ref.abs().max()).item()
+    assert rel <= GEMV_TOL, rel
+
+
 def test_qwen3_8b_output_projection_vs_torch_fp64(runtime):
     """The largest decode GEMV of the sweeps: Qwen3-8B's 151936 x 4096 Q6_K output
     projection (510 MB of weights) at N = 1, against a float64 matmul of the
