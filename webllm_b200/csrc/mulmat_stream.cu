@@ -18,7 +18,7 @@
 // kRedDelay units later, when the others are normally done, and writes the
 // rows.
 //
-// Q4_K and Q6_K run on integer tensor cores (mma.sync m16n8k32, u8 x s8 ->
+// Every type runs on integer tensor cores (mma.sync m16n8k32, u8 / s8 x s8 ->
 // s32):
 //  - activations: per 256-element block and vector, x = (l0 + l1/128) / s with
 //    s = 127 / max|x| and int8 limbs l0 = rint(x s), l1 = rint(128 (x s - l0))
@@ -36,8 +36,9 @@
 //    per group assembles the 6-bit quants from ql and qh; int8 scales are
 //    applied in integer, the -32 offset through exact sums of x over
 //    16-element sub-blocks.
-// Q8_0 runs on CUDA cores: lanes 8j..8j+7 take row 4q+j (q = 0..3), lane
-// chunk c = lane%8 owns one 32-element block of each 8-block group.
+//  - Q8_0 weights (34-byte blocks): the signed quants are the A operands as
+//    they are (aligned 32-bit loads and a funnel shift); each block's s32
+//    result is scaled by its rows' f16 d in f32.
 //
 // Launch: programmatic dependent launch. CTAs trigger their dependents at
 // entry; the copy warp streams weights (never written by a preceding kernel)
@@ -77,7 +78,7 @@ constexpr int kMaxNT = 2;
 // until the image is built.
 constexpr int kPreStages = 2;
 static_assert((kCW & (kCW - 1)) == 0, "unit ownership rotates with a mask");
-constexpr int kXF4 = 16;                      // float4 of x per consumer thread: K <= 16384
+constexpr int kMaxK = 16384;                  // activation image in shared memory
 constexpr uint32_t kSpinLimit = 1u << 26;     // polls before a wait gives up (well over a second)
 constexpr int kSmemBudget = 200 * 1024;       // one CTA per SM, up to 8 stages in flight
 
@@ -249,6 +250,15 @@ __device__ __forceinline__ void imma_u8s8_acc(int (&d)[4], uint32_t a0, uint32_t
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
+// D += A (16x32 s8, row) * B (32x8 s8, col), s32.
+__device__ __forceinline__ void imma_s8s8_acc(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                              uint32_t b0, uint32_t b1) {
+    asm("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
 __host__ __device__ __forceinline__ int seg_cap(int type) {
     return type == kTypeQ4_K ? kQ4kSegBlocks : (type == kTypeQ6_K ? kQ6kSegBlocks : kQ80SegBlocks);
 }
@@ -258,13 +268,14 @@ __device__ __forceinline__ int block_bytes_of(int type) {
 }
 
 // Byte layout of the shared-memory activation image.
-//  Q4_K and Q6_K (one shared image): int8 limb columns [2N][K + kXPad]
+//  Every type (one shared image): int8 limb columns [2N][K + kXPad]
 //        (column 2t + l = limb l of vector t), then f32 d-factors [N][K/256]
 //        (max|x| / (127 * 16) per block), then exact f32 sums of x over
 //        32-element sub-blocks [N][K/32] (Q4_K) and over 16-element
-//        sub-blocks [N][K/16] (Q6_K).
-//  Q8_0: f32 x permuted per lane chunk, [N][K/256][8 f][8 c] float4.
-__host__ __device__ __forceinline__ bool limb_image(int type) { return type == kTypeQ4_K || type == kTypeQ6_K; }
+//        sub-blocks [N][K/16] (Q6_K). Q8_0 uses the limbs and d-factors.
+__host__ __device__ __forceinline__ bool limb_image(int type) {
+    return type == kTypeQ4_K || type == kTypeQ6_K || type == kTypeQ8_0;
+}
 __host__ __device__ __forceinline__ int img_col_bytes(int K) { return K + kXPad; }
 __host__ __device__ __forceinline__ int img_inv_off(int K, int N) { return 2 * N * img_col_bytes(K); }
 // (16-byte aligned: the sums are read as float2)
@@ -272,14 +283,7 @@ __host__ __device__ __forceinline__ int img_sum_off(int K, int N) {
     return (img_inv_off(K, N) + 4 * N * (K / 256) + 15) & ~15;
 }
 __host__ __device__ __forceinline__ int img_sum16_off(int K, int N) { return img_sum_off(K, N) + 4 * N * (K / 32); }
-__host__ __device__ __forceinline__ int img_bytes(int type, int K, int N) {
-    if (limb_image(type)) return img_sum16_off(K, N) + 4 * N * (K / 16);
-    return 4 * K * N;
-}
-
-// Element offset (within its 256-element group) of float4 f of lane chunk c
-// (Q8_0: lane chunk c is block c of the group); the image is xs4[group][f][c].
-__device__ __forceinline__ int chunk_elem(int c, int f) { return 32 * c + 4 * f; }
+__host__ __device__ __forceinline__ int img_bytes(int K, int N) { return img_sum16_off(K, N) + 4 * N * (K / 16); }
 
 // 4 bytes at any 2-byte-aligned shared address.
 __device__ __forceinline__ uint32_t lds_u32_any(const uint8_t* p) {
@@ -471,37 +475,46 @@ __device__ __forceinline__ void q6k_item(const uint8_t* pg, const uint8_t* ph, u
     yh = fmaf(dh, fmaf(fmaf(static_cast<float>(a3), 0.0078125f, static_cast<float>(a2)), xf, -32.f * sh), yh);
 }
 
-template <int NT>
-__device__ __forceinline__ void item_q8_0(const uint8_t* blk, const float4 (&xr)[NT][8], float (&acc)[NT]) {
-    const float d = f16_bits_to_f32(lds_u16(blk));
-    // the 32 quant bytes at blk+2 (2-byte aligned): 9 aligned words, then funnel shifts
-    const uint8_t* q = blk + 2;
-    const uint32_t mis = static_cast<uint32_t>(reinterpret_cast<uintptr_t>(q) & 3);
-    const uint32_t* wp = reinterpret_cast<const uint32_t*>(q - mis);
-    uint32_t wv[9];
+// One Q8_0 item: 16 rows x one group of 8 blocks (256 elements, one x
+// scale), for NP = N rounded up to a power of two. Each 32-element block is
+// one MMA on the signed quants as they are; as for Q4_K, NS = 4/NP blocks
+// share an accumulator through the B-column slots (block j: slot j % NS,
+// chain j / NS), and lane (g, c) scales its slot's blocks j = q NS + sl of
+// rows g and g + 8 by their f16 d in f32. Blocks are 34 bytes, so they sit
+// 2-byte aligned in shared memory: aligned 32-bit loads and a funnel shift.
+template <int NP>
+__device__ __forceinline__ void q8_item(const uint8_t* pg, const uint8_t* ph, uint32_t xaddr, uint32_t xzero,
+                                        bool xv0, bool xv1, float xf, int c, int sl, float& yg, float& yh) {
+    constexpr int NS = 4 / NP, NCH = 8 / NS;
+    int D[NCH][4];
 #pragma unroll
-    for (int i = 0; i < 9; ++i) wv[i] = wp[i];
-    float2 s[NT];
+    for (int q = 0; q < NCH; ++q) D[q][0] = D[q][1] = D[q][2] = D[q][3] = 0;
 #pragma unroll
-    for (int n = 0; n < NT; ++n) s[n] = make_float2(0.f, 0.f);
+    for (int pp = 0; pp < 4; ++pp) {  // blocks 2pp, 2pp+1: one ldmatrix of activations
+        uint32_t x[4];
+        ldmatrix_x4_at(x, ((pp & 1) ? xv1 : xv0) ? xaddr + 64 * pp : xzero);
 #pragma unroll
-    for (int f = 0; f < 8; ++f) {
-        const uint32_t w = __funnelshift_r(wv[f], wv[f + 1], mis * 8) ^ 0x80808080u;  // u = q + 128
-        // 2^23 + u exactly, minus 2^23 + 128 -> q
-        const float q0 = __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7440u)) - 8388736.f;
-        const float q1 = __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7441u)) - 8388736.f;
-        const float q2 = __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7442u)) - 8388736.f;
-        const float q3 = __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7443u)) - 8388736.f;
-#pragma unroll
-        for (int n = 0; n < NT; ++n) {
-            const float4 xv = xr[n][f];
-            s[n] = __ffma2_rn(make_float2(q0, q1), make_float2(xv.x, xv.y), s[n]);
-            s[n] = __ffma2_rn(make_float2(q2, q3), make_float2(xv.z, xv.w), s[n]);
+        for (int h = 0; h < 2; ++h) {
+            const int j = 2 * pp + h;
+            const uint8_t* bg = pg + 34 * j + 2 + 4 * c;
+            const uint8_t* bh = ph + 34 * j + 2 + 4 * c;
+            imma_s8s8_acc(D[j / NS], lds_u32_any(bg), lds_u32_any(bh), lds_u32_any(bg + 16), lds_u32_any(bh + 16),
+                          x[2 * h], x[2 * h + 1]);
         }
     }
+    // |D| <= 32 * 127 * 127 per block
+    float ag = 0.f, ah = 0.f;
 #pragma unroll
-    for (int n = 0; n < NT; ++n) acc[n] += d * (s[n].x + s[n].y);
+    for (int q = 0; q < NCH; ++q) {
+        const int j = q * NS + sl;
+        const float dg = f16_bits_to_f32(lds_u16(pg + 34 * j)), dh = f16_bits_to_f32(lds_u16(ph + 34 * j));
+        ag = fmaf(fmaf(static_cast<float>(D[q][1]), 0.0078125f, static_cast<float>(D[q][0])), dg, ag);
+        ah = fmaf(fmaf(static_cast<float>(D[q][3]), 0.0078125f, static_cast<float>(D[q][2])), dh, ah);
+    }
+    yg = fmaf(ag, xf, yg);
+    yh = fmaf(ah, xf, yh);
 }
+
 
 // Per-op fields the kernel reads in its loops, copied from the parameter
 // block into shared memory at entry: the parameter block (with one tensor map
@@ -549,12 +562,12 @@ struct OpTable {
 };
 
 
-// Builds the activation image of `op` in shared memory (all consumer threads;
-// one L2 round trip per vector).
-__device__ __forceinline__ void stage_activations(const OpInfo& op, uint8_t* xsm, int ct, int lane, int cw) {
-    const int K = op.K, N = op.N, per4 = K / 4;
+// Builds the activation image of `op` in shared memory (all consumer warps;
+// one L2 round trip).
+__device__ __forceinline__ void stage_activations(const OpInfo& op, uint8_t* xsm, int lane, int cw) {
+    const int K = op.K, N = op.N;
     const uint8_t* xb = reinterpret_cast<const uint8_t*>(op.x);
-    if (limb_image(op.type)) {
+    {
         const int nblk = K / 256, XS = img_col_bytes(K);
         float* dfac = reinterpret_cast<float*>(xsm + img_inv_off(K, N));
         float* Xs = reinterpret_cast<float*>(xsm + img_sum_off(K, N));
@@ -612,29 +625,6 @@ __device__ __forceinline__ void stage_activations(const OpInfo& op, uint8_t* xsm
                     X16[tt * (K / 16) + bb * 16 + h] = a16;
                     if ((h & 1) == 0) Xs[tt * (K / 32) + bb * 8 + (h >> 1)] = a;
                     if (h == 0) dfac[tt * nblk + bb] = mx * (1.f / 2032.f);  // 1 / (16 s)
-                }
-            }
-        }
-        consumers_sync();
-    } else {
-        float4* xs4 = reinterpret_cast<float4*>(xsm);
-        constexpr int kB = 8;  // float4 loads in flight per thread
-        for (int t = 0; t < N; ++t) {
-            const float* xf = reinterpret_cast<const float*>(xb + t * op.x_nb1);
-            for (int i0 = 0; i0 < kXF4 && i0 * kCW * 32 < per4; i0 += kB) {
-                float4 v[kB];
-#pragma unroll
-                for (int i = 0; i < kB; ++i) {
-                    const int idx = (i0 + i) * kCW * 32 + ct;
-                    if (idx < per4) {
-                        const int g = idx >> 6, f = (idx >> 3) & 7, c = idx & 7;
-                        v[i] = __ldg(reinterpret_cast<const float4*>(xf + g * 256 + chunk_elem(c, f)));
-                    }
-                }
-#pragma unroll
-                for (int i = 0; i < kB; ++i) {
-                    const int idx = (i0 + i) * kCW * 32 + ct;
-                    if (idx < per4) xs4[t * per4 + idx] = v[i];
                 }
             }
         }
@@ -876,6 +866,47 @@ __device__ bool tp_wait_peers(const uint32_t* const* sig, int world, int rank, u
     return true;
 }
 
+// All segments of one Q8_0 unit for this consumer warp (see q6k_unit); an
+// item is a group of 8 blocks (segments hold whole groups).
+template <int NP, int NT>
+__device__ __forceinline__ void q8_unit(const OpRegs& op, const Q4Lane& q, Ring& R, uint32_t xzero, uint32_t glo,
+                                        int lane, int cw, float* ub) {
+    const int N = op.N, nblocks = op.K / 32;
+    const int g = lane >> 2, c = lane & 3, sl = q.sl, tk = q.tk;
+    const uint32_t nb1 = static_cast<uint32_t>(op.w_nb1);
+    float yg = 0.f, yh = 0.f;
+    for (int sg = 0; sg < op.nseg; ++sg) {
+        const int b0 = sg * op.seg_blocks;
+        const int ng = (min(op.seg_blocks, nblocks - b0) + 7) / 8;  // groups of this segment
+        const int i0 = (cw - static_cast<int>(R.item_base % kCW) + kCW) % kCW;
+        if (i0 < ng) {
+            ring_wait(R, lane);
+            const uint8_t* stage = R.stages + R.slot * R.SB;
+            const uint32_t gl = glo + static_cast<uint32_t>(b0 * 34);
+            const uint8_t* pg = stage + g * op.wbox + ((gl + static_cast<uint32_t>(g) * nb1) & 15u);
+            const uint8_t* ph = stage + (g + 8) * op.wbox + ((gl + static_cast<uint32_t>(g + 8) * nb1) & 15u);
+            for (int i = i0; i < ng; i += kCW) {
+                const int gg = b0 / 8 + i;  // 256-element group
+                q8_item<NP>(pg + i * 272, ph + i * 272, q.xcol + gg * 256, xzero, q.xv0, q.xv1, 16.f * q.dfac[gg], c,
+                            sl, yg, yh);
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cnt(&R.empty[R.slot], i0 == 0 ? 1u + kCW - min(ng, kCW) : 1u);
+        }
+        R.item_base += ng;
+        R.advance();
+    }
+#pragma unroll
+    for (int o = NP; o < 4; o <<= 1) {
+        yg += __shfl_xor_sync(0xffffffffu, yg, o);
+        yh += __shfl_xor_sync(0xffffffffu, yh, o);
+    }
+    if (sl == 0 && tk < N) {
+        ub[g * NT + tk] = yg;
+        ub[(g + 8) * NT + tk] = yh;
+    }
+}
+
 template <int NT>
 __global__ void __launch_bounds__(kThreads, 1) stream_gemv_kernel(const __grid_constant__ SList L) {
     extern __shared__ __align__(128) uint8_t smem[];
@@ -1089,11 +1120,12 @@ __global__ void __launch_bounds__(kThreads, 1) stream_gemv_kernel(const __grid_c
             if (staged < 0 || T.op[staged].x != oo.x || T.op[staged].K != oo.K || T.op[staged].N != oo.N ||
                 T.op[staged].x_nb1 != oo.x_nb1 || limb_image(T.op[staged].type) != limb_image(oo.type)) {
                 consumers_sync();  // nobody still reads the previous image
-                stage_activations(oo, xsm, ct, lane, cw);
+                stage_activations(oo, xsm, lane, cw);
                 if (ct == 0 && useq == 0) mbar_arrive_cnt(xready, 1u);  // the copy warp may go on
                 staged = oi;
             }
-            if (oo.type == kTypeQ4_K) q4 = (NT == 1 || oo.N == 1) ? q4k_lane<1>(oo, xsm, lane) : q4k_lane<2>(oo, xsm, lane);
+            if (oo.type == kTypeQ4_K || oo.type == kTypeQ8_0)
+                q4 = (NT == 1 || oo.N == 1) ? q4k_lane<1>(oo, xsm, lane) : q4k_lane<2>(oo, xsm, lane);
             if (oo.type == kTypeQ6_K) q6 = (NT == 1 || oo.N == 1) ? q6k_lane<1>(oo, xsm, lane) : q6k_lane<2>(oo, xsm, lane);
             op = op_regs(oo);
             next_begin = oi + 1 < n_ops ? T.op[oi + 1].unit_begin : total;
@@ -1120,67 +1152,13 @@ __global__ void __launch_bounds__(kThreads, 1) stream_gemv_kernel(const __grid_c
             else
                 q6k_unit<2, NT>(op, q6, R, smem_u32(zrow), glo, lane, cw, ub);
         } else {
-            // ================= Q8_0, CUDA cores =================
-            const int j = lane >> 3, c = lane & 7;
-            const int K256 = K / 256;
-            const float4* xs4 = reinterpret_cast<const float4*>(xsm);
-            const uint32_t wlo = static_cast<uint32_t>(reinterpret_cast<uintptr_t>(op.w + static_cast<int64_t>(r0) * op.w_nb1));
-            const uint32_t nb1lo = static_cast<uint32_t>(op.w_nb1);
-            float acc[4][NT];
-#pragma unroll
-            for (int q = 0; q < 4; ++q)
-#pragma unroll
-                for (int n = 0; n < NT; ++n) acc[q][n] = 0.f;
-            for (int sg = 0; sg < op.nseg; ++sg) {
-                const int b0 = sg * op.seg_blocks;
-                const int nb = min(op.seg_blocks, nblocks - b0);
-                const int ngroups = (nb + 7) / 8;  // 256-element groups of 8 blocks
-                const int g0 = (cw - static_cast<int>(R.item_base % kCW) + kCW) % kCW;
-                if (g0 >= ngroups) {  // no item here: the warp with item 0 releases the stage
-                    R.item_base += ngroups;
-                    R.advance();
-                    continue;
-                }
-                ring_wait(R, lane);
-                const uint8_t* stage = stages + R.slot * SB;
-                const uint32_t glo = wlo + static_cast<uint32_t>(b0 * bb);
-                const uint8_t* base[4];
-#pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    const int r = 4 * q + j;
-                    // each row's copy window starts at its segment start rounded down to 16 bytes
-                    base[q] = stage + r * op.wbox + ((glo + static_cast<uint32_t>(r) * nb1lo) & 15u);
-                }
-                for (int gi = g0; gi < ngroups; gi += kCW) {
-                    const int gg = b0 / 8 + gi;  // 256-element group index
-                    float4 xr[NT][8];
-#pragma unroll
-                    for (int n = 0; n < NT; ++n) {
-                        const int nn = n < N ? n : 0;
-#pragma unroll
-                        for (int f = 0; f < 8; ++f) xr[n][f] = xs4[(nn * K256 + gg) * 64 + f * 8 + c];
-                    }
-                    const int blk = gg * 8 + c;
-                    if (blk < b0 + nb) {
-#pragma unroll
-                        for (int q = 0; q < 4; ++q) item_q8_0<NT>(base[q] + (blk - b0) * 34, xr, acc[q]);
-                    }
-                }
-                R.item_base += ngroups;
-                __syncwarp();
-                if (lane == 0) mbar_arrive_cnt(&R.empty[R.slot], g0 == 0 ? 1u + kCW - min(ngroups, kCW) : 1u);
-                R.advance();
-            }
-#pragma unroll
-            for (int q = 0; q < 4; ++q)
-#pragma unroll
-                for (int n = 0; n < NT; ++n) {
-                    float v = acc[q][n];
-                    v += __shfl_xor_sync(0xffffffffu, v, 1);
-                    v += __shfl_xor_sync(0xffffffffu, v, 2);
-                    v += __shfl_xor_sync(0xffffffffu, v, 4);
-                    if (c == 0 && n < N) ub[(4 * q + j) * NT + n] = v;
-                }
+            // ================= Q8_0, integer tensor cores =================
+            const uint32_t glo =
+                static_cast<uint32_t>(reinterpret_cast<uintptr_t>(op.w + static_cast<int64_t>(r0) * op.w_nb1));
+            if (NT == 1 || N == 1)
+                q8_unit<1, NT>(op, q4, R, smem_u32(zrow), glo, lane, cw, ub);
+            else
+                q8_unit<2, NT>(op, q4, R, smem_u32(zrow), glo, lane, cw, ub);
         }
         // ---- unit hand-off: publish this warp's partials; the owner sums them later ----
         if (own == cw && lane == 0) {
@@ -1276,7 +1254,7 @@ bool stream_supported(const MulMatOp* ops, int n_ops) {
         if (o.ne2 != 1 || o.ne3 != 1) return false;
         if (o.N < 1 || o.N > kMaxNT) return false;
         if (o.K % 256 != 0) return false;  // whole 256-element groups (Q8_0 too)
-        if (o.K > kXF4 * kCW * 32 * 4) return false;
+        if (o.K > kMaxK) return false;
         if (o.type == kTypeQ4_K && ((reinterpret_cast<uintptr_t>(o.w) | static_cast<uintptr_t>(o.w_nb1)) & 15))
             return false;  // 16-byte header loads from shared memory
         if ((reinterpret_cast<uintptr_t>(o.w) | static_cast<uintptr_t>(o.w_nb1)) & 1)
@@ -1330,7 +1308,7 @@ int launch_stream(const MulMatOp* ops, int n_ops, cudaStream_t stream, int num_s
         wmax = wbox > wmax ? wbox : wmax;
         units += (o.M + kRows - 1) / kRows;
         max_n = o.N > max_n ? o.N : max_n;
-        const int xb = (img_bytes(o.type, o.K, o.N) + 15) / 16 * 16;
+        const int xb = (img_bytes(o.K, o.N) + 15) / 16 * 16;
         x_bytes = xb > x_bytes ? xb : x_bytes;
     }
     L.total_units = units;
