@@ -389,6 +389,17 @@ __device__ __forceinline__ void q4k_items(const uint8_t* blk, int wbox, uint32_t
     }
 }
 
+// rint(v) for |v| < 2^22 without the conversion pipe: adding 1.5 * 2^23
+// rounds v to an integer (round to nearest even), and the sum's bit pattern
+// is 0x4B400000 + rint(v), so its low byte is the low byte of rint(v) in
+// two's complement; `r` gets rint(v) as a float (exact).
+__device__ __forceinline__ int round_low_byte(float v, float& r) {
+    constexpr float kRound = 12582912.f;  // 1.5 * 2^23
+    const float t = __fadd_rn(v, kRound);
+    r = __fsub_rn(t, kRound);
+    return __float_as_int(t);
+}
+
 // Low bytes of four ints -> one word.
 __device__ __forceinline__ uint32_t pack_b4(int a, int b, int c, int d) {
     return __byte_perm(__byte_perm(static_cast<uint32_t>(a), static_cast<uint32_t>(b), 0x0040u),
@@ -567,69 +578,75 @@ struct OpTable {
 __device__ __forceinline__ void stage_activations(const OpInfo& op, uint8_t* xsm, int lane, int cw) {
     const int K = op.K, N = op.N;
     const uint8_t* xb = reinterpret_cast<const uint8_t*>(op.x);
-    {
-        const int nblk = K / 256, XS = img_col_bytes(K);
-        float* dfac = reinterpret_cast<float*>(xsm + img_inv_off(K, N));
-        float* Xs = reinterpret_cast<float*>(xsm + img_sum_off(K, N));
-        float* X16 = reinterpret_cast<float*>(xsm + img_sum16_off(K, N));
-        // one (vector, block) per half-warp and round: lane h = lane%16 covers
-        // elements 16h .. 16h+15. Two rounds' loads are issued before any
-        // arithmetic (K = 8192 at N = 1 is two rounds: one L2 round trip)
-        const int hw = lane >> 4, h = lane & 15, total = N * nblk;
-        for (int tb0 = 2 * cw + hw; tb0 - hw < total; tb0 += 4 * kCW) {  // warp-uniform
-            float4 v[2][4];
-            bool act[2];
-            int t[2], b[2];
+    const int nblk = K / 256, XS = img_col_bytes(K);
+    float* dfac = reinterpret_cast<float*>(xsm + img_inv_off(K, N));
+    float* Xs = reinterpret_cast<float*>(xsm + img_sum_off(K, N));
+    float* X16 = reinterpret_cast<float*>(xsm + img_sum16_off(K, N));
+    // one (vector, block) per half-warp and round: lane h = lane%16 covers
+    // elements 16h .. 16h+15. Two rounds' loads are issued before any
+    // arithmetic (K = 8192 at N = 1 is two rounds: one L2 round trip)
+    const int hw = lane >> 4, h = lane & 15, total = N * nblk;
+    for (int tb0 = 2 * cw + hw; tb0 - hw < total; tb0 += 4 * kCW) {  // warp-uniform
+        float4 v[2][4];
+        bool act[2];
+        int t[2], b[2];
+        // the second round only where the warp has one (warp-uniform)
+        const int rounds = tb0 - hw + 2 * kCW < total ? 2 : 1;
 #pragma unroll
-            for (int r = 0; r < 2; ++r) {
-                const int tb = tb0 + 2 * kCW * r;
-                act[r] = tb < total;
-                t[r] = act[r] ? tb / nblk : 0;
-                b[r] = act[r] ? tb - t[r] * nblk : 0;
-                const float4* xv = reinterpret_cast<const float4*>(xb + t[r] * op.x_nb1) + b[r] * 64 + 4 * h;
+        for (int r = 0; r < 2; ++r) {
+            const int tb = tb0 + 2 * kCW * r;
+            act[r] = tb < total;
+            t[r] = act[r] ? tb / nblk : 0;
+            b[r] = act[r] ? tb - t[r] * nblk : 0;
+            const float4* xv = reinterpret_cast<const float4*>(xb + t[r] * op.x_nb1) + b[r] * 64 + 4 * h;
+            if (r < rounds) {
 #pragma unroll
                 for (int k = 0; k < 4; ++k) v[r][k] = act[r] ? __ldg(xv + k) : make_float4(0.f, 0.f, 0.f, 0.f);
             }
+        }
 #pragma unroll
-            for (int r = 0; r < 2; ++r) {
-                float mx = 0.f;
+        for (int r = 0; r < 2; ++r) {
+            if (r >= rounds) break;
+            float mx = 0.f;
 #pragma unroll
-                for (int k = 0; k < 4; ++k)
-                    mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v[r][k].x), fabsf(v[r][k].y)),
-                                         fmaxf(fabsf(v[r][k].z), fabsf(v[r][k].w))));
+            for (int k = 0; k < 4; ++k)
+                mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v[r][k].x), fabsf(v[r][k].y)),
+                                     fmaxf(fabsf(v[r][k].z), fabsf(v[r][k].w))));
 #pragma unroll
-                for (int o = 8; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));  // within the half
-                const float sc = mx > 0.f ? 127.f / mx : 0.f;
-                uint32_t p0[4], p1[4];
+            for (int o = 8; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));  // within the half
+            const float sc = mx > 0.f ? 127.f / mx : 0.f;
+            // l0 = rint(x s) (|l0| <= 127), l1 = rint(128 (x s - l0)) (|l1| <= 64)
+            uint32_t p0[4], p1[4];
 #pragma unroll
-                for (int k = 0; k < 4; ++k) {
-                    const float4 e = v[r][k];
-                    const int q0 = __float2int_rn(e.x * sc), q1 = __float2int_rn(e.y * sc);  // |l0| <= 127
-                    const int q2 = __float2int_rn(e.z * sc), q3 = __float2int_rn(e.w * sc);
-                    p0[k] = pack_b4(q0, q1, q2, q3);
-                    // |l1| <= 64
-                    p1[k] = pack_b4(__float2int_rn(fmaf(e.x, sc, -static_cast<float>(q0)) * 128.f),
-                                    __float2int_rn(fmaf(e.y, sc, -static_cast<float>(q1)) * 128.f),
-                                    __float2int_rn(fmaf(e.z, sc, -static_cast<float>(q2)) * 128.f),
-                                    __float2int_rn(fmaf(e.w, sc, -static_cast<float>(q3)) * 128.f));
+            for (int k = 0; k < 4; ++k) {
+                const float e[4] = {v[r][k].x, v[r][k].y, v[r][k].z, v[r][k].w};
+                int b0[4], b1[4];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    float l0;
+                    b0[j] = round_low_byte(__fmul_rn(e[j], sc), l0);
+                    float l1;
+                    b1[j] = round_low_byte(fmaf(e[j], sc, -l0) * 128.f, l1);
                 }
-                float a16 = 0.f;  // a lane's 16 elements: one Q6_K sub-block
+                p0[k] = pack_b4(b0[0], b0[1], b0[2], b0[3]);
+                p1[k] = pack_b4(b1[0], b1[1], b1[2], b1[3]);
+            }
+            float a16 = 0.f;  // a lane's 16 elements: one Q6_K sub-block
 #pragma unroll
-                for (int k = 0; k < 4; ++k) a16 += (v[r][k].x + v[r][k].y) + (v[r][k].z + v[r][k].w);
-                const float a = a16 + __shfl_xor_sync(0xffffffffu, a16, 1);  // a Q4_K sub-block is two lanes
-                if (act[r]) {
-                    const int tt = t[r], bb = b[r];
-                    uint8_t* c0 = xsm + (2 * tt) * XS + bb * 256 + 16 * h;
-                    *reinterpret_cast<uint4*>(c0) = make_uint4(p0[0], p0[1], p0[2], p0[3]);
-                    *reinterpret_cast<uint4*>(c0 + XS) = make_uint4(p1[0], p1[1], p1[2], p1[3]);
-                    X16[tt * (K / 16) + bb * 16 + h] = a16;
-                    if ((h & 1) == 0) Xs[tt * (K / 32) + bb * 8 + (h >> 1)] = a;
-                    if (h == 0) dfac[tt * nblk + bb] = mx * (1.f / 2032.f);  // 1 / (16 s)
-                }
+            for (int k = 0; k < 4; ++k) a16 += (v[r][k].x + v[r][k].y) + (v[r][k].z + v[r][k].w);
+            const float a = a16 + __shfl_xor_sync(0xffffffffu, a16, 1);  // a Q4_K sub-block is two lanes
+            if (act[r]) {
+                const int tt = t[r], bb = b[r];
+                uint8_t* c0 = xsm + (2 * tt) * XS + bb * 256 + 16 * h;
+                *reinterpret_cast<uint4*>(c0) = make_uint4(p0[0], p0[1], p0[2], p0[3]);
+                *reinterpret_cast<uint4*>(c0 + XS) = make_uint4(p1[0], p1[1], p1[2], p1[3]);
+                X16[tt * (K / 16) + bb * 16 + h] = a16;
+                if ((h & 1) == 0) Xs[tt * (K / 32) + bb * 8 + (h >> 1)] = a;
+                if (h == 0) dfac[tt * nblk + bb] = mx * (1.f / 2032.f);  // 1 / (16 s)
             }
         }
-        consumers_sync();
     }
+    consumers_sync();
 }
 
 // Where a unit's rows go; written and read by the unit's owner warp only.
