@@ -375,20 +375,28 @@ def run_b200(args, rank: int, world: int, local_rank: int):
         sigs = [s_ptr if r == rank else jsep.ipc_open(handles[r][1]) for r in range(world)]
         tp = jsep.tp_group(world, rank, sigs, st_ptr)
         gview = torch.as_tensor(DevArray(g_ptr, per_layer * layers), device=dev)
-    # ---- resident weights (row shard of every matrix), inputs, outputs
+    # ---- resident weights (row shard of every matrix), inputs, outputs.
+    # Every group's activations are a slice of one buffer, and at one GPU
+    # every group's outputs too, so the end-to-end step moves each with one copy.
+    x_all = torch.empty(layers * sum(kin for kin, _ in groups), device=dev)
+    y_all = torch.zeros(layers * sum(gtot), device=dev) if world == 1 else None
+    x_pos = y_pos = 0
     W, X, Y, ops, peer_outs = [], [], [], [], []
     for li in range(layers):
         lw, lx, ly, lops, louts = [], [], [], [], []
         base = li * per_layer
         for gi, (kin, mats) in enumerate(groups):
-            x = torch.randn(1, kin, device=dev, generator=gen.manual_seed(10_000 * li + 10 * gi))
+            x = x_all[x_pos:x_pos + kin].view(1, kin)
+            x_pos += kin
+            x.copy_(torch.randn(1, kin, device=dev, generator=gen.manual_seed(10_000 * li + 10 * gi)))
             lx.append(x)
             pads = [row_shard(M, world, rank).padded for (_, _, M, _) in mats]
             offs = [sum(pads[:i]) for i in range(len(pads))]
             if world > 1:
                 out = gview[base:base + world * gtot[gi]].view(1, -1)  # the group's gathered rows
             else:
-                out = torch.zeros(1, gtot[gi], device=dev)
+                out = y_all[y_pos:y_pos + gtot[gi]].view(1, -1)
+                y_pos += gtot[gi]
             gops, gouts = [], []
             for mi, (name, t, M, K) in enumerate(mats):
                 # this rank's contiguous row shard; every rank reserves `padded` rows
@@ -464,22 +472,20 @@ def run_b200(args, rank: int, world: int, local_rank: int):
     dev_ms = max_over_ranks(ev0.elapsed_time(ev1)) / args.steps
     clk = clocks.summary()
 
-    # ---- e2e: pinned host activations in, outputs out, every step
-    flat_x = [x for lx in X for x in lx]
-    x_host = [torch.randn_like(x, device="cpu").pin_memory() for x in flat_x]
-    # every group's output (at N > 1 the gathered rows of all ranks)
-    outs = [o for ly in Y for o in ly]
-    y_host = [torch.empty_like(o, device="cpu").pin_memory() for o in outs]
-    h2d = sum(t.numel() * 4 for t in x_host)
-    d2h = sum(t.numel() * 4 for t in y_host) if rank == 0 else 0
+    # ---- e2e: pinned host activations in, outputs out, every step: one copy
+    # of all the step's activations, one of all its outputs (at N > 1 the
+    # gathered rows of all ranks)
+    x_host = torch.randn(x_all.numel()).pin_memory()
+    outs = y_all if world == 1 else gview
+    y_host = torch.empty(outs.numel()).pin_memory()
+    h2d = x_host.numel() * 4
+    d2h = y_host.numel() * 4 if rank == 0 else 0
 
     def e2e_step():
-        for xd, xh in zip(flat_x, x_host):
-            xd.copy_(xh, non_blocking=True)
+        x_all.copy_(x_host, non_blocking=True)
         graph.replay()
         if rank == 0:
-            for yh, yd in zip(y_host, outs):
-                yh.copy_(yd, non_blocking=True)
+            y_host.copy_(outs, non_blocking=True)
 
     for _ in range(args.warmup):
         e2e_step()
