@@ -188,6 +188,59 @@ def test_qwen3_8b_output_projection_vs_torch_fp64(runtime):
     assert rel <= GEMV_TOL, rel
 
 
+PARTIAL_ROUND_LAUNCHES = {
+    # more units than SMs, the last round partial: CTAs own different unit counts
+    "down_q6k": [(jsep.GGML_TYPE_Q6_K, 3072, 8192)],
+    "o_q4k": [(jsep.GGML_TYPE_Q4_K, 3072, 3072)],
+    "qkv_mixed": [(jsep.GGML_TYPE_Q4_K, 3072, 3072), (jsep.GGML_TYPE_Q4_K, 1024, 3072), (jsep.GGML_TYPE_Q6_K, 1024, 3072)],
+    "q8_0": [(jsep.GGML_TYPE_Q8_0, 2848, 2304)],
+    # a long-K op followed by many tiny units of a second op
+    "wide_and_tiny": [(jsep.GGML_TYPE_Q4_K, 2528, 16384), (jsep.GGML_TYPE_Q4_K, 640, 256)],
+    "ragged_rows": [(jsep.GGML_TYPE_Q6_K, 2371, 4096)],
+}
+
+
+@pytest.mark.parametrize("N", [1, 2])
+@pytest.mark.parametrize("case", sorted(PARTIAL_ROUND_LAUNCHES))
+def test_partial_round_launches_vs_torch_fp64(runtime, case, N):
+    """Grouped decode launches with more 16-row units than SMs and a partial
+    last round (mixed types, mixed K, ragged rows): against a float64 matmul
+    of the device-dequantized weights, and bit-identical over three launches
+    in a row."""
+    import torch
+
+    dev = torch.device("cuda", 0)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(len(case) * 101 + N)
+    mats = PARTIAL_ROUND_LAUNCHES[case]
+    ws, xs, ys, ops = [], [], [], []
+    for t, M, K in mats:
+        w = synth.weights_torch(gen, t, M, K, dev)
+        x = torch.randn(N, K, device=dev, generator=gen)
+        y = torch.empty(N, M, device=dev)
+        ws.append(w)
+        xs.append(x)
+        ys.append(y)
+        ops.append(jsep.MulMatArgs(t, M, K, N, w.data_ptr(), w.shape[1], x.data_ptr(), K, y.data_ptr(), M))
+    torch.cuda.synchronize()  # the library runs on its own stream
+    stream = jsep.library_stream()
+    runs = []
+    for _ in range(3):
+        jsep.mul_mat_batch(ops, stream)
+        runtime.jsep_sync()
+        runs.append([y.clone() for y in ys])
+    for (t, M, K), w, x, y in zip(mats, ws, xs, runs[0]):
+        wf = torch.empty(M, K, device=dev)
+        jsep.dequantize_device(t, w.data_ptr(), wf.data_ptr(), M * K, stream)
+        runtime.jsep_sync()
+        ref = (wf.double() @ x.double().t()).t()
+        rel = ((y.double() - ref).abs().max() / ref.abs().max()).item()
+        assert rel <= GEMV_TOL, (t, M, K, rel)
+    for later in runs[1:]:
+        for a, b in zip(runs[0], later):
+            assert torch.equal(a, b)
+
+
 @pytest.mark.parametrize("qtype", [jsep.GGML_TYPE_Q4_K, jsep.GGML_TYPE_Q6_K, jsep.GGML_TYPE_Q8_0])
 def test_streaming_edge_shapes(runtime, qtype):
     """Shapes around the streaming kernel's unit/segment boundaries: rows not
