@@ -140,6 +140,58 @@ def test_q8_0_batched_decode(runtime, name, M, K, N):
     assert O.rel_error(got, O.mul_mat_f64(jsep.GGML_TYPE_Q8_0, w, x)) <= GEMV_TOL
 
 
+@pytest.mark.parametrize("N", [3, 4, 8, 16, 33, 64])
+@pytest.mark.parametrize("qtype,M,K", [(jsep.GGML_TYPE_Q4_K, 4096, 4096), (jsep.GGML_TYPE_Q4_K, 14336, 4096),
+                                       (jsep.GGML_TYPE_Q6_K, 4096, 14336), (jsep.GGML_TYPE_Q6_K, 1024, 3072)])
+def test_kquant_small_batches_vs_torch_fp64(runtime, qtype, M, K, N):
+    """Q4_K / Q6_K with 3 to 64 vectors (several sequences decoding together,
+    short prefill tiles) on the integer tensor-core batched GEMM, split K
+    included; Q6_K 1024 x 3072 has 2520-byte rows (8-byte aligned). Against a
+    float64 matmul of the device-dequantized weights."""
+    import torch
+
+    dev = torch.device("cuda", 0)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(M + K + N)
+    w = synth.weights_torch(gen, qtype, M, K, dev)
+    x = torch.randn(N, K, device=dev, generator=gen)
+    y = torch.empty(N, M, device=dev)
+    torch.cuda.synchronize()  # the library runs on its own stream
+    stream = jsep.library_stream()
+    jsep.mul_mat_device(qtype, w.data_ptr(), w.shape[1], x.data_ptr(), K, y.data_ptr(), M, M, K, N, stream)
+    wf = torch.empty(M, K, device=dev)
+    jsep.dequantize_device(qtype, w.data_ptr(), wf.data_ptr(), M * K, stream)
+    runtime.jsep_sync()
+    ref = (wf.double() @ x.double().t()).t()
+    rel = ((y.double() - ref).abs().max() / ref.abs().max()).item()
+    assert rel <= GEMV_TOL, rel
+
+
+@pytest.mark.parametrize("N", [65, 200])
+def test_q6k_prefill_sizes_vs_torch_fp64(runtime, N):
+    """Q6_K with more than 64 vectors (prefill; several 32-vector tiles) on the
+    batched GEMM: Llama-3.2-3B ffn_down 3072 x 8192."""
+    import torch
+
+    M, K = 3072, 8192
+    dev = torch.device("cuda", 0)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(N)
+    w = synth.weights_torch(gen, jsep.GGML_TYPE_Q6_K, M, K, dev)
+    x = torch.randn(N, K, device=dev, generator=gen)
+    y = torch.empty(N, M, device=dev)
+    torch.cuda.synchronize()
+    stream = jsep.library_stream()
+    jsep.mul_mat_device(jsep.GGML_TYPE_Q6_K, w.data_ptr(), w.shape[1], x.data_ptr(), K, y.data_ptr(), M, M, K, N,
+                        stream)
+    wf = torch.empty(M, K, device=dev)
+    jsep.dequantize_device(jsep.GGML_TYPE_Q6_K, w.data_ptr(), wf.data_ptr(), M * K, stream)
+    runtime.jsep_sync()
+    ref = (wf.double() @ x.double().t()).t()
+    rel = ((y.double() - ref).abs().max() / ref.abs().max()).item()
+    assert rel <= GEMV_TOL, rel
+
+
 @pytest.mark.parametrize("qtype,M,K", [(jsep.GGML_TYPE_Q4_K, 4096, 4096), (jsep.GGML_TYPE_Q4_K, 1024, 4096),
                                        (jsep.GGML_TYPE_Q4_K, 12288, 4096), (jsep.GGML_TYPE_Q4_K, 4096, 12288)])
 def test_qwen3_8b_layer_shapes_vs_torch_fp64(runtime, qtype, M, K):

@@ -1,29 +1,39 @@
-// Small-batch quantized MUL_MAT for Q8_0 weights (N >= 3 activation vectors:
-// several sequences decoding together, the GEMV-to-GEMM crossover) on integer
-// tensor cores (mma.sync m16n8k32, s8 x s8 -> s32).
+// Small-batch quantized MUL_MAT (N >= 3 activation vectors: several sequences
+// decoding together, short prefill tiles, the GEMV-to-GEMM crossover) for
+// Q8_0, Q4_K and Q6_K weights on integer tensor cores (mma.sync m16n8k32,
+// s8 / u8 x s8 -> s32).
 //
 //   y[m + M n] = sum_k W[m, k] x[k + K n]   (ggml MUL_MAT, matmul.ts:10-17)
 //
-// A Q8_0 block is 32 int8 quants q and an f16 scale d: W = d q. One MMA's
-// k = 32 is exactly one block, so every MMA result is scaled by its rows' d
-// in f32 and the quants enter the MMA as they are.
-//
 // Activations: a pre-pass turns x into two int8 limbs per element,
 // x = (l0 + l1 / 128) / s with s = 127 / max|x| per 256 elements and vector
-// (|error| <= max|x| / 32512), stored as [N][2][K] with the factors 1 / s as
-// [K / 256][N rounded up to 4]. The eight B columns of an MMA are four vectors
-// x two limbs.
+// (|error| <= max|x| / 32512), stored as [N][2][K], with the factors 1 / s as
+// [K / 256][N rounded up to 4] and, for Q4_K, the f32 sums of x over each
+// 16-element sub-block as [K / 256][N rounded up to 4][16]. The eight B
+// columns of an MMA are four vectors x two limbs.
+//
+// Weights, per 32-element MMA step (k = 32):
+//  - Q8_0: one block; the s8 quants enter the MMA as they are and the s32
+//    result is scaled by the rows' f16 d in f32;
+//  - Q4_K: one 32-element sub-block; its u8 nibbles, the low ones as they are
+//    and the high ones in place (16 q), times the 6-bit scale (16 sc for the
+//    low-nibble sub-blocks) in integer over the 256-element block, then
+//    d / (16 s); the mins through the sub-block sums of x;
+//  - Q6_K: two 16-element sub-blocks, one MMA each (the other half of the A
+//    fragment zero); the quants q - 32 enter the MMA as s8 (a 6-bit sign
+//    extension), times the int8 scale in integer, then d / s.
 //
 // Tiling: a CTA (4 warps) computes 64 rows x NV vectors (NV = 8 .. 64); warp w
-// rows 16 w .. 16 w + 15. K is walked in chunks of 256 (8 blocks): the chunk's
-// raw rows (64 x 272 B) and limbs (NV x 2 x 256 B) go to shared memory with
-// cp.async, 2 to 4 chunks in flight. Q8_0 blocks are 34 bytes, so a block sits at any
-// even offset: A fragments come from aligned 32-bit loads and a funnel shift;
-// B fragments from ldmatrix.
+// rows 16 w .. 16 w + 15. K is walked in chunks of 256 elements (8 Q8_0
+// blocks, one K-quant block): the chunk's raw rows, limbs, factors and sums go
+// to shared memory with cp.async, 2 to 4 chunks in flight. Q8_0 and Q6_K
+// blocks are 34 and 210 bytes, so they sit at any even offset: their A
+// fragments come from aligned 32-bit loads and a funnel shift; Q4_K rows are
+// 16-byte aligned. B fragments come from ldmatrix.
 //
-// Split K: grids below one wave of two CTAs per SM split the chunks S ways (grid z); each
-// split stores its tile in workspace and the tile's last split sums the S
-// tiles in split order (deterministic).
+// Split K: grids below one wave of two CTAs per SM split the chunks S ways
+// (grid z); each split stores its tile in workspace and the tile's last split
+// sums the S tiles in split order (deterministic).
 #include <cuda_fp16.h>
 #include <stdint.h>
 
@@ -37,17 +47,29 @@ constexpr int kRowsB = 64;                  // rows per CTA
 constexpr int kWarpsB = 4;
 constexpr int kThreadsB = 32 * kWarpsB;
 constexpr int kChunk = 256;                 // K per stage
-constexpr int kWRow = 272;                  // bytes of a row's chunk (8 blocks x 34)
 constexpr int kXRow = kChunk + 16;          // bytes of a limb row in shared memory (ldmatrix bank spread)
 constexpr int kMaxVec = 64;
 constexpr int kSlotsB = 2 * 148;            // CTAs resident at once
 constexpr int kMaxSplitsB = 16;
+
+// Shared-memory bytes of one row's chunk (16-byte pieces copied): Q8_0 8 x 34
+// = 272; Q4_K one 144-byte block; Q6_K one 210-byte block at any even offset
+// in a 240-byte window (60 words: the 8 rows a warp reads hit 8 bank groups).
+template <int TYPE>
+__host__ __device__ constexpr int row_stride() {
+    return TYPE == kTypeQ8_0 ? 272 : (TYPE == kTypeQ4_K ? 144 : 240);
+}
+template <int TYPE>
+__host__ __device__ constexpr int sum_floats() {  // x sub-block sums per vector and chunk
+    return TYPE == kTypeQ4_K ? 16 : 0;
+}
 
 struct BatchedArgs {
     const uint8_t* w;
     int64_t w_nb1;
     const int8_t* xl;      // limbs [N][2][K]
     const float* inv_s;    // [K / 256][n_pad]
+    const float* xsum;     // [K / 256][n_pad][16] (Q4_K)
     float* y;
     int64_t y_nb1;         // bytes between output vectors
     int32_t M, K, N, n_pad;
@@ -56,9 +78,9 @@ struct BatchedArgs {
     unsigned* counters;    // [tile]
 };
 
-template <int NV>
+template <int TYPE, int NV>
 __host__ __device__ constexpr int stage_bytes() {
-    return kRowsB * kWRow + NV * 2 * kXRow + NV * 4;
+    return kRowsB * row_stride<TYPE>() + NV * 2 * kXRow + NV * 4 + NV * 4 * sum_floats<TYPE>();
 }
 // Pipeline depth: enough bytes in flight per SM (two CTAs) to cover the HBM
 // latency, within the shared memory of two CTAs.
@@ -96,6 +118,14 @@ __device__ __forceinline__ void imma_s8(int (&d)[4], uint32_t a0, uint32_t a1, u
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
 }
 
+// D = A (16x32 u8, row) * B (32x8 s8, col), s32.
+__device__ __forceinline__ void imma_u8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                        uint32_t b1) {
+    asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};"
+        : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
+}
+
 // 4 bytes at a 2-byte-aligned shared address.
 __device__ __forceinline__ uint32_t lds_u32_any(const uint8_t* p) {
     const uint32_t mis = static_cast<uint32_t>(reinterpret_cast<uintptr_t>(p) & 3);
@@ -103,9 +133,67 @@ __device__ __forceinline__ uint32_t lds_u32_any(const uint8_t* p) {
     return __funnelshift_r(q[0], q[1], mis * 8);
 }
 
+// The eight (scale, min) pairs of a Q4_K block header h (get_scale_min_k4,
+// src/inference/jsep/ops/matmul.ts:408-424): sc as an int, times 16 for the
+// even (low-nibble) sub-blocks, whose quants enter the MMA unscaled; the mins
+// as dmin * m.
+__device__ __forceinline__ void q4k_scales8(const uint4 h, int (&sc)[8], float (&mdm)[8], float& d) {
+    d = f16_bits_to_f32(h.x & 0xFFFFu);
+    const float dmin = f16_bits_to_f32(h.x >> 16);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        const uint32_t sel = 0x4440u + static_cast<uint32_t>(j & 3);  // byte j%4, zero-extended
+        uint32_t scv, mv;
+        if (j < 4) {
+            scv = __byte_perm(h.y, 0u, sel) & 63u;
+            mv = __byte_perm(h.z, 0u, sel) & 63u;
+        } else {
+            const uint32_t b1 = __byte_perm(h.y, 0u, sel), b2 = __byte_perm(h.z, 0u, sel), b3 = __byte_perm(h.w, 0u, sel);
+            scv = (b3 & 15u) | ((b1 >> 2) & 0x30u);
+            mv = (b3 >> 4) | ((b2 >> 2) & 0x30u);
+        }
+        sc[j] = static_cast<int>(scv << ((j & 1) ? 0 : 4));
+        mdm[j] = dmin * static_cast<float>(mv);
+    }
+}
+
+// The scale of sub-block j alone (as in q4k_scales8).
+__device__ __forceinline__ int q4k_scale_j(const uint4 h, int j) {
+    const uint32_t sel = 0x4440u + static_cast<uint32_t>(j & 3);
+    uint32_t scv;
+    if (j < 4) {
+        scv = __byte_perm(h.y, 0u, sel) & 63u;
+    } else {
+        const uint32_t b1 = __byte_perm(h.y, 0u, sel), b3 = __byte_perm(h.w, 0u, sel);
+        scv = (b3 & 15u) | ((b1 >> 2) & 0x30u);
+    }
+    return static_cast<int>(scv << ((j & 1) ? 0 : 4));
+}
+
+// The A operand of 32-element group t of one Q6_K half-block at one fragment
+// position: ql0 / ql1 hold four bytes of the half's low-quant chunks 0 / 1
+// (ql[64h + l], ql[64h + 32 + l]), qh the four matching high-bit bytes
+// (qh[32h + l]). Group t holds the 6-bit quants (0..63) of elements
+// 128h + 32t + l: the low nibble of chunk t&1 for t < 2, the high nibble for
+// t >= 2, and bits 2t, 2t+1 of qh as bits 4, 5 (ggml's dequantize_row_q6_K
+// layout; the reference has no Q6_K code of its own).
+__device__ __forceinline__ uint32_t q6k_group(uint32_t ql0, uint32_t ql1, uint32_t qh, int t) {
+    const uint32_t ql = (t & 1) ? ql1 : ql0;
+    const uint32_t lo = ((t & 2) ? (ql >> 4) : ql) & 0x0F0F0F0Fu;
+    return lo | (((qh >> (2 * t)) & 0x03030303u) << 4);
+}
+
+// Four 6-bit quants q (0..63, one per byte) -> the int8 bytes q - 32: q ^ 32
+// is q - 32 as a 6-bit two's-complement number; copy its sign bit (bit 5)
+// into bits 6 and 7.
+__device__ __forceinline__ uint32_t q6_signed(uint32_t q) {
+    const uint32_t t = q ^ 0x20202020u, s = t & 0x20202020u;
+    return t | (s << 1) | (s << 2);
+}
+
 // Pre-pass: one warp per (vector, 256-element block).
 __global__ void x_limbs_kernel(const float* __restrict__ x, int64_t x_nb1, int8_t* __restrict__ xl,
-                               float* __restrict__ inv_s, int K, int N, int n_pad) {
+                               float* __restrict__ inv_s, float* __restrict__ xsum, int K, int N, int n_pad) {
     const int lane = threadIdx.x & 31;
     const int nblk = K / 256;
     const int64_t item = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
@@ -145,12 +233,20 @@ __global__ void x_limbs_kernel(const float* __restrict__ x, int64_t x_nb1, int8_
         *reinterpret_cast<uint2*>(base + K) = make_uint2(l1[0], l1[1]);
     }
     if (lane == 0) inv_s[static_cast<int64_t>(b) * n_pad + n] = mx * (1.f / 127.f);
+    if (xsum) {
+        // 16-element sums: lanes 2i, 2i+1 hold sub-block i
+        const float s8 = ((v[0] + v[1]) + (v[2] + v[3])) + ((v[4] + v[5]) + (v[6] + v[7]));
+        const float s16 = s8 + __shfl_xor_sync(0xffffffffu, s8, 1);
+        if ((lane & 1) == 0) xsum[(static_cast<int64_t>(b) * n_pad + n) * 16 + (lane >> 1)] = s16;
+    }
 }
 
-template <int NV>
-__global__ void __launch_bounds__(kThreadsB, 2) batched_q8_kernel(const __grid_constant__ BatchedArgs P) {
+template <int TYPE, int NV>
+__global__ void __launch_bounds__(kThreadsB, 2) batched_kernel(const __grid_constant__ BatchedArgs P) {
     extern __shared__ __align__(128) uint8_t smem[];
-    constexpr int SB = stage_bytes<NV>();
+    constexpr int RS = row_stride<TYPE>();
+    constexpr int RP = TYPE == kTypeQ8_0 ? 17 : (TYPE == kTypeQ4_K ? 9 : 14);  // 16-byte pieces per row (Q6_K: 14 cover any offset)
+    constexpr int SB = stage_bytes<TYPE, NV>();
     constexpr int NT = NV / 4;  // MMA column tiles: 4 vectors x 2 limbs each
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int g = lane >> 2, c = lane & 3;
@@ -159,18 +255,32 @@ __global__ void __launch_bounds__(kThreadsB, 2) batched_q8_kernel(const __grid_c
     const int ch0 = blockIdx.z * P.chunks_per_split;
     const int nch = min(nchunks - ch0, P.chunks_per_split);
 
-    // one chunk's copies: 64 rows x 17 pieces of 16 B, NV x 2 limb rows x 16
-    // pieces, NV factors (16 B pieces of 4)
+    // one chunk's copies: 64 rows x RP pieces of 16 B, NV x 2 limb rows x 16
+    // pieces, NV factors (16 B pieces of 4), NV x 16 sums
     auto load = [&](int ch, int buf) {
         uint8_t* sw = smem + buf * SB;
-        uint8_t* sx = sw + kRowsB * kWRow;
+        uint8_t* sx = sw + kRowsB * RS;
         uint8_t* ss = sx + NV * 2 * kXRow;
+        uint8_t* su = ss + NV * 4;
         const int k0 = (ch0 + ch) * kChunk;
-        for (int i = threadIdx.x; i < kRowsB * 17; i += kThreadsB) {
-            const int r = i / 17, pc = i - r * 17;
-            const bool ok = m0 + r < P.M;
-            const uint8_t* src = P.w + static_cast<int64_t>(ok ? m0 + r : 0) * P.w_nb1 + (k0 / 32) * 34 + 16 * pc;
-            cp_async16(sw + r * kWRow + 16 * pc, src, ok);
+        for (int i = threadIdx.x; i < kRowsB * RP; i += kThreadsB) {
+            const int r = i / RP, pc = i - r * RP;
+            bool ok = m0 + r < P.M;
+            const uint8_t* row = P.w + static_cast<int64_t>(ok ? m0 + r : 0) * P.w_nb1;
+            const uint8_t* src;
+            if (TYPE == kTypeQ8_0) {
+                src = row + (k0 / 32) * 34 + 16 * pc;
+            } else if (TYPE == kTypeQ4_K) {
+                src = row + (k0 / 256) * 144 + 16 * pc;
+            } else {
+                // the 16-byte pieces that meet the 210-byte block (none past the
+                // 16-byte boundary after its last byte)
+                const uintptr_t a = reinterpret_cast<uintptr_t>(row + (k0 / 256) * 210);
+                const uintptr_t ga = a & ~uintptr_t(15);
+                ok = ok && ga + 16 * pc < a + 210;
+                src = reinterpret_cast<const uint8_t*>(ga + 16 * pc);
+            }
+            cp_async16(sw + r * RS + 16 * pc, ok ? src : P.w, ok);
         }
         for (int i = threadIdx.x; i < NV * 2 * 16; i += kThreadsB) {
             const int rowl = i >> 4, pc = i & 15;  // rowl = 2 v + limb
@@ -184,11 +294,29 @@ __global__ void __launch_bounds__(kThreadsB, 2) batched_q8_kernel(const __grid_c
             const bool ok = n0 + v < P.n_pad;
             cp_async16(ss + 16 * i, P.inv_s + static_cast<int64_t>(ch0 + ch) * P.n_pad + (ok ? n0 + v : 0), ok);
         }
+        if (TYPE == kTypeQ4_K) {
+            for (int i = threadIdx.x; i < NV * 4; i += kThreadsB) {
+                const int v = i >> 2, pc = i & 3;
+                const bool ok = n0 + v < P.n_pad;
+                cp_async16(su + 16 * i,
+                           P.xsum + (static_cast<int64_t>(ch0 + ch) * P.n_pad + (ok ? n0 + v : 0)) * 16 + 4 * pc, ok);
+            }
+        }
     };
 
     float acc[NT][2];
 #pragma unroll
     for (int t = 0; t < NT; ++t) acc[t][0] = acc[t][1] = 0.f;
+
+    // ldmatrix row address: matrix mi = lane/8 (column tile 2 tp + mi/2, k half mi&1),
+    // row rr = lane%8 = B column: vector rr/2, limb rr&1
+    const int mi = lane >> 3, rr = lane & 7;
+    const uint32_t xoff = static_cast<uint32_t>((2 * (4 * (mi >> 1) + (rr >> 1)) + (rr & 1)) * kXRow + 16 * (mi & 1));
+    // Q6_K: where row g / g+8's block sits in its 16-byte window (the window
+    // offset changes by 210 mod 16 from chunk to chunk)
+    const uintptr_t rowg_addr =
+        reinterpret_cast<uintptr_t>(P.w) + static_cast<uintptr_t>(static_cast<int64_t>(m0 + 16 * warp + g) * P.w_nb1);
+    const uintptr_t rowh_addr = rowg_addr + static_cast<uintptr_t>(8 * P.w_nb1);
 
     constexpr int ST = stages_of<NV>();
 #pragma unroll
@@ -202,40 +330,154 @@ __global__ void __launch_bounds__(kThreadsB, 2) batched_q8_kernel(const __grid_c
         if (ch + ST - 1 < nch) load(ch + ST - 1, (ch + ST - 1) % ST);
         cp_async_commit();
         const uint8_t* sw = smem + (ch % ST) * SB;
-        const uint8_t* sx = sw + kRowsB * kWRow;
+        const uint8_t* sx = sw + kRowsB * RS;
         const float* ss = reinterpret_cast<const float*>(sx + NV * 2 * kXRow);
+        const float* su = ss + NV;
+        const uint32_t xbase = smem_u32(sx) + xoff;
+        const uint8_t* rg = sw + (16 * warp + g) * RS;
+        const uint8_t* rh = rg + 8 * RS;
         float is[NT];  // 1 / s of this lane's vector in each column tile
 #pragma unroll
         for (int t = 0; t < NT; ++t) is[t] = ss[4 * t + c];
-        const uint8_t* rg = sw + (16 * warp + g) * kWRow;
-        const uint8_t* rh = rg + 8 * kWRow;
-        // ldmatrix row address: matrix mi = lane/8 (column tile 2 tp + mi/2, k half mi&1),
-        // row rr = lane%8 = B column: vector rr/2, limb rr&1
-        const int mi = lane >> 3, rr = lane & 7;
-        const uint32_t xbase = smem_u32(sx) + static_cast<uint32_t>((2 * (4 * (mi >> 1) + (rr >> 1)) + (rr & 1)) * kXRow +
-                                                                    16 * (mi & 1));
+
+        if (TYPE == kTypeQ8_0) {
 #pragma unroll
-        for (int b = 0; b < 8; ++b) {
-            const uint8_t* bg = rg + 34 * b;
-            const uint8_t* bh = rh + 34 * b;
-            const float dg = f16_bits_to_f32(*reinterpret_cast<const uint16_t*>(bg));
-            const float dh = f16_bits_to_f32(*reinterpret_cast<const uint16_t*>(bh));
-            const uint32_t a0 = lds_u32_any(bg + 2 + 4 * c), a1 = lds_u32_any(bh + 2 + 4 * c);
-            const uint32_t a2 = lds_u32_any(bg + 18 + 4 * c), a3 = lds_u32_any(bh + 18 + 4 * c);
+            for (int b = 0; b < 8; ++b) {
+                const uint8_t* bg = rg + 34 * b;
+                const uint8_t* bh = rh + 34 * b;
+                const float dg = f16_bits_to_f32(*reinterpret_cast<const uint16_t*>(bg));
+                const float dh = f16_bits_to_f32(*reinterpret_cast<const uint16_t*>(bh));
+                const uint32_t a0 = lds_u32_any(bg + 2 + 4 * c), a1 = lds_u32_any(bh + 2 + 4 * c);
+                const uint32_t a2 = lds_u32_any(bg + 18 + 4 * c), a3 = lds_u32_any(bh + 18 + 4 * c);
 #pragma unroll
-            for (int tp = 0; tp < NT / 2; ++tp) {
-                uint32_t xb[4];
-                ldmatrix_x4(xb, xbase + static_cast<uint32_t>(tp * 8 * 2 * kXRow + 32 * b));
+                for (int tp = 0; tp < NT / 2; ++tp) {
+                    uint32_t xb[4];
+                    ldmatrix_x4(xb, xbase + static_cast<uint32_t>(tp * 8 * 2 * kXRow + 32 * b));
 #pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    const int t = 2 * tp + h;
-                    int D[4];
-                    imma_s8(D, a0, a1, a2, a3, xb[2 * h], xb[2 * h + 1]);
-                    const float vg = fmaf(static_cast<float>(D[1]), 0.0078125f, static_cast<float>(D[0]));
-                    const float vh = fmaf(static_cast<float>(D[3]), 0.0078125f, static_cast<float>(D[2]));
-                    acc[t][0] = fmaf(vg, dg * is[t], acc[t][0]);
-                    acc[t][1] = fmaf(vh, dh * is[t], acc[t][1]);
+                    for (int h = 0; h < 2; ++h) {
+                        const int t = 2 * tp + h;
+                        int D[4];
+                        imma_s8(D, a0, a1, a2, a3, xb[2 * h], xb[2 * h + 1]);
+                        const float vg = fmaf(static_cast<float>(D[1]), 0.0078125f, static_cast<float>(D[0]));
+                        const float vh = fmaf(static_cast<float>(D[3]), 0.0078125f, static_cast<float>(D[2]));
+                        acc[t][0] = fmaf(vg, dg * is[t], acc[t][0]);
+                        acc[t][1] = fmaf(vh, dh * is[t], acc[t][1]);
+                    }
                 }
+            }
+        } else if (TYPE == kTypeQ4_K) {
+            const uint4 hg = *reinterpret_cast<const uint4*>(rg), hh4 = *reinterpret_cast<const uint4*>(rh);
+            // |D| <= 32 * 240 * 127 per sub-block, times sc <= 63 (or 16 sc with
+            // the unscaled low nibbles), over 8 sub-blocks: inside int32
+            int a[NT][4];
+#pragma unroll
+            for (int t = 0; t < NT; ++t) a[t][0] = a[t][1] = a[t][2] = a[t][3] = 0;
+#pragma unroll 1
+            for (int p = 0; p < 4; ++p) {
+                // fragment words of sub-block pair p (qs bytes 32p .. 32p+31): row
+                // g / g+8, k 4c.. / 16+4c..
+                const uint32_t w0 = *reinterpret_cast<const uint32_t*>(rg + 16 + 32 * p + 4 * c);
+                const uint32_t w1 = *reinterpret_cast<const uint32_t*>(rh + 16 + 32 * p + 4 * c);
+                const uint32_t w2 = *reinterpret_cast<const uint32_t*>(rg + 32 + 32 * p + 4 * c);
+                const uint32_t w3 = *reinterpret_cast<const uint32_t*>(rh + 32 + 32 * p + 4 * c);
+#pragma unroll
+                for (int hi = 0; hi < 2; ++hi) {
+                    const int j = 2 * p + hi;
+                    const uint32_t msk = hi ? 0xF0F0F0F0u : 0x0F0F0F0Fu;
+                    const int scj = q4k_scale_j(hg, j), shj = q4k_scale_j(hh4, j);
+#pragma unroll
+                    for (int tp = 0; tp < NT / 2; ++tp) {
+                        uint32_t xb[4];
+                        ldmatrix_x4(xb, xbase + static_cast<uint32_t>(tp * 8 * 2 * kXRow + 32 * j));
+#pragma unroll
+                        for (int h = 0; h < 2; ++h) {
+                            const int t = 2 * tp + h;
+                            int D[4];
+                            imma_u8(D, w0 & msk, w1 & msk, w2 & msk, w3 & msk, xb[2 * h], xb[2 * h + 1]);
+                            a[t][0] += scj * D[0];
+                            a[t][1] += scj * D[1];
+                            a[t][2] += shj * D[2];
+                            a[t][3] += shj * D[3];
+                        }
+                    }
+                }
+            }
+            int scg[8], sch[8];
+            float mg[8], mh[8], dg, dh;
+            q4k_scales8(hg, scg, mg, dg);
+            q4k_scales8(hh4, sch, mh, dh);
+#pragma unroll
+            for (int t = 0; t < NT; ++t) {
+                const float* xs = su + (4 * t + c) * 16;  // the lane's vector's 16-element sums
+                float og = 0.f, oh = 0.f;
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    const float X = xs[2 * j] + xs[2 * j + 1];
+                    og = fmaf(mg[j], X, og);
+                    oh = fmaf(mh[j], X, oh);
+                }
+                const float f = is[t] * 0.0625f;
+                acc[t][0] += fmaf(dg * fmaf(static_cast<float>(a[t][1]), 0.0078125f, static_cast<float>(a[t][0])), f, -og);
+                acc[t][1] += fmaf(dh * fmaf(static_cast<float>(a[t][3]), 0.0078125f, static_cast<float>(a[t][2])), f, -oh);
+            }
+        } else {
+            // Q6_K: the block of row g / g+8 at its offset in the 16-byte window
+            const uintptr_t boff = static_cast<uintptr_t>((ch0 + ch) * 210);
+            const uint8_t* pg = rg + ((rowg_addr + boff) & 15);
+            const uint8_t* ph = rh + ((rowh_addr + boff) & 15);
+            // |D| <= 16 * 32 * 127 per sub-block, times |sc| <= 128, over 16
+            // sub-blocks: inside int32
+            int a[NT][4];
+#pragma unroll
+            for (int t = 0; t < NT; ++t) a[t][0] = a[t][1] = a[t][2] = a[t][3] = 0;
+#pragma unroll 1
+            for (int h = 0; h < 2; ++h) {
+                // the fragment words of half h at position r (0: row g k 4c.., 1: row
+                // g+8, 2: row g k 16+4c.., 3: row g+8): low-quant chunks 0, 1, high bits
+                uint32_t q0[4], q1[4], qb[4];
+#pragma unroll
+                for (int r = 0; r < 4; ++r) {
+                    const uint8_t* b = ((r & 1) ? ph : pg) + 4 * c + 16 * (r >> 1);
+                    q0[r] = lds_u32_any(b + 64 * h);
+                    q1[r] = lds_u32_any(b + 64 * h + 32);
+                    qb[r] = lds_u32_any(b + 128 + 32 * h);
+                }
+#pragma unroll 1
+                for (int gi = 0; gi < 4; ++gi) {  // elements 32i .. 32i+31 (i = 4h + gi): sub-blocks 2i, 2i+1
+                    const int i = 4 * h + gi;
+                    uint32_t A[4];
+#pragma unroll
+                    for (int r = 0; r < 4; ++r) A[r] = q6_signed(q6k_group(q0[r], q1[r], qb[r], gi));
+                    const int sge = static_cast<int>(*reinterpret_cast<const int8_t*>(pg + 192 + 2 * i));
+                    const int sgo = static_cast<int>(*reinterpret_cast<const int8_t*>(pg + 193 + 2 * i));
+                    const int she = static_cast<int>(*reinterpret_cast<const int8_t*>(ph + 192 + 2 * i));
+                    const int sho = static_cast<int>(*reinterpret_cast<const int8_t*>(ph + 193 + 2 * i));
+#pragma unroll
+                    for (int tp = 0; tp < NT / 2; ++tp) {
+                        uint32_t xb[4];
+                        ldmatrix_x4(xb, xbase + static_cast<uint32_t>(tp * 8 * 2 * kXRow + 32 * i));
+#pragma unroll
+                        for (int hh = 0; hh < 2; ++hh) {
+                            const int t = 2 * tp + hh;
+                            int De[4], Do[4];
+                            imma_s8(De, A[0], A[1], 0u, 0u, xb[2 * hh], xb[2 * hh + 1]);
+                            imma_s8(Do, 0u, 0u, A[2], A[3], xb[2 * hh], xb[2 * hh + 1]);
+                            a[t][0] += sge * De[0] + sgo * Do[0];
+                            a[t][1] += sge * De[1] + sgo * Do[1];
+                            a[t][2] += she * De[2] + sho * Do[2];
+                            a[t][3] += she * De[3] + sho * Do[3];
+                        }
+                    }
+                }
+            }
+            const float dg = f16_bits_to_f32(*reinterpret_cast<const uint16_t*>(pg + 208));
+            const float dh = f16_bits_to_f32(*reinterpret_cast<const uint16_t*>(ph + 208));
+#pragma unroll
+            for (int t = 0; t < NT; ++t) {
+                acc[t][0] = fmaf(dg * is[t], fmaf(static_cast<float>(a[t][1]), 0.0078125f, static_cast<float>(a[t][0])),
+                                 acc[t][0]);
+                acc[t][1] = fmaf(dh * is[t], fmaf(static_cast<float>(a[t][3]), 0.0078125f, static_cast<float>(a[t][2])),
+                                 acc[t][1]);
             }
         }
     }
@@ -284,10 +526,16 @@ __global__ void __launch_bounds__(kThreadsB, 2) batched_q8_kernel(const __grid_c
     }
 }
 
-int pick_nv(int N) { return N <= 8 ? 8 : (N <= 16 ? 16 : (N <= 32 ? 32 : 64)); }
+// Vectors per CTA tile: N rounded up to 8, 16, 32 or 64 (Q6_K at most 32:
+// its two MMAs per 32 elements need the registers of the wider tile).
+int pick_nv(const MulMatOp& o) {
+    const int N = o.N, cap = o.type == kTypeQ6_K ? 32 : 64;
+    const int nv = N <= 8 ? 8 : (N <= 16 ? 16 : (N <= 32 ? 32 : 64));
+    return nv < cap ? nv : cap;
+}
 
 void plan(const MulMatOp& o, int* nv, int* splits, int* cps) {
-    *nv = pick_nv(o.N);
+    *nv = pick_nv(o);
     const int tiles = ((o.M + kRowsB - 1) / kRowsB) * ((o.N + *nv - 1) / *nv);
     const int nchunks = o.K / kChunk;
     int s = kSlotsB / tiles;                         // at most one wave of two CTAs per SM
@@ -298,10 +546,14 @@ void plan(const MulMatOp& o, int* nv, int* splits, int* cps) {
     *splits = (nchunks + *cps - 1) / *cps;           // no empty split
 }
 
+int n_pad_of(const MulMatOp& o) { return (o.N + 3) & ~3; }
 size_t limbs_bytes(const MulMatOp& o) { return (static_cast<size_t>(o.N) * 2 * o.K + 255) & ~size_t(255); }
 size_t factors_bytes(const MulMatOp& o) {
-    const int n_pad = (o.N + 3) & ~3;
-    return (static_cast<size_t>(o.K / 256) * n_pad * 4 + 255) & ~size_t(255);
+    return (static_cast<size_t>(o.K / 256) * n_pad_of(o) * 4 + 255) & ~size_t(255);
+}
+size_t sums_bytes(const MulMatOp& o) {
+    if (o.type != kTypeQ4_K) return 0;
+    return (static_cast<size_t>(o.K / 256) * n_pad_of(o) * 16 * 4 + 255) & ~size_t(255);
 }
 size_t partial_bytes(const MulMatOp& o) {
     int nv, s, cps;
@@ -311,31 +563,53 @@ size_t partial_bytes(const MulMatOp& o) {
     return tiles * s * kMaxVec * kRowsB * 4 + tiles * 4;
 }
 
-template <int NV>
+template <int TYPE, int NV>
 cudaError_t launch_nv(const BatchedArgs& P, dim3 grid, cudaStream_t stream) {
-    constexpr int smem = stages_of<NV>() * stage_bytes<NV>();
+    constexpr int smem = stages_of<NV>() * stage_bytes<TYPE, NV>();
     static bool configured = false;
     if (!configured) {
         const cudaError_t e =
-            cudaFuncSetAttribute(batched_q8_kernel<NV>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+            cudaFuncSetAttribute(batched_kernel<TYPE, NV>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         if (e != cudaSuccess) return e;
         configured = true;
     }
-    batched_q8_kernel<NV><<<grid, kThreadsB, smem, stream>>>(P);
+    batched_kernel<TYPE, NV><<<grid, kThreadsB, smem, stream>>>(P);
     return cudaGetLastError();
+}
+
+template <int TYPE>
+cudaError_t launch_type(int nv, const BatchedArgs& P, dim3 grid, cudaStream_t stream) {
+    switch (nv) {
+        case 8: return launch_nv<TYPE, 8>(P, grid, stream);
+        case 16: return launch_nv<TYPE, 16>(P, grid, stream);
+        case 32: return launch_nv<TYPE, 32>(P, grid, stream);
+        default: return launch_nv<TYPE, 64>(P, grid, stream);
+    }
+}
+template <>
+cudaError_t launch_type<kTypeQ6_K>(int nv, const BatchedArgs& P, dim3 grid, cudaStream_t stream) {
+    switch (nv) {
+        case 8: return launch_nv<kTypeQ6_K, 8>(P, grid, stream);
+        case 16: return launch_nv<kTypeQ6_K, 16>(P, grid, stream);
+        default: return launch_nv<kTypeQ6_K, 32>(P, grid, stream);
+    }
 }
 
 }  // namespace
 
 bool batched_supported(const MulMatOp& o) {
-    if (o.type != kTypeQ8_0 || o.N < 3 || o.ne2 != 1 || o.ne3 != 1) return false;
+    if (o.type != kTypeQ8_0 && o.type != kTypeQ4_K && o.type != kTypeQ6_K) return false;
+    if (o.N < 3 || o.ne2 != 1 || o.ne3 != 1) return false;
     if (o.K % 256 != 0 || o.M < 1) return false;
-    if ((reinterpret_cast<uintptr_t>(o.w) | static_cast<uintptr_t>(o.w_nb1)) & 15) return false;  // 16-byte copies
+    const uintptr_t wa = reinterpret_cast<uintptr_t>(o.w) | static_cast<uintptr_t>(o.w_nb1);
+    if (o.type == kTypeQ6_K ? (wa & 1) : (wa & 15)) return false;  // 16-byte copies (Q6_K: 2-byte loads)
     if ((reinterpret_cast<uintptr_t>(o.x) | static_cast<uintptr_t>(o.x_nb1)) & 15) return false;  // float4 reads
     return true;
 }
 
-size_t batched_workspace_bytes(const MulMatOp& o) { return limbs_bytes(o) + factors_bytes(o) + partial_bytes(o) + 256; }
+size_t batched_workspace_bytes(const MulMatOp& o) {
+    return limbs_bytes(o) + factors_bytes(o) + sums_bytes(o) + partial_bytes(o) + 256;
+}
 
 int launch_batched(const MulMatOp& o, void* workspace, size_t workspace_bytes, cudaStream_t stream) {
     if (!batched_supported(o)) return -static_cast<int>(cudaErrorInvalidValue);
@@ -349,17 +623,18 @@ int launch_batched(const MulMatOp& o, void* workspace, size_t workspace_bytes, c
     P.w_nb1 = o.w_nb1;
     P.xl = reinterpret_cast<int8_t*>(ws);
     P.inv_s = reinterpret_cast<float*>(ws + limbs_bytes(o));
+    P.xsum = o.type == kTypeQ4_K ? reinterpret_cast<float*>(ws + limbs_bytes(o) + factors_bytes(o)) : nullptr;
     P.y = o.y;
     P.y_nb1 = o.y_nb1;
     P.M = o.M;
     P.K = o.K;
     P.N = o.N;
-    P.n_pad = (o.N + 3) & ~3;
+    P.n_pad = n_pad_of(o);
     P.splits = splits;
     P.chunks_per_split = cps;
     const int tiles_m = (o.M + kRowsB - 1) / kRowsB, tiles_n = (o.N + nv - 1) / nv;
     if (splits > 1) {
-        P.partial = reinterpret_cast<float*>(ws + limbs_bytes(o) + factors_bytes(o));
+        P.partial = reinterpret_cast<float*>(ws + limbs_bytes(o) + factors_bytes(o) + sums_bytes(o));
         P.counters = reinterpret_cast<unsigned*>(P.partial + static_cast<size_t>(tiles_m) * tiles_n * splits * kMaxVec * kRowsB);
         const cudaError_t e = cudaMemsetAsync(P.counters, 0, static_cast<size_t>(tiles_m) * tiles_n * 4, stream);
         if (e != cudaSuccess) return -static_cast<int>(e);
@@ -367,19 +642,18 @@ int launch_batched(const MulMatOp& o, void* workspace, size_t workspace_bytes, c
     {
         const int64_t items = static_cast<int64_t>(P.n_pad) * (o.K / 256);
         const int64_t blocks = (items * 32 + 255) / 256;
-        x_limbs_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(o.x, o.x_nb1, const_cast<int8_t*>(P.xl),
-                                                                          const_cast<float*>(P.inv_s), o.K, o.N,
-                                                                          P.n_pad);
+        x_limbs_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
+            o.x, o.x_nb1, const_cast<int8_t*>(P.xl), const_cast<float*>(P.inv_s), const_cast<float*>(P.xsum), o.K, o.N,
+            P.n_pad);
         const cudaError_t e = cudaGetLastError();
         if (e != cudaSuccess) return -static_cast<int>(e);
     }
     const dim3 grid(tiles_m, tiles_n, splits);
     cudaError_t e;
-    switch (nv) {
-        case 8: e = launch_nv<8>(P, grid, stream); break;
-        case 16: e = launch_nv<16>(P, grid, stream); break;
-        case 32: e = launch_nv<32>(P, grid, stream); break;
-        default: e = launch_nv<64>(P, grid, stream); break;
+    switch (o.type) {
+        case kTypeQ8_0: e = launch_type<kTypeQ8_0>(nv, P, grid, stream); break;
+        case kTypeQ4_K: e = launch_type<kTypeQ4_K>(nv, P, grid, stream); break;
+        default: e = launch_type<kTypeQ6_K>(nv, P, grid, stream); break;
     }
     return e == cudaSuccess ? 2 : -static_cast<int>(e);
 }

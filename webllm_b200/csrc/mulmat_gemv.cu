@@ -255,8 +255,8 @@ size_t mulmat_workspace_bytes(const MulMatOp* ops, int n_ops) {
 int launch_mulmat(const MulMatOp* ops, int n_ops, cudaStream_t stream, int num_sms, void* workspace,
                   size_t workspace_bytes) {
     if (n_ops < 1 || n_ops > kMaxOpsPerLaunch) return -static_cast<int>(cudaErrorInvalidValue);
-    // prefill-sized ops (Q4_K) and small batches (Q8_0) run as tensor-core GEMMs, one
-    // launch each; the rest together
+    // prefill-sized ops (Q4_K, N >= 65) and small batches (N >= 3, every type) run as
+    // tensor-core GEMMs, one launch each; the rest together
     int launched = 0;
     MulMatOp rest[kMaxOpsPerLaunch];
     int n_rest = 0;

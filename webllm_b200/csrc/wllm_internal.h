@@ -93,9 +93,9 @@ size_t prefill_min_workspace_bytes(const MulMatOp& op);
 int launch_prefill(const MulMatOp& op, void* workspace, size_t workspace_bytes, cudaStream_t stream);
 unsigned read_and_clear_prefill_error();
 
-// Small-batch GEMM (mulmat_batched.cu): Q8_0 weights with N >= 3 vectors on
-// integer tensor cores; workspace holds the activation limbs (and split-K
-// partial tiles). Returns the number of kernels launched (2) or a negative
+// Small-batch GEMM (mulmat_batched.cu): Q8_0, Q4_K and Q6_K weights with
+// N >= 3 vectors on integer tensor cores; workspace holds the activation limbs,
+// factors and sub-block sums (and split-K partial tiles). Returns the number of kernels launched (2) or a negative
 // cudaError_t.
 bool batched_supported(const MulMatOp& op);
 size_t batched_workspace_bytes(const MulMatOp& op);
