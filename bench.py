@@ -145,51 +145,61 @@ class DevArray:
 
 
 def batched_measure(dev, reps: int = 10, warmup: int = 3):
-    """Gemma-2-2B ffn_up (Q8_0 9216x2304) with 1..64 sequences decoding
-    together: N = 1, 2 run the streaming GEMV, N >= 3 the integer tensor-core
-    batched GEMM. 24 distinct weight copies (541 MB, over 4x the L2) rotate
-    between launches so every launch streams its weights from HBM. Returns
-    the JSON object."""
+    """Several sequences decoding together (N = 1 .. 64) on three weights:
+    Gemma-2-2B ffn_up (Q8_0 9216x2304), Llama-3-8B ffn_gate (Q4_K 14336x4096)
+    and ffn_down (Q6_K 4096x14336). N = 1, 2 run the streaming GEMV, N >= 3
+    the integer tensor-core batched GEMM. Distinct weight copies (over 2x the
+    L2) rotate between launches so every launch streams its weights from HBM.
+    Returns the JSON object: the Q8_0 shape at the top level, the K-quant
+    shapes under "kquant"."""
     import torch
 
     from webllm_b200 import jsep, synth
 
-    name, t, M, K = synth.GEMMA2_2B_SHAPES[0]
-    copies = 24
+    gname, gt, gM, gK = synth.GEMMA2_2B_SHAPES[0]
+    shapes = [(f"gemma-2-2b {gname}", gt, gM, gK, 24),
+              ("llama-3-8b ffn_gate", jsep.GGML_TYPE_Q4_K, 14336, 4096, 8),
+              ("llama-3-8b ffn_down", jsep.GGML_TYPE_Q6_K, 4096, 14336, 6)]
     stream_ptr = jsep.library_stream()
     lib_stream = torch.cuda.ExternalStream(stream_ptr)
-    gen = torch.Generator(device=dev)
-    gen.manual_seed(zlib.crc32(name.encode()))
-    ws = [synth.weights_torch(gen, t, M, K, dev) for _ in range(copies)]
-    per = []
     hbm, _ = measured_peaks()
-    for N in (1, 8, 16, 32, 64):
-        x = torch.randn(N, K, device=dev, generator=gen)
-        y = torch.empty(N, M, device=dev)
-        torch.cuda.synchronize()
+    out = []
+    for name, t, M, K, copies in shapes:
+        gen = torch.Generator(device=dev)
+        gen.manual_seed(zlib.crc32(name.encode()))
+        ws = [synth.weights_torch(gen, t, M, K, dev) for _ in range(copies)]
+        per = []
+        for N in (1, 8, 16, 32, 64):
+            x = torch.randn(N, K, device=dev, generator=gen)
+            y = torch.empty(N, M, device=dev)
+            torch.cuda.synchronize()
 
-        def run(i):
-            w = ws[i % copies]
-            jsep.mul_mat_device(t, w.data_ptr(), w.shape[1], x.data_ptr(), K, y.data_ptr(), M, M, K, N, stream_ptr)
+            def run(i):
+                w = ws[i % copies]
+                jsep.mul_mat_device(t, w.data_ptr(), w.shape[1], x.data_ptr(), K, y.data_ptr(), M, M, K, N, stream_ptr)
 
-        for i in range(warmup):
-            run(i)
-        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        with torch.cuda.stream(lib_stream):
-            ev0.record()
-            for i in range(reps * copies):
+            for i in range(warmup):
                 run(i)
-            ev1.record()
-        ev1.synchronize()
-        us = ev0.elapsed_time(ev1) * 1e3 / (reps * copies)
-        nbytes = synth.algorithmic_bytes(t, M, K, N)
-        per.append({"n": N, "us": round(us, 2), "gbs": round(nbytes / (us * 1e-6) / 1e9, 1),
-                    "hbm_frac": round(nbytes / (us * 1e-6) / 1e9 / hbm, 4),
-                    "tflops": round(2.0 * M * K * N / (us * 1e-6) / 1e12, 2)})
-    del ws
-    return {"workload": f"gemma-2-2b {name} Q8_0 {M}x{K}, N sequences decoding together",
-            "unit": "GB/s", "per_n": per,
-            "note": "N <= 2: streaming GEMV; N >= 3: integer tensor-core batched GEMM (x pre-pass included)"}
+            ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            with torch.cuda.stream(lib_stream):
+                ev0.record()
+                for i in range(reps * copies):
+                    run(i)
+                ev1.record()
+            ev1.synchronize()
+            us = ev0.elapsed_time(ev1) * 1e3 / (reps * copies)
+            nbytes = synth.algorithmic_bytes(t, M, K, N)
+            per.append({"n": N, "us": round(us, 2), "gbs": round(nbytes / (us * 1e-6) / 1e9, 1),
+                        "hbm_frac": round(nbytes / (us * 1e-6) / 1e9 / hbm, 4),
+                        "tflops": round(2.0 * M * K * N / (us * 1e-6) / 1e12, 2)})
+        del ws
+        tname = {jsep.GGML_TYPE_Q8_0: "Q8_0", jsep.GGML_TYPE_Q4_K: "Q4_K", jsep.GGML_TYPE_Q6_K: "Q6_K"}[t]
+        out.append({"workload": f"{name} {tname} {M}x{K}, N sequences decoding together", "unit": "GB/s",
+                    "per_n": per})
+    res = dict(out[0])
+    res["kquant"] = out[1:]
+    res["note"] = "N <= 2: streaming GEMV; N >= 3: integer tensor-core batched GEMM (x pre-pass included)"
+    return res
 
 
 def layer_groups():

@@ -34,6 +34,10 @@
 // Split K: grids below one wave of two CTAs per SM split the chunks S ways
 // (grid z); each split stores its tile in workspace and the tile's last split
 // sums the S tiles in split order (deterministic).
+//
+// Both kernels are programmatic dependent launches: the pre-pass waits for
+// the previous kernel before it reads x or writes the workspace; the GEMM
+// requests its first weight chunks, then waits for the pre-pass.
 #include <cuda_fp16.h>
 #include <stdint.h>
 
@@ -51,6 +55,10 @@ constexpr int kXRow = kChunk + 16;          // bytes of a limb row in shared mem
 constexpr int kMaxVec = 64;
 constexpr int kSlotsB = 2 * 148;            // CTAs resident at once
 constexpr int kMaxSplitsB = 16;
+
+// Split-K arrival counts, one per output tile (a launch splits K only when it
+// has at most kSlotsB / 2 tiles); the tile's last split resets its count.
+__device__ unsigned g_tile_counters[kSlotsB];
 
 // Shared-memory bytes of one row's chunk (16-byte pieces copied): Q8_0 8 x 34
 // = 272; Q4_K one 144-byte block; Q6_K one 210-byte block at any even offset
@@ -75,7 +83,6 @@ struct BatchedArgs {
     int32_t M, K, N, n_pad;
     int32_t splits, chunks_per_split;
     float* partial;        // [tile][split][kMaxVec][kRowsB]
-    unsigned* counters;    // [tile]
 };
 
 template <int TYPE, int NV>
@@ -191,9 +198,13 @@ __device__ __forceinline__ uint32_t q6_signed(uint32_t q) {
     return t | (s << 1) | (s << 2);
 }
 
-// Pre-pass: one warp per (vector, 256-element block).
+// Pre-pass: one warp per (vector, 256-element block). Launched as a
+// programmatic dependent: it waits for the previous kernel before it reads x
+// or writes the workspace.
 __global__ void x_limbs_kernel(const float* __restrict__ x, int64_t x_nb1, int8_t* __restrict__ xl,
                                float* __restrict__ inv_s, float* __restrict__ xsum, int K, int N, int n_pad) {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const int lane = threadIdx.x & 31;
     const int nblk = K / 256;
     const int64_t item = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
@@ -255,13 +266,10 @@ __global__ void __launch_bounds__(kThreadsB, 2) batched_kernel(const __grid_cons
     const int ch0 = blockIdx.z * P.chunks_per_split;
     const int nch = min(nchunks - ch0, P.chunks_per_split);
 
-    // one chunk's copies: 64 rows x RP pieces of 16 B, NV x 2 limb rows x 16
-    // pieces, NV factors (16 B pieces of 4), NV x 16 sums
-    auto load = [&](int ch, int buf) {
+    // one chunk's copies: 64 rows x RP pieces of 16 B (load_w), NV x 2 limb
+    // rows x 16 pieces, NV factors (16 B pieces of 4), NV x 16 sums (load_x)
+    auto load_w = [&](int ch, int buf) {
         uint8_t* sw = smem + buf * SB;
-        uint8_t* sx = sw + kRowsB * RS;
-        uint8_t* ss = sx + NV * 2 * kXRow;
-        uint8_t* su = ss + NV * 4;
         const int k0 = (ch0 + ch) * kChunk;
         for (int i = threadIdx.x; i < kRowsB * RP; i += kThreadsB) {
             const int r = i / RP, pc = i - r * RP;
@@ -282,6 +290,12 @@ __global__ void __launch_bounds__(kThreadsB, 2) batched_kernel(const __grid_cons
             }
             cp_async16(sw + r * RS + 16 * pc, ok ? src : P.w, ok);
         }
+    };
+    auto load_x = [&](int ch, int buf) {
+        uint8_t* sx = smem + buf * SB + kRowsB * RS;
+        uint8_t* ss = sx + NV * 2 * kXRow;
+        uint8_t* su = ss + NV * 4;
+        const int k0 = (ch0 + ch) * kChunk;
         for (int i = threadIdx.x; i < NV * 2 * 16; i += kThreadsB) {
             const int rowl = i >> 4, pc = i & 15;  // rowl = 2 v + limb
             const int v = rowl >> 1;
@@ -318,16 +332,27 @@ __global__ void __launch_bounds__(kThreadsB, 2) batched_kernel(const __grid_cons
         reinterpret_cast<uintptr_t>(P.w) + static_cast<uintptr_t>(static_cast<int64_t>(m0 + 16 * warp + g) * P.w_nb1);
     const uintptr_t rowh_addr = rowg_addr + static_cast<uintptr_t>(8 * P.w_nb1);
 
+    // Programmatic dependent launch: the first chunks' weights are requested
+    // before the wait for the kernel that writes the activations (the x
+    // pre-pass); they join the first chunk's copy group.
     constexpr int ST = stages_of<NV>();
 #pragma unroll
+    for (int sidx = 0; sidx < ST - 1; ++sidx)
+        if (sidx < nch) load_w(sidx, sidx);
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+#pragma unroll
     for (int sidx = 0; sidx < ST - 1; ++sidx) {
-        if (sidx < nch) load(sidx, sidx);
+        if (sidx < nch) load_x(sidx, sidx);
         cp_async_commit();
     }
     for (int ch = 0; ch < nch; ++ch) {
         cp_async_wait<ST - 2>();  // chunk ch has landed
         __syncthreads();          // ... for every thread, and chunk ch - 1's buffer is free
-        if (ch + ST - 1 < nch) load(ch + ST - 1, (ch + ST - 1) % ST);
+        if (ch + ST - 1 < nch) {
+            load_w(ch + ST - 1, (ch + ST - 1) % ST);
+            load_x(ch + ST - 1, (ch + ST - 1) % ST);
+        }
         cp_async_commit();
         const uint8_t* sw = smem + (ch % ST) * SB;
         const uint8_t* sx = sw + kRowsB * RS;
@@ -507,9 +532,9 @@ __global__ void __launch_bounds__(kThreadsB, 2) batched_kernel(const __grid_cons
     __syncthreads();
     if (threadIdx.x == 0) {
         __threadfence();  // this split's tile before the count
-        last = atomicAdd(P.counters + tile, 1u) == static_cast<unsigned>(P.splits - 1);
+        last = atomicAdd(g_tile_counters + tile, 1u) == static_cast<unsigned>(P.splits - 1);
         if (last) {
-            P.counters[tile] = 0u;
+            g_tile_counters[tile] = 0u;
             __threadfence();  // the other splits' tiles after the count
         }
     }
@@ -560,7 +585,7 @@ size_t partial_bytes(const MulMatOp& o) {
     plan(o, &nv, &s, &cps);
     if (s <= 1) return 0;
     const size_t tiles = static_cast<size_t>((o.M + kRowsB - 1) / kRowsB) * ((o.N + nv - 1) / nv);
-    return tiles * s * kMaxVec * kRowsB * 4 + tiles * 4;
+    return tiles * s * kMaxVec * kRowsB * 4;
 }
 
 template <int TYPE, int NV>
@@ -573,8 +598,18 @@ cudaError_t launch_nv(const BatchedArgs& P, dim3 grid, cudaStream_t stream) {
         if (e != cudaSuccess) return e;
         configured = true;
     }
-    batched_kernel<TYPE, NV><<<grid, kThreadsB, smem, stream>>>(P);
-    return cudaGetLastError();
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(kThreadsB);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, batched_kernel<TYPE, NV>, P);
+    return e == cudaSuccess ? cudaGetLastError() : e;
 }
 
 template <int TYPE>
@@ -633,19 +668,23 @@ int launch_batched(const MulMatOp& o, void* workspace, size_t workspace_bytes, c
     P.splits = splits;
     P.chunks_per_split = cps;
     const int tiles_m = (o.M + kRowsB - 1) / kRowsB, tiles_n = (o.N + nv - 1) / nv;
-    if (splits > 1) {
-        P.partial = reinterpret_cast<float*>(ws + limbs_bytes(o) + factors_bytes(o) + sums_bytes(o));
-        P.counters = reinterpret_cast<unsigned*>(P.partial + static_cast<size_t>(tiles_m) * tiles_n * splits * kMaxVec * kRowsB);
-        const cudaError_t e = cudaMemsetAsync(P.counters, 0, static_cast<size_t>(tiles_m) * tiles_n * 4, stream);
-        if (e != cudaSuccess) return -static_cast<int>(e);
-    }
+    if (splits > 1) P.partial = reinterpret_cast<float*>(ws + limbs_bytes(o) + factors_bytes(o) + sums_bytes(o));
+    if (splits > 1 && tiles_m * tiles_n > kSlotsB) return -static_cast<int>(cudaErrorInvalidValue);  // (plan keeps it below)
     {
         const int64_t items = static_cast<int64_t>(P.n_pad) * (o.K / 256);
         const int64_t blocks = (items * 32 + 255) / 256;
-        x_limbs_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
-            o.x, o.x_nb1, const_cast<int8_t*>(P.xl), const_cast<float*>(P.inv_s), const_cast<float*>(P.xsum), o.K, o.N,
-            P.n_pad);
-        const cudaError_t e = cudaGetLastError();
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(static_cast<unsigned>(blocks));
+        cfg.blockDim = dim3(256);
+        cfg.stream = stream;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        cudaError_t e = cudaLaunchKernelEx(&cfg, x_limbs_kernel, o.x, o.x_nb1, const_cast<int8_t*>(P.xl),
+                                           const_cast<float*>(P.inv_s), const_cast<float*>(P.xsum), o.K, o.N, P.n_pad);
+        if (e == cudaSuccess) e = cudaGetLastError();
         if (e != cudaSuccess) return -static_cast<int>(e);
     }
     const dim3 grid(tiles_m, tiles_n, splits);
