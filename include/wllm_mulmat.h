@@ -2,7 +2,7 @@
  * wllm_mulmat — C ABI of the B200 quantized MUL_MAT library.
  *
  * Drop-in for one op of paulrobello/webllm: ggml MUL_MAT with a GGUF
- * quantized src0 (Q4_K, Q6_K, Q8_0) and f32 src1/dst. The ABI mirrors the
+ * quantized src0 (Q4_K, Q5_K, Q6_K, Q4_0, Q8_0) and f32 src1/dst. The ABI mirrors the
  * JSEP operator-plugin seam the ggml backend calls per graph node
  * (src/inference/jsep/index.ts:1-21,129-305): seven callbacks
  * alloc/free/write/read/clear/run_op/sync over integer buffer handles, and
@@ -49,6 +49,7 @@ extern "C" {
 #define WLLM_TYPE_Q4_0 2
 #define WLLM_TYPE_Q8_0 8
 #define WLLM_TYPE_Q4_K 12
+#define WLLM_TYPE_Q5_K 13
 #define WLLM_TYPE_Q6_K 14
 
 /* Descriptor geometry (matmul.ts:22-41): [op, n_src, dst block, src blocks...],
@@ -242,7 +243,7 @@ int32_t wllm_mul_mat_prefill_static(int32_t src0_type, const void* w, int64_t w_
 /* Device dequantization of n elements (n a multiple of the block size) of
  * raw GGUF blocks to f32. Replaces the libllama oracle shim
  * webllm_dequantize_q4_K (webgpu-bridge.cpp:692-708) on the device, for
- * Q4_K, Q6_K and Q8_0. Returns -1 on bad arguments. */
+ * Q4_K, Q5_K, Q6_K, Q4_0 and Q8_0. Returns -1 on bad arguments. */
 int32_t wllm_dequantize(int32_t type, const void* src, float* dst, int64_t n, void* stream);
 
 /* Library build/version string. */

@@ -24,8 +24,10 @@ _lock = threading.Lock()
 _lib = None
 
 TYPE_F32 = 0
+TYPE_Q4_0 = 2
 TYPE_Q8_0 = 8
 TYPE_Q4_K = 12
+TYPE_Q5_K = 13
 TYPE_Q6_K = 14
 
 

@@ -45,8 +45,10 @@ float oracle_f16_to_f32(uint16_t h) {
 int32_t oracle_block_elems(int32_t type) {
     switch (type) {
         case ORACLE_TYPE_F32: return 1;
+        case ORACLE_TYPE_Q4_0: return 32;
         case ORACLE_TYPE_Q8_0: return 32;
         case ORACLE_TYPE_Q4_K: return 256;
+        case ORACLE_TYPE_Q5_K: return 256;
         case ORACLE_TYPE_Q6_K: return 256;
         default: return 0;
     }
@@ -56,8 +58,10 @@ int32_t oracle_block_bytes(int32_t type) {
     /* src/models/gguf-parser.ts:273-294 (ggmlTypeSize). */
     switch (type) {
         case ORACLE_TYPE_F32: return 4;
+        case ORACLE_TYPE_Q4_0: return 18;
         case ORACLE_TYPE_Q8_0: return 34;
         case ORACLE_TYPE_Q4_K: return 144;
+        case ORACLE_TYPE_Q5_K: return 176;
         case ORACLE_TYPE_Q6_K: return 210;
         default: return 0;
     }
@@ -96,6 +100,41 @@ static void dequant_block_q4_K(const uint8_t* b, float* y) {
             y[64 * p + l] = d1 * (float)(qs[32 * p + l] & 0xF) - mm1;
             y[64 * p + 32 + l] = d2 * (float)(qs[32 * p + l] >> 4) - mm2;
         }
+    }
+}
+
+/* One 176-byte Q5_K super-block -> 256 floats (ggml block_q5_K: f16 d @0,
+ * f16 dmin @2, scales[12] @4 packed as for Q4_K, qh[32] @16, qs[128] @48).
+ * Sub-block j (0..7) holds elements 32j..32j+31; element 32j+l has the
+ * nibble of qs[32(j/2)+l] (low for even j, high for odd) and bit j of
+ * qh[l] as bit 4: q = 0..31, y = d*sc_j*q - dmin*m_j. */
+static void dequant_block_q5_K(const uint8_t* b, float* y) {
+    const float d = oracle_f16_to_f32(rd16(b));
+    const float dmin = oracle_f16_to_f32(rd16(b + 2));
+    const uint8_t* scales = b + 4;
+    const uint8_t* qh = b + 16;
+    const uint8_t* qs = b + 48;
+    for (int j = 0; j < 8; ++j) {
+        int sc, m;
+        q4k_scale_min(scales, j, &sc, &m);
+        const float ds = d * (float)sc, dm = dmin * (float)m;
+        for (int l = 0; l < 32; ++l) {
+            const int nib = (j & 1) ? (qs[32 * (j / 2) + l] >> 4) : (qs[32 * (j / 2) + l] & 0xF);
+            const int q = nib | (((qh[l] >> j) & 1) << 4);
+            y[32 * j + l] = ds * (float)q - dm;
+        }
+    }
+}
+
+/* One 18-byte Q4_0 block -> 32 floats (ggml block_q4_0: f16 d @0, qs[16]
+ * @2): element l < 16 is the low nibble of qs[l], element 16+l the high
+ * nibble; y = d*(q - 8). */
+static void dequant_block_q4_0(const uint8_t* b, float* y) {
+    const float d = oracle_f16_to_f32(rd16(b));
+    const uint8_t* qs = b + 2;
+    for (int l = 0; l < 16; ++l) {
+        y[l] = d * (float)((int)(qs[l] & 0xF) - 8);
+        y[16 + l] = d * (float)((int)(qs[l] >> 4) - 8);
     }
 }
 
@@ -142,7 +181,9 @@ int32_t oracle_dequantize_row(int32_t type, const void* src, float* dst, int64_t
     for (int64_t i = 0; i < nb; ++i) {
         switch (type) {
             case ORACLE_TYPE_Q4_K: dequant_block_q4_K(s + i * bb, dst + i * be); break;
+            case ORACLE_TYPE_Q5_K: dequant_block_q5_K(s + i * bb, dst + i * be); break;
             case ORACLE_TYPE_Q6_K: dequant_block_q6_K(s + i * bb, dst + i * be); break;
+            case ORACLE_TYPE_Q4_0: dequant_block_q4_0(s + i * bb, dst + i * be); break;
             case ORACLE_TYPE_Q8_0: dequant_block_q8_0(s + i * bb, dst + i * be); break;
             case ORACLE_TYPE_F32: memcpy(dst + i, s + 4 * i, 4); break;
             default: return -1;

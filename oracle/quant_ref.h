@@ -2,7 +2,8 @@
  * CPU oracle for the quantized MUL_MAT path (TEST INFRASTRUCTURE ONLY).
  *
  * This is a plain-C restatement of the reference's algorithm for
- * ggml MUL_MAT with a quantized src0 (Q4_K, Q6_K, Q8_0) and f32 src1/dst.
+ * ggml MUL_MAT with a quantized src0 (Q4_K, Q5_K, Q6_K, Q4_0, Q8_0) and f32
+ * src1/dst.
  * It is the checker for the CUDA path and the timed CPU baseline; it is
  * never linked into, loaded by or called from the product library.
  *
@@ -16,6 +17,10 @@
  *     block_q6_K / block_q8_0 format (llama.cpp ggml-quants.c
  *     dequantize_row_q6_K / dequantize_row_q8_0, also restated by the gguf
  *     python package 0.19.0, gguf/quants.py:396-402,554-575).
+ *   Q5_K / Q4_0 (fleet formats listed in docs/MODEL_SUPPORT.md:133-138): no
+ *     code in the reference repo either; ggml's block_q5_K / block_q4_0
+ *     (dequantize_row_q5_K / dequantize_row_q4_0), restated by gguf 0.19.0
+ *     gguf/quants.py:241-251 (Q4_0) and :525-549 (Q5_K).
  *   MUL_MAT semantics dst[m + M*n] = sum_k W[m,k] * x[k + K*n]:
  *     tests/jsep-matmul-golden.test.ts:67-90 (cpuMatmul),
  *     smoke-test/p2-v2-spike.src.ts:1197-1214 (k-major f32 loop + f64 reference).
@@ -30,7 +35,14 @@ extern "C" {
 #endif
 
 /* ggml_type ids (src/inference/ggml-wasm.ts:8-25). */
-enum { ORACLE_TYPE_F32 = 0, ORACLE_TYPE_Q8_0 = 8, ORACLE_TYPE_Q4_K = 12, ORACLE_TYPE_Q6_K = 14 };
+enum {
+    ORACLE_TYPE_F32 = 0,
+    ORACLE_TYPE_Q4_0 = 2,
+    ORACLE_TYPE_Q8_0 = 8,
+    ORACLE_TYPE_Q4_K = 12,
+    ORACLE_TYPE_Q5_K = 13,
+    ORACLE_TYPE_Q6_K = 14
+};
 
 /* Exact IEEE binary16 -> binary32 (normals, subnormals, inf, nan). */
 float oracle_f16_to_f32(uint16_t h);

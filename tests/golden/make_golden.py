@@ -22,10 +22,11 @@ q4k_synth_64x2048.npz
     runMatmulProductionSelfTest (smoke-test/p2-v2-spike.src.ts:287-330,340-360),
     expected dequant and the f64-accumulated reference product.
 gguf_blocks.npz
-    Random blocks of Q4_K, Q6_K and Q8_0 (seeded) with the dequantization
-    of the third-party `gguf` python package 0.19.0 (gguf.quants.dequantize),
-    the published ggml block formats the reference's llama.cpp fork uses.
-    The reference repository has no Q6_K/Q8_0 code of its own.
+    Random blocks of Q4_K, Q6_K, Q8_0, Q5_K and Q4_0 (seeded) with the
+    dequantization of the third-party `gguf` python package 0.19.0
+    (gguf.quants.dequantize), the published ggml block formats the
+    reference's llama.cpp fork uses. The reference repository has no
+    Q6_K/Q8_0/Q5_K/Q4_0 code of its own.
 """
 from __future__ import annotations
 
@@ -148,12 +149,16 @@ def make_gguf_blocks():
     from importlib.metadata import version
 
     out = {"gguf_version": np.array(version("gguf"))}
-    for name, t, bb in (("q4_k", T.Q4_K, 144), ("q6_k", T.Q6_K, 210), ("q8_0", T.Q8_0, 34)):
+    # (the Q5_K / Q4_0 blocks come after the others: the earlier arrays keep
+    # their random streams)
+    scale_offsets = {T.Q4_K: (0, 2), T.Q5_K: (0, 2), T.Q6_K: (208,), T.Q8_0: (0,), T.Q4_0: (0,)}
+    for name, t, bb in (("q4_k", T.Q4_K, 144), ("q6_k", T.Q6_K, 210), ("q8_0", T.Q8_0, 34), ("q5_k", T.Q5_K, 176),
+                        ("q4_0", T.Q4_0, 18)):
         nblk = 64
         raw = rng.integers(0, 256, size=(nblk, bb), dtype=np.uint8)
         # finite f16 scales spanning normals and subnormals
-        for off in ((0, 2) if t == T.Q4_K else ((208,) if t == T.Q6_K else (0,))):
-            mag = np.abs(rng.standard_normal(nblk)) * (2e-3 if t != T.Q8_0 else 1e-2)
+        for off in scale_offsets[t]:
+            mag = np.abs(rng.standard_normal(nblk)) * (1e-2 if t in (T.Q8_0, T.Q4_0) else 2e-3)
             mag[:4] = [0.0, 3e-8, 6e-6, 6.0e-5]  # zero and f16 subnormals
             raw[:, off:off + 2] = mag.astype(np.float16).view(np.uint8).reshape(nblk, 2)
         deq = quants.dequantize(raw.reshape(-1), t).astype(np.float32).reshape(-1)

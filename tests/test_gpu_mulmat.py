@@ -64,7 +64,8 @@ def test_q4k_synth_64x2048(runtime, golden):
 
 
 @pytest.mark.parametrize("qtype,name", [(jsep.GGML_TYPE_Q4_K, "q4_k"), (jsep.GGML_TYPE_Q6_K, "q6_k"),
-                                        (jsep.GGML_TYPE_Q8_0, "q8_0")])
+                                        (jsep.GGML_TYPE_Q8_0, "q8_0"), (jsep.GGML_TYPE_Q5_K, "q5_k"),
+                                        (jsep.GGML_TYPE_Q4_0, "q4_0")])
 def test_device_dequant_bit_exact(runtime, golden, qtype, name):
     z = golden("gguf_blocks.npz")
     raw = z[f"{name}_raw"]
@@ -94,7 +95,8 @@ def test_device_dequant_bit_exact(runtime, golden, qtype, name):
 SHAPES = [(1, 256, 1), (7, 512, 1), (33, 768, 2), (257, 1024, 3), (64, 2048, 5), (96, 3072, 8), (40, 2304, 13)]
 
 
-@pytest.mark.parametrize("qtype", [jsep.GGML_TYPE_Q4_K, jsep.GGML_TYPE_Q6_K, jsep.GGML_TYPE_Q8_0])
+@pytest.mark.parametrize("qtype", [jsep.GGML_TYPE_Q4_K, jsep.GGML_TYPE_Q6_K, jsep.GGML_TYPE_Q8_0,
+                                   jsep.GGML_TYPE_Q5_K, jsep.GGML_TYPE_Q4_0])
 @pytest.mark.parametrize("M,K,N", SHAPES)
 def test_gemv_random_shapes(runtime, qtype, M, K, N):
     be, _ = jsep.BLOCK_GEOMETRY[qtype]
@@ -142,12 +144,15 @@ def test_q8_0_batched_decode(runtime, name, M, K, N):
 
 @pytest.mark.parametrize("N", [3, 4, 8, 16, 33, 64])
 @pytest.mark.parametrize("qtype,M,K", [(jsep.GGML_TYPE_Q4_K, 4096, 4096), (jsep.GGML_TYPE_Q4_K, 14336, 4096),
-                                       (jsep.GGML_TYPE_Q6_K, 4096, 14336), (jsep.GGML_TYPE_Q6_K, 1024, 3072)])
+                                       (jsep.GGML_TYPE_Q6_K, 4096, 14336), (jsep.GGML_TYPE_Q6_K, 1024, 3072),
+                                       (jsep.GGML_TYPE_Q5_K, 4096, 4096), (jsep.GGML_TYPE_Q4_0, 4096, 4096),
+                                       (jsep.GGML_TYPE_Q5_K, 1000, 2304), (jsep.GGML_TYPE_Q4_0, 1000, 2304)])
 def test_kquant_small_batches_vs_torch_fp64(runtime, qtype, M, K, N):
-    """Q4_K / Q6_K with 3 to 64 vectors (several sequences decoding together,
-    short prefill tiles) on the integer tensor-core batched GEMM, split K
-    included; Q6_K 1024 x 3072 has 2520-byte rows (8-byte aligned). Against a
-    float64 matmul of the device-dequantized weights."""
+    """Q4_K / Q5_K / Q6_K / Q4_0 with 3 to 64 vectors (several sequences
+    decoding together, short prefill tiles) on the integer tensor-core batched
+    GEMM, split K included; Q6_K 1024 x 3072 has 2520-byte rows (8-byte
+    aligned), M = 1000 leaves a partial 64-row tile. Against a float64 matmul
+    of the device-dequantized weights."""
     import torch
 
     dev = torch.device("cuda", 0)

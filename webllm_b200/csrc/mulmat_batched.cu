@@ -1,24 +1,28 @@
 // Small-batch quantized MUL_MAT (N >= 3 activation vectors: several sequences
 // decoding together, short prefill tiles, the GEMV-to-GEMM crossover) for
-// Q8_0, Q4_K and Q6_K weights on integer tensor cores (mma.sync m16n8k32,
-// s8 / u8 x s8 -> s32).
+// Q8_0, Q4_0, Q4_K, Q5_K and Q6_K weights on integer tensor cores
+// (mma.sync m16n8k32, s8 / u8 x s8 -> s32).
 //
 //   y[m + M n] = sum_k W[m, k] x[k + K n]   (ggml MUL_MAT, matmul.ts:10-17)
 //
 // Activations: a pre-pass turns x into two int8 limbs per element,
 // x = (l0 + l1 / 128) / s with s = 127 / max|x| per 256 elements and vector
 // (|error| <= max|x| / 32512), stored as [N][2][K], with the factors 1 / s as
-// [K / 256][N rounded up to 4] and, for Q4_K, the f32 sums of x over each
+// [K / 256][N rounded up to 4] and, for Q4_K / Q5_K, the f32 sums of x over each
 // 16-element sub-block as [K / 256][N rounded up to 4][16]. The eight B
 // columns of an MMA are four vectors x two limbs.
 //
 // Weights, per 32-element MMA step (k = 32):
 //  - Q8_0: one block; the s8 quants enter the MMA as they are and the s32
 //    result is scaled by the rows' f16 d in f32;
+//  - Q4_0: one block; the nibbles enter as s8 q - 8 (a 4-bit sign
+//    extension), then as Q8_0;
 //  - Q4_K: one 32-element sub-block; its u8 nibbles, the low ones as they are
 //    and the high ones in place (16 q), times the 6-bit scale (16 sc for the
 //    low-nibble sub-blocks) in integer over the 256-element block, then
 //    d / (16 s); the mins through the sub-block sums of x;
+//  - Q5_K: as Q4_K with the 5-bit quants (nibble | qh bit << 4) as u8 and
+//    sc for every sub-block, then d / s;
 //  - Q6_K: two 16-element sub-blocks, one MMA each (the other half of the A
 //    fragment zero); the quants q - 32 enter the MMA as s8 (a 6-bit sign
 //    extension), times the int8 scale in integer, then d / s.
@@ -61,15 +65,20 @@ constexpr int kMaxSplitsB = 16;
 __device__ unsigned g_tile_counters[kSlotsB];
 
 // Shared-memory bytes of one row's chunk (16-byte pieces copied): Q8_0 8 x 34
-// = 272; Q4_K one 144-byte block; Q6_K one 210-byte block at any even offset
-// in a 240-byte window (60 words: the 8 rows a warp reads hit 8 bank groups).
+// = 272; Q4_0 8 x 18 = 144; Q4_K one 144-byte block; Q5_K one 176-byte block;
+// Q6_K one 210-byte block at any even offset in a 240-byte window (60 words:
+// the 8 rows a warp reads hit 8 bank groups).
 template <int TYPE>
 __host__ __device__ constexpr int row_stride() {
-    return TYPE == kTypeQ8_0 ? 272 : (TYPE == kTypeQ4_K ? 144 : 240);
+    return TYPE == kTypeQ8_0 ? 272 : (TYPE == kTypeQ6_K ? 240 : (TYPE == kTypeQ5_K ? 176 : 144));
 }
 template <int TYPE>
-__host__ __device__ constexpr int sum_floats() {  // x sub-block sums per vector and chunk
-    return TYPE == kTypeQ4_K ? 16 : 0;
+__host__ __device__ constexpr int row_pieces() {  // 16-byte pieces copied per row (Q6_K: 14 cover any offset)
+    return TYPE == kTypeQ8_0 ? 17 : (TYPE == kTypeQ6_K ? 14 : (TYPE == kTypeQ5_K ? 11 : 9));
+}
+template <int TYPE>
+__host__ __device__ constexpr int sum_floats() {  // x sub-block sums per vector and chunk (the mins)
+    return (TYPE == kTypeQ4_K || TYPE == kTypeQ5_K) ? 16 : 0;
 }
 
 struct BatchedArgs {
@@ -190,6 +199,14 @@ __device__ __forceinline__ uint32_t q6k_group(uint32_t ql0, uint32_t ql1, uint32
     return lo | (((qh >> (2 * t)) & 0x03030303u) << 4);
 }
 
+// Four 4-bit quants q (0..15, one per byte) -> the int8 bytes q - 8: q ^ 8 is
+// q - 8 as a 4-bit two's-complement number; copy its sign bit (bit 3) into
+// bits 4..7 (0x08 * 0x1E = 0xF0 stays inside each byte).
+__device__ __forceinline__ uint32_t q4_signed(uint32_t q) {
+    const uint32_t t = q ^ 0x08080808u;
+    return t | ((t & 0x08080808u) * 0x1Eu);
+}
+
 // Four 6-bit quants q (0..63, one per byte) -> the int8 bytes q - 32: q ^ 32
 // is q - 32 as a 6-bit two's-complement number; copy its sign bit (bit 5)
 // into bits 6 and 7.
@@ -256,7 +273,7 @@ template <int TYPE, int NV>
 __global__ void __launch_bounds__(kThreadsB, 2) batched_kernel(const __grid_constant__ BatchedArgs P) {
     extern __shared__ __align__(128) uint8_t smem[];
     constexpr int RS = row_stride<TYPE>();
-    constexpr int RP = TYPE == kTypeQ8_0 ? 17 : (TYPE == kTypeQ4_K ? 9 : 14);  // 16-byte pieces per row (Q6_K: 14 cover any offset)
+    constexpr int RP = row_pieces<TYPE>();
     constexpr int SB = stage_bytes<TYPE, NV>();
     constexpr int NT = NV / 4;  // MMA column tiles: 4 vectors x 2 limbs each
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -278,8 +295,12 @@ __global__ void __launch_bounds__(kThreadsB, 2) batched_kernel(const __grid_cons
             const uint8_t* src;
             if (TYPE == kTypeQ8_0) {
                 src = row + (k0 / 32) * 34 + 16 * pc;
+            } else if (TYPE == kTypeQ4_0) {
+                src = row + (k0 / 32) * 18 + 16 * pc;
             } else if (TYPE == kTypeQ4_K) {
                 src = row + (k0 / 256) * 144 + 16 * pc;
+            } else if (TYPE == kTypeQ5_K) {
+                src = row + (k0 / 256) * 176 + 16 * pc;
             } else {
                 // the 16-byte pieces that meet the 210-byte block (none past the
                 // 16-byte boundary after its last byte)
@@ -308,7 +329,7 @@ __global__ void __launch_bounds__(kThreadsB, 2) batched_kernel(const __grid_cons
             const bool ok = n0 + v < P.n_pad;
             cp_async16(ss + 16 * i, P.inv_s + static_cast<int64_t>(ch0 + ch) * P.n_pad + (ok ? n0 + v : 0), ok);
         }
-        if (TYPE == kTypeQ4_K) {
+        if (sum_floats<TYPE>() > 0) {
             for (int i = threadIdx.x; i < NV * 4; i += kThreadsB) {
                 const int v = i >> 2, pc = i & 3;
                 const bool ok = n0 + v < P.n_pad;
@@ -390,8 +411,47 @@ __global__ void __launch_bounds__(kThreadsB, 2) batched_kernel(const __grid_cons
                     }
                 }
             }
-        } else if (TYPE == kTypeQ4_K) {
+        } else if (TYPE == kTypeQ4_0) {
+#pragma unroll
+            for (int b = 0; b < 8; ++b) {
+                const uint8_t* bg = rg + 18 * b;
+                const uint8_t* bh = rh + 18 * b;
+                const float dg = f16_bits_to_f32(*reinterpret_cast<const uint16_t*>(bg));
+                const float dh = f16_bits_to_f32(*reinterpret_cast<const uint16_t*>(bh));
+                const uint32_t wg = lds_u32_any(bg + 2 + 4 * c), wh = lds_u32_any(bh + 2 + 4 * c);
+                // elements 4c.. are the low nibbles, 16+4c.. the high ones
+                const uint32_t a0 = q4_signed(wg & 0x0F0F0F0Fu), a1 = q4_signed(wh & 0x0F0F0F0Fu);
+                const uint32_t a2 = q4_signed((wg >> 4) & 0x0F0F0F0Fu), a3 = q4_signed((wh >> 4) & 0x0F0F0F0Fu);
+#pragma unroll
+                for (int tp = 0; tp < NT / 2; ++tp) {
+                    uint32_t xb[4];
+                    ldmatrix_x4(xb, xbase + static_cast<uint32_t>(tp * 8 * 2 * kXRow + 32 * b));
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        const int t = 2 * tp + h;
+                        int D[4];
+                        imma_s8(D, a0, a1, a2, a3, xb[2 * h], xb[2 * h + 1]);
+                        const float vg = fmaf(static_cast<float>(D[1]), 0.0078125f, static_cast<float>(D[0]));
+                        const float vh = fmaf(static_cast<float>(D[3]), 0.0078125f, static_cast<float>(D[2]));
+                        acc[t][0] = fmaf(vg, dg * is[t], acc[t][0]);
+                        acc[t][1] = fmaf(vh, dh * is[t], acc[t][1]);
+                    }
+                }
+            }
+        } else if (TYPE == kTypeQ4_K || TYPE == kTypeQ5_K) {
+            // Q4_K: nibbles (low as they are, high in place = 16 q) times 16 sc /
+            // sc; Q5_K: the 5-bit quants (nibble | qh bit j << 4) times sc
+            constexpr bool k5 = TYPE == kTypeQ5_K;
+            constexpr int QS = k5 ? 48 : 16;  // quant bytes in the block
             const uint4 hg = *reinterpret_cast<const uint4*>(rg), hh4 = *reinterpret_cast<const uint4*>(rh);
+            // Q5_K high-bit words qh[4c..], qh[16+4c..] of rows g / g+8
+            uint32_t hb[4] = {0u, 0u, 0u, 0u};
+            if (k5) {
+                hb[0] = *reinterpret_cast<const uint32_t*>(rg + 16 + 4 * c);
+                hb[1] = *reinterpret_cast<const uint32_t*>(rh + 16 + 4 * c);
+                hb[2] = *reinterpret_cast<const uint32_t*>(rg + 32 + 4 * c);
+                hb[3] = *reinterpret_cast<const uint32_t*>(rh + 32 + 4 * c);
+            }
             // |D| <= 32 * 240 * 127 per sub-block, times sc <= 63 (or 16 sc with
             // the unscaled low nibbles), over 8 sub-blocks: inside int32
             int a[NT][4];
@@ -401,15 +461,29 @@ __global__ void __launch_bounds__(kThreadsB, 2) batched_kernel(const __grid_cons
             for (int p = 0; p < 4; ++p) {
                 // fragment words of sub-block pair p (qs bytes 32p .. 32p+31): row
                 // g / g+8, k 4c.. / 16+4c..
-                const uint32_t w0 = *reinterpret_cast<const uint32_t*>(rg + 16 + 32 * p + 4 * c);
-                const uint32_t w1 = *reinterpret_cast<const uint32_t*>(rh + 16 + 32 * p + 4 * c);
-                const uint32_t w2 = *reinterpret_cast<const uint32_t*>(rg + 32 + 32 * p + 4 * c);
-                const uint32_t w3 = *reinterpret_cast<const uint32_t*>(rh + 32 + 32 * p + 4 * c);
+                const uint32_t w0 = *reinterpret_cast<const uint32_t*>(rg + QS + 32 * p + 4 * c);
+                const uint32_t w1 = *reinterpret_cast<const uint32_t*>(rh + QS + 32 * p + 4 * c);
+                const uint32_t w2 = *reinterpret_cast<const uint32_t*>(rg + QS + 16 + 32 * p + 4 * c);
+                const uint32_t w3 = *reinterpret_cast<const uint32_t*>(rh + QS + 16 + 32 * p + 4 * c);
 #pragma unroll
                 for (int hi = 0; hi < 2; ++hi) {
                     const int j = 2 * p + hi;
-                    const uint32_t msk = hi ? 0xF0F0F0F0u : 0x0F0F0F0Fu;
-                    const int scj = q4k_scale_j(hg, j), shj = q4k_scale_j(hh4, j);
+                    uint32_t A[4];
+                    if (k5) {
+                        const uint32_t w[4] = {w0, w1, w2, w3};
+#pragma unroll
+                        for (int r = 0; r < 4; ++r)
+                            A[r] = ((hi ? (w[r] >> 4) : w[r]) & 0x0F0F0F0Fu) | (((hb[r] >> j) & 0x01010101u) << 4);
+                    } else {
+                        const uint32_t msk = hi ? 0xF0F0F0F0u : 0x0F0F0F0Fu;
+                        A[0] = w0 & msk;
+                        A[1] = w1 & msk;
+                        A[2] = w2 & msk;
+                        A[3] = w3 & msk;
+                    }
+                    // (q4k_scale_j gives 16 sc for even j: Q5_K takes sc)
+                    const int scj = q4k_scale_j(hg, j) >> (k5 && !hi ? 4 : 0);
+                    const int shj = q4k_scale_j(hh4, j) >> (k5 && !hi ? 4 : 0);
 #pragma unroll
                     for (int tp = 0; tp < NT / 2; ++tp) {
                         uint32_t xb[4];
@@ -418,7 +492,7 @@ __global__ void __launch_bounds__(kThreadsB, 2) batched_kernel(const __grid_cons
                         for (int h = 0; h < 2; ++h) {
                             const int t = 2 * tp + h;
                             int D[4];
-                            imma_u8(D, w0 & msk, w1 & msk, w2 & msk, w3 & msk, xb[2 * h], xb[2 * h + 1]);
+                            imma_u8(D, A[0], A[1], A[2], A[3], xb[2 * h], xb[2 * h + 1]);
                             a[t][0] += scj * D[0];
                             a[t][1] += scj * D[1];
                             a[t][2] += shj * D[2];
@@ -441,7 +515,7 @@ __global__ void __launch_bounds__(kThreadsB, 2) batched_kernel(const __grid_cons
                     og = fmaf(mg[j], X, og);
                     oh = fmaf(mh[j], X, oh);
                 }
-                const float f = is[t] * 0.0625f;
+                const float f = k5 ? is[t] : is[t] * 0.0625f;
                 acc[t][0] += fmaf(dg * fmaf(static_cast<float>(a[t][1]), 0.0078125f, static_cast<float>(a[t][0])), f, -og);
                 acc[t][1] += fmaf(dh * fmaf(static_cast<float>(a[t][3]), 0.0078125f, static_cast<float>(a[t][2])), f, -oh);
             }
@@ -577,7 +651,7 @@ size_t factors_bytes(const MulMatOp& o) {
     return (static_cast<size_t>(o.K / 256) * n_pad_of(o) * 4 + 255) & ~size_t(255);
 }
 size_t sums_bytes(const MulMatOp& o) {
-    if (o.type != kTypeQ4_K) return 0;
+    if (o.type != kTypeQ4_K && o.type != kTypeQ5_K) return 0;
     return (static_cast<size_t>(o.K / 256) * n_pad_of(o) * 16 * 4 + 255) & ~size_t(255);
 }
 size_t partial_bytes(const MulMatOp& o) {
@@ -633,7 +707,9 @@ cudaError_t launch_type<kTypeQ6_K>(int nv, const BatchedArgs& P, dim3 grid, cuda
 }  // namespace
 
 bool batched_supported(const MulMatOp& o) {
-    if (o.type != kTypeQ8_0 && o.type != kTypeQ4_K && o.type != kTypeQ6_K) return false;
+    if (o.type != kTypeQ8_0 && o.type != kTypeQ4_K && o.type != kTypeQ6_K && o.type != kTypeQ5_K &&
+        o.type != kTypeQ4_0)
+        return false;
     if (o.N < 3 || o.ne2 != 1 || o.ne3 != 1) return false;
     if (o.K % 256 != 0 || o.M < 1) return false;
     const uintptr_t wa = reinterpret_cast<uintptr_t>(o.w) | static_cast<uintptr_t>(o.w_nb1);
@@ -658,7 +734,9 @@ int launch_batched(const MulMatOp& o, void* workspace, size_t workspace_bytes, c
     P.w_nb1 = o.w_nb1;
     P.xl = reinterpret_cast<int8_t*>(ws);
     P.inv_s = reinterpret_cast<float*>(ws + limbs_bytes(o));
-    P.xsum = o.type == kTypeQ4_K ? reinterpret_cast<float*>(ws + limbs_bytes(o) + factors_bytes(o)) : nullptr;
+    P.xsum = (o.type == kTypeQ4_K || o.type == kTypeQ5_K)
+                 ? reinterpret_cast<float*>(ws + limbs_bytes(o) + factors_bytes(o))
+                 : nullptr;
     P.y = o.y;
     P.y_nb1 = o.y_nb1;
     P.M = o.M;
@@ -692,6 +770,8 @@ int launch_batched(const MulMatOp& o, void* workspace, size_t workspace_bytes, c
     switch (o.type) {
         case kTypeQ8_0: e = launch_type<kTypeQ8_0>(nv, P, grid, stream); break;
         case kTypeQ4_K: e = launch_type<kTypeQ4_K>(nv, P, grid, stream); break;
+        case kTypeQ5_K: e = launch_type<kTypeQ5_K>(nv, P, grid, stream); break;
+        case kTypeQ4_0: e = launch_type<kTypeQ4_0>(nv, P, grid, stream); break;
         default: e = launch_type<kTypeQ6_K>(nv, P, grid, stream); break;
     }
     return e == cudaSuccess ? 2 : -static_cast<int>(e);

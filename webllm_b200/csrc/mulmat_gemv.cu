@@ -81,6 +81,50 @@ __device__ __forceinline__ void row_q4_k(const uint8_t* wrow, const float* const
     }
 }
 
+// Q5_K row: as Q4_K (qs at +48), with bit j of qh[l] as the fifth bit of
+// sub-block j's element l.
+template <int NT>
+__device__ __forceinline__ void row_q5_k(const uint8_t* wrow, const float* const* xs, int nt,
+                                         int nblocks, bool vec, int lane, float (&acc)[NT]) {
+    const int p = lane >> 3;
+    const int l0 = (lane & 7) << 2;
+    for (int b = 0; b < nblocks; ++b) {
+        const uint8_t* blk = wrow + static_cast<size_t>(b) * 176;
+        const uint32_t dm = ldg_u32(blk);
+        uint32_t s[3];
+        s[0] = ldg_u32(blk + 4);
+        s[1] = ldg_u32(blk + 8);
+        s[2] = ldg_u32(blk + 12);
+        const uint32_t q = ldg_u32(blk + 48 + 4 * lane);
+        const uint32_t hb = ldg_u32(blk + 16 + l0);  // qh[l0 .. l0+3]
+        const float d = f16_bits_to_f32(dm), dmin = f16_bits_to_f32(dm >> 16);
+        int sc0, m0, sc1, m1;
+        q4k_scale_min(s, 2 * p, sc0, m0);
+        q4k_scale_min(s, 2 * p + 1, sc1, m1);
+        const float ds0 = d * static_cast<float>(sc0), dm0 = dmin * static_cast<float>(m0);
+        const float ds1 = d * static_cast<float>(sc1), dm1 = dmin * static_cast<float>(m1);
+        float ql[4], qh[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            ql[i] = static_cast<float>(((q >> (8 * i)) & 0xFu) | (((hb >> (8 * i + 2 * p)) & 1u) << 4));
+            qh[i] = static_cast<float>(((q >> (8 * i + 4)) & 0xFu) | (((hb >> (8 * i + 2 * p + 1)) & 1u) << 4));
+        }
+        const int k0 = b * 256 + 64 * p + l0;
+#pragma unroll
+        for (int n = 0; n < NT; ++n) {
+            if (n < nt) {
+                const float4 xl = ldx4(xs[n] + k0, vec);
+                const float4 xh = ldx4(xs[n] + k0 + 32, vec);
+                const float sl = ql[0] * xl.x + ql[1] * xl.y + ql[2] * xl.z + ql[3] * xl.w;
+                const float sh = qh[0] * xh.x + qh[1] * xh.y + qh[2] * xh.z + qh[3] * xh.w;
+                const float xsl = (xl.x + xl.y) + (xl.z + xl.w);
+                const float xsh = (xh.x + xh.y) + (xh.z + xh.w);
+                acc[n] += ds0 * sl - dm0 * xsl + ds1 * sh - dm1 * xsh;
+            }
+        }
+    }
+}
+
 // Q6_K row: lane handles l = 2*(lane%16), l+1 of half h = lane/16, i.e. the
 // two elements at each of the four quarter offsets 0/32/64/96 of the half.
 template <int NT>
@@ -160,6 +204,42 @@ __device__ __forceinline__ void row_q8_0(const uint8_t* wrow, const float* const
     }
 }
 
+// Q4_0 row: 8 blocks (256 elements) per warp step; lane handles 8 elements
+// of block lane/4: part 0/1 the low nibbles of qs[0..7] / qs[8..15]
+// (elements 0..15), part 2/3 their high nibbles (16..31).
+template <int NT>
+__device__ __forceinline__ void row_q4_0(const uint8_t* wrow, const float* const* xs, int nt,
+                                         int nblocks, bool vec, int lane, float (&acc)[NT]) {
+    const int j = lane >> 2;
+    const int part = lane & 3;
+    for (int b0 = 0; b0 < nblocks; b0 += 8) {
+        const int bi = b0 + j;
+        if (bi < nblocks) {
+            const uint8_t* blk = wrow + static_cast<size_t>(bi) * 18;
+            const float d = f16_bits_to_f32(ldg_u16(blk));
+            const int sh = part >= 2 ? 4 : 0;
+            float q[8];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const uint32_t v = ldg_u16(blk + 2 + 8 * (part & 1) + 2 * i);
+                q[2 * i] = static_cast<float>(static_cast<int>((v >> sh) & 0xFu) - 8);
+                q[2 * i + 1] = static_cast<float>(static_cast<int>((v >> (8 + sh)) & 0xFu) - 8);
+            }
+            const int k0 = bi * 32 + 8 * part;
+#pragma unroll
+            for (int n = 0; n < NT; ++n) {
+                if (n < nt) {
+                    const float4 xa = ldx4(xs[n] + k0, vec);
+                    const float4 xb = ldx4(xs[n] + k0 + 4, vec);
+                    const float s = q[0] * xa.x + q[1] * xa.y + q[2] * xa.z + q[3] * xa.w + q[4] * xb.x +
+                                    q[5] * xb.y + q[6] * xb.z + q[7] * xb.w;
+                    acc[n] += d * s;
+                }
+            }
+        }
+    }
+}
+
 template <int NT>
 __global__ void __launch_bounds__(kWarps * 32) gemv_kernel(const __grid_constant__ OpList L) {
     int oi = 0;
@@ -177,7 +257,7 @@ __global__ void __launch_bounds__(kWarps * 32) gemv_kernel(const __grid_constant
     const uint8_t* xb = reinterpret_cast<const uint8_t*>(op.x) + b2 * op.x_nb2 + b3 * op.x_nb3;
     uint8_t* yb = reinterpret_cast<uint8_t*>(op.y) + b2 * op.y_nb2 + b3 * op.y_nb3;
     const bool vec = ((reinterpret_cast<uintptr_t>(xb) | static_cast<uintptr_t>(op.x_nb1)) & 15u) == 0;
-    const int nblocks = op.K / (op.type == kTypeQ8_0 ? 32 : 256);
+    const int nblocks = op.K / ((op.type == kTypeQ8_0 || op.type == kTypeQ4_0) ? 32 : 256);
 
     for (int n0 = 0; n0 < op.N; n0 += NT) {
         const int nt = min(NT, op.N - n0);
@@ -190,8 +270,12 @@ __global__ void __launch_bounds__(kWarps * 32) gemv_kernel(const __grid_constant
         for (int n = 0; n < NT; ++n) acc[n] = 0.f;
         if (op.type == kTypeQ4_K) {
             row_q4_k<NT>(wrow, xs, nt, nblocks, vec, lane, acc);
+        } else if (op.type == kTypeQ5_K) {
+            row_q5_k<NT>(wrow, xs, nt, nblocks, vec, lane, acc);
         } else if (op.type == kTypeQ6_K) {
             row_q6_k<NT>(wrow, xs, nt, nblocks, lane, acc);
+        } else if (op.type == kTypeQ4_0) {
+            row_q4_0<NT>(wrow, xs, nt, nblocks, vec, lane, acc);
         } else {
             row_q8_0<NT>(wrow, xs, nt, nblocks, vec, lane, acc);
         }
@@ -209,6 +293,10 @@ __global__ void dequant_kernel(int type, const uint8_t* __restrict__ src, float*
     if (i >= n) return;
     if (type == kTypeQ4_K) {
         dst[i] = q4k_dequant_elem(src + (i >> 8) * 144, static_cast<int>(i & 255));
+    } else if (type == kTypeQ5_K) {
+        dst[i] = q5k_dequant_elem(src + (i >> 8) * 176, static_cast<int>(i & 255));
+    } else if (type == kTypeQ4_0) {
+        dst[i] = q4_0_dequant_elem(src + (i >> 5) * 18, static_cast<int>(i & 31));
     } else if (type == kTypeQ6_K) {
         dst[i] = q6k_dequant_elem(src + (i >> 8) * 210, static_cast<int>(i & 255));
     } else {
@@ -219,16 +307,18 @@ __global__ void dequant_kernel(int type, const uint8_t* __restrict__ src, float*
 }  // namespace
 
 const char* check_mulmat_op(const MulMatOp& op) {
-    if (op.type != kTypeQ4_K && op.type != kTypeQ6_K && op.type != kTypeQ8_0) return "unsupported src0 type";
+    if (op.type != kTypeQ4_K && op.type != kTypeQ5_K && op.type != kTypeQ6_K && op.type != kTypeQ4_0 &&
+        op.type != kTypeQ8_0)
+        return "unsupported src0 type";
     if (op.M <= 0 || op.K <= 0 || op.N <= 0 || op.ne2 <= 0 || op.ne3 <= 0) return "empty or negative shape";
     if (op.r2 <= 0 || op.r3 <= 0) return "bad broadcast factor";
     if (op.K % block_elems(op.type) != 0) return "K is not a multiple of the block size";
     const uintptr_t wa = reinterpret_cast<uintptr_t>(op.w);
-    const int need = op.type == kTypeQ4_K ? 4 : 2;
+    const int need = (op.type == kTypeQ4_K || op.type == kTypeQ5_K) ? 4 : 2;
     if ((wa | static_cast<uintptr_t>(op.w_nb1) | static_cast<uintptr_t>(op.w_nb2) |
          static_cast<uintptr_t>(op.w_nb3)) % need)
-        return op.type == kTypeQ4_K ? "src0 data/strides must be 4-byte aligned for Q4_K"
-                                    : "src0 data/strides must be 2-byte aligned";
+        return need == 4 ? "src0 data/strides must be 4-byte aligned for Q4_K/Q5_K"
+                         : "src0 data/strides must be 2-byte aligned";
     if (op.w_nb1 < static_cast<int64_t>(op.K / block_elems(op.type)) * block_bytes(op.type)) return "src0 nb1 too small";
     if ((reinterpret_cast<uintptr_t>(op.x) | static_cast<uintptr_t>(op.x_nb1) | static_cast<uintptr_t>(op.x_nb2) |
          static_cast<uintptr_t>(op.x_nb3)) % 4)

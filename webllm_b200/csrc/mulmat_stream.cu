@@ -1268,6 +1268,7 @@ bool encode_weight_map(SOp& s, int row_bytes) {
 bool stream_supported(const MulMatOp* ops, int n_ops) {
     for (int i = 0; i < n_ops; ++i) {
         const MulMatOp& o = ops[i];
+        if (o.type != kTypeQ4_K && o.type != kTypeQ6_K && o.type != kTypeQ8_0) return false;
         if (o.ne2 != 1 || o.ne3 != 1) return false;
         if (o.N < 1 || o.N > kMaxNT) return false;
         if (o.K % 256 != 0) return false;  // whole 256-element groups (Q8_0 too)

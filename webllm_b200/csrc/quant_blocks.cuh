@@ -1,4 +1,4 @@
-// Device-side decoding of GGUF quant blocks (Q4_K, Q6_K, Q8_0).
+// Device-side decoding of GGUF quant blocks (Q4_K, Q5_K, Q6_K, Q4_0, Q8_0).
 //
 // Block layouts (bytes):
 //   Q4_K (256 elements, 144 B): f16 d @0, f16 dmin @2, scales[12] @4,
@@ -8,7 +8,13 @@
 //        6-bit pair unpacked as in src/inference/jsep/ops/matmul.ts:408-424.
 //   Q6_K (256 elements, 210 B): ql[128] @0, qh[64] @128, int8 scales[16]
 //        @192, f16 d @208. y = d*scales[e/16]*(q6 - 32).
+//   Q5_K (256 elements, 176 B): f16 d @0, f16 dmin @2, scales[12] @4 (as
+//        Q4_K), qh[32] @16, qs[128] @48. Element 32j+l: the nibble of
+//        qs[32(j/2)+l] (low for even j) plus bit j of qh[l] as bit 4;
+//        y = d*sc_j*q - dmin*m_j.
 //   Q8_0 (32 elements, 34 B): f16 d @0, int8 qs[32] @2. y = d*q.
+//   Q4_0 (32 elements, 18 B): f16 d @0, qs[16] @2; element l < 16 the low
+//        nibble of qs[l], 16+l the high one; y = d*(q - 8).
 #pragma once
 
 #include <cuda_fp16.h>
@@ -75,6 +81,32 @@ __device__ __forceinline__ float q6k_dequant_elem(const uint8_t* blk, int e) {
     const int sc = static_cast<int8_t>(blk[192 + (e >> 4)]);
     const float d = f16_bits_to_f32(ldg_u16(blk + 208));
     return __fmul_rn(__fmul_rn(d, static_cast<float>(sc)), static_cast<float>(q));
+}
+
+// Exact dequantization of element e (0..255) of a Q5_K block.
+__device__ __forceinline__ float q5k_dequant_elem(const uint8_t* blk, int e) {
+    const uint32_t dm = ldg_u16(blk) | (ldg_u16(blk + 2) << 16);
+    const float d = f16_bits_to_f32(dm), dmin = f16_bits_to_f32(dm >> 16);
+    uint32_t s[3];
+    s[0] = ldg_u16(blk + 4) | (ldg_u16(blk + 6) << 16);
+    s[1] = ldg_u16(blk + 8) | (ldg_u16(blk + 10) << 16);
+    s[2] = ldg_u16(blk + 12) | (ldg_u16(blk + 14) << 16);
+    const int j = e >> 5, l = e & 31;
+    int sc, m;
+    q4k_scale_min(s, j, sc, m);
+    const uint32_t byte = blk[48 + 32 * (j >> 1) + l];
+    const uint32_t q = ((j & 1) ? (byte >> 4) : (byte & 0xFu)) | (((blk[16 + l] >> j) & 1u) << 4);
+    // d*sc*q (q <= 31) and dmin*m are exact in f32; one rounding, as in the oracle
+    return __fsub_rn(__fmul_rn(__fmul_rn(d, static_cast<float>(sc)), static_cast<float>(q)),
+                     __fmul_rn(dmin, static_cast<float>(m)));
+}
+
+// Exact dequantization of element e (0..31) of a Q4_0 block.
+__device__ __forceinline__ float q4_0_dequant_elem(const uint8_t* blk, int e) {
+    const float d = f16_bits_to_f32(ldg_u16(blk));
+    const uint32_t byte = blk[2 + (e & 15)];
+    const int q = static_cast<int>(e < 16 ? (byte & 0xFu) : (byte >> 4)) - 8;
+    return __fmul_rn(d, static_cast<float>(q));
 }
 
 // Exact dequantization of element e (0..31) of a Q8_0 block.

@@ -100,6 +100,12 @@ uint64_t size_class(uint64_t size) {
     return (need + g - 1) / g * g;
 }
 
+// The src0 types this library runs (others: NOT_IMPLEMENTED, the caller falls back).
+bool quant_type_supported(int32_t t) {
+    return t == WLLM_TYPE_Q4_K || t == WLLM_TYPE_Q5_K || t == WLLM_TYPE_Q6_K || t == WLLM_TYPE_Q4_0 ||
+           t == WLLM_TYPE_Q8_0;
+}
+
 bool ensure_init(State& s) {
     if (s.device >= 0) return true;
     fail(s, "wllm_init has not been called");
@@ -205,8 +211,8 @@ int32_t decode_mulmat(State& s, const int32_t* desc, int32_t desc_words, Decoded
     const TensorMeta src0 = read_block(desc + 2 + WLLM_TENSOR_BLOCK_I32);
     const TensorMeta src1 = read_block(desc + 2 + 2 * WLLM_TENSOR_BLOCK_I32);
 
-    if (src0.type != WLLM_TYPE_Q4_K && src0.type != WLLM_TYPE_Q6_K && src0.type != WLLM_TYPE_Q8_0)
-        return WLLM_STATUS_NOT_IMPLEMENTED;  // F32/F16/Q4_0 and others: caller falls back
+    if (!quant_type_supported(src0.type))
+        return WLLM_STATUS_NOT_IMPLEMENTED;  // F32/F16 and other quant types: caller falls back
     if (src1.type != WLLM_TYPE_F32 || dst.type != WLLM_TYPE_F32)
         return fail(s, "dispatchMatmul: only src1=F32, dst=F32 (got src1=%d, dst=%d)", src1.type, dst.type);
 
@@ -346,8 +352,7 @@ int32_t ops_from_args(State& s, const char* what, const wllm_mulmat_args* ops, i
         return fail(s, "%s: n_ops=%d outside 1..%d", what, n_ops, wllm::kMaxOpsPerLaunch);
     for (int i = 0; i < n_ops; ++i) {
         const wllm_mulmat_args& a = ops[i];
-        if (a.src0_type != WLLM_TYPE_Q4_K && a.src0_type != WLLM_TYPE_Q6_K && a.src0_type != WLLM_TYPE_Q8_0)
-            return WLLM_STATUS_NOT_IMPLEMENTED;
+        if (!quant_type_supported(a.src0_type)) return WLLM_STATUS_NOT_IMPLEMENTED;
         if (!a.w || !a.x || !a.y) return fail(s, "%s: null pointer in op %d", what, i);
         MulMatOp& o = m[i];
         o = MulMatOp{};
@@ -741,8 +746,7 @@ int32_t wllm_mul_mat(int32_t src0_type, const void* w, int64_t w_row_bytes, cons
     State& s = S();
     std::lock_guard<std::mutex> g(s.mu);
     if (!ensure_init(s)) return WLLM_STATUS_FAILED;
-    if (src0_type != WLLM_TYPE_Q4_K && src0_type != WLLM_TYPE_Q6_K && src0_type != WLLM_TYPE_Q8_0)
-        return WLLM_STATUS_NOT_IMPLEMENTED;
+    if (!quant_type_supported(src0_type)) return WLLM_STATUS_NOT_IMPLEMENTED;
     if (!w || !x || !y) return fail(s, "wllm_mul_mat: null pointer");
     MulMatOp m{};
     m.w = static_cast<const uint8_t*>(w);
@@ -812,8 +816,7 @@ int32_t wllm_dequantize(int32_t type, const void* src, float* dst, int64_t n, vo
     State& s = S();
     std::lock_guard<std::mutex> g(s.mu);
     if (!ensure_init(s)) return WLLM_STATUS_FAILED;
-    if (type != WLLM_TYPE_Q4_K && type != WLLM_TYPE_Q6_K && type != WLLM_TYPE_Q8_0)
-        return fail(s, "wllm_dequantize: unsupported type %d", type);
+    if (!quant_type_supported(type)) return fail(s, "wllm_dequantize: unsupported type %d", type);
     if (!src || !dst || n <= 0 || n % wllm::block_elems(type) != 0)
         return fail(s, "wllm_dequantize: bad arguments");
     if (reinterpret_cast<uintptr_t>(src) % 2) return fail(s, "wllm_dequantize: src must be 2-byte aligned");

@@ -9,14 +9,18 @@ namespace wllm {
 
 // GGUF block geometry (src/models/gguf-parser.ts:273-294).
 constexpr int kTypeF32 = 0;
+constexpr int kTypeQ4_0 = 2;
 constexpr int kTypeQ8_0 = 8;
 constexpr int kTypeQ4_K = 12;
+constexpr int kTypeQ5_K = 13;
 constexpr int kTypeQ6_K = 14;
 
 inline int block_elems(int type) {
     switch (type) {
+        case kTypeQ4_0: return 32;
         case kTypeQ8_0: return 32;
         case kTypeQ4_K: return 256;
+        case kTypeQ5_K: return 256;
         case kTypeQ6_K: return 256;
         case kTypeF32: return 1;
         default: return 0;
@@ -24,8 +28,10 @@ inline int block_elems(int type) {
 }
 inline int block_bytes(int type) {
     switch (type) {
+        case kTypeQ4_0: return 18;
         case kTypeQ8_0: return 34;
         case kTypeQ4_K: return 144;
+        case kTypeQ5_K: return 176;
         case kTypeQ6_K: return 210;
         case kTypeF32: return 4;
         default: return 0;

@@ -32,6 +32,7 @@ GGML_TYPE_F16 = 1
 GGML_TYPE_Q4_0 = 2
 GGML_TYPE_Q8_0 = 8
 GGML_TYPE_Q4_K = 12
+GGML_TYPE_Q5_K = 13
 GGML_TYPE_Q6_K = 14
 
 TENSOR_BLOCK_I32 = 19
@@ -43,6 +44,7 @@ BLOCK_GEOMETRY = {
     GGML_TYPE_Q4_0: (32, 18),
     GGML_TYPE_Q8_0: (32, 34),
     GGML_TYPE_Q4_K: (256, 144),
+    GGML_TYPE_Q5_K: (256, 176),
     GGML_TYPE_Q6_K: (256, 210),
 }
 

@@ -8,6 +8,9 @@ Distributions (per block):
   Q6_K: 6-bit quants uniform in 0..63 (uniform ql/qh bytes), int8 scales
         uniform in -128..127, d = f16(|N(0,1)| * 2e-3).
   Q8_0: int8 quants uniform in -127..127, d = f16(|N(0,1)| * 1e-2).
+  Q5_K: as Q4_K, with the 32 high-bit bytes uniform (5-bit quants uniform in
+        0..31).
+  Q4_0: 4-bit quants uniform in 0..15, d = f16(|N(0,1)| * 1e-2).
 Activations are f32 N(0,1). No public dataset is involved.
 
 Model shapes are the per-layer MUL_MATs (name, src0 type, M rows, K).
@@ -16,9 +19,10 @@ from __future__ import annotations
 
 import numpy as np
 
-from .jsep import BLOCK_GEOMETRY, GGML_TYPE_Q4_K, GGML_TYPE_Q6_K, GGML_TYPE_Q8_0
+from .jsep import BLOCK_GEOMETRY, GGML_TYPE_Q4_0, GGML_TYPE_Q4_K, GGML_TYPE_Q5_K, GGML_TYPE_Q6_K, GGML_TYPE_Q8_0
 
 Q4_K, Q6_K, Q8_0 = GGML_TYPE_Q4_K, GGML_TYPE_Q6_K, GGML_TYPE_Q8_0
+Q5_K, Q4_0 = GGML_TYPE_Q5_K, GGML_TYPE_Q4_0
 
 # Llama-3.2-3B decode: hidden 3072, FFN 8192, 24 q heads / 8 kv heads x 128.
 LLAMA32_3B_LAYER = [
@@ -102,9 +106,30 @@ def q8_0_blocks(rng: np.random.Generator, M: int, K: int) -> np.ndarray:
     return blk.reshape(M, -1)
 
 
+def q5_k_blocks(rng: np.random.Generator, M: int, K: int) -> np.ndarray:
+    nb = M * (K // 256)
+    blk = np.empty((nb, 176), dtype=np.uint8)
+    blk[:, 0:2] = _f16_scale(rng, nb, 2e-3).view(np.uint8).reshape(nb, 2)
+    blk[:, 2:4] = _f16_scale(rng, nb, 2e-3).view(np.uint8).reshape(nb, 2)
+    blk[:, 4:] = rng.integers(0, 256, size=(nb, 172), dtype=np.uint8)
+    return blk.reshape(M, -1)
+
+
+def q4_0_blocks(rng: np.random.Generator, M: int, K: int) -> np.ndarray:
+    nb = M * (K // 32)
+    blk = np.empty((nb, 18), dtype=np.uint8)
+    blk[:, 0:2] = _f16_scale(rng, nb, 1e-2).view(np.uint8).reshape(nb, 2)
+    blk[:, 2:] = rng.integers(0, 256, size=(nb, 16), dtype=np.uint8)
+    return blk.reshape(M, -1)
+
+
 def weights(rng: np.random.Generator, qtype: int, M: int, K: int) -> np.ndarray:
     if qtype == Q4_K:
         return q4_k_blocks(rng, M, K)
+    if qtype == Q5_K:
+        return q5_k_blocks(rng, M, K)
+    if qtype == Q4_0:
+        return q4_0_blocks(rng, M, K)
     if qtype == Q6_K:
         return q6_k_blocks(rng, M, K)
     if qtype == Q8_0:
@@ -128,9 +153,11 @@ def weights_torch(gen, qtype: int, M: int, K: int, device):
         v = (torch.randn(nb, device=device, generator=gen).abs() * scale).to(torch.float16)
         return v.view(torch.uint8).view(nb, 2)
 
-    if qtype == Q4_K:
+    if qtype in (Q4_K, Q5_K):
         blk[:, 0:2] = f16(2e-3)
         blk[:, 2:4] = f16(2e-3)
+    elif qtype == Q4_0:
+        blk[:, 0:2] = f16(1e-2)
     elif qtype == Q6_K:
         blk[:, 208:210] = f16(2e-3)
     elif qtype == Q8_0:
