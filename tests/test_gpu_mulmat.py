@@ -172,6 +172,34 @@ def test_kquant_small_batches_vs_torch_fp64(runtime, qtype, M, K, N):
     assert rel <= GEMV_TOL, rel
 
 
+@pytest.mark.parametrize("N", [1, 2])
+@pytest.mark.parametrize("qtype,M,K", [(jsep.GGML_TYPE_Q5_K, 4096, 4096), (jsep.GGML_TYPE_Q5_K, 14336, 4096),
+                                       (jsep.GGML_TYPE_Q5_K, 4096, 14336), (jsep.GGML_TYPE_Q4_0, 4096, 4096),
+                                       (jsep.GGML_TYPE_Q4_0, 3000, 2304), (jsep.GGML_TYPE_Q4_0, 4096, 14336)])
+def test_q5k_q4_0_decode_vs_torch_fp64(runtime, qtype, M, K, N):
+    """Q5_K / Q4_0 decode (batch 1 and 2) on the streaming integer
+    tensor-core GEMV, against a float64 matmul of the device-dequantized
+    weights (bit-exact with the oracle's dequantization)."""
+    import torch
+
+    dev = torch.device("cuda", 0)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(qtype * 1000 + M + K + N)
+    w = synth.weights_torch(gen, qtype, M, K, dev)
+    x = torch.randn(N, K, device=dev, generator=gen)
+    y = torch.empty(N, M, device=dev)
+    torch.cuda.synchronize()
+    stream = jsep.library_stream()
+    assert jsep.mul_mat_device(qtype, w.data_ptr(), w.shape[1], x.data_ptr(), K, y.data_ptr(), M, M, K, N,
+                               stream) == jsep.STATUS_OK
+    wf = torch.empty(M, K, device=dev)
+    jsep.dequantize_device(qtype, w.data_ptr(), wf.data_ptr(), M * K, stream)
+    runtime.jsep_sync()
+    ref = (wf.double() @ x.double().t()).t()
+    rel = ((y.double() - ref).abs().max() / ref.abs().max()).item()
+    assert rel <= GEMV_TOL, rel
+
+
 @pytest.mark.parametrize("N", [65, 200])
 def test_q6k_prefill_sizes_vs_torch_fp64(runtime, N):
     """Q6_K with more than 64 vectors (prefill; several 32-vector tiles) on the

@@ -2,8 +2,8 @@
 // persistent, warp-specialised streaming GEMV over raw GGUF blocks.
 //
 // Data movement. The weight matrix is cut into units of 16 rows (one MMA
-// tile); each unit's rows into segments of at most 14 Q4_K / 9 Q6_K / 32 Q8_0
-// blocks. Warp 0 (copy warp, lane 0) moves each (unit, segment) into a ring
+// tile); each unit's rows into segments of at most 14 Q4_K / 11 Q5_K / 9 Q6_K
+// / 32 Q8_0 / 64 Q4_0 blocks. Warp 0 (copy warp, lane 0) moves each (unit, segment) into a ring
 // of shared-memory stages with ONE 2D tensor-map TMA copy (16 rows x the
 // segment, rounded out to 16-byte columns; evict-first L2 policy, each
 // weight byte is read once). Row layouts whose stride is not a multiple of 16
@@ -39,6 +39,11 @@
 //  - Q8_0 weights (34-byte blocks): the signed quants are the A operands as
 //    they are (aligned 32-bit loads and a funnel shift); each block's s32
 //    result is scaled by its rows' f16 d in f32.
+//  - Q5_K weights (176-byte blocks): as Q4_K, with the high-bit plane as a
+//    fifth ldmatrix per item; each sub-block's 5-bit quants (u8 0..31) enter
+//    the MMA and are scaled by sc.
+//  - Q4_0 weights (18-byte blocks): as Q8_0, the nibbles entering as s8
+//    q - 8.
 //
 // Launch: programmatic dependent launch. CTAs trigger their dependents at
 // entry; the copy warp streams weights (never written by a preceding kernel)
@@ -64,6 +69,8 @@ constexpr int kRows = 16;                     // rows per unit (one MMA m-tile)
 constexpr int kQ4kSegBlocks = 14;             // <= 2016 B per row and stage (a TMA box row is <= 2048 B)
 constexpr int kQ6kSegBlocks = 9;              // <= 1890 B (+ 16-byte window slack: a 1936 B box row)
 constexpr int kQ80SegBlocks = 32;             // 1088 B, whole 8-block groups
+constexpr int kQ5kSegBlocks = 11;             // <= 1936 B
+constexpr int kQ40SegBlocks = 64;             // 1152 B, whole 8-block groups
 constexpr int kMaxStages = 8;
 constexpr int kRedDelay = 2;                  // a unit's partials are summed this many units later
 // Unit slots in flight: consumer warps drift apart by at most kMaxStages
@@ -260,22 +267,42 @@ __device__ __forceinline__ void imma_s8s8_acc(int (&d)[4], uint32_t a0, uint32_t
 }
 
 __host__ __device__ __forceinline__ int seg_cap(int type) {
-    return type == kTypeQ4_K ? kQ4kSegBlocks : (type == kTypeQ6_K ? kQ6kSegBlocks : kQ80SegBlocks);
+    switch (type) {
+        case kTypeQ4_K: return kQ4kSegBlocks;
+        case kTypeQ5_K: return kQ5kSegBlocks;
+        case kTypeQ6_K: return kQ6kSegBlocks;
+        case kTypeQ4_0: return kQ40SegBlocks;
+        default: return kQ80SegBlocks;
+    }
 }
-__device__ __forceinline__ int block_elems_of(int type) { return type == kTypeQ8_0 ? 32 : 256; }
+__device__ __forceinline__ int block_elems_of(int type) {
+    return (type == kTypeQ8_0 || type == kTypeQ4_0) ? 32 : 256;
+}
 __device__ __forceinline__ int block_bytes_of(int type) {
-    return type == kTypeQ4_K ? 144 : (type == kTypeQ6_K ? 210 : 34);
+    switch (type) {
+        case kTypeQ4_K: return 144;
+        case kTypeQ5_K: return 176;
+        case kTypeQ6_K: return 210;
+        case kTypeQ4_0: return 18;
+        default: return 34;
+    }
+}
+
+// Four 4-bit quants q (0..15, one per byte) -> the int8 bytes q - 8: q ^ 8 is
+// q - 8 as a 4-bit two's-complement number; copy its sign bit (bit 3) into
+// bits 4..7 (0x08 * 0x1E = 0xF0 stays inside each byte).
+__device__ __forceinline__ uint32_t q4_signed(uint32_t q) {
+    const uint32_t t = q ^ 0x08080808u;
+    return t | ((t & 0x08080808u) * 0x1Eu);
 }
 
 // Byte layout of the shared-memory activation image.
 //  Every type (one shared image): int8 limb columns [2N][K + kXPad]
 //        (column 2t + l = limb l of vector t), then f32 d-factors [N][K/256]
 //        (max|x| / (127 * 16) per block), then exact f32 sums of x over
-//        32-element sub-blocks [N][K/32] (Q4_K) and over 16-element
-//        sub-blocks [N][K/16] (Q6_K). Q8_0 uses the limbs and d-factors.
-__host__ __device__ __forceinline__ bool limb_image(int type) {
-    return type == kTypeQ4_K || type == kTypeQ6_K || type == kTypeQ8_0;
-}
+//        32-element sub-blocks [N][K/32] (Q4_K, Q5_K) and over 16-element
+//        sub-blocks [N][K/16] (Q6_K). Q8_0 and Q4_0 use the limbs and
+//        d-factors.
 __host__ __device__ __forceinline__ int img_col_bytes(int K) { return K + kXPad; }
 __host__ __device__ __forceinline__ int img_inv_off(int K, int N) { return 2 * N * img_col_bytes(K); }
 // (16-byte aligned: the sums are read as float2)
@@ -298,9 +325,10 @@ __device__ __forceinline__ uint32_t lds_u16(const uint8_t* p) { return *reinterp
 // for j < 4 sc = s[j]&63, m = s[j+4]&63; for j >= 4 sc = (s[j+4]&15) |
 // (s[j-4]>>6)<<4, m = (s[j+4]>>4) | (s[j]>>6)<<4). sc comes out as an int,
 // times 16 for even (low-nibble) sub-blocks, whose quants enter the MMA
-// unscaled; m as dmin*m, exactly rounded: (2^23 + m) dmin - 2^23 dmin in one
-// FMA (both products exact: dmin has at most 11 significant bits).
-template <int NS, int NCH>
+// unscaled (RAW, for Q5_K: sc for every sub-block); m as dmin*m, exactly
+// rounded: (2^23 + m) dmin - 2^23 dmin in one FMA (both products exact: dmin
+// has at most 11 significant bits).
+template <int NS, int NCH, bool RAW = false>
 __device__ __forceinline__ void q4k_slot_scales(const uint4 h, int sl, int (&sc)[NCH], float (&mdm)[NCH], float& d) {
     d = f16_bits_to_f32(h.x);
     const float dmin = f16_bits_to_f32(h.x >> 16);
@@ -318,7 +346,7 @@ __device__ __forceinline__ void q4k_slot_scales(const uint4 h, int sl, int (&sc)
             scv = (b3 & 15u) | ((b1 >> 2) & 0x30u);
             mv = (b3 >> 4) | ((b2 >> 2) & 0x30u);
         }
-        sc[q] = static_cast<int>(scv << ((jj & 1) ? 0 : 4));
+        sc[q] = static_cast<int>(scv << (((jj & 1) || RAW) ? 0 : 4));
         mdm[q] = fmaf(__uint_as_float(0x4B000000u | mv), dmin, -dm23);
     }
 }
@@ -378,6 +406,75 @@ __device__ __forceinline__ void q4k_items(const uint8_t* blk, int wbox, uint32_t
             a3 += sch[k][q] * D[k][q][3];
         }
         const float xf = df[k * kCW];
+        yg = fmaf(fmaf(static_cast<float>(a1), 0.0078125f, static_cast<float>(a0)), dg[k] * xf, yg);
+        yh = fmaf(fmaf(static_cast<float>(a3), 0.0078125f, static_cast<float>(a2)), dh[k] * xf, yh);
+#pragma unroll
+        for (int q = 0; q < NCH; ++q) {
+            const float X = xs[k * kCW * 8 + q * NS + sl];
+            yg = fmaf(-mg[k][q], X, yg);
+            yh = fmaf(-mh[k][q], X, yh);
+        }
+    }
+}
+
+// One Q5_K item (176-byte blocks, 16-byte aligned like Q4_K): as q4k_items,
+// with the high-bit plane qh[32] at +16 (one more ldmatrix per item, same
+// lane layout as a quant pair) and the quants at +48. Sub-block j's 5-bit
+// quants are its nibbles (the high ones shifted down) with bit j of qh as
+// bit 4, u8 0..31; the scales are sc for every sub-block and the x factor
+// is 1/s (16 dfac).
+template <int NP, int NI>
+__device__ __forceinline__ void q5k_items(const uint8_t* blk, int wbox, uint32_t wl, uint32_t xaddr, uint32_t xzero,
+                                          bool xv0, bool xv1, const float* df, const float* xs, int g, int sl,
+                                          float& yg, float& yh) {
+    constexpr int NS = 4 / NP, NCH = 8 / NS;
+    constexpr int BS = kCW * 176;  // stage bytes between the items
+    constexpr int XS = kCW * 256;  // activation bytes between the items
+    int scg[NI][NCH], sch[NI][NCH];
+    float mg[NI][NCH], mh[NI][NCH], dg[NI], dh[NI];
+#pragma unroll
+    for (int k = 0; k < NI; ++k) {
+        const uint4 hg = *reinterpret_cast<const uint4*>(blk + k * BS + g * wbox);
+        const uint4 hh = *reinterpret_cast<const uint4*>(blk + k * BS + (g + 8) * wbox);
+        q4k_slot_scales<NS, NCH, true>(hg, sl, scg[k], mg[k], dg[k]);
+        q4k_slot_scales<NS, NCH, true>(hh, sl, sch[k], mh[k], dh[k]);
+    }
+    int D[NI][NCH][4];
+#pragma unroll
+    for (int k = 0; k < NI; ++k)
+#pragma unroll
+        for (int q = 0; q < NCH; ++q) D[k][q][0] = D[k][q][1] = D[k][q][2] = D[k][q][3] = 0;
+    const uint32_t wbase = smem_u32(blk) + wl;  // wl points at +16: qh, then the quant pairs at +48
+    uint32_t hq[NI][4];
+#pragma unroll
+    for (int k = 0; k < NI; ++k) ldmatrix_x4_at(hq[k], wbase + k * BS);
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {
+#pragma unroll
+        for (int k = 0; k < NI; ++k) {
+            uint32_t w[4], x[4], lo[4], hi[4];
+            ldmatrix_x4_at(w, wbase + k * BS + 32 + 32 * p);
+            ldmatrix_x4_at(x, ((p & 1) ? xv1 : xv0) ? xaddr + k * XS + 64 * p : xzero);
+#pragma unroll
+            for (int r = 0; r < 4; ++r) {
+                lo[r] = (w[r] & 0x0F0F0F0Fu) | (((hq[k][r] >> (2 * p)) & 0x01010101u) << 4);
+                hi[r] = ((w[r] >> 4) & 0x0F0F0F0Fu) | (((hq[k][r] >> (2 * p + 1)) & 0x01010101u) << 4);
+            }
+            imma_u8s8_acc(D[k][(2 * p) / NS], lo[0], lo[1], lo[2], lo[3], x[0], x[1]);
+            imma_u8s8_acc(D[k][(2 * p + 1) / NS], hi[0], hi[1], hi[2], hi[3], x[2], x[3]);
+        }
+    }
+#pragma unroll
+    for (int k = 0; k < NI; ++k) {
+        int a0 = 0, a1 = 0, a2 = 0, a3 = 0;  // (g, limb 0), (g, limb 1), (g+8, l0), (g+8, l1)
+#pragma unroll
+        for (int q = 0; q < NCH; ++q) {
+            a0 += scg[k][q] * D[k][q][0];
+            a1 += scg[k][q] * D[k][q][1];
+            a2 += sch[k][q] * D[k][q][2];
+            a3 += sch[k][q] * D[k][q][3];
+        }
+        const float xf = 16.f * df[k * kCW];
         yg = fmaf(fmaf(static_cast<float>(a1), 0.0078125f, static_cast<float>(a0)), dg[k] * xf, yg);
         yh = fmaf(fmaf(static_cast<float>(a3), 0.0078125f, static_cast<float>(a2)), dh[k] * xf, yh);
 #pragma unroll
@@ -486,17 +583,19 @@ __device__ __forceinline__ void q6k_item(const uint8_t* pg, const uint8_t* ph, u
     yh = fmaf(dh, fmaf(fmaf(static_cast<float>(a3), 0.0078125f, static_cast<float>(a2)), xf, -32.f * sh), yh);
 }
 
-// One Q8_0 item: 16 rows x one group of 8 blocks (256 elements, one x
+// One Q8_0 / Q4_0 item: 16 rows x one group of 8 blocks (256 elements, one x
 // scale), for NP = N rounded up to a power of two. Each 32-element block is
 // one MMA on the signed quants as they are; as for Q4_K, NS = 4/NP blocks
 // share an accumulator through the B-column slots (block j: slot j % NS,
 // chain j / NS), and lane (g, c) scales its slot's blocks j = q NS + sl of
-// rows g and g + 8 by their f16 d in f32. Blocks are 34 bytes, so they sit
-// 2-byte aligned in shared memory: aligned 32-bit loads and a funnel shift.
-template <int NP>
+// rows g and g + 8 by their f16 d in f32. Blocks are 34 (18) bytes, so they
+// sit 2-byte aligned in shared memory: aligned 32-bit loads and a funnel
+// shift. Q4_0's nibbles enter as s8 q - 8 (a 4-bit sign extension).
+template <int NP, int TYPE>
 __device__ __forceinline__ void q8_item(const uint8_t* pg, const uint8_t* ph, uint32_t xaddr, uint32_t xzero,
                                         bool xv0, bool xv1, float xf, int c, int sl, float& yg, float& yh) {
     constexpr int NS = 4 / NP, NCH = 8 / NS;
+    constexpr int BB = TYPE == kTypeQ4_0 ? 18 : 34;  // block bytes
     int D[NCH][4];
 #pragma unroll
     for (int q = 0; q < NCH; ++q) D[q][0] = D[q][1] = D[q][2] = D[q][3] = 0;
@@ -507,10 +606,18 @@ __device__ __forceinline__ void q8_item(const uint8_t* pg, const uint8_t* ph, ui
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
             const int j = 2 * pp + h;
-            const uint8_t* bg = pg + 34 * j + 2 + 4 * c;
-            const uint8_t* bh = ph + 34 * j + 2 + 4 * c;
-            imma_s8s8_acc(D[j / NS], lds_u32_any(bg), lds_u32_any(bh), lds_u32_any(bg + 16), lds_u32_any(bh + 16),
-                          x[2 * h], x[2 * h + 1]);
+            const uint8_t* bg = pg + BB * j + 2 + 4 * c;
+            const uint8_t* bh = ph + BB * j + 2 + 4 * c;
+            if (TYPE == kTypeQ4_0) {
+                // elements 4c.. are the low nibbles of qs[4c..], 16+4c.. the high ones
+                const uint32_t wg = lds_u32_any(bg), wh = lds_u32_any(bh);
+                imma_s8s8_acc(D[j / NS], q4_signed(wg & 0x0F0F0F0Fu), q4_signed(wh & 0x0F0F0F0Fu),
+                              q4_signed((wg >> 4) & 0x0F0F0F0Fu), q4_signed((wh >> 4) & 0x0F0F0F0Fu), x[2 * h],
+                              x[2 * h + 1]);
+            } else {
+                imma_s8s8_acc(D[j / NS], lds_u32_any(bg), lds_u32_any(bh), lds_u32_any(bg + 16), lds_u32_any(bh + 16),
+                              x[2 * h], x[2 * h + 1]);
+            }
         }
     }
     // |D| <= 32 * 127 * 127 per block
@@ -518,7 +625,7 @@ __device__ __forceinline__ void q8_item(const uint8_t* pg, const uint8_t* ph, ui
 #pragma unroll
     for (int q = 0; q < NCH; ++q) {
         const int j = q * NS + sl;
-        const float dg = f16_bits_to_f32(lds_u16(pg + 34 * j)), dh = f16_bits_to_f32(lds_u16(ph + 34 * j));
+        const float dg = f16_bits_to_f32(lds_u16(pg + BB * j)), dh = f16_bits_to_f32(lds_u16(ph + BB * j));
         ag = fmaf(fmaf(static_cast<float>(D[q][1]), 0.0078125f, static_cast<float>(D[q][0])), dg, ag);
         ah = fmaf(fmaf(static_cast<float>(D[q][3]), 0.0078125f, static_cast<float>(D[q][2])), dh, ah);
     }
@@ -806,6 +913,57 @@ __device__ __forceinline__ void q4k_unit(const OpRegs& op, const Q4Lane& q, Ring
     }
 }
 
+// All segments of one Q5_K unit for this consumer warp (see q4k_unit).
+template <int NP, int NT>
+__device__ __forceinline__ void q5k_unit(const OpRegs& op, const Q4Lane& q, Ring& R, uint32_t xzero, int lane,
+                                         int cw, float* ub) {
+    const int N = op.N, nblocks = op.K / 256;
+    const int g = lane >> 2, sl = q.sl, tk = q.tk;
+    const uint32_t wl = q.wl, xcol = q.xcol;
+    const bool xv0 = q.xv0, xv1 = q.xv1;
+    const float* dfac = q.dfac;
+    const float* Xs = q.Xs;
+    float yg = 0.f, yh = 0.f;  // slot sl's part of vector tk, rows g and g + 8
+    for (int sg = 0; sg < op.nseg; ++sg) {
+        const int b0 = sg * op.seg_blocks;
+        const int nb = min(op.seg_blocks, nblocks - b0);
+        // this warp's first item of the segment; a warp without one neither
+        // waits for nor releases the stage (the warp with item 0 releases it
+        // for them)
+        const int i0 = (cw - static_cast<int>(R.item_base % kCW) + kCW) % kCW;
+        if (i0 < nb) {
+            ring_wait(R, lane);
+            const uint8_t* stage = R.stages + R.slot * R.SB;
+            int i = i0;
+            // item pairs at N = 1 (at N = 2 the doubled accumulators would spill)
+            for (; NP == 1 && i + kCW < nb; i += 2 * kCW) {
+                const int bg = b0 + i;
+                q5k_items<NP, 2>(stage + i * 176, op.wbox, wl, xcol + bg * 256, xzero, xv0, xv1, dfac + bg,
+                                 Xs + bg * 8, g, sl, yg, yh);
+            }
+            for (; i < nb; i += kCW) {
+                const int bg = b0 + i;
+                q5k_items<NP, 1>(stage + i * 176, op.wbox, wl, xcol + bg * 256, xzero, xv0, xv1, dfac + bg,
+                                 Xs + bg * 8, g, sl, yg, yh);
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cnt(&R.empty[R.slot], i0 == 0 ? 1u + kCW - min(nb, kCW) : 1u);
+        }
+        R.item_base += nb;
+        R.advance();
+    }
+    // sum the slots of each vector (lanes c with the same c % NP)
+#pragma unroll
+    for (int o = NP; o < 4; o <<= 1) {
+        yg += __shfl_xor_sync(0xffffffffu, yg, o);
+        yh += __shfl_xor_sync(0xffffffffu, yh, o);
+    }
+    if (sl == 0 && tk < N) {
+        ub[g * NT + tk] = yg;
+        ub[(g + 8) * NT + tk] = yh;
+    }
+}
+
 // All segments of one Q6_K unit for this consumer warp (see q4k_unit). Each
 // row's copy window starts at its segment start rounded down to 16 bytes;
 // glo is the low word of the unit's first row address.
@@ -883,11 +1041,12 @@ __device__ bool tp_wait_peers(const uint32_t* const* sig, int world, int rank, u
     return true;
 }
 
-// All segments of one Q8_0 unit for this consumer warp (see q6k_unit); an
-// item is a group of 8 blocks (segments hold whole groups).
-template <int NP, int NT>
+// All segments of one Q8_0 / Q4_0 unit for this consumer warp (see
+// q6k_unit); an item is a group of 8 blocks (segments hold whole groups).
+template <int NP, int NT, int TYPE>
 __device__ __forceinline__ void q8_unit(const OpRegs& op, const Q4Lane& q, Ring& R, uint32_t xzero, uint32_t glo,
                                         int lane, int cw, float* ub) {
+    constexpr int BB = TYPE == kTypeQ4_0 ? 18 : 34;  // block bytes
     const int N = op.N, nblocks = op.K / 32;
     const int g = lane >> 2, c = lane & 3, sl = q.sl, tk = q.tk;
     const uint32_t nb1 = static_cast<uint32_t>(op.w_nb1);
@@ -899,13 +1058,13 @@ __device__ __forceinline__ void q8_unit(const OpRegs& op, const Q4Lane& q, Ring&
         if (i0 < ng) {
             ring_wait(R, lane);
             const uint8_t* stage = R.stages + R.slot * R.SB;
-            const uint32_t gl = glo + static_cast<uint32_t>(b0 * 34);
+            const uint32_t gl = glo + static_cast<uint32_t>(b0 * BB);
             const uint8_t* pg = stage + g * op.wbox + ((gl + static_cast<uint32_t>(g) * nb1) & 15u);
             const uint8_t* ph = stage + (g + 8) * op.wbox + ((gl + static_cast<uint32_t>(g + 8) * nb1) & 15u);
             for (int i = i0; i < ng; i += kCW) {
                 const int gg = b0 / 8 + i;  // 256-element group
-                q8_item<NP>(pg + i * 272, ph + i * 272, q.xcol + gg * 256, xzero, q.xv0, q.xv1, 16.f * q.dfac[gg], c,
-                            sl, yg, yh);
+                q8_item<NP, TYPE>(pg + i * 8 * BB, ph + i * 8 * BB, q.xcol + gg * 256, xzero, q.xv0, q.xv1,
+                                  16.f * q.dfac[gg], c, sl, yg, yh);
             }
             __syncwarp();
             if (lane == 0) mbar_arrive_cnt(&R.empty[R.slot], i0 == 0 ? 1u + kCW - min(ng, kCW) : 1u);
@@ -1135,13 +1294,13 @@ __global__ void __launch_bounds__(kThreads, 1) stream_gemv_kernel(const __grid_c
             } while (oi + 1 < n_ops && u >= T.op[oi + 1].unit_begin);
             const OpInfo& oo = T.op[oi];
             if (staged < 0 || T.op[staged].x != oo.x || T.op[staged].K != oo.K || T.op[staged].N != oo.N ||
-                T.op[staged].x_nb1 != oo.x_nb1 || limb_image(T.op[staged].type) != limb_image(oo.type)) {
+                T.op[staged].x_nb1 != oo.x_nb1) {
                 consumers_sync();  // nobody still reads the previous image
                 stage_activations(oo, xsm, lane, cw);
                 if (ct == 0 && useq == 0) mbar_arrive_cnt(xready, 1u);  // the copy warp may go on
                 staged = oi;
             }
-            if (oo.type == kTypeQ4_K || oo.type == kTypeQ8_0)
+            if (oo.type != kTypeQ6_K)
                 q4 = (NT == 1 || oo.N == 1) ? q4k_lane<1>(oo, xsm, lane) : q4k_lane<2>(oo, xsm, lane);
             if (oo.type == kTypeQ6_K) q6 = (NT == 1 || oo.N == 1) ? q6k_lane<1>(oo, xsm, lane) : q6k_lane<2>(oo, xsm, lane);
             op = op_regs(oo);
@@ -1160,6 +1319,12 @@ __global__ void __launch_bounds__(kThreads, 1) stream_gemv_kernel(const __grid_c
                 q4k_unit<1, NT>(op, q4, R, smem_u32(zrow), lane, cw, ub);
             else
                 q4k_unit<2, NT>(op, q4, R, smem_u32(zrow), lane, cw, ub);
+        } else if (op.type == kTypeQ5_K) {
+            // ================= Q5_K, integer tensor cores =================
+            if (NT == 1 || N == 1)
+                q5k_unit<1, NT>(op, q4, R, smem_u32(zrow), lane, cw, ub);
+            else
+                q5k_unit<2, NT>(op, q4, R, smem_u32(zrow), lane, cw, ub);
         } else if (op.type == kTypeQ6_K) {
             // ================= Q6_K, integer tensor cores =================
             const uint32_t glo =
@@ -1169,13 +1334,20 @@ __global__ void __launch_bounds__(kThreads, 1) stream_gemv_kernel(const __grid_c
             else
                 q6k_unit<2, NT>(op, q6, R, smem_u32(zrow), glo, lane, cw, ub);
         } else {
-            // ================= Q8_0, integer tensor cores =================
+            // ============= Q8_0 / Q4_0, integer tensor cores =============
             const uint32_t glo =
                 static_cast<uint32_t>(reinterpret_cast<uintptr_t>(op.w + static_cast<int64_t>(r0) * op.w_nb1));
-            if (NT == 1 || N == 1)
-                q8_unit<1, NT>(op, q4, R, smem_u32(zrow), glo, lane, cw, ub);
-            else
-                q8_unit<2, NT>(op, q4, R, smem_u32(zrow), glo, lane, cw, ub);
+            if (op.type == kTypeQ4_0) {
+                if (NT == 1 || N == 1)
+                    q8_unit<1, NT, kTypeQ4_0>(op, q4, R, smem_u32(zrow), glo, lane, cw, ub);
+                else
+                    q8_unit<2, NT, kTypeQ4_0>(op, q4, R, smem_u32(zrow), glo, lane, cw, ub);
+            } else {
+                if (NT == 1 || N == 1)
+                    q8_unit<1, NT, kTypeQ8_0>(op, q4, R, smem_u32(zrow), glo, lane, cw, ub);
+                else
+                    q8_unit<2, NT, kTypeQ8_0>(op, q4, R, smem_u32(zrow), glo, lane, cw, ub);
+            }
         }
         // ---- unit hand-off: publish this warp's partials; the owner sums them later ----
         if (own == cw && lane == 0) {
@@ -1268,13 +1440,16 @@ bool encode_weight_map(SOp& s, int row_bytes) {
 bool stream_supported(const MulMatOp* ops, int n_ops) {
     for (int i = 0; i < n_ops; ++i) {
         const MulMatOp& o = ops[i];
-        if (o.type != kTypeQ4_K && o.type != kTypeQ6_K && o.type != kTypeQ8_0) return false;
+        if (o.type != kTypeQ4_K && o.type != kTypeQ5_K && o.type != kTypeQ6_K && o.type != kTypeQ4_0 &&
+            o.type != kTypeQ8_0)
+            return false;
         if (o.ne2 != 1 || o.ne3 != 1) return false;
         if (o.N < 1 || o.N > kMaxNT) return false;
         if (o.K % 256 != 0) return false;  // whole 256-element groups (Q8_0 too)
         if (o.K > kMaxK) return false;
-        if (o.type == kTypeQ4_K && ((reinterpret_cast<uintptr_t>(o.w) | static_cast<uintptr_t>(o.w_nb1)) & 15))
-            return false;  // 16-byte header loads from shared memory
+        if ((o.type == kTypeQ4_K || o.type == kTypeQ5_K) &&
+            ((reinterpret_cast<uintptr_t>(o.w) | static_cast<uintptr_t>(o.w_nb1)) & 15))
+            return false;  // 16-byte header loads and ldmatrix rows from shared memory
         if ((reinterpret_cast<uintptr_t>(o.w) | static_cast<uintptr_t>(o.w_nb1)) & 1)
             return false;  // 2-byte f16 and word-pair loads from shared memory
         if ((reinterpret_cast<uintptr_t>(o.x) | static_cast<uintptr_t>(o.x_nb1)) & 15) return false;
@@ -1313,13 +1488,14 @@ int launch_stream(const MulMatOp* ops, int n_ops, cudaStream_t stream, int num_s
         const int cap = seg_cap(o.type);
         const int nseg = (nblocks + cap - 1) / cap;
         int seg = (nblocks + nseg - 1) / nseg;
-        if (o.type == kTypeQ8_0) seg = (seg + 7) / 8 * 8;
+        if (o.type == kTypeQ8_0 || o.type == kTypeQ4_0) seg = (seg + 7) / 8 * 8;
         s.seg_blocks = seg;
         s.nseg = (nblocks + seg - 1) / seg;
         // stage row width: the segment plus room for the 16-byte window rounding,
         // made == 16 mod 32 so the 8 rows a warp reads hit 8 different bank groups
         const int bb = block_bytes(o.type);
-        int wbox = o.type == kTypeQ4_K ? seg * bb : (seg * bb + 30 + 15) / 16 * 16;
+        const bool aligned_rows = o.type == kTypeQ4_K || o.type == kTypeQ5_K;  // 16-byte blocks
+        int wbox = aligned_rows ? seg * bb : (seg * bb + 30 + 15) / 16 * 16;
         if (wbox % 32 == 0) wbox += 16;
         s.wbox = wbox;
         s.use_tma = encode_weight_map(s, nblocks * bb) ? 1 : 0;
