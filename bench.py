@@ -46,7 +46,7 @@ WORKLOAD = "llama-3.2-3b decode sweep (28 layers x 7 GEMVs, Q4_K/Q6_K x f32, bat
 # DRAM bytes (read + write) of one layer's four GEMV launches, summed from an
 # ncu capture of this workload (profiles/stream_gemv_llama32_3b_decode.md);
 # the algorithmic bytes are 64,139,264 per layer.
-NCU_DRAM_BYTES_PER_LAYER = 64_273_024
+NCU_DRAM_BYTES_PER_LAYER = 64_314_496
 FALLBACK_HBM_GBS = 6650.0
 
 
