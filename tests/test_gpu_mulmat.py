@@ -285,7 +285,7 @@ PARTIAL_ROUND_LAUNCHES = {
 }
 
 
-@pytest.mark.parametrize("N", [1, 2])
+@pytest.mark.parametrize("N", [1, 2, 3, 4])
 @pytest.mark.parametrize("case", sorted(PARTIAL_ROUND_LAUNCHES))
 def test_partial_round_launches_vs_torch_fp64(runtime, case, N):
     """Grouped decode launches with more 16-row units than SMs and a partial

@@ -345,8 +345,9 @@ size_t mulmat_workspace_bytes(const MulMatOp* ops, int n_ops) {
 int launch_mulmat(const MulMatOp* ops, int n_ops, cudaStream_t stream, int num_sms, void* workspace,
                   size_t workspace_bytes) {
     if (n_ops < 1 || n_ops > kMaxOpsPerLaunch) return -static_cast<int>(cudaErrorInvalidValue);
-    // prefill-sized ops (Q4_K, N >= 65) and small batches (N >= 3, every type) run as
-    // tensor-core GEMMs, one launch each; the rest together
+    // prefill-sized ops (Q4_K, N >= 65) and small batches (N >= 5, or 3-4 where
+    // the streaming kernel cannot take them) run as tensor-core GEMMs, one
+    // launch each; the rest together
     int launched = 0;
     MulMatOp rest[kMaxOpsPerLaunch];
     int n_rest = 0;
@@ -355,7 +356,8 @@ int launch_mulmat(const MulMatOp* ops, int n_ops, cudaStream_t stream, int num_s
             const int rc = launch_prefill(ops[i], workspace, workspace_bytes, stream);
             if (rc < 0) return rc;
             launched += rc;
-        } else if (batched_supported(ops[i]) && workspace && workspace_bytes >= batched_workspace_bytes(ops[i])) {
+        } else if (batched_supported(ops[i]) && !(ops[i].N <= 4 && stream_supported(&ops[i], 1)) && workspace &&
+                   workspace_bytes >= batched_workspace_bytes(ops[i])) {
             const int rc = launch_batched(ops[i], workspace, workspace_bytes, stream);
             if (rc < 0) return rc;
             launched += rc;

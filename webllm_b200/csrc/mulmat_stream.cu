@@ -1,4 +1,4 @@
-// Decode-regime quantized MUL_MAT (N = 1 or 2 activation vectors): a
+// Decode-regime quantized MUL_MAT (N = 1 to 4 activation vectors): a
 // persistent, warp-specialised streaming GEMV over raw GGUF blocks.
 //
 // Data movement. The weight matrix is cut into units of 16 rows (one MMA
@@ -78,7 +78,8 @@ constexpr int kRedDelay = 2;                  // a unit's partials are summed th
 // is summed before any warp writes it again.
 constexpr int kUnitSlots = kMaxStages + kRedDelay + 2;
 constexpr int kXPad = 16;                     // bytes after each int8 activation column (ldmatrix banks)
-constexpr int kMaxNT = 2;
+constexpr int kMaxNT = 4;
+constexpr int kMaxK34 = 8192;                 // K limit for 3 or 4 vectors (their activation image)
 // Boxes the copy warp issues before the consumers have staged the first
 // activation image: the activation loads wait behind whatever weight requests
 // are queued in the memory system, so a launch's first boxes are held back
@@ -538,7 +539,7 @@ __device__ __forceinline__ void q6k_item(const uint8_t* pg, const uint8_t* ph, u
                                          bool xv, float xf, const float* xs, int c, int sl, float& yg, float& yh) {
     constexpr int NS = 4 / NP, NCH = 16 / NS, NCHH = NCH / 2;  // chains per half-block
     // |D| <= 16 * 63 * 127 per sub-block; times |sc| <= 128, summed over the
-    // lane's 4 or 8 sub-blocks: well inside int32
+    // lane's 4, 8 or 16 sub-blocks: well inside int32
     int a0 = 0, a1 = 0, a2 = 0, a3 = 0;
     float sg = 0.f, sh = 0.f;
 #pragma unroll
@@ -559,9 +560,19 @@ __device__ __forceinline__ void q6k_item(const uint8_t* pg, const uint8_t* ph, u
             const int p = 2 * h + pp;  // MMAs 2p, 2p+1 = groups 2pp, 2pp+1 of half h
             uint32_t x[4];
             ldmatrix_x4_at(x, xv ? xaddr + 64 * p : xzero);
-            imma_u8s8_acc(D[(4 * pp) / NS], A[0][2 * pp], A[1][2 * pp], A[2][2 * pp], A[3][2 * pp], x[0], x[1]);
-            imma_u8s8_acc(D[(4 * pp + 2) / NS], A[0][2 * pp + 1], A[1][2 * pp + 1], A[2][2 * pp + 1],
-                          A[3][2 * pp + 1], x[2], x[3]);
+            if constexpr (NS == 1) {
+                // one slot (4 vectors): the two 16-element sub-blocks of an MMA
+                // step cannot share its columns, so each gets its own MMA with
+                // the other half of the A fragment zero
+                imma_u8s8_acc(D[4 * pp], A[0][2 * pp], A[1][2 * pp], 0u, 0u, x[0], x[1]);
+                imma_u8s8_acc(D[4 * pp + 1], 0u, 0u, A[2][2 * pp], A[3][2 * pp], x[0], x[1]);
+                imma_u8s8_acc(D[4 * pp + 2], A[0][2 * pp + 1], A[1][2 * pp + 1], 0u, 0u, x[2], x[3]);
+                imma_u8s8_acc(D[4 * pp + 3], 0u, 0u, A[2][2 * pp + 1], A[3][2 * pp + 1], x[2], x[3]);
+            } else {
+                imma_u8s8_acc(D[(4 * pp) / NS], A[0][2 * pp], A[1][2 * pp], A[2][2 * pp], A[3][2 * pp], x[0], x[1]);
+                imma_u8s8_acc(D[(4 * pp + 2) / NS], A[0][2 * pp + 1], A[1][2 * pp + 1], A[2][2 * pp + 1],
+                              A[3][2 * pp + 1], x[2], x[3]);
+            }
         }
         // chain q of this half holds sub-blocks (h NCHH + q) NS + slot
 #pragma unroll
@@ -1269,8 +1280,8 @@ __global__ void __launch_bounds__(kThreads, 1) stream_gemv_kernel(const __grid_c
         const int slot = j % kUnitSlots;
         ring_barrier_wait(&ubar[slot], static_cast<uint32_t>(j / kUnitSlots) & 1u, poisoned, lane);
         const UnitMeta m = umeta[slot];
-        if (lane < kRows * m.n) {
-            const int r = lane / m.n, n = lane - r * m.n;
+        for (int e = lane; e < kRows * m.n; e += 32) {  // (two rounds at 3 or 4 vectors)
+            const int r = e / m.n, n = e - r * m.n;
             const float* vb = ubuf + slot * kCW * kRows * NT + r * NT + n;
             float v = 0.f;
 #pragma unroll
@@ -1301,8 +1312,11 @@ __global__ void __launch_bounds__(kThreads, 1) stream_gemv_kernel(const __grid_c
                 staged = oi;
             }
             if (oo.type != kTypeQ6_K)
-                q4 = (NT == 1 || oo.N == 1) ? q4k_lane<1>(oo, xsm, lane) : q4k_lane<2>(oo, xsm, lane);
-            if (oo.type == kTypeQ6_K) q6 = (NT == 1 || oo.N == 1) ? q6k_lane<1>(oo, xsm, lane) : q6k_lane<2>(oo, xsm, lane);
+                q4 = (NT == 1 || oo.N == 1) ? q4k_lane<1>(oo, xsm, lane)
+                                            : ((NT == 2 || oo.N == 2) ? q4k_lane<2>(oo, xsm, lane) : q4k_lane<4>(oo, xsm, lane));
+            if (oo.type == kTypeQ6_K)
+                q6 = (NT == 1 || oo.N == 1) ? q6k_lane<1>(oo, xsm, lane)
+                                            : ((NT == 2 || oo.N == 2) ? q6k_lane<2>(oo, xsm, lane) : q6k_lane<4>(oo, xsm, lane));
             op = op_regs(oo);
             next_begin = oi + 1 < n_ops ? T.op[oi + 1].unit_begin : total;
         }
@@ -1317,22 +1331,28 @@ __global__ void __launch_bounds__(kThreads, 1) stream_gemv_kernel(const __grid_c
             // ================= Q4_K, integer tensor cores =================
             if (NT == 1 || N == 1)
                 q4k_unit<1, NT>(op, q4, R, smem_u32(zrow), lane, cw, ub);
-            else
+            else if (NT == 2 || N == 2)
                 q4k_unit<2, NT>(op, q4, R, smem_u32(zrow), lane, cw, ub);
+            else if constexpr (NT == 4)
+                q4k_unit<4, NT>(op, q4, R, smem_u32(zrow), lane, cw, ub);
         } else if (op.type == kTypeQ5_K) {
             // ================= Q5_K, integer tensor cores =================
             if (NT == 1 || N == 1)
                 q5k_unit<1, NT>(op, q4, R, smem_u32(zrow), lane, cw, ub);
-            else
+            else if (NT == 2 || N == 2)
                 q5k_unit<2, NT>(op, q4, R, smem_u32(zrow), lane, cw, ub);
+            else if constexpr (NT == 4)
+                q5k_unit<4, NT>(op, q4, R, smem_u32(zrow), lane, cw, ub);
         } else if (op.type == kTypeQ6_K) {
             // ================= Q6_K, integer tensor cores =================
             const uint32_t glo =
                 static_cast<uint32_t>(reinterpret_cast<uintptr_t>(op.w + static_cast<int64_t>(r0) * op.w_nb1));
             if (NT == 1 || N == 1)
                 q6k_unit<1, NT>(op, q6, R, smem_u32(zrow), glo, lane, cw, ub);
-            else
+            else if (NT == 2 || N == 2)
                 q6k_unit<2, NT>(op, q6, R, smem_u32(zrow), glo, lane, cw, ub);
+            else if constexpr (NT == 4)
+                q6k_unit<4, NT>(op, q6, R, smem_u32(zrow), glo, lane, cw, ub);
         } else {
             // ============= Q8_0 / Q4_0, integer tensor cores =============
             const uint32_t glo =
@@ -1340,13 +1360,17 @@ __global__ void __launch_bounds__(kThreads, 1) stream_gemv_kernel(const __grid_c
             if (op.type == kTypeQ4_0) {
                 if (NT == 1 || N == 1)
                     q8_unit<1, NT, kTypeQ4_0>(op, q4, R, smem_u32(zrow), glo, lane, cw, ub);
-                else
+                else if (NT == 2 || N == 2)
                     q8_unit<2, NT, kTypeQ4_0>(op, q4, R, smem_u32(zrow), glo, lane, cw, ub);
+                else if constexpr (NT == 4)
+                    q8_unit<4, NT, kTypeQ4_0>(op, q4, R, smem_u32(zrow), glo, lane, cw, ub);
             } else {
                 if (NT == 1 || N == 1)
                     q8_unit<1, NT, kTypeQ8_0>(op, q4, R, smem_u32(zrow), glo, lane, cw, ub);
-                else
+                else if (NT == 2 || N == 2)
                     q8_unit<2, NT, kTypeQ8_0>(op, q4, R, smem_u32(zrow), glo, lane, cw, ub);
+                else if constexpr (NT == 4)
+                    q8_unit<4, NT, kTypeQ8_0>(op, q4, R, smem_u32(zrow), glo, lane, cw, ub);
             }
         }
         // ---- unit hand-off: publish this warp's partials; the owner sums them later ----
@@ -1445,6 +1469,7 @@ bool stream_supported(const MulMatOp* ops, int n_ops) {
             return false;
         if (o.ne2 != 1 || o.ne3 != 1) return false;
         if (o.N < 1 || o.N > kMaxNT) return false;
+        if (o.N > 2 && o.K > kMaxK34) return false;  // the 3- or 4-vector image with a two-stage ring
         if (o.K % 256 != 0) return false;  // whole 256-element groups (Q8_0 too)
         if (o.K > kMaxK) return false;
         if ((o.type == kTypeQ4_K || o.type == kTypeQ5_K) &&
@@ -1510,7 +1535,7 @@ int launch_stream(const MulMatOp* ops, int n_ops, cudaStream_t stream, int num_s
     for (int i = 0; i < n_ops; ++i) L.all_tma &= L.op[i].use_tma;
     L.x_bytes = x_bytes;
     L.stage_bytes = kRows * wmax;
-    const int nt = max_n <= 1 ? 1 : 2;
+    const int nt = max_n <= 1 ? 1 : (max_n <= 2 ? 2 : 4);
     const size_t fixed = smem_bytes(0, L.stage_bytes, x_bytes, nt);
     const size_t per_stage = smem_bytes(1, L.stage_bytes, x_bytes, nt) - fixed;
     int stages = fixed >= static_cast<size_t>(kSmemBudget)
@@ -1536,18 +1561,17 @@ int launch_stream(const MulMatOp* ops, int n_ops, cudaStream_t stream, int num_s
     cfg.numAttrs = 1;
     // raise the kernel's dynamic shared-memory limit to this launch's need
     // (once per size increase; the attribute call is not a stream operation)
-    static size_t configured[2] = {0, 0};
-    const int ti = nt - 1;
+    static size_t configured[3] = {0, 0, 0};
+    const int ti = nt == 1 ? 0 : (nt == 2 ? 1 : 2);
+    void (*const kernel)(SList) =
+        ti == 0 ? stream_gemv_kernel<1> : (ti == 1 ? stream_gemv_kernel<2> : stream_gemv_kernel<4>);
     cudaError_t e;
     if (configured[ti] < smem) {
-        e = ti == 0 ? cudaFuncSetAttribute(stream_gemv_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           static_cast<int>(smem))
-                    : cudaFuncSetAttribute(stream_gemv_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           static_cast<int>(smem));
+        e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
         if (e != cudaSuccess) return -static_cast<int>(e);
         configured[ti] = smem;
     }
-    e = ti == 0 ? cudaLaunchKernelEx(&cfg, stream_gemv_kernel<1>, L) : cudaLaunchKernelEx(&cfg, stream_gemv_kernel<2>, L);
+    e = cudaLaunchKernelEx(&cfg, kernel, L);
     if (e == cudaSuccess) e = cudaGetLastError();
     return e == cudaSuccess ? 1 : -static_cast<int>(e);
 }
