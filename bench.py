@@ -61,6 +61,7 @@ def parse_args():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-prefill", action="store_true", help="skip the prefill GEMM measurement")
     ap.add_argument("--no-batched", action="store_true", help="skip the batched Q8_0 decode measurement")
+    ap.add_argument("--no-fused-norm", action="store_true", help="skip the fused RMS_NORM measurement")
     return ap.parse_args()
 
 
@@ -83,6 +84,77 @@ def measured_tensor_peak():
         if "bf16_tflops" in d:
             return float(d["bf16_tflops"]), "measured bf16_tflops (burst, cuBLAS)"
     return 1590.0, "fallback (1.59 PFLOP/s burst)"
+
+
+def fused_norm_measure(dev, layers: int = 12, reps: int = 20):
+    """The two normed groups of the Llama-3.2-3B decode layer (attn_norm ->
+    q|k|v, ffn_norm -> gate|up), `layers` distinct layers replayed as one
+    CUDA graph, three ways: the plain GEMVs (activations already normed),
+    RMS_NORM * gain fused into the GEMVs (wllm_mul_mat_rms_norm_batch), and
+    the norm and gain as separate ops (torch) before the plain GEMVs. Returns
+    the JSON object (µs per layer)."""
+    import torch
+
+    from webllm_b200 import jsep, synth
+
+    L = {n: (n, t, M, K) for n, t, M, K in synth.LLAMA32_3B_LAYER}
+    groups = [[L["attn_q"], L["attn_k"], L["attn_v"]], [L["ffn_gate"], L["ffn_up"]]]
+    eps, K = 1e-5, 3072
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(5)
+    keep, plan = [], []
+    for li in range(layers):
+        for mats in groups:
+            x = torch.randn(1, K, device=dev, generator=gen)
+            xn = torch.empty_like(x)
+            g = torch.rand(K, device=dev, generator=gen) + 0.5
+            out = torch.empty(1, sum(M for _, _, M, _ in mats), device=dev)
+            ops_x, ops_n, off = [], [], 0
+            for (_, t, M, _) in mats:
+                w = synth.weights_torch(gen, t, M, K, dev)
+                keep.append(w)
+                ops_x.append(jsep.MulMatArgs(t, M, K, 1, w.data_ptr(), w.shape[1], x.data_ptr(), K, out.data_ptr() + 4 * off, M))
+                ops_n.append(jsep.MulMatArgs(t, M, K, 1, w.data_ptr(), w.shape[1], xn.data_ptr(), K, out.data_ptr() + 4 * off, M))
+                off += M
+            keep += [x, xn, g, out]
+            plan.append((x, xn, g, ops_x, ops_n))
+    stream_ptr = torch.cuda.current_stream().cuda_stream
+
+    def plain(sp):
+        for (_, _, _, ops_x, _) in plan:
+            jsep.mul_mat_batch(ops_x, sp)
+
+    def fused(sp):
+        for (_, _, g, ops_x, _) in plan:
+            if jsep.mul_mat_rms_norm_batch(ops_x, g.data_ptr(), eps, sp) != jsep.STATUS_OK:
+                raise RuntimeError("fused RMS_NORM not taken")
+
+    def separate(sp):
+        for (x, xn, g, _, ops_n) in plan:
+            torch.mul(x * torch.rsqrt(x.pow(2).mean(dim=1, keepdim=True) + eps), g, out=xn)
+            jsep.mul_mat_batch(ops_n, sp)
+
+    res = {}
+    for name, fn in (("plain_gemv", plain), ("fused_norm_gemv", fused), ("separate_norm_then_gemv", separate)):
+        fn(stream_ptr)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            fn(torch.cuda.current_stream().cuda_stream)
+        for _ in range(3):
+            graph.replay()
+        torch.cuda.synchronize()
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ev0.record()
+        for _ in range(reps):
+            graph.replay()
+        ev1.record()
+        torch.cuda.synchronize()
+        res[name] = round(ev0.elapsed_time(ev1) * 1e3 / (reps * layers), 2)
+        del graph
+    return {"workload": "llama-3.2-3b decode, attn_norm -> q|k|v and ffn_norm -> gate|up per layer, batch 1",
+            "unit": "us per layer", **res,
+            "note": "separate = torch RMS_NORM * gain kernels, then the plain GEMVs; fused = one launch per group"}
 
 
 def prefill_measure(dev, reps: int = 10, warmup: int = 3):
@@ -517,9 +589,11 @@ def run_b200(args, rank: int, world: int, local_rank: int):
         jsep_e2e = jsep_path_e2e(args, layers)
 
     # ---- prefill GEMMs (tensor cores) and batched decode, rank 0 at one GPU
-    prefill = batched = None
+    prefill = batched = fused_norm = None
     if world == 1 and not args.no_prefill:
         prefill = prefill_measure(dev)
+    if world == 1 and not args.no_fused_norm:
+        fused_norm = fused_norm_measure(dev)
     if world == 1 and not args.no_batched:
         batched = batched_measure(dev)
 
@@ -561,6 +635,8 @@ def run_b200(args, rank: int, world: int, local_rank: int):
             line["prefill"] = prefill
         if batched is not None:
             line["batched"] = batched
+        if fused_norm is not None:
+            line["fused_norm"] = fused_norm
     if world > 1:
         del graph
         torch.cuda.synchronize()

@@ -164,6 +164,19 @@ typedef struct wllm_mulmat_args {
  * `stream` (NULL = the library stream). */
 int32_t wllm_mul_mat_batch(const wllm_mulmat_args* ops, int32_t n_ops, void* stream);
 
+/* wllm_mul_mat_batch with the RMS_NORM and gain MUL that feed the ops fused
+ * into the kernel: each op reads x / sqrt(mean(x^2) + eps) * gain (per
+ * vector, mean over K) instead of x. Replaces the graph's
+ * MUL_MAT(W, MUL(RMS_NORM(x, eps), gain)) chain
+ * (src/inference/model-inference.ts:2281 attn_norm -> q/k/v,
+ * :2478-2481 ffn_norm -> gate/up; RMS_NORM per
+ * src/inference/jsep/ops/rms-norm.ts:14-15,61-67). gain: K floats, 16-byte
+ * aligned, or NULL for RMS_NORM alone; every op has the same K. Decode
+ * shapes only (N <= 4, as the streaming kernel takes them): NOT_IMPLEMENTED
+ * otherwise, and the caller runs the three ops unfused. x is not modified. */
+int32_t wllm_mul_mat_rms_norm_batch(const wllm_mulmat_args* ops, int32_t n_ops, const float* gain, float eps,
+                                    void* stream);
+
 /* ---- Row-sharded multi-GPU decode with the gather fused into the GEMV ----
  * No counterpart in the reference, which runs on one browser GPU. The
  * reference's op semantics (dst[m + M*n], matmul.ts:10-17) make output rows

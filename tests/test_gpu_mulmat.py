@@ -200,6 +200,78 @@ def test_q5k_q4_0_decode_vs_torch_fp64(runtime, qtype, M, K, N):
     assert rel <= GEMV_TOL, rel
 
 
+FUSED_NORM_GROUPS = {
+    # name: (eps, [(type, M), ...], K) -- the ops that read one normed activation
+    "llama32_attn_qkv": (1e-5, [(jsep.GGML_TYPE_Q4_K, 3072), (jsep.GGML_TYPE_Q4_K, 1024), (jsep.GGML_TYPE_Q6_K, 1024)], 3072),
+    "llama32_ffn_gate_up": (1e-5, [(jsep.GGML_TYPE_Q4_K, 8192), (jsep.GGML_TYPE_Q4_K, 8192)], 3072),
+    "qwen3_attn_qkv": (1e-6, [(jsep.GGML_TYPE_Q4_K, 4096), (jsep.GGML_TYPE_Q4_K, 1024), (jsep.GGML_TYPE_Q4_K, 1024)], 4096),
+    "gemma2_ffn_up": (1e-6, [(jsep.GGML_TYPE_Q8_0, 9216)], 2304),
+    "mixed_types": (1e-5, [(jsep.GGML_TYPE_Q5_K, 640), (jsep.GGML_TYPE_Q4_0, 333)], 8192),
+}
+
+
+@pytest.mark.parametrize("with_gain", [True, False])
+@pytest.mark.parametrize("N", [1, 2, 3])
+@pytest.mark.parametrize("group", sorted(FUSED_NORM_GROUPS))
+def test_fused_rms_norm_vs_torch_fp64(runtime, group, N, with_gain):
+    """wllm_mul_mat_rms_norm_batch: the RMS_NORM (times gain) feeding a group
+    of projections, fused into the streaming kernel, against float64
+    x / sqrt(mean(x^2) + eps) * gain, then a float64 matmul of the
+    device-dequantized weights. The activations are left as they were."""
+    import torch
+
+    eps, mats, K = FUSED_NORM_GROUPS[group]
+    dev = torch.device("cuda", 0)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(len(group) * 7 + N + int(with_gain))
+    x = 3.0 * torch.randn(N, K, device=dev, generator=gen) + 0.5
+    gain = (torch.rand(K, device=dev, generator=gen) * 2.0 - 0.5) if with_gain else None
+    x0 = x.clone()
+    ws, ys, ops = [], [], []
+    for t, M in mats:
+        w = synth.weights_torch(gen, t, M, K, dev)
+        y = torch.empty(N, M, device=dev)
+        ws.append(w)
+        ys.append(y)
+        ops.append(jsep.MulMatArgs(t, M, K, N, w.data_ptr(), w.shape[1], x.data_ptr(), K, y.data_ptr(), M))
+    torch.cuda.synchronize()
+    stream = jsep.library_stream()
+    rc = jsep.mul_mat_rms_norm_batch(ops, gain.data_ptr() if with_gain else 0, eps, stream)
+    assert rc == jsep.STATUS_OK
+    runtime.jsep_sync()
+    xd = x0.double()
+    xn = xd / torch.sqrt((xd * xd).mean(dim=1, keepdim=True) + eps)
+    if with_gain:
+        xn = xn * gain.double()
+    for (t, M), w, y in zip(mats, ws, ys):
+        wf = torch.empty(M, K, device=dev)
+        jsep.dequantize_device(t, w.data_ptr(), wf.data_ptr(), M * K, stream)
+        runtime.jsep_sync()
+        ref = (wf.double() @ xn.t()).t()
+        rel = ((y.double() - ref).abs().max() / ref.abs().max()).item()
+        assert rel <= GEMV_TOL, (t, M, rel)
+    assert torch.equal(x, x0)
+
+
+def test_fused_rms_norm_outside_decode_is_not_implemented(runtime):
+    """More vectors than the streaming kernel takes: NOT_IMPLEMENTED, so the
+    caller runs RMS_NORM, MUL and MUL_MAT unfused; nothing is written."""
+    import torch
+
+    dev = torch.device("cuda", 0)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(3)
+    M, K, N = 256, 1024, 8
+    w = synth.weights_torch(gen, jsep.GGML_TYPE_Q4_K, M, K, dev)
+    x = torch.randn(N, K, device=dev, generator=gen)
+    y = torch.full((N, M), 7.0, device=dev)
+    torch.cuda.synchronize()
+    op = jsep.MulMatArgs(jsep.GGML_TYPE_Q4_K, M, K, N, w.data_ptr(), w.shape[1], x.data_ptr(), K, y.data_ptr(), M)
+    assert jsep.mul_mat_rms_norm_batch([op], 0, 1e-5, jsep.library_stream()) == jsep.STATUS_NOT_IMPLEMENTED
+    runtime.jsep_sync()
+    assert bool((y == 7.0).all())
+
+
 @pytest.mark.parametrize("N", [65, 200])
 def test_q6k_prefill_sizes_vs_torch_fp64(runtime, N):
     """Q6_K with more than 64 vectors (prefill; several 32-vector tiles) on the

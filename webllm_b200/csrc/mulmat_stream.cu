@@ -105,6 +105,16 @@ struct SOp {
     float* y_peer[kMaxRanks];     // row-sharded launch: this op's rows on rank r (own rank unused)
 };
 
+// Fused RMS_NORM (+ gain MUL) of the activations: each vector x becomes
+// x / sqrt(mean(x^2) + eps) * gain before the limb split
+// (src/inference/jsep/ops/rms-norm.ts:14-15,61-67; the gain is the separate
+// MUL of src/inference/model-inference.ts:2281,2478-2481).
+struct NormArgs {
+    const float* gain;  // K floats, or null (no gain)
+    float eps;
+    int32_t on;
+};
+
 // Row-sharded launch: sig[r] is rank r's signal array, state this rank's
 // counters ([0] CTAs done with the launch, [1] launches done).
 struct TpSig {
@@ -122,6 +132,7 @@ struct SList {
     int32_t x_bytes;      // shared-memory bytes reserved for the activation image
     int32_t all_tma;      // every op is copied with its tensor map
     TpSig tp;             // world > 1: every output row also goes to the other ranks
+    NormArgs norm;        // on: every op's activations are RMS-normalized (times gain) first
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -688,18 +699,70 @@ __device__ __forceinline__ OpRegs op_regs(const OpInfo& o) {
 struct OpTable {
     OpInfo op[kMaxOpsPerLaunch];
     int32_t n_ops, total_units;
+    NormArgs norm;
 };
 
 
 // Builds the activation image of `op` in shared memory (all consumer warps;
 // one L2 round trip).
-__device__ __forceinline__ void stage_activations(const OpInfo& op, uint8_t* xsm, int lane, int cw) {
+// With a fused RMS_NORM, a first pass over the same elements sums x^2 per
+// vector: per warp, then over the 8 warps in warp order (deterministic); it
+// keeps each half-warp's first (vector, block) pair and its gains in
+// registers for the second pass (at batch 1 and K <= 4096 that is every pair;
+// the others come from L1). Every element is then scaled by
+// 1 / sqrt(mean(x^2) + eps) and then by its gain.
+template <bool NORM>
+__device__ __forceinline__ void stage_activations(const OpInfo& op, uint8_t* xsm, int lane, int cw, const NormArgs& nrm,
+                                                  float (*nred)[kMaxNT]) {
     const int K = op.K, N = op.N;
     const uint8_t* xb = reinterpret_cast<const uint8_t*>(op.x);
     const int nblk = K / 256, XS = img_col_bytes(K);
     float* dfac = reinterpret_cast<float*>(xsm + img_inv_off(K, N));
     float* Xs = reinterpret_cast<float*>(xsm + img_sum_off(K, N));
     float* X16 = reinterpret_cast<float*>(xsm + img_sum16_off(K, N));
+    float inv[kMaxNT] = {1.f, 1.f, 1.f, 1.f};
+    float4 keep_x[4], keep_g[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) keep_g[k] = keep_x[k] = make_float4(1.f, 1.f, 1.f, 1.f);
+    if constexpr (NORM) {
+        float ssl[kMaxNT] = {0.f, 0.f, 0.f, 0.f};
+        for (int tb = 2 * cw + (lane >> 4); tb < N * nblk; tb += 2 * kCW) {
+            const int t = tb / nblk, b = tb - t * nblk;
+            const float4* xv = reinterpret_cast<const float4*>(xb + t * op.x_nb1) + b * 64 + 4 * (lane & 15);
+            const bool first = tb == 2 * cw + (lane >> 4);
+            float a = 0.f;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const float4 e = __ldg(xv + k);
+                if (first) {  // the second pass's first pair: kept in registers with its gains
+                    keep_x[k] = e;
+                    if (nrm.gain) keep_g[k] = __ldg(reinterpret_cast<const float4*>(nrm.gain) + b * 64 + 4 * (lane & 15) + k);
+                }
+                a = fmaf(e.x, e.x, a);
+                a = fmaf(e.y, e.y, a);
+                a = fmaf(e.z, e.z, a);
+                a = fmaf(e.w, e.w, a);
+            }
+#pragma unroll
+            for (int q = 0; q < kMaxNT; ++q) ssl[q] += q == t ? a : 0.f;
+        }
+#pragma unroll
+        for (int q = 0; q < kMaxNT; ++q) {
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) ssl[q] += __shfl_xor_sync(0xffffffffu, ssl[q], o);
+        }
+        if (lane == 0)
+#pragma unroll
+            for (int q = 0; q < kMaxNT; ++q) nred[cw][q] = ssl[q];
+        consumers_sync();
+#pragma unroll
+        for (int q = 0; q < kMaxNT; ++q) {
+            float ss = 0.f;
+#pragma unroll
+            for (int w2 = 0; w2 < kCW; ++w2) ss += nred[w2][q];
+            inv[q] = 1.f / sqrtf(ss / static_cast<float>(K) + nrm.eps);
+        }
+    }
     // one (vector, block) per half-warp and round: lane h = lane%16 covers
     // elements 16h .. 16h+15. Two rounds' loads are issued before any
     // arithmetic (K = 8192 at N = 1 is two rounds: one L2 round trip)
@@ -718,8 +781,29 @@ __device__ __forceinline__ void stage_activations(const OpInfo& op, uint8_t* xsm
             b[r] = act[r] ? tb - t[r] * nblk : 0;
             const float4* xv = reinterpret_cast<const float4*>(xb + t[r] * op.x_nb1) + b[r] * 64 + 4 * h;
             if (r < rounds) {
+                const bool kept = NORM && r == 0 && tb0 == 2 * cw + hw;  // loaded by the first pass
 #pragma unroll
-                for (int k = 0; k < 4; ++k) v[r][k] = act[r] ? __ldg(xv + k) : make_float4(0.f, 0.f, 0.f, 0.f);
+                for (int k = 0; k < 4; ++k)
+                    v[r][k] = !act[r] ? make_float4(0.f, 0.f, 0.f, 0.f) : (kept ? keep_x[k] : __ldg(xv + k));
+            }
+        }
+        if constexpr (NORM) {
+            // (x * inv_rms) * gain: the reference's two ops, in order (after
+            // both rounds' loads are issued)
+#pragma unroll
+            for (int r = 0; r < 2; ++r) {
+                if (r >= rounds || !act[r]) continue;
+                const float sc = t[r] == 0 ? inv[0] : (t[r] == 1 ? inv[1] : (t[r] == 2 ? inv[2] : inv[3]));
+                const float4* gv = reinterpret_cast<const float4*>(nrm.gain) + b[r] * 64 + 4 * h;
+                const bool kept = r == 0 && tb0 == 2 * cw + hw;
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    const float4 gk = !nrm.gain ? make_float4(1.f, 1.f, 1.f, 1.f) : (kept ? keep_g[k] : __ldg(gv + k));
+                    v[r][k] = make_float4(__fmul_rn(__fmul_rn(v[r][k].x, sc), gk.x),
+                                          __fmul_rn(__fmul_rn(v[r][k].y, sc), gk.y),
+                                          __fmul_rn(__fmul_rn(v[r][k].z, sc), gk.z),
+                                          __fmul_rn(__fmul_rn(v[r][k].w, sc), gk.w));
+                }
             }
         }
 #pragma unroll
@@ -1094,7 +1178,9 @@ __device__ __forceinline__ void q8_unit(const OpRegs& op, const Q4Lane& q, Ring&
     }
 }
 
-template <int NT>
+// NORM: the fused RMS_NORM launches (a separate instantiation, so the plain
+// GEMV carries none of its code).
+template <int NT, bool NORM>
 __global__ void __launch_bounds__(kThreads, 1) stream_gemv_kernel(const __grid_constant__ SList L) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int S = L.stages;
@@ -1123,6 +1209,7 @@ __global__ void __launch_bounds__(kThreads, 1) stream_gemv_kernel(const __grid_c
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     __shared__ OpTable T;
+    __shared__ float nred[kCW][kMaxNT];  // fused RMS_NORM: per-warp sums of x^2
     if (threadIdx.x < L.n_ops) {
         const SOp& o = L.op[threadIdx.x];
         OpInfo& d = T.op[threadIdx.x];
@@ -1146,6 +1233,7 @@ __global__ void __launch_bounds__(kThreads, 1) stream_gemv_kernel(const __grid_c
     }
     if (threadIdx.x == 0) {
         T.n_ops = L.n_ops;
+        T.norm = L.norm;
         T.total_units = L.total_units;
     }
     __syncthreads();
@@ -1307,7 +1395,7 @@ __global__ void __launch_bounds__(kThreads, 1) stream_gemv_kernel(const __grid_c
             if (staged < 0 || T.op[staged].x != oo.x || T.op[staged].K != oo.K || T.op[staged].N != oo.N ||
                 T.op[staged].x_nb1 != oo.x_nb1) {
                 consumers_sync();  // nobody still reads the previous image
-                stage_activations(oo, xsm, lane, cw);
+                stage_activations<NORM>(oo, xsm, lane, cw, T.norm, nred);
                 if (ct == 0 && useq == 0) mbar_arrive_cnt(xready, 1u);  // the copy warp may go on
                 staged = oi;
             }
@@ -1482,9 +1570,15 @@ bool stream_supported(const MulMatOp* ops, int n_ops) {
     return true;
 }
 
-int launch_stream(const MulMatOp* ops, int n_ops, cudaStream_t stream, int num_sms, const TpLaunch* tp) {
+int launch_stream(const MulMatOp* ops, int n_ops, cudaStream_t stream, int num_sms, const TpLaunch* tp,
+                  const NormLaunch* norm) {
     SList L{};
     L.n_ops = n_ops;
+    if (norm) {
+        L.norm.gain = norm->gain;
+        L.norm.eps = norm->eps;
+        L.norm.on = 1;
+    }
     L.tp.world = 1;
     if (tp) {
         L.tp.world = tp->world;
@@ -1561,10 +1655,12 @@ int launch_stream(const MulMatOp* ops, int n_ops, cudaStream_t stream, int num_s
     cfg.numAttrs = 1;
     // raise the kernel's dynamic shared-memory limit to this launch's need
     // (once per size increase; the attribute call is not a stream operation)
-    static size_t configured[3] = {0, 0, 0};
-    const int ti = nt == 1 ? 0 : (nt == 2 ? 1 : 2);
-    void (*const kernel)(SList) =
-        ti == 0 ? stream_gemv_kernel<1> : (ti == 1 ? stream_gemv_kernel<2> : stream_gemv_kernel<4>);
+    static size_t configured[6] = {0, 0, 0, 0, 0, 0};
+    const int ti = (nt == 1 ? 0 : (nt == 2 ? 1 : 2)) + (norm ? 3 : 0);
+    void (*const kernels[6])(SList) = {stream_gemv_kernel<1, false>, stream_gemv_kernel<2, false>,
+                                       stream_gemv_kernel<4, false>, stream_gemv_kernel<1, true>,
+                                       stream_gemv_kernel<2, true>,  stream_gemv_kernel<4, true>};
+    void (*const kernel)(SList) = kernels[ti];
     cudaError_t e;
     if (configured[ti] < smem) {
         e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));

@@ -835,6 +835,29 @@ int32_t wllm_mul_mat_batch(const wllm_mulmat_args* ops, int32_t n_ops, void* str
     return launch(s, m, n_ops, stream ? static_cast<cudaStream_t>(stream) : s.stream);
 }
 
+int32_t wllm_mul_mat_rms_norm_batch(const wllm_mulmat_args* ops, int32_t n_ops, const float* gain, float eps,
+                                    void* stream) {
+    State& s = S();
+    std::lock_guard<std::mutex> g(s.mu);
+    if (!ensure_init(s)) return WLLM_STATUS_FAILED;
+    const char* what = "wllm_mul_mat_rms_norm_batch";
+    MulMatOp m[wllm::kMaxOpsPerLaunch];
+    if (const int32_t rc = ops_from_args(s, what, ops, n_ops, m)) return rc;
+    if (!(eps >= 0.f) || eps > 1.f) return fail(s, "%s: eps must be in [0, 1]", what);
+    if (gain && (reinterpret_cast<uintptr_t>(gain) & 15)) return fail(s, "%s: gain must be 16-byte aligned", what);
+    for (int i = 1; i < n_ops; ++i)
+        if (m[i].K != m[0].K) return fail(s, "%s: every op must have the same K (one gain vector)", what);
+    // the fused form exists for the decode regime only: the caller runs the
+    // RMS_NORM, MUL and MUL_MAT ops unfused otherwise
+    if (!wllm::stream_supported(m, n_ops)) return WLLM_STATUS_NOT_IMPLEMENTED;
+    const wllm::NormLaunch nl{gain, eps};
+    const int rc = wllm::launch_stream(m, n_ops, stream ? static_cast<cudaStream_t>(stream) : s.stream, s.num_sms,
+                                       nullptr, &nl);
+    if (rc < 0) return cuda_fail(s, static_cast<cudaError_t>(-rc), "wllm_mul_mat_rms_norm_batch launch");
+    s.counters.kernels_launched += static_cast<uint64_t>(rc);
+    return WLLM_STATUS_OK;
+}
+
 int32_t wllm_ipc_alloc(uint64_t size, void** out_ptr, void* out_handle) {
     State& s = S();
     std::lock_guard<std::mutex> g(s.mu);

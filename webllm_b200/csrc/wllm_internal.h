@@ -78,8 +78,16 @@ struct TpLaunch {
     float* y_peer[kMaxOpsPerLaunch][kMaxRanks];  // op i's rows on rank r (own rank unused)
 };
 
+// Fused RMS_NORM (+ gain) of every op's activations before the streaming
+// GEMV: x / sqrt(mean(x^2) + eps) * gain (gain null: none).
+struct NormLaunch {
+    const float* gain;
+    float eps;
+};
+
 bool stream_supported(const MulMatOp* ops, int n_ops);
-int launch_stream(const MulMatOp* ops, int n_ops, cudaStream_t stream, int num_sms, const TpLaunch* tp = nullptr);
+int launch_stream(const MulMatOp* ops, int n_ops, cudaStream_t stream, int num_sms, const TpLaunch* tp = nullptr,
+                  const NormLaunch* norm = nullptr);
 // One-thread kernel that waits (bounded) for every peer's signal of the
 // rank's last row-sharded launch.
 int launch_tp_wait(const TpLaunch& tp, cudaStream_t stream);

@@ -56,7 +56,7 @@ EXPORTED_SYMBOLS = (
     "wllm_init", "wllm_shutdown", "wllm_alloc", "wllm_free", "wllm_write", "wllm_read",
     "wllm_read_async_begin", "wllm_read_async_poll", "wllm_read_async_finish", "wllm_read_async_cancel",
     "wllm_clear", "wllm_run_op", "wllm_run_ops", "wllm_sync", "wllm_last_error", "wllm_get_counters",
-    "wllm_buffer_device_ptr", "wllm_mul_mat", "wllm_mul_mat_batch", "wllm_get_stream",
+    "wllm_buffer_device_ptr", "wllm_mul_mat", "wllm_mul_mat_batch", "wllm_mul_mat_rms_norm_batch", "wllm_get_stream",
     "wllm_graph_begin", "wllm_graph_end", "wllm_graph_launch", "wllm_graph_destroy",
     "wllm_dequantize", "wllm_version", "wllm_mul_mat_prefill_static",
     "wllm_ipc_alloc", "wllm_ipc_open", "wllm_ipc_close", "wllm_ipc_free", "wllm_mul_mat_batch_tp", "wllm_tp_wait",
@@ -126,6 +126,7 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
         "wllm_mul_mat_prefill_static": ([i32, vp, i64, vp, i64, vp, i64, i32, i32, i32, vp], i32),
         "wllm_dequantize": ([i32, vp, vp, i64, vp], i32),
         "wllm_mul_mat_batch": ([P(MulMatArgs), i32, vp], i32),
+        "wllm_mul_mat_rms_norm_batch": ([P(MulMatArgs), i32, vp, ctypes.c_float, vp], i32),
         "wllm_ipc_alloc": ([u64, P(vp), vp], i32),
         "wllm_ipc_open": ([vp, P(vp)], i32),
         "wllm_ipc_close": ([vp], i32),
@@ -422,6 +423,16 @@ def mul_mat_batch(ops: Sequence[MulMatArgs], stream: int = 0) -> int:
     L = load_library()
     arr = (MulMatArgs * len(ops))(*ops)
     return _check(L.wllm_mul_mat_batch(arr, len(ops), int(stream) or None), "wllm_mul_mat_batch")
+
+
+def mul_mat_rms_norm_batch(ops: Sequence[MulMatArgs], gain_ptr: int, eps: float, stream: int = 0) -> int:
+    """MUL_MATs of RMS_NORM(x) * gain with the norm fused into the kernel
+    (wllm_mul_mat_rms_norm_batch): STATUS_OK, or STATUS_NOT_IMPLEMENTED outside
+    the decode regime (the caller then runs the ops unfused)."""
+    L = load_library()
+    arr = (MulMatArgs * len(ops))(*ops)
+    return _check(L.wllm_mul_mat_rms_norm_batch(arr, len(ops), int(gain_ptr) or None, float(eps),
+                                                int(stream) or None), "wllm_mul_mat_rms_norm_batch")
 
 
 def ipc_alloc(size: int) -> tuple[int, bytes]:
