@@ -61,7 +61,7 @@ def parse_args():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-prefill", action="store_true", help="skip the prefill GEMM measurement")
     ap.add_argument("--no-batched", action="store_true", help="skip the batched Q8_0 decode measurement")
-    ap.add_argument("--no-fused-norm", action="store_true", help="skip the fused RMS_NORM measurement")
+    ap.add_argument("--no-fused-norm", action="store_true", help="skip the fused RMS_NORM and GLU measurements")
     return ap.parse_args()
 
 
@@ -118,7 +118,6 @@ def fused_norm_measure(dev, layers: int = 12, reps: int = 20):
                 off += M
             keep += [x, xn, g, out]
             plan.append((x, xn, g, ops_x, ops_n))
-    stream_ptr = torch.cuda.current_stream().cuda_stream
 
     def plain(sp):
         for (_, _, _, ops_x, _) in plan:
@@ -134,9 +133,21 @@ def fused_norm_measure(dev, layers: int = 12, reps: int = 20):
             torch.mul(x * torch.rsqrt(x.pow(2).mean(dim=1, keepdim=True) + eps), g, out=xn)
             jsep.mul_mat_batch(ops_n, sp)
 
+    res = graph_times_us((("plain_gemv", plain), ("fused_norm_gemv", fused), ("separate_norm_then_gemv", separate)),
+                         layers, reps)
+    return {"workload": "llama-3.2-3b decode, attn_norm -> q|k|v and ffn_norm -> gate|up per layer, batch 1",
+            "unit": "us per layer", **res,
+            "note": "separate = torch RMS_NORM * gain kernels, then the plain GEMVs; fused = one launch per group"}
+
+
+def graph_times_us(fns, layers: int, reps: int) -> dict:
+    """Each fn(stream) recorded as one CUDA graph on torch's current stream,
+    3 untimed replays, then `reps` replays between CUDA events: µs per layer."""
+    import torch
+
     res = {}
-    for name, fn in (("plain_gemv", plain), ("fused_norm_gemv", fused), ("separate_norm_then_gemv", separate)):
-        fn(stream_ptr)
+    for name, fn in fns:
+        fn(torch.cuda.current_stream().cuda_stream)
         torch.cuda.synchronize()
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph):
@@ -152,9 +163,52 @@ def fused_norm_measure(dev, layers: int = 12, reps: int = 20):
         torch.cuda.synchronize()
         res[name] = round(ev0.elapsed_time(ev1) * 1e3 / (reps * layers), 2)
         del graph
-    return {"workload": "llama-3.2-3b decode, attn_norm -> q|k|v and ffn_norm -> gate|up per layer, batch 1",
+    return res
+
+
+def fused_glu_measure(dev, layers: int = 12, reps: int = 20):
+    """The Llama-3.2-3B decode layer's down projection (Q6_K 3072 x 8192) fed
+    by silu(gate) * up, `layers` distinct layers replayed as one CUDA graph,
+    three ways: the plain GEMV (its input already computed), the GLU fused into
+    the GEMV (wllm_mul_mat_glu_batch), and the GLU as separate ops (torch)
+    before the plain GEMV. Returns the JSON object (µs per layer)."""
+    import torch
+
+    from webllm_b200 import jsep, synth
+
+    _, t, M, K = {n: (n, t, M, K) for n, t, M, K in synth.LLAMA32_3B_LAYER}["ffn_down"]
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(6)
+    plan = []
+    for _ in range(layers):
+        g = 2.0 * torch.randn(1, K, device=dev, generator=gen)
+        u = torch.randn(1, K, device=dev, generator=gen)
+        h = torch.empty_like(g)
+        y = torch.empty(1, M, device=dev)
+        w = synth.weights_torch(gen, t, M, K, dev)
+        op_g = jsep.MulMatArgs(t, M, K, 1, w.data_ptr(), w.shape[1], g.data_ptr(), K, y.data_ptr(), M)
+        op_h = jsep.MulMatArgs(t, M, K, 1, w.data_ptr(), w.shape[1], h.data_ptr(), K, y.data_ptr(), M)
+        plan.append((g, u, h, y, w, op_g, op_h))
+
+    def plain(sp):
+        for p in plan:
+            jsep.mul_mat_batch([p[6]], sp)
+
+    def fused(sp):
+        for (_, u, _, _, _, op_g, _) in plan:
+            if jsep.mul_mat_glu_batch([op_g], u.data_ptr(), K, jsep.GLU_SWIGLU, sp) != jsep.STATUS_OK:
+                raise RuntimeError("fused GLU not taken")
+
+    def separate(sp):
+        for (g, u, h, _, _, _, op_h) in plan:
+            torch.mul(torch.nn.functional.silu(g), u, out=h)
+            jsep.mul_mat_batch([op_h], sp)
+
+    res = graph_times_us((("plain_gemv", plain), ("fused_glu_gemv", fused), ("separate_glu_then_gemv", separate)),
+                         layers, reps)
+    return {"workload": "llama-3.2-3b decode, silu(ffn_gate) * ffn_up -> ffn_down (Q6_K 3072 x 8192), batch 1",
             "unit": "us per layer", **res,
-            "note": "separate = torch RMS_NORM * gain kernels, then the plain GEMVs; fused = one launch per group"}
+            "note": "separate = torch silu and mul kernels, then the plain GEMV; fused = one launch"}
 
 
 def prefill_measure(dev, reps: int = 10, warmup: int = 3):
@@ -589,11 +643,12 @@ def run_b200(args, rank: int, world: int, local_rank: int):
         jsep_e2e = jsep_path_e2e(args, layers)
 
     # ---- prefill GEMMs (tensor cores) and batched decode, rank 0 at one GPU
-    prefill = batched = fused_norm = None
+    prefill = batched = fused_norm = fused_glu = None
     if world == 1 and not args.no_prefill:
         prefill = prefill_measure(dev)
     if world == 1 and not args.no_fused_norm:
         fused_norm = fused_norm_measure(dev)
+        fused_glu = fused_glu_measure(dev)
     if world == 1 and not args.no_batched:
         batched = batched_measure(dev)
 
@@ -637,6 +692,8 @@ def run_b200(args, rank: int, world: int, local_rank: int):
             line["batched"] = batched
         if fused_norm is not None:
             line["fused_norm"] = fused_norm
+        if fused_glu is not None:
+            line["fused_glu"] = fused_glu
     if world > 1:
         del graph
         torch.cuda.synchronize()

@@ -177,6 +177,25 @@ int32_t wllm_mul_mat_batch(const wllm_mulmat_args* ops, int32_t n_ops, void* str
 int32_t wllm_mul_mat_rms_norm_batch(const wllm_mulmat_args* ops, int32_t n_ops, const float* gain, float eps,
                                     void* stream);
 
+/* GLU kinds for wllm_mul_mat_glu_batch. */
+#define WLLM_GLU_SWIGLU 1 /* silu(gate) * up: gate / (1 + e^-gate), times up */
+#define WLLM_GLU_GELU 2   /* gelu(gate) * up: tanh form, rounded to f16 like ggml's CPU GELU */
+
+/* wllm_mul_mat_batch with the GLU between the FFN's gate/up projections and
+ * its down projection fused into the kernel: the ops' x is the gate
+ * projection's output, and each op reads act(x) * up instead of x. Replaces
+ * MUL_MAT(W_down, SWIGLU_SPLIT(gate, up)) (src/inference/model-inference.ts:
+ * 2484-2489; op_swiglu_split, src/wasm/webgpu-bridge.cpp:272-275) and, with
+ * WLLM_GLU_GELU, the Gemma form MUL_MAT(W_down, MUL(GELU(gate), up))
+ * (model-inference.ts:2486-2487). up: laid out like x, up_stride floats
+ * between vectors (a multiple of 4), 16-byte aligned. Every op reads the
+ * same x. Decode
+ * shapes only (N <= 4, as the streaming kernel takes them): NOT_IMPLEMENTED
+ * otherwise, and the caller runs the ops unfused. gate and up are not
+ * modified. */
+int32_t wllm_mul_mat_glu_batch(const wllm_mulmat_args* ops, int32_t n_ops, const float* up, int64_t up_stride,
+                               int32_t glu, void* stream);
+
 /* ---- Row-sharded multi-GPU decode with the gather fused into the GEMV ----
  * No counterpart in the reference, which runs on one browser GPU. The
  * reference's op semantics (dst[m + M*n], matmul.ts:10-17) make output rows

@@ -272,6 +272,111 @@ def test_fused_rms_norm_outside_decode_is_not_implemented(runtime):
     assert bool((y == 7.0).all())
 
 
+FUSED_GLU_GROUPS = {
+    # name: ([(type, M), ...], K) -- the down projections that read one act(gate) * up
+    "llama32_ffn_down_q6k": ([(jsep.GGML_TYPE_Q6_K, 3072)], 8192),
+    "llama32_ffn_down_q4k": ([(jsep.GGML_TYPE_Q4_K, 3072)], 8192),
+    "llama3_8b_ffn_down": ([(jsep.GGML_TYPE_Q4_K, 4096)], 14336),
+    "gemma2_ffn_down": ([(jsep.GGML_TYPE_Q8_0, 2304)], 9216),
+    "mixed_types": ([(jsep.GGML_TYPE_Q5_K, 640), (jsep.GGML_TYPE_Q4_0, 333)], 4096),
+}
+
+
+def glu_fp64(gate, up, glu):
+    """act(gate) * up in float64: silu, or ggml's CPU GELU (tanh form with its
+    input and output rounded to f16; 0 at gate <= -10, gate at gate >= 10)."""
+    import torch
+
+    g = gate.double()
+    if glu == jsep.GLU_SWIGLU:
+        a = g / (1.0 + torch.exp(-g))
+    else:
+        h = gate.half().double()
+        t = 0.5 * h * (1.0 + torch.tanh(0.7978845608028654 * h * (1.0 + 0.044715 * h * h)))
+        a = torch.where(g <= -10.0, torch.zeros_like(g), torch.where(g >= 10.0, g, t.half().double()))
+    return a * up.double()
+
+
+@pytest.mark.parametrize("N", [1, 2, 3])
+@pytest.mark.parametrize("glu", [jsep.GLU_SWIGLU, jsep.GLU_GELU])
+@pytest.mark.parametrize("group", sorted(FUSED_GLU_GROUPS))
+def test_fused_glu_vs_torch_fp64(runtime, group, glu, N):
+    """wllm_mul_mat_glu_batch: the GLU between the FFN's gate/up projections
+    and its down projection, fused into the streaming kernel, against float64
+    act(gate) * up, then a float64 matmul of the device-dequantized weights.
+    Gate values past +-10 exercise GELU's two clamps. Three vectors of a
+    K above 8192 are outside the streaming kernel: NOT_IMPLEMENTED, nothing
+    written. gate and up are left as they were."""
+    import torch
+
+    mats, K = FUSED_GLU_GROUPS[group]
+    dev = torch.device("cuda", 0)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(len(group) * 11 + N + 5 * glu)
+    up_stride = K + 64  # up in a wider buffer: its own stride
+    gate = 2.5 * torch.randn(N, K, device=dev, generator=gen)
+    gate[:, ::97] = 12.0 * torch.sign(torch.randn(N, (K + 96) // 97, device=dev, generator=gen))
+    upbuf = torch.randn(N, up_stride, device=dev, generator=gen)
+    up = upbuf[:, :K]
+    gate0, up0 = gate.clone(), upbuf.clone()
+    ws, ys, ops = [], [], []
+    for t, M in mats:
+        w = synth.weights_torch(gen, t, M, K, dev)
+        y = torch.full((N, M), 7.0, device=dev)
+        ws.append(w)
+        ys.append(y)
+        ops.append(jsep.MulMatArgs(t, M, K, N, w.data_ptr(), w.shape[1], gate.data_ptr(), K, y.data_ptr(), M))
+    torch.cuda.synchronize()
+    stream = jsep.library_stream()
+    rc = jsep.mul_mat_glu_batch(ops, up.data_ptr(), up_stride, glu, stream)
+    runtime.jsep_sync()
+    if N > 2 and K > 8192:
+        assert rc == jsep.STATUS_NOT_IMPLEMENTED
+        assert all(bool((y == 7.0).all()) for y in ys)
+        return
+    assert rc == jsep.STATUS_OK
+    h = glu_fp64(gate0, up0[:, :K], glu)
+    for (t, M), w, y in zip(mats, ws, ys):
+        wf = torch.empty(M, K, device=dev)
+        jsep.dequantize_device(t, w.data_ptr(), wf.data_ptr(), M * K, stream)
+        runtime.jsep_sync()
+        ref = (wf.double() @ h.t()).t()
+        rel = ((y.double() - ref).abs().max() / ref.abs().max()).item()
+        assert rel <= GEMV_TOL, (t, M, rel)
+    assert torch.equal(gate, gate0) and torch.equal(upbuf, up0)
+
+
+def test_fused_glu_rejects_bad_arguments(runtime):
+    """Ops that read different gates, an unknown kind, a misaligned up: FAILED
+    with a message; NOT_IMPLEMENTED beyond 4 vectors. Nothing is written."""
+    import torch
+
+    dev = torch.device("cuda", 0)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(5)
+    M, K = 256, 1024
+    w = synth.weights_torch(gen, jsep.GGML_TYPE_Q4_K, M, K, dev)
+    g = torch.randn(8, K, device=dev, generator=gen)
+    u = torch.randn(8, K + 4, device=dev, generator=gen)
+    y = torch.full((8, M), 7.0, device=dev)
+    torch.cuda.synchronize()
+    s = jsep.library_stream()
+
+    def op(x_off, n):
+        return jsep.MulMatArgs(jsep.GGML_TYPE_Q4_K, M, K, n, w.data_ptr(), w.shape[1], g.data_ptr() + 4 * x_off, K,
+                               y.data_ptr(), M)
+
+    assert jsep.mul_mat_glu_batch([op(0, 8)], u.data_ptr(), K, jsep.GLU_SWIGLU, s) == jsep.STATUS_NOT_IMPLEMENTED
+    for args in (([op(0, 1), op(K, 1)], u.data_ptr(), K, jsep.GLU_SWIGLU),
+                 ([op(0, 1)], u.data_ptr(), K, 7),
+                 ([op(0, 1)], u.data_ptr() + 4, K, jsep.GLU_GELU),
+                 ([op(0, 2)], u.data_ptr(), K + 2, jsep.GLU_GELU)):
+        with pytest.raises(jsep.WllmError):
+            jsep.mul_mat_glu_batch(*args, stream=s)
+    runtime.jsep_sync()
+    assert bool((y == 7.0).all())
+
+
 @pytest.mark.parametrize("N", [65, 200])
 def test_q6k_prefill_sizes_vs_torch_fp64(runtime, N):
     """Q6_K with more than 64 vectors (prefill; several 32-vector tiles) on the

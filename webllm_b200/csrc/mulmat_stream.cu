@@ -105,14 +105,20 @@ struct SOp {
     float* y_peer[kMaxRanks];     // row-sharded launch: this op's rows on rank r (own rank unused)
 };
 
-// Fused RMS_NORM (+ gain MUL) of the activations: each vector x becomes
-// x / sqrt(mean(x^2) + eps) * gain before the limb split
-// (src/inference/jsep/ops/rms-norm.ts:14-15,61-67; the gain is the separate
-// MUL of src/inference/model-inference.ts:2281,2478-2481).
-struct NormArgs {
-    const float* gain;  // K floats, or null (no gain)
-    float eps;
-    int32_t on;
+// Fused prologue of the activations, applied before the limb split:
+// - kProNorm: RMS_NORM (+ gain MUL), x / sqrt(mean(x^2) + eps) * gain
+//   (src/inference/jsep/ops/rms-norm.ts:14-15,61-67; the gain is the separate
+//   MUL of src/inference/model-inference.ts:2281,2478-2481);
+// - kProSwiglu: silu(x) * up, x the gate projection's output
+//   (model-inference.ts:2484-2489, op_swiglu_split of
+//   src/wasm/webgpu-bridge.cpp:272-275);
+// - kProGelu: gelu(x) * up, the Gemma form (model-inference.ts:2486-2487).
+struct ProArgs {
+    const float* gain;  // kProNorm: K floats, or null (no gain)
+    const float* up;    // kProSwiglu / kProGelu: the up projection's output, laid out like x
+    int64_t up_nb1;     // bytes between its vectors
+    float eps;          // kProNorm
+    int32_t kind;
 };
 
 // Row-sharded launch: sig[r] is rank r's signal array, state this rank's
@@ -132,7 +138,7 @@ struct SList {
     int32_t x_bytes;      // shared-memory bytes reserved for the activation image
     int32_t all_tma;      // every op is copied with its tensor map
     TpSig tp;             // world > 1: every output row also goes to the other ranks
-    NormArgs norm;        // on: every op's activations are RMS-normalized (times gain) first
+    ProArgs pro;          // prologue applied to every op's activations (kind kProNone: none)
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -699,9 +705,45 @@ __device__ __forceinline__ OpRegs op_regs(const OpInfo& o) {
 struct OpTable {
     OpInfo op[kMaxOpsPerLaunch];
     int32_t n_ops, total_units;
-    NormArgs norm;
+    ProArgs pro;
 };
 
+
+// x * sigmoid(z) = x / (1 + e^-z) with the SFU exponential and reciprocal
+// (__expf, __fdividef: a few f32 ulps from the correctly rounded forms,
+// below the activation's 14-bit limb split). e^-z = inf gives x / inf = 0.
+__device__ __forceinline__ float x_sigmoid(float x, float z) { return __fdividef(x, 1.f + __expf(-z)); }
+
+// silu(g) * u: ggml's scalar CPU kernel, g / (1 + e^-g) times u
+// (ggml_vec_swiglu_f32).
+__device__ __forceinline__ float swiglu1(float g, float u) { return __fmul_rn(x_sigmoid(g, g), u); }
+
+// gelu(g) * u as ggml's CPU GELU computes it (its GGML_GELU_FP16 table): g
+// rounded to f16, the tanh form 0.5 f (1 + tanh(s)), s = sqrt(2/pi) f (1 +
+// 0.044715 f^2), rounded to f16; 0 at g <= -10 and g itself at g >= 10. The
+// tanh form is evaluated as f * sigmoid(2 s), the same function. The MUL by
+// u is a separate f32 op in the reference.
+__device__ __forceinline__ float gelu1(float g, float u) {
+    float y;
+    if (g <= -10.f) {
+        y = 0.f;
+    } else if (g >= 10.f) {
+        y = g;
+    } else {
+        const float f = __half2float(__float2half_rn(g));
+        const float s = (0.7978845608028654f * f) * (1.f + (0.044715f * f) * f);
+        y = __half2float(__float2half_rn(x_sigmoid(f, 2.f * s)));
+    }
+    return __fmul_rn(y, u);
+}
+
+template <int PRO>
+__device__ __forceinline__ float4 glu4(float4 g, float4 u) {
+    if constexpr (PRO == kProSwiglu)
+        return make_float4(swiglu1(g.x, u.x), swiglu1(g.y, u.y), swiglu1(g.z, u.z), swiglu1(g.w, u.w));
+    else
+        return make_float4(gelu1(g.x, u.x), gelu1(g.y, u.y), gelu1(g.z, u.z), gelu1(g.w, u.w));
+}
 
 // Builds the activation image of `op` in shared memory (all consumer warps;
 // one L2 round trip).
@@ -710,10 +752,13 @@ struct OpTable {
 // keeps each half-warp's first (vector, block) pair and its gains in
 // registers for the second pass (at batch 1 and K <= 4096 that is every pair;
 // the others come from L1). Every element is then scaled by
-// 1 / sqrt(mean(x^2) + eps) and then by its gain.
-template <bool NORM>
-__device__ __forceinline__ void stage_activations(const OpInfo& op, uint8_t* xsm, int lane, int cw, const NormArgs& nrm,
+// 1 / sqrt(mean(x^2) + eps) and then by its gain. With a fused GLU the up
+// projection's values are loaded beside the gate's and combined with them.
+template <int PRO>
+__device__ __forceinline__ void stage_activations(const OpInfo& op, uint8_t* xsm, int lane, int cw, const ProArgs& nrm,
                                                   float (*nred)[kMaxNT]) {
+    constexpr bool NORM = PRO == kProNorm;
+    constexpr bool GLU = PRO == kProSwiglu || PRO == kProGelu;
     const int K = op.K, N = op.N;
     const uint8_t* xb = reinterpret_cast<const uint8_t*>(op.x);
     const int nblk = K / 256, XS = img_col_bytes(K);
@@ -768,7 +813,7 @@ __device__ __forceinline__ void stage_activations(const OpInfo& op, uint8_t* xsm
     // arithmetic (K = 8192 at N = 1 is two rounds: one L2 round trip)
     const int hw = lane >> 4, h = lane & 15, total = N * nblk;
     for (int tb0 = 2 * cw + hw; tb0 - hw < total; tb0 += 4 * kCW) {  // warp-uniform
-        float4 v[2][4];
+        float4 v[2][4], uq[2][4];
         bool act[2];
         int t[2], b[2];
         // the second round only where the warp has one (warp-uniform)
@@ -785,6 +830,20 @@ __device__ __forceinline__ void stage_activations(const OpInfo& op, uint8_t* xsm
 #pragma unroll
                 for (int k = 0; k < 4; ++k)
                     v[r][k] = !act[r] ? make_float4(0.f, 0.f, 0.f, 0.f) : (kept ? keep_x[k] : __ldg(xv + k));
+                if constexpr (GLU) {
+                    const float4* uv = reinterpret_cast<const float4*>(reinterpret_cast<const uint8_t*>(nrm.up) +
+                                                                       t[r] * nrm.up_nb1) + b[r] * 64 + 4 * h;
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) uq[r][k] = act[r] ? __ldg(uv + k) : make_float4(0.f, 0.f, 0.f, 0.f);
+                }
+            }
+        }
+        if constexpr (GLU) {
+#pragma unroll
+            for (int r = 0; r < 2; ++r) {
+                if (r >= rounds) continue;
+#pragma unroll
+                for (int k = 0; k < 4; ++k) v[r][k] = glu4<PRO>(v[r][k], uq[r][k]);
             }
         }
         if constexpr (NORM) {
@@ -1178,9 +1237,9 @@ __device__ __forceinline__ void q8_unit(const OpRegs& op, const Q4Lane& q, Ring&
     }
 }
 
-// NORM: the fused RMS_NORM launches (a separate instantiation, so the plain
-// GEMV carries none of its code).
-template <int NT, bool NORM>
+// PRO: the fused activation prologue (kProNone for the plain GEMV; each kind
+// is a separate instantiation, so the plain GEMV carries none of their code).
+template <int NT, int PRO>
 __global__ void __launch_bounds__(kThreads, 1) stream_gemv_kernel(const __grid_constant__ SList L) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int S = L.stages;
@@ -1233,12 +1292,17 @@ __global__ void __launch_bounds__(kThreads, 1) stream_gemv_kernel(const __grid_c
     }
     if (threadIdx.x == 0) {
         T.n_ops = L.n_ops;
-        T.norm = L.norm;
+        T.pro = L.pro;
         T.total_units = L.total_units;
     }
     __syncthreads();
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
+    // Boxes issued before the first activation image is staged. A fused GLU's
+    // staging is SFU-bound after its loads, so the whole ring may go first
+    // (measured 0.2 us faster on a Q6_K 3072 x 8192 down projection; the
+    // RMS_NORM's two load passes were 0.8 us slower with it).
+    constexpr int pre = PRO == kProSwiglu || PRO == kProGelu ? kMaxStages : kPreStages;
     if (warp == 0 && L.all_tma) {
         // ---------------- copy warp, tensor-map path: lane 0 alone ----------------
         // One thread issues every box: a warp-wide loop (shuffles, reconvergence)
@@ -1259,7 +1323,7 @@ __global__ void __launch_bounds__(kThreads, 1) stream_gemv_kernel(const __grid_c
             const CUtensorMap* tm = &L.op[oi].tmap;
             for (int sg = 0, col = 0; sg < nseg; ++sg, col += step) {
                 if (!mbar_wait(&empty[s], phase, 1u, poisoned)) return;
-                if (issued++ == kPreStages && !mbar_wait(xready, 0u, 3u, poisoned)) return;
+                if (issued++ == pre && !mbar_wait(xready, 0u, 3u, poisoned)) return;
                 // one box: 16 rows x wbox bytes from the 16-byte-aligned column at or
                 // below the segment start (rows past M and columns past the row end
                 // read as zeros)
@@ -1298,7 +1362,7 @@ __global__ void __launch_bounds__(kThreads, 1) stream_gemv_kernel(const __grid_c
                 int ok = 0;
                 if (lane == 0) {
                     ok = mbar_wait(&empty[s], phase, 1u, poisoned);
-                    if (ok && issued == kPreStages) ok = mbar_wait(xready, 0u, 3u, poisoned);
+                    if (ok && issued == pre) ok = mbar_wait(xready, 0u, 3u, poisoned);
                 }
                 ++issued;
                 if (!__shfl_sync(0xffffffffu, ok, 0)) {
@@ -1395,7 +1459,7 @@ __global__ void __launch_bounds__(kThreads, 1) stream_gemv_kernel(const __grid_c
             if (staged < 0 || T.op[staged].x != oo.x || T.op[staged].K != oo.K || T.op[staged].N != oo.N ||
                 T.op[staged].x_nb1 != oo.x_nb1) {
                 consumers_sync();  // nobody still reads the previous image
-                stage_activations<NORM>(oo, xsm, lane, cw, T.norm, nred);
+                stage_activations<PRO>(oo, xsm, lane, cw, T.pro, nred);
                 if (ct == 0 && useq == 0) mbar_arrive_cnt(xready, 1u);  // the copy warp may go on
                 staged = oi;
             }
@@ -1571,13 +1635,17 @@ bool stream_supported(const MulMatOp* ops, int n_ops) {
 }
 
 int launch_stream(const MulMatOp* ops, int n_ops, cudaStream_t stream, int num_sms, const TpLaunch* tp,
-                  const NormLaunch* norm) {
+                  const ProLaunch* pro) {
     SList L{};
     L.n_ops = n_ops;
-    if (norm) {
-        L.norm.gain = norm->gain;
-        L.norm.eps = norm->eps;
-        L.norm.on = 1;
+    const int kind = pro ? pro->kind : kProNone;
+    if (kind < kProNone || kind > kProGelu) return -static_cast<int>(cudaErrorInvalidValue);
+    if (pro) {
+        L.pro.gain = pro->gain;
+        L.pro.up = pro->up;
+        L.pro.up_nb1 = pro->up_nb1;
+        L.pro.eps = pro->eps;
+        L.pro.kind = kind;
     }
     L.tp.world = 1;
     if (tp) {
@@ -1655,11 +1723,13 @@ int launch_stream(const MulMatOp* ops, int n_ops, cudaStream_t stream, int num_s
     cfg.numAttrs = 1;
     // raise the kernel's dynamic shared-memory limit to this launch's need
     // (once per size increase; the attribute call is not a stream operation)
-    static size_t configured[6] = {0, 0, 0, 0, 0, 0};
-    const int ti = (nt == 1 ? 0 : (nt == 2 ? 1 : 2)) + (norm ? 3 : 0);
-    void (*const kernels[6])(SList) = {stream_gemv_kernel<1, false>, stream_gemv_kernel<2, false>,
-                                       stream_gemv_kernel<4, false>, stream_gemv_kernel<1, true>,
-                                       stream_gemv_kernel<2, true>,  stream_gemv_kernel<4, true>};
+    static size_t configured[12] = {};
+    const int ti = (nt == 1 ? 0 : (nt == 2 ? 1 : 2)) + 3 * kind;
+    void (*const kernels[12])(SList) = {
+        stream_gemv_kernel<1, kProNone>,   stream_gemv_kernel<2, kProNone>,   stream_gemv_kernel<4, kProNone>,
+        stream_gemv_kernel<1, kProNorm>,   stream_gemv_kernel<2, kProNorm>,   stream_gemv_kernel<4, kProNorm>,
+        stream_gemv_kernel<1, kProSwiglu>, stream_gemv_kernel<2, kProSwiglu>, stream_gemv_kernel<4, kProSwiglu>,
+        stream_gemv_kernel<1, kProGelu>,   stream_gemv_kernel<2, kProGelu>,   stream_gemv_kernel<4, kProGelu>};
     void (*const kernel)(SList) = kernels[ti];
     cudaError_t e;
     if (configured[ti] < smem) {

@@ -850,10 +850,38 @@ int32_t wllm_mul_mat_rms_norm_batch(const wllm_mulmat_args* ops, int32_t n_ops, 
     // the fused form exists for the decode regime only: the caller runs the
     // RMS_NORM, MUL and MUL_MAT ops unfused otherwise
     if (!wllm::stream_supported(m, n_ops)) return WLLM_STATUS_NOT_IMPLEMENTED;
-    const wllm::NormLaunch nl{gain, eps};
+    const wllm::ProLaunch pl{wllm::kProNorm, gain, eps, nullptr, 0};
     const int rc = wllm::launch_stream(m, n_ops, stream ? static_cast<cudaStream_t>(stream) : s.stream, s.num_sms,
-                                       nullptr, &nl);
+                                       nullptr, &pl);
     if (rc < 0) return cuda_fail(s, static_cast<cudaError_t>(-rc), "wllm_mul_mat_rms_norm_batch launch");
+    s.counters.kernels_launched += static_cast<uint64_t>(rc);
+    return WLLM_STATUS_OK;
+}
+
+int32_t wllm_mul_mat_glu_batch(const wllm_mulmat_args* ops, int32_t n_ops, const float* up, int64_t up_stride,
+                               int32_t glu, void* stream) {
+    State& s = S();
+    std::lock_guard<std::mutex> g(s.mu);
+    if (!ensure_init(s)) return WLLM_STATUS_FAILED;
+    const char* what = "wllm_mul_mat_glu_batch";
+    MulMatOp m[wllm::kMaxOpsPerLaunch];
+    if (const int32_t rc = ops_from_args(s, what, ops, n_ops, m)) return rc;
+    if (glu != WLLM_GLU_SWIGLU && glu != WLLM_GLU_GELU) return fail(s, "%s: unknown glu kind %d", what, glu);
+    if (!up) return fail(s, "%s: null up", what);
+    if ((reinterpret_cast<uintptr_t>(up) & 15) || (up_stride & 3))
+        return fail(s, "%s: up must be 16-byte aligned and up_stride a multiple of 4", what);
+    if (m[0].N > 1 && up_stride < m[0].K) return fail(s, "%s: up_stride below one vector (K floats)", what);
+    const int64_t up_nb1 = 4 * up_stride;
+    for (int i = 1; i < n_ops; ++i)
+        if (m[i].x != m[0].x || m[i].x_nb1 != m[0].x_nb1 || m[i].K != m[0].K || m[i].N != m[0].N)
+            return fail(s, "%s: every op must read the same activations (one up tensor)", what);
+    // the fused form exists for the decode regime only: the caller runs the
+    // GLU and MUL_MAT ops unfused otherwise
+    if (!wllm::stream_supported(m, n_ops)) return WLLM_STATUS_NOT_IMPLEMENTED;
+    const wllm::ProLaunch pl{glu == WLLM_GLU_SWIGLU ? wllm::kProSwiglu : wllm::kProGelu, nullptr, 0.f, up, up_nb1};
+    const int rc = wllm::launch_stream(m, n_ops, stream ? static_cast<cudaStream_t>(stream) : s.stream, s.num_sms,
+                                       nullptr, &pl);
+    if (rc < 0) return cuda_fail(s, static_cast<cudaError_t>(-rc), "wllm_mul_mat_glu_batch launch");
     s.counters.kernels_launched += static_cast<uint64_t>(rc);
     return WLLM_STATUS_OK;
 }

@@ -78,16 +78,24 @@ struct TpLaunch {
     float* y_peer[kMaxOpsPerLaunch][kMaxRanks];  // op i's rows on rank r (own rank unused)
 };
 
-// Fused RMS_NORM (+ gain) of every op's activations before the streaming
-// GEMV: x / sqrt(mean(x^2) + eps) * gain (gain null: none).
-struct NormLaunch {
-    const float* gain;
-    float eps;
+// Fused prologue of every op's activations before the streaming GEMV.
+enum ProKind : int32_t {
+    kProNone = 0,
+    kProNorm = 1,    // RMS_NORM (+ gain): x / sqrt(mean(x^2) + eps) * gain (gain null: none)
+    kProSwiglu = 2,  // silu(x) * up
+    kProGelu = 3,    // gelu(x) * up (tanh form, f16-rounded like ggml's CPU GELU)
+};
+struct ProLaunch {
+    int32_t kind;
+    const float* gain;  // kProNorm
+    float eps;          // kProNorm
+    const float* up;    // kProSwiglu / kProGelu: the up projection's output, laid out like x
+    int64_t up_nb1;     // bytes between its vectors
 };
 
 bool stream_supported(const MulMatOp* ops, int n_ops);
 int launch_stream(const MulMatOp* ops, int n_ops, cudaStream_t stream, int num_sms, const TpLaunch* tp = nullptr,
-                  const NormLaunch* norm = nullptr);
+                  const ProLaunch* pro = nullptr);
 // One-thread kernel that waits (bounded) for every peer's signal of the
 // rank's last row-sharded launch.
 int launch_tp_wait(const TpLaunch& tp, cudaStream_t stream);

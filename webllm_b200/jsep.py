@@ -27,6 +27,9 @@ GGML_OP_RMS_NORM = 25
 GGML_OP_MUL_MAT = 29
 GGML_OP_SET_ROWS = 42
 
+GLU_SWIGLU = 1  # silu(gate) * up
+GLU_GELU = 2  # gelu(gate) * up (tanh form, f16-rounded like ggml's CPU GELU)
+
 GGML_TYPE_F32 = 0
 GGML_TYPE_F16 = 1
 GGML_TYPE_Q4_0 = 2
@@ -56,7 +59,9 @@ EXPORTED_SYMBOLS = (
     "wllm_init", "wllm_shutdown", "wllm_alloc", "wllm_free", "wllm_write", "wllm_read",
     "wllm_read_async_begin", "wllm_read_async_poll", "wllm_read_async_finish", "wllm_read_async_cancel",
     "wllm_clear", "wllm_run_op", "wllm_run_ops", "wllm_sync", "wllm_last_error", "wllm_get_counters",
-    "wllm_buffer_device_ptr", "wllm_mul_mat", "wllm_mul_mat_batch", "wllm_mul_mat_rms_norm_batch", "wllm_get_stream",
+    "wllm_buffer_device_ptr", "wllm_mul_mat", "wllm_mul_mat_batch", "wllm_mul_mat_rms_norm_batch",
+    "wllm_mul_mat_glu_batch",
+    "wllm_get_stream",
     "wllm_graph_begin", "wllm_graph_end", "wllm_graph_launch", "wllm_graph_destroy",
     "wllm_dequantize", "wllm_version", "wllm_mul_mat_prefill_static",
     "wllm_ipc_alloc", "wllm_ipc_open", "wllm_ipc_close", "wllm_ipc_free", "wllm_mul_mat_batch_tp", "wllm_tp_wait",
@@ -127,6 +132,7 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
         "wllm_dequantize": ([i32, vp, vp, i64, vp], i32),
         "wllm_mul_mat_batch": ([P(MulMatArgs), i32, vp], i32),
         "wllm_mul_mat_rms_norm_batch": ([P(MulMatArgs), i32, vp, ctypes.c_float, vp], i32),
+        "wllm_mul_mat_glu_batch": ([P(MulMatArgs), i32, vp, i64, i32, vp], i32),
         "wllm_ipc_alloc": ([u64, P(vp), vp], i32),
         "wllm_ipc_open": ([vp, P(vp)], i32),
         "wllm_ipc_close": ([vp], i32),
@@ -433,6 +439,17 @@ def mul_mat_rms_norm_batch(ops: Sequence[MulMatArgs], gain_ptr: int, eps: float,
     arr = (MulMatArgs * len(ops))(*ops)
     return _check(L.wllm_mul_mat_rms_norm_batch(arr, len(ops), int(gain_ptr) or None, float(eps),
                                                 int(stream) or None), "wllm_mul_mat_rms_norm_batch")
+
+
+def mul_mat_glu_batch(ops: Sequence[MulMatArgs], up_ptr: int, up_stride: int, glu: int, stream: int = 0) -> int:
+    """MUL_MATs of act(gate) * up with the GLU fused into the kernel
+    (wllm_mul_mat_glu_batch; the ops' x is the gate, up_stride is in floats):
+    STATUS_OK, or STATUS_NOT_IMPLEMENTED outside the decode regime (the caller
+    then runs the ops unfused)."""
+    L = load_library()
+    arr = (MulMatArgs * len(ops))(*ops)
+    return _check(L.wllm_mul_mat_glu_batch(arr, len(ops), int(up_ptr) or None, int(up_stride), int(glu),
+                                           int(stream) or None), "wllm_mul_mat_glu_batch")
 
 
 def ipc_alloc(size: int) -> tuple[int, bytes]:
