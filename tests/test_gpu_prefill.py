@@ -1,6 +1,7 @@
-"""GPU parity tests of the prefill path: Q4_K MUL_MAT with N > 64 vectors runs
-as a tcgen05 tensor-core GEMM (f16 dequantized weights and activations, f32
-accumulation).
+"""GPU parity tests of the prefill path: Q4_K and Q6_K MUL_MAT with N > 64
+vectors runs as a tcgen05 tensor-core GEMM (f16 dequantized weights and
+activations, f32 accumulation). Q6_K takes it when its rows are a multiple of
+16 bytes (K a multiple of 2048), as the tensor-memory copies need.
 
 Bar: max relative error <= 2e-2 (rel = max|y - r| / max|r|) against
  - the oracle's f64 dequant-then-dot (small and ragged shapes), and
@@ -98,6 +99,47 @@ def test_prefill_large_grids_vs_torch_fp32(runtime, M, K, N):
         jsep.mul_mat_device(O.TYPE_Q4_K, w.data_ptr(), w.shape[1], x.data_ptr(), K, y.data_ptr(), M, M, K, N, stream)
     wf = torch.empty(M, K, device=dev)
     jsep.dequantize_device(O.TYPE_Q4_K, w.data_ptr(), wf.data_ptr(), M * K, stream)
+    runtime.jsep_sync()
+    ref = (x.double() @ wf.double().t()).float()
+    rel = ((y - ref).abs().max() / ref.abs().max()).item()
+    assert rel <= PREFILL_TOL, rel
+
+
+@pytest.mark.parametrize("M,K,N", [
+    (128, 2048, 128),    # one tile, 8 blocks (block offsets 0, 2, ..., 14 in their 16-byte words)
+    (200, 2048, 65),     # partial row tile, smallest prefill N
+    (384, 4096, 300),    # partial vector tile
+])
+def test_prefill_q6k_matches_oracle(runtime, M, K, N):
+    rng = np.random.default_rng(2000 + M + K + N)
+    w = synth.weights(rng, O.TYPE_Q6_K, M, K)
+    x = synth.activations(rng, N, K)
+    k0 = counters().kernels_launched
+    y = run_mul_mat(runtime, O.TYPE_Q6_K, w, x)
+    assert counters().kernels_launched - k0 == 2, "expected the f16 pre-pass and the tensor-core GEMM"
+    r = O.mul_mat_f64(O.TYPE_Q6_K, w, x)
+    assert O.rel_error(y, r) <= PREFILL_TOL
+
+
+@pytest.mark.parametrize("M,K,N", [(4096, 14336, 512), (1024, 4096, 512), (3072, 8192, 200), (14336, 4096, 77)])
+def test_prefill_q6k_shapes_vs_torch_fp32(runtime, M, K, N):
+    """Q6_K projections of Q4_K_M models in prefill: Llama-3-8B ffn_down and
+    attn_v (512 tokens), Llama-3.2-3B ffn_down, and a wide one at a short N."""
+    import torch
+
+    dev = torch.device("cuda", 0)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(M * 5 + K + N)
+    w = synth.weights_torch(gen, O.TYPE_Q6_K, M, K, dev)
+    x = torch.randn(N, K, device=dev, generator=gen)
+    y = torch.empty(N, M, device=dev)
+    torch.cuda.synchronize()  # the library runs on its own stream
+    stream = jsep.library_stream()
+    k0 = counters().kernels_launched
+    jsep.mul_mat_device(O.TYPE_Q6_K, w.data_ptr(), w.shape[1], x.data_ptr(), K, y.data_ptr(), M, M, K, N, stream)
+    assert counters().kernels_launched - k0 == 2
+    wf = torch.empty(M, K, device=dev)
+    jsep.dequantize_device(O.TYPE_Q6_K, w.data_ptr(), wf.data_ptr(), M * K, stream)
     runtime.jsep_sync()
     ref = (x.double() @ wf.double().t()).float()
     rel = ((y - ref).abs().max() / ref.abs().max()).item()

@@ -1,6 +1,6 @@
 // Prefill-regime quantized MUL_MAT (N >= kPrefillMinN activation vectors, Q4_K
-// weights): a tcgen05 tensor-core GEMM that dequantizes the GGUF blocks to f16
-// in shared memory.
+// or Q6_K weights): a tcgen05 tensor-core GEMM that dequantizes the GGUF blocks
+// to f16 on the way into tensor memory.
 //
 //   y[m + M n] = sum_k W[m, k] x[k + K n]   (ggml MUL_MAT, matmul.ts:10-17)
 //
@@ -9,8 +9,10 @@
 // dequantized weight feeds 256 vectors, which keeps the dequantization (the
 // CUDA-core side) ahead of the MMAs. K is walked in chunks of 64.
 //
-//  - warp 0 (TMA): per 256-element Q4_K block, one 2D box of the 128 rows'
-//    raw blocks (128 x 144 B) into a raw ring; per 64-chunk, one 2D box of the
+//  - warp 0 (TMA): per 256-element block, one 2D box of the 128 rows' raw
+//    blocks into a raw ring (Q4_K: 128 x 144 B; Q6_K: 128 x 240 B, the 210-byte
+//    block from the 16-byte boundary at or below its start, which is 2 kb mod 16
+//    bytes into the row's box); per 64-chunk, one 2D box of the
 //    f16 activations (64 x 256, TMA 128-byte swizzle) into a B stage: the
 //    canonical K-major UMMA layout (vector n at (n/8)*1024 + (n%8)*128 bytes,
 //    its 16-byte piece j at position j ^ (n%8)).
@@ -57,8 +59,11 @@ constexpr int kTileM = 128;                      // rows of W per CTA (TMEM lane
 constexpr int kTileN = 256;                      // vectors per CTA (TMEM columns)
 constexpr int kChunkK = 64;                      // K per stage (one 128-byte swizzle atom of f16)
 constexpr int kStages = 4;                       // B stages in smem, A stages in TMEM
-constexpr int kRawSlots = 2;                     // raw Q4_K blocks in flight (each feeds 4 chunks)
-constexpr int kRawBytes = kTileM * 144;          // 18432
+constexpr int kRawSlots = 2;                     // raw blocks in flight (each feeds 4 chunks)
+constexpr int kQ6Box = 240;                      // bytes of a Q6_K box row: offset (<= 14) + 210, rounded to 16
+                                                 // and made 60 words (16-byte loads of 8 rows hit 32 banks)
+template <int TYPE>
+__host__ __device__ constexpr int raw_bytes() { return TYPE == kTypeQ6_K ? kTileM * kQ6Box : kTileM * 144; }  // 30720 / 18432
 constexpr int kBBytes = kTileN * kChunkK * 2;    // 32768
 constexpr int kDqWarps = 16;
 constexpr int kThreads = 32 * (2 + kDqWarps);    // TMA warp, MMA warp, dequant/epilogue warps
@@ -70,7 +75,8 @@ static_assert(kTileN + kStages * kACols <= kTmemCols, "TMEM budget");
 constexpr uint32_t kSpinLimit = 1u << 26;
 
 struct PrefillArgs {
-    CUtensorMap wmap;   // weights: [M rows][row_bytes / 8] uint64, box 18 x 128 (one block column)
+    CUtensorMap wmap;   // weights: Q4_K [M rows][row_bytes / 8] uint64, box 18 x 128 (one block column);
+                        // Q6_K [M rows][row_bytes] uint8, box 240 x 128
     CUtensorMap xmap;   // f16 activations: [N][K], box 64 x 128, 128-byte swizzle
     float* y;
     int64_t y_nb1;      // bytes between output vectors
@@ -172,7 +178,24 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
     for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-__global__ void __launch_bounds__(kThreads, 1) prefill_q4k_kernel(const __grid_constant__ PrefillArgs P) {
+// 16 bytes at byte o + c of a Q6_K box row (c a multiple of 16, o the block's
+// offset: even, the same for every row and thread of the block), from the two
+// aligned 16-byte words at c: word select by o / 4, then a funnel shift by
+// 8 (o % 4) bits.
+__device__ __forceinline__ uint4 q6_load16(const uint8_t* rowp, int c, int q4, uint32_t sh) {
+    const uint4* a = reinterpret_cast<const uint4*>(rowp + c);
+    const uint4 lo = a[0], hi = a[1];
+    const uint32_t w[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
+    uint32_t v[5];
+#pragma unroll
+    for (int i = 0; i < 5; ++i) v[i] = q4 == 0 ? w[i] : (q4 == 1 ? w[i + 1] : (q4 == 2 ? w[i + 2] : w[i + 3]));
+    return make_uint4(__funnelshift_r(v[0], v[1], sh), __funnelshift_r(v[1], v[2], sh), __funnelshift_r(v[2], v[3], sh),
+                      __funnelshift_r(v[3], v[4], sh));
+}
+
+template <int TYPE>
+__global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_constant__ PrefillArgs P) {
+    constexpr int kRawBytes = raw_bytes<TYPE>();
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     // 1024-byte alignment for the swizzled tiles
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -228,7 +251,10 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_q4k_kernel(const __grid_c
                     const int r = kb % kRawSlots;
                     if (kb >= kRawSlots && !mbar_wait(&raw_free[r], ((kb / kRawSlots) - 1) & 1, 1u, poisoned)) break;
                     mbar_expect_tx(&raw_full[r], kRawBytes);
-                    tma_2d(raw + r * kRawBytes, &P.wmap, (kb0 + kb) * 18, m0, &raw_full[r]);
+                    // x: Q4_K in uint64 words (18 per block); Q6_K in bytes, the
+                    // block's start rounded down to 16
+                    const int x = TYPE == kTypeQ6_K ? ((kb0 + kb) * 210) & ~15 : (kb0 + kb) * 18;
+                    tma_2d(raw + r * kRawBytes, &P.wmap, x, m0, &raw_full[r]);
                 }
                 const int s = q % kStages;
                 if (q >= kStages && !mbar_wait(&st_free[s], ((q / kStages) - 1) & 1, 1u, poisoned)) break;
@@ -271,51 +297,103 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_q4k_kernel(const __grid_c
         for (int kb = 0; kb < nblk && !stop; ++kb) {
             const int rs = kb % kRawSlots;
             if (!mbar_wait(&raw_full[rs], (kb / kRawSlots) & 1, 3u, poisoned)) break;
-            const uint8_t* blk = raw + rs * kRawBytes + r * 144;
-            // scales of this thread's sub-blocks j = 2p + h (p = 0..3), get_scale_min_k4
-            // (src/inference/jsep/ops/matmul.ts:408-424) on the bytes of the three scale words
-            const uint4 hdr = *reinterpret_cast<const uint4*>(blk);
-            const float d = f16_bits_to_f32(hdr.x), dmin = f16_bits_to_f32(hdr.x >> 16);
-            const uint32_t w1a = __byte_perm(hdr.y, 0u, sel_a), w1b = __byte_perm(hdr.y, 0u, sel_b);
-            const uint32_t w2a = __byte_perm(hdr.z, 0u, sel_a), w2b = __byte_perm(hdr.z, 0u, sel_b);
-            const uint32_t w3a = __byte_perm(hdr.w, 0u, sel_a), w3b = __byte_perm(hdr.w, 0u, sel_b);
-            const uint32_t scv[4] = {w1a & 63u, w1b & 63u, (w3a & 15u) | ((w1a >> 6) << 4), (w3b & 15u) | ((w1b >> 6) << 4)};
-            const uint32_t mv[4] = {w2a & 63u, w2b & 63u, (w3a >> 4) | ((w2a >> 6) << 4), (w3b >> 4) | ((w2b >> 6) << 4)};
-            const uint4* qs = reinterpret_cast<const uint4*>(blk + 16);
-#pragma unroll
-            for (int p = 0; p < 4; ++p, ++q) {
-                const int s = q % kStages;
-                if (q >= kStages && !mbar_wait(&st_free[s], ((q / kStages) - 1) & 1, 3u, poisoned)) {
-                    stop = true;
-                    break;
+            if constexpr (TYPE == kTypeQ6_K) {
+                // Q6_K (ggml's dequantize_row_q6_K layout, as in quant_blocks.cuh):
+                // element 64p + 32h + 16qq + l of the block is in half p/2,
+                // j = 2 (p%2) + h: ql byte 64 (p/2) + 32 h + 16 qq + l (high nibble when
+                // p is odd), qh byte 128 + 32 (p/2) + 16 qq + l shifted by 2 j, scale
+                // 192 + 8 (p/2) + 2 j + qq; w = d sc (q - 32)
+                const int o = ((kb0 + kb) * 210) & 15;
+                const uint8_t* rowp = raw + rs * kRawBytes + r * kQ6Box;
+                const int q4 = o >> 2;
+                const uint32_t sh = 8u * static_cast<uint32_t>(o & 3);
+                const float d = __half2float(*reinterpret_cast<const __half*>(rowp + o + 208));
+                const __half2 k1056 = __float2half2_rn(1056.f);
+                uint4 ql = make_uint4(0u, 0u, 0u, 0u), qh = ql;
+    #pragma unroll
+                for (int p = 0; p < 4; ++p, ++q) {
+                    const int s = q % kStages;
+                    if (q >= kStages && !mbar_wait(&st_free[s], ((q / kStages) - 1) & 1, 3u, poisoned)) {
+                        stop = true;
+                        break;
+                    }
+                    const int ip = p >> 1, hb = p & 1, j = 2 * hb + h;
+                    if (hb == 0) {  // one load of each array per half
+                        ql = q6_load16(rowp, 64 * ip + 32 * h + 16 * qq, q4, sh);
+                        qh = q6_load16(rowp, 128 + 32 * ip + 16 * qq, q4, sh);
+                    }
+                    const float sc = static_cast<float>(static_cast<int8_t>(rowp[o + 192 + 8 * ip + 2 * j + qq]));
+                    const __half2 ds2 = __float2half2_rn(d * sc);
+                    const uint32_t lw[4] = {ql.x, ql.y, ql.z, ql.w}, hw[4] = {qh.x, qh.y, qh.z, qh.w};
+                    uint32_t out[8];  // 16 f16, element order l = 0..15
+    #pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const uint32_t qv = ((lw[i] >> (4 * hb)) & 0x0F0F0F0Fu) | (((hw[i] >> (2 * j)) & 0x03030303u) << 4);
+                        // f16 1024 + q (exact, q < 64), minus 1056: q - 32 exactly
+                        const uint32_t e01 = __byte_perm(qv, 0x00006464u, 0x5140u);
+                        const uint32_t e23 = __byte_perm(qv, 0x00006464u, 0x5342u);
+                        const __half2 q01 = __hsub2(*reinterpret_cast<const __half2*>(&e01), k1056);
+                        const __half2 q23 = __hsub2(*reinterpret_cast<const __half2*>(&e23), k1056);
+                        const __half2 w01 = __hmul2(q01, ds2), w23 = __hmul2(q23, ds2);
+                        out[2 * i] = *reinterpret_cast<const uint32_t*>(&w01);
+                        out[2 * i + 1] = *reinterpret_cast<const uint32_t*>(&w23);
+                    }
+                    tmem_st8(trow + static_cast<uint32_t>(kTileN + s * kACols + 16 * h + 8 * qq), out);
+                    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) {
+                        mbar_arrive(&a_full[s]);
+                        if (p == 3) mbar_arrive(&raw_free[rs]);
+                    }
                 }
-                const __half2 sc2 = __float2half2_rn(d * static_cast<float>(scv[p]));
-                const __half2 mn2 = __float2half2_rn(-dmin * static_cast<float>(mv[p]));
-                // bytes 16 qq .. 16 qq + 15 of pair p; this thread's quants are their low
-                // (h = 0) or high (h = 1) nibbles: elements 64p + 32h + 16qq + l, l = 0..15
-                const uint4 v0 = qs[2 * p + qq];
-                const uint32_t wv[4] = {v0.x, v0.y, v0.z, v0.w};
-                uint32_t out[8];  // 16 f16, element order l = 0..15
-#pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    const uint32_t nib = (wv[i] >> (4 * h)) & 0x0F0F0F0Fu;
-                    // f16 1024 + q (exact) for bytes (0, 1) and (2, 3): 0x64 in each high byte
-                    const uint32_t e01 = __byte_perm(nib, 0x00006464u, 0x5140u);
-                    const uint32_t e23 = __byte_perm(nib, 0x00006464u, 0x5342u);
-                    const __half2 q01 = __hsub2(*reinterpret_cast<const __half2*>(&e01), k1024);
-                    const __half2 q23 = __hsub2(*reinterpret_cast<const __half2*>(&e23), k1024);
-                    const __half2 w01 = __hfma2(q01, sc2, mn2), w23 = __hfma2(q23, sc2, mn2);
-                    out[2 * i] = *reinterpret_cast<const uint32_t*>(&w01);
-                    out[2 * i + 1] = *reinterpret_cast<const uint32_t*>(&w23);
-                }
-                // k = 32h + 16qq + l of this chunk: TMEM columns 16h + 8qq .. +7 of A stage s
-                tmem_st8(trow + static_cast<uint32_t>(kTileN + s * kACols + 16 * h + 8 * qq), out);
-                asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) {
-                    mbar_arrive(&a_full[s]);
-                    if (p == 3) mbar_arrive(&raw_free[rs]);
+            } else {
+                const uint8_t* blk = raw + rs * kRawBytes + r * 144;
+                // scales of this thread's sub-blocks j = 2p + h (p = 0..3), get_scale_min_k4
+                // (src/inference/jsep/ops/matmul.ts:408-424) on the bytes of the three scale words
+                const uint4 hdr = *reinterpret_cast<const uint4*>(blk);
+                const float d = f16_bits_to_f32(hdr.x), dmin = f16_bits_to_f32(hdr.x >> 16);
+                const uint32_t w1a = __byte_perm(hdr.y, 0u, sel_a), w1b = __byte_perm(hdr.y, 0u, sel_b);
+                const uint32_t w2a = __byte_perm(hdr.z, 0u, sel_a), w2b = __byte_perm(hdr.z, 0u, sel_b);
+                const uint32_t w3a = __byte_perm(hdr.w, 0u, sel_a), w3b = __byte_perm(hdr.w, 0u, sel_b);
+                const uint32_t scv[4] = {w1a & 63u, w1b & 63u, (w3a & 15u) | ((w1a >> 6) << 4), (w3b & 15u) | ((w1b >> 6) << 4)};
+                const uint32_t mv[4] = {w2a & 63u, w2b & 63u, (w3a >> 4) | ((w2a >> 6) << 4), (w3b >> 4) | ((w2b >> 6) << 4)};
+                const uint4* qs = reinterpret_cast<const uint4*>(blk + 16);
+    #pragma unroll
+                for (int p = 0; p < 4; ++p, ++q) {
+                    const int s = q % kStages;
+                    if (q >= kStages && !mbar_wait(&st_free[s], ((q / kStages) - 1) & 1, 3u, poisoned)) {
+                        stop = true;
+                        break;
+                    }
+                    const __half2 sc2 = __float2half2_rn(d * static_cast<float>(scv[p]));
+                    const __half2 mn2 = __float2half2_rn(-dmin * static_cast<float>(mv[p]));
+                    // bytes 16 qq .. 16 qq + 15 of pair p; this thread's quants are their low
+                    // (h = 0) or high (h = 1) nibbles: elements 64p + 32h + 16qq + l, l = 0..15
+                    const uint4 v0 = qs[2 * p + qq];
+                    const uint32_t wv[4] = {v0.x, v0.y, v0.z, v0.w};
+                    uint32_t out[8];  // 16 f16, element order l = 0..15
+    #pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const uint32_t nib = (wv[i] >> (4 * h)) & 0x0F0F0F0Fu;
+                        // f16 1024 + q (exact) for bytes (0, 1) and (2, 3): 0x64 in each high byte
+                        const uint32_t e01 = __byte_perm(nib, 0x00006464u, 0x5140u);
+                        const uint32_t e23 = __byte_perm(nib, 0x00006464u, 0x5342u);
+                        const __half2 q01 = __hsub2(*reinterpret_cast<const __half2*>(&e01), k1024);
+                        const __half2 q23 = __hsub2(*reinterpret_cast<const __half2*>(&e23), k1024);
+                        const __half2 w01 = __hfma2(q01, sc2, mn2), w23 = __hfma2(q23, sc2, mn2);
+                        out[2 * i] = *reinterpret_cast<const uint32_t*>(&w01);
+                        out[2 * i + 1] = *reinterpret_cast<const uint32_t*>(&w23);
+                    }
+                    // k = 32h + 16qq + l of this chunk: TMEM columns 16h + 8qq .. +7 of A stage s
+                    tmem_st8(trow + static_cast<uint32_t>(kTileN + s * kACols + 16 * h + 8 * qq), out);
+                    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) {
+                        mbar_arrive(&a_full[s]);
+                        if (p == 3) mbar_arrive(&raw_free[rs]);
+                    }
                 }
             }
         }
@@ -430,8 +508,12 @@ EncodeFn encoder() {
     return fn;
 }
 
-constexpr size_t kSmemBytes = 1024 /* alignment */ + kStages * kBBytes + kRawSlots * kRawBytes +
-                              8 * (3 * kStages + 2 * kRawSlots + 1) + 16;
+template <int TYPE>
+constexpr size_t smem_bytes() {
+    return 1024 /* alignment */ + kStages * kBBytes + kRawSlots * raw_bytes<TYPE>() + 8 * (3 * kStages + 2 * kRawSlots + 1) +
+           16;
+}
+static_assert(smem_bytes<kTypeQ6_K>() <= 227 * 1024, "shared memory");
 constexpr int kSlots = 148;  // CTAs resident at once (one per SM)
 constexpr int kMaxSplits = 8;
 
@@ -467,11 +549,14 @@ size_t split_bytes(const MulMatOp& o, int splits) {
 }  // namespace
 
 bool prefill_supported(const MulMatOp& o) {
-    if (o.type != kTypeQ4_K || o.N < kPrefillMinN || o.ne2 != 1 || o.ne3 != 1) return false;
+    if ((o.type != kTypeQ4_K && o.type != kTypeQ6_K) || o.N < kPrefillMinN || o.ne2 != 1 || o.ne3 != 1) return false;
     if (o.K % 256 != 0 || o.M < 1) return false;
-    const int64_t row_bytes = static_cast<int64_t>(o.K / 256) * 144;
-    if ((reinterpret_cast<uintptr_t>(o.w) | static_cast<uintptr_t>(o.w_nb1)) & 15) return false;  // TMA rows
+    const int64_t row_bytes = static_cast<int64_t>(o.K / 256) * (o.type == kTypeQ6_K ? 210 : 144);
+    // TMA rows: 16-byte aligned base and row stride (Q6_K: K a multiple of 2048
+    // for unpadded rows; other Q6_K shapes take the batched GEMM)
+    if ((reinterpret_cast<uintptr_t>(o.w) | static_cast<uintptr_t>(o.w_nb1)) & 15) return false;
     if (o.w_nb1 < row_bytes) return false;
+    if (o.type == kTypeQ6_K && row_bytes < kQ6Box) return false;  // the box stays within a row's width
     if ((reinterpret_cast<uintptr_t>(o.x) | static_cast<uintptr_t>(o.x_nb1)) & 15) return false;  // float4 reads
     return encoder() != nullptr;
 }
@@ -499,14 +584,19 @@ int launch_prefill(const MulMatOp& o, void* workspace, size_t workspace_bytes, c
     }
     PrefillArgs P{};
     const EncodeFn enc = encoder();
+    const bool q6 = o.type == kTypeQ6_K;
     {
-        const cuuint64_t dims[2] = {static_cast<cuuint64_t>(o.K / 256) * 18, static_cast<cuuint64_t>(o.M)};
+        // Q4_K: uint64 words, one 18-word block column per box; Q6_K: bytes, a
+        // 240-byte box from the block's 16-byte-rounded start (the box's end may
+        // pass the row's last block: zeros, never read)
+        const cuuint64_t dims[2] = {q6 ? static_cast<cuuint64_t>(o.K / 256) * 210 : static_cast<cuuint64_t>(o.K / 256) * 18,
+                                    static_cast<cuuint64_t>(o.M)};
         const cuuint64_t strides[1] = {static_cast<cuuint64_t>(o.w_nb1)};
-        const cuuint32_t box[2] = {18, kTileM};
+        const cuuint32_t box[2] = {q6 ? static_cast<cuuint32_t>(kQ6Box) : 18u, kTileM};
         const cuuint32_t es[2] = {1, 1};
-        if (enc(&P.wmap, CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, const_cast<uint8_t*>(o.w), dims, strides, box, es,
-                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+        if (enc(&P.wmap, q6 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, const_cast<uint8_t*>(o.w),
+                dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
             return -static_cast<int>(cudaErrorInvalidValue);
     }
     {
@@ -534,15 +624,17 @@ int launch_prefill(const MulMatOp& o, void* workspace, size_t workspace_bytes, c
         const cudaError_t e = cudaMemsetAsync(P.counters, 0, tiles * 4, stream);
         if (e != cudaSuccess) return -static_cast<int>(e);
     }
-    static bool configured = false;
-    if (!configured) {
-        const cudaError_t e = cudaFuncSetAttribute(prefill_q4k_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                   static_cast<int>(kSmemBytes));
+    static bool configured[2] = {false, false};
+    void (*const kernel)(PrefillArgs) = q6 ? prefill_kernel<kTypeQ6_K> : prefill_kernel<kTypeQ4_K>;
+    const size_t smem = q6 ? smem_bytes<kTypeQ6_K>() : smem_bytes<kTypeQ4_K>();
+    if (!configured[q6]) {
+        const cudaError_t e =
+            cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
         if (e != cudaSuccess) return -static_cast<int>(e);
-        configured = true;
+        configured[q6] = true;
     }
     const dim3 grid((o.M + kTileM - 1) / kTileM, (o.N + kTileN - 1) / kTileN, splits);
-    prefill_q4k_kernel<<<grid, kThreads, kSmemBytes, stream>>>(P);
+    kernel<<<grid, kThreads, smem, stream>>>(P);
     const cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? launched : -static_cast<int>(e);
 }
