@@ -134,12 +134,15 @@ def test_gemma2_q8_0_shapes(runtime, name, qtype, M, K, N):
                                          ("attn_proxy", 2304, 2304, 65), ("ragged", 200, 768, 3)])
 def test_q8_0_batched_decode(runtime, name, M, K, N):
     """Several sequences decoding together (Gemma-2-2B Q8_0 shapes, batch up to
-    64 and one past it): the integer tensor-core batched GEMM, split K included."""
+    64): the integer tensor-core batched GEMM, split K included, at the GEMV
+    bar. One past it (N = 65) is the f16 tcgen05 prefill GEMM, at the prefill
+    bar (2e-2)."""
     rng = np.random.default_rng(zlib.crc32(name.encode()) + N)
     w = synth.weights(rng, jsep.GGML_TYPE_Q8_0, M, K)
     x = synth.activations(rng, N, K)
     got = run_mul_mat(runtime, jsep.GGML_TYPE_Q8_0, w, x)
-    assert O.rel_error(got, O.mul_mat_f64(jsep.GGML_TYPE_Q8_0, w, x)) <= GEMV_TOL
+    tol = GEMV_TOL if N <= 64 else 2e-2
+    assert O.rel_error(got, O.mul_mat_f64(jsep.GGML_TYPE_Q8_0, w, x)) <= tol
 
 
 @pytest.mark.parametrize("N", [3, 4, 8, 16, 33, 64])

@@ -1,5 +1,5 @@
-"""GPU parity tests of the prefill path: Q4_K and Q6_K MUL_MAT with N > 64
-vectors runs as a tcgen05 tensor-core GEMM (f16 dequantized weights and
+"""GPU parity tests of the prefill path: Q4_K, Q5_K, Q6_K and Q8_0 MUL_MAT with
+N > 64 vectors runs as a tcgen05 tensor-core GEMM (f16 dequantized weights and
 activations, f32 accumulation). Q6_K takes it when its rows are a multiple of
 16 bytes (K a multiple of 2048), as the tensor-memory copies need.
 
@@ -140,6 +140,48 @@ def test_prefill_q6k_shapes_vs_torch_fp32(runtime, M, K, N):
     assert counters().kernels_launched - k0 == 2
     wf = torch.empty(M, K, device=dev)
     jsep.dequantize_device(O.TYPE_Q6_K, w.data_ptr(), wf.data_ptr(), M * K, stream)
+    runtime.jsep_sync()
+    ref = (x.double() @ wf.double().t()).float()
+    rel = ((y - ref).abs().max() / ref.abs().max()).item()
+    assert rel <= PREFILL_TOL, rel
+
+
+@pytest.mark.parametrize("qtype,M,K,N", [
+    (O.TYPE_Q5_K, 128, 256, 65),      # one block, smallest prefill N
+    (O.TYPE_Q5_K, 200, 2048, 130),    # partial row and vector tiles
+    (O.TYPE_Q8_0, 128, 256, 128),     # one 8-block group
+    (O.TYPE_Q8_0, 333, 2304, 300),    # Gemma-2-2B hidden: 9 groups; partial tiles
+])
+def test_prefill_q5k_q8_0_matches_oracle(runtime, qtype, M, K, N):
+    rng = np.random.default_rng(3000 + qtype + M + K + N)
+    w = synth.weights(rng, qtype, M, K)
+    x = synth.activations(rng, N, K)
+    k0 = counters().kernels_launched
+    y = run_mul_mat(runtime, qtype, w, x)
+    assert counters().kernels_launched - k0 == 2, "expected the f16 pre-pass and the tensor-core GEMM"
+    assert O.rel_error(y, O.mul_mat_f64(qtype, w, x)) <= PREFILL_TOL
+
+
+@pytest.mark.parametrize("qtype,M,K,N", [(O.TYPE_Q8_0, 9216, 2304, 512), (O.TYPE_Q8_0, 2304, 9216, 256),
+                                         (O.TYPE_Q5_K, 14336, 4096, 512), (O.TYPE_Q5_K, 4096, 14336, 200)])
+def test_prefill_q5k_q8_0_shapes_vs_torch_fp32(runtime, qtype, M, K, N):
+    """Gemma-2-2B ffn_up / ffn_down (Q8_0) and Llama-3-8B ffn_gate / ffn_down
+    (Q5_K) in prefill."""
+    import torch
+
+    dev = torch.device("cuda", 0)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(M * 3 + K + N + qtype)
+    w = synth.weights_torch(gen, qtype, M, K, dev)
+    x = torch.randn(N, K, device=dev, generator=gen)
+    y = torch.empty(N, M, device=dev)
+    torch.cuda.synchronize()  # the library runs on its own stream
+    stream = jsep.library_stream()
+    k0 = counters().kernels_launched
+    jsep.mul_mat_device(qtype, w.data_ptr(), w.shape[1], x.data_ptr(), K, y.data_ptr(), M, M, K, N, stream)
+    assert counters().kernels_launched - k0 == 2
+    wf = torch.empty(M, K, device=dev)
+    jsep.dequantize_device(qtype, w.data_ptr(), wf.data_ptr(), M * K, stream)
     runtime.jsep_sync()
     ref = (x.double() @ wf.double().t()).float()
     rel = ((y - ref).abs().max() / ref.abs().max()).item()

@@ -1,5 +1,5 @@
-// Prefill-regime quantized MUL_MAT (N >= kPrefillMinN activation vectors, Q4_K
-// or Q6_K weights): a tcgen05 tensor-core GEMM that dequantizes the GGUF blocks
+// Prefill-regime quantized MUL_MAT (N >= kPrefillMinN activation vectors, Q4_K,
+// Q5_K, Q6_K or Q8_0 weights): a tcgen05 tensor-core GEMM that dequantizes the GGUF blocks
 // to f16 on the way into tensor memory.
 //
 //   y[m + M n] = sum_k W[m, k] x[k + K n]   (ggml MUL_MAT, matmul.ts:10-17)
@@ -63,7 +63,13 @@ constexpr int kRawSlots = 2;                     // raw blocks in flight (each f
 constexpr int kQ6Box = 240;                      // bytes of a Q6_K box row: offset (<= 14) + 210, rounded to 16
                                                  // and made 60 words (16-byte loads of 8 rows hit 32 banks)
 template <int TYPE>
-__host__ __device__ constexpr int raw_bytes() { return TYPE == kTypeQ6_K ? kTileM * kQ6Box : kTileM * 144; }  // 30720 / 18432
+__host__ __device__ constexpr int raw_row_bytes() {
+    return TYPE == kTypeQ6_K ? kQ6Box : (TYPE == kTypeQ5_K ? 176 : (TYPE == kTypeQ8_0 ? 272 : 144));
+}
+// one box row per 256 elements: Q4_K 144 B, Q5_K 176 B, Q8_0 272 B (8 blocks),
+// Q6_K 240 B; all rows 16-byte multiples with conflict-free 16-byte loads
+template <int TYPE>
+__host__ __device__ constexpr int raw_bytes() { return kTileM * raw_row_bytes<TYPE>(); }
 constexpr int kBBytes = kTileN * kChunkK * 2;    // 32768
 constexpr int kDqWarps = 16;
 constexpr int kThreads = 32 * (2 + kDqWarps);    // TMA warp, MMA warp, dequant/epilogue warps
@@ -184,7 +190,7 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
 // 8 (o % 4) bits.
 __device__ __forceinline__ uint4 q6_load16(const uint8_t* rowp, int c, int q4, uint32_t sh) {
     const uint4* a = reinterpret_cast<const uint4*>(rowp + c);
-    const uint4 lo = a[0], hi = a[1];
+    const uint4 lo = a[0], hi = (q4 | sh) ? a[1] : lo;  // an aligned piece needs no second word
     const uint32_t w[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
     uint32_t v[5];
 #pragma unroll
@@ -251,9 +257,9 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
                     const int r = kb % kRawSlots;
                     if (kb >= kRawSlots && !mbar_wait(&raw_free[r], ((kb / kRawSlots) - 1) & 1, 1u, poisoned)) break;
                     mbar_expect_tx(&raw_full[r], kRawBytes);
-                    // x: Q4_K in uint64 words (18 per block); Q6_K in bytes, the
-                    // block's start rounded down to 16
-                    const int x = TYPE == kTypeQ6_K ? ((kb0 + kb) * 210) & ~15 : (kb0 + kb) * 18;
+                    // x: uint64 words per 256 elements (Q4_K 18, Q5_K 22, Q8_0 34);
+                    // Q6_K in bytes, the block's start rounded down to 16
+                    const int x = TYPE == kTypeQ6_K ? ((kb0 + kb) * 210) & ~15 : (kb0 + kb) * (raw_row_bytes<TYPE>() / 8);
                     tma_2d(raw + r * kRawBytes, &P.wmap, x, m0, &raw_full[r]);
                 }
                 const int s = q % kStages;
@@ -310,7 +316,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
                 const float d = __half2float(*reinterpret_cast<const __half*>(rowp + o + 208));
                 const __half2 k1056 = __float2half2_rn(1056.f);
                 uint4 ql = make_uint4(0u, 0u, 0u, 0u), qh = ql;
-    #pragma unroll
+#pragma unroll
                 for (int p = 0; p < 4; ++p, ++q) {
                     const int s = q % kStages;
                     if (q >= kStages && !mbar_wait(&st_free[s], ((q / kStages) - 1) & 1, 3u, poisoned)) {
@@ -326,7 +332,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
                     const __half2 ds2 = __float2half2_rn(d * sc);
                     const uint32_t lw[4] = {ql.x, ql.y, ql.z, ql.w}, hw[4] = {qh.x, qh.y, qh.z, qh.w};
                     uint32_t out[8];  // 16 f16, element order l = 0..15
-    #pragma unroll
+#pragma unroll
                     for (int i = 0; i < 4; ++i) {
                         const uint32_t qv = ((lw[i] >> (4 * hb)) & 0x0F0F0F0Fu) | (((hw[i] >> (2 * j)) & 0x03030303u) << 4);
                         // f16 1024 + q (exact, q < 64), minus 1056: q - 32 exactly
@@ -347,8 +353,50 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
                         if (p == 3) mbar_arrive(&raw_free[rs]);
                     }
                 }
+            } else if constexpr (TYPE == kTypeQ8_0) {
+                // Q8_0: 8 blocks of 34 B (f16 d, 32 int8) per 256 elements; this
+                // thread's 16 quants of chunk p are bytes 16qq .. +15 of block
+                // 2p + h, w = d q. Their start is 2 (2p + h) + 2 bytes past a
+                // 16-byte boundary (warp-uniform)
+                const uint8_t* rowp = raw + rs * kRawBytes + r * 272;
+                const __half2 k1152 = __float2half2_rn(1152.f);
+#pragma unroll
+                for (int p = 0; p < 4; ++p, ++q) {
+                    const int s = q % kStages;
+                    if (q >= kStages && !mbar_wait(&st_free[s], ((q / kStages) - 1) & 1, 3u, poisoned)) {
+                        stop = true;
+                        break;
+                    }
+                    const int bo = 34 * (2 * p + h), a = bo + 2 + 16 * qq, o = a & 15;
+                    const __half2 d2 = __half2half2(*reinterpret_cast<const __half*>(rowp + bo));
+                    const uint4 v0 = q6_load16(rowp, a & ~15, o >> 2, 8u * static_cast<uint32_t>(o & 3));
+                    const uint32_t wv[4] = {v0.x, v0.y, v0.z, v0.w};
+                    uint32_t out[8];  // 16 f16, element order l = 0..15
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        // f16 1024 + (q + 128) (exact), minus 1152: q exactly
+                        const uint32_t u = wv[i] ^ 0x80808080u;
+                        const uint32_t e01 = __byte_perm(u, 0x00006464u, 0x5140u);
+                        const uint32_t e23 = __byte_perm(u, 0x00006464u, 0x5342u);
+                        const __half2 q01 = __hsub2(*reinterpret_cast<const __half2*>(&e01), k1152);
+                        const __half2 q23 = __hsub2(*reinterpret_cast<const __half2*>(&e23), k1152);
+                        const __half2 w01 = __hmul2(q01, d2), w23 = __hmul2(q23, d2);
+                        out[2 * i] = *reinterpret_cast<const uint32_t*>(&w01);
+                        out[2 * i + 1] = *reinterpret_cast<const uint32_t*>(&w23);
+                    }
+                    tmem_st8(trow + static_cast<uint32_t>(kTileN + s * kACols + 16 * h + 8 * qq), out);
+                    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) {
+                        mbar_arrive(&a_full[s]);
+                        if (p == 3) mbar_arrive(&raw_free[rs]);
+                    }
+                }
             } else {
-                const uint8_t* blk = raw + rs * kRawBytes + r * 144;
+                // Q4_K, and Q5_K (the same header; qh[32] @16, qs[128] @48; bit
+                // 2p + h of qh byte 16qq + l is the fifth bit of the element)
+                const uint8_t* blk = raw + rs * kRawBytes + r * raw_row_bytes<TYPE>();
                 // scales of this thread's sub-blocks j = 2p + h (p = 0..3), get_scale_min_k4
                 // (src/inference/jsep/ops/matmul.ts:408-424) on the bytes of the three scale words
                 const uint4 hdr = *reinterpret_cast<const uint4*>(blk);
@@ -358,8 +406,11 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
                 const uint32_t w3a = __byte_perm(hdr.w, 0u, sel_a), w3b = __byte_perm(hdr.w, 0u, sel_b);
                 const uint32_t scv[4] = {w1a & 63u, w1b & 63u, (w3a & 15u) | ((w1a >> 6) << 4), (w3b & 15u) | ((w1b >> 6) << 4)};
                 const uint32_t mv[4] = {w2a & 63u, w2b & 63u, (w3a >> 4) | ((w2a >> 6) << 4), (w3b >> 4) | ((w2b >> 6) << 4)};
-                const uint4* qs = reinterpret_cast<const uint4*>(blk + 16);
-    #pragma unroll
+                const uint4* qs = reinterpret_cast<const uint4*>(blk + (TYPE == kTypeQ5_K ? 48 : 16));
+                uint4 qh = make_uint4(0u, 0u, 0u, 0u);
+                if constexpr (TYPE == kTypeQ5_K) qh = *reinterpret_cast<const uint4*>(blk + 16 + 16 * qq);
+                const uint32_t hv[4] = {qh.x, qh.y, qh.z, qh.w};
+#pragma unroll
                 for (int p = 0; p < 4; ++p, ++q) {
                     const int s = q % kStages;
                     if (q >= kStages && !mbar_wait(&st_free[s], ((q / kStages) - 1) & 1, 3u, poisoned)) {
@@ -373,9 +424,10 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
                     const uint4 v0 = qs[2 * p + qq];
                     const uint32_t wv[4] = {v0.x, v0.y, v0.z, v0.w};
                     uint32_t out[8];  // 16 f16, element order l = 0..15
-    #pragma unroll
+#pragma unroll
                     for (int i = 0; i < 4; ++i) {
-                        const uint32_t nib = (wv[i] >> (4 * h)) & 0x0F0F0F0Fu;
+                        uint32_t nib = (wv[i] >> (4 * h)) & 0x0F0F0F0Fu;
+                        if constexpr (TYPE == kTypeQ5_K) nib |= ((hv[i] >> (2 * p + h)) & 0x01010101u) << 4;
                         // f16 1024 + q (exact) for bytes (0, 1) and (2, 3): 0x64 in each high byte
                         const uint32_t e01 = __byte_perm(nib, 0x00006464u, 0x5140u);
                         const uint32_t e23 = __byte_perm(nib, 0x00006464u, 0x5342u);
@@ -513,7 +565,7 @@ constexpr size_t smem_bytes() {
     return 1024 /* alignment */ + kStages * kBBytes + kRawSlots * raw_bytes<TYPE>() + 8 * (3 * kStages + 2 * kRawSlots + 1) +
            16;
 }
-static_assert(smem_bytes<kTypeQ6_K>() <= 227 * 1024, "shared memory");
+static_assert(smem_bytes<kTypeQ8_0>() <= 227 * 1024 && smem_bytes<kTypeQ6_K>() <= 227 * 1024, "shared memory");
 constexpr int kSlots = 148;  // CTAs resident at once (one per SM)
 constexpr int kMaxSplits = 8;
 
@@ -539,6 +591,11 @@ int plan_splits(const MulMatOp& o) {
     return best;
 }
 
+// Bytes of 256 elements of a row: Q4_K 144, Q5_K 176, Q6_K 210, Q8_0 272.
+int block_group_bytes(int type) {
+    return type == kTypeQ6_K ? 210 : (type == kTypeQ5_K ? 176 : (type == kTypeQ8_0 ? 272 : 144));
+}
+
 size_t x16_bytes(const MulMatOp& o) { return (static_cast<size_t>(o.N) * o.K * 2 + 255) & ~size_t(255); }
 size_t split_bytes(const MulMatOp& o, int splits) {
     if (splits <= 1) return 0;
@@ -549,9 +606,11 @@ size_t split_bytes(const MulMatOp& o, int splits) {
 }  // namespace
 
 bool prefill_supported(const MulMatOp& o) {
-    if ((o.type != kTypeQ4_K && o.type != kTypeQ6_K) || o.N < kPrefillMinN || o.ne2 != 1 || o.ne3 != 1) return false;
+    if ((o.type != kTypeQ4_K && o.type != kTypeQ5_K && o.type != kTypeQ6_K && o.type != kTypeQ8_0) ||
+        o.N < kPrefillMinN || o.ne2 != 1 || o.ne3 != 1)
+        return false;
     if (o.K % 256 != 0 || o.M < 1) return false;
-    const int64_t row_bytes = static_cast<int64_t>(o.K / 256) * (o.type == kTypeQ6_K ? 210 : 144);
+    const int64_t row_bytes = static_cast<int64_t>(o.K / 256) * block_group_bytes(o.type);
     // TMA rows: 16-byte aligned base and row stride (Q6_K: K a multiple of 2048
     // for unpadded rows; other Q6_K shapes take the batched GEMM)
     if ((reinterpret_cast<uintptr_t>(o.w) | static_cast<uintptr_t>(o.w_nb1)) & 15) return false;
@@ -586,13 +645,14 @@ int launch_prefill(const MulMatOp& o, void* workspace, size_t workspace_bytes, c
     const EncodeFn enc = encoder();
     const bool q6 = o.type == kTypeQ6_K;
     {
-        // Q4_K: uint64 words, one 18-word block column per box; Q6_K: bytes, a
+        // Q4_K / Q5_K / Q8_0: uint64 words, one 256-element column per box
+        // (18 / 22 / 34 words); Q6_K: bytes, a
         // 240-byte box from the block's 16-byte-rounded start (the box's end may
         // pass the row's last block: zeros, never read)
-        const cuuint64_t dims[2] = {q6 ? static_cast<cuuint64_t>(o.K / 256) * 210 : static_cast<cuuint64_t>(o.K / 256) * 18,
-                                    static_cast<cuuint64_t>(o.M)};
+        const cuuint64_t group = static_cast<cuuint64_t>(block_group_bytes(o.type));
+        const cuuint64_t dims[2] = {static_cast<cuuint64_t>(o.K / 256) * (q6 ? group : group / 8), static_cast<cuuint64_t>(o.M)};
         const cuuint64_t strides[1] = {static_cast<cuuint64_t>(o.w_nb1)};
-        const cuuint32_t box[2] = {q6 ? static_cast<cuuint32_t>(kQ6Box) : 18u, kTileM};
+        const cuuint32_t box[2] = {q6 ? static_cast<cuuint32_t>(kQ6Box) : static_cast<cuuint32_t>(group / 8), kTileM};
         const cuuint32_t es[2] = {1, 1};
         if (enc(&P.wmap, q6 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, const_cast<uint8_t*>(o.w),
                 dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
@@ -624,14 +684,19 @@ int launch_prefill(const MulMatOp& o, void* workspace, size_t workspace_bytes, c
         const cudaError_t e = cudaMemsetAsync(P.counters, 0, tiles * 4, stream);
         if (e != cudaSuccess) return -static_cast<int>(e);
     }
-    static bool configured[2] = {false, false};
-    void (*const kernel)(PrefillArgs) = q6 ? prefill_kernel<kTypeQ6_K> : prefill_kernel<kTypeQ4_K>;
-    const size_t smem = q6 ? smem_bytes<kTypeQ6_K>() : smem_bytes<kTypeQ4_K>();
-    if (!configured[q6]) {
+    static bool configured[4] = {false, false, false, false};
+    const int ti = o.type == kTypeQ4_K ? 0 : (o.type == kTypeQ5_K ? 1 : (q6 ? 2 : 3));
+    void (*const kernels[4])(PrefillArgs) = {prefill_kernel<kTypeQ4_K>, prefill_kernel<kTypeQ5_K>,
+                                             prefill_kernel<kTypeQ6_K>, prefill_kernel<kTypeQ8_0>};
+    const size_t smems[4] = {smem_bytes<kTypeQ4_K>(), smem_bytes<kTypeQ5_K>(), smem_bytes<kTypeQ6_K>(),
+                             smem_bytes<kTypeQ8_0>()};
+    void (*const kernel)(PrefillArgs) = kernels[ti];
+    const size_t smem = smems[ti];
+    if (!configured[ti]) {
         const cudaError_t e =
             cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
         if (e != cudaSuccess) return -static_cast<int>(e);
-        configured[q6] = true;
+        configured[ti] = true;
     }
     const dim3 grid((o.M + kTileM - 1) / kTileM, (o.N + kTileN - 1) / kTileN, splits);
     kernel<<<grid, kThreads, smem, stream>>>(P);
