@@ -255,9 +255,36 @@ def prefill_measure(dev, reps: int = 10, warmup: int = 3):
     total_us = sum(p["us"] for p in per)
     tflops = total_flop / (total_us * 1e-6) / 1e12
     peak, src = measured_tensor_peak()
+    # every weight type the prefill GEMM takes, on the ffn_down shape
+    M, K = 4096, 14336
+    x = torch.randn(N, K, device=dev, generator=gen)
+    y = torch.empty(N, M, device=dev)
+    per_type = []
+    for tname, t in (("q4_k", jsep.GGML_TYPE_Q4_K), ("q5_k", jsep.GGML_TYPE_Q5_K), ("q6_k", jsep.GGML_TYPE_Q6_K),
+                     ("q8_0", jsep.GGML_TYPE_Q8_0), ("q4_0", jsep.GGML_TYPE_Q4_0)):
+        gen.manual_seed(zlib.crc32(tname.encode()))
+        ws = [synth.weights_torch(gen, t, M, K, dev) for _ in range(2)]
+        torch.cuda.synchronize()
+
+        def one(copy: int):
+            jsep.mul_mat_device(t, ws[copy].data_ptr(), ws[copy].shape[1], x.data_ptr(), K, y.data_ptr(), M, M, K, N,
+                                stream_ptr)
+
+        for w in range(warmup):
+            one(w & 1)
+        with torch.cuda.stream(lib_stream):
+            ev0.record()
+            for r in range(reps):
+                one(r & 1)
+            ev1.record()
+        ev1.synchronize()
+        ms = ev0.elapsed_time(ev1) / reps
+        per_type.append({"type": tname, "shape": f"{M}x{K}", "n": N, "us": round(ms * 1e3, 2),
+                         "tflops": round(2.0 * M * N * K / (ms * 1e-3) / 1e12, 1)})
+        del ws
     return {"workload": "llama-3-8b prefill GEMMs (Q4_K 4096x4096, 1024x4096, 14336x4096, 4096x14336; 512 tokens)",
             "value": round(tflops, 1), "unit": "TFLOP/s", "dtype": "f16 x f16 -> f32 (tcgen05)",
-            "per_shape": per,
+            "per_shape": per, "per_type": per_type,
             "roofline": {"bound": "tensor", "achieved": round(tflops, 1), "peak": peak, "unit": "TFLOP/s",
                          "frac": round(tflops / peak, 4), "peak_source": src,
                          "note": "time includes the f32->f16 activation pre-pass of each MUL_MAT"}}

@@ -1,4 +1,4 @@
-"""GPU parity tests of the prefill path: Q4_K, Q5_K, Q6_K and Q8_0 MUL_MAT with
+"""GPU parity tests of the prefill path: Q4_K, Q5_K, Q6_K, Q8_0 and Q4_0 MUL_MAT with
 N > 64 vectors runs as a tcgen05 tensor-core GEMM (f16 dequantized weights and
 activations, f32 accumulation). Q6_K takes it when its rows are a multiple of
 16 bytes (K a multiple of 2048), as the tensor-memory copies need.
@@ -151,8 +151,10 @@ def test_prefill_q6k_shapes_vs_torch_fp32(runtime, M, K, N):
     (O.TYPE_Q5_K, 200, 2048, 130),    # partial row and vector tiles
     (O.TYPE_Q8_0, 128, 256, 128),     # one 8-block group
     (O.TYPE_Q8_0, 333, 2304, 300),    # Gemma-2-2B hidden: 9 groups; partial tiles
+    (O.TYPE_Q4_0, 128, 256, 65),
+    (O.TYPE_Q4_0, 260, 2304, 200),
 ])
-def test_prefill_q5k_q8_0_matches_oracle(runtime, qtype, M, K, N):
+def test_prefill_other_types_matches_oracle(runtime, qtype, M, K, N):
     rng = np.random.default_rng(3000 + qtype + M + K + N)
     w = synth.weights(rng, qtype, M, K)
     x = synth.activations(rng, N, K)
@@ -163,10 +165,11 @@ def test_prefill_q5k_q8_0_matches_oracle(runtime, qtype, M, K, N):
 
 
 @pytest.mark.parametrize("qtype,M,K,N", [(O.TYPE_Q8_0, 9216, 2304, 512), (O.TYPE_Q8_0, 2304, 9216, 256),
-                                         (O.TYPE_Q5_K, 14336, 4096, 512), (O.TYPE_Q5_K, 4096, 14336, 200)])
-def test_prefill_q5k_q8_0_shapes_vs_torch_fp32(runtime, qtype, M, K, N):
+                                         (O.TYPE_Q5_K, 14336, 4096, 512), (O.TYPE_Q5_K, 4096, 14336, 200),
+                                         (O.TYPE_Q4_0, 14336, 4096, 512), (O.TYPE_Q4_0, 4096, 14336, 128)])
+def test_prefill_other_types_shapes_vs_torch_fp32(runtime, qtype, M, K, N):
     """Gemma-2-2B ffn_up / ffn_down (Q8_0) and Llama-3-8B ffn_gate / ffn_down
-    (Q5_K) in prefill."""
+    (Q5_K, Q4_0) in prefill."""
     import torch
 
     dev = torch.device("cuda", 0)

@@ -1,5 +1,5 @@
 // Prefill-regime quantized MUL_MAT (N >= kPrefillMinN activation vectors, Q4_K,
-// Q5_K, Q6_K or Q8_0 weights): a tcgen05 tensor-core GEMM that dequantizes the GGUF blocks
+// Q5_K, Q6_K, Q8_0 or Q4_0 weights): a tcgen05 tensor-core GEMM that dequantizes the GGUF blocks
 // to f16 on the way into tensor memory.
 //
 //   y[m + M n] = sum_k W[m, k] x[k + K n]   (ggml MUL_MAT, matmul.ts:10-17)
@@ -67,7 +67,8 @@ __host__ __device__ constexpr int raw_row_bytes() {
     return TYPE == kTypeQ6_K ? kQ6Box : (TYPE == kTypeQ5_K ? 176 : (TYPE == kTypeQ8_0 ? 272 : 144));
 }
 // one box row per 256 elements: Q4_K 144 B, Q5_K 176 B, Q8_0 272 B (8 blocks),
-// Q6_K 240 B; all rows 16-byte multiples with conflict-free 16-byte loads
+// Q4_0 144 B (8 blocks), Q6_K 240 B; all rows 16-byte multiples with
+// conflict-free 16-byte loads
 template <int TYPE>
 __host__ __device__ constexpr int raw_bytes() { return kTileM * raw_row_bytes<TYPE>(); }
 constexpr int kBBytes = kTileN * kChunkK * 2;    // 32768
@@ -353,6 +354,47 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
                         if (p == 3) mbar_arrive(&raw_free[rs]);
                     }
                 }
+            } else if constexpr (TYPE == kTypeQ4_0) {
+                // Q4_0: 8 blocks of 18 B (f16 d, 16 bytes of nibbles: elements
+                // 0..15 low, 16..31 high) per 256 elements; this thread's 16
+                // quants of chunk p are the low (qq = 0) or high nibbles of block
+                // 2p + h, w = d (q - 8). The 16 bytes start 2 (2p + h) + 2 bytes
+                // past a 16-byte boundary (warp-uniform)
+                const uint8_t* rowp = raw + rs * kRawBytes + r * 144;
+                const __half2 k1032 = __float2half2_rn(1032.f);
+#pragma unroll
+                for (int p = 0; p < 4; ++p, ++q) {
+                    const int s = q % kStages;
+                    if (q >= kStages && !mbar_wait(&st_free[s], ((q / kStages) - 1) & 1, 3u, poisoned)) {
+                        stop = true;
+                        break;
+                    }
+                    const int bo = 18 * (2 * p + h), a = bo + 2, o = a & 15;
+                    const __half2 d2 = __half2half2(*reinterpret_cast<const __half*>(rowp + bo));
+                    const uint4 v0 = q6_load16(rowp, a & ~15, o >> 2, 8u * static_cast<uint32_t>(o & 3));
+                    const uint32_t wv[4] = {v0.x, v0.y, v0.z, v0.w};
+                    uint32_t out[8];  // 16 f16, element order l = 0..15
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        // f16 1024 + q (exact), minus 1032: q - 8 exactly
+                        const uint32_t nib = (wv[i] >> (4 * qq)) & 0x0F0F0F0Fu;
+                        const uint32_t e01 = __byte_perm(nib, 0x00006464u, 0x5140u);
+                        const uint32_t e23 = __byte_perm(nib, 0x00006464u, 0x5342u);
+                        const __half2 q01 = __hsub2(*reinterpret_cast<const __half2*>(&e01), k1032);
+                        const __half2 q23 = __hsub2(*reinterpret_cast<const __half2*>(&e23), k1032);
+                        const __half2 w01 = __hmul2(q01, d2), w23 = __hmul2(q23, d2);
+                        out[2 * i] = *reinterpret_cast<const uint32_t*>(&w01);
+                        out[2 * i + 1] = *reinterpret_cast<const uint32_t*>(&w23);
+                    }
+                    tmem_st8(trow + static_cast<uint32_t>(kTileN + s * kACols + 16 * h + 8 * qq), out);
+                    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) {
+                        mbar_arrive(&a_full[s]);
+                        if (p == 3) mbar_arrive(&raw_free[rs]);
+                    }
+                }
             } else if constexpr (TYPE == kTypeQ8_0) {
                 // Q8_0: 8 blocks of 34 B (f16 d, 32 int8) per 256 elements; this
                 // thread's 16 quants of chunk p are bytes 16qq .. +15 of block
@@ -591,7 +633,7 @@ int plan_splits(const MulMatOp& o) {
     return best;
 }
 
-// Bytes of 256 elements of a row: Q4_K 144, Q5_K 176, Q6_K 210, Q8_0 272.
+// Bytes of 256 elements of a row: Q4_K 144, Q5_K 176, Q6_K 210, Q8_0 272, Q4_0 144.
 int block_group_bytes(int type) {
     return type == kTypeQ6_K ? 210 : (type == kTypeQ5_K ? 176 : (type == kTypeQ8_0 ? 272 : 144));
 }
@@ -606,7 +648,8 @@ size_t split_bytes(const MulMatOp& o, int splits) {
 }  // namespace
 
 bool prefill_supported(const MulMatOp& o) {
-    if ((o.type != kTypeQ4_K && o.type != kTypeQ5_K && o.type != kTypeQ6_K && o.type != kTypeQ8_0) ||
+    if ((o.type != kTypeQ4_K && o.type != kTypeQ5_K && o.type != kTypeQ6_K && o.type != kTypeQ8_0 &&
+         o.type != kTypeQ4_0) ||
         o.N < kPrefillMinN || o.ne2 != 1 || o.ne3 != 1)
         return false;
     if (o.K % 256 != 0 || o.M < 1) return false;
@@ -645,8 +688,8 @@ int launch_prefill(const MulMatOp& o, void* workspace, size_t workspace_bytes, c
     const EncodeFn enc = encoder();
     const bool q6 = o.type == kTypeQ6_K;
     {
-        // Q4_K / Q5_K / Q8_0: uint64 words, one 256-element column per box
-        // (18 / 22 / 34 words); Q6_K: bytes, a
+        // Q4_K / Q5_K / Q8_0 / Q4_0: uint64 words, one 256-element column per
+        // box (18 / 22 / 34 / 18 words); Q6_K: bytes, a
         // 240-byte box from the block's 16-byte-rounded start (the box's end may
         // pass the row's last block: zeros, never read)
         const cuuint64_t group = static_cast<cuuint64_t>(block_group_bytes(o.type));
@@ -684,12 +727,13 @@ int launch_prefill(const MulMatOp& o, void* workspace, size_t workspace_bytes, c
         const cudaError_t e = cudaMemsetAsync(P.counters, 0, tiles * 4, stream);
         if (e != cudaSuccess) return -static_cast<int>(e);
     }
-    static bool configured[4] = {false, false, false, false};
-    const int ti = o.type == kTypeQ4_K ? 0 : (o.type == kTypeQ5_K ? 1 : (q6 ? 2 : 3));
-    void (*const kernels[4])(PrefillArgs) = {prefill_kernel<kTypeQ4_K>, prefill_kernel<kTypeQ5_K>,
-                                             prefill_kernel<kTypeQ6_K>, prefill_kernel<kTypeQ8_0>};
-    const size_t smems[4] = {smem_bytes<kTypeQ4_K>(), smem_bytes<kTypeQ5_K>(), smem_bytes<kTypeQ6_K>(),
-                             smem_bytes<kTypeQ8_0>()};
+    static bool configured[5] = {false, false, false, false, false};
+    const int ti = o.type == kTypeQ4_K ? 0 : (o.type == kTypeQ5_K ? 1 : (q6 ? 2 : (o.type == kTypeQ8_0 ? 3 : 4)));
+    void (*const kernels[5])(PrefillArgs) = {prefill_kernel<kTypeQ4_K>, prefill_kernel<kTypeQ5_K>,
+                                             prefill_kernel<kTypeQ6_K>, prefill_kernel<kTypeQ8_0>,
+                                             prefill_kernel<kTypeQ4_0>};
+    const size_t smems[5] = {smem_bytes<kTypeQ4_K>(), smem_bytes<kTypeQ5_K>(), smem_bytes<kTypeQ6_K>(),
+                             smem_bytes<kTypeQ8_0>(), smem_bytes<kTypeQ4_0>()};
     void (*const kernel)(PrefillArgs) = kernels[ti];
     const size_t smem = smems[ti];
     if (!configured[ti]) {

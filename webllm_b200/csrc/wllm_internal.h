@@ -102,7 +102,7 @@ int launch_tp_wait(const TpLaunch& tp, cudaStream_t stream);
 // Error code recorded by a bounded wait that timed out (0 = none); clears it.
 unsigned read_and_clear_stream_error();
 
-// Prefill GEMM (mulmat_prefill.cu): Q4_K, Q5_K and Q8_0 weights, or Q6_K with
+// Prefill GEMM (mulmat_prefill.cu): Q4_K, Q5_K, Q8_0 and Q4_0 weights, or Q6_K with
 // 16-byte multiple rows, with N >= kPrefillMinN vectors on tcgen05 tensor cores (f16 operands, f32 accumulation). The
 // activations are first converted to f16 into caller-provided workspace of
 // prefill_workspace_bytes(op) bytes (256-byte aligned). Returns the number of
