@@ -43,6 +43,14 @@ import numpy as np  # noqa: E402
 
 METRIC = "quantized MUL_MAT GB/s & % HBM peak (decode); prefill TFLOPS; at 1/2/4/8 GPU"
 WORKLOAD = "llama-3.2-3b decode sweep (28 layers x 7 GEMVs, Q4_K/Q6_K x f32, batch 1)"
+# --model qwen3-8b: the row-sharded decode of the multi-GPU configuration
+# (Qwen3-8B, 36 layers x 7 Q4_K GEMVs, hidden 4096, FFN 12288; its 151936 x
+# 4096 output projection is not in the step)
+WORKLOADS = {
+    "llama-3.2-3b": (WORKLOAD, 28),
+    "qwen3-8b": ("qwen3-8b decode sweep (36 layers x 7 GEMVs, Q4_K x f32, batch 1; output projection excluded)", 36),
+}
+_MODEL = "llama-3.2-3b"
 # DRAM bytes (read + write) of one layer's four GEMV launches, summed from an
 # ncu capture of this workload (profiles/stream_gemv_llama32_3b_decode.md);
 # the algorithmic bytes are 64,139,264 per layer.
@@ -56,7 +64,9 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
-    ap.add_argument("--layers", type=int, default=28)
+    ap.add_argument("--model", choices=sorted(WORKLOADS), default="llama-3.2-3b",
+                    help="decode sweep shapes (default: the single-GPU headline workload)")
+    ap.add_argument("--layers", type=int, default=None, help="layers per step (default: the model's)")
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU-baseline sample budget")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-prefill", action="store_true", help="skip the prefill GEMM measurement")
@@ -355,23 +365,29 @@ def batched_measure(dev, reps: int = 10, warmup: int = 3):
     return res
 
 
-def layer_groups():
-    """[(input K, [(name, qtype, M, K), ...]), ...] for one layer."""
+def layer_table():
+    """The 7 GEMVs of one decode layer of the selected model: [(name, qtype, M, K)]."""
     from webllm_b200 import synth
 
-    L = {n: (n, t, M, K) for n, t, M, K in synth.LLAMA32_3B_LAYER}
+    return synth.QWEN3_8B_LAYER if _MODEL == "qwen3-8b" else synth.LLAMA32_3B_LAYER
+
+
+def layer_groups():
+    """[(input K, [(name, qtype, M, K), ...]), ...] for one layer: the launch
+    groups that share an input (q|k|v, o, gate|up, down)."""
+    L = {n: (n, t, M, K) for n, t, M, K in layer_table()}
     return [
-        (3072, [L["attn_q"], L["attn_k"], L["attn_v"]]),
-        (3072, [L["attn_output"]]),
-        (3072, [L["ffn_gate"], L["ffn_up"]]),
-        (8192, [L["ffn_down"]]),
+        (L["attn_q"][3], [L["attn_q"], L["attn_k"], L["attn_v"]]),
+        (L["attn_output"][3], [L["attn_output"]]),
+        (L["ffn_gate"][3], [L["ffn_gate"], L["ffn_up"]]),
+        (L["ffn_down"][3], [L["ffn_down"]]),
     ]
 
 
 def step_bytes(layers: int) -> int:
     from webllm_b200 import synth
 
-    return layers * sum(synth.algorithmic_bytes(t, M, K, 1) for _, t, M, K in synth.LLAMA32_3B_LAYER)
+    return layers * sum(synth.algorithmic_bytes(t, M, K, 1) for _, t, M, K in layer_table())
 
 
 class ClockSampler:
@@ -436,7 +452,7 @@ def cpu_layers(n: int):
 
     rng = np.random.default_rng(1234)
     return [[(t, synth.weights(rng, t, M, K), synth.activations(rng, 1, K), synth.algorithmic_bytes(t, M, K, 1))
-             for _, t, M, K in synth.LLAMA32_3B_LAYER] for _ in range(n)]
+             for _, t, M, K in layer_table()] for _ in range(n)]
 
 
 def cpu_sample(layers_budget_s: float, threads: int | None = None):
@@ -485,14 +501,14 @@ def run_reference(args, rank: int):
         one_step()
     el = time.perf_counter() - t0
     gbs = layer_bytes * args.steps / el / 1e9
-    sample = (f"each step: 1 of the 28 layers (7 GEMVs, {layer_bytes/1e6:.1f} MB of algorithmic bytes), cycling "
+    sample = (f"each step: 1 of the {WORKLOADS[_MODEL][1]} layers (7 GEMVs, {layer_bytes/1e6:.1f} MB of algorithmic bytes), cycling "
               f"over {len(layers)} distinct layers (513 MB) so weights stream from DRAM; f32 dequant-then-dot "
               f"oracle (the reference's llama.cpp CPU kernels are not vendored in the reference repository)")
     line = {
         "impl": "reference", "metric": METRIC, "value": round(gbs, 3), "unit": "GB/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(el / args.steps * 1e3, 3),
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": WORKLOAD, "batch": 1, "layers_per_step": 1},
+        "config": {"workload": WORKLOADS[_MODEL][0], "batch": 1, "layers_per_step": 1},
         "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": cores, "kind": "port", "sample": sample},
         "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -692,14 +708,14 @@ def run_b200(args, rank: int, world: int, local_rank: int):
             "metric": METRIC, "value": round(gbs, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(dev_ms, 4), "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": WORKLOAD, "layers": layers, "batch": 1, "bytes_per_step": total_bytes,
-                       "l2": "inputs larger than L2 (1.80 GB of distinct weights per step), no flush",
+            "config": {"workload": WORKLOADS[_MODEL][0], "layers": layers, "batch": 1, "bytes_per_step": total_bytes,
+                       "l2": f"inputs larger than L2 ({total_bytes / 1e9:.2f} GB of distinct weights per step), no flush",
                        "parallelism": f"tp{world} row-sharded" + (" + NVLink peer-write gather fused into the GEMV"
                                                                       if world > 1 else ""),
                        "launch": "4 grouped launches per layer, one CUDA graph per step"},
             "roofline": {"bound": "hbm", "achieved": round(gbs, 2), "peak": peak, "unit": "GB/s",
                          "frac": round(gbs / peak, 4),
-                         "traffic": NCU_DRAM_BYTES_PER_LAYER * layers if world == 1 else None,
+                         "traffic": NCU_DRAM_BYTES_PER_LAYER * layers if world == 1 and _MODEL == "llama-3.2-3b" else None,
                          "traffic_note": "ncu dram__bytes_read.sum + dram__bytes_write.sum of the step's GEMV launches",
                          "peak_source": f"{peak_src} hbm_gbs (burst copy)",
                          "note": "achieved = step algorithmic bytes / step device time over all launches of the GEMV kernel"
@@ -814,7 +830,11 @@ def jsep_path_e2e(args, layers: int):
 
 
 def main():
+    global _MODEL
     args = parse_args()
+    _MODEL = args.model
+    if args.layers is None:
+        args.layers = WORKLOADS[_MODEL][1]
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
