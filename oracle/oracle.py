@@ -148,3 +148,49 @@ def rel_error(y: np.ndarray, r: np.ndarray) -> float:
     if denom == 0.0:
         return float(np.max(np.abs(y - r))) if r.size else 0.0
     return float(np.max(np.abs(y - r)) / denom)
+
+
+# ---- the activation-side ops fused into the GEMV (float64 restatements) ----
+
+
+def rms_norm_f64(x: np.ndarray, eps: float, gain: np.ndarray | None = None) -> np.ndarray:
+    """RMS_NORM per vector (last axis), then the gain MUL when given:
+    x / sqrt(mean(x^2) + eps) * gain, in float64.
+
+    Follows src/inference/jsep/ops/rms-norm.ts:14-15,61-67 (the op) and the
+    CPU reference of tests/jsep-rms-norm-golden.test.ts:64-86 (cpuRmsNorm:
+    sum of squares over the row, 1 / sqrt(sum / cols + eps), times x); the
+    gain is the separate MUL of src/inference/model-inference.ts:2281,2478-2481.
+    """
+    xd = np.asarray(x, dtype=np.float64)
+    y = xd * (1.0 / np.sqrt((xd * xd).mean(axis=-1, keepdims=True) + eps))
+    if gain is not None:
+        y = y * np.asarray(gain, dtype=np.float64)
+    return y
+
+
+def swiglu_f64(gate: np.ndarray, up: np.ndarray) -> np.ndarray:
+    """silu(gate) * up in float64: gate / (1 + e^-gate) * up, the SwiGLU the
+    reference applies between the FFN's gate/up and down projections
+    (src/inference/model-inference.ts:2484-2489, op_swiglu_split of
+    src/wasm/webgpu-bridge.cpp:272-275; ggml's scalar CPU form)."""
+    g = np.asarray(gate, dtype=np.float64)
+    with np.errstate(over="ignore"):
+        return g / (1.0 + np.exp(-g)) * np.asarray(up, dtype=np.float64)
+
+
+def gelu_ggml(gate: np.ndarray) -> np.ndarray:
+    """GELU as ggml's CPU backend computes it with its f16 table: the input
+    rounded to f16, the tanh form 0.5 f (1 + tanh(sqrt(2/pi) f (1 + 0.044715
+    f^2))), the result rounded to f16; 0 at gate <= -10 and gate itself at
+    gate >= 10. Returned as float64 (src/inference/model-inference.ts:
+    2486-2487, Gemma's GELU(gate) before the MUL by up)."""
+    g = np.asarray(gate, dtype=np.float32)
+    f = g.astype(np.float16).astype(np.float64)
+    t = (0.5 * f * (1.0 + np.tanh(0.7978845608028654 * f * (1.0 + 0.044715 * f * f)))).astype(np.float16)
+    return np.where(g <= -10.0, 0.0, np.where(g >= 10.0, g.astype(np.float64), t.astype(np.float64)))
+
+
+def geglu_f64(gate: np.ndarray, up: np.ndarray) -> np.ndarray:
+    """gelu_ggml(gate) * up in float64 (the Gemma FFN's MUL)."""
+    return gelu_ggml(gate) * np.asarray(up, dtype=np.float64)

@@ -242,10 +242,7 @@ def test_fused_rms_norm_vs_torch_fp64(runtime, group, N, with_gain):
     rc = jsep.mul_mat_rms_norm_batch(ops, gain.data_ptr() if with_gain else 0, eps, stream)
     assert rc == jsep.STATUS_OK
     runtime.jsep_sync()
-    xd = x0.double()
-    xn = xd / torch.sqrt((xd * xd).mean(dim=1, keepdim=True) + eps)
-    if with_gain:
-        xn = xn * gain.double()
+    xn = torch.from_numpy(O.rms_norm_f64(x0.cpu().numpy(), eps, gain.cpu().numpy() if with_gain else None)).to(dev)
     for (t, M), w, y in zip(mats, ws, ys):
         wf = torch.empty(M, K, device=dev)
         jsep.dequantize_device(t, w.data_ptr(), wf.data_ptr(), M * K, stream)
@@ -254,6 +251,34 @@ def test_fused_rms_norm_vs_torch_fp64(runtime, group, N, with_gain):
         rel = ((y.double() - ref).abs().max() / ref.abs().max()).item()
         assert rel <= GEMV_TOL, (t, M, rel)
     assert torch.equal(x, x0)
+
+
+def test_fused_rms_norm_reference_golden_input(runtime):
+    """The reference's RMS_NORM golden case 1 x 2048, eps 1e-5
+    (tests/jsep-rms-norm-golden.test.ts:129,182-184: x[i] = ((i * 7) % 31) *
+    0.05 - 0.7), fused into a Q4_K projection: against the oracle's norm, then
+    a float64 matmul of the device-dequantized weights."""
+    import torch
+
+    K, M, eps = 2048, 512, 1e-5
+    dev = torch.device("cuda", 0)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(21)
+    i = np.arange(K)
+    xh = (((i * 7) % 31) * 0.05 - 0.7).astype(np.float32)[None, :]
+    x = torch.from_numpy(xh).to(dev)
+    w = synth.weights_torch(gen, jsep.GGML_TYPE_Q4_K, M, K, dev)
+    y = torch.empty(1, M, device=dev)
+    torch.cuda.synchronize()
+    stream = jsep.library_stream()
+    op = jsep.MulMatArgs(jsep.GGML_TYPE_Q4_K, M, K, 1, w.data_ptr(), w.shape[1], x.data_ptr(), K, y.data_ptr(), M)
+    assert jsep.mul_mat_rms_norm_batch([op], 0, eps, stream) == jsep.STATUS_OK
+    wf = torch.empty(M, K, device=dev)
+    jsep.dequantize_device(jsep.GGML_TYPE_Q4_K, w.data_ptr(), wf.data_ptr(), M * K, stream)
+    runtime.jsep_sync()
+    ref = (wf.double() @ torch.from_numpy(O.rms_norm_f64(xh, eps)).to(dev).t()).t()
+    rel = ((y.double() - ref).abs().max() / ref.abs().max()).item()
+    assert rel <= GEMV_TOL, rel
 
 
 def test_fused_rms_norm_outside_decode_is_not_implemented(runtime):
@@ -286,18 +311,13 @@ FUSED_GLU_GROUPS = {
 
 
 def glu_fp64(gate, up, glu):
-    """act(gate) * up in float64: silu, or ggml's CPU GELU (tanh form with its
-    input and output rounded to f16; 0 at gate <= -10, gate at gate >= 10)."""
+    """act(gate) * up in float64 from the oracle: silu, or ggml's CPU GELU
+    (tanh form with its input and output rounded to f16; 0 at gate <= -10,
+    gate at gate >= 10)."""
     import torch
 
-    g = gate.double()
-    if glu == jsep.GLU_SWIGLU:
-        a = g / (1.0 + torch.exp(-g))
-    else:
-        h = gate.half().double()
-        t = 0.5 * h * (1.0 + torch.tanh(0.7978845608028654 * h * (1.0 + 0.044715 * h * h)))
-        a = torch.where(g <= -10.0, torch.zeros_like(g), torch.where(g >= 10.0, g, t.half().double()))
-    return a * up.double()
+    fn = O.swiglu_f64 if glu == jsep.GLU_SWIGLU else O.geglu_f64
+    return torch.from_numpy(fn(gate.cpu().numpy(), up.cpu().numpy())).to(gate.device)
 
 
 @pytest.mark.parametrize("N", [1, 2, 3])

@@ -115,3 +115,52 @@ def test_synth_distributions():
     assert synth.algorithmic_bytes(synth.Q4_K, 4096, 4096, 1) == 9_469_952
     layer = sum(synth.algorithmic_bytes(t, M, K, 1) for _, t, M, K in synth.LLAMA32_3B_LAYER)
     assert layer == 64_139_264
+
+
+def rms_norm_golden_input(n: int) -> np.ndarray:
+    """The reference's RMS_NORM golden input: x[i] = ((i * 7) % 31) * 0.05 - 0.7
+    (tests/jsep-rms-norm-golden.test.ts:129), as f32."""
+    i = np.arange(n)
+    return (((i * 7) % 31) * 0.05 - 0.7).astype(np.float32)
+
+
+@pytest.mark.parametrize("cols,eps", [(2048, 1e-5), (64, 1e-6)])
+def test_rms_norm_matches_reference_golden(cols, eps):
+    """The reference's two RMS_NORM golden cases (1 x 2048, eps 1e-5; 1 x 64,
+    eps 1e-6; tests/jsep-rms-norm-golden.test.ts:182-188), against its CPU
+    reference written out as a per-element loop in f64 (cpuRmsNorm, :64-86),
+    at its tolerance 1e-4 (max abs)."""
+    x = rms_norm_golden_input(cols)
+    sum_sq = 0.0
+    for v in x.tolist():
+        sum_sq += v * v
+    inv = 1.0 / float(np.sqrt(sum_sq / cols + eps))
+    ref = np.array([v * inv for v in x.tolist()], dtype=np.float32)
+    got = O.rms_norm_f64(x[None, :], eps)[0]
+    assert np.max(np.abs(got - ref)) < 1e-4
+    # rows are independent, and the gain multiplies after the norm
+    two = np.stack([x, 3.0 * x])
+    g = np.linspace(0.5, 1.5, cols)
+    out = O.rms_norm_f64(two, eps, g)
+    assert np.allclose(out[0], O.rms_norm_f64(x, eps) * g)
+    assert np.allclose(out[1], O.rms_norm_f64(3.0 * x, eps) * g)
+
+
+def test_glu_restatements():
+    """SwiGLU: silu(g) * u with silu(0) = 0 and silu(g) -> g for large g.
+    GELU (ggml's f16-table form): the clamps at +-10, exact f16 values
+    elsewhere, and the tanh form within f16 rounding."""
+    g = np.array([-50.0, -10.0, -9.99, -1.0, 0.0, 0.5, 3.0, 9.99, 10.0, 40.0], dtype=np.float32)
+    u = np.linspace(-2.0, 2.0, g.size).astype(np.float32)
+    s = O.swiglu_f64(g, u)
+    assert s[4] == 0.0 and abs(s[-1] - 40.0 * u[-1]) < 1e-9 and abs(s[0]) < 1e-15
+    gd = g.astype(np.float64)
+    assert np.allclose(s, gd / (1.0 + np.exp(-gd)) * u)
+    e = O.gelu_ggml(g)
+    assert e[0] == 0.0 and e[1] == 0.0 and e[8] == 10.0 and e[9] == 40.0
+    inner = e[2:8]
+    assert np.array_equal(inner, inner.astype(np.float16).astype(np.float64))  # f16 values
+    f = gd[2:8]
+    exact = 0.5 * f * (1.0 + np.tanh(np.sqrt(2.0 / np.pi) * f * (1.0 + 0.044715 * f * f)))
+    assert np.allclose(inner, exact, rtol=2e-3, atol=1e-3)
+    assert np.allclose(O.geglu_f64(g, u), e * u)
