@@ -259,7 +259,8 @@ int32_t wllm_graph_destroy(int32_t graph);
 
 /* Prefill MUL_MAT that allocates nothing: the same arguments and result as
  * wllm_mul_mat for the prefill path (Q4_K, Q5_K, Q8_0 or Q4_0 weights, or Q6_K with
- * K a multiple of 2048; N >= 65 vectors, 16-byte aligned rows and activations), with the f16 activation workspace
+ * rows of a multiple of 16 bytes, or of 8 with M even; N >= 65 vectors, 16-byte
+ * aligned weights and activations), with the f16 activation workspace
  * in a fixed 16 MiB device array of the library instead of library-allocated
  * memory: N * K * 2 + 256 bytes must fit, otherwise WLLM_STATUS_FAILED with
  * the sizes in wllm_last_error(). No cudaMalloc or cudaFree happens. The

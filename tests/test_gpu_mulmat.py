@@ -403,12 +403,12 @@ def test_fused_glu_rejects_bad_arguments(runtime):
 @pytest.mark.parametrize("N", [65, 200])
 def test_q6k_prefill_sizes_vs_torch_fp64(runtime, N):
     """Q6_K with more than 64 vectors (prefill; several 32-vector tiles) whose
-    2520-byte rows are not a multiple of 16 bytes, so the tensor-memory copies
-    of the tcgen05 path cannot take them: the batched GEMM, at the GEMV bar.
-    Llama-3.2-3B attn_v 1024 x 3072."""
+    1890-byte rows are neither a multiple of 16 bytes nor of 8, so the
+    tensor-memory copies of the tcgen05 path cannot take them: the batched
+    GEMM, at the GEMV bar. 1024 x 2304."""
     import torch
 
-    M, K = 1024, 3072
+    M, K = 1024, 2304
     dev = torch.device("cuda", 0)
     gen = torch.Generator(device=dev)
     gen.manual_seed(N)

@@ -1,7 +1,8 @@
 """GPU parity tests of the prefill path: Q4_K, Q5_K, Q6_K, Q8_0 and Q4_0 MUL_MAT with
 N > 64 vectors runs as a tcgen05 tensor-core GEMM (f16 dequantized weights and
 activations, f32 accumulation). Q6_K takes it when its rows are a multiple of
-16 bytes (K a multiple of 2048), as the tensor-memory copies need.
+16 bytes (K a multiple of 2048), as the tensor-memory copies need, or of 8
+bytes with M even (K = 3072: rows copied in pairs).
 
 Bar: max relative error <= 2e-2 (rel = max|y - r| / max|r|) against
  - the oracle's f64 dequant-then-dot (small and ragged shapes), and
@@ -189,3 +190,29 @@ def test_prefill_other_types_shapes_vs_torch_fp32(runtime, qtype, M, K, N):
     ref = (x.double() @ wf.double().t()).float()
     rel = ((y - ref).abs().max() / ref.abs().max()).item()
     assert rel <= PREFILL_TOL, rel
+
+
+@pytest.mark.parametrize("M,K,N", [
+    (1024, 3072, 65),    # Llama-3.2-3B attn_v: 2520-byte rows, copied as pairs
+    (1000, 3072, 130),   # partial row tile (M even)
+    (3072, 1024, 300),   # 840-byte rows
+])
+def test_prefill_q6k_row_pairs_matches_oracle(runtime, M, K, N):
+    rng = np.random.default_rng(4000 + M + K + N)
+    w = synth.weights(rng, O.TYPE_Q6_K, M, K)
+    x = synth.activations(rng, N, K)
+    k0 = counters().kernels_launched
+    y = run_mul_mat(runtime, O.TYPE_Q6_K, w, x)
+    assert counters().kernels_launched - k0 == 2, "expected the f16 pre-pass and the tensor-core GEMM"
+    assert O.rel_error(y, O.mul_mat_f64(O.TYPE_Q6_K, w, x)) <= PREFILL_TOL
+
+
+def test_prefill_q6k_odd_rows_take_the_batched_gemm(runtime):
+    """M odd with 2520-byte rows: no row pairs, so the batched GEMM runs it, at
+    the GEMV bar."""
+    rng = np.random.default_rng(4100)
+    M, K, N = 333, 3072, 70
+    w = synth.weights(rng, O.TYPE_Q6_K, M, K)
+    x = synth.activations(rng, N, K)
+    y = run_mul_mat(runtime, O.TYPE_Q6_K, w, x)
+    assert O.rel_error(y, O.mul_mat_f64(O.TYPE_Q6_K, w, x)) <= 1e-3

@@ -92,6 +92,11 @@ struct PrefillArgs {
     // writes its f32 tile to partial[tile][z][col][row], and the tile's last CTA
     // (counted in counters[tile], zero at launch) sums the splits in order
     int32_t splits, kb_split;
+    // Q6_K rows of 8 mod 16 bytes (K = 3072: 2520 B): the map is over row
+    // pairs (2 w_nb1 bytes, a legal stride), and each block takes two boxes of
+    // 64 pairs, the even rows' bytes and the odd rows' (w_nb1 further on)
+    int32_t q6_pairs;
+    int32_t w_nb1;
     float* partial;
     unsigned* counters;
 };
@@ -261,7 +266,13 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
                     // x: uint64 words per 256 elements (Q4_K 18, Q5_K 22, Q8_0 34);
                     // Q6_K in bytes, the block's start rounded down to 16
                     const int x = TYPE == kTypeQ6_K ? ((kb0 + kb) * 210) & ~15 : (kb0 + kb) * (raw_row_bytes<TYPE>() / 8);
-                    tma_2d(raw + r * kRawBytes, &P.wmap, x, m0, &raw_full[r]);
+                    if (TYPE == kTypeQ6_K && P.q6_pairs) {
+                        const int xo = ((kb0 + kb) * 210 + P.w_nb1) & ~15;
+                        tma_2d(raw + r * kRawBytes, &P.wmap, x, m0 / 2, &raw_full[r]);
+                        tma_2d(raw + r * kRawBytes + (kTileM / 2) * kQ6Box, &P.wmap, xo, m0 / 2, &raw_full[r]);
+                    } else {
+                        tma_2d(raw + r * kRawBytes, &P.wmap, x, m0, &raw_full[r]);
+                    }
                 }
                 const int s = q % kStages;
                 if (q >= kStages && !mbar_wait(&st_free[s], ((q / kStages) - 1) & 1, 1u, poisoned)) break;
@@ -310,8 +321,12 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
                 // j = 2 (p%2) + h: ql byte 64 (p/2) + 32 h + 16 qq + l (high nibble when
                 // p is odd), qh byte 128 + 32 (p/2) + 16 qq + l shifted by 2 j, scale
                 // 192 + 8 (p/2) + 2 j + qq; w = d sc (q - 32)
-                const int o = ((kb0 + kb) * 210) & 15;
-                const uint8_t* rowp = raw + rs * kRawBytes + r * kQ6Box;
+                // row pairs: odd rows are in the second box, w_nb1 bytes on (their
+                // offset differs from the even rows': per thread, not per warp)
+                const bool odd = P.q6_pairs && (r & 1);
+                const int o = ((kb0 + kb) * 210 + (odd ? P.w_nb1 : 0)) & 15;
+                const uint8_t* rowp =
+                    raw + rs * kRawBytes + (P.q6_pairs ? (odd ? kTileM / 2 : 0) + (r >> 1) : r) * kQ6Box;
                 const int q4 = o >> 2;
                 const uint32_t sh = 8u * static_cast<uint32_t>(o & 3);
                 const float d = __half2float(*reinterpret_cast<const __half*>(rowp + o + 208));
@@ -633,6 +648,11 @@ int plan_splits(const MulMatOp& o) {
     return best;
 }
 
+// Whether a Q6_K op's rows are copied as pairs: 8 mod 16 bytes apart, M even.
+bool q6_row_pairs(const MulMatOp& o) {
+    return o.type == kTypeQ6_K && (o.w_nb1 & 15) == 8 && o.M % 2 == 0 && o.w_nb1 < (int64_t(1) << 30);
+}
+
 // Bytes of 256 elements of a row: Q4_K 144, Q5_K 176, Q6_K 210, Q8_0 272, Q4_0 144.
 int block_group_bytes(int type) {
     return type == kTypeQ6_K ? 210 : (type == kTypeQ5_K ? 176 : (type == kTypeQ8_0 ? 272 : 144));
@@ -654,9 +674,11 @@ bool prefill_supported(const MulMatOp& o) {
         return false;
     if (o.K % 256 != 0 || o.M < 1) return false;
     const int64_t row_bytes = static_cast<int64_t>(o.K / 256) * block_group_bytes(o.type);
-    // TMA rows: 16-byte aligned base and row stride (Q6_K: K a multiple of 2048
-    // for unpadded rows; other Q6_K shapes take the batched GEMM)
-    if ((reinterpret_cast<uintptr_t>(o.w) | static_cast<uintptr_t>(o.w_nb1)) & 15) return false;
+    // TMA rows: 16-byte aligned base and row stride. Q6_K also takes rows of 8
+    // mod 16 bytes (K = 1024 (mod 2048), unpadded) as row pairs when M is even;
+    // other Q6_K shapes take the batched GEMM
+    const bool pairs = q6_row_pairs(o);
+    if ((reinterpret_cast<uintptr_t>(o.w) & 15) || ((o.w_nb1 & 15) && !pairs)) return false;
     if (o.w_nb1 < row_bytes) return false;
     if (o.type == kTypeQ6_K && row_bytes < kQ6Box) return false;  // the box stays within a row's width
     if ((reinterpret_cast<uintptr_t>(o.x) | static_cast<uintptr_t>(o.x_nb1)) & 15) return false;  // float4 reads
@@ -693,9 +715,16 @@ int launch_prefill(const MulMatOp& o, void* workspace, size_t workspace_bytes, c
         // 240-byte box from the block's 16-byte-rounded start (the box's end may
         // pass the row's last block: zeros, never read)
         const cuuint64_t group = static_cast<cuuint64_t>(block_group_bytes(o.type));
-        const cuuint64_t dims[2] = {static_cast<cuuint64_t>(o.K / 256) * (q6 ? group : group / 8), static_cast<cuuint64_t>(o.M)};
-        const cuuint64_t strides[1] = {static_cast<cuuint64_t>(o.w_nb1)};
-        const cuuint32_t box[2] = {q6 ? static_cast<cuuint32_t>(kQ6Box) : static_cast<cuuint32_t>(group / 8), kTileM};
+        const bool pairs = q6_row_pairs(o);
+        // row pairs: [M / 2][2 w_nb1 bytes], the odd row's bytes from w_nb1 on
+        const cuuint64_t dims[2] = {pairs ? 2 * static_cast<cuuint64_t>(o.w_nb1)
+                                          : static_cast<cuuint64_t>(o.K / 256) * (q6 ? group : group / 8),
+                                    static_cast<cuuint64_t>(pairs ? o.M / 2 : o.M)};
+        const cuuint64_t strides[1] = {static_cast<cuuint64_t>(pairs ? 2 * o.w_nb1 : o.w_nb1)};
+        const cuuint32_t box[2] = {q6 ? static_cast<cuuint32_t>(kQ6Box) : static_cast<cuuint32_t>(group / 8),
+                                   pairs ? kTileM / 2u : static_cast<cuuint32_t>(kTileM)};
+        P.q6_pairs = pairs ? 1 : 0;
+        P.w_nb1 = static_cast<int32_t>(o.w_nb1);
         const cuuint32_t es[2] = {1, 1};
         if (enc(&P.wmap, q6 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, const_cast<uint8_t*>(o.w),
                 dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,

@@ -103,7 +103,7 @@ int launch_tp_wait(const TpLaunch& tp, cudaStream_t stream);
 unsigned read_and_clear_stream_error();
 
 // Prefill GEMM (mulmat_prefill.cu): Q4_K, Q5_K, Q8_0 and Q4_0 weights, or Q6_K with
-// 16-byte multiple rows, with N >= kPrefillMinN vectors on tcgen05 tensor cores (f16 operands, f32 accumulation). The
+// rows of 16-byte multiples (or 8-byte, M even), with N >= kPrefillMinN vectors on tcgen05 tensor cores (f16 operands, f32 accumulation). The
 // activations are first converted to f16 into caller-provided workspace of
 // prefill_workspace_bytes(op) bytes (256-byte aligned). Returns the number of
 // kernels launched (2) or a negative cudaError_t.
