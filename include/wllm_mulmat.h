@@ -173,7 +173,8 @@ int32_t wllm_mul_mat_batch(const wllm_mulmat_args* ops, int32_t n_ops, void* str
  * src/inference/jsep/ops/rms-norm.ts:14-15,61-67). gain: K floats, 16-byte
  * aligned, or NULL for RMS_NORM alone; every op has the same K. Decode
  * shapes only (N <= 4, as the streaming kernel takes them): NOT_IMPLEMENTED
- * otherwise, and the caller runs the three ops unfused. x is not modified. */
+ * otherwise, and the caller runs the three ops unfused. x is not modified.
+ * No op's y may overlap an op's x or the gain (WLLM_STATUS_FAILED). */
 int32_t wllm_mul_mat_rms_norm_batch(const wllm_mulmat_args* ops, int32_t n_ops, const float* gain, float eps,
                                     void* stream);
 
@@ -192,7 +193,7 @@ int32_t wllm_mul_mat_rms_norm_batch(const wllm_mulmat_args* ops, int32_t n_ops, 
  * same x. Decode
  * shapes only (N <= 4, as the streaming kernel takes them): NOT_IMPLEMENTED
  * otherwise, and the caller runs the ops unfused. gate and up are not
- * modified. */
+ * modified; no op's y may overlap them (WLLM_STATUS_FAILED). */
 int32_t wllm_mul_mat_glu_batch(const wllm_mulmat_args* ops, int32_t n_ops, const float* up, int64_t up_stride,
                                int32_t glu, void* stream);
 

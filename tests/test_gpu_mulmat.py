@@ -370,8 +370,9 @@ def test_fused_glu_vs_torch_fp64(runtime, group, glu, N):
 
 
 def test_fused_glu_rejects_bad_arguments(runtime):
-    """Ops that read different gates, an unknown kind, a misaligned up: FAILED
-    with a message; NOT_IMPLEMENTED beyond 4 vectors. Nothing is written."""
+    """Ops that read different gates, an unknown kind, a misaligned up, an
+    output overlapping the gate, up or gain input: FAILED with a message;
+    NOT_IMPLEMENTED beyond 4 vectors. Nothing is written."""
     import torch
 
     dev = torch.device("cuda", 0)
@@ -390,12 +391,19 @@ def test_fused_glu_rejects_bad_arguments(runtime):
                                y.data_ptr(), M)
 
     assert jsep.mul_mat_glu_batch([op(0, 8)], u.data_ptr(), K, jsep.GLU_SWIGLU, s) == jsep.STATUS_NOT_IMPLEMENTED
+    def op_y(y_ptr):
+        return jsep.MulMatArgs(jsep.GGML_TYPE_Q4_K, M, K, 1, w.data_ptr(), w.shape[1], g.data_ptr(), K, y_ptr, M)
+
     for args in (([op(0, 1), op(K, 1)], u.data_ptr(), K, jsep.GLU_SWIGLU),
                  ([op(0, 1)], u.data_ptr(), K, 7),
                  ([op(0, 1)], u.data_ptr() + 4, K, jsep.GLU_GELU),
-                 ([op(0, 2)], u.data_ptr(), K + 2, jsep.GLU_GELU)):
+                 ([op(0, 2)], u.data_ptr(), K + 2, jsep.GLU_GELU),
+                 ([op_y(u.data_ptr())], u.data_ptr(), K, jsep.GLU_SWIGLU),   # y inside up
+                 ([op_y(g.data_ptr())], u.data_ptr(), K, jsep.GLU_SWIGLU)):  # y inside the gate
         with pytest.raises(jsep.WllmError):
             jsep.mul_mat_glu_batch(*args, stream=s)
+    with pytest.raises(jsep.WllmError):  # the gain inside y
+        jsep.mul_mat_rms_norm_batch([op(0, 1)], y.data_ptr(), 1e-5, s)
     runtime.jsep_sync()
     assert bool((y == 7.0).all())
 

@@ -835,6 +835,33 @@ int32_t wllm_mul_mat_batch(const wllm_mulmat_args* ops, int32_t n_ops, void* str
     return launch(s, m, n_ops, stream ? static_cast<cudaStream_t>(stream) : s.stream);
 }
 
+namespace {
+
+// Byte range [first, end) of n vectors of len floats, stride floats apart.
+struct ByteRange {
+    uintptr_t first, end;
+};
+ByteRange vec_range(const void* p, int64_t stride, int32_t n, int64_t len) {
+    const uintptr_t b = reinterpret_cast<uintptr_t>(p);
+    return {b, b + 4 * static_cast<uintptr_t>(stride * (n - 1) + len)};
+}
+bool overlap(ByteRange a, ByteRange b) { return a.first < b.end && b.first < a.end; }
+
+// The fused entry points read their inputs (x, gain, up) in every CTA while
+// other CTAs store outputs: no op's y may overlap any of them.
+const char* fused_output_overlap(const wllm_mulmat_args* ops, int32_t n_ops, ByteRange extra) {
+    for (int i = 0; i < n_ops; ++i) {
+        const ByteRange y = vec_range(ops[i].y, ops[i].y_stride, ops[i].N, ops[i].M);
+        if (extra.end > extra.first && overlap(y, extra)) return "an op's y overlaps the gain / up input";
+        for (int j = 0; j < n_ops; ++j)
+            if (overlap(y, vec_range(ops[j].x, ops[j].x_stride, ops[j].N, ops[j].K)))
+                return "an op's y overlaps an op's x";
+    }
+    return nullptr;
+}
+
+}  // namespace
+
 int32_t wllm_mul_mat_rms_norm_batch(const wllm_mulmat_args* ops, int32_t n_ops, const float* gain, float eps,
                                     void* stream) {
     State& s = S();
@@ -847,6 +874,8 @@ int32_t wllm_mul_mat_rms_norm_batch(const wllm_mulmat_args* ops, int32_t n_ops, 
     if (gain && (reinterpret_cast<uintptr_t>(gain) & 15)) return fail(s, "%s: gain must be 16-byte aligned", what);
     for (int i = 1; i < n_ops; ++i)
         if (m[i].K != m[0].K) return fail(s, "%s: every op must have the same K (one gain vector)", what);
+    if (const char* why = fused_output_overlap(ops, n_ops, gain ? vec_range(gain, 0, 1, m[0].K) : ByteRange{0, 0}))
+        return fail(s, "%s: %s", what, why);
     // the fused form exists for the decode regime only: the caller runs the
     // RMS_NORM, MUL and MUL_MAT ops unfused otherwise
     if (!wllm::stream_supported(m, n_ops)) return WLLM_STATUS_NOT_IMPLEMENTED;
@@ -875,6 +904,8 @@ int32_t wllm_mul_mat_glu_batch(const wllm_mulmat_args* ops, int32_t n_ops, const
     for (int i = 1; i < n_ops; ++i)
         if (m[i].x != m[0].x || m[i].x_nb1 != m[0].x_nb1 || m[i].K != m[0].K || m[i].N != m[0].N)
             return fail(s, "%s: every op must read the same activations (one up tensor)", what);
+    if (const char* why = fused_output_overlap(ops, n_ops, vec_range(up, up_stride, m[0].N, m[0].K)))
+        return fail(s, "%s: %s", what, why);
     // the fused form exists for the decode regime only: the caller runs the
     // GLU and MUL_MAT ops unfused otherwise
     if (!wllm::stream_supported(m, n_ops)) return WLLM_STATUS_NOT_IMPLEMENTED;
