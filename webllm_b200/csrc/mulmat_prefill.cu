@@ -83,7 +83,8 @@ constexpr uint32_t kSpinLimit = 1u << 26;
 
 struct PrefillArgs {
     CUtensorMap wmap;   // weights: Q4_K [M rows][row_bytes / 8] uint64, box 18 x 128 (one block column);
-                        // Q6_K [M rows][row_bytes] uint8, box 240 x 128
+                        // Q6_K [M rows][row_bytes] uint8, box 240 x 128 (rows of 8 mod 16
+                        // bytes: [M / 2 row pairs][2 w_nb1] uint8, box 240 x 64)
     CUtensorMap xmap;   // f16 activations: [N][K], box 64 x 128, 128-byte swizzle
     float* y;
     int64_t y_nb1;      // bytes between output vectors
