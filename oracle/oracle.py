@@ -150,6 +150,22 @@ def rel_error(y: np.ndarray, r: np.ndarray) -> float:
     return float(np.max(np.abs(y - r)) / denom)
 
 
+def rel_error_elem(y: np.ndarray, r: np.ndarray, floor: float = 1e-2) -> float:
+    """Per-element relative error max_i |y_i - r_i| / |r_i| over the elements
+    with |r_i| >= floor * max|r| (r accumulated in f64): the second of the
+    path's two GEMV error metrics, which a max-normalized figure can hide
+    when a few large outputs dominate."""
+    r = np.asarray(r, dtype=np.float64)
+    y = np.asarray(y, dtype=np.float64)
+    if not r.size:
+        return 0.0
+    mx = float(np.max(np.abs(r)))
+    if mx == 0.0:
+        return float(np.max(np.abs(y - r)))
+    sel = np.abs(r) >= floor * mx
+    return float(np.max(np.abs(y[sel] - r[sel]) / np.abs(r[sel])))
+
+
 # ---- the activation-side ops fused into the GEMV (float64 restatements) ----
 
 

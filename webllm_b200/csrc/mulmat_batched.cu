@@ -5,12 +5,14 @@
 //
 //   y[m + M n] = sum_k W[m, k] x[k + K n]   (ggml MUL_MAT, matmul.ts:10-17)
 //
-// Activations: a pre-pass turns x into two int8 limbs per element,
-// x = (l0 + l1 / 128) / s with s = 127 / max|x| per 256 elements and vector
-// (|error| <= max|x| / 32512), stored as [N][2][K], with the factors 1 / s as
-// [K / 256][N rounded up to 4] and, for Q4_K / Q5_K, the f32 sums of x over each
-// 16-element sub-block as [K / 256][N rounded up to 4][16]. The eight B
-// columns of an MMA are four vectors x two limbs.
+// Activations: a pre-pass turns x into three int8 limbs per element,
+// x = (l0 + l1 / 128 + l2 / 16384) / s with s = 127 / max|x| per 256 elements
+// and vector (|error| <= max|x| / 4161536), stored as [N][3][K], with the
+// factors 1 / s as [K / 256][N rounded up to 4] and, for Q4_K / Q5_K, the f32
+// sums of x over each 16-element sub-block as [K / 256][N rounded up to
+// 4][16]. The eight B columns of an MMA are one limb of eight vectors: each
+// 32-element step takes three MMAs per vector octet, whose s32 results are
+// combined in f32 as D0 + D1 / 128 + D2 / 16384.
 //
 // Weights, per 32-element MMA step (k = 32):
 //  - Q8_0: one block; the s8 quants enter the MMA as they are and the s32
@@ -18,16 +20,16 @@
 //  - Q4_0: one block; the nibbles enter as s8 q - 8 (a 4-bit sign
 //    extension), then as Q8_0;
 //  - Q4_K: one 32-element sub-block; its u8 nibbles, the low ones as they are
-//    and the high ones in place (16 q), times the 6-bit scale (16 sc for the
-//    low-nibble sub-blocks) in integer over the 256-element block, then
-//    d / (16 s); the mins through the sub-block sums of x;
+//    and the high ones in place (16 q), the combined limbs times the 6-bit
+//    scale (16 sc for the low-nibble sub-blocks) summed over the 256-element
+//    block, then d / (16 s); the mins through the sub-block sums of x;
 //  - Q5_K: as Q4_K with the 5-bit quants (nibble | qh bit << 4) as u8 and
 //    sc for every sub-block, then d / s;
 //  - Q6_K: two 16-element sub-blocks, one MMA each (the other half of the A
 //    fragment zero); the quants q - 32 enter the MMA as s8 (a 6-bit sign
-//    extension), times the int8 scale in integer, then d / s.
+//    extension), times the int8 scale, then d / s.
 //
-// Tiling: a CTA (4 warps) computes 64 rows x NV vectors (NV = 8 .. 64); warp w
+// Tiling: a CTA (4 warps) computes 64 rows x NV vectors (NV = 8, 16, 32); warp w
 // rows 16 w .. 16 w + 15. K is walked in chunks of 256 elements (8 Q8_0
 // blocks, one K-quant block): the chunk's raw rows, limbs, factors and sums go
 // to shared memory with cp.async, 2 to 4 chunks in flight. Q8_0 and Q6_K
@@ -56,7 +58,9 @@ constexpr int kWarpsB = 4;
 constexpr int kThreadsB = 32 * kWarpsB;
 constexpr int kChunk = 256;                 // K per stage
 constexpr int kXRow = kChunk + 16;          // bytes of a limb row in shared memory (ldmatrix bank spread)
-constexpr int kMaxVec = 64;
+constexpr int kMaxVec = 32;
+constexpr int kLimbsB = 3;                  // int8 limbs per activation element
+constexpr int kSmemPerCta = 113 * 1024;     // two CTAs per SM
 constexpr int kSlotsB = 2 * 148;            // CTAs resident at once
 constexpr int kMaxSplitsB = 16;
 
@@ -84,7 +88,7 @@ __host__ __device__ constexpr int sum_floats() {  // x sub-block sums per vector
 struct BatchedArgs {
     const uint8_t* w;
     int64_t w_nb1;
-    const int8_t* xl;      // limbs [N][2][K]
+    const int8_t* xl;      // limbs [N][3][K]
     const float* inv_s;    // [K / 256][n_pad]
     const float* xsum;     // [K / 256][n_pad][16] (Q4_K)
     float* y;
@@ -96,14 +100,15 @@ struct BatchedArgs {
 
 template <int TYPE, int NV>
 __host__ __device__ constexpr int stage_bytes() {
-    return kRowsB * row_stride<TYPE>() + NV * 2 * kXRow + NV * 4 + NV * 4 * sum_floats<TYPE>();
+    return kRowsB * row_stride<TYPE>() + NV * kLimbsB * kXRow + NV * 4 + NV * 4 * sum_floats<TYPE>();
 }
-// Pipeline depth: enough bytes in flight per SM (two CTAs) to cover the HBM
-// latency, within the shared memory of two CTAs.
-template <int NV>
+// Pipeline depth: as many chunks in flight (at most 4) as the shared memory
+// of two CTAs per SM holds.
+template <int TYPE, int NV>
 __host__ __device__ constexpr int stages_of() {
-    return NV <= 16 ? 4 : (NV == 32 ? 3 : 2);
+    return kSmemPerCta / stage_bytes<TYPE, NV>() > 4 ? 4 : kSmemPerCta / stage_bytes<TYPE, NV>();
 }
+static_assert(stages_of<kTypeQ8_0, 32>() >= 2 && stages_of<kTypeQ6_K, 32>() >= 2, "two stages per CTA");
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -124,6 +129,10 @@ __device__ __forceinline__ void ldmatrix_x4(uint32_t (&r)[4], uint32_t addr) {
     asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
                  : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
                  : "r"(addr));
+}
+// Two 8x8 b16 matrices (lanes 0-15 supply the row addresses).
+__device__ __forceinline__ void ldmatrix_x2(uint32_t (&r)[2], uint32_t addr) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0,%1}, [%2];" : "=r"(r[0]), "=r"(r[1]) : "r"(addr));
 }
 
 // D = A (16x32 s8, row) * B (32x8 s8, col), s32.
@@ -242,23 +251,30 @@ __global__ void x_limbs_kernel(const float* __restrict__ x, int64_t x_nb1, int8_
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
     const float sc = mx > 0.f ? 127.f / mx : 0.f;
-    uint32_t l0[2], l1[2];
+    uint32_t l0[2], l1[2], l2[2];
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
-        int q0[4], q1[4];
+        int q0[4], q1[4], q2[4];
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
+            // l0 = rint(x s) (|l0| <= 127), l1 = rint(r1) with r1 = 128 (x s - l0)
+            // (|l1| <= 64), l2 = rint(128 (r1 - l1)) (|l2| <= 64); fmaf takes the
+            // exact product x s, r1 - l1 and the scalings by 128 are exact
             const float e = v[4 * h + i];
-            q0[i] = __float2int_rn(e * sc);                                     // |l0| <= 127
-            q1[i] = __float2int_rn(fmaf(e, sc, -static_cast<float>(q0[i])) * 128.f);  // |l1| <= 64
+            q0[i] = __float2int_rn(e * sc);
+            const float r1 = fmaf(e, sc, -static_cast<float>(q0[i])) * 128.f;
+            q1[i] = __float2int_rn(r1);
+            q2[i] = __float2int_rn(__fsub_rn(r1, static_cast<float>(q1[i])) * 128.f);
         }
         l0[h] = __byte_perm(__byte_perm(q0[0], q0[1], 0x0040u), __byte_perm(q0[2], q0[3], 0x0040u), 0x5410u);
         l1[h] = __byte_perm(__byte_perm(q1[0], q1[1], 0x0040u), __byte_perm(q1[2], q1[3], 0x0040u), 0x5410u);
+        l2[h] = __byte_perm(__byte_perm(q2[0], q2[1], 0x0040u), __byte_perm(q2[2], q2[3], 0x0040u), 0x5410u);
     }
     if (n < N) {
-        int8_t* base = xl + (static_cast<int64_t>(n) * 2) * K + b * 256 + 8 * lane;
+        int8_t* base = xl + (static_cast<int64_t>(n) * kLimbsB) * K + b * 256 + 8 * lane;
         *reinterpret_cast<uint2*>(base) = make_uint2(l0[0], l0[1]);
         *reinterpret_cast<uint2*>(base + K) = make_uint2(l1[0], l1[1]);
+        *reinterpret_cast<uint2*>(base + 2 * K) = make_uint2(l2[0], l2[1]);
     }
     if (lane == 0) inv_s[static_cast<int64_t>(b) * n_pad + n] = mx * (1.f / 127.f);
     if (xsum) {
@@ -269,13 +285,41 @@ __global__ void x_limbs_kernel(const float* __restrict__ x, int64_t x_nb1, int8_
     }
 }
 
+// The three limbs of one vector octet times one A fragment (32 elements at
+// shared addresses xa01: limbs 0 and 1, xa2: limb 2), combined in f32:
+// v = D0 + D1 / 128 + D2 / 16384 for the lane's four accumulator elements
+// (rows g, g + 8 x vectors 2c, 2c + 1 of the octet). |D| < 2^20, so each
+// conversion is exact and the sum is rounded twice (2^-24 relative).
+template <bool U8>
+__device__ __forceinline__ void mma_limbs(float (&v)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                          uint32_t xa01, uint32_t xa2) {
+    uint32_t b01[4], b2[2];
+    ldmatrix_x4(b01, xa01);
+    ldmatrix_x2(b2, xa2);
+    int D0[4], D1[4], D2[4];
+    if (U8) {
+        imma_u8(D0, a0, a1, a2, a3, b01[0], b01[1]);
+        imma_u8(D1, a0, a1, a2, a3, b01[2], b01[3]);
+        imma_u8(D2, a0, a1, a2, a3, b2[0], b2[1]);
+    } else {
+        imma_s8(D0, a0, a1, a2, a3, b01[0], b01[1]);
+        imma_s8(D1, a0, a1, a2, a3, b01[2], b01[3]);
+        imma_s8(D2, a0, a1, a2, a3, b2[0], b2[1]);
+    }
+#pragma unroll
+    for (int e = 0; e < 4; ++e)
+        v[e] = fmaf(static_cast<float>(D2[e]), 6.103515625e-05f,
+                    fmaf(static_cast<float>(D1[e]), 0.0078125f, static_cast<float>(D0[e])));
+}
+
 template <int TYPE, int NV>
 __global__ void __launch_bounds__(kThreadsB, 2) batched_kernel(const __grid_constant__ BatchedArgs P) {
     extern __shared__ __align__(128) uint8_t smem[];
     constexpr int RS = row_stride<TYPE>();
     constexpr int RP = row_pieces<TYPE>();
     constexpr int SB = stage_bytes<TYPE, NV>();
-    constexpr int NT = NV / 4;  // MMA column tiles: 4 vectors x 2 limbs each
+    constexpr int NO = NV / 8;                       // vector octets (one MMA column tile per limb)
+    constexpr uint32_t OCT = 8 * kLimbsB * kXRow;   // shared bytes between octets
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int g = lane >> 2, c = lane & 3;
     const int m0 = blockIdx.x * kRowsB, n0 = blockIdx.y * NV;
@@ -283,7 +327,7 @@ __global__ void __launch_bounds__(kThreadsB, 2) batched_kernel(const __grid_cons
     const int ch0 = blockIdx.z * P.chunks_per_split;
     const int nch = min(nchunks - ch0, P.chunks_per_split);
 
-    // one chunk's copies: 64 rows x RP pieces of 16 B (load_w), NV x 2 limb
+    // one chunk's copies: 64 rows x RP pieces of 16 B (load_w), NV x 3 limb
     // rows x 16 pieces, NV factors (16 B pieces of 4), NV x 16 sums (load_x)
     auto load_w = [&](int ch, int buf) {
         uint8_t* sw = smem + buf * SB;
@@ -314,14 +358,14 @@ __global__ void __launch_bounds__(kThreadsB, 2) batched_kernel(const __grid_cons
     };
     auto load_x = [&](int ch, int buf) {
         uint8_t* sx = smem + buf * SB + kRowsB * RS;
-        uint8_t* ss = sx + NV * 2 * kXRow;
+        uint8_t* ss = sx + NV * kLimbsB * kXRow;
         uint8_t* su = ss + NV * 4;
         const int k0 = (ch0 + ch) * kChunk;
-        for (int i = threadIdx.x; i < NV * 2 * 16; i += kThreadsB) {
-            const int rowl = i >> 4, pc = i & 15;  // rowl = 2 v + limb
-            const int v = rowl >> 1;
+        for (int i = threadIdx.x; i < NV * kLimbsB * 16; i += kThreadsB) {
+            const int rowl = i >> 4, pc = i & 15;  // rowl = 3 v + limb
+            const int v = rowl / kLimbsB, l = rowl - v * kLimbsB;
             const bool ok = n0 + v < P.N;
-            const int8_t* src = P.xl + (static_cast<int64_t>(ok ? n0 + v : 0) * 2 + (rowl & 1)) * P.K + k0 + 16 * pc;
+            const int8_t* src = P.xl + (static_cast<int64_t>(ok ? n0 + v : 0) * kLimbsB + l) * P.K + k0 + 16 * pc;
             cp_async16(sx + rowl * kXRow + 16 * pc, src, ok);
         }
         for (int i = threadIdx.x; i < NV / 4; i += kThreadsB) {
@@ -339,14 +383,17 @@ __global__ void __launch_bounds__(kThreadsB, 2) batched_kernel(const __grid_cons
         }
     };
 
-    float acc[NT][2];
+    // lane (g, c): rows g, g + 8 of the warp's 16 x vectors 8 o + 2c, 8 o + 2c + 1
+    float acc[NO][4];
 #pragma unroll
-    for (int t = 0; t < NT; ++t) acc[t][0] = acc[t][1] = 0.f;
+    for (int o = 0; o < NO; ++o) acc[o][0] = acc[o][1] = acc[o][2] = acc[o][3] = 0.f;
 
-    // ldmatrix row address: matrix mi = lane/8 (column tile 2 tp + mi/2, k half mi&1),
-    // row rr = lane%8 = B column: vector rr/2, limb rr&1
+    // ldmatrix row addresses: matrix mi = lane/8, row rr = lane%8 = B column =
+    // vector rr of the octet; x4: limb mi/2, k half mi&1; x2 (lanes 0-15):
+    // limb 2, k half mi
     const int mi = lane >> 3, rr = lane & 7;
-    const uint32_t xoff = static_cast<uint32_t>((2 * (4 * (mi >> 1) + (rr >> 1)) + (rr & 1)) * kXRow + 16 * (mi & 1));
+    const uint32_t xoff01 = static_cast<uint32_t>((kLimbsB * rr + (mi >> 1)) * kXRow + 16 * (mi & 1));
+    const uint32_t xoff2 = static_cast<uint32_t>((kLimbsB * rr + 2) * kXRow + 16 * (mi & 1));
     // Q6_K: where row g / g+8's block sits in its 16-byte window (the window
     // offset changes by 210 mod 16 from chunk to chunk)
     const uintptr_t rowg_addr =
@@ -356,7 +403,7 @@ __global__ void __launch_bounds__(kThreadsB, 2) batched_kernel(const __grid_cons
     // Programmatic dependent launch: the first chunks' weights are requested
     // before the wait for the kernel that writes the activations (the x
     // pre-pass); they join the first chunk's copy group.
-    constexpr int ST = stages_of<NV>();
+    constexpr int ST = stages_of<TYPE, NV>();
 #pragma unroll
     for (int sidx = 0; sidx < ST - 1; ++sidx)
         if (sidx < nch) load_w(sidx, sidx);
@@ -377,65 +424,48 @@ __global__ void __launch_bounds__(kThreadsB, 2) batched_kernel(const __grid_cons
         cp_async_commit();
         const uint8_t* sw = smem + (ch % ST) * SB;
         const uint8_t* sx = sw + kRowsB * RS;
-        const float* ss = reinterpret_cast<const float*>(sx + NV * 2 * kXRow);
+        const float* ss = reinterpret_cast<const float*>(sx + NV * kLimbsB * kXRow);
         const float* su = ss + NV;
-        const uint32_t xbase = smem_u32(sx) + xoff;
+        const uint32_t xb01 = smem_u32(sx) + xoff01, xb2 = smem_u32(sx) + xoff2;
         const uint8_t* rg = sw + (16 * warp + g) * RS;
         const uint8_t* rh = rg + 8 * RS;
-        float is[NT];  // 1 / s of this lane's vector in each column tile
+        float is[NO][2];  // 1 / s of the lane's two vectors in each octet
 #pragma unroll
-        for (int t = 0; t < NT; ++t) is[t] = ss[4 * t + c];
+        for (int o = 0; o < NO; ++o) {
+            is[o][0] = ss[8 * o + 2 * c];
+            is[o][1] = ss[8 * o + 2 * c + 1];
+        }
 
-        if (TYPE == kTypeQ8_0) {
+        if (TYPE == kTypeQ8_0 || TYPE == kTypeQ4_0) {
+            constexpr int BB = TYPE == kTypeQ8_0 ? 34 : 18;
 #pragma unroll
             for (int b = 0; b < 8; ++b) {
-                const uint8_t* bg = rg + 34 * b;
-                const uint8_t* bh = rh + 34 * b;
+                const uint8_t* bg = rg + BB * b;
+                const uint8_t* bh = rh + BB * b;
                 const float dg = f16_bits_to_f32(*reinterpret_cast<const uint16_t*>(bg));
                 const float dh = f16_bits_to_f32(*reinterpret_cast<const uint16_t*>(bh));
-                const uint32_t a0 = lds_u32_any(bg + 2 + 4 * c), a1 = lds_u32_any(bh + 2 + 4 * c);
-                const uint32_t a2 = lds_u32_any(bg + 18 + 4 * c), a3 = lds_u32_any(bh + 18 + 4 * c);
-#pragma unroll
-                for (int tp = 0; tp < NT / 2; ++tp) {
-                    uint32_t xb[4];
-                    ldmatrix_x4(xb, xbase + static_cast<uint32_t>(tp * 8 * 2 * kXRow + 32 * b));
-#pragma unroll
-                    for (int h = 0; h < 2; ++h) {
-                        const int t = 2 * tp + h;
-                        int D[4];
-                        imma_s8(D, a0, a1, a2, a3, xb[2 * h], xb[2 * h + 1]);
-                        const float vg = fmaf(static_cast<float>(D[1]), 0.0078125f, static_cast<float>(D[0]));
-                        const float vh = fmaf(static_cast<float>(D[3]), 0.0078125f, static_cast<float>(D[2]));
-                        acc[t][0] = fmaf(vg, dg * is[t], acc[t][0]);
-                        acc[t][1] = fmaf(vh, dh * is[t], acc[t][1]);
-                    }
+                uint32_t a0, a1, a2, a3;
+                if (TYPE == kTypeQ8_0) {
+                    a0 = lds_u32_any(bg + 2 + 4 * c);
+                    a1 = lds_u32_any(bh + 2 + 4 * c);
+                    a2 = lds_u32_any(bg + 18 + 4 * c);
+                    a3 = lds_u32_any(bh + 18 + 4 * c);
+                } else {
+                    // elements 4c.. are the low nibbles, 16+4c.. the high ones
+                    const uint32_t wg = lds_u32_any(bg + 2 + 4 * c), wh = lds_u32_any(bh + 2 + 4 * c);
+                    a0 = q4_signed(wg & 0x0F0F0F0Fu);
+                    a1 = q4_signed(wh & 0x0F0F0F0Fu);
+                    a2 = q4_signed((wg >> 4) & 0x0F0F0F0Fu);
+                    a3 = q4_signed((wh >> 4) & 0x0F0F0F0Fu);
                 }
-            }
-        } else if (TYPE == kTypeQ4_0) {
 #pragma unroll
-            for (int b = 0; b < 8; ++b) {
-                const uint8_t* bg = rg + 18 * b;
-                const uint8_t* bh = rh + 18 * b;
-                const float dg = f16_bits_to_f32(*reinterpret_cast<const uint16_t*>(bg));
-                const float dh = f16_bits_to_f32(*reinterpret_cast<const uint16_t*>(bh));
-                const uint32_t wg = lds_u32_any(bg + 2 + 4 * c), wh = lds_u32_any(bh + 2 + 4 * c);
-                // elements 4c.. are the low nibbles, 16+4c.. the high ones
-                const uint32_t a0 = q4_signed(wg & 0x0F0F0F0Fu), a1 = q4_signed(wh & 0x0F0F0F0Fu);
-                const uint32_t a2 = q4_signed((wg >> 4) & 0x0F0F0F0Fu), a3 = q4_signed((wh >> 4) & 0x0F0F0F0Fu);
-#pragma unroll
-                for (int tp = 0; tp < NT / 2; ++tp) {
-                    uint32_t xb[4];
-                    ldmatrix_x4(xb, xbase + static_cast<uint32_t>(tp * 8 * 2 * kXRow + 32 * b));
-#pragma unroll
-                    for (int h = 0; h < 2; ++h) {
-                        const int t = 2 * tp + h;
-                        int D[4];
-                        imma_s8(D, a0, a1, a2, a3, xb[2 * h], xb[2 * h + 1]);
-                        const float vg = fmaf(static_cast<float>(D[1]), 0.0078125f, static_cast<float>(D[0]));
-                        const float vh = fmaf(static_cast<float>(D[3]), 0.0078125f, static_cast<float>(D[2]));
-                        acc[t][0] = fmaf(vg, dg * is[t], acc[t][0]);
-                        acc[t][1] = fmaf(vh, dh * is[t], acc[t][1]);
-                    }
+                for (int o = 0; o < NO; ++o) {
+                    float v[4];
+                    mma_limbs<false>(v, a0, a1, a2, a3, xb01 + o * OCT + 32 * b, xb2 + o * OCT + 32 * b);
+                    acc[o][0] = fmaf(v[0], dg * is[o][0], acc[o][0]);
+                    acc[o][1] = fmaf(v[1], dg * is[o][1], acc[o][1]);
+                    acc[o][2] = fmaf(v[2], dh * is[o][0], acc[o][2]);
+                    acc[o][3] = fmaf(v[3], dh * is[o][1], acc[o][3]);
                 }
             }
         } else if (TYPE == kTypeQ4_K || TYPE == kTypeQ5_K) {
@@ -452,11 +482,9 @@ __global__ void __launch_bounds__(kThreadsB, 2) batched_kernel(const __grid_cons
                 hb[2] = *reinterpret_cast<const uint32_t*>(rg + 32 + 4 * c);
                 hb[3] = *reinterpret_cast<const uint32_t*>(rh + 32 + 4 * c);
             }
-            // |D| <= 32 * 240 * 127 per sub-block, times sc <= 63 (or 16 sc with
-            // the unscaled low nibbles), over 8 sub-blocks: inside int32
-            int a[NT][4];
+            float af[NO][4];  // the block's scaled sub-block sums
 #pragma unroll
-            for (int t = 0; t < NT; ++t) a[t][0] = a[t][1] = a[t][2] = a[t][3] = 0;
+            for (int o = 0; o < NO; ++o) af[o][0] = af[o][1] = af[o][2] = af[o][3] = 0.f;
 #pragma unroll 1
             for (int p = 0; p < 4; ++p) {
                 // fragment words of sub-block pair p (qs bytes 32p .. 32p+31): row
@@ -482,22 +510,16 @@ __global__ void __launch_bounds__(kThreadsB, 2) batched_kernel(const __grid_cons
                         A[3] = w3 & msk;
                     }
                     // (q4k_scale_j gives 16 sc for even j: Q5_K takes sc)
-                    const int scj = q4k_scale_j(hg, j) >> (k5 && !hi ? 4 : 0);
-                    const int shj = q4k_scale_j(hh4, j) >> (k5 && !hi ? 4 : 0);
+                    const float scj = static_cast<float>(q4k_scale_j(hg, j) >> (k5 && !hi ? 4 : 0));
+                    const float shj = static_cast<float>(q4k_scale_j(hh4, j) >> (k5 && !hi ? 4 : 0));
 #pragma unroll
-                    for (int tp = 0; tp < NT / 2; ++tp) {
-                        uint32_t xb[4];
-                        ldmatrix_x4(xb, xbase + static_cast<uint32_t>(tp * 8 * 2 * kXRow + 32 * j));
-#pragma unroll
-                        for (int h = 0; h < 2; ++h) {
-                            const int t = 2 * tp + h;
-                            int D[4];
-                            imma_u8(D, A[0], A[1], A[2], A[3], xb[2 * h], xb[2 * h + 1]);
-                            a[t][0] += scj * D[0];
-                            a[t][1] += scj * D[1];
-                            a[t][2] += shj * D[2];
-                            a[t][3] += shj * D[3];
-                        }
+                    for (int o = 0; o < NO; ++o) {
+                        float v[4];
+                        mma_limbs<true>(v, A[0], A[1], A[2], A[3], xb01 + o * OCT + 32 * j, xb2 + o * OCT + 32 * j);
+                        af[o][0] = fmaf(scj, v[0], af[o][0]);
+                        af[o][1] = fmaf(scj, v[1], af[o][1]);
+                        af[o][2] = fmaf(shj, v[2], af[o][2]);
+                        af[o][3] = fmaf(shj, v[3], af[o][3]);
                     }
                 }
             }
@@ -506,29 +528,30 @@ __global__ void __launch_bounds__(kThreadsB, 2) batched_kernel(const __grid_cons
             q4k_scales8(hg, scg, mg, dg);
             q4k_scales8(hh4, sch, mh, dh);
 #pragma unroll
-            for (int t = 0; t < NT; ++t) {
-                const float* xs = su + (4 * t + c) * 16;  // the lane's vector's 16-element sums
-                float og = 0.f, oh = 0.f;
+            for (int o = 0; o < NO; ++o) {
 #pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    const float X = xs[2 * j] + xs[2 * j + 1];
-                    og = fmaf(mg[j], X, og);
-                    oh = fmaf(mh[j], X, oh);
+                for (int e = 0; e < 2; ++e) {  // the lane's vectors 8 o + 2 c + e
+                    const float* xs = su + (8 * o + 2 * c + e) * 16;  // its 16-element sums
+                    float og = 0.f, oh = 0.f;
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) {
+                        const float X = xs[2 * j] + xs[2 * j + 1];
+                        og = fmaf(mg[j], X, og);
+                        oh = fmaf(mh[j], X, oh);
+                    }
+                    const float f = k5 ? is[o][e] : is[o][e] * 0.0625f;
+                    acc[o][e] += fmaf(dg * af[o][e], f, -og);
+                    acc[o][2 + e] += fmaf(dh * af[o][2 + e], f, -oh);
                 }
-                const float f = k5 ? is[t] : is[t] * 0.0625f;
-                acc[t][0] += fmaf(dg * fmaf(static_cast<float>(a[t][1]), 0.0078125f, static_cast<float>(a[t][0])), f, -og);
-                acc[t][1] += fmaf(dh * fmaf(static_cast<float>(a[t][3]), 0.0078125f, static_cast<float>(a[t][2])), f, -oh);
             }
         } else {
             // Q6_K: the block of row g / g+8 at its offset in the 16-byte window
             const uintptr_t boff = static_cast<uintptr_t>((ch0 + ch) * 210);
             const uint8_t* pg = rg + ((rowg_addr + boff) & 15);
             const uint8_t* ph = rh + ((rowh_addr + boff) & 15);
-            // |D| <= 16 * 32 * 127 per sub-block, times |sc| <= 128, over 16
-            // sub-blocks: inside int32
-            int a[NT][4];
+            float af[NO][4];  // the block's scaled sub-block sums
 #pragma unroll
-            for (int t = 0; t < NT; ++t) a[t][0] = a[t][1] = a[t][2] = a[t][3] = 0;
+            for (int o = 0; o < NO; ++o) af[o][0] = af[o][1] = af[o][2] = af[o][3] = 0.f;
 #pragma unroll 1
             for (int h = 0; h < 2; ++h) {
                 // the fragment words of half h at position r (0: row g k 4c.., 1: row
@@ -547,60 +570,62 @@ __global__ void __launch_bounds__(kThreadsB, 2) batched_kernel(const __grid_cons
                     uint32_t A[4];
 #pragma unroll
                     for (int r = 0; r < 4; ++r) A[r] = q6_signed(q6k_group(q0[r], q1[r], qb[r], gi));
-                    const int sge = static_cast<int>(*reinterpret_cast<const int8_t*>(pg + 192 + 2 * i));
-                    const int sgo = static_cast<int>(*reinterpret_cast<const int8_t*>(pg + 193 + 2 * i));
-                    const int she = static_cast<int>(*reinterpret_cast<const int8_t*>(ph + 192 + 2 * i));
-                    const int sho = static_cast<int>(*reinterpret_cast<const int8_t*>(ph + 193 + 2 * i));
+                    const float sge = static_cast<float>(*reinterpret_cast<const int8_t*>(pg + 192 + 2 * i));
+                    const float sgo = static_cast<float>(*reinterpret_cast<const int8_t*>(pg + 193 + 2 * i));
+                    const float she = static_cast<float>(*reinterpret_cast<const int8_t*>(ph + 192 + 2 * i));
+                    const float sho = static_cast<float>(*reinterpret_cast<const int8_t*>(ph + 193 + 2 * i));
 #pragma unroll
-                    for (int tp = 0; tp < NT / 2; ++tp) {
-                        uint32_t xb[4];
-                        ldmatrix_x4(xb, xbase + static_cast<uint32_t>(tp * 8 * 2 * kXRow + 32 * i));
-#pragma unroll
-                        for (int hh = 0; hh < 2; ++hh) {
-                            const int t = 2 * tp + hh;
-                            int De[4], Do[4];
-                            imma_s8(De, A[0], A[1], 0u, 0u, xb[2 * hh], xb[2 * hh + 1]);
-                            imma_s8(Do, 0u, 0u, A[2], A[3], xb[2 * hh], xb[2 * hh + 1]);
-                            a[t][0] += sge * De[0] + sgo * Do[0];
-                            a[t][1] += sge * De[1] + sgo * Do[1];
-                            a[t][2] += she * De[2] + sho * Do[2];
-                            a[t][3] += she * De[3] + sho * Do[3];
-                        }
+                    for (int o = 0; o < NO; ++o) {
+                        // the two 16-element sub-blocks on separate MMAs (the other
+                        // half of the A fragment zero)
+                        float ve[4], vo[4];
+                        mma_limbs<false>(ve, A[0], A[1], 0u, 0u, xb01 + o * OCT + 32 * i, xb2 + o * OCT + 32 * i);
+                        mma_limbs<false>(vo, 0u, 0u, A[2], A[3], xb01 + o * OCT + 32 * i, xb2 + o * OCT + 32 * i);
+                        af[o][0] = fmaf(sge, ve[0], fmaf(sgo, vo[0], af[o][0]));
+                        af[o][1] = fmaf(sge, ve[1], fmaf(sgo, vo[1], af[o][1]));
+                        af[o][2] = fmaf(she, ve[2], fmaf(sho, vo[2], af[o][2]));
+                        af[o][3] = fmaf(she, ve[3], fmaf(sho, vo[3], af[o][3]));
                     }
                 }
             }
             const float dg = f16_bits_to_f32(*reinterpret_cast<const uint16_t*>(pg + 208));
             const float dh = f16_bits_to_f32(*reinterpret_cast<const uint16_t*>(ph + 208));
 #pragma unroll
-            for (int t = 0; t < NT; ++t) {
-                acc[t][0] = fmaf(dg * is[t], fmaf(static_cast<float>(a[t][1]), 0.0078125f, static_cast<float>(a[t][0])),
-                                 acc[t][0]);
-                acc[t][1] = fmaf(dh * is[t], fmaf(static_cast<float>(a[t][3]), 0.0078125f, static_cast<float>(a[t][2])),
-                                 acc[t][1]);
+            for (int o = 0; o < NO; ++o) {
+                acc[o][0] = fmaf(dg * is[o][0], af[o][0], acc[o][0]);
+                acc[o][1] = fmaf(dg * is[o][1], af[o][1], acc[o][1]);
+                acc[o][2] = fmaf(dh * is[o][0], af[o][2], acc[o][2]);
+                acc[o][3] = fmaf(dh * is[o][1], af[o][3], acc[o][3]);
             }
         }
     }
 
-    // ---- outputs: lane (g, c) holds rows 16 warp + g (+8) of vector 4 t + c ----
+    // ---- outputs: lane (g, c) holds rows 16 warp + g (+8) of vectors 8 o + 2 c (+1) ----
     const int tile = blockIdx.y * gridDim.x + blockIdx.x;
     if (P.splits == 1) {
 #pragma unroll
-        for (int t = 0; t < NT; ++t) {
-            const int n = n0 + 4 * t + c;
-            if (n >= P.N) continue;
-            float* yn = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(P.y) + n * P.y_nb1);
-            const int r = m0 + 16 * warp + g;
-            if (r < P.M) yn[r] = acc[t][0];
-            if (r + 8 < P.M) yn[r + 8] = acc[t][1];
+        for (int o = 0; o < NO; ++o) {
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+                const int n = n0 + 8 * o + 2 * c + e;
+                if (n >= P.N) continue;
+                float* yn = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(P.y) + n * P.y_nb1);
+                const int r = m0 + 16 * warp + g;
+                if (r < P.M) yn[r] = acc[o][e];
+                if (r + 8 < P.M) yn[r + 8] = acc[o][2 + e];
+            }
         }
         return;
     }
     float* part = P.partial + (static_cast<int64_t>(tile) * P.splits + blockIdx.z) * (kMaxVec * kRowsB);
 #pragma unroll
-    for (int t = 0; t < NT; ++t) {
-        const int v = 4 * t + c;
-        part[v * kRowsB + 16 * warp + g] = acc[t][0];
-        part[v * kRowsB + 16 * warp + g + 8] = acc[t][1];
+    for (int o = 0; o < NO; ++o) {
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+            const int v = 8 * o + 2 * c + e;
+            part[v * kRowsB + 16 * warp + g] = acc[o][e];
+            part[v * kRowsB + 16 * warp + g + 8] = acc[o][2 + e];
+        }
     }
     __shared__ int last;
     __syncthreads();
@@ -625,12 +650,12 @@ __global__ void __launch_bounds__(kThreadsB, 2) batched_kernel(const __grid_cons
     }
 }
 
-// Vectors per CTA tile: N rounded up to 8, 16, 32 or 64 (Q6_K at most 32:
-// its two MMAs per 32 elements need the registers of the wider tile).
+// Vectors per CTA tile: N rounded up to 8, 16 or 32; wider N takes several
+// 32-vector tiles (a 64-vector tile's three limb rows per vector would leave
+// room for one CTA per SM).
 int pick_nv(const MulMatOp& o) {
-    const int N = o.N, cap = o.type == kTypeQ6_K ? 32 : 64;
-    const int nv = N <= 8 ? 8 : (N <= 16 ? 16 : (N <= 32 ? 32 : 64));
-    return nv < cap ? nv : cap;
+    const int N = o.N;
+    return N <= 8 ? 8 : (N <= 16 ? 16 : 32);
 }
 
 void plan(const MulMatOp& o, int* nv, int* splits, int* cps) {
@@ -646,7 +671,7 @@ void plan(const MulMatOp& o, int* nv, int* splits, int* cps) {
 }
 
 int n_pad_of(const MulMatOp& o) { return (o.N + 3) & ~3; }
-size_t limbs_bytes(const MulMatOp& o) { return (static_cast<size_t>(o.N) * 2 * o.K + 255) & ~size_t(255); }
+size_t limbs_bytes(const MulMatOp& o) { return (static_cast<size_t>(o.N) * kLimbsB * o.K + 255) & ~size_t(255); }
 size_t factors_bytes(const MulMatOp& o) {
     return (static_cast<size_t>(o.K / 256) * n_pad_of(o) * 4 + 255) & ~size_t(255);
 }
@@ -664,13 +689,18 @@ size_t partial_bytes(const MulMatOp& o) {
 
 template <int TYPE, int NV>
 cudaError_t launch_nv(const BatchedArgs& P, dim3 grid, cudaStream_t stream) {
-    constexpr int smem = stages_of<NV>() * stage_bytes<TYPE, NV>();
-    static bool configured = false;
-    if (!configured) {
+    constexpr int smem = stages_of<TYPE, NV>() * stage_bytes<TYPE, NV>();
+    // the attribute is per device: one flag per device ordinal
+    static bool configured[kMaxDevices] = {};
+    int dev = 0;
+    cudaError_t e0 = cudaGetDevice(&dev);
+    if (e0 != cudaSuccess) return e0;
+    if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+    if (!configured[dev]) {
         const cudaError_t e =
             cudaFuncSetAttribute(batched_kernel<TYPE, NV>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         if (e != cudaSuccess) return e;
-        configured = true;
+        configured[dev] = true;
     }
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -691,16 +721,7 @@ cudaError_t launch_type(int nv, const BatchedArgs& P, dim3 grid, cudaStream_t st
     switch (nv) {
         case 8: return launch_nv<TYPE, 8>(P, grid, stream);
         case 16: return launch_nv<TYPE, 16>(P, grid, stream);
-        case 32: return launch_nv<TYPE, 32>(P, grid, stream);
-        default: return launch_nv<TYPE, 64>(P, grid, stream);
-    }
-}
-template <>
-cudaError_t launch_type<kTypeQ6_K>(int nv, const BatchedArgs& P, dim3 grid, cudaStream_t stream) {
-    switch (nv) {
-        case 8: return launch_nv<kTypeQ6_K, 8>(P, grid, stream);
-        case 16: return launch_nv<kTypeQ6_K, 16>(P, grid, stream);
-        default: return launch_nv<kTypeQ6_K, 32>(P, grid, stream);
+        default: return launch_nv<TYPE, 32>(P, grid, stream);
     }
 }
 

@@ -757,7 +757,11 @@ int launch_prefill(const MulMatOp& o, void* workspace, size_t workspace_bytes, c
         const cudaError_t e = cudaMemsetAsync(P.counters, 0, tiles * 4, stream);
         if (e != cudaSuccess) return -static_cast<int>(e);
     }
-    static bool configured[5] = {false, false, false, false, false};
+    // the attribute is per device: one flag per device ordinal and kernel
+    static bool configured[kMaxDevices][5] = {};
+    int dev = 0;
+    if (const cudaError_t e = cudaGetDevice(&dev); e != cudaSuccess) return -static_cast<int>(e);
+    if (dev < 0 || dev >= kMaxDevices) return -static_cast<int>(cudaErrorInvalidDevice);
     const int ti = o.type == kTypeQ4_K ? 0 : (o.type == kTypeQ5_K ? 1 : (q6 ? 2 : (o.type == kTypeQ8_0 ? 3 : 4)));
     void (*const kernels[5])(PrefillArgs) = {prefill_kernel<kTypeQ4_K>, prefill_kernel<kTypeQ5_K>,
                                              prefill_kernel<kTypeQ6_K>, prefill_kernel<kTypeQ8_0>,
@@ -766,11 +770,11 @@ int launch_prefill(const MulMatOp& o, void* workspace, size_t workspace_bytes, c
                              smem_bytes<kTypeQ8_0>(), smem_bytes<kTypeQ4_0>()};
     void (*const kernel)(PrefillArgs) = kernels[ti];
     const size_t smem = smems[ti];
-    if (!configured[ti]) {
+    if (!configured[dev][ti]) {
         const cudaError_t e =
             cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
         if (e != cudaSuccess) return -static_cast<int>(e);
-        configured[ti] = true;
+        configured[dev][ti] = true;
     }
     const dim3 grid((o.M + kTileM - 1) / kTileM, (o.N + kTileN - 1) / kTileN, splits);
     kernel<<<grid, kThreads, smem, stream>>>(P);
@@ -788,10 +792,10 @@ static __device__ __align__(256) unsigned char g_prefill_static_ws[kPrefillStati
 void* prefill_static_workspace(const char** err) {
     // the array's device address, looked up once per device (the lookup must
     // not happen while a stream is being captured)
-    static void* addr[64] = {};
-    static bool looked_up[64] = {};
+    static void* addr[kMaxDevices] = {};
+    static bool looked_up[kMaxDevices] = {};
     int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
         cudaGetLastError();
         *err = "cannot query the current device";
         return nullptr;

@@ -20,12 +20,18 @@
 //
 // Every type runs on integer tensor cores (mma.sync m16n8k32, u8 / s8 x s8 ->
 // s32):
-//  - activations: per 256-element block and vector, x = (l0 + l1/128) / s with
-//    s = 127 / max|x| and int8 limbs l0 = rint(x s), l1 = rint(128 (x s - l0))
-//    (|error| <= max|x| / 32512); the two limbs of each vector are two B
-//    columns, so the MMA's eight columns hold sub-block slots x vectors x
-//    limbs, and a sub-block's MMA reads real B rows only in its own slot's
-//    columns: several sub-blocks share one accumulator without mixing;
+//  - activations: per 256-element block and vector, x = (l0 + l1/128 +
+//    l2/16384) / s with s = 127 / max|x| and int8 limbs l0 = rint(x s),
+//    l1 = rint(128 (x s - l0)), l2 = rint(128 (128 (x s - l0) - l1))
+//    (|error| <= max|x| / 4161536, about 22 bits of the block maximum: two
+//    limbs, 15 bits, left elements next to a 100x outlier channel with a few
+//    percent error); the MMA's eight B columns are two (slot, vector) pairs of
+//    four columns each, limbs 0, 1, 2 and a zero column, so a lane's two
+//    accumulator columns always belong to one pair (even lanes: limbs 0 and
+//    1, odd lanes: limb 2). Sub-blocks in different slots share one
+//    accumulator without mixing, since a sub-block's MMA reads real B rows
+//    only in its own slot's columns. Four vectors take two passes over each
+//    weight fragment, one per vector pair;
 //  - Q4_K weights: ldmatrix hands each lane the bytes of its fragment; the
 //    low nibbles (v & 0x0F0F0F0F) and the high nibbles kept in place
 //    (v & 0xF0F0F0F0 = 16 q) are the A operands; 6-bit scales are applied in
@@ -315,14 +321,15 @@ __device__ __forceinline__ uint32_t q4_signed(uint32_t q) {
 }
 
 // Byte layout of the shared-memory activation image.
-//  Every type (one shared image): int8 limb columns [2N][K + kXPad]
-//        (column 2t + l = limb l of vector t), then f32 d-factors [N][K/256]
+//  Every type (one shared image): int8 limb columns [3N][K + kXPad]
+//        (column 3t + l = limb l of vector t), then f32 d-factors [N][K/256]
 //        (max|x| / (127 * 16) per block), then exact f32 sums of x over
 //        32-element sub-blocks [N][K/32] (Q4_K, Q5_K) and over 16-element
 //        sub-blocks [N][K/16] (Q6_K). Q8_0 and Q4_0 use the limbs and
 //        d-factors.
 __host__ __device__ __forceinline__ int img_col_bytes(int K) { return K + kXPad; }
-__host__ __device__ __forceinline__ int img_inv_off(int K, int N) { return 2 * N * img_col_bytes(K); }
+constexpr int kLimbs = 3;  // int8 limbs per activation element
+__host__ __device__ __forceinline__ int img_inv_off(int K, int N) { return kLimbs * N * img_col_bytes(K); }
 // (16-byte aligned: the sums are read as float2)
 __host__ __device__ __forceinline__ int img_sum_off(int K, int N) {
     return (img_inv_off(K, N) + 4 * N * (K / 256) + 15) & ~15;
@@ -369,20 +376,24 @@ __device__ __forceinline__ void q4k_slot_scales(const uint4 h, int sl, int (&sc)
     }
 }
 
-// One Q4_K item: 16 rows x one 256-element block, for NP = N rounded up to a
-// power of two. The MMA's 8 columns are NS = 4/NP sub-block slots x NP
-// vectors x 2 limbs (column 2 NP slot + 2 t + l). A sub-block's MMA reads the
-// activation rows of its own slot; every other B row is the zero row, so the
-// NS sub-blocks of a chain accumulate into one fragment without mixing, and
-// lane (g, c) ends up with its slot's sub-blocks (slot c / NP, vector c % NP)
-// of rows g and g+8: it scales only those, NCH = 8 / NS per row.
+// One Q4_K item: 16 rows x one 256-element block, for NP = 1 or 2 vectors
+// (four vectors run this twice, once per vector pair). The MMA's 8 columns
+// are two (slot, vector) pairs of limbs 0, 1, 2 and a zero column: NS = 2
+// sub-block slots of one vector, or one slot of two vectors (column
+// 4 u + l). A sub-block's MMA reads the activation rows of its own slot;
+// every other B row is the zero row, so the NS sub-blocks of a chain
+// accumulate into one fragment without mixing, and lane (g, c) ends up with
+// pair u = c / 2 of rows g and g+8: limbs 0 and 1 (hl = c & 1 = 0) or limb 2
+// (hl = 1). It scales only its slot's sub-blocks, NCH = 8 / NS per row; the
+// mins are added by the hl = 0 lane of each pair.
 template <int NP, int NI>
 __device__ __forceinline__ void q4k_items(const uint8_t* blk, int wbox, uint32_t wl, uint32_t xaddr, uint32_t xzero,
-                                          bool xv0, bool xv1, const float* df, const float* xs, int g, int sl,
+                                          bool xv0, bool xv1, const float* df, const float* xs, int g, int sl, int hl,
                                           float& yg, float& yh) {
     // NI items of one unit at once (blocks kCW apart): independent chains the
     // scheduler interleaves
-    constexpr int NS = 4 / NP, NCH = 8 / NS;
+    static_assert(NP == 1 || NP == 2, "vector pairs");
+    constexpr int NS = NP == 1 ? 2 : 1, NCH = 8 / NS;
     constexpr int BS = kCW * 144;  // stage bytes between the items
     constexpr int XS = kCW * 256;  // activation bytes between the items
     int scg[NI][NCH], sch[NI][NCH];
@@ -413,9 +424,11 @@ __device__ __forceinline__ void q4k_items(const uint8_t* blk, int wbox, uint32_t
                           w[3] & 0xF0F0F0F0u, x[2], x[3]);
         }
     }
+    // limb weights of the lane's two columns: (1, 1/128) or (1/16384, 0)
+    const float lf = hl ? 6.103515625e-05f : 1.f;
 #pragma unroll
     for (int k = 0; k < NI; ++k) {
-        int a0 = 0, a1 = 0, a2 = 0, a3 = 0;  // (g, limb 0), (g, limb 1), (g+8, l0), (g+8, l1)
+        int a0 = 0, a1 = 0, a2 = 0, a3 = 0;  // (g, col 0), (g, col 1), (g+8, col 0), (g+8, col 1)
 #pragma unroll
         for (int q = 0; q < NCH; ++q) {
             a0 += scg[k][q] * D[k][q][0];
@@ -424,13 +437,15 @@ __device__ __forceinline__ void q4k_items(const uint8_t* blk, int wbox, uint32_t
             a3 += sch[k][q] * D[k][q][3];
         }
         const float xf = df[k * kCW];
-        yg = fmaf(fmaf(static_cast<float>(a1), 0.0078125f, static_cast<float>(a0)), dg[k] * xf, yg);
-        yh = fmaf(fmaf(static_cast<float>(a3), 0.0078125f, static_cast<float>(a2)), dh[k] * xf, yh);
+        yg = fmaf(fmaf(static_cast<float>(a1), 0.0078125f, static_cast<float>(a0) * lf), dg[k] * xf, yg);
+        yh = fmaf(fmaf(static_cast<float>(a3), 0.0078125f, static_cast<float>(a2) * lf), dh[k] * xf, yh);
+        if (!hl) {
 #pragma unroll
-        for (int q = 0; q < NCH; ++q) {
-            const float X = xs[k * kCW * 8 + q * NS + sl];
-            yg = fmaf(-mg[k][q], X, yg);
-            yh = fmaf(-mh[k][q], X, yh);
+            for (int q = 0; q < NCH; ++q) {
+                const float X = xs[k * kCW * 8 + q * NS + sl];
+                yg = fmaf(-mg[k][q], X, yg);
+                yh = fmaf(-mh[k][q], X, yh);
+            }
         }
     }
 }
@@ -443,9 +458,10 @@ __device__ __forceinline__ void q4k_items(const uint8_t* blk, int wbox, uint32_t
 // is 1/s (16 dfac).
 template <int NP, int NI>
 __device__ __forceinline__ void q5k_items(const uint8_t* blk, int wbox, uint32_t wl, uint32_t xaddr, uint32_t xzero,
-                                          bool xv0, bool xv1, const float* df, const float* xs, int g, int sl,
+                                          bool xv0, bool xv1, const float* df, const float* xs, int g, int sl, int hl,
                                           float& yg, float& yh) {
-    constexpr int NS = 4 / NP, NCH = 8 / NS;
+    static_assert(NP == 1 || NP == 2, "vector pairs");
+    constexpr int NS = NP == 1 ? 2 : 1, NCH = 8 / NS;
     constexpr int BS = kCW * 176;  // stage bytes between the items
     constexpr int XS = kCW * 256;  // activation bytes between the items
     int scg[NI][NCH], sch[NI][NCH];
@@ -482,9 +498,10 @@ __device__ __forceinline__ void q5k_items(const uint8_t* blk, int wbox, uint32_t
             imma_u8s8_acc(D[k][(2 * p + 1) / NS], hi[0], hi[1], hi[2], hi[3], x[2], x[3]);
         }
     }
+    const float lf = hl ? 6.103515625e-05f : 1.f;  // limb weights (see q4k_items)
 #pragma unroll
     for (int k = 0; k < NI; ++k) {
-        int a0 = 0, a1 = 0, a2 = 0, a3 = 0;  // (g, limb 0), (g, limb 1), (g+8, l0), (g+8, l1)
+        int a0 = 0, a1 = 0, a2 = 0, a3 = 0;  // (g, col 0), (g, col 1), (g+8, col 0), (g+8, col 1)
 #pragma unroll
         for (int q = 0; q < NCH; ++q) {
             a0 += scg[k][q] * D[k][q][0];
@@ -493,13 +510,15 @@ __device__ __forceinline__ void q5k_items(const uint8_t* blk, int wbox, uint32_t
             a3 += sch[k][q] * D[k][q][3];
         }
         const float xf = 16.f * df[k * kCW];
-        yg = fmaf(fmaf(static_cast<float>(a1), 0.0078125f, static_cast<float>(a0)), dg[k] * xf, yg);
-        yh = fmaf(fmaf(static_cast<float>(a3), 0.0078125f, static_cast<float>(a2)), dh[k] * xf, yh);
+        yg = fmaf(fmaf(static_cast<float>(a1), 0.0078125f, static_cast<float>(a0) * lf), dg[k] * xf, yg);
+        yh = fmaf(fmaf(static_cast<float>(a3), 0.0078125f, static_cast<float>(a2) * lf), dh[k] * xf, yh);
+        if (!hl) {
 #pragma unroll
-        for (int q = 0; q < NCH; ++q) {
-            const float X = xs[k * kCW * 8 + q * NS + sl];
-            yg = fmaf(-mg[k][q], X, yg);
-            yh = fmaf(-mh[k][q], X, yh);
+            for (int q = 0; q < NCH; ++q) {
+                const float X = xs[k * kCW * 8 + q * NS + sl];
+                yg = fmaf(-mg[k][q], X, yg);
+                yh = fmaf(-mh[k][q], X, yh);
+            }
         }
     }
 }
@@ -544,17 +563,20 @@ __device__ __forceinline__ void q6k_groups(uint32_t ql0, uint32_t ql1, uint32_t 
 // sits at any even offset in shared memory: the A fragments come from aligned
 // 32-bit loads and a funnel shift (ldmatrix needs 16-byte rows). MMA i covers
 // elements 32i .. 32i+31, i.e. the 16-element sub-blocks 2i (k 0..15) and
-// 2i+1 (k 16..31). As for Q4_K, the 8 B columns are NS = 4/NP sub-block slots
-// x NP vectors x 2 limbs; sub-block j uses slot j % NS of chain j / NS, its
-// B rows are real only in its slot's columns, so NS sub-blocks share one
-// fragment without mixing. Lane (g, c) scales the chains' slot c / NP: the
-// sub-blocks j = q NS + sl of rows g and g + 8, with their int8 scales in
-// integer. The -32 offset of every quant is applied through the exact
-// 16-element sums of x: sum sc (q - 32) x = sum sc q x - 32 sum sc X.
+// 2i+1 (k 16..31). As for Q4_K (NP = 1 or 2), the 8 B columns are two
+// (slot, vector) pairs of limbs 0..2 and a zero column, NS = 2 / NP slots;
+// sub-block j uses slot j % NS of chain j / NS, its B rows are real only in
+// its slot's columns, so NS sub-blocks share one fragment without mixing.
+// Lane (g, c) scales the chains' slot sl: the sub-blocks j = q NS + sl of
+// rows g and g + 8, with their int8 scales in integer. The -32 offset of
+// every quant is applied through the exact 16-element sums of x:
+// sum sc (q - 32) x = sum sc q x - 32 sum sc X (by the hl = 0 lane of a pair).
 template <int NP>
 __device__ __forceinline__ void q6k_item(const uint8_t* pg, const uint8_t* ph, uint32_t xaddr, uint32_t xzero,
-                                         bool xv, float xf, const float* xs, int c, int sl, float& yg, float& yh) {
-    constexpr int NS = 4 / NP, NCH = 16 / NS, NCHH = NCH / 2;  // chains per half-block
+                                         bool xv, float xf, const float* xs, int c, int sl, int hl, float& yg,
+                                         float& yh) {
+    static_assert(NP == 1 || NP == 2, "vector pairs");
+    constexpr int NS = NP == 1 ? 2 : 1, NCH = 16 / NS, NCHH = NCH / 2;  // chains per half-block
     // |D| <= 16 * 63 * 127 per sub-block; times |sc| <= 128, summed over the
     // lane's 4, 8 or 16 sub-blocks: well inside int32
     int a0 = 0, a1 = 0, a2 = 0, a3 = 0;
@@ -578,7 +600,7 @@ __device__ __forceinline__ void q6k_item(const uint8_t* pg, const uint8_t* ph, u
             uint32_t x[4];
             ldmatrix_x4_at(x, xv ? xaddr + 64 * p : xzero);
             if constexpr (NS == 1) {
-                // one slot (4 vectors): the two 16-element sub-blocks of an MMA
+                // one slot (a vector pair): the two 16-element sub-blocks of an MMA
                 // step cannot share its columns, so each gets its own MMA with
                 // the other half of the A fragment zero
                 imma_u8s8_acc(D[4 * pp], A[0][2 * pp], A[1][2 * pp], 0u, 0u, x[0], x[1]);
@@ -607,22 +629,25 @@ __device__ __forceinline__ void q6k_item(const uint8_t* pg, const uint8_t* ph, u
         }
     }
     const float dg = f16_bits_to_f32(lds_u16(pg + 208)), dh = f16_bits_to_f32(lds_u16(ph + 208));
-    yg = fmaf(dg, fmaf(fmaf(static_cast<float>(a1), 0.0078125f, static_cast<float>(a0)), xf, -32.f * sg), yg);
-    yh = fmaf(dh, fmaf(fmaf(static_cast<float>(a3), 0.0078125f, static_cast<float>(a2)), xf, -32.f * sh), yh);
+    const float lf = hl ? 6.103515625e-05f : 1.f;  // limb weights (see q4k_items)
+    const float mf = hl ? 0.f : -32.f;             // the offset once per pair
+    yg = fmaf(dg, fmaf(fmaf(static_cast<float>(a1), 0.0078125f, static_cast<float>(a0) * lf), xf, mf * sg), yg);
+    yh = fmaf(dh, fmaf(fmaf(static_cast<float>(a3), 0.0078125f, static_cast<float>(a2) * lf), xf, mf * sh), yh);
 }
 
 // One Q8_0 / Q4_0 item: 16 rows x one group of 8 blocks (256 elements, one x
-// scale), for NP = N rounded up to a power of two. Each 32-element block is
-// one MMA on the signed quants as they are; as for Q4_K, NS = 4/NP blocks
-// share an accumulator through the B-column slots (block j: slot j % NS,
-// chain j / NS), and lane (g, c) scales its slot's blocks j = q NS + sl of
-// rows g and g + 8 by their f16 d in f32. Blocks are 34 (18) bytes, so they
+// scale), for NP = 1 or 2 vectors. Each 32-element block is one MMA on the
+// signed quants as they are; as for Q4_K, NS = 2/NP blocks share an
+// accumulator through the B-column slots (block j: slot j % NS, chain j / NS),
+// and lane (g, c) scales its slot's blocks j = q NS + sl of rows g and g + 8
+// by their f16 d in f32. Blocks are 34 (18) bytes, so they
 // sit 2-byte aligned in shared memory: aligned 32-bit loads and a funnel
 // shift. Q4_0's nibbles enter as s8 q - 8 (a 4-bit sign extension).
 template <int NP, int TYPE>
 __device__ __forceinline__ void q8_item(const uint8_t* pg, const uint8_t* ph, uint32_t xaddr, uint32_t xzero,
-                                        bool xv0, bool xv1, float xf, int c, int sl, float& yg, float& yh) {
-    constexpr int NS = 4 / NP, NCH = 8 / NS;
+                                        bool xv0, bool xv1, float xf, int c, int sl, int hl, float& yg, float& yh) {
+    static_assert(NP == 1 || NP == 2, "vector pairs");
+    constexpr int NS = NP == 1 ? 2 : 1, NCH = 8 / NS;
     constexpr int BB = TYPE == kTypeQ4_0 ? 18 : 34;  // block bytes
     int D[NCH][4];
 #pragma unroll
@@ -649,13 +674,14 @@ __device__ __forceinline__ void q8_item(const uint8_t* pg, const uint8_t* ph, ui
         }
     }
     // |D| <= 32 * 127 * 127 per block
+    const float lf = hl ? 6.103515625e-05f : 1.f;  // limb weights (see q4k_items)
     float ag = 0.f, ah = 0.f;
 #pragma unroll
     for (int q = 0; q < NCH; ++q) {
         const int j = q * NS + sl;
         const float dg = f16_bits_to_f32(lds_u16(pg + BB * j)), dh = f16_bits_to_f32(lds_u16(ph + BB * j));
-        ag = fmaf(fmaf(static_cast<float>(D[q][1]), 0.0078125f, static_cast<float>(D[q][0])), dg, ag);
-        ah = fmaf(fmaf(static_cast<float>(D[q][3]), 0.0078125f, static_cast<float>(D[q][2])), dh, ah);
+        ag = fmaf(fmaf(static_cast<float>(D[q][1]), 0.0078125f, static_cast<float>(D[q][0]) * lf), dg, ag);
+        ah = fmaf(fmaf(static_cast<float>(D[q][3]), 0.0078125f, static_cast<float>(D[q][2]) * lf), dh, ah);
     }
     yg = fmaf(ag, xf, yg);
     yh = fmaf(ah, xf, yh);
@@ -876,21 +902,25 @@ __device__ __forceinline__ void stage_activations(const OpInfo& op, uint8_t* xsm
 #pragma unroll
             for (int o = 8; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));  // within the half
             const float sc = mx > 0.f ? 127.f / mx : 0.f;
-            // l0 = rint(x s) (|l0| <= 127), l1 = rint(128 (x s - l0)) (|l1| <= 64)
-            uint32_t p0[4], p1[4];
+            // l0 = rint(x s) (|l0| <= 127), l1 = rint(r1) with r1 = 128 (x s - l0)
+            // (|l1| <= 65), l2 = rint(128 (r1 - l1)) (|l2| <= 64). fmaf takes the
+            // exact product x s; r1 - l1 and the scalings by 128 are exact.
+            uint32_t p0[4], p1[4], p2[4];
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
                 const float e[4] = {v[r][k].x, v[r][k].y, v[r][k].z, v[r][k].w};
-                int b0[4], b1[4];
+                int b0[4], b1[4], b2[4];
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
-                    float l0;
+                    float l0, l1, l2;
                     b0[j] = round_low_byte(__fmul_rn(e[j], sc), l0);
-                    float l1;
-                    b1[j] = round_low_byte(fmaf(e[j], sc, -l0) * 128.f, l1);
+                    const float r1 = fmaf(e[j], sc, -l0) * 128.f;
+                    b1[j] = round_low_byte(r1, l1);
+                    b2[j] = round_low_byte(__fsub_rn(r1, l1) * 128.f, l2);
                 }
                 p0[k] = pack_b4(b0[0], b0[1], b0[2], b0[3]);
                 p1[k] = pack_b4(b1[0], b1[1], b1[2], b1[3]);
+                p2[k] = pack_b4(b2[0], b2[1], b2[2], b2[3]);
             }
             float a16 = 0.f;  // a lane's 16 elements: one Q6_K sub-block
 #pragma unroll
@@ -898,9 +928,10 @@ __device__ __forceinline__ void stage_activations(const OpInfo& op, uint8_t* xsm
             const float a = a16 + __shfl_xor_sync(0xffffffffu, a16, 1);  // a Q4_K sub-block is two lanes
             if (act[r]) {
                 const int tt = t[r], bb = b[r];
-                uint8_t* c0 = xsm + (2 * tt) * XS + bb * 256 + 16 * h;
+                uint8_t* c0 = xsm + (kLimbs * tt) * XS + bb * 256 + 16 * h;
                 *reinterpret_cast<uint4*>(c0) = make_uint4(p0[0], p0[1], p0[2], p0[3]);
                 *reinterpret_cast<uint4*>(c0 + XS) = make_uint4(p1[0], p1[1], p1[2], p1[3]);
+                *reinterpret_cast<uint4*>(c0 + 2 * XS) = make_uint4(p2[0], p2[1], p2[2], p2[3]);
                 X16[tt * (K / 16) + bb * 16 + h] = a16;
                 if ((h & 1) == 0) Xs[tt * (K / 32) + bb * 8 + (h >> 1)] = a;
                 if (h == 0) dfac[tt * nblk + bb] = mx * (1.f / 2032.f);  // 1 / (16 s)
@@ -938,62 +969,72 @@ struct Ring {
     }
 };
 
-// Per-op constants of a consumer lane on the Q4_K path (see q4k_item).
+// Per-op constants of a consumer lane on the Q4_K path (see q4k_items), for
+// one vector pair: NP = 1 (one vector) or 2 (vectors 2G, 2G + 1).
 struct Q4Lane {
     uint32_t wl;        // weights ldmatrix row offset in a stage
     uint32_t xcol;      // activations ldmatrix row address (block 0, pair 0)
     bool xv0, xv1;      // that row is real (not the zero row) for even / odd pairs
     const float* dfac;  // d-factors of vector tk
     const float* Xs;    // sub-block sums of vector tk
-    int sl, tk;         // slot and vector of the lane's accumulator columns
+    int sl, tk, hl;     // slot, vector and limb half of the lane's accumulator columns
 };
 
+// B column rr of an MMA (0..7) is limb rr & 3 (3: the zero column) of pair
+// rr >> 2: slot rr >> 2 of vector 2G at NP = 1, vector 2G + (rr >> 2) at NP = 2.
 template <int NP>
-__device__ __forceinline__ Q4Lane q4k_lane(const OpInfo& op, const uint8_t* xsm, int lane) {
-    constexpr int NS = 4 / NP;
+__device__ __forceinline__ Q4Lane q4k_lane(const OpInfo& op, const uint8_t* xsm, int lane, int G) {
+    constexpr int NS = NP == 1 ? 2 : 1;
     const int K = op.K, N = op.N, XS = img_col_bytes(K), nblocks = K / 256;
     const int c = lane & 3;
     Q4Lane q;
-    q.sl = c / NP;
-    q.tk = c % NP;
+    q.sl = NP == 1 ? c >> 1 : 0;
+    q.tk = (NP == 1 ? 0 : c >> 1) + 2 * G;
+    q.hl = c & 1;
     // weights ldmatrix: matrix lane/8 = rows 0-7 / 8-15 of the pair's 16-byte chunk 0 / 1
     q.wl = static_cast<uint32_t>(((lane & 7) + 8 * ((lane >> 3) & 1)) * op.wbox + 16 + 16 * (lane >> 4));
     // activations ldmatrix: matrix mi = lane/8 (0, 1: b0, b1 of the low-nibble
     // sub-block of a pair; 2, 3: of the high one), row rr = lane%8 = B column
     const int mi = lane >> 3, rr = lane & 7;
-    const int slot_r = rr / (2 * NP), t_r = (rr >> 1) % NP, l_r = rr & 1;
-    q.xv0 = t_r < N && slot_r == (mi >> 1) % NS;        // even pairs
-    q.xv1 = t_r < N && slot_r == (2 + (mi >> 1)) % NS;  // odd pairs
-    q.xcol = smem_u32(xsm) + static_cast<uint32_t>((2 * t_r + l_r) * XS + 16 * mi);
+    const int u_r = rr >> 2, l_r = rr & 3;
+    const int slot_r = NP == 1 ? u_r : 0, t_r = (NP == 1 ? 0 : u_r) + 2 * G;
+    const bool real = l_r < kLimbs && t_r < N;
+    q.xv0 = real && slot_r == (mi >> 1) % NS;        // even pairs
+    q.xv1 = real && slot_r == (2 + (mi >> 1)) % NS;  // odd pairs
+    q.xcol = smem_u32(xsm) + static_cast<uint32_t>((kLimbs * (real ? t_r : 0) + (real ? l_r : 0)) * XS + 16 * mi);
     const int tkc = q.tk < N ? q.tk : 0;
     q.dfac = reinterpret_cast<const float*>(xsm + img_inv_off(K, N)) + tkc * nblocks;
     q.Xs = reinterpret_cast<const float*>(xsm + img_sum_off(K, N)) + tkc * (K / 32);
     return q;
 }
 
-// Per-op constants of a consumer lane on the Q6_K path (see q6k_item).
+// Per-op constants of a consumer lane on the Q6_K path (see q6k_item), for
+// one vector pair as in q4k_lane.
 struct Q6Lane {
     uint32_t xcol;      // activations ldmatrix row address (block 0, pair 0)
     bool xv;            // that row is real (not the zero row)
     const float* dfac;  // d-factors of vector tk
     const float* X16;   // 16-element sub-block sums of vector tk
-    int sl, tk;         // slot and vector of the lane's accumulator columns
+    int sl, tk, hl;     // slot, vector and limb half of the lane's accumulator columns
 };
 
 template <int NP>
-__device__ __forceinline__ Q6Lane q6k_lane(const OpInfo& op, const uint8_t* xsm, int lane) {
-    constexpr int NS = 4 / NP;
+__device__ __forceinline__ Q6Lane q6k_lane(const OpInfo& op, const uint8_t* xsm, int lane, int G) {
+    constexpr int NS = NP == 1 ? 2 : 1;
     const int K = op.K, N = op.N, XS = img_col_bytes(K);
     const int c = lane & 3;
     Q6Lane q;
-    q.sl = c / NP;
-    q.tk = c % NP;
+    q.sl = NP == 1 ? c >> 1 : 0;
+    q.tk = (NP == 1 ? 0 : c >> 1) + 2 * G;
+    q.hl = c & 1;
     // matrix mi = lane/8 of a pair's ldmatrix is sub-block 4p + mi (k half
     // mi&1 of MMA 2p + mi/2), slot mi % NS; row rr = lane%8 = B column
     const int mi = lane >> 3, rr = lane & 7;
-    const int slot_r = rr / (2 * NP), t_r = (rr >> 1) % NP, l_r = rr & 1;
-    q.xv = t_r < N && slot_r == mi % NS;
-    q.xcol = smem_u32(xsm) + static_cast<uint32_t>((2 * t_r + l_r) * XS + 16 * mi);
+    const int u_r = rr >> 2, l_r = rr & 3;
+    const int slot_r = NP == 1 ? u_r : 0, t_r = (NP == 1 ? 0 : u_r) + 2 * G;
+    const bool real = l_r < kLimbs && t_r < N;
+    q.xv = real && slot_r == mi % NS;
+    q.xcol = smem_u32(xsm) + static_cast<uint32_t>((kLimbs * (real ? t_r : 0) + (real ? l_r : 0)) * XS + 16 * mi);
     const int tkc = q.tk < N ? q.tk : 0;
     q.dfac = reinterpret_cast<const float*>(xsm + img_inv_off(K, N)) + tkc * (K / 256);
     q.X16 = reinterpret_cast<const float*>(xsm + img_sum16_off(K, N)) + tkc * (K / 16);
@@ -1015,69 +1056,46 @@ __device__ __forceinline__ void ring_wait(Ring& R, int lane) {
     mbar_wait_warp(&R.full[R.slot], R.phase, 2u, R.poisoned, lane);
 }
 
-// All segments of one Q4_K unit for this consumer warp; writes the warp's
-// partial sums of the unit's 16 rows (zeros where it had no item) to ub.
-template <int NP, int NT>
-__device__ __forceinline__ void q4k_unit(const OpRegs& op, const Q4Lane& q, Ring& R, uint32_t xzero, int lane,
-                                         int cw, float* ub) {
-    const int N = op.N, nblocks = op.K / 256;
-    const int g = lane >> 2, sl = q.sl, tk = q.tk;
-    const uint32_t wl = q.wl, xcol = q.xcol;
-    const bool xv0 = q.xv0, xv1 = q.xv1;
-    const float* dfac = q.dfac;
-    const float* Xs = q.Xs;
-    float yg = 0.f, yh = 0.f;  // slot sl's part of vector tk, rows g and g + 8
-    for (int sg = 0; sg < op.nseg; ++sg) {
-        const int b0 = sg * op.seg_blocks;
-        const int nb = min(op.seg_blocks, nblocks - b0);
-        // this warp's first item of the segment; a warp without one neither
-        // waits for nor releases the stage (the warp with item 0 releases it
-        // for them)
-        const int i0 = (cw - static_cast<int>(R.item_base % kCW) + kCW) % kCW;
-        if (i0 < nb) {
-            ring_wait(R, lane);
-            const uint8_t* stage = R.stages + R.slot * R.SB;
-            int i = i0;
-            // item pairs at N = 1 (at N = 2 the doubled accumulators would spill)
-            for (; NP == 1 && i + kCW < nb; i += 2 * kCW) {
-                const int bg = b0 + i;
-                q4k_items<NP, 2>(stage + i * 144, op.wbox, wl, xcol + bg * 256, xzero, xv0, xv1, dfac + bg,
-                                 Xs + bg * 8, g, sl, yg, yh);
-            }
-            for (; i < nb; i += kCW) {
-                const int bg = b0 + i;
-                q4k_items<NP, 1>(stage + i * 144, op.wbox, wl, xcol + bg * 256, xzero, xv0, xv1, dfac + bg,
-                                 Xs + bg * 8, g, sl, yg, yh);
-            }
-            __syncwarp();
-            if (lane == 0) mbar_arrive_cnt(&R.empty[R.slot], i0 == 0 ? 1u + kCW - min(nb, kCW) : 1u);
-        }
-        R.item_base += nb;
-        R.advance();
-    }
-    // sum the slots of each vector (lanes c with the same c % NP)
+// Sums a lane's partial rows over the lanes of its vector and writes them to
+// the warp's unit buffer: at one vector all four lanes of a row group hold
+// parts of it (two slots x two limb halves), at two or four the lane pair
+// 2u, 2u + 1 (two limb halves).
+template <int NP, int NT, int NG>
+__device__ __forceinline__ void write_partials(float (&yg)[NG], float (&yh)[NG], const int (&tk)[NG], int N, int lane,
+                                               float* ub) {
+    const int g = lane >> 2;
 #pragma unroll
-    for (int o = NP; o < 4; o <<= 1) {
-        yg += __shfl_xor_sync(0xffffffffu, yg, o);
-        yh += __shfl_xor_sync(0xffffffffu, yh, o);
-    }
-    if (sl == 0 && tk < N) {
-        ub[g * NT + tk] = yg;
-        ub[(g + 8) * NT + tk] = yh;
+    for (int G = 0; G < NG; ++G) {
+        yg[G] += __shfl_xor_sync(0xffffffffu, yg[G], 1);
+        yh[G] += __shfl_xor_sync(0xffffffffu, yh[G], 1);
+        if (NP == 1) {
+            yg[G] += __shfl_xor_sync(0xffffffffu, yg[G], 2);
+            yh[G] += __shfl_xor_sync(0xffffffffu, yh[G], 2);
+        }
+        const bool writer = NP == 1 ? (lane & 3) == 0 : (lane & 1) == 0;
+        if (writer && tk[G] < N) {
+            ub[g * NT + tk[G]] = yg[G];
+            ub[(g + 8) * NT + tk[G]] = yh[G];
+        }
     }
 }
 
-// All segments of one Q5_K unit for this consumer warp (see q4k_unit).
-template <int NP, int NT>
-__device__ __forceinline__ void q5k_unit(const OpRegs& op, const Q4Lane& q, Ring& R, uint32_t xzero, int lane,
-                                         int cw, float* ub) {
+// All segments of one Q4_K (Q5_K with Q5 = true) unit for this consumer
+// warp; writes the warp's partial sums of the unit's 16 rows (zeros where it
+// had no item) to ub. Four vectors take two passes over each item, one per
+// vector pair (qa, qb).
+template <int NP, int NT, bool Q5>
+__device__ __forceinline__ void q4k_unit(const OpRegs& op, const Q4Lane& qa, const Q4Lane& qb, Ring& R,
+                                         uint32_t xzero, int lane, int cw, float* ub) {
+    constexpr int NPI = NP == 1 ? 1 : 2;  // vectors per pass
+    constexpr int NG = NP == 4 ? 2 : 1;   // passes
+    constexpr int BB = Q5 ? 176 : 144;
     const int N = op.N, nblocks = op.K / 256;
-    const int g = lane >> 2, sl = q.sl, tk = q.tk;
-    const uint32_t wl = q.wl, xcol = q.xcol;
-    const bool xv0 = q.xv0, xv1 = q.xv1;
-    const float* dfac = q.dfac;
-    const float* Xs = q.Xs;
-    float yg = 0.f, yh = 0.f;  // slot sl's part of vector tk, rows g and g + 8
+    const int g = lane >> 2;
+    const Q4Lane qs[2] = {qa, qb};
+    float yg[NG], yh[NG];  // the lane's columns of rows g and g + 8, per pass
+#pragma unroll
+    for (int G = 0; G < NG; ++G) yg[G] = yh[G] = 0.f;
     for (int sg = 0; sg < op.nseg; ++sg) {
         const int b0 = sg * op.seg_blocks;
         const int nb = min(op.seg_blocks, nblocks - b0);
@@ -1092,13 +1110,26 @@ __device__ __forceinline__ void q5k_unit(const OpRegs& op, const Q4Lane& q, Ring
             // item pairs at N = 1 (at N = 2 the doubled accumulators would spill)
             for (; NP == 1 && i + kCW < nb; i += 2 * kCW) {
                 const int bg = b0 + i;
-                q5k_items<NP, 2>(stage + i * 176, op.wbox, wl, xcol + bg * 256, xzero, xv0, xv1, dfac + bg,
-                                 Xs + bg * 8, g, sl, yg, yh);
+                const Q4Lane& q = qs[0];
+                if (Q5)
+                    q5k_items<1, 2>(stage + i * BB, op.wbox, q.wl, q.xcol + bg * 256, xzero, q.xv0, q.xv1,
+                                    q.dfac + bg, q.Xs + bg * 8, g, q.sl, q.hl, yg[0], yh[0]);
+                else
+                    q4k_items<1, 2>(stage + i * BB, op.wbox, q.wl, q.xcol + bg * 256, xzero, q.xv0, q.xv1,
+                                    q.dfac + bg, q.Xs + bg * 8, g, q.sl, q.hl, yg[0], yh[0]);
             }
             for (; i < nb; i += kCW) {
                 const int bg = b0 + i;
-                q5k_items<NP, 1>(stage + i * 176, op.wbox, wl, xcol + bg * 256, xzero, xv0, xv1, dfac + bg,
-                                 Xs + bg * 8, g, sl, yg, yh);
+#pragma unroll
+                for (int G = 0; G < NG; ++G) {
+                    const Q4Lane& q = qs[G];
+                    if (Q5)
+                        q5k_items<NPI, 1>(stage + i * BB, op.wbox, q.wl, q.xcol + bg * 256, xzero, q.xv0, q.xv1,
+                                          q.dfac + bg, q.Xs + bg * 8, g, q.sl, q.hl, yg[G], yh[G]);
+                    else
+                        q4k_items<NPI, 1>(stage + i * BB, op.wbox, q.wl, q.xcol + bg * 256, xzero, q.xv0, q.xv1,
+                                          q.dfac + bg, q.Xs + bg * 8, g, q.sl, q.hl, yg[G], yh[G]);
+                }
             }
             __syncwarp();
             if (lane == 0) mbar_arrive_cnt(&R.empty[R.slot], i0 == 0 ? 1u + kCW - min(nb, kCW) : 1u);
@@ -1106,32 +1137,27 @@ __device__ __forceinline__ void q5k_unit(const OpRegs& op, const Q4Lane& q, Ring
         R.item_base += nb;
         R.advance();
     }
-    // sum the slots of each vector (lanes c with the same c % NP)
+    int tk[NG];
 #pragma unroll
-    for (int o = NP; o < 4; o <<= 1) {
-        yg += __shfl_xor_sync(0xffffffffu, yg, o);
-        yh += __shfl_xor_sync(0xffffffffu, yh, o);
-    }
-    if (sl == 0 && tk < N) {
-        ub[g * NT + tk] = yg;
-        ub[(g + 8) * NT + tk] = yh;
-    }
+    for (int G = 0; G < NG; ++G) tk[G] = qs[G].tk;
+    write_partials<NP, NT, NG>(yg, yh, tk, N, lane, ub);
 }
 
 // All segments of one Q6_K unit for this consumer warp (see q4k_unit). Each
 // row's copy window starts at its segment start rounded down to 16 bytes;
 // glo is the low word of the unit's first row address.
 template <int NP, int NT>
-__device__ __forceinline__ void q6k_unit(const OpRegs& op, const Q6Lane& q, Ring& R, uint32_t xzero, uint32_t glo,
-                                         int lane, int cw, float* ub) {
+__device__ __forceinline__ void q6k_unit(const OpRegs& op, const Q6Lane& qa, const Q6Lane& qb, Ring& R,
+                                         uint32_t xzero, uint32_t glo, int lane, int cw, float* ub) {
+    constexpr int NPI = NP == 1 ? 1 : 2;  // vectors per pass
+    constexpr int NG = NP == 4 ? 2 : 1;   // passes
     const int N = op.N, nblocks = op.K / 256;
-    const int g = lane >> 2, c = lane & 3, sl = q.sl, tk = q.tk;
+    const int g = lane >> 2, c = lane & 3;
     const uint32_t nb1 = static_cast<uint32_t>(op.w_nb1);
-    const uint32_t xcol = q.xcol;
-    const bool xv = q.xv;
-    const float* dfac = q.dfac;
-    const float* X16 = q.X16;
-    float yg = 0.f, yh = 0.f;
+    const Q6Lane qs[2] = {qa, qb};
+    float yg[NG], yh[NG];
+#pragma unroll
+    for (int G = 0; G < NG; ++G) yg[G] = yh[G] = 0.f;
     for (int sg = 0; sg < op.nseg; ++sg) {
         const int b0 = sg * op.seg_blocks;
         const int nb = min(op.seg_blocks, nblocks - b0);
@@ -1144,8 +1170,12 @@ __device__ __forceinline__ void q6k_unit(const OpRegs& op, const Q6Lane& q, Ring
             const uint8_t* ph = stage + (g + 8) * op.wbox + ((gl + static_cast<uint32_t>(g + 8) * nb1) & 15u);
             for (int i = i0; i < nb; i += kCW) {
                 const int bg = b0 + i;
-                q6k_item<NP>(pg + i * 210, ph + i * 210, xcol + bg * 256, xzero, xv, 16.f * dfac[bg], X16 + bg * 16,
-                             c, sl, yg, yh);
+#pragma unroll
+                for (int G = 0; G < NG; ++G) {
+                    const Q6Lane& q = qs[G];
+                    q6k_item<NPI>(pg + i * 210, ph + i * 210, q.xcol + bg * 256, xzero, q.xv, 16.f * q.dfac[bg],
+                                  q.X16 + bg * 16, c, q.sl, q.hl, yg[G], yh[G]);
+                }
             }
             __syncwarp();
             if (lane == 0) mbar_arrive_cnt(&R.empty[R.slot], i0 == 0 ? 1u + kCW - min(nb, kCW) : 1u);
@@ -1153,15 +1183,10 @@ __device__ __forceinline__ void q6k_unit(const OpRegs& op, const Q6Lane& q, Ring
         R.item_base += nb;
         R.advance();
     }
+    int tk[NG];
 #pragma unroll
-    for (int o = NP; o < 4; o <<= 1) {
-        yg += __shfl_xor_sync(0xffffffffu, yg, o);
-        yh += __shfl_xor_sync(0xffffffffu, yh, o);
-    }
-    if (sl == 0 && tk < N) {
-        ub[g * NT + tk] = yg;
-        ub[(g + 8) * NT + tk] = yh;
-    }
+    for (int G = 0; G < NG; ++G) tk[G] = qs[G].tk;
+    write_partials<NP, NT, NG>(yg, yh, tk, N, lane, ub);
 }
 
 // One thread: every other rank's count of this rank's sync points goes up by
@@ -1198,13 +1223,18 @@ __device__ bool tp_wait_peers(const uint32_t* const* sig, int world, int rank, u
 // All segments of one Q8_0 / Q4_0 unit for this consumer warp (see
 // q6k_unit); an item is a group of 8 blocks (segments hold whole groups).
 template <int NP, int NT, int TYPE>
-__device__ __forceinline__ void q8_unit(const OpRegs& op, const Q4Lane& q, Ring& R, uint32_t xzero, uint32_t glo,
-                                        int lane, int cw, float* ub) {
+__device__ __forceinline__ void q8_unit(const OpRegs& op, const Q4Lane& qa, const Q4Lane& qb, Ring& R,
+                                        uint32_t xzero, uint32_t glo, int lane, int cw, float* ub) {
+    constexpr int NPI = NP == 1 ? 1 : 2;  // vectors per pass
+    constexpr int NG = NP == 4 ? 2 : 1;   // passes
     constexpr int BB = TYPE == kTypeQ4_0 ? 18 : 34;  // block bytes
     const int N = op.N, nblocks = op.K / 32;
-    const int g = lane >> 2, c = lane & 3, sl = q.sl, tk = q.tk;
+    const int g = lane >> 2, c = lane & 3;
     const uint32_t nb1 = static_cast<uint32_t>(op.w_nb1);
-    float yg = 0.f, yh = 0.f;
+    const Q4Lane qs[2] = {qa, qb};
+    float yg[NG], yh[NG];
+#pragma unroll
+    for (int G = 0; G < NG; ++G) yg[G] = yh[G] = 0.f;
     for (int sg = 0; sg < op.nseg; ++sg) {
         const int b0 = sg * op.seg_blocks;
         const int ng = (min(op.seg_blocks, nblocks - b0) + 7) / 8;  // groups of this segment
@@ -1217,8 +1247,12 @@ __device__ __forceinline__ void q8_unit(const OpRegs& op, const Q4Lane& q, Ring&
             const uint8_t* ph = stage + (g + 8) * op.wbox + ((gl + static_cast<uint32_t>(g + 8) * nb1) & 15u);
             for (int i = i0; i < ng; i += kCW) {
                 const int gg = b0 / 8 + i;  // 256-element group
-                q8_item<NP, TYPE>(pg + i * 8 * BB, ph + i * 8 * BB, q.xcol + gg * 256, xzero, q.xv0, q.xv1,
-                                  16.f * q.dfac[gg], c, sl, yg, yh);
+#pragma unroll
+                for (int G = 0; G < NG; ++G) {
+                    const Q4Lane& q = qs[G];
+                    q8_item<NPI, TYPE>(pg + i * 8 * BB, ph + i * 8 * BB, q.xcol + gg * 256, xzero, q.xv0, q.xv1,
+                                       16.f * q.dfac[gg], c, q.sl, q.hl, yg[G], yh[G]);
+                }
             }
             __syncwarp();
             if (lane == 0) mbar_arrive_cnt(&R.empty[R.slot], i0 == 0 ? 1u + kCW - min(ng, kCW) : 1u);
@@ -1226,15 +1260,10 @@ __device__ __forceinline__ void q8_unit(const OpRegs& op, const Q4Lane& q, Ring&
         R.item_base += ng;
         R.advance();
     }
+    int tk[NG];
 #pragma unroll
-    for (int o = NP; o < 4; o <<= 1) {
-        yg += __shfl_xor_sync(0xffffffffu, yg, o);
-        yh += __shfl_xor_sync(0xffffffffu, yh, o);
-    }
-    if (sl == 0 && tk < N) {
-        ub[g * NT + tk] = yg;
-        ub[(g + 8) * NT + tk] = yh;
-    }
+    for (int G = 0; G < NG; ++G) tk[G] = qs[G].tk;
+    write_partials<NP, NT, NG>(yg, yh, tk, N, lane, ub);
 }
 
 // PRO: the fused activation prologue (kProNone for the plain GEMV; each kind
@@ -1423,8 +1452,8 @@ __global__ void __launch_bounds__(kThreads, 1) stream_gemv_kernel(const __grid_c
     int next_begin = -1;     // first unit of the next op
     int uslot = 0, own = 0;  // useq % kUnitSlots, useq % kCW
     OpRegs op{};
-    Q4Lane q4{};
-    Q6Lane q6{};
+    Q4Lane q4{}, q4b{};  // vector pairs 0 and 1 (the second only at 3 or 4 vectors)
+    Q6Lane q6{}, q6b{};
     // Sums the 8 warps' partials of this CTA's unit number j (fixed order:
     // deterministic) and writes its rows; done by the unit's owner warp
     // kRedDelay units later, when the other warps are normally long done.
@@ -1463,12 +1492,14 @@ __global__ void __launch_bounds__(kThreads, 1) stream_gemv_kernel(const __grid_c
                 if (ct == 0 && useq == 0) mbar_arrive_cnt(xready, 1u);  // the copy warp may go on
                 staged = oi;
             }
-            if (oo.type != kTypeQ6_K)
-                q4 = (NT == 1 || oo.N == 1) ? q4k_lane<1>(oo, xsm, lane)
-                                            : ((NT == 2 || oo.N == 2) ? q4k_lane<2>(oo, xsm, lane) : q4k_lane<4>(oo, xsm, lane));
-            if (oo.type == kTypeQ6_K)
-                q6 = (NT == 1 || oo.N == 1) ? q6k_lane<1>(oo, xsm, lane)
-                                            : ((NT == 2 || oo.N == 2) ? q6k_lane<2>(oo, xsm, lane) : q6k_lane<4>(oo, xsm, lane));
+            const bool one = NT == 1 || oo.N == 1;
+            if (oo.type != kTypeQ6_K) {
+                q4 = one ? q4k_lane<1>(oo, xsm, lane, 0) : q4k_lane<2>(oo, xsm, lane, 0);
+                if (NT == 4 && oo.N > 2) q4b = q4k_lane<2>(oo, xsm, lane, 1);
+            } else {
+                q6 = one ? q6k_lane<1>(oo, xsm, lane, 0) : q6k_lane<2>(oo, xsm, lane, 0);
+                if (NT == 4 && oo.N > 2) q6b = q6k_lane<2>(oo, xsm, lane, 1);
+            }
             op = op_regs(oo);
             next_begin = oi + 1 < n_ops ? T.op[oi + 1].unit_begin : total;
         }
@@ -1482,47 +1513,47 @@ __global__ void __launch_bounds__(kThreads, 1) stream_gemv_kernel(const __grid_c
         if (op.type == kTypeQ4_K) {
             // ================= Q4_K, integer tensor cores =================
             if (NT == 1 || N == 1)
-                q4k_unit<1, NT>(op, q4, R, smem_u32(zrow), lane, cw, ub);
+                q4k_unit<1, NT, false>(op, q4, q4b, R, smem_u32(zrow), lane, cw, ub);
             else if (NT == 2 || N == 2)
-                q4k_unit<2, NT>(op, q4, R, smem_u32(zrow), lane, cw, ub);
+                q4k_unit<2, NT, false>(op, q4, q4b, R, smem_u32(zrow), lane, cw, ub);
             else if constexpr (NT == 4)
-                q4k_unit<4, NT>(op, q4, R, smem_u32(zrow), lane, cw, ub);
+                q4k_unit<4, NT, false>(op, q4, q4b, R, smem_u32(zrow), lane, cw, ub);
         } else if (op.type == kTypeQ5_K) {
             // ================= Q5_K, integer tensor cores =================
             if (NT == 1 || N == 1)
-                q5k_unit<1, NT>(op, q4, R, smem_u32(zrow), lane, cw, ub);
+                q4k_unit<1, NT, true>(op, q4, q4b, R, smem_u32(zrow), lane, cw, ub);
             else if (NT == 2 || N == 2)
-                q5k_unit<2, NT>(op, q4, R, smem_u32(zrow), lane, cw, ub);
+                q4k_unit<2, NT, true>(op, q4, q4b, R, smem_u32(zrow), lane, cw, ub);
             else if constexpr (NT == 4)
-                q5k_unit<4, NT>(op, q4, R, smem_u32(zrow), lane, cw, ub);
+                q4k_unit<4, NT, true>(op, q4, q4b, R, smem_u32(zrow), lane, cw, ub);
         } else if (op.type == kTypeQ6_K) {
             // ================= Q6_K, integer tensor cores =================
             const uint32_t glo =
                 static_cast<uint32_t>(reinterpret_cast<uintptr_t>(op.w + static_cast<int64_t>(r0) * op.w_nb1));
             if (NT == 1 || N == 1)
-                q6k_unit<1, NT>(op, q6, R, smem_u32(zrow), glo, lane, cw, ub);
+                q6k_unit<1, NT>(op, q6, q6b, R, smem_u32(zrow), glo, lane, cw, ub);
             else if (NT == 2 || N == 2)
-                q6k_unit<2, NT>(op, q6, R, smem_u32(zrow), glo, lane, cw, ub);
+                q6k_unit<2, NT>(op, q6, q6b, R, smem_u32(zrow), glo, lane, cw, ub);
             else if constexpr (NT == 4)
-                q6k_unit<4, NT>(op, q6, R, smem_u32(zrow), glo, lane, cw, ub);
+                q6k_unit<4, NT>(op, q6, q6b, R, smem_u32(zrow), glo, lane, cw, ub);
         } else {
             // ============= Q8_0 / Q4_0, integer tensor cores =============
             const uint32_t glo =
                 static_cast<uint32_t>(reinterpret_cast<uintptr_t>(op.w + static_cast<int64_t>(r0) * op.w_nb1));
             if (op.type == kTypeQ4_0) {
                 if (NT == 1 || N == 1)
-                    q8_unit<1, NT, kTypeQ4_0>(op, q4, R, smem_u32(zrow), glo, lane, cw, ub);
+                    q8_unit<1, NT, kTypeQ4_0>(op, q4, q4b, R, smem_u32(zrow), glo, lane, cw, ub);
                 else if (NT == 2 || N == 2)
-                    q8_unit<2, NT, kTypeQ4_0>(op, q4, R, smem_u32(zrow), glo, lane, cw, ub);
+                    q8_unit<2, NT, kTypeQ4_0>(op, q4, q4b, R, smem_u32(zrow), glo, lane, cw, ub);
                 else if constexpr (NT == 4)
-                    q8_unit<4, NT, kTypeQ4_0>(op, q4, R, smem_u32(zrow), glo, lane, cw, ub);
+                    q8_unit<4, NT, kTypeQ4_0>(op, q4, q4b, R, smem_u32(zrow), glo, lane, cw, ub);
             } else {
                 if (NT == 1 || N == 1)
-                    q8_unit<1, NT, kTypeQ8_0>(op, q4, R, smem_u32(zrow), glo, lane, cw, ub);
+                    q8_unit<1, NT, kTypeQ8_0>(op, q4, q4b, R, smem_u32(zrow), glo, lane, cw, ub);
                 else if (NT == 2 || N == 2)
-                    q8_unit<2, NT, kTypeQ8_0>(op, q4, R, smem_u32(zrow), glo, lane, cw, ub);
+                    q8_unit<2, NT, kTypeQ8_0>(op, q4, q4b, R, smem_u32(zrow), glo, lane, cw, ub);
                 else if constexpr (NT == 4)
-                    q8_unit<4, NT, kTypeQ8_0>(op, q4, R, smem_u32(zrow), glo, lane, cw, ub);
+                    q8_unit<4, NT, kTypeQ8_0>(op, q4, q4b, R, smem_u32(zrow), glo, lane, cw, ub);
             }
         }
         // ---- unit hand-off: publish this warp's partials; the owner sums them later ----
@@ -1723,7 +1754,11 @@ int launch_stream(const MulMatOp* ops, int n_ops, cudaStream_t stream, int num_s
     cfg.numAttrs = 1;
     // raise the kernel's dynamic shared-memory limit to this launch's need
     // (once per size increase; the attribute call is not a stream operation)
-    static size_t configured[12] = {};
+    // (the attribute is per device: one size per device ordinal and kernel)
+    static size_t configured[kMaxDevices][12] = {};
+    int dev = 0;
+    if (const cudaError_t e = cudaGetDevice(&dev); e != cudaSuccess) return -static_cast<int>(e);
+    if (dev < 0 || dev >= kMaxDevices) return -static_cast<int>(cudaErrorInvalidDevice);
     const int ti = (nt == 1 ? 0 : (nt == 2 ? 1 : 2)) + 3 * kind;
     void (*const kernels[12])(SList) = {
         stream_gemv_kernel<1, kProNone>,   stream_gemv_kernel<2, kProNone>,   stream_gemv_kernel<4, kProNone>,
@@ -1732,10 +1767,10 @@ int launch_stream(const MulMatOp* ops, int n_ops, cudaStream_t stream, int num_s
         stream_gemv_kernel<1, kProGelu>,   stream_gemv_kernel<2, kProGelu>,   stream_gemv_kernel<4, kProGelu>};
     void (*const kernel)(SList) = kernels[ti];
     cudaError_t e;
-    if (configured[ti] < smem) {
+    if (configured[dev][ti] < smem) {
         e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
         if (e != cudaSuccess) return -static_cast<int>(e);
-        configured[ti] = smem;
+        configured[dev][ti] = smem;
     }
     e = cudaLaunchKernelEx(&cfg, kernel, L);
     if (e == cudaSuccess) e = cudaGetLastError();

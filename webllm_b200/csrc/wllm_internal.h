@@ -53,6 +53,9 @@ struct MulMatOp {
 };
 
 constexpr int kMaxOpsPerLaunch = 16;
+// Device ordinals tracked by per-device caches (function attributes, symbol
+// addresses): one process may drive several devices.
+constexpr int kMaxDevices = 64;
 
 // Checks alignment/shape preconditions the kernels rely on. Returns an
 // empty string when the op can be launched, else the reason.

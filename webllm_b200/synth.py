@@ -141,6 +141,23 @@ def activations(rng: np.random.Generator, N: int, K: int) -> np.ndarray:
     return rng.standard_normal((N, K), dtype=np.float32)
 
 
+def activations_with_outliers(rng: np.random.Generator, N: int, K: int, value: float,
+                              blocks: tuple[str, ...] = ("first", "middle", "last")) -> np.ndarray:
+    """N(0,1) activations with 1-4 channels per named 256-element block set to
+    +-value, the shape of real residual streams (a few channels 100-1000x the
+    rest): within such a block every other element is small next to the
+    block maximum that scales the GEMV's activation limbs."""
+    x = rng.standard_normal((N, K), dtype=np.float32)
+    nb = K // 256
+    idx = {"first": 0, "middle": nb // 2, "last": nb - 1}
+    for n in range(N):
+        for name in blocks:
+            b = idx[name]
+            ch = rng.choice(256, size=int(rng.integers(1, 5)), replace=False)
+            x[n, b * 256 + ch] = np.float32(value) * rng.choice(np.array([-1.0, 1.0], dtype=np.float32), size=len(ch))
+    return x
+
+
 def weights_torch(gen, qtype: int, M: int, K: int, device):
     """Same distributions as weights(), generated on the device with torch."""
     import torch
