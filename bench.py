@@ -2,21 +2,30 @@
 """Benchmark of the quantized MUL_MAT hot path on B200.
 
 Workload (one step = one decode token through every MUL_MAT of the model):
-Llama-3.2-3B-shaped decode sweep, batch 1, 28 layers x 7 GEMVs:
-attn_q/k/o and ffn_gate/up as Q4_K, attn_v and ffn_down as Q6_K, f32 N(0,1)
-activations, seeded synthetic weights (1.80 GB of distinct weights per step,
-larger than the 126 MB L2, so no L2 flush is needed). Launch grouping follows
-the real decode dependencies: {q,k,v} share one input, {gate,up} another, o
-and down stand alone: 4 launches per layer, replayed as one CUDA graph.
+Qwen3-8B-shaped decode, batch 1: 36 layers x 7 Q4_K GEMVs (hidden 4096, FFN
+12288, 32 q / 8 kv heads x 128) plus the 151936 x 4096 Q6_K output
+projection, f32 N(0,1) activations, seeded synthetic weights: 4.42 GB of
+distinct weights per step, larger than the 126 MB L2, so no L2 flush is
+needed. Launch grouping follows the real decode dependencies: {q,k,v} share
+one input, {gate,up} another, o and down stand alone: 4 launches per layer and
+one for the output projection, replayed as one CUDA graph.
 
 With N GPUs (torchrun, one rank per GPU) every weight is row-sharded across
-the ranks and each group's outputs are all-gathered over NVLink with NCCL,
-so the total work is fixed ("strong" scaling).
+the ranks. The GEMV kernel's epilogue writes each finished row into every
+rank's gather buffer over NVLink (peer stores into CUDA-IPC memory), and each
+launch waits, bounded, until every rank's rows of the previous launch have
+landed: no collective library call on the data path. Total work is fixed
+("strong" scaling). `tp_split` adds the same step without the gather (each
+rank's GEMVs alone) so the cost of the exchange shows.
 
 value = algorithmic bytes of the whole step (sum over GEMVs of M*K*bpw +
 4*N*K + 4*N*M) / device time (CUDA events, max over ranks).
 e2e = the same bytes / the time of a step that also copies that step's
 activations host->device from pinned memory and its outputs back.
+parity = the step's outputs (layer 0, the last layer and the output
+projection, every rank's rows) against a float64 matmul of the
+library-dequantized weights (that dequantization is bit-exact with the
+reference's), both error metrics of the path.
 
 `--impl reference` times the reference algorithm's CPU path (the f32
 dequant-then-dot oracle restatement; the reference's llama.cpp CPU kernels
@@ -27,6 +36,7 @@ from __future__ import annotations
 
 import argparse
 import json
+import math
 import os
 import statistics
 import subprocess
@@ -42,19 +52,16 @@ if REPO not in sys.path:
 import numpy as np  # noqa: E402
 
 METRIC = "quantized MUL_MAT GB/s & % HBM peak (decode); prefill TFLOPS; at 1/2/4/8 GPU"
-WORKLOAD = "llama-3.2-3b decode sweep (28 layers x 7 GEMVs, Q4_K/Q6_K x f32, batch 1)"
-# --model qwen3-8b: the row-sharded decode of the multi-GPU configuration
-# (Qwen3-8B, 36 layers x 7 Q4_K GEMVs, hidden 4096, FFN 12288; its 151936 x
-# 4096 output projection is not in the step)
+# model: (workload description, layers, output projection in the step)
 WORKLOADS = {
-    "llama-3.2-3b": (WORKLOAD, 28),
-    "qwen3-8b": ("qwen3-8b decode sweep (36 layers x 7 GEMVs, Q4_K x f32, batch 1; output projection excluded)", 36),
+    "qwen3-8b": ("qwen3-8b decode (36 layers x 7 Q4_K GEMVs + 151936x4096 Q6_K output projection, f32 "
+                 "activations, batch 1)", 36, True),
+    "llama-3.2-3b": ("llama-3.2-3b decode sweep (28 layers x 7 GEMVs, Q4_K/Q6_K x f32, batch 1)", 28, False),
 }
-_MODEL = "llama-3.2-3b"
-# DRAM bytes (read + write) of one layer's four GEMV launches, summed from an
-# ncu capture of this workload (profiles/stream_gemv_llama32_3b_decode.md);
-# the algorithmic bytes are 64,139,264 per layer.
-NCU_DRAM_BYTES_PER_LAYER = 64_314_496
+_MODEL = "qwen3-8b"
+# DRAM bytes (read + write) of one Llama-3.2-3B layer's four GEMV launches
+# from an ncu capture; its algorithmic bytes are 64,139,264 per layer.
+NCU_DRAM_BYTES_PER_LAYER_LLAMA32 = 64_314_496
 FALLBACK_HBM_GBS = 6650.0
 
 
@@ -64,14 +71,17 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
-    ap.add_argument("--model", choices=sorted(WORKLOADS), default="llama-3.2-3b",
-                    help="decode sweep shapes (default: the single-GPU headline workload)")
+    ap.add_argument("--model", choices=sorted(WORKLOADS), default="qwen3-8b",
+                    help="decode shapes (default: the row-sharded multi-GPU configuration, also the largest "
+                         "that fits one GPU)")
     ap.add_argument("--layers", type=int, default=None, help="layers per step (default: the model's)")
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU-baseline sample budget")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-prefill", action="store_true", help="skip the prefill GEMM measurement")
     ap.add_argument("--no-batched", action="store_true", help="skip the batched Q8_0 decode measurement")
     ap.add_argument("--no-fused-norm", action="store_true", help="skip the fused RMS_NORM and GLU measurements")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="skip every measurement besides the step (prefill, batched, fused ops, sweeps, single GEMV)")
     return ap.parse_args()
 
 
@@ -365,17 +375,17 @@ def batched_measure(dev, reps: int = 10, warmup: int = 3):
     return res
 
 
-def layer_table():
-    """The 7 GEMVs of one decode layer of the selected model: [(name, qtype, M, K)]."""
+def layer_table(model: str | None = None):
+    """The 7 GEMVs of one decode layer: [(name, qtype, M, K)]."""
     from webllm_b200 import synth
 
-    return synth.QWEN3_8B_LAYER if _MODEL == "qwen3-8b" else synth.LLAMA32_3B_LAYER
+    return synth.QWEN3_8B_LAYER if (model or _MODEL) == "qwen3-8b" else synth.LLAMA32_3B_LAYER
 
 
-def layer_groups():
+def layer_groups(model: str | None = None):
     """[(input K, [(name, qtype, M, K), ...]), ...] for one layer: the launch
     groups that share an input (q|k|v, o, gate|up, down)."""
-    L = {n: (n, t, M, K) for n, t, M, K in layer_table()}
+    L = {n: (n, t, M, K) for n, t, M, K in layer_table(model)}
     return [
         (L["attn_q"][3], [L["attn_q"], L["attn_k"], L["attn_v"]]),
         (L["attn_output"][3], [L["attn_output"]]),
@@ -384,10 +394,23 @@ def layer_groups():
     ]
 
 
-def step_bytes(layers: int) -> int:
+def step_groups(layers: int, model: str | None = None):
+    """Every launch of one step in order: [(layer, group, input K, mats)];
+    the output projection (when the model's step has it) is layer `layers`."""
     from webllm_b200 import synth
 
-    return layers * sum(synth.algorithmic_bytes(t, M, K, 1) for _, t, M, K in layer_table())
+    model = model or _MODEL
+    out = [(li, gi, kin, mats) for li in range(layers) for gi, (kin, mats) in enumerate(layer_groups(model))]
+    if WORKLOADS[model][2]:
+        out.append((layers, 0, synth.QWEN3_8B_OUTPUT[3], [synth.QWEN3_8B_OUTPUT]))
+    return out
+
+
+def step_bytes(layers: int, model: str | None = None) -> int:
+    from webllm_b200 import synth
+
+    return sum(synth.algorithmic_bytes(t, M, K, 1) for _, _, _, mats in step_groups(layers, model)
+               for _, t, M, K in mats)
 
 
 class ClockSampler:
@@ -443,79 +466,177 @@ class ClockSampler:
 # ------------------------------------------------------------------ CPU arms
 
 
-CPU_DISTINCT_LAYERS = 8  # 513 MB of weights: larger than any host's last-level cache
+CPU_DISTINCT_LAYERS = 8  # 0.5-0.9 GB of weights: larger than any host's last-level cache
 
 
-def cpu_layers(n: int):
-    """n distinct synthetic layers of the sweep: [[(type, w, x, bytes) x7] x n]."""
-    from webllm_b200 import synth
+class CpuWork:
+    """The oracle's f32 dequant-then-dot (the reference algorithm's CPU path)
+    over the step's GEMVs: 8 distinct synthetic layers cycled so the weights
+    stream from DRAM, and the output projection once per `layers` layers so
+    the byte mix is the step's."""
 
-    rng = np.random.default_rng(1234)
-    return [[(t, synth.weights(rng, t, M, K), synth.activations(rng, 1, K), synth.algorithmic_bytes(t, M, K, 1))
-             for _, t, M, K in layer_table()] for _ in range(n)]
+    def __init__(self, layers: int):
+        from oracle import oracle as O
+        from webllm_b200 import synth
+
+        rng = np.random.default_rng(1234)
+        self.O = O
+        self.layers_per_step = layers
+        self.distinct = [[(t, synth.weights(rng, t, M, K), synth.activations(rng, 1, K),
+                           synth.algorithmic_bytes(t, M, K, 1)) for _, t, M, K in layer_table()]
+                         for _ in range(CPU_DISTINCT_LAYERS)]
+        self.output = None
+        if WORKLOADS[_MODEL][2]:
+            _, t, M, K = synth.QWEN3_8B_OUTPUT
+            self.output = (t, synth.weights(rng, t, M, K), synth.activations(rng, 1, K),
+                           synth.algorithmic_bytes(t, M, K, 1))
+        self.cores = O.max_threads()
+        self.done_layers = 0
+        self.weight_mb = (sum(m[1].nbytes for L in self.distinct for m in L)
+                          + (self.output[1].nbytes if self.output else 0)) / 1e6
+
+    def layer(self) -> int:
+        """One layer's 7 GEMVs (and the output projection after every
+        `layers` layers); returns the algorithmic bytes done."""
+        b = 0
+        for t, w, x, nb in self.distinct[self.done_layers % len(self.distinct)]:
+            self.O.mul_mat_f32(t, w, x, threads=self.cores)
+            b += nb
+        self.done_layers += 1
+        if self.output is not None and self.done_layers % self.layers_per_step == 0:
+            t, w, x, nb = self.output
+            self.O.mul_mat_f32(t, w, x, threads=self.cores)
+            b += nb
+        return b
+
+    def describe(self) -> str:
+        out = " + the 151936x4096 Q6_K output projection once per 36 layers" if self.output else ""
+        return (f"whole layers of the step (7 GEMVs each){out}, cycling over {len(self.distinct)} distinct "
+                f"layers ({self.weight_mb:.0f} MB of weights) so they stream from DRAM; f32 dequant-then-dot "
+                f"oracle on {self.cores} threads (the reference's llama.cpp CPU kernels are not vendored in the "
+                f"reference repository)")
 
 
-def cpu_sample(layers_budget_s: float, threads: int | None = None):
-    """Time the oracle's f32 dequant-then-dot on whole layers of the sweep,
-    cycling through 8 distinct layers so the weights stream from DRAM, until
-    about `layers_budget_s` seconds have passed. Returns (GB/s, cores,
-    sample description)."""
-    from oracle import oracle as O
-
-    layers = cpu_layers(CPU_DISTINCT_LAYERS)
-    cores = O.max_threads() if threads is None else threads
-    O.mul_mat_f32(layers[0][0][0], layers[0][0][1][:8], layers[0][0][2], threads=cores)  # start the thread pool
-    done_bytes, t0, n_layers = 0, time.perf_counter(), 0
+def cpu_sample(budget_s: float, layers: int):
+    """Time the CPU path on whole layers for about `budget_s` seconds after
+    one untimed pass over the distinct layers (page-in, thread pool).
+    Returns (GB/s, cores, sample description)."""
+    work = CpuWork(layers)
+    for _ in range(CPU_DISTINCT_LAYERS):
+        work.layer()
+    done, t0 = 0, time.perf_counter()
     while True:
-        for t, w, x, b in layers[n_layers % len(layers)]:
-            O.mul_mat_f32(t, w, x, threads=cores)
-            done_bytes += b
-        n_layers += 1
+        done += work.layer()
         el = time.perf_counter() - t0
-        if el >= layers_budget_s:
+        if el >= budget_s:
             break
-    return done_bytes / el / 1e9, cores, (f"{n_layers} layers of the sweep (7 GEMVs each, cycling over "
-                                          f"{len(layers)} distinct layers = 513 MB), {done_bytes/1e6:.0f} MB in {el:.1f} s")
+    n = work.done_layers - CPU_DISTINCT_LAYERS
+    return done / el / 1e9, work.cores, f"{n} layers, {done / 1e9:.1f} GB in {el:.1f} s: " + work.describe()
 
 
 def run_reference(args, rank: int):
+    """The reference arm: the CPU path on this box's host cores, rank 0 only.
+    Every step is the same number of whole layers, chosen from an untimed
+    pass so that the K timed steps take about --cpu-seconds together (the
+    same budget and sample as the GPU arm's cpu_baseline)."""
     if rank != 0:
         return
-    from oracle import oracle as O
-    from webllm_b200 import synth
-
-    cores = O.max_threads()
-    layers = cpu_layers(CPU_DISTINCT_LAYERS)
-    layer_bytes = sum(m[3] for m in layers[0])
-    counter = [0]
-
-    def one_step():
-        for t, w, x, _ in layers[counter[0] % len(layers)]:
-            O.mul_mat_f32(t, w, x, threads=cores)
-        counter[0] += 1
-
-    for _ in range(args.warmup):
-        one_step()
+    work = CpuWork(args.layers)
     t0 = time.perf_counter()
+    for _ in range(CPU_DISTINCT_LAYERS):
+        work.layer()
+    per_layer_s = (time.perf_counter() - t0) / CPU_DISTINCT_LAYERS
+    layers_per_step = max(1, math.ceil(args.cpu_seconds / max(1, args.steps) / per_layer_s))
+    for _ in range(args.warmup):
+        for _ in range(layers_per_step):
+            work.layer()
+    done, t0 = 0, time.perf_counter()
     for _ in range(args.steps):
-        one_step()
+        for _ in range(layers_per_step):
+            done += work.layer()
     el = time.perf_counter() - t0
-    gbs = layer_bytes * args.steps / el / 1e9
-    sample = (f"each step: 1 of the {WORKLOADS[_MODEL][1]} layers (7 GEMVs, {layer_bytes/1e6:.1f} MB of algorithmic bytes), cycling "
-              f"over {len(layers)} distinct layers (513 MB) so weights stream from DRAM; f32 dequant-then-dot "
-              f"oracle (the reference's llama.cpp CPU kernels are not vendored in the reference repository)")
+    gbs = done / el / 1e9
+    sample = f"each step: {layers_per_step} " + work.describe()
     line = {
         "impl": "reference", "metric": METRIC, "value": round(gbs, 3), "unit": "GB/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(el / args.steps * 1e3, 3),
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": WORKLOADS[_MODEL][0], "batch": 1, "layers_per_step": 1},
-        "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": cores, "kind": "port", "sample": sample},
+        "config": {"workload": WORKLOADS[_MODEL][0], "batch": 1, "layers_per_step": layers_per_step,
+                   "timed_s": round(el, 2)},
+        "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": work.cores, "kind": "port",
+                         "sample": sample},
         "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 
 
 # ------------------------------------------------------------------ GPU arm
+
+
+def weight_seed(li: int, gi: int, mi: int, rank: int) -> int:
+    """Seed of rank `rank`'s row shard of launch (li, gi)'s op mi: any rank
+    can regenerate any other rank's weights (the parity check does)."""
+    return 1_000_000 + 10_000 * li + 100 * gi + 10 * mi + rank
+
+
+def check_parity(dev, launches, world: int, rank: int, layers: int, stream_ptr: int) -> dict:
+    """Both error metrics of the path for the outputs of layer 0, the last
+    layer and the output projection, every rank's rows (other ranks' weight
+    shards are regenerated from their seeds), against a float64 matmul of the
+    library-dequantized weights (bit-exact with the reference's
+    dequantization). Row chunks keep the float64 copy small."""
+    import torch
+
+    from webllm_b200 import jsep, synth
+    from webllm_b200.tp import row_shard
+
+    def rel(y, r):
+        mx = r.abs().max()
+        a = ((y - r).abs().max() / mx).item()
+        sel = r.abs() >= 1e-2 * mx
+        b = ((y[sel] - r[sel]).abs() / r[sel].abs()).max().item()
+        return a, b
+
+    gen = torch.Generator(device=dev)
+    worst_a = worst_b = 0.0
+    n_ops = n_rows = 0
+    for L in launches:
+        if L["li"] not in (0, layers - 1, layers):
+            continue
+        x = L["x"].double()
+        for mi, (name, t, M, K) in enumerate(L["mats"]):
+            got_parts, ref_parts = [], []
+            for r in range(world):
+                sh = row_shard(M, world, r)
+                if sh.count == 0:
+                    continue
+                if r == rank:
+                    w = L["w"][mi]
+                else:
+                    gen.manual_seed(weight_seed(L["li"], L["gi"], mi, r))
+                    w = synth.weights_torch(gen, t, sh.count, K, dev)
+                col = r * L["gtot"] + L["offs"][mi]
+                got_parts.append(L["out"][0, col:col + sh.count].double())
+                rb = synth.row_bytes(t, K)
+                for r0 in range(0, sh.count, 16384):
+                    rows = min(16384, sh.count - r0)
+                    # the dequantization runs on the library stream: torch's
+                    # stream must be done with the memory it is handed
+                    torch.cuda.synchronize()
+                    wf = torch.empty(rows, K, device=dev)
+                    jsep.dequantize_device(t, w.data_ptr() + r0 * rb, wf.data_ptr(), rows * K, stream_ptr)
+                    torch.cuda.ExternalStream(stream_ptr).synchronize()
+                    ref_parts.append((wf.double() @ x.t()).t()[0])
+                    torch.cuda.synchronize()
+                    del wf
+            a, b = rel(torch.cat(got_parts), torch.cat(ref_parts))
+            worst_a, worst_b = max(worst_a, a), max(worst_b, b)
+            n_ops += 1
+            n_rows += M
+    return {"max_rel": float(f"{worst_a:.3e}"), "max_rel_elem": float(f"{worst_b:.3e}"), "tol": 1e-3,
+            "ok": bool(worst_a <= 1e-3 and worst_b <= 1e-3), "ops_checked": n_ops, "rows_checked": n_rows,
+            "reference": "float64 matmul of the library-dequantized weights; layer 0, the last layer and the "
+                         "output projection, all ranks' rows; max-normalized and per-element (|r| >= 1e-2 max|r|)"}
 
 
 def run_b200(args, rank: int, world: int, local_rank: int):
@@ -535,17 +656,17 @@ def run_b200(args, rank: int, world: int, local_rank: int):
         dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
 
     layers = args.layers
-    groups = layer_groups()
+    plan = step_groups(layers)
     gen = torch.Generator(device=dev)
-    # Row-sharded (world > 1): each group's rows from every rank land in one
-    # gathered buffer per rank, [world][group rows]. The GEMV writes this
+    # Row-sharded (world > 1): each launch's rows from every rank land in one
+    # gathered buffer per rank, [world][launch rows]. The GEMV writes this
     # rank's rows into every rank's buffer over NVLink (peer memory opened
     # with CUDA IPC); one bounded wait at the end of the step completes them.
+    gtot = [sum(row_shard(M, world, rank).padded for (_, _, M, _) in mats) for *_, mats in plan]
+    gather_floats = sum(world * g for g in gtot)
     tp = gview = None
-    gtot = [sum(row_shard(M, world, rank).padded for (_, _, M, _) in mats) for _, mats in groups]
-    per_layer = sum(world * g for g in gtot)
     if world > 1:
-        g_ptr, g_handle = jsep.ipc_alloc(4 * per_layer * layers)
+        g_ptr, g_handle = jsep.ipc_alloc(4 * gather_floats)
         s_ptr, s_handle = jsep.ipc_alloc(4 * jsep.MAX_RANKS)
         st_ptr, _ = jsep.ipc_alloc(16)
         handles = [None] * world
@@ -553,76 +674,72 @@ def run_b200(args, rank: int, world: int, local_rank: int):
         gbase = [g_ptr if r == rank else jsep.ipc_open(handles[r][0]) for r in range(world)]
         sigs = [s_ptr if r == rank else jsep.ipc_open(handles[r][1]) for r in range(world)]
         tp = jsep.tp_group(world, rank, sigs, st_ptr)
-        gview = torch.as_tensor(DevArray(g_ptr, per_layer * layers), device=dev)
+        gview = torch.as_tensor(DevArray(g_ptr, gather_floats), device=dev)
     # ---- resident weights (row shard of every matrix), inputs, outputs.
-    # Every group's activations are a slice of one buffer, and at one GPU
-    # every group's outputs too, so the end-to-end step moves each with one copy.
-    x_all = torch.empty(layers * sum(kin for kin, _ in groups), device=dev)
-    y_all = torch.zeros(layers * sum(gtot), device=dev) if world == 1 else None
-    x_pos = y_pos = 0
-    W, X, Y, ops, peer_outs = [], [], [], [], []
-    for li in range(layers):
-        lw, lx, ly, lops, louts = [], [], [], [], []
-        base = li * per_layer
-        for gi, (kin, mats) in enumerate(groups):
-            x = x_all[x_pos:x_pos + kin].view(1, kin)
-            x_pos += kin
-            x.copy_(torch.randn(1, kin, device=dev, generator=gen.manual_seed(10_000 * li + 10 * gi)))
-            lx.append(x)
-            pads = [row_shard(M, world, rank).padded for (_, _, M, _) in mats]
-            offs = [sum(pads[:i]) for i in range(len(pads))]
+    # Every launch's activations are a slice of one buffer, and at one GPU
+    # every launch's outputs too, so the end-to-end step moves each with one copy.
+    x_all = torch.empty(sum(kin for _, _, kin, _ in plan), device=dev)
+    y_all = torch.zeros(sum(gtot), device=dev) if world == 1 else None
+    x_pos = y_pos = g_pos = 0
+    launches = []
+    for idx, (li, gi, kin, mats) in enumerate(plan):
+        x = x_all[x_pos:x_pos + kin].view(1, kin)
+        x_pos += kin
+        x.copy_(torch.randn(1, kin, device=dev, generator=gen.manual_seed(10_000 * li + 10 * gi)))
+        pads = [row_shard(M, world, rank).padded for (_, _, M, _) in mats]
+        offs = [sum(pads[:i]) for i in range(len(pads))]
+        if world > 1:
+            out = gview[g_pos:g_pos + world * gtot[idx]].view(1, -1)  # the launch's gathered rows
+        else:
+            out = y_all[y_pos:y_pos + gtot[idx]].view(1, -1)
+            y_pos += gtot[idx]
+        gops, gouts, ws = [], [], []
+        for mi, (name, t, M, K) in enumerate(mats):
+            # this rank's contiguous row shard; every rank reserves `padded` rows
+            Mr = row_shard(M, world, rank).count
+            gen.manual_seed(weight_seed(li, gi, mi, rank))
+            w = synth.weights_torch(gen, t, Mr, K, dev)
+            ws.append(w)
+            col = rank * gtot[idx] + offs[mi]  # float offset of this rank's rows in the launch's rows
+            gops.append(jsep.MulMatArgs(t, Mr, K, 1, w.data_ptr(), synth.row_bytes(t, K), x.data_ptr(), K,
+                                        out.data_ptr() + 4 * col, Mr))
             if world > 1:
-                out = gview[base:base + world * gtot[gi]].view(1, -1)  # the group's gathered rows
-            else:
-                out = y_all[y_pos:y_pos + gtot[gi]].view(1, -1)
-                y_pos += gtot[gi]
-            gops, gouts = [], []
-            for mi, (name, t, M, K) in enumerate(mats):
-                # this rank's contiguous row shard; every rank reserves `padded` rows
-                sh = row_shard(M, world, rank)
-                Mr = sh.count
-                gen.manual_seed(1_000_000 + 10_000 * li + 100 * gi + 10 * mi + rank)
-                w = synth.weights_torch(gen, t, Mr, K, dev)
-                lw.append(w)
-                col = rank * gtot[gi] + offs[mi]  # float offset of this rank's rows in the group's rows
-                gops.append(jsep.MulMatArgs(t, Mr, K, 1, w.data_ptr(), synth.row_bytes(t, K), x.data_ptr(), K,
-                                            out.data_ptr() + 4 * col, Mr))
-                if world > 1:
-                    gouts.append([gbase[r] + 4 * (base + col) for r in range(world)])
-            ly.append(out)
-            lops.append(gops)
-            louts.append(gouts)
-            base += world * gtot[gi]
-        W.append(lw)
-        X.append(lx)
-        Y.append(ly)
-        ops.append(lops)
-        peer_outs.append(louts)
+                gouts.append([gbase[r] + 4 * (g_pos + col) for r in range(world)])
+        launches.append({"li": li, "gi": gi, "mats": mats, "x": x, "out": out, "ops": gops, "outs": gouts,
+                         "w": ws, "gtot": gtot[idx], "offs": offs})
+        g_pos += world * gtot[idx]
     torch.cuda.synchronize()
-    launches_per_step = layers * len(groups) + (1 if world > 1 else 0)
+    launches_per_step = len(launches) + (1 if world > 1 else 0)
 
     def step(stream_ptr: int):
-        for li in range(layers):
-            for gi in range(len(groups)):
-                if world > 1:
-                    jsep.mul_mat_batch_tp(ops[li][gi], peer_outs[li][gi], tp, stream_ptr)
-                else:
-                    jsep.mul_mat_batch(ops[li][gi], stream_ptr)
+        for L in launches:
+            if world > 1:
+                jsep.mul_mat_batch_tp(L["ops"], L["outs"], tp, stream_ptr)
+            else:
+                jsep.mul_mat_batch(L["ops"], stream_ptr)
         if world > 1:
             jsep.tp_wait(tp, stream_ptr)
 
-    # ---- warm-up, then capture the step as one CUDA graph
-    s = torch.cuda.current_stream()
-    for _ in range(max(1, args.warmup)):
-        step(s.cuda_stream)
-    torch.cuda.synchronize()
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph):
-        step(torch.cuda.current_stream().cuda_stream)
-    torch.cuda.synchronize()
-    for _ in range(args.warmup):
-        graph.replay()
-    torch.cuda.synchronize()
+    def gemv_only(stream_ptr: int):
+        # each rank's row-shard GEMVs with no gather and no cross-rank wait
+        for L in launches:
+            jsep.mul_mat_batch(L["ops"], stream_ptr)
+
+    def capture(fn):
+        s = torch.cuda.current_stream()
+        for _ in range(max(1, args.warmup)):
+            fn(s.cuda_stream)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            fn(torch.cuda.current_stream().cuda_stream)
+        torch.cuda.synchronize()
+        for _ in range(args.warmup):
+            g.replay()
+        torch.cuda.synchronize()
+        return g
+
+    graph = capture(step)
 
     def barrier():
         if world > 1:
@@ -635,26 +752,51 @@ def run_b200(args, rank: int, world: int, local_rank: int):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
+    def time_graph(g) -> float:
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier()
+        torch.cuda.synchronize()
+        e0.record()
+        for _ in range(args.steps):
+            g.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        barrier()
+        return max_over_ranks(e0.elapsed_time(e1)) / args.steps
+
     # ---- timed region: device-resident inputs
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     uuid = getattr(torch.cuda.get_device_properties(dev), "uuid", None)
     gpu_id = f"GPU-{uuid}" if uuid is not None and not str(uuid).startswith("GPU-") else (str(uuid) if uuid else str(local_rank))
     with ClockSampler(gpu_id) as clocks:
-        barrier()
-        torch.cuda.synchronize()
-        ev0.record()
-        for _ in range(args.steps):
-            graph.replay()
-        ev1.record()
-        torch.cuda.synchronize()
-        barrier()
-    dev_ms = max_over_ranks(ev0.elapsed_time(ev1)) / args.steps
+        dev_ms = time_graph(graph)
     clk = clocks.summary()
+
+    # ---- parity of the step's outputs (rank 0 checks every rank's rows)
+    parity = None
+    if rank == 0:
+        parity = check_parity(dev, launches, world, rank, layers, jsep.library_stream())
+    barrier()
+
+    # ---- the same step without the exchange (row-shard GEMVs alone)
+    tp_split = None
+    total_bytes = step_bytes(layers)
+    if world > 1:
+        g2 = capture(gemv_only)
+        only_ms = time_graph(g2)
+        del g2
+        tp_split = {"gemv_only": {"ms_per_step": round(only_ms, 4),
+                                  "aggregate_gbs": round(total_bytes / (only_ms * 1e-3) / 1e9, 2),
+                                  "per_gpu_gbs": round(total_bytes / world / (only_ms * 1e-3) / 1e9, 2)},
+                    "with_gather": {"ms_per_step": round(dev_ms, 4),
+                                    "aggregate_gbs": round(total_bytes / (dev_ms * 1e-3) / 1e9, 2),
+                                    "per_gpu_gbs": round(total_bytes / world / (dev_ms * 1e-3) / 1e9, 2)},
+                    "note": "gemv_only: each rank's row-shard GEMVs, no peer writes, no cross-rank wait "
+                            "(outputs incomplete); with_gather: the fused NVLink gather and its per-launch wait"}
 
     # ---- e2e: pinned host activations in, outputs out, every step: one copy
     # of all the step's activations, one of all its outputs (at N > 1 the
-    # gathered rows of all ranks)
-    x_host = torch.randn(x_all.numel()).pin_memory()
+    # gathered rows of all ranks); the host activations are the same on every rank
+    x_host = torch.randn(x_all.numel(), generator=torch.Generator().manual_seed(7)).pin_memory()
     outs = y_all if world == 1 else gview
     y_host = torch.empty(outs.numel()).pin_memory()
     h2d = x_host.numel() * 4
@@ -666,6 +808,7 @@ def run_b200(args, rank: int, world: int, local_rank: int):
         if rank == 0:
             y_host.copy_(outs, non_blocking=True)
 
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     for _ in range(args.warmup):
         e2e_step()
     torch.cuda.synchronize()
@@ -680,30 +823,33 @@ def run_b200(args, rank: int, world: int, local_rank: int):
     e2e_ms = max_over_ranks(max(ev0.elapsed_time(ev1) / args.steps, wall_ms))
     barrier()
 
-    # ---- C-ABI (descriptor + handle) e2e on rank 0 at one GPU
-    jsep_e2e = None
-    if world == 1:
-        jsep_e2e = jsep_path_e2e(args, layers)
+    # ---- extras at one GPU: the C-ABI e2e, prefill, batched, fused ops, sweeps
+    extras = {}
+    if world == 1 and not args.no_extras:
+        del launches, graph  # free the step's weights
+        torch.cuda.empty_cache()
+        extras["e2e_c_abi"] = jsep_path_e2e(args, layers)
+        extras["single_gemv"] = single_gemv_measure(dev)
+        extras["llama32_sweep"] = sweep_measure(dev, "llama-3.2-3b", args)
+        if not args.no_prefill:
+            extras["prefill"] = prefill_measure(dev)
+        if not args.no_fused_norm:
+            extras["fused_norm"] = fused_norm_measure(dev)
+            extras["fused_glu"] = fused_glu_measure(dev)
+        if not args.no_batched:
+            extras["batched"] = batched_measure(dev)
 
-    # ---- prefill GEMMs (tensor cores) and batched decode, rank 0 at one GPU
-    prefill = batched = fused_norm = fused_glu = None
-    if world == 1 and not args.no_prefill:
-        prefill = prefill_measure(dev)
-    if world == 1 and not args.no_fused_norm:
-        fused_norm = fused_norm_measure(dev)
-        fused_glu = fused_glu_measure(dev)
-    if world == 1 and not args.no_batched:
-        batched = batched_measure(dev)
-
-    total_bytes = step_bytes(layers)
     gbs = total_bytes / (dev_ms * 1e-3) / 1e9
     peak, peak_src = measured_peaks()
     line = None
     if rank == 0:
         cpu = None
         if world == 1 and not args.no_cpu_baseline:
-            v, cores, sample = cpu_sample(args.cpu_seconds)
+            v, cores, sample = cpu_sample(args.cpu_seconds, layers)
             cpu = {"value": round(v, 3), "unit": "GB/s", "cores": cores, "kind": "port", "sample": sample}
+        traffic = None
+        if world == 1 and _MODEL == "llama-3.2-3b":
+            traffic = NCU_DRAM_BYTES_PER_LAYER_LLAMA32 * layers
         line = {
             "metric": METRIC, "value": round(gbs, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(dev_ms, 4), "higher_is_better": True,
@@ -712,14 +858,16 @@ def run_b200(args, rank: int, world: int, local_rank: int):
                        "l2": f"inputs larger than L2 ({total_bytes / 1e9:.2f} GB of distinct weights per step), no flush",
                        "parallelism": f"tp{world} row-sharded" + (" + NVLink peer-write gather fused into the GEMV"
                                                                       if world > 1 else ""),
-                       "launch": "4 grouped launches per layer, one CUDA graph per step"},
+                       "launch": f"{len(plan)} grouped launches per step (4 per layer"
+                                 + (" + the output projection" if WORKLOADS[_MODEL][2] else "")
+                                 + "), one CUDA graph per step"},
             "roofline": {"bound": "hbm", "achieved": round(gbs, 2), "peak": peak, "unit": "GB/s",
-                         "frac": round(gbs / peak, 4),
-                         "traffic": NCU_DRAM_BYTES_PER_LAYER * layers if world == 1 and _MODEL == "llama-3.2-3b" else None,
+                         "frac": round(gbs / peak, 4), "traffic": traffic,
                          "traffic_note": "ncu dram__bytes_read.sum + dram__bytes_write.sum of the step's GEMV launches",
                          "peak_source": f"{peak_src} hbm_gbs (burst copy)",
                          "note": "achieved = step algorithmic bytes / step device time over all launches of the GEMV kernel"
-                                 + (" (includes the fused gather and its end-of-step wait)" if world > 1 else "")},
+                                 + (" (includes the fused gather and its per-launch waits)" if world > 1 else "")},
+            "parity": parity,
             "cpu_baseline": cpu,
             "e2e": {"value": round(total_bytes / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 4),
@@ -727,16 +875,9 @@ def run_b200(args, rank: int, world: int, local_rank: int):
             "gpu_launches": launches_per_step * args.steps,
             "clocks": clk,
         }
-        if jsep_e2e is not None:
-            line["e2e_c_abi"] = jsep_e2e
-        if prefill is not None:
-            line["prefill"] = prefill
-        if batched is not None:
-            line["batched"] = batched
-        if fused_norm is not None:
-            line["fused_norm"] = fused_norm
-        if fused_glu is not None:
-            line["fused_glu"] = fused_glu
+        if tp_split is not None:
+            line["tp_split"] = tp_split
+        line.update(extras)
     if world > 1:
         del graph
         torch.cuda.synchronize()
@@ -753,45 +894,105 @@ def run_b200(args, rank: int, world: int, local_rank: int):
         print(json.dumps(line), flush=True)
 
 
+def sweep_measure(dev, model: str, args, reps: int = 20) -> dict:
+    """A whole decode sweep of `model` at one GPU (the step's grouped launches,
+    one CUDA graph): GB/s and the HBM fraction."""
+    import torch
+
+    from webllm_b200 import jsep, synth
+
+    layers = WORKLOADS[model][1]
+    plan = step_groups(layers, model)
+    gen = torch.Generator(device=dev)
+    keep, calls = [], []
+    for li, gi, kin, mats in plan:
+        x = torch.randn(1, kin, device=dev, generator=gen.manual_seed(10_000 * li + 10 * gi))
+        out = torch.empty(1, sum(M for _, _, M, _ in mats), device=dev)
+        ops, off = [], 0
+        for mi, (name, t, M, K) in enumerate(mats):
+            gen.manual_seed(weight_seed(li, gi, mi, 0))
+            w = synth.weights_torch(gen, t, M, K, dev)
+            keep.append(w)
+            ops.append(jsep.MulMatArgs(t, M, K, 1, w.data_ptr(), synth.row_bytes(t, K), x.data_ptr(), K,
+                                       out.data_ptr() + 4 * off, M))
+            off += M
+        keep += [x, out]
+        calls.append(ops)
+
+    def fn(sp):
+        for ops in calls:
+            jsep.mul_mat_batch(ops, sp)
+
+    us = graph_times_us((("step", fn),), 1, reps)["step"]
+    nbytes = step_bytes(layers, model)
+    peak, _ = measured_peaks()
+    gbs = nbytes / (us * 1e-6) / 1e9
+    del keep
+    return {"workload": WORKLOADS[model][0], "us_per_step": us, "gbs": round(gbs, 2),
+            "hbm_frac": round(gbs / peak, 4), "launches_per_step": len(plan)}
+
+
+def single_gemv_measure(dev, reps: int = 20) -> dict:
+    """One Q4_K 4096 x 4096 decode GEMV (9.44 MB of weights, batch 1): 54
+    distinct weight copies (510 MB, over 4x the 126 MB L2) rotated in one CUDA
+    graph, so every launch streams its weights from HBM."""
+    import torch
+
+    from webllm_b200 import jsep, synth
+
+    t, M, K, copies = jsep.GGML_TYPE_Q4_K, 4096, 4096, 54
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(4096)
+    ws = [synth.weights_torch(gen, t, M, K, dev) for _ in range(copies)]
+    xs = [torch.randn(1, K, device=dev, generator=gen) for _ in range(copies)]
+    ys = [torch.empty(1, M, device=dev) for _ in range(copies)]
+    ops = [[jsep.MulMatArgs(t, M, K, 1, w.data_ptr(), synth.row_bytes(t, K), x.data_ptr(), K, y.data_ptr(), M)]
+           for w, x, y in zip(ws, xs, ys)]
+
+    def fn(sp):
+        for o in ops:
+            jsep.mul_mat_batch(o, sp)
+
+    us = graph_times_us((("gemv", fn),), copies, reps)["gemv"]
+    nbytes = synth.algorithmic_bytes(t, M, K, 1)
+    peak, _ = measured_peaks()
+    gbs = nbytes / (us * 1e-6) / 1e9
+    return {"workload": "single Q4_K 4096x4096 decode GEMV, batch 1 (54 distinct weight copies rotated, 510 MB)",
+            "us": us, "gbs": round(gbs, 2), "hbm_frac": round(gbs / peak, 4), "bytes": nbytes}
+
+
 def jsep_path_e2e(args, layers: int):
     """Same step through the reference-facing seam: descriptors + handles,
     pageable host activations written with wllm_write, one recorded graph of
-    the 112 wllm_run_ops calls, outputs read back with wllm_read."""
+    the step's wllm_run_ops calls, outputs read back with wllm_read."""
     from webllm_b200 import jsep, synth
 
     rt = jsep.install_jsep_callbacks(jsep._runtime.device if jsep._runtime else 0)
     dm = rt.data_manager
-    groups = layer_groups()
+    plan = step_groups(layers)
     rng = np.random.default_rng(99)
-    # one buffer per layer holding its 7 weights; one buffer for all inputs, one for all outputs
-    x_off, y_off, descs = 0, 0, []
-    x_layout, y_layout = [], []
-    for li in range(layers):
-        for gi, (kin, mats) in enumerate(groups):
-            x_layout.append((li, gi, x_off, kin))
-            x_off += 4 * kin
-            for (name, t, M, K) in mats:
-                y_layout.append((li, gi, name, y_off, M))
-                y_off += 4 * M
+    # one buffer per weight; one buffer for all inputs, one for all outputs
+    x_off, y_off = 0, 0
+    layout = []
+    for li, gi, kin, mats in plan:
+        ys = []
+        for (name, t, M, K) in mats:
+            ys.append(y_off)
+            y_off += 4 * M
+        layout.append((x_off, kin, mats, ys))
+        x_off += 4 * kin
     hx, hy = dm.alloc(x_off), dm.alloc(y_off)
-    wh = []
-    for li in range(layers):
-        for gi, (kin, mats) in enumerate(groups):
-            for (name, t, M, K) in mats:
-                w = synth.weights(rng, t, M, K)
-                h = dm.alloc(w.nbytes)
-                dm.write(h, 0, w)
-                wh.append(h)
-    wi, yi = 0, 0
-    for (li, gi, xo, kin) in x_layout:
+    wh, descs = [], []
+    for xo, kin, mats, ys in layout:
         gdescs = []
-        for (name, t, M, K) in groups[gi][1]:
-            _, _, _, yo, _ = y_layout[yi]
-            yi += 1
+        for (name, t, M, K), yo in zip(mats, ys):
+            w = synth.weights(rng, t, M, K)
+            h = dm.alloc(w.nbytes)
+            dm.write(h, 0, w)
+            wh.append(h)
             gdescs.append(jsep.JsepOpDescriptor(
                 29, 2, jsep.meta_for(hy, 0, (M, 1, 1, 1), offset=yo),
-                [jsep.meta_for(wh[wi], t, (K, M, 1, 1)), jsep.meta_for(hx, 0, (K, 1, 1, 1), offset=xo)]))
-            wi += 1
+                [jsep.meta_for(h, t, (K, M, 1, 1)), jsep.meta_for(hx, 0, (K, 1, 1, 1), offset=xo)]))
         descs.append(gdescs)
     x_host = rng.standard_normal(x_off // 4, dtype=np.float32)
     y_host = np.empty(y_off // 4, dtype=np.float32)
@@ -825,7 +1026,7 @@ def jsep_path_e2e(args, layers: int):
         dm.free(h)
     return {"value": round(step_bytes(layers) / (ms * 1e-3) / 1e9, 2), "unit": "GB/s", "ms_per_step": round(ms, 4),
             "h2d_bytes_per_step": x_off, "d2h_bytes_per_step": y_off,
-            "path": f"wllm_write(pageable host) -> wllm_graph_launch({layers * len(layer_groups())} recorded "
+            "path": f"wllm_write(pageable host) -> wllm_graph_launch({len(plan)} recorded "
                     "wllm_run_ops) -> wllm_read"}
 
 
