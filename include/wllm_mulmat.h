@@ -244,6 +244,16 @@ int32_t wllm_mul_mat_batch_tp(const wllm_mulmat_args* ops, const wllm_tp_outputs
  * is reported by the next wllm_sync. */
 int32_t wllm_tp_wait(const wllm_tp_group* group, void* stream);
 
+/* How many polls a bounded device-side wait of the decode kernels (pipeline
+ * barriers, a peer rank's signal) makes before it gives up, for launches
+ * enqueued after this call; 0 restores the default of 2^26 polls (seconds).
+ * A wait that gives up records an error code, the kernel still ends, and the
+ * next wllm_sync returns WLLM_STATUS_FAILED with the code in its message: a
+ * dead or stalled peer rank surfaces as an error rather than a hang. A small
+ * limit can fail healthy but slow launches. No counterpart in the reference
+ * (one browser GPU, no device-side waits). */
+int32_t wllm_set_wait_limit(uint32_t polls);
+
 /* The library's CUDA stream (a cudaStream_t), so a host can order its own
  * work (collectives, events) with the library's. */
 int32_t wllm_get_stream(void** out_stream);

@@ -114,3 +114,50 @@ def test_parse_errors():
     ok = header(nkv=1) + struct.pack("<Q", len(k)) + k + struct.pack("<II", G.UINT32, 64)
     ctx = G.parse(ok)
     assert ctx.alignment == 64 and ctx.data_offset == 64 and ctx.total_data_size == 0
+
+
+def test_alignment_and_fractional_sizes():
+    """UINT64 alignment is honoured (the reference converts it with Number());
+    an alignment <= 0 is a clear error; a tensor that is not whole blocks
+    parses with a fractional total size, as the reference computes it."""
+    def header(nt=0, nkv=0):
+        return struct.pack("<IIQQ", G.GGUF_MAGIC, 3, nt, nkv)
+    k = b"general.alignment"
+    kv = lambda vt, fmt, v: struct.pack("<Q", len(k)) + k + struct.pack("<I", vt) + struct.pack(fmt, v)  # noqa: E731
+    assert G.parse(header(nkv=1) + kv(G.UINT64, "<Q", 128)).alignment == 128
+    with pytest.raises(ValueError, match="alignment"):
+        G.parse(header(nkv=1) + kv(G.UINT32, "<I", 0))
+    name = b"t"
+    info = struct.pack("<Q", len(name)) + name + struct.pack("<I", 1) + struct.pack("<Q", 100) + \
+        struct.pack("<I", 12) + struct.pack("<Q", 0)  # 100 Q4_K elements: not a whole block
+    ctx = G.parse(header(nt=1) + info)
+    assert ctx.total_data_size == pytest.approx(100 * 144 / 256)
+    with pytest.raises(ValueError, match="whole blocks"):
+        G.tensor_nbytes(ctx.tensors[0])
+
+
+class FailingDataManager(FakeDataManager):
+    """Fails the write of the second tensor; records frees."""
+
+    def __init__(self):
+        super().__init__()
+        self.freed = []
+
+    def write(self, h, off, data):
+        if h == 2:
+            raise RuntimeError("device write failed")
+        super().write(h, off, data)
+
+    def free(self, h):
+        self.freed.append(h)
+
+
+def test_stream_to_buffers_failure_frees_and_keeps_the_error(tmp_path):
+    """A failing tensor frees the handles already allocated and raises the
+    original error (the memory map still closes cleanly)."""
+    path = tmp_path / "m.gguf"
+    write_model(path)
+    dm = FailingDataManager()
+    with pytest.raises(RuntimeError, match="device write failed"):
+        G.stream_to_buffers(str(path), dm, chunk_bytes=100)
+    assert sorted(dm.freed) == [1, 2]

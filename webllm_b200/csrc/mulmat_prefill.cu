@@ -119,6 +119,14 @@ __device__ __forceinline__ bool mbar_try(uint64_t* bar, uint32_t parity) {
         : "memory");
     return ok != 0;
 }
+// Bounded wait for a phase whatever the poison flag says (draining copies and
+// MMAs in flight before the CTA exits); false on time-out.
+__device__ __forceinline__ bool mbar_wait_drain(uint64_t* bar, uint32_t parity) {
+    for (uint32_t i = 0; i < kSpinLimit; ++i)
+        if (mbar_try(bar, parity)) return true;
+    return false;
+}
+
 // Bounded wait; a timeout poisons the CTA (every later wait returns at once).
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned code, volatile int* poisoned) {
     for (uint32_t i = 0; i < kSpinLimit; ++i) {
@@ -258,6 +266,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
         if (lane == 0) {
             asm volatile("prefetch.tensormap [%0];" ::"l"(&P.wmap) : "memory");
             asm volatile("prefetch.tensormap [%0];" ::"l"(&P.xmap) : "memory");
+            int raw_issued = 0, b_issued = 0;  // copies issued (for the drain below)
             for (int q = 0; q < nchunk; ++q) {
                 const int kb = q >> 2, c = q & 3;
                 if (c == 0) {
@@ -274,22 +283,43 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
                     } else {
                         tma_2d(raw + r * kRawBytes, &P.wmap, x, m0, &raw_full[r]);
                     }
+                    raw_issued = kb + 1;
                 }
                 const int s = q % kStages;
                 if (q >= kStages && !mbar_wait(&st_free[s], ((q / kStages) - 1) & 1, 1u, poisoned)) break;
                 mbar_expect_tx(&b_full[s], kBBytes);
                 tma_2d(B + s * kBBytes, &P.xmap, (4 * kb0 + q) * kChunkK, n0, &b_full[s]);
+                b_issued = q + 1;
             }
+            // Before the CTA can exit: the last copy into every raw slot and
+            // stage has landed (bounded, whatever the poison flag says). In a
+            // healthy launch the consumers waited for all of them already; after
+            // a time-out they may not have, and a copy still in flight would
+            // write into the shared memory of the next CTA on this SM.
+            for (int kb = max(0, raw_issued - kRawSlots); kb < raw_issued; ++kb)
+                if (!mbar_wait_drain(&raw_full[kb % kRawSlots], (kb / kRawSlots) & 1)) atomicOr(&g_prefill_error, 16u);
+            for (int q = max(0, b_issued - kStages); q < b_issued; ++q)
+                if (!mbar_wait_drain(&b_full[q % kStages], (q / kStages) & 1)) atomicOr(&g_prefill_error, 16u);
         }
     } else if (warp == 1) {
         // ---------------- MMA issuer ----------------
+        int committed = 0;  // chunks whose MMAs were committed
         for (int q = 0; q < nchunk; ++q) {
             const int s = q % kStages;
             const uint32_t par = (q / kStages) & 1;
             int ok = 1;
             if (lane == 0) ok = mbar_wait(&b_full[s], par, 2u, poisoned) && mbar_wait(&a_full[s], par, 2u, poisoned);
             ok = __shfl_sync(0xffffffffu, ok, 0);
-            if (!ok) break;
+            if (!ok) {
+                // a time-out: the MMAs already issued still write TMEM, which is
+                // freed at the end; wait (bounded) for the last commit, which
+                // tracks all of them
+                if (lane == 0 && committed > 0 &&
+                    !mbar_wait_drain(&st_free[(committed - 1) % kStages], ((committed - 1) / kStages) & 1))
+                    atomicOr(&g_prefill_error, 16u);
+                __syncwarp();
+                break;
+            }
             tc_fence_after();
             if (lane == 0) {
                 const uint32_t a0 = tmem + static_cast<uint32_t>(kTileN + s * kACols), b0 = smem_u32(B + s * kBBytes);
@@ -299,6 +329,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
                 umma_commit(&st_free[s]);  // the stage is free once these MMAs have read it
                 if (q == nchunk - 1) umma_commit(acc_full);
             }
+            committed = q + 1;
             __syncwarp();
         }
     } else {
@@ -537,9 +568,15 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
             __shared__ int last;
             asm volatile("bar.sync 1, %0;" ::"n"(kDqWarps * 32) : "memory");
             if (threadIdx.x == 64) {
+                // the count's low 16 bits are splits done, the high ones splits
+                // that gave up waiting (their partial tiles were not written):
+                // then nobody sums the tile, and wllm_sync reports the error
                 __threadfence();  // this CTA's partial tile before the count
-                last = atomicAdd(P.counters + tile, 1u) == static_cast<unsigned>(P.splits - 1);
+                const unsigned add = 1u + (*poisoned ? 0x10000u : 0u);
+                const unsigned old = atomicAdd(P.counters + tile, add);
+                last = (old & 0xFFFFu) == static_cast<unsigned>(P.splits - 1);
                 if (last) {
+                    if ((old + add) >> 16) last = 0;
                     P.counters[tile] = 0u;
                     __threadfence();  // the other splits' partial tiles after the count
                 }

@@ -60,6 +60,8 @@
 #include <cuda_fp16.h>
 #include <stdint.h>
 
+#include <atomic>
+
 #include "quant_blocks.cuh"
 #include "wllm_internal.h"
 
@@ -93,7 +95,10 @@ constexpr int kMaxK34 = 8192;                 // K limit for 3 or 4 vectors (the
 constexpr int kPreStages = 2;
 static_assert((kCW & (kCW - 1)) == 0, "unit ownership rotates with a mask");
 constexpr int kMaxK = 16384;                  // activation image in shared memory
-constexpr uint32_t kSpinLimit = 1u << 26;     // polls before a wait gives up (well over a second)
+// Polls before a bounded wait gives up (well over a second), unless the host
+// set another limit (wllm_set_wait_limit). The limit travels in the launch
+// parameters and sits in shared memory beside the CTA's poison flag.
+constexpr uint32_t kSpinLimit = 1u << 26;
 constexpr int kSmemBudget = 200 * 1024;       // one CTA per SM, up to 8 stages in flight
 
 struct SOp {
@@ -133,6 +138,7 @@ struct TpSig {
     int32_t world, rank;  // world 1: not row-sharded
     uint32_t* sig[kMaxRanks];
     uint32_t* state;
+    uint32_t spin_limit;  // polls of the peer wait before it gives up
 };
 
 struct SList {
@@ -145,6 +151,7 @@ struct SList {
     int32_t all_tma;      // every op is copied with its tensor map
     TpSig tp;             // world > 1: every output row also goes to the other ranks
     ProArgs pro;          // prologue applied to every op's activations (kind kProNone: none)
+    uint32_t spin_limit;  // polls before a bounded wait gives up
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -190,9 +197,15 @@ __device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
 // error is reported by wllm_sync). The poison flag is read once per 256
 // polls: every poll is a shared-memory operation, and polls of many warps
 // were measured to slow the copy warp's own barrier and TMA operations.
+// The CTA's wait limit: the word after its poison flag.
+__device__ __forceinline__ uint32_t spin_limit_of(volatile int* poisoned) {
+    return reinterpret_cast<volatile uint32_t*>(poisoned)[1];
+}
+
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned code, volatile int* poisoned) {
     if (mbar_test_wait(bar, parity)) return true;
-    for (uint32_t i = 0; i < kSpinLimit; ++i) {
+    const uint32_t lim = spin_limit_of(poisoned);
+    for (uint32_t i = 0; i < lim; ++i) {
         if (mbar_try_wait(bar, parity)) return true;
         if ((i & 255u) == 255u && *poisoned) return false;
     }
@@ -210,7 +223,8 @@ __device__ __forceinline__ void mbar_wait_warp(uint64_t* bar, uint32_t parity, u
     int ok = 1;
     if (lane == 0) {
         ok = 0;
-        for (uint32_t i = 0; i < kSpinLimit; ++i) {
+        const uint32_t lim = spin_limit_of(poisoned);
+        for (uint32_t i = 0; i < lim; ++i) {
             if (mbar_try_wait(bar, parity)) {
                 ok = 1;
                 break;
@@ -224,6 +238,23 @@ __device__ __forceinline__ void mbar_wait_warp(uint64_t* bar, uint32_t parity, u
         }
     }
     if (__shfl_sync(0xffffffffu, ok, 0)) (void)mbar_try_wait(bar, parity);
+}
+
+// Before the copy warp leaves: waits (bounded, whatever the poison flag
+// says) until the last copy issued into each stage has landed, so that no
+// bulk copy still writes into this CTA's shared memory after it exits. In a
+// healthy launch the consumers have waited for all of them already; after a
+// time-out they may not have. Bit s of `issued` marks a stage that received
+// a copy, bit s of `par` the parity of its last full phase.
+__device__ __forceinline__ void drain_copies(uint64_t* full, int S, uint32_t issued, uint32_t par,
+                                             volatile int* poisoned) {
+    const uint32_t lim = spin_limit_of(poisoned);
+    for (int st = 0; st < S; ++st) {
+        if (!((issued >> st) & 1u)) continue;
+        uint32_t i = 0;
+        while (i < lim && !mbar_try_wait(&full[st], (par >> st) & 1u)) ++i;
+        if (i == lim) atomicOr(&g_stream_error, 8u);
+    }
 }
 
 __device__ __forceinline__ void mbar_arrive_cnt(uint64_t* bar, uint32_t count) {
@@ -1200,7 +1231,8 @@ __device__ void tp_signal_peers(uint32_t* const* sig, int world, int rank) {
 
 // Bounded wait (one thread) until every other rank has signalled `seq`
 // sync points to this rank; false (and an error code) on time-out.
-__device__ bool tp_wait_peers(const uint32_t* const* sig, int world, int rank, uint32_t seq, volatile int* poisoned) {
+__device__ bool tp_wait_peers(const uint32_t* const* sig, int world, int rank, uint32_t seq, volatile int* poisoned,
+                              uint32_t lim) {
     for (int src = 0; src < world; ++src) {
         if (src == rank) continue;
         const uint32_t* f = sig[rank] + src;
@@ -1209,7 +1241,7 @@ __device__ bool tp_wait_peers(const uint32_t* const* sig, int world, int rank, u
         for (;; ++i) {
             asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
             if (static_cast<int32_t>(v - seq) >= 0) break;
-            if (i == kSpinLimit || (poisoned && *poisoned)) {
+            if (i == lim || (poisoned && *poisoned)) {
                 if (poisoned) *poisoned = 1;
                 atomicOr(&g_stream_error, 4u);
                 return false;
@@ -1294,6 +1326,7 @@ __global__ void __launch_bounds__(kThreads, 1) stream_gemv_kernel(const __grid_c
         for (int s = 0; s < kUnitSlots; ++s) mbar_init(&ubar[s], kCW);
         mbar_init(xready, 1);
         *poisoned = 0;
+        reinterpret_cast<volatile uint32_t*>(poisoned)[1] = L.spin_limit;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     __shared__ OpTable T;
@@ -1343,7 +1376,9 @@ __global__ void __launch_bounds__(kThreads, 1) stream_gemv_kernel(const __grid_c
         while (oi + 1 < n_ops && u >= T.op[oi + 1].unit_begin) ++oi;
         int s = 0, issued = 0;
         uint32_t phase = 1;  // the first pass finds every slot free
-        for (; u < total; u += gridDim.x) {
+        uint32_t issued_mask = 0, par_mask = 0;  // for drain_copies
+        bool stop = false;
+        for (; u < total && !stop; u += gridDim.x) {
             while (oi + 1 < n_ops && u >= T.op[oi + 1].unit_begin) ++oi;
             const OpInfo& op = T.op[oi];
             const int bb = block_bytes_of(op.type), nseg = op.nseg, step = op.seg_blocks * bb;
@@ -1351,19 +1386,25 @@ __global__ void __launch_bounds__(kThreads, 1) stream_gemv_kernel(const __grid_c
             const int r0 = (u - op.unit_begin) * kRows;
             const CUtensorMap* tm = &L.op[oi].tmap;
             for (int sg = 0, col = 0; sg < nseg; ++sg, col += step) {
-                if (!mbar_wait(&empty[s], phase, 1u, poisoned)) return;
-                if (issued++ == pre && !mbar_wait(xready, 0u, 3u, poisoned)) return;
+                if (!mbar_wait(&empty[s], phase, 1u, poisoned) ||
+                    (issued++ == pre && !mbar_wait(xready, 0u, 3u, poisoned))) {
+                    stop = true;
+                    break;
+                }
                 // one box: 16 rows x wbox bytes from the 16-byte-aligned column at or
                 // below the segment start (rows past M and columns past the row end
                 // read as zeros)
                 mbar_arrive_expect_tx(&full[s], box);
                 tma_2d_g2s(stages + s * SB, tm, (col & ~15) / 8, r0, &full[s], policy);
+                issued_mask |= 1u << s;
+                par_mask = (par_mask & ~(1u << s)) | (((phase ^ 1u) & 1u) << s);
                 if (++s == S) {
                     s = 0;
                     phase ^= 1u;
                 }
             }
         }
+        drain_copies(full, S, issued_mask, par_mask, poisoned);
         return;
     }
     if (warp == 0) {
@@ -1377,6 +1418,7 @@ __global__ void __launch_bounds__(kThreads, 1) stream_gemv_kernel(const __grid_c
         while (oi + 1 < n_ops && u >= T.op[oi + 1].unit_begin) ++oi;
         int s = 0, issued = 0;
         uint32_t phase = 1;  // the first pass finds every slot free
+        uint32_t issued_mask = 0, par_mask = 0;  // for drain_copies
         for (; u < total; u += gridDim.x) {
             while (oi + 1 < n_ops && u >= T.op[oi + 1].unit_begin) ++oi;
             const OpInfo& op = T.op[oi];
@@ -1420,6 +1462,8 @@ __global__ void __launch_bounds__(kThreads, 1) stream_gemv_kernel(const __grid_c
                     __syncwarp();
                     if (active) bulk_g2s(dst + lane * wbox, reinterpret_cast<const void*>(ga), bytes, &full[s], policy);
                 }
+                issued_mask |= 1u << s;
+                par_mask = (par_mask & ~(1u << s)) | (((phase ^ 1u) & 1u) << s);
                 if (++s == S) {
                     s = 0;
                     phase ^= 1u;
@@ -1427,6 +1471,7 @@ __global__ void __launch_bounds__(kThreads, 1) stream_gemv_kernel(const __grid_c
             }
             if (stop) break;
         }
+        if (lane == 0) drain_copies(full, S, issued_mask, par_mask, poisoned);
         return;
     }
 
@@ -1444,7 +1489,7 @@ __global__ void __launch_bounds__(kThreads, 1) stream_gemv_kernel(const __grid_c
     if (L.tp.world > 1 && ct == 0) {
         tp_seq = *reinterpret_cast<volatile uint32_t*>(L.tp.state + 1);
         if (blockIdx.x == 0) tp_signal_peers(L.tp.sig, L.tp.world, L.tp.rank);
-        tp_wait_peers(L.tp.sig, L.tp.world, L.tp.rank, tp_seq + 1u, poisoned);
+        tp_wait_peers(L.tp.sig, L.tp.world, L.tp.rank, tp_seq + 1u, poisoned, L.spin_limit);
     }
     Ring R{stages, full, empty, poisoned, SB, S, 0, 0u, 0u};
     const int n_ops = T.n_ops, total = T.total_units;
@@ -1593,7 +1638,7 @@ __global__ void tp_wait_kernel(const __grid_constant__ TpSig t) {
     if (threadIdx.x == 0) {
         const uint32_t seq = t.state[1];
         tp_signal_peers(t.sig, t.world, t.rank);
-        tp_wait_peers(t.sig, t.world, t.rank, seq + 1u, nullptr);
+        tp_wait_peers(t.sig, t.world, t.rank, seq + 1u, nullptr, t.spin_limit);
         t.state[1] = seq + 1u;
     }
 }
@@ -1665,10 +1710,18 @@ bool stream_supported(const MulMatOp* ops, int n_ops) {
     return true;
 }
 
+namespace {
+std::atomic<uint32_t> g_wait_limit{kSpinLimit};
+}
+
+void set_stream_wait_limit(uint32_t polls) { g_wait_limit.store(polls ? polls : kSpinLimit); }
+
 int launch_stream(const MulMatOp* ops, int n_ops, cudaStream_t stream, int num_sms, const TpLaunch* tp,
                   const ProLaunch* pro) {
     SList L{};
     L.n_ops = n_ops;
+    L.spin_limit = g_wait_limit.load();
+    L.tp.spin_limit = L.spin_limit;
     const int kind = pro ? pro->kind : kProNone;
     if (kind < kProNone || kind > kProGelu) return -static_cast<int>(cudaErrorInvalidValue);
     if (pro) {
@@ -1779,6 +1832,7 @@ int launch_stream(const MulMatOp* ops, int n_ops, cudaStream_t stream, int num_s
 
 int launch_tp_wait(const TpLaunch& tp, cudaStream_t stream) {
     TpSig t{};
+    t.spin_limit = g_wait_limit.load();
     t.world = tp.world;
     t.rank = tp.rank;
     for (int r = 0; r < kMaxRanks; ++r) t.sig[r] = tp.sig[r];

@@ -708,7 +708,18 @@ int32_t wllm_sync(void) {
     e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(s, e, "wllm_sync (pending error)");
     const unsigned kerr = wllm::read_and_clear_stream_error() | (wllm::read_and_clear_prefill_error() << 8);
-    if (kerr) return fail(s, "wllm_sync: a kernel gave up waiting on a pipeline barrier (code 0x%x)", kerr);
+    if (kerr)
+        return fail(s,
+                    "wllm_sync: a kernel gave up waiting (code 0x%x: bits 0-1 a pipeline barrier, 2 a row-sharded "
+                    "peer's signal, 3 an in-flight copy; bits 8+ the prefill GEMM)",
+                    kerr);
+    return WLLM_STATUS_OK;
+}
+
+int32_t wllm_set_wait_limit(uint32_t polls) {
+    State& s = S();
+    std::lock_guard<std::mutex> g(s.mu);
+    wllm::set_stream_wait_limit(polls);
     return WLLM_STATUS_OK;
 }
 

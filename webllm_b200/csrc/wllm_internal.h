@@ -104,6 +104,9 @@ int launch_stream(const MulMatOp* ops, int n_ops, cudaStream_t stream, int num_s
 int launch_tp_wait(const TpLaunch& tp, cudaStream_t stream);
 // Error code recorded by a bounded wait that timed out (0 = none); clears it.
 unsigned read_and_clear_stream_error();
+// Polls a bounded wait of the streaming kernel (and the row-sharded peer
+// wait) makes before it gives up; 0 restores the default (2^26, seconds).
+void set_stream_wait_limit(uint32_t polls);
 
 // Prefill GEMM (mulmat_prefill.cu): Q4_K, Q5_K, Q8_0 and Q4_0 weights, or Q6_K with
 // rows of 16-byte multiples (or 8-byte, M even), with N >= kPrefillMinN vectors on tcgen05 tensor cores (f16 operands, f32 accumulation). The

@@ -3,8 +3,14 @@ buffers (device memory) straight from the file.
 
 The parser mirrors the reference's GgufParser (src/models/gguf-parser.ts:
 19-66 `parse`, 144-294 the readers; constants src/models/gguf-types.ts:2-24):
-same fields, the same alignment rule (`general.alignment`, default 32) and
-the same errors (bad magic, a version other than 3, an unknown value type).
+same fields, the same alignment rule (`general.alignment` when it is a
+number, UINT64/INT64 included since the reference converts those with
+Number(); otherwise 32) and the same errors (bad magic, a version other than
+3, an unknown value type). `total_data_size` is, as in the reference's
+calculateTotalDataSize, elements x bytes per element, fractional when a
+tensor is not whole blocks; only streaming such a tensor raises. One
+deliberate difference: an alignment <= 0 raises ValueError here, where the
+reference would compute a NaN or infinite data offset.
 
 `stream_to_buffers` replaces the reference's upload path, which copies each
 tensor through a 4 MiB scratch buffer in the wasm heap
@@ -15,8 +21,10 @@ block layout the kernels read, so there is no repacking.
 """
 from __future__ import annotations
 
+import math
 import mmap
 import struct
+import traceback
 from dataclasses import dataclass, field
 from fractions import Fraction
 
@@ -91,11 +99,17 @@ class _Reader:
         raise ValueError(f"Unknown GGUF value type: {vtype}")
 
 
-def tensor_nbytes(t: GgufTensorInfo) -> int:
-    """Bytes of a tensor's data: elements x the type's bytes per element."""
+def _elements(t: GgufTensorInfo) -> int:
     n = 1
     for d in t.dimensions:
         n *= int(d)
+    return n
+
+
+def tensor_nbytes(t: GgufTensorInfo) -> int:
+    """Bytes of a tensor's data: elements x the type's bytes per element
+    (ValueError when that is not whole blocks)."""
+    n = _elements(t)
     size = n * TYPE_SIZE.get(t.type, Fraction(4))
     if size.denominator != 1:
         raise ValueError(f"tensor {t.name}: {n} elements are not whole blocks of type {t.type}")
@@ -124,10 +138,13 @@ def parse(data) -> GgufContext:
         ttype = r.scalar("<I")
         ctx.tensors.append(GgufTensorInfo(name, nd, dims, ttype, r.scalar("<Q")))
     align = ctx.metadata.get("general.alignment")
-    if align is not None and isinstance(align[1], int) and not isinstance(align[1], bool):
+    if align is not None and isinstance(align[1], (int, float)) and not isinstance(align[1], bool):
+        if not align[1] > 0:
+            raise ValueError(f"Invalid GGUF alignment: {align[1]}")
         ctx.alignment = align[1]
-    ctx.data_offset = -(-r.pos // ctx.alignment) * ctx.alignment
-    ctx.total_data_size = max((t.offset + tensor_nbytes(t) for t in ctx.tensors), default=0)
+    ctx.data_offset = math.ceil(r.pos / ctx.alignment) * ctx.alignment
+    total = max((t.offset + _elements(t) * TYPE_SIZE.get(t.type, Fraction(4)) for t in ctx.tensors), default=0)
+    ctx.total_data_size = int(total) if Fraction(total).denominator == 1 else float(total)
     return ctx
 
 
@@ -135,15 +152,21 @@ def stream_to_buffers(path: str, data_manager, chunk_bytes: int = 64 << 20, name
     """Allocate one library buffer per tensor (all, or those in `names`) and
     write its bytes from the memory-mapped file in chunks of `chunk_bytes`.
     `data_manager` has the GpuDataManager interface (alloc(size) -> handle,
-    write(handle, offset, uint8 array)). Returns {name: (handle, info,
-    nbytes)}. The caller frees the handles."""
+    write(handle, offset, uint8 array), free(handle)). Returns {name:
+    (handle, info, nbytes)}; the caller frees the handles. If any tensor
+    fails, the handles already allocated are freed and the error is raised
+    once the mapping is closed (its traceback is attached as a note: frames
+    kept alive by it would hold views of the mapping and stop it closing)."""
     if chunk_bytes <= 0:
         raise ValueError("chunk_bytes must be positive")
     out = {}
-    with open(path, "rb") as f, mmap.mmap(f.fileno(), 0, access=mmap.ACCESS_READ) as mm:
-        ctx = parse(mm)
-        base = np.frombuffer(mm, dtype=np.uint8)
+    pending = None
+    with open(path, "rb") as f:
+        mm = mmap.mmap(f.fileno(), 0, access=mmap.ACCESS_READ)
         try:
+            base = np.frombuffer(mm, dtype=np.uint8)
+            view = None
+            ctx = parse(mm)
             for t in ctx.tensors:
                 if names is not None and t.name not in names:
                     continue
@@ -155,7 +178,20 @@ def stream_to_buffers(path: str, data_manager, chunk_bytes: int = 64 << 20, name
                 out[t.name] = (h, t, nbytes)
                 for off in range(0, nbytes, chunk_bytes):
                     n = min(chunk_bytes, nbytes - off)
-                    data_manager.write(h, off, base[start + off:start + off + n])
+                    view = base[start + off:start + off + n]
+                    data_manager.write(h, off, view)
+                    del view
+        except BaseException as e:  # noqa: BLE001 - re-raised below, after the mapping closes
+            for h, _, _ in out.values():
+                data_manager.free(h)
+            out = {}
+            pending = e
+            pending.add_note("".join(traceback.format_exception(e)))
+            pending.__traceback__ = None
+            del e
         finally:
-            del base  # the mapping closes only once no array refers to it
+            base = view = None  # the mapping closes only once no array refers to it
+            mm.close()
+    if pending is not None:
+        raise pending
     return out

@@ -64,7 +64,7 @@ EXPORTED_SYMBOLS = (
     "wllm_get_stream",
     "wllm_graph_begin", "wllm_graph_end", "wllm_graph_launch", "wllm_graph_destroy",
     "wllm_dequantize", "wllm_version", "wllm_mul_mat_prefill_static",
-    "wllm_ipc_alloc", "wllm_ipc_open", "wllm_ipc_close", "wllm_ipc_free", "wllm_mul_mat_batch_tp", "wllm_tp_wait",
+    "wllm_ipc_alloc", "wllm_ipc_open", "wllm_ipc_close", "wllm_ipc_free", "wllm_mul_mat_batch_tp", "wllm_tp_wait", "wllm_set_wait_limit",
 )
 
 MAX_RANKS = 8
@@ -139,6 +139,7 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
         "wllm_ipc_free": ([vp], i32),
         "wllm_mul_mat_batch_tp": ([P(MulMatArgs), P(TpOutputs), i32, P(TpGroup), vp], i32),
         "wllm_tp_wait": ([P(TpGroup), vp], i32),
+        "wllm_set_wait_limit": ([ctypes.c_uint32], i32),
         "wllm_get_stream": ([P(vp)], i32),
         "wllm_graph_begin": ([], i32),
         "wllm_graph_end": ([P(i32)], i32),
@@ -500,6 +501,12 @@ def mul_mat_batch_tp(ops: Sequence[MulMatArgs], outs: Sequence[Sequence[int]], g
 def tp_wait(group: TpGroup, stream: int = 0) -> int:
     """Waits (on the stream, bounded) for every peer's rows of the last row-sharded launch."""
     return _check(load_library().wllm_tp_wait(ctypes.byref(group), int(stream) or None), "wllm_tp_wait")
+
+
+def set_wait_limit(polls: int) -> None:
+    """Polls before a device-side wait of the decode kernels gives up (0: the
+    default); a wait that gives up fails the next sync instead of hanging."""
+    _check(load_library().wllm_set_wait_limit(int(polls)), "wllm_set_wait_limit")
 
 
 def library_stream() -> int:
