@@ -2,7 +2,7 @@
  * wllm_mulmat — C ABI of the B200 quantized MUL_MAT library.
  *
  * Drop-in for one op of paulrobello/webllm: ggml MUL_MAT with a GGUF
- * quantized src0 (Q4_K, Q5_K, Q6_K, Q4_0, Q8_0) and f32 src1/dst. The ABI mirrors the
+ * quantized src0 (Q4_K, Q5_K, Q6_K, Q4_0, Q8_0, IQ4_XS) and f32 src1/dst. The ABI mirrors the
  * JSEP operator-plugin seam the ggml backend calls per graph node
  * (src/inference/jsep/index.ts:1-21,129-305): seven callbacks
  * alloc/free/write/read/clear/run_op/sync over integer buffer handles, and
@@ -51,6 +51,7 @@ extern "C" {
 #define WLLM_TYPE_Q4_K 12
 #define WLLM_TYPE_Q5_K 13
 #define WLLM_TYPE_Q6_K 14
+#define WLLM_TYPE_IQ4_XS 23
 
 /* Descriptor geometry (matmul.ts:22-41): [op, n_src, dst block, src blocks...],
  * each block = buf_handle, offset, type, ne[4] lo, ne[4] hi, nb[4] lo, nb[4] hi.

@@ -29,6 +29,7 @@ TYPE_Q8_0 = 8
 TYPE_Q4_K = 12
 TYPE_Q5_K = 13
 TYPE_Q6_K = 14
+TYPE_IQ4_XS = 23
 
 
 def build(force: bool = False) -> str:

@@ -50,6 +50,7 @@ int32_t oracle_block_elems(int32_t type) {
         case ORACLE_TYPE_Q4_K: return 256;
         case ORACLE_TYPE_Q5_K: return 256;
         case ORACLE_TYPE_Q6_K: return 256;
+        case ORACLE_TYPE_IQ4_XS: return 256;
         default: return 0;
     }
 }
@@ -63,6 +64,7 @@ int32_t oracle_block_bytes(int32_t type) {
         case ORACLE_TYPE_Q4_K: return 144;
         case ORACLE_TYPE_Q5_K: return 176;
         case ORACLE_TYPE_Q6_K: return 210;
+        case ORACLE_TYPE_IQ4_XS: return 136; /* ggml block_iq4_xs; not in the reference's ggmlTypeSize */
         default: return 0;
     }
 }
@@ -166,6 +168,35 @@ static void dequant_block_q6_K(const uint8_t* b, float* y) {
     }
 }
 
+/* The 16 non-linear 4-bit levels of IQ4_NL / IQ4_XS (ggml's kvalues_iq4nl,
+ * a fixed part of the format). */
+static const int8_t kIq4Levels[16] = {-127, -104, -83, -65, -49, -35, -22, -10, 1, 13, 25, 38, 53, 69, 89, 113};
+
+/* One 136-byte IQ4_XS super-block -> 256 floats (ggml block_iq4_xs: f16 d
+ * @0, u16 scales_h @2, scales_l[4] @4, qs[128] @8). The reference has no
+ * IQ4_XS code of its own (ggml is in the un-vendored llama.cpp fork; the
+ * type appears as file type 30 in src/models/model-loader.ts:906 and as a
+ * canonical fleet quant in docs/MODEL_SUPPORT.md:135,294). Sub-block j
+ * (0..7) holds elements 32j..32j+31 with the 6-bit scale
+ * ls = (scales_l[j/2] >> 4(j%2)) & 15 | ((scales_h >> 2j) & 3) << 4; element
+ * 32j+l (l < 16) is level[qs[16j+l] & 15], element 32j+16+l is
+ * level[qs[16j+l] >> 4]; y = d*(ls - 32)*level. d*(ls - 32) has at most 16
+ * significant bits and the level 7, so both products are exact in f32. */
+static void dequant_block_iq4_xs(const uint8_t* b, float* y) {
+    const float d = oracle_f16_to_f32(rd16(b));
+    const unsigned scales_h = rd16(b + 2);
+    const uint8_t* scales_l = b + 4;
+    const uint8_t* qs = b + 8;
+    for (int j = 0; j < 8; ++j) {
+        const int ls = ((scales_l[j / 2] >> (4 * (j % 2))) & 0xF) | (((scales_h >> (2 * j)) & 3) << 4);
+        const float dl = d * (float)(ls - 32);
+        for (int l = 0; l < 16; ++l) {
+            y[32 * j + l] = dl * (float)kIq4Levels[qs[16 * j + l] & 0xF];
+            y[32 * j + 16 + l] = dl * (float)kIq4Levels[qs[16 * j + l] >> 4];
+        }
+    }
+}
+
 /* One 34-byte Q8_0 block -> 32 floats: f16 d @0, int8 qs[32] @2; y = d*q. */
 static void dequant_block_q8_0(const uint8_t* b, float* y) {
     const float d = oracle_f16_to_f32(rd16(b));
@@ -185,6 +216,7 @@ int32_t oracle_dequantize_row(int32_t type, const void* src, float* dst, int64_t
             case ORACLE_TYPE_Q6_K: dequant_block_q6_K(s + i * bb, dst + i * be); break;
             case ORACLE_TYPE_Q4_0: dequant_block_q4_0(s + i * bb, dst + i * be); break;
             case ORACLE_TYPE_Q8_0: dequant_block_q8_0(s + i * bb, dst + i * be); break;
+            case ORACLE_TYPE_IQ4_XS: dequant_block_iq4_xs(s + i * bb, dst + i * be); break;
             case ORACLE_TYPE_F32: memcpy(dst + i, s + 4 * i, 4); break;
             default: return -1;
         }

@@ -41,7 +41,8 @@ enum {
     ORACLE_TYPE_Q8_0 = 8,
     ORACLE_TYPE_Q4_K = 12,
     ORACLE_TYPE_Q5_K = 13,
-    ORACLE_TYPE_Q6_K = 14
+    ORACLE_TYPE_Q6_K = 14,
+    ORACLE_TYPE_IQ4_XS = 23
 };
 
 /* Exact IEEE binary16 -> binary32 (normals, subnormals, inf, nan). */

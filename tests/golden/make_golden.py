@@ -22,11 +22,11 @@ q4k_synth_64x2048.npz
     runMatmulProductionSelfTest (smoke-test/p2-v2-spike.src.ts:287-330,340-360),
     expected dequant and the f64-accumulated reference product.
 gguf_blocks.npz
-    Random blocks of Q4_K, Q6_K, Q8_0, Q5_K and Q4_0 (seeded) with the
-    dequantization of the third-party `gguf` python package 0.19.0
+    Random blocks of Q4_K, Q6_K, Q8_0, Q5_K, Q4_0 and IQ4_XS (seeded) with
+    the dequantization of the third-party `gguf` python package 0.19.0
     (gguf.quants.dequantize), the published ggml block formats the
     reference's llama.cpp fork uses. The reference repository has no
-    Q6_K/Q8_0/Q5_K/Q4_0 code of its own.
+    Q6_K/Q8_0/Q5_K/Q4_0/IQ4_XS code of its own.
 """
 from __future__ import annotations
 
@@ -149,11 +149,11 @@ def make_gguf_blocks():
     from importlib.metadata import version
 
     out = {"gguf_version": np.array(version("gguf"))}
-    # (the Q5_K / Q4_0 blocks come after the others: the earlier arrays keep
-    # their random streams)
-    scale_offsets = {T.Q4_K: (0, 2), T.Q5_K: (0, 2), T.Q6_K: (208,), T.Q8_0: (0,), T.Q4_0: (0,)}
+    # (blocks of types added later come after the others: the earlier arrays
+    # keep their random streams)
+    scale_offsets = {T.Q4_K: (0, 2), T.Q5_K: (0, 2), T.Q6_K: (208,), T.Q8_0: (0,), T.Q4_0: (0,), T.IQ4_XS: (0,)}
     for name, t, bb in (("q4_k", T.Q4_K, 144), ("q6_k", T.Q6_K, 210), ("q8_0", T.Q8_0, 34), ("q5_k", T.Q5_K, 176),
-                        ("q4_0", T.Q4_0, 18)):
+                        ("q4_0", T.Q4_0, 18), ("iq4_xs", T.IQ4_XS, 136)):
         nblk = 64
         raw = rng.integers(0, 256, size=(nblk, bb), dtype=np.uint8)
         # finite f16 scales spanning normals and subnormals

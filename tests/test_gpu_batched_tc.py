@@ -1,0 +1,90 @@
+"""The tcgen05 small-batch GEMM (Q4_K and Q5_K weights, several sequences
+decoding together, N = 5..64, and N = 3-4 where the streaming kernel cannot
+take the shape): both error metrics of the path (max-normalized and
+per-element, 1e-3) against a float64 matmul of the device-dequantized
+weights, on N(0,1) activations and on outlier channels; shapes with partial
+row tiles, split K and K not a multiple of 1024."""
+from __future__ import annotations
+
+import zlib
+
+import numpy as np
+import pytest
+
+from oracle import oracle as O
+from webllm_b200 import jsep, synth
+
+pytestmark = pytest.mark.gpu
+
+TOL = 1e-3
+
+
+def _run(runtime, qtype, M, K, x_np, seed):
+    import torch
+
+    dev = torch.device("cuda", 0)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(seed)
+    N = x_np.shape[0]
+    w = synth.weights_torch(gen, qtype, M, K, dev)
+    x = torch.from_numpy(x_np).to(dev)
+    y = torch.full((N, M), float("nan"), device=dev)
+    torch.cuda.synchronize()
+    stream = jsep.library_stream()
+    k0 = _kernels()
+    assert jsep.mul_mat_device(qtype, w.data_ptr(), w.shape[1], x.data_ptr(), K, y.data_ptr(), M, M, K, N,
+                               stream) == jsep.STATUS_OK, jsep.last_error()
+    launched = _kernels() - k0
+    wf = torch.empty(M, K, device=dev)
+    jsep.dequantize_device(qtype, w.data_ptr(), wf.data_ptr(), M * K, stream)
+    runtime.jsep_sync()
+    ref = (wf.double() @ x.double().t()).t()
+    return y.double().cpu().numpy(), ref.cpu().numpy(), launched
+
+
+def _kernels():
+    c = jsep.WllmCounters()
+    jsep.load_library().wllm_get_counters(c)
+    return c.kernels_launched
+
+
+@pytest.mark.parametrize("N", [5, 8, 16, 33, 64])
+@pytest.mark.parametrize("qtype,M,K", [(jsep.GGML_TYPE_Q4_K, 4096, 4096), (jsep.GGML_TYPE_Q4_K, 14336, 4096),
+                                       (jsep.GGML_TYPE_Q4_K, 4096, 14336), (jsep.GGML_TYPE_Q4_K, 1000, 2304),
+                                       (jsep.GGML_TYPE_Q5_K, 4096, 4096), (jsep.GGML_TYPE_Q5_K, 333, 3072),
+                                       (jsep.GGML_TYPE_Q4_K, 128, 256)])
+def test_batched_tc_both_metrics(runtime, qtype, M, K, N):
+    rng = np.random.default_rng(zlib.crc32(repr((qtype, M, K, N)).encode()))
+    x = synth.activations(rng, N, K)
+    y, r, launched = _run(runtime, qtype, M, K, x, seed=M + K + N)
+    assert launched == 2  # the activation pre-pass and the GEMM
+    assert np.all(np.isfinite(y))
+    a, b = O.rel_error(y, r), O.rel_error_elem(y, r)
+    assert a <= TOL and b <= TOL, (a, b)
+
+
+@pytest.mark.parametrize("value", [100.0, 1000.0, 3e4])
+@pytest.mark.parametrize("N", [8, 64])
+def test_batched_tc_outlier_channels(runtime, N, value):
+    """Outlier channels (the activation split is per element, so they cost
+    nothing), up to 3e4 (the f16 range is handled by the per-vector scale)."""
+    rng = np.random.default_rng(int(value) + N)
+    x = synth.activations_with_outliers(rng, N, 4096, value)
+    y, r, _ = _run(runtime, jsep.GGML_TYPE_Q4_K, 12288, 4096, x, seed=N)
+    a, b = O.rel_error(y, r), O.rel_error_elem(y, r)
+    assert a <= TOL and b <= TOL, (a, b)
+
+
+def test_batched_tc_tiny_and_huge_activations(runtime):
+    """Vectors scaled by 1e-30 and 1e30 and an all-zero vector in one batch:
+    each vector has its own power-of-two scale."""
+    rng = np.random.default_rng(9)
+    x = synth.activations(rng, 8, 2048)
+    x[1] *= np.float32(1e-30)
+    x[2] *= np.float32(1e30)
+    x[3] = 0.0
+    y, r, _ = _run(runtime, jsep.GGML_TYPE_Q4_K, 512, 2048, x, seed=9)
+    assert np.all(y[3] == 0.0)
+    for n in (0, 1, 2, 4):
+        a, b = O.rel_error(y[n], r[n]), O.rel_error_elem(y[n], r[n])
+        assert a <= TOL and b <= TOL, (n, a, b)

@@ -65,7 +65,7 @@ def test_q4k_synth_64x2048(runtime, golden):
 
 @pytest.mark.parametrize("qtype,name", [(jsep.GGML_TYPE_Q4_K, "q4_k"), (jsep.GGML_TYPE_Q6_K, "q6_k"),
                                         (jsep.GGML_TYPE_Q8_0, "q8_0"), (jsep.GGML_TYPE_Q5_K, "q5_k"),
-                                        (jsep.GGML_TYPE_Q4_0, "q4_0")])
+                                        (jsep.GGML_TYPE_Q4_0, "q4_0"), (jsep.GGML_TYPE_IQ4_XS, "iq4_xs")])
 def test_device_dequant_bit_exact(runtime, golden, qtype, name):
     z = golden("gguf_blocks.npz")
     raw = z[f"{name}_raw"]
@@ -96,7 +96,7 @@ SHAPES = [(1, 256, 1), (7, 512, 1), (33, 768, 2), (257, 1024, 3), (64, 2048, 5),
 
 
 @pytest.mark.parametrize("qtype", [jsep.GGML_TYPE_Q4_K, jsep.GGML_TYPE_Q6_K, jsep.GGML_TYPE_Q8_0,
-                                   jsep.GGML_TYPE_Q5_K, jsep.GGML_TYPE_Q4_0])
+                                   jsep.GGML_TYPE_Q5_K, jsep.GGML_TYPE_Q4_0, jsep.GGML_TYPE_IQ4_XS])
 @pytest.mark.parametrize("M,K,N", SHAPES)
 def test_gemv_random_shapes(runtime, qtype, M, K, N):
     be, _ = jsep.BLOCK_GEOMETRY[qtype]
@@ -710,3 +710,47 @@ def test_buffers_roundtrip_clear_and_async_read(runtime):
     c = runtime.counters()
     assert c["alloc"] >= 1 and c["write"] >= 1 and c["read"] >= 2
     dm.free(h)
+
+
+@pytest.mark.parametrize("N", [1, 2, 3, 4])
+@pytest.mark.parametrize("M,K", [(4096, 4096), (1024, 4096), (12288, 4096), (4096, 12288), (3072, 3072),
+                                 (1000, 2304), (33, 256)])
+def test_iq4_xs_decode_vs_torch_fp64(runtime, M, K, N):
+    """IQ4_XS (136-byte blocks, non-linear 4-bit levels, 6-bit sub-block
+    scales) on the streaming integer tensor-core GEMV (and the general
+    kernel where the streaming one does not take the shape: K = 2304 rows
+    are 1224 bytes, not 16-byte aligned, so they are copied row by row),
+    against a float64 matmul of the device-dequantized weights, both
+    metrics."""
+    import torch
+
+    dev = torch.device("cuda", 0)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(23 * 1000 + M + K + N)
+    t = jsep.GGML_TYPE_IQ4_XS
+    w = synth.weights_torch(gen, t, M, K, dev)
+    x = torch.randn(N, K, device=dev, generator=gen)
+    y = torch.full((N, M), float("nan"), device=dev)
+    torch.cuda.synchronize()
+    stream = jsep.library_stream()
+    assert jsep.mul_mat_device(t, w.data_ptr(), w.shape[1], x.data_ptr(), K, y.data_ptr(), M, M, K, N,
+                               stream) == jsep.STATUS_OK
+    wf = torch.empty(M, K, device=dev)
+    jsep.dequantize_device(t, w.data_ptr(), wf.data_ptr(), M * K, stream)
+    runtime.jsep_sync()
+    ref = (wf.double() @ x.double().t()).t().cpu().numpy()
+    got = y.double().cpu().numpy()
+    assert O.rel_error(got, ref) <= GEMV_TOL and O.rel_error_elem(got, ref) <= GEMV_TOL
+
+
+def test_iq4_xs_through_the_descriptor_seam_vs_oracle(runtime):
+    """IQ4_XS through wllm_run_op (the jsepRunOp descriptor), against the
+    oracle's f64 dequant-then-dot (pinned to gguf 0.19.0's dequantization)."""
+    rng = np.random.default_rng(2300)
+    t = jsep.GGML_TYPE_IQ4_XS
+    for M, K, N in ((96, 2048, 1), (40, 4096, 2), (17, 1024, 5)):
+        w = synth.weights(rng, t, M, K)
+        x = synth.activations(rng, N, K)
+        got = run_mul_mat(runtime, t, w, x)
+        r = O.mul_mat_f64(t, w, x)
+        assert O.rel_error(got, r) <= GEMV_TOL and O.rel_error_elem(got, r) <= GEMV_TOL, (M, K, N)

@@ -43,6 +43,8 @@ SHAPES = [
     ("gemma2_down", jsep.GGML_TYPE_Q8_0, 2304, 9216),
     ("q5k", jsep.GGML_TYPE_Q5_K, 4096, 4096),
     ("q4_0", jsep.GGML_TYPE_Q4_0, 4096, 4096),
+    ("iq4_xs", jsep.GGML_TYPE_IQ4_XS, 4096, 4096),
+    ("iq4_xs_down", jsep.GGML_TYPE_IQ4_XS, 4096, 12288),
 ]
 
 

@@ -75,7 +75,7 @@ def test_q4k_synth_matrix(golden):
 
 @pytest.mark.parametrize("name,qtype,be", [("q4_k", O.TYPE_Q4_K, 256), ("q6_k", O.TYPE_Q6_K, 256),
                                             ("q8_0", O.TYPE_Q8_0, 32), ("q5_k", O.TYPE_Q5_K, 256),
-                                            ("q4_0", O.TYPE_Q4_0, 32)])
+                                            ("q4_0", O.TYPE_Q4_0, 32), ("iq4_xs", O.TYPE_IQ4_XS, 256)])
 def test_dequant_matches_gguf(golden, name, qtype, be):
     z = golden("gguf_blocks.npz")
     raw = z[f"{name}_raw"]
@@ -84,7 +84,7 @@ def test_dequant_matches_gguf(golden, name, qtype, be):
     assert np.array_equal(got.view(np.uint32), ref.view(np.uint32)), name
 
 
-@pytest.mark.parametrize("qtype", [O.TYPE_Q4_K, O.TYPE_Q6_K, O.TYPE_Q8_0, O.TYPE_Q5_K, O.TYPE_Q4_0])
+@pytest.mark.parametrize("qtype", [O.TYPE_Q4_K, O.TYPE_Q6_K, O.TYPE_Q8_0, O.TYPE_Q5_K, O.TYPE_Q4_0, O.TYPE_IQ4_XS])
 def test_f32_baseline_close_to_f64(qtype):
     rng = np.random.default_rng(7)
     M, K, N = 37, 1024, 3

@@ -20,7 +20,8 @@ REPO_DIR = os.path.dirname(PKG_DIR)
 CSRC = os.path.join(PKG_DIR, "csrc")
 LIB_PATH = os.path.join(PKG_DIR, "libwllm_mulmat.so")
 
-SOURCES = ["runtime.cpp", "mulmat_gemv.cu", "mulmat_stream.cu", "mulmat_prefill.cu", "mulmat_batched.cu"]
+SOURCES = ["runtime.cpp", "mulmat_gemv.cu", "mulmat_stream.cu", "mulmat_prefill.cu", "mulmat_batched.cu",
+           "mulmat_batched_tc.cu"]
 HEADERS = ["wllm_internal.h", "quant_blocks.cuh"]
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 

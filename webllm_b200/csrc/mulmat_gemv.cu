@@ -81,6 +81,40 @@ __device__ __forceinline__ void row_q4_k(const uint8_t* wrow, const float* const
     }
 }
 
+// IQ4_XS row: lane handles qs bytes 4*lane..4*lane+3 of every block, i.e.
+// elements l0..l0+3 (low nibbles) and 16+l0..16+l0+3 (high nibbles) of
+// sub-block j = lane/4, l0 = 4*(lane%4); the levels come from the table.
+template <int NT>
+__device__ __forceinline__ void row_iq4_xs(const uint8_t* wrow, const float* const* xs, int nt,
+                                           int nblocks, bool vec, int lane, float (&acc)[NT]) {
+    const int j = lane >> 2;
+    const int l0 = (lane & 3) << 2;
+    for (int b = 0; b < nblocks; ++b) {
+        const uint8_t* blk = wrow + static_cast<size_t>(b) * 136;
+        const float d = f16_bits_to_f32(ldg_u16(blk));
+        const uint32_t sh = ldg_u16(blk + 2), sl = ldg_u16(blk + 4) | (ldg_u16(blk + 6) << 16);
+        const uint32_t q = ldg_u32(blk + 8 + 4 * lane);
+        const float dl = d * static_cast<float>(iq4xs_scale(sh, sl, j));
+        float ql[4], qh[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            ql[i] = static_cast<float>(iq4_level((q >> (8 * i)) & 0xFu));
+            qh[i] = static_cast<float>(iq4_level((q >> (8 * i + 4)) & 0xFu));
+        }
+        const int k0 = b * 256 + 32 * j + l0;
+#pragma unroll
+        for (int n = 0; n < NT; ++n) {
+            if (n < nt) {
+                const float4 xl = ldx4(xs[n] + k0, vec);
+                const float4 xh = ldx4(xs[n] + k0 + 16, vec);
+                const float s = ql[0] * xl.x + ql[1] * xl.y + ql[2] * xl.z + ql[3] * xl.w + qh[0] * xh.x +
+                                qh[1] * xh.y + qh[2] * xh.z + qh[3] * xh.w;
+                acc[n] += dl * s;
+            }
+        }
+    }
+}
+
 // Q5_K row: as Q4_K (qs at +48), with bit j of qh[l] as the fifth bit of
 // sub-block j's element l.
 template <int NT>
@@ -276,6 +310,8 @@ __global__ void __launch_bounds__(kWarps * 32) gemv_kernel(const __grid_constant
             row_q6_k<NT>(wrow, xs, nt, nblocks, lane, acc);
         } else if (op.type == kTypeQ4_0) {
             row_q4_0<NT>(wrow, xs, nt, nblocks, vec, lane, acc);
+        } else if (op.type == kTypeIQ4_XS) {
+            row_iq4_xs<NT>(wrow, xs, nt, nblocks, vec, lane, acc);
         } else {
             row_q8_0<NT>(wrow, xs, nt, nblocks, vec, lane, acc);
         }
@@ -299,6 +335,8 @@ __global__ void dequant_kernel(int type, const uint8_t* __restrict__ src, float*
         dst[i] = q4_0_dequant_elem(src + (i >> 5) * 18, static_cast<int>(i & 31));
     } else if (type == kTypeQ6_K) {
         dst[i] = q6k_dequant_elem(src + (i >> 8) * 210, static_cast<int>(i & 255));
+    } else if (type == kTypeIQ4_XS) {
+        dst[i] = iq4xs_dequant_elem(src + (i >> 8) * 136, static_cast<int>(i & 255));
     } else {
         dst[i] = q8_0_dequant_elem(src + (i >> 5) * 34, static_cast<int>(i & 31));
     }
@@ -308,16 +346,16 @@ __global__ void dequant_kernel(int type, const uint8_t* __restrict__ src, float*
 
 const char* check_mulmat_op(const MulMatOp& op) {
     if (op.type != kTypeQ4_K && op.type != kTypeQ5_K && op.type != kTypeQ6_K && op.type != kTypeQ4_0 &&
-        op.type != kTypeQ8_0)
+        op.type != kTypeQ8_0 && op.type != kTypeIQ4_XS)
         return "unsupported src0 type";
     if (op.M <= 0 || op.K <= 0 || op.N <= 0 || op.ne2 <= 0 || op.ne3 <= 0) return "empty or negative shape";
     if (op.r2 <= 0 || op.r3 <= 0) return "bad broadcast factor";
     if (op.K % block_elems(op.type) != 0) return "K is not a multiple of the block size";
     const uintptr_t wa = reinterpret_cast<uintptr_t>(op.w);
-    const int need = (op.type == kTypeQ4_K || op.type == kTypeQ5_K) ? 4 : 2;
+    const int need = (op.type == kTypeQ4_K || op.type == kTypeQ5_K || op.type == kTypeIQ4_XS) ? 4 : 2;
     if ((wa | static_cast<uintptr_t>(op.w_nb1) | static_cast<uintptr_t>(op.w_nb2) |
          static_cast<uintptr_t>(op.w_nb3)) % need)
-        return need == 4 ? "src0 data/strides must be 4-byte aligned for Q4_K/Q5_K"
+        return need == 4 ? "src0 data/strides must be 4-byte aligned for Q4_K/Q5_K/IQ4_XS"
                          : "src0 data/strides must be 2-byte aligned";
     if (op.w_nb1 < static_cast<int64_t>(op.K / block_elems(op.type)) * block_bytes(op.type)) return "src0 nb1 too small";
     if ((reinterpret_cast<uintptr_t>(op.x) | static_cast<uintptr_t>(op.x_nb1) | static_cast<uintptr_t>(op.x_nb2) |
@@ -331,11 +369,19 @@ const char* check_mulmat_op(const MulMatOp& op) {
     return nullptr;
 }
 
+// Q4_K / Q5_K with 5 to 64 vectors (and 3 or 4 where the streaming kernel
+// cannot take them) run on the tcgen05 small-batch GEMM.
+bool use_batched_tc(const MulMatOp& o) {
+    if (!batched_tc_supported(o) || o.N < 3) return false;
+    return o.N >= 5 || !stream_supported(&o, 1);
+}
+
 size_t mulmat_workspace_bytes(const MulMatOp* ops, int n_ops) {
     size_t need = 0;
     for (int i = 0; i < n_ops; ++i) {
         size_t b = 0;
         if (prefill_supported(ops[i])) b = prefill_workspace_bytes(ops[i]);
+        else if (use_batched_tc(ops[i])) b = batched_tc_workspace_bytes(ops[i]);
         else if (batched_supported(ops[i])) b = batched_workspace_bytes(ops[i]);
         need = b > need ? b : need;
     }
@@ -354,6 +400,10 @@ int launch_mulmat(const MulMatOp* ops, int n_ops, cudaStream_t stream, int num_s
     for (int i = 0; i < n_ops; ++i) {
         if (prefill_supported(ops[i]) && workspace && workspace_bytes >= prefill_workspace_bytes(ops[i])) {
             const int rc = launch_prefill(ops[i], workspace, workspace_bytes, stream);
+            if (rc < 0) return rc;
+            launched += rc;
+        } else if (use_batched_tc(ops[i]) && workspace && workspace_bytes >= batched_tc_workspace_bytes(ops[i])) {
+            const int rc = launch_batched_tc(ops[i], workspace, workspace_bytes, stream, num_sms);
             if (rc < 0) return rc;
             launched += rc;
         } else if (batched_supported(ops[i]) && !(ops[i].N <= 4 && stream_supported(&ops[i], 1)) && workspace &&

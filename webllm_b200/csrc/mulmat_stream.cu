@@ -79,6 +79,7 @@ constexpr int kQ6kSegBlocks = 9;              // <= 1890 B (+ 16-byte window sla
 constexpr int kQ80SegBlocks = 32;             // 1088 B, whole 8-block groups
 constexpr int kQ5kSegBlocks = 11;             // <= 1936 B
 constexpr int kQ40SegBlocks = 64;             // 1152 B, whole 8-block groups
+constexpr int kIq4SegBlocks = 14;             // 1904 B (+ 16-byte window slack: a 1936 B box row)
 constexpr int kMaxStages = 8;
 constexpr int kRedDelay = 2;                  // a unit's partials are summed this many units later
 // Unit slots in flight: consumer warps drift apart by at most kMaxStages
@@ -327,6 +328,7 @@ __host__ __device__ __forceinline__ int seg_cap(int type) {
         case kTypeQ5_K: return kQ5kSegBlocks;
         case kTypeQ6_K: return kQ6kSegBlocks;
         case kTypeQ4_0: return kQ40SegBlocks;
+        case kTypeIQ4_XS: return kIq4SegBlocks;
         default: return kQ80SegBlocks;
     }
 }
@@ -339,6 +341,7 @@ __device__ __forceinline__ int block_bytes_of(int type) {
         case kTypeQ5_K: return 176;
         case kTypeQ6_K: return 210;
         case kTypeQ4_0: return 18;
+        case kTypeIQ4_XS: return 136;
         default: return 34;
     }
 }
@@ -664,6 +667,69 @@ __device__ __forceinline__ void q6k_item(const uint8_t* pg, const uint8_t* ph, u
     const float mf = hl ? 0.f : -32.f;             // the offset once per pair
     yg = fmaf(dg, fmaf(fmaf(static_cast<float>(a1), 0.0078125f, static_cast<float>(a0) * lf), xf, mf * sg), yg);
     yh = fmaf(dh, fmaf(fmaf(static_cast<float>(a3), 0.0078125f, static_cast<float>(a2) * lf), xf, mf * sh), yh);
+}
+
+// Four IQ4_XS level indices (0..15, one per byte) -> their int8 levels. A
+// byte permute picks from the table's low half (levels 0-7) and another from
+// its high half, by the index's low 3 bits (__byte_perm reads 3 bits per
+// selector nibble); bit 3 of each index, spread over its byte, selects between
+// the two.
+__device__ __forceinline__ uint32_t iq4_lut4(uint32_t idx) {
+    const uint32_t y = idx | (idx >> 4);
+    const uint32_t sel = __byte_perm(y, 0u, 0x4420u) & 0x7777u;  // i0 | i1 << 4 | i2 << 8 | i3 << 12, low 3 bits
+    const uint32_t lo = __byte_perm(kIq4Lv0, kIq4Lv1, sel);
+    const uint32_t hi = __byte_perm(kIq4Lv2, kIq4Lv3, sel);
+    const uint32_t hsel = ((idx >> 3) & 0x01010101u) * 0xFFu;  // 0xFF where the index is 8..15
+    return (hi & hsel) | (lo & ~hsel);
+}
+
+// One IQ4_XS item: 16 rows x one 136-byte block (256 elements), for NP = 1 or
+// 2 vectors. Sub-block j (32 elements) is one MMA on the int8 levels: lane
+// (g, c)'s A fragment for rows g / g+8 is the low nibbles of qs[16j + 4c ..
+// + 3] (k = 4c ..) and their high nibbles (k = 16 + 4c ..), looked up in the
+// level table. As for Q4_K, NS = 2/NP sub-blocks share an accumulator through
+// the B-column slots (sub-block j: slot j % NS, chain j / NS); lane (g, c)
+// scales its slot's sub-blocks by ls - 32 in integer, then by the rows' f16 d.
+// Blocks sit 8-byte aligned in shared memory.
+template <int NP>
+__device__ __forceinline__ void iq4xs_item(const uint8_t* pg, const uint8_t* ph, uint32_t xaddr, uint32_t xzero,
+                                           bool xv0, bool xv1, float xf, int c, int sl, int hl, float& yg,
+                                           float& yh) {
+    static_assert(NP == 1 || NP == 2, "vector pairs");
+    constexpr int NS = NP == 1 ? 2 : 1, NCH = 8 / NS;
+    int D[NCH][4];
+#pragma unroll
+    for (int q = 0; q < NCH; ++q) D[q][0] = D[q][1] = D[q][2] = D[q][3] = 0;
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {  // sub-blocks 2p, 2p+1: one ldmatrix of activations
+        uint32_t x[4];
+        ldmatrix_x4_at(x, ((p & 1) ? xv1 : xv0) ? xaddr + 64 * p : xzero);
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int j = 2 * p + h;
+            const uint32_t wg = lds_u32_any(pg + 8 + 16 * j + 4 * c), wh = lds_u32_any(ph + 8 + 16 * j + 4 * c);
+            imma_s8s8_acc(D[j / NS], iq4_lut4(wg & 0x0F0F0F0Fu), iq4_lut4(wh & 0x0F0F0F0Fu),
+                          iq4_lut4((wg >> 4) & 0x0F0F0F0Fu), iq4_lut4((wh >> 4) & 0x0F0F0F0Fu), x[2 * h],
+                          x[2 * h + 1]);
+        }
+    }
+    // |D| <= 32 * 127 * 127 per sub-block, times |ls - 32| <= 32, over 8: inside int32
+    const uint32_t shg = lds_u16(pg + 2), slg = lds_u32_any(pg + 4);
+    const uint32_t shh = lds_u16(ph + 2), slh = lds_u32_any(ph + 4);
+    int a0 = 0, a1 = 0, a2 = 0, a3 = 0;
+#pragma unroll
+    for (int q = 0; q < NCH; ++q) {
+        const int j = q * NS + sl;
+        const int scg = iq4xs_scale(shg, slg, j), sch = iq4xs_scale(shh, slh, j);
+        a0 += scg * D[q][0];
+        a1 += scg * D[q][1];
+        a2 += sch * D[q][2];
+        a3 += sch * D[q][3];
+    }
+    const float lf = hl ? 6.103515625e-05f : 1.f;  // limb weights (see q4k_items)
+    const float dg = f16_bits_to_f32(lds_u16(pg)), dh = f16_bits_to_f32(lds_u16(ph));
+    yg = fmaf(fmaf(static_cast<float>(a1), 0.0078125f, static_cast<float>(a0) * lf), dg * xf, yg);
+    yh = fmaf(fmaf(static_cast<float>(a3), 0.0078125f, static_cast<float>(a2) * lf), dh * xf, yh);
 }
 
 // One Q8_0 / Q4_0 item: 16 rows x one group of 8 blocks (256 elements, one x
@@ -1298,6 +1364,51 @@ __device__ __forceinline__ void q8_unit(const OpRegs& op, const Q4Lane& qa, cons
     write_partials<NP, NT, NG>(yg, yh, tk, N, lane, ub);
 }
 
+// All segments of one IQ4_XS unit for this consumer warp (see q6k_unit): an
+// item is one block.
+template <int NP, int NT>
+__device__ __forceinline__ void iq4xs_unit(const OpRegs& op, const Q4Lane& qa, const Q4Lane& qb, Ring& R,
+                                           uint32_t xzero, uint32_t glo, int lane, int cw, float* ub) {
+    constexpr int NPI = NP == 1 ? 1 : 2;  // vectors per pass
+    constexpr int NG = NP == 4 ? 2 : 1;   // passes
+    const int N = op.N, nblocks = op.K / 256;
+    const int g = lane >> 2, c = lane & 3;
+    const uint32_t nb1 = static_cast<uint32_t>(op.w_nb1);
+    const Q4Lane qs[2] = {qa, qb};
+    float yg[NG], yh[NG];
+#pragma unroll
+    for (int G = 0; G < NG; ++G) yg[G] = yh[G] = 0.f;
+    for (int sg = 0; sg < op.nseg; ++sg) {
+        const int b0 = sg * op.seg_blocks;
+        const int nb = min(op.seg_blocks, nblocks - b0);
+        const int i0 = (cw - static_cast<int>(R.item_base % kCW) + kCW) % kCW;
+        if (i0 < nb) {
+            ring_wait(R, lane);
+            const uint8_t* stage = R.stages + R.slot * R.SB;
+            const uint32_t gl = glo + static_cast<uint32_t>(b0 * 136);
+            const uint8_t* pg = stage + g * op.wbox + ((gl + static_cast<uint32_t>(g) * nb1) & 15u);
+            const uint8_t* ph = stage + (g + 8) * op.wbox + ((gl + static_cast<uint32_t>(g + 8) * nb1) & 15u);
+            for (int i = i0; i < nb; i += kCW) {
+                const int bg = b0 + i;
+#pragma unroll
+                for (int G = 0; G < NG; ++G) {
+                    const Q4Lane& q = qs[G];
+                    iq4xs_item<NPI>(pg + i * 136, ph + i * 136, q.xcol + bg * 256, xzero, q.xv0, q.xv1,
+                                    16.f * q.dfac[bg], c, q.sl, q.hl, yg[G], yh[G]);
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cnt(&R.empty[R.slot], i0 == 0 ? 1u + kCW - min(nb, kCW) : 1u);
+        }
+        R.item_base += nb;
+        R.advance();
+    }
+    int tk[NG];
+#pragma unroll
+    for (int G = 0; G < NG; ++G) tk[G] = qs[G].tk;
+    write_partials<NP, NT, NG>(yg, yh, tk, N, lane, ub);
+}
+
 // PRO: the fused activation prologue (kProNone for the plain GEMV; each kind
 // is a separate instantiation, so the plain GEMV carries none of their code).
 template <int NT, int PRO>
@@ -1581,6 +1692,16 @@ __global__ void __launch_bounds__(kThreads, 1) stream_gemv_kernel(const __grid_c
                 q6k_unit<2, NT>(op, q6, q6b, R, smem_u32(zrow), glo, lane, cw, ub);
             else if constexpr (NT == 4)
                 q6k_unit<4, NT>(op, q6, q6b, R, smem_u32(zrow), glo, lane, cw, ub);
+        } else if (op.type == kTypeIQ4_XS) {
+            // ================= IQ4_XS, integer tensor cores =================
+            const uint32_t glo =
+                static_cast<uint32_t>(reinterpret_cast<uintptr_t>(op.w + static_cast<int64_t>(r0) * op.w_nb1));
+            if (NT == 1 || N == 1)
+                iq4xs_unit<1, NT>(op, q4, q4b, R, smem_u32(zrow), glo, lane, cw, ub);
+            else if (NT == 2 || N == 2)
+                iq4xs_unit<2, NT>(op, q4, q4b, R, smem_u32(zrow), glo, lane, cw, ub);
+            else if constexpr (NT == 4)
+                iq4xs_unit<4, NT>(op, q4, q4b, R, smem_u32(zrow), glo, lane, cw, ub);
         } else {
             // ============= Q8_0 / Q4_0, integer tensor cores =============
             const uint32_t glo =
@@ -1693,7 +1814,7 @@ bool stream_supported(const MulMatOp* ops, int n_ops) {
     for (int i = 0; i < n_ops; ++i) {
         const MulMatOp& o = ops[i];
         if (o.type != kTypeQ4_K && o.type != kTypeQ5_K && o.type != kTypeQ6_K && o.type != kTypeQ4_0 &&
-            o.type != kTypeQ8_0)
+            o.type != kTypeQ8_0 && o.type != kTypeIQ4_XS)
             return false;
         if (o.ne2 != 1 || o.ne3 != 1) return false;
         if (o.N < 1 || o.N > kMaxNT) return false;

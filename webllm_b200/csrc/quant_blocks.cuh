@@ -15,6 +15,12 @@
 //   Q8_0 (32 elements, 34 B): f16 d @0, int8 qs[32] @2. y = d*q.
 //   Q4_0 (32 elements, 18 B): f16 d @0, qs[16] @2; element l < 16 the low
 //        nibble of qs[l], 16+l the high one; y = d*(q - 8).
+//   IQ4_XS (256 elements, 136 B): f16 d @0, u16 scales_h @2, scales_l[4] @4,
+//        qs[128] @8. Sub-block j (32 elements) has the 6-bit scale
+//        ls = (scales_l[j/2] >> 4(j%2)) & 15 | ((scales_h >> 2j) & 3) << 4;
+//        element 32j+l (l < 16) is level[qs[16j+l] & 15], 32j+16+l is
+//        level[qs[16j+l] >> 4], with the 16 non-linear levels of kIq4Levels;
+//        y = d*(ls - 32)*level.
 #pragma once
 
 #include <cuda_fp16.h>
@@ -107,6 +113,34 @@ __device__ __forceinline__ float q4_0_dequant_elem(const uint8_t* blk, int e) {
     const uint32_t byte = blk[2 + (e & 15)];
     const int q = static_cast<int>(e < 16 ? (byte & 0xFu) : (byte >> 4)) - 8;
     return __fmul_rn(d, static_cast<float>(q));
+}
+
+// The 16 non-linear 4-bit levels of IQ4_NL / IQ4_XS (ggml's kvalues_iq4nl, a
+// fixed part of the format: -127 -104 -83 -65 -49 -35 -22 -10 1 13 25 38 53
+// 69 89 113), as int8 bytes packed four to a word.
+constexpr uint32_t kIq4Lv0 = 0xBFAD9881u, kIq4Lv1 = 0xF6EADDCFu, kIq4Lv2 = 0x26190D01u, kIq4Lv3 = 0x71594535u;
+
+__device__ __forceinline__ int iq4_level(uint32_t i) {
+    const uint32_t w = __byte_perm((i & 8u) ? kIq4Lv2 : kIq4Lv0, (i & 8u) ? kIq4Lv3 : kIq4Lv1, i & 7u);
+    return static_cast<int8_t>(w & 0xFFu);
+}
+
+// The 6-bit scale (ls - 32, -32..31) of sub-block j (0..7) of an IQ4_XS block.
+__device__ __forceinline__ int iq4xs_scale(uint32_t scales_h, uint32_t scales_l4, int j) {
+    const uint32_t lo = (scales_l4 >> (4 * j)) & 0xFu;  // scales_l[j/2] >> 4(j%2), the four bytes as one word
+    const uint32_t hi = (scales_h >> (2 * j)) & 3u;
+    return static_cast<int>(lo | (hi << 4)) - 32;
+}
+
+// Exact dequantization of element e (0..255) of an IQ4_XS block: d*(ls - 32)
+// has at most 16 significant bits and the level 7, so both products are exact.
+__device__ __forceinline__ float iq4xs_dequant_elem(const uint8_t* blk, int e) {
+    const float d = f16_bits_to_f32(ldg_u16(blk));
+    const uint32_t sh = ldg_u16(blk + 2), sl = ldg_u16(blk + 4) | (ldg_u16(blk + 6) << 16);
+    const int j = e >> 5, l = e & 31;
+    const uint32_t byte = blk[8 + 16 * j + (l & 15)];
+    const int q = iq4_level(l < 16 ? (byte & 0xFu) : (byte >> 4));
+    return __fmul_rn(__fmul_rn(d, static_cast<float>(iq4xs_scale(sh, sl, j))), static_cast<float>(q));
 }
 
 // Exact dequantization of element e (0..31) of a Q8_0 block.

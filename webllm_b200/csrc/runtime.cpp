@@ -103,7 +103,7 @@ uint64_t size_class(uint64_t size) {
 // The src0 types this library runs (others: NOT_IMPLEMENTED, the caller falls back).
 bool quant_type_supported(int32_t t) {
     return t == WLLM_TYPE_Q4_K || t == WLLM_TYPE_Q5_K || t == WLLM_TYPE_Q6_K || t == WLLM_TYPE_Q4_0 ||
-           t == WLLM_TYPE_Q8_0;
+           t == WLLM_TYPE_Q8_0 || t == WLLM_TYPE_IQ4_XS;
 }
 
 bool ensure_init(State& s) {
@@ -707,11 +707,12 @@ int32_t wllm_sync(void) {
     if (e != cudaSuccess) return cuda_fail(s, e, "wllm_sync");
     e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(s, e, "wllm_sync (pending error)");
-    const unsigned kerr = wllm::read_and_clear_stream_error() | (wllm::read_and_clear_prefill_error() << 8);
+    const unsigned kerr = wllm::read_and_clear_stream_error() | (wllm::read_and_clear_prefill_error() << 8) |
+                          (wllm::read_and_clear_btc_error() << 16);
     if (kerr)
         return fail(s,
                     "wllm_sync: a kernel gave up waiting (code 0x%x: bits 0-1 a pipeline barrier, 2 a row-sharded "
-                    "peer's signal, 3 an in-flight copy; bits 8+ the prefill GEMM)",
+                    "peer's signal, 3 an in-flight copy; bits 8-15 the prefill GEMM, 16+ the small-batch tcgen05 GEMM)",
                     kerr);
     return WLLM_STATUS_OK;
 }

@@ -14,6 +14,7 @@ constexpr int kTypeQ8_0 = 8;
 constexpr int kTypeQ4_K = 12;
 constexpr int kTypeQ5_K = 13;
 constexpr int kTypeQ6_K = 14;
+constexpr int kTypeIQ4_XS = 23;
 
 inline int block_elems(int type) {
     switch (type) {
@@ -22,6 +23,7 @@ inline int block_elems(int type) {
         case kTypeQ4_K: return 256;
         case kTypeQ5_K: return 256;
         case kTypeQ6_K: return 256;
+        case kTypeIQ4_XS: return 256;
         case kTypeF32: return 1;
         default: return 0;
     }
@@ -33,6 +35,7 @@ inline int block_bytes(int type) {
         case kTypeQ4_K: return 144;
         case kTypeQ5_K: return 176;
         case kTypeQ6_K: return 210;
+        case kTypeIQ4_XS: return 136;
         case kTypeF32: return 4;
         default: return 0;
     }
@@ -128,6 +131,16 @@ unsigned read_and_clear_prefill_error();
 bool batched_supported(const MulMatOp& op);
 size_t batched_workspace_bytes(const MulMatOp& op);
 int launch_batched(const MulMatOp& op, void* workspace, size_t workspace_bytes, cudaStream_t stream);
+
+// Small-batch GEMM on tcgen05 (mulmat_batched_tc.cu): Q4_K and Q5_K weights,
+// 1 <= N <= 64 vectors, exact to about 2^-22 of each activation (f16 hi/lo
+// activations against the integer-scaled quants); workspace holds the
+// activation and sums images and the split-K partial tiles. Returns the
+// number of kernels launched (2) or a negative cudaError_t.
+bool batched_tc_supported(const MulMatOp& op);
+size_t batched_tc_workspace_bytes(const MulMatOp& op);
+int launch_batched_tc(const MulMatOp& op, void* workspace, size_t workspace_bytes, cudaStream_t stream, int num_sms);
+unsigned read_and_clear_btc_error();
 
 // Size of the prefill path's fixed device workspace (wllm_mul_mat_prefill_static):
 // ops with N * K * 2 + 256 bytes of f16 activations up to this size.

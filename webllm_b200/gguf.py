@@ -40,11 +40,13 @@ _SCALARS = {UINT8: "<B", INT8: "<b", UINT16: "<H", INT16: "<h", UINT32: "<I", IN
             UINT64: "<Q", INT64: "<q", FLOAT64: "<d"}
 
 # bytes per element of each ggml type (the reference's ggmlTypeSize,
-# src/models/gguf-parser.ts:274-294; unknown types count 4 bytes there too)
+# src/models/gguf-parser.ts:274-294; unknown types count 4 bytes there too).
+# IQ4_XS (23, 136 bytes per 256 elements) is added: the reference's table has
+# no I-quant and would count it at 4 bytes per element, too much to stream.
 TYPE_SIZE = {0: Fraction(4), 1: Fraction(2), 2: Fraction(18, 32), 3: Fraction(20, 32), 6: Fraction(22, 32),
              7: Fraction(24, 32), 8: Fraction(34, 32), 9: Fraction(36, 32), 10: Fraction(84, 256),
              11: Fraction(110, 256), 12: Fraction(144, 256), 13: Fraction(176, 256), 14: Fraction(210, 256),
-             15: Fraction(292, 256), 26: Fraction(4), 30: Fraction(2)}
+             15: Fraction(292, 256), 23: Fraction(136, 256), 26: Fraction(4), 30: Fraction(2)}
 
 
 @dataclass

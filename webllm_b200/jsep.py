@@ -37,6 +37,7 @@ GGML_TYPE_Q8_0 = 8
 GGML_TYPE_Q4_K = 12
 GGML_TYPE_Q5_K = 13
 GGML_TYPE_Q6_K = 14
+GGML_TYPE_IQ4_XS = 23
 
 TENSOR_BLOCK_I32 = 19
 
@@ -48,6 +49,7 @@ BLOCK_GEOMETRY = {
     GGML_TYPE_Q8_0: (32, 34),
     GGML_TYPE_Q4_K: (256, 144),
     GGML_TYPE_Q5_K: (256, 176),
+    GGML_TYPE_IQ4_XS: (256, 136),
     GGML_TYPE_Q6_K: (256, 210),
 }
 

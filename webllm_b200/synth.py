@@ -11,6 +11,9 @@ Distributions (per block):
   Q5_K: as Q4_K, with the 32 high-bit bytes uniform (5-bit quants uniform in
         0..31).
   Q4_0: 4-bit quants uniform in 0..15, d = f16(|N(0,1)| * 1e-2).
+  IQ4_XS: 6-bit sub-block scales and 4-bit level indices uniform (uniform
+        scale and quant bytes), d = f16(|N(0,1)| * 5e-4), which puts the
+        weights (d (ls - 32) level, |level| <= 127) in the other types' range.
 Activations are f32 N(0,1). No public dataset is involved.
 
 Model shapes are the per-layer MUL_MATs (name, src0 type, M rows, K).
@@ -19,10 +22,12 @@ from __future__ import annotations
 
 import numpy as np
 
-from .jsep import BLOCK_GEOMETRY, GGML_TYPE_Q4_0, GGML_TYPE_Q4_K, GGML_TYPE_Q5_K, GGML_TYPE_Q6_K, GGML_TYPE_Q8_0
+from .jsep import (BLOCK_GEOMETRY, GGML_TYPE_IQ4_XS, GGML_TYPE_Q4_0, GGML_TYPE_Q4_K, GGML_TYPE_Q5_K, GGML_TYPE_Q6_K,
+                   GGML_TYPE_Q8_0)
 
 Q4_K, Q6_K, Q8_0 = GGML_TYPE_Q4_K, GGML_TYPE_Q6_K, GGML_TYPE_Q8_0
 Q5_K, Q4_0 = GGML_TYPE_Q5_K, GGML_TYPE_Q4_0
+IQ4_XS = GGML_TYPE_IQ4_XS
 
 # Llama-3.2-3B decode: hidden 3072, FFN 8192, 24 q heads / 8 kv heads x 128.
 LLAMA32_3B_LAYER = [
@@ -123,6 +128,14 @@ def q4_0_blocks(rng: np.random.Generator, M: int, K: int) -> np.ndarray:
     return blk.reshape(M, -1)
 
 
+def iq4_xs_blocks(rng: np.random.Generator, M: int, K: int) -> np.ndarray:
+    nb = M * (K // 256)
+    blk = np.empty((nb, 136), dtype=np.uint8)
+    blk[:, 0:2] = _f16_scale(rng, nb, 5e-4).view(np.uint8).reshape(nb, 2)
+    blk[:, 2:] = rng.integers(0, 256, size=(nb, 134), dtype=np.uint8)
+    return blk.reshape(M, -1)
+
+
 def weights(rng: np.random.Generator, qtype: int, M: int, K: int) -> np.ndarray:
     if qtype == Q4_K:
         return q4_k_blocks(rng, M, K)
@@ -134,6 +147,8 @@ def weights(rng: np.random.Generator, qtype: int, M: int, K: int) -> np.ndarray:
         return q6_k_blocks(rng, M, K)
     if qtype == Q8_0:
         return q8_0_blocks(rng, M, K)
+    if qtype == IQ4_XS:
+        return iq4_xs_blocks(rng, M, K)
     raise ValueError(f"unsupported type {qtype}")
 
 
@@ -177,6 +192,8 @@ def weights_torch(gen, qtype: int, M: int, K: int, device):
         blk[:, 0:2] = f16(1e-2)
     elif qtype == Q6_K:
         blk[:, 208:210] = f16(2e-3)
+    elif qtype == IQ4_XS:
+        blk[:, 0:2] = f16(5e-4)
     elif qtype == Q8_0:
         blk[:, 0:2] = f16(1e-2)
         q = torch.randint(-127, 128, (nb, 32), dtype=torch.int16, device=device, generator=gen)
