@@ -11,28 +11,37 @@
 // and X[s, n] the sum of x over sub-block s. Both inner sums are f16 MMAs
 // with f32 accumulators in tensor memory, read back once per block and scaled
 // there by the block's d and dmin in f32:
-//  - activations: per vector a power-of-two scale 2^e (its maximum lands in
-//    [2^14, 2^15)) and two f16 parts, hi = f16(x 2^-e), lo = f16(x 2^-e - hi),
-//    about 22 bits of each element whatever its neighbours (an outlier channel
-//    costs nothing); hi and lo are stacked along K, so the main MMA sums
-//    A (hi + lo) into one accumulator column per vector;
+//  - activations: per vector and 256-element block a power-of-two scale 2^e
+//    (the block's maximum lands in [2^14, 2^15)) and two f16 parts,
+//    hi = f16(x 2^-e), lo = f16(x 2^-e - hi), about 22 bits of each element
+//    whatever its neighbours (an outlier channel costs nothing); hi and lo are
+//    stacked along N, so one MMA of N = 2 nv per K step covers both (the
+//    epilogue adds the two columns);
 //  - the mins: A_min = (m_0 .. m_7, m_0 .. m_7) (K = 16) against the sub-block
 //    sums split the same way (scale 2^(e + 5)), one MMA per block.
-// A pre-pass (btc_prep_kernel) writes the activation image [hi | lo][np][K],
-// the sums image [block][np][64] and the per-vector scales into workspace.
+// A pre-pass (btc_prep_kernel, one warp per vector and block) writes the
+// activation image, the sums image and the scales into workspace.
 //
-// CTA: 128 rows x np vectors (np = N rounded up to 16, at most 64).
-//  - warp 0 (TMA): per block, one 2D box of the 128 rows' raw blocks and the
-//    block's sums box into a raw slot; per 64-element chunk, the hi and lo
-//    boxes of the activations (128-byte swizzle) into a B stage;
-//  - warp 1: TMEM allocation; one thread issues per chunk 8 MMAs (4 K-steps x
-//    hi, lo; A from TMEM) into the block's accumulator, per block the mins MMA,
-//    and commits them;
-//  - warps 2..17: dequantize A = sc q straight into TMEM (tcgen05.st), as the
-//    prefill GEMM does, write A_min, and run the previous block's epilogue
-//    (tcgen05.ld of its two accumulators, y += d s_n main - dmin s'_n mins).
-// Accumulators are double-buffered by block parity, so the MMAs of block b
-// overlap the epilogue of block b - 1. Split K as in the prefill GEMM.
+// One thread issues a tcgen05.mma in about 50 cycles and waits on an mbarrier
+// in about 150, whatever the MMA's N (16 to 128), so at these sizes the issue
+// loop, not the tensor pipe, is the limit; two issuing warps run at twice the
+// rate. The kernel is laid out for that:
+//
+// CTA: 128 rows x nv vectors (nv = 16 or 32; N > 32 runs two vector groups as
+// grid y). Per block everything moves as one unit:
+//  - warp 0 (TMA): the 128 rows' raw blocks and the block's scales into a raw
+//    slot (4 slots); the block's four hi+lo activation boxes (64 x 2 nv,
+//    128-byte swizzle) and its sums box into a B stage (2 or 4 stages);
+//  - warps 1 and 2: MMA issuer i (one thread) takes the blocks b = i mod 2,
+//    with its own accumulators (main 2 nv columns, mins nv), its own A stage
+//    (the block's 4 x 64 f16 per row, 128 TMEM columns) and A_min: per block
+//    three waits, the mins MMA and 16 main MMAs, three commits;
+//  - warps 3..10: dequantize A = sc q straight into TMEM (tcgen05.st), A_min
+//    too, one store wait and one arrival per block;
+//  - warps 11..18: the epilogue of each block (tcgen05.ld of its accumulators,
+//    y += d s_n main - dmin s'_n mins, with d, dmin and the block's scales s_n,
+//    s'_n from the raw slot, which they release).
+// Split K as in the prefill GEMM.
 //
 // Every mbarrier wait is bounded; on timeout the CTA records an error code
 // (read by wllm_sync), stops issuing work, drains what it issued and still
@@ -50,29 +59,39 @@ __device__ unsigned int g_btc_error = 0;
 
 namespace {
 
-constexpr int kTM = 128;                  // rows of W per CTA (TMEM lanes)
-constexpr int kMaxNP = 64;                // vectors per CTA
-constexpr int kChunk = 64;                // K per stage (one 128-byte swizzle atom of f16)
-constexpr int kSt = 4;                    // A (TMEM) and B (shared) stages
-constexpr int kRaw = 4;                   // raw blocks in flight
-constexpr int kDq = 16;                   // dequant / epilogue warps
-constexpr int kThr = 32 * (2 + kDq);
-constexpr int kACol0 = 256, kACols = 32;  // A stage s: TMEM columns 256 + 32 s (two f16 per column)
-constexpr int kMinCol0 = 384;             // A_min of block parity p: columns 384 + 8 p
-constexpr int kTmemCols = 512;            // accumulators: block parity p at columns 2 np p (main) and + np (mins)
+constexpr int kTM = 128;      // rows of W per CTA (TMEM lanes)
+constexpr int kMaxNP = 64;    // vectors per launch
+constexpr int kMaxNV = 32;    // vectors per CTA
+constexpr int kChunk = 64;    // K per activation box (one 128-byte swizzle atom of f16)
+constexpr int kMaxStB = 4;    // B stages (blocks of activations), at most
+constexpr int kRaw = 4;       // raw blocks in flight
+constexpr int kDq = 8;        // dequant warps
+constexpr int kEp = 8;        // epilogue warps
+constexpr int kFirstDq = 3;   // warps: 0 TMA, 1-2 MMA issuers, then dequant, then epilogue
+constexpr int kFirstEp = kFirstDq + kDq;
+constexpr int kThr = 32 * (kFirstEp + kEp);
+constexpr int kACols = 128;   // TMEM columns of one A stage (256 f16 per row, two per column)
+// TMEM, issuer i (block parity): the main accumulator at columns W i (2 nv:
+// hi then lo), the mins accumulator after it (nv); W (accw) leaves room for the
+// epilogue's 16-column loads past the last vector; A_min of issuer i at 2 W +
+// 8 i; A stage i at acol0 + 128 i
+constexpr int kTmemCols = 512;
 constexpr uint32_t kSpin = 1u << 26;
 constexpr int kMaxSplits = 16;
 
 struct BtcArgs {
     CUtensorMap wmap;     // weights [M][row bytes / 8] uint64, box (block bytes / 8) x 128
-    CUtensorMap xmap;     // activations [2 np][K] f16 (rows 0..np-1 hi, np.. lo), box 64 x np, 128-byte swizzle
-    CUtensorMap smap;     // sub-block sums [blocks x np][64] f16 (k 0..7 hi, 8..15 lo, rest 0), box 64 x np
-    const float* vscale;  // [2][np]: 2^e_n (activations), 2^(e_n + 5) (sums)
+    CUtensorMap xmap;     // activations [groups][hi, lo][nv][K] f16, box 64 x 2 nv, 128-byte swizzle
+    CUtensorMap smap;     // sub-block sums [blocks x np][64] f16 (k 0..7 hi, 8..15 lo, rest 0), box 64 x nv
+    const float* vscale;  // [block][group][2][nv]: 2^e (activations), 2^(e + 5) (sums)
     float* y;
     int64_t y_nb1;        // bytes between output vectors
-    int32_t M, K, N, np;
+    int32_t M, K, N;
+    int32_t nv, groups;   // vectors per CTA, vector groups (grid y)
+    int32_t nstb;         // B stages (2 or 4)
+    int32_t accw, acol0;  // TMEM columns of one issuer's accumulators; first A column
     int32_t splits, kb_split;
-    float* partial;       // [tile][split][np][128] (split K)
+    float* partial;       // [tile][split][kMaxNV][128] (split K)
     unsigned* counters;   // [tile] (split K, zero at launch)
 };
 
@@ -128,6 +147,13 @@ __device__ __forceinline__ void tma_2d(void* dst, const CUtensorMap* tm, int x, 
         "l"(tm), "r"(x), "r"(y), "r"(smem_u32(bar))
         : "memory");
 }
+// Untiled bulk copy global -> shared (16-byte aligned addresses, size a multiple of 16).
+__device__ __forceinline__ void bulk_copy(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     smem_u32(dst)),
+                 "l"(src), "r"(bytes), "r"(smem_u32(bar))
+                 : "memory");
+}
 // UMMA shared-memory descriptor: K-major, 128-byte swizzle, 8-row groups 1024
 // bytes apart (SBO), version 1.
 __device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr) {
@@ -151,42 +177,63 @@ __device__ __forceinline__ void umma_commit(uint64_t* bar) {
 }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-// 8 consecutive 32-bit TMEM columns of this warp's 32 lanes.
+// 8 consecutive 32-bit TMEM columns of this warp's 32 lanes. No memory
+// clobber: it reads registers only, so the compiler may schedule shared-memory
+// loads around it (volatile asm statements keep their order among themselves,
+// and tcgen05.wait::st, which does clobber memory, orders it before the
+// barrier arrivals).
 __device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&v)[8]) {
     asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr), "r"(v[0]),
-                 "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
-                 : "memory");
+                 "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]));
 }
-// 16 consecutive f32 columns of this warp's 32 TMEM lanes.
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
-    uint32_t r[16];
+// 16 consecutive f32 columns of this warp's 32 TMEM lanes at three column
+// addresses, with one wait for all of them inside the same statement (so no
+// use of the registers can be scheduled before the wait).
+#define WLLM_R16(o) "=r"(r[o]), "=r"(r[o + 1]), "=r"(r[o + 2]), "=r"(r[o + 3]), "=r"(r[o + 4]), "=r"(r[o + 5]), \
+    "=r"(r[o + 6]), "=r"(r[o + 7]), "=r"(r[o + 8]), "=r"(r[o + 9]), "=r"(r[o + 10]), "=r"(r[o + 11]), "=r"(r[o + 12]), \
+    "=r"(r[o + 13]), "=r"(r[o + 14]), "=r"(r[o + 15])
+__device__ __forceinline__ void tmem_ld16x3(uint32_t t0, uint32_t t1, uint32_t t2, float (&v0)[16], float (&v1)[16],
+                                            float (&v2)[16]) {
+    uint32_t r[48];
     asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-        : "r"(taddr));
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%48];\n\t"
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%49];\n\t"
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47}, [%50];\n\t"
+        "tcgen05.wait::ld.sync.aligned;"
+        : WLLM_R16(0), WLLM_R16(16), WLLM_R16(32)
+        : "r"(t0), "r"(t1), "r"(t2)
+        : "memory");
 #pragma unroll
-    for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+    for (int i = 0; i < 16; ++i) {
+        v0[i] = __uint_as_float(r[i]);
+        v1[i] = __uint_as_float(r[16 + i]);
+        v2[i] = __uint_as_float(r[32 + i]);
+    }
 }
+#undef WLLM_R16
 
-// Shared-memory layout (from a 1024-byte aligned base): B stages, sums slots,
-// raw slots, barriers.
+// Shared-memory layout (from a 1024-byte aligned base): B stages (four hi+lo
+// activation boxes, then the sums box), raw slots, scale slots, barriers.
 struct Smem {
-    uint32_t b_bytes, s_bytes, raw_bytes;
-    __host__ __device__ Smem(int np, int bb) {
-        b_bytes = static_cast<uint32_t>(2 * np * 128);  // hi + lo boxes of one chunk
-        s_bytes = static_cast<uint32_t>(np * 128);
+    uint32_t box_bytes, s_bytes, b_bytes, raw_bytes, v_bytes, nstb;
+    __host__ __device__ Smem(int nv, int bb, int nstb_) {
+        box_bytes = static_cast<uint32_t>(2 * nv * 128);  // hi + lo rows of one 64-element chunk
+        s_bytes = static_cast<uint32_t>(nv * 128);
+        b_bytes = 4 * box_bytes + s_bytes;
         raw_bytes = static_cast<uint32_t>(kTM * bb);
+        v_bytes = static_cast<uint32_t>(2 * nv * 4);  // the block's 2 nv scales
+        nstb = static_cast<uint32_t>(nstb_);
     }
     __host__ __device__ uint32_t b_off(int s) const { return s * b_bytes; }
-    __host__ __device__ uint32_t s_off(int r) const { return kSt * b_bytes + r * s_bytes; }
-    __host__ __device__ uint32_t raw_off(int r) const { return kSt * b_bytes + kRaw * s_bytes + r * raw_bytes; }
-    __host__ __device__ uint32_t bar_off() const { return (kSt * b_bytes + kRaw * s_bytes + kRaw * raw_bytes + 7) & ~7u; }
-    // barriers: b_full[kSt], a_full[kSt], st_free[kSt], raw_full[kRaw], raw_free[kRaw], amin_full[2],
-    // acc_full[2], acc_free[2]; then the TMEM base address word, the poison flag and 2 np scales
-    __host__ __device__ uint32_t total(int np) const {
-        return bar_off() + 8 * (3 * kSt + 2 * kRaw + 6) + 16 + 8 * np + 1024;  // + alignment slack
+    __host__ __device__ uint32_t raw_off(int r) const { return nstb * b_bytes + r * raw_bytes; }
+    __host__ __device__ uint32_t v_off(int r) const { return nstb * b_bytes + kRaw * raw_bytes + r * v_bytes; }
+    __host__ __device__ uint32_t bar_off() const { return nstb * b_bytes + kRaw * (raw_bytes + v_bytes); }
+    // barriers: b_full, b_free [kMaxStB], raw_full, raw_free [kRaw], a_full,
+    // a_free, acc_full, acc_free [2]; then the TMEM base address word and the
+    // poison flag
+    static constexpr uint32_t kBars = 2 * kMaxStB + 2 * kRaw + 8;
+    __host__ __device__ uint32_t total() const {
+        return bar_off() + 8 * kBars + 16 + 1024;  // + alignment slack
     }
 };
 
@@ -195,46 +242,46 @@ __global__ void __launch_bounds__(kThr, 1) btc_kernel(const __grid_constant__ Bt
     extern __shared__ __align__(128) uint8_t smem_raw[];
     uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     constexpr int BB = blk_bytes<TYPE>();
-    const int np = P.np;
-    const Smem L(np, BB);
+    const int nv = P.nv, nstb = P.nstb;
+    const Smem L(nv, BB, nstb);
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L.bar_off());
     uint64_t* b_full = bars;
-    uint64_t* a_full = b_full + kSt;
-    uint64_t* st_free = a_full + kSt;
-    uint64_t* raw_full = st_free + kSt;
+    uint64_t* b_free = b_full + kMaxStB;
+    uint64_t* raw_full = b_free + kMaxStB;
     uint64_t* raw_free = raw_full + kRaw;
-    uint64_t* amin_full = raw_free + kRaw;
-    uint64_t* acc_full = amin_full + 2;
+    uint64_t* a_full = raw_free + kRaw;
+    uint64_t* a_free = a_full + 2;
+    uint64_t* acc_full = a_free + 2;
     uint64_t* acc_free = acc_full + 2;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_free + 2);
     volatile int* poisoned = reinterpret_cast<volatile int*>(tmem_slot + 1);
-    float* vs = reinterpret_cast<float*>(tmem_slot + 4);  // [2][np]
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int m0 = blockIdx.x * kTM;
+    const int grp = blockIdx.y;                // vector group: vectors nv grp ..
     const int kb0 = blockIdx.z * P.kb_split;  // first K block of this split
     const int nblk = min(P.K / 256 - kb0, P.kb_split);
-    const uint32_t idesc = (1u << 4) | (static_cast<uint32_t>(np >> 3) << 17) | (static_cast<uint32_t>(kTM >> 4) << 24);
+    const int accw = P.accw;
+    const uint32_t mincol0 = static_cast<uint32_t>(2 * accw);
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < kSt; ++s) {
-            mbar_init(&b_full[s], 1);
-            mbar_init(&a_full[s], kDq);
-            mbar_init(&st_free[s], 1);
+        for (int i = 0; i < kMaxStB; ++i) {
+            mbar_init(&b_full[i], 1);
+            mbar_init(&b_free[i], 1);
         }
         for (int r = 0; r < kRaw; ++r) {
             mbar_init(&raw_full[r], 1);
-            mbar_init(&raw_free[r], kDq + 1);  // the dequant warps and the mins MMA's commit
+            mbar_init(&raw_free[r], kDq + kEp);
         }
         for (int p = 0; p < 2; ++p) {
-            mbar_init(&amin_full[p], 4);  // one warp per TMEM lane quarter
+            mbar_init(&a_full[p], kDq);
+            mbar_init(&a_free[p], 1);
             mbar_init(&acc_full[p], 1);
-            mbar_init(&acc_free[p], kDq);
+            mbar_init(&acc_free[p], kEp);
         }
         *poisoned = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
-    for (int i = threadIdx.x; i < 2 * np; i += kThr) vs[i] = P.vscale[i];
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
                      "r"(kTmemCols));
@@ -245,244 +292,239 @@ __global__ void __launch_bounds__(kThr, 1) btc_kernel(const __grid_constant__ Bt
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
+    const int lgb = nstb == 4 ? 2 : 1;  // log2 of the B stages (2 or 4)
     if (warp == 0) {
         // ---------------- TMA producer ----------------
         if (lane == 0) {
             asm volatile("prefetch.tensormap [%0];" ::"l"(&P.wmap) : "memory");
             asm volatile("prefetch.tensormap [%0];" ::"l"(&P.xmap) : "memory");
             asm volatile("prefetch.tensormap [%0];" ::"l"(&P.smap) : "memory");
-            int raw_issued = 0, b_issued = 0;
-            bool stop = false;
-            for (int b = 0; b < nblk && !stop; ++b) {
-                const int r = b % kRaw;
-                if (b >= kRaw && !mbar_wait(&raw_free[r], ((b / kRaw) - 1) & 1, 1u, poisoned)) break;
-                mbar_expect_tx(&raw_full[r], L.raw_bytes + L.s_bytes);
-                tma_2d(smem + L.raw_off(r), &P.wmap, (kb0 + b) * (BB / 8), m0, &raw_full[r]);
-                tma_2d(smem + L.s_off(r), &P.smap, 0, (kb0 + b) * np, &raw_full[r]);
-                raw_issued = b + 1;
-                for (int c = 0; c < 4; ++c) {
-                    const int q = 4 * b + c, s = q % kSt;
-                    if (q >= kSt && !mbar_wait(&st_free[s], ((q / kSt) - 1) & 1, 1u, poisoned)) {
-                        stop = true;
-                        break;
-                    }
-                    mbar_expect_tx(&b_full[s], L.b_bytes);
-                    const int kx = (kb0 + b) * 256 + kChunk * c;
-                    tma_2d(smem + L.b_off(s), &P.xmap, kx, 0, &b_full[s]);
-                    tma_2d(smem + L.b_off(s) + L.b_bytes / 2, &P.xmap, kx, np, &b_full[s]);
-                    b_issued = q + 1;
+            int issued = 0;  // blocks whose copies are all in flight
+            for (int b = 0; b < nblk; ++b) {
+                const int r = b & (kRaw - 1), s = b & (nstb - 1), kb = kb0 + b;
+                if (b >= kRaw && !mbar_wait(&raw_free[r], ((b >> 2) - 1) & 1, 1u, poisoned)) break;
+                mbar_expect_tx(&raw_full[r], L.raw_bytes + L.v_bytes);
+                tma_2d(smem + L.raw_off(r), &P.wmap, kb * (BB / 8), m0, &raw_full[r]);
+                bulk_copy(smem + L.v_off(r), P.vscale + (static_cast<int64_t>(kb) * P.groups + grp) * 2 * nv, L.v_bytes,
+                          &raw_full[r]);
+                if (b >= nstb && !mbar_wait(&b_free[s], ((b >> lgb) - 1) & 1, 1u, poisoned)) {
+                    issued = -(b + 1);  // the raw slot of block b is in flight, its B stage is not
+                    break;
                 }
+                uint8_t* dst = smem + L.b_off(s);
+                mbar_expect_tx(&b_full[s], L.b_bytes);
+#pragma unroll
+                for (int c = 0; c < 4; ++c)
+                    tma_2d(dst + c * L.box_bytes, &P.xmap, kb * 256 + kChunk * c, grp * 2 * nv, &b_full[s]);
+                tma_2d(dst + 4 * L.box_bytes, &P.smap, 0, kb * P.groups * nv + grp * nv, &b_full[s]);
+                issued = b + 1;
             }
             // before the CTA exits, the last copy into every slot and stage has
             // landed (bounded, whatever the poison flag says)
+            const int raw_issued = issued < 0 ? -issued : issued;
+            const int b_issued = issued < 0 ? -issued - 1 : issued;
             for (int b = max(0, raw_issued - kRaw); b < raw_issued; ++b)
-                if (!mbar_wait_drain(&raw_full[b % kRaw], (b / kRaw) & 1)) atomicOr(&g_btc_error, 16u);
-            for (int q = max(0, b_issued - kSt); q < b_issued; ++q)
-                if (!mbar_wait_drain(&b_full[q % kSt], (q / kSt) & 1)) atomicOr(&g_btc_error, 16u);
+                if (!mbar_wait_drain(&raw_full[b & (kRaw - 1)], (b >> 2) & 1)) atomicOr(&g_btc_error, 16u);
+            for (int b = max(0, b_issued - nstb); b < b_issued; ++b)
+                if (!mbar_wait_drain(&b_full[b & (nstb - 1)], (b >> lgb) & 1)) atomicOr(&g_btc_error, 16u);
         }
-    } else if (warp == 1) {
-        // ---------------- MMA issuer ----------------
-        int committed = 0;  // chunks committed (for the drain after a time-out)
-        bool stop = false;
-        for (int b = 0; b < nblk && !stop; ++b) {
-            const int buf = b & 1;
-            const uint32_t dmain = tmem + static_cast<uint32_t>(2 * np * buf), dmin = dmain + static_cast<uint32_t>(np);
-            int ok = 1;
-            if (lane == 0 && b >= 2) ok = mbar_wait(&acc_free[buf], ((b / 2) - 1) & 1, 2u, poisoned);
-            if (!__shfl_sync(0xffffffffu, ok, 0)) break;
-            for (int c = 0; c < 4; ++c) {
-                const int q = 4 * b + c, s = q % kSt;
-                const uint32_t par = (q / kSt) & 1;
-                ok = 1;
-                if (lane == 0) ok = mbar_wait(&b_full[s], par, 2u, poisoned) && mbar_wait(&a_full[s], par, 2u, poisoned);
-                if (!__shfl_sync(0xffffffffu, ok, 0)) {
-                    stop = true;
+    } else if (warp < kFirstDq) {
+        // ---------------- MMA issuer i: blocks b = i, i + 2, ... ----------------
+        const int i = warp - 1;
+        if (lane == 0) {
+            uint64_t* last_bar = nullptr;  // the last commit (it tracks every MMA before it)
+            uint32_t last_par = 0;
+            const uint64_t bdesc0 = umma_desc_sw128(smem_u32(smem));  // + (byte offset >> 4)
+            const uint32_t dmain = tmem + static_cast<uint32_t>(accw * i), dmin = dmain + static_cast<uint32_t>(2 * nv);
+            const uint32_t amin = tmem + mincol0 + static_cast<uint32_t>(8 * i);
+            const uint32_t a0 = tmem + static_cast<uint32_t>(P.acol0 + kACols * i);
+            // f32 accumulators, f16 A and B (K-major), M = 128; N = 2 nv (hi, lo) or nv (mins)
+            const uint32_t idesc_main =
+                (1u << 4) | (static_cast<uint32_t>((2 * nv) >> 3) << 17) | (static_cast<uint32_t>(kTM >> 4) << 24);
+            const uint32_t idesc_min = (1u << 4) | (static_cast<uint32_t>(nv >> 3) << 17) | (static_cast<uint32_t>(kTM >> 4) << 24);
+            for (int b = i, u = 0; b < nblk; b += 2, ++u) {  // u: this issuer's block count (its phases)
+                const int s = b & (nstb - 1);
+                if (u >= 1 && !mbar_wait(&acc_free[i], (u - 1) & 1, 2u, poisoned)) break;
+                if (!mbar_wait(&b_full[s], (b >> lgb) & 1, 2u, poisoned) || !mbar_wait(&a_full[i], u & 1, 2u, poisoned))
                     break;
-                }
                 tc_fence_after();
-                if (lane == 0) {
-                    const uint32_t a0 = tmem + static_cast<uint32_t>(kACol0 + s * kACols);
-                    const uint32_t bhi = smem_u32(smem + L.b_off(s)), blo = bhi + L.b_bytes / 2;
+                const uint64_t bd = bdesc0 + (L.b_off(s) >> 4);
+                // the mins: A_min (K = 16) against the block's sums box
+                umma_f16_ts(dmin, amin, bd + ((4 * L.box_bytes) >> 4), idesc_min, 0u);
 #pragma unroll
-                    for (int ks = 0; ks < kChunk / 16; ++ks) {  // K = 16 per MMA: 8 A columns, 32 bytes of B rows
-                        umma_f16_ts(dmain, a0 + 8 * ks, umma_desc_sw128(bhi + 32 * ks), idesc, (c | ks) ? 1u : 0u);
-                        umma_f16_ts(dmain, a0 + 8 * ks, umma_desc_sw128(blo + 32 * ks), idesc, 1u);
-                    }
-                    umma_commit(&st_free[s]);  // A and B stage s are free once these have read them
+                for (int c = 0; c < 4; ++c) {
+                    const uint64_t bc = bd + ((c * L.box_bytes) >> 4);
+#pragma unroll
+                    for (int ks = 0; ks < kChunk / 16; ++ks)  // K = 16 per MMA: 8 A columns, 32 bytes of B rows
+                        umma_f16_ts(dmain, a0 + 32 * c + 8 * ks, bc + 2 * ks, idesc_main, (c | ks) ? 1u : 0u);
                 }
-                committed = q + 1;
-                __syncwarp();
+                umma_commit(&a_free[i]);  // A stage, A_min and B stage are free once these have read them
+                umma_commit(&b_free[s]);
+                umma_commit(&acc_full[i]);
+                last_bar = &acc_full[i];
+                last_par = static_cast<uint32_t>(u & 1);
             }
-            if (stop) break;
-            // the mins: A_min (K = 16) against the block's sums box
-            const int r = b % kRaw;
-            ok = 1;
-            if (lane == 0)
-                ok = mbar_wait(&raw_full[r], (b / kRaw) & 1, 2u, poisoned) &&
-                     mbar_wait(&amin_full[buf], (b / 2) & 1, 2u, poisoned);
-            if (!__shfl_sync(0xffffffffu, ok, 0)) break;
-            tc_fence_after();
-            if (lane == 0) {
-                umma_f16_ts(dmin, tmem + static_cast<uint32_t>(kMinCol0 + 8 * buf), umma_desc_sw128(smem_u32(smem + L.s_off(r))),
-                            idesc, 0u);
-                umma_commit(&raw_free[r]);  // the sums box is read
-                umma_commit(&acc_full[buf]);
-            }
-            __syncwarp();
-        }
-        if (*poisoned) {
             // a time-out: the MMAs already issued still write TMEM, which is freed
-            // at the end; wait (bounded) for the last commit, which tracks them all
-            if (lane == 0 && committed > 0 &&
-                !mbar_wait_drain(&st_free[(committed - 1) % kSt], ((committed - 1) / kSt) & 1))
-                atomicOr(&g_btc_error, 16u);
-            __syncwarp();
+            // at the end; wait (bounded) for the last commit
+            if (*poisoned && last_bar && !mbar_wait_drain(last_bar, last_par)) atomicOr(&g_btc_error, 16u);
         }
-    } else {
-        // ---------------- dequant, A_min and epilogue ----------------
-        const int quarter = warp & 3;  // TMEM lanes this warp may access
-        const int dw = warp - 2;
-        const int part = dw >> 2;      // quarter of each chunk's K; quarter of the vectors in the epilogue
-        const int r = 32 * quarter + lane, h = part >> 1, qq = part & 1;  // row; sub-block 2p + h, its half qq
+        __syncwarp();
+    } else if (warp < kFirstEp) {
+        // ---------------- dequant: A and A_min of each block ----------------
+        const int quarter = warp & 3;                // TMEM lanes this warp may access
+        const int h = (warp - kFirstDq) >> 2;        // sub-block 2p + h of chunk p (both halves)
+        const int r = 32 * quarter + lane;
         const uint32_t trow = tmem + (static_cast<uint32_t>(32 * quarter) << 16);
         const uint32_t sel_a = 0x4440u + static_cast<uint32_t>(h);      // byte h, zero-extended
         const uint32_t sel_b = 0x4440u + 2u + static_cast<uint32_t>(h);  // byte 2 + h
-        const int nq = np / 4, n0 = part * nq;  // this warp's vectors in the epilogue
-        float yacc[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) yacc[i] = 0.f;
-        float dprev = 0.f, dminprev = 0.f;
-        bool stop = false;
-        // the epilogue of block pb: y += d s_n main - dmin s'_n mins
-        auto epilogue = [&](int pb, float d, float dm) {
-            const int pbuf = pb & 1;
-            const bool ok = mbar_wait(&acc_full[pbuf], (pb / 2) & 1, 4u, poisoned);
-            tc_fence_after();
-            if (ok) {
-                float mv[16], nv[16];
-                tmem_ld16(trow + static_cast<uint32_t>(2 * np * pbuf + n0), mv);
-                tmem_ld16(trow + static_cast<uint32_t>(2 * np * pbuf + np + n0), nv);
-#pragma unroll
-                for (int i = 0; i < 16; ++i) {
-                    if (i < nq)
-                        yacc[i] = fmaf(mv[i], d * vs[n0 + i], fmaf(-nv[i], dm * vs[np + n0 + i], yacc[i]));
-                }
-            }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&acc_free[pbuf]);
-            return ok;
-        };
-        int q = 0;
-        for (int b = 0; b < nblk && !stop; ++b) {
-            const int rs = b % kRaw, buf = b & 1;
-            if (!mbar_wait(&raw_full[rs], (b / kRaw) & 1, 3u, poisoned)) break;
+        const __half2 k1024 = __float2half2_rn(1024.f), km1024 = __float2half2_rn(-1024.f);
+        for (int b = 0; b < nblk; ++b) {
+            const int rs = b & (kRaw - 1), i = b & 1;
+            if (!mbar_wait(&raw_full[rs], (b >> 2) & 1, 3u, poisoned)) break;
             const uint8_t* blk = smem + L.raw_off(rs) + r * BB;
             // scales of this thread's sub-blocks j = 2p + h (p = 0..3), get_scale_min_k4
             // (src/inference/jsep/ops/matmul.ts:408-424) on the bytes of the three scale words
             const uint4 hdr = *reinterpret_cast<const uint4*>(blk);
-            const float d = f16_bits_to_f32(hdr.x), dmin = f16_bits_to_f32(hdr.x >> 16);
             const uint32_t w1a = __byte_perm(hdr.y, 0u, sel_a), w1b = __byte_perm(hdr.y, 0u, sel_b);
             const uint32_t w3a = __byte_perm(hdr.w, 0u, sel_a), w3b = __byte_perm(hdr.w, 0u, sel_b);
             const uint32_t scv[4] = {w1a & 63u, w1b & 63u, (w3a & 15u) | ((w1a >> 6) << 4),
                                      (w3b & 15u) | ((w1b >> 6) << 4)};
+            // the block's quants (and Q5_K high bits), read before the stage wait
             const uint4* qs = reinterpret_cast<const uint4*>(blk + (TYPE == kTypeQ5_K ? 48 : 16));
-            uint4 qh = make_uint4(0u, 0u, 0u, 0u);
-            if constexpr (TYPE == kTypeQ5_K) qh = *reinterpret_cast<const uint4*>(blk + 16 + 16 * qq);
-            const uint32_t hv[4] = {qh.x, qh.y, qh.z, qh.w};
+            uint4 qv[8];
 #pragma unroll
-            for (int p = 0; p < 4; ++p, ++q) {
-                const int s = q % kSt;
-                if (q >= kSt && !mbar_wait(&st_free[s], ((q / kSt) - 1) & 1, 3u, poisoned)) {
-                    stop = true;
-                    break;
-                }
-                // A = sc q exactly: (1024 + q) sc - 1024 sc in one f16 FMA (the
-                // exact result, at most 1953, is an f16 integer)
-                const float scf = static_cast<float>(scv[p]);
-                const __half2 sc2 = __float2half2_rn(scf), mn2 = __float2half2_rn(-1024.f * scf);
-                // bytes 16 qq .. 16 qq + 15 of pair p; this thread's quants are their low
-                // (h = 0) or high (h = 1) nibbles: elements 64p + 32h + 16qq + l, l = 0..15
-                const uint4 v0 = qs[2 * p + qq];
-                const uint32_t wv[4] = {v0.x, v0.y, v0.z, v0.w};
-                uint32_t out[8];  // 16 f16, element order l = 0..15
+            for (int j = 0; j < 8; ++j) qv[j] = qs[j];
+            uint32_t hv[2][4] = {{0u, 0u, 0u, 0u}, {0u, 0u, 0u, 0u}};
+            if constexpr (TYPE == kTypeQ5_K) {
 #pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    uint32_t nib = (wv[i] >> (4 * h)) & 0x0F0F0F0Fu;
-                    if constexpr (TYPE == kTypeQ5_K) nib |= ((hv[i] >> (2 * p + h)) & 0x01010101u) << 4;
-                    // f16 1024 + q (exact) for bytes (0, 1) and (2, 3): 0x64 in each high byte
-                    const uint32_t e01 = __byte_perm(nib, 0x00006464u, 0x5140u);
-                    const uint32_t e23 = __byte_perm(nib, 0x00006464u, 0x5342u);
-                    const __half2 w01 = __hfma2(*reinterpret_cast<const __half2*>(&e01), sc2, mn2);
-                    const __half2 w23 = __hfma2(*reinterpret_cast<const __half2*>(&e23), sc2, mn2);
-                    out[2 * i] = *reinterpret_cast<const uint32_t*>(&w01);
-                    out[2 * i + 1] = *reinterpret_cast<const uint32_t*>(&w23);
+                for (int qq = 0; qq < 2; ++qq) {
+                    const uint4 t = *reinterpret_cast<const uint4*>(blk + 16 + 16 * qq);
+                    hv[qq][0] = t.x;
+                    hv[qq][1] = t.y;
+                    hv[qq][2] = t.z;
+                    hv[qq][3] = t.w;
                 }
-                // k = 32h + 16qq + l of this chunk: TMEM columns 16h + 8qq .. +7 of A stage s
-                tmem_st8(trow + static_cast<uint32_t>(kACol0 + s * kACols + 16 * h + 8 * qq), out);
-                asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&a_full[s]);
             }
-            if (stop) break;
-            if (part == 0) {
+            // A stage i (and A_min i) is free once issuer i's MMAs of block b - 2 have read it
+            if (b >= 2 && !mbar_wait(&a_free[i], ((b >> 1) - 1) & 1, 3u, poisoned)) break;
+            tc_fence_after();
+            const uint32_t acol = static_cast<uint32_t>(P.acol0 + kACols * i + 16 * h);
+#pragma unroll
+            for (int p = 0; p < 4; ++p) {
+                // A = sc q exactly: (1024 + q) sc - 1024 sc in one f16 FMA (the
+                // exact result, at most 1953, is an f16 integer); sc itself as the
+                // f16 (1024 + sc) - 1024, both halves
+                const uint32_t sbits = 0x64006400u | (scv[p] * 0x00010001u);
+                const __half2 sc2 = __hsub2(*reinterpret_cast<const __half2*>(&sbits), k1024);
+                const __half2 mn2 = __hmul2(sc2, km1024);
+#pragma unroll
+                for (int qq = 0; qq < 2; ++qq) {
+                    // bytes 16 qq .. 16 qq + 15 of pair p; this thread's quants are their
+                    // low (h = 0) or high (h = 1) nibbles: elements 64p + 32h + 16qq + l
+                    const uint4 v0 = qv[2 * p + qq];
+                    const uint32_t wv[4] = {v0.x, v0.y, v0.z, v0.w};
+                    uint32_t out[8];  // 16 f16, element order l = 0..15
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        uint32_t nib = (wv[j] >> (4 * h)) & 0x0F0F0F0Fu;
+                        if constexpr (TYPE == kTypeQ5_K) nib |= ((hv[qq][j] >> (2 * p + h)) & 0x01010101u) << 4;
+                        // f16 1024 + q (exact) for bytes (0, 1) and (2, 3): 0x64 in each high byte
+                        const uint32_t e01 = __byte_perm(nib, 0x00006464u, 0x5140u);
+                        const uint32_t e23 = __byte_perm(nib, 0x00006464u, 0x5342u);
+                        const __half2 w01 = __hfma2(*reinterpret_cast<const __half2*>(&e01), sc2, mn2);
+                        const __half2 w23 = __hfma2(*reinterpret_cast<const __half2*>(&e23), sc2, mn2);
+                        out[2 * j] = *reinterpret_cast<const uint32_t*>(&w01);
+                        out[2 * j + 1] = *reinterpret_cast<const uint32_t*>(&w23);
+                    }
+                    // k = 64p + 32h + 16qq + l of the block: TMEM columns 32p + 16h + 8qq .. +7 of A stage i
+                    tmem_st8(trow + acol + static_cast<uint32_t>(32 * p + 8 * qq), out);
+                }
+            }
+            if (h == 0) {
                 // A_min of this block: the eight 6-bit mins (get_scale_min_k4), twice,
-                // as f16 pairs (k 0..7 meet the sums' hi parts, 8..15 their lo parts).
-                // Block b - 2's mins MMA, which read these columns, is complete: this
-                // warp waited for its accumulator in the previous epilogue.
-                const uint32_t mv0 = hdr.z & 0x3F3F3F3Fu;  // m_0..m_3 (bytes 8..11, low 6 bits)
+                // as f16 pairs (k 0..7 meet the sums' hi parts, 8..15 their lo parts)
+                const uint32_t mlo = hdr.z & 0x3F3F3F3Fu;                                                  // m_0..m_3
+                const uint32_t mhi = ((hdr.w >> 4) & 0x0F0F0F0Fu) | (((hdr.z >> 6) & 0x03030303u) << 4);  // m_4..m_7
                 uint32_t mm[4];
-                const uint32_t mhi = (((hdr.w >> 4) & 0x0F0F0F0Fu)) | (((hdr.z >> 6) & 0x03030303u) << 4);  // m_4..m_7
-                const uint32_t mq[2] = {mv0, mhi};
+                const uint32_t mq[2] = {mlo, mhi};
 #pragma unroll
                 for (int t = 0; t < 2; ++t) {
                     const uint32_t e01 = __byte_perm(mq[t], 0x00006464u, 0x5140u);
                     const uint32_t e23 = __byte_perm(mq[t], 0x00006464u, 0x5342u);
-                    const __half2 k1024 = __float2half2_rn(1024.f);
                     const __half2 m01 = __hsub2(*reinterpret_cast<const __half2*>(&e01), k1024);
                     const __half2 m23 = __hsub2(*reinterpret_cast<const __half2*>(&e23), k1024);
                     mm[2 * t] = *reinterpret_cast<const uint32_t*>(&m01);
                     mm[2 * t + 1] = *reinterpret_cast<const uint32_t*>(&m23);
                 }
                 const uint32_t amin[8] = {mm[0], mm[1], mm[2], mm[3], mm[0], mm[1], mm[2], mm[3]};
-                tmem_st8(trow + static_cast<uint32_t>(kMinCol0 + 8 * buf), amin);
-                asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&amin_full[buf]);
+                tmem_st8(trow + mincol0 + static_cast<uint32_t>(8 * i), amin);
             }
-            if (lane == 0) mbar_arrive(&raw_free[rs]);
-            if (b >= 1 && !epilogue(b - 1, dprev, dminprev)) {
-                stop = true;
-                break;
+            // one wait for the block's stores, then one arrival
+            asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(&a_full[i]);
+                mbar_arrive(&raw_free[rs]);
             }
-            dprev = d;
-            dminprev = dmin;
         }
-        if (!stop && nblk > 0) epilogue(nblk - 1, dprev, dminprev);
+    } else {
+        // ---------------- epilogue ----------------
+        const int quarter = warp & 3;
+        const int ep = (warp - kFirstEp) >> 2;  // half of the group's vectors
+        const int r = 32 * quarter + lane;
+        const uint32_t trow = tmem + (static_cast<uint32_t>(32 * quarter) << 16);
+        const int nh = nv / 2, n0 = ep * nh;  // this warp's vectors (8 or 16)
+        float yacc[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) yacc[j] = 0.f;
+        for (int b = 0; b < nblk; ++b) {
+            const int i = b & 1, rs = b & (kRaw - 1);
+            if (!mbar_wait(&acc_full[i], (b >> 1) & 1, 4u, poisoned)) break;
+            if (!mbar_wait(&raw_full[rs], (b >> 2) & 1, 4u, poisoned)) break;
+            tc_fence_after();
+            const uint32_t dm = *reinterpret_cast<const uint32_t*>(smem + L.raw_off(rs) + r * BB);
+            const float d = f16_bits_to_f32(dm), dmin = f16_bits_to_f32(dm >> 16);
+            const float* vs = reinterpret_cast<const float*>(smem + L.v_off(rs));  // [2][nv]
+            const uint32_t c0 = trow + static_cast<uint32_t>(accw * i + n0);
+            float mv[16], lv[16], sv[16];
+            tmem_ld16x3(c0, c0 + nv, c0 + 2 * nv, mv, lv, sv);  // hi part, lo part, mins
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+                if (j < nh) {
+                    const int n = n0 + j;
+                    yacc[j] = fmaf(mv[j] + lv[j], d * vs[n], fmaf(-sv[j], dmin * vs[nv + n], yacc[j]));
+                }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(&acc_free[i]);
+                mbar_arrive(&raw_free[rs]);
+            }
+        }
         // ---------------- outputs ----------------
         const int row = m0 + r;
+        const int nbase = grp * nv;  // first vector of this group
         const int tile = blockIdx.y * gridDim.x + blockIdx.x;
         if (P.splits == 1) {
             if (row < P.M) {
 #pragma unroll
-                for (int i = 0; i < 16; ++i) {
-                    const int n = n0 + i;
-                    if (i < nq && n < P.N)
-                        *reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(P.y) + n * P.y_nb1 + 4LL * row) = yacc[i];
+                for (int j = 0; j < 16; ++j) {
+                    const int n = nbase + n0 + j;
+                    if (j < nh && n < P.N)
+                        *reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(P.y) + n * P.y_nb1 + 4LL * row) = yacc[j];
                 }
             }
         } else {
-            float* ptile = P.partial + (static_cast<int64_t>(tile) * P.splits + blockIdx.z) * (kMaxNP * kTM);
+            float* ptile = P.partial + (static_cast<int64_t>(tile) * P.splits + blockIdx.z) * (kMaxNV * kTM);
 #pragma unroll
-            for (int i = 0; i < 16; ++i)
-                if (i < nq) ptile[(n0 + i) * kTM + r] = yacc[i];
+            for (int j = 0; j < 16; ++j)
+                if (j < nh) ptile[(n0 + j) * kTM + r] = yacc[j];
             // the tile's last split sums all of them in split order (deterministic);
             // a split that gave up waiting counts in the high half and nobody sums
             __shared__ int last;
-            asm volatile("bar.sync 1, %0;" ::"n"(kDq * 32) : "memory");
-            if (threadIdx.x == 64) {
+            asm volatile("bar.sync 1, %0;" ::"n"(kEp * 32) : "memory");
+            if (threadIdx.x == 32 * kFirstEp) {
                 __threadfence();
                 const unsigned add = 1u + (*poisoned ? 0x10000u : 0u);
                 const unsigned old = atomicAdd(P.counters + tile, add);
@@ -493,15 +535,16 @@ __global__ void __launch_bounds__(kThr, 1) btc_kernel(const __grid_constant__ Bt
                     __threadfence();
                 }
             }
-            asm volatile("bar.sync 1, %0;" ::"n"(kDq * 32) : "memory");
+            asm volatile("bar.sync 1, %0;" ::"n"(kEp * 32) : "memory");
             if (last) {
-                const float* base = P.partial + static_cast<int64_t>(tile) * P.splits * (kMaxNP * kTM);
-                for (int i = threadIdx.x - 64; i < np * kTM; i += kDq * 32) {
-                    const int n = i / kTM, rr = i - n * kTM;
+                const float* base = P.partial + static_cast<int64_t>(tile) * P.splits * (kMaxNV * kTM);
+                for (int e = threadIdx.x - 32 * kFirstEp; e < nv * kTM; e += kEp * 32) {
+                    const int n = e / kTM, rr = e - n * kTM;
                     float acc = 0.f;
-                    for (int z = 0; z < P.splits; ++z) acc += __ldcg(base + z * (kMaxNP * kTM) + i);
-                    if (n < P.N && m0 + rr < P.M)
-                        *reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(P.y) + n * P.y_nb1 + 4LL * (m0 + rr)) = acc;
+                    for (int z = 0; z < P.splits; ++z) acc += __ldcg(base + z * (kMaxNV * kTM) + e);
+                    if (nbase + n < P.N && m0 + rr < P.M)
+                        *reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(P.y) + (nbase + n) * P.y_nb1 + 4LL * (m0 + rr)) =
+                            acc;
                 }
             }
         }
@@ -514,57 +557,73 @@ __global__ void __launch_bounds__(kThr, 1) btc_kernel(const __grid_constant__ Bt
     }
 }
 
-// The activation image of vector blockIdx.x: its power-of-two scale 2^e (the
-// maximum |x| in [2^14, 2^15) after scaling), hi / lo f16 parts, and the f16
-// hi / lo parts of its 32-element sums at scale 2^(e + 5); zeros past N.
+// The activation image, one warp per vector n and 256-element block b (lane
+// l holds elements 8 l .. 8 l + 7): the block's power-of-two scale 2^e (its
+// maximum |x| in [2^14, 2^15) after scaling), the hi / lo f16 parts, and the
+// f16 hi / lo parts of its eight 32-element sums at scale 2^(e + 5) (each sum
+// in double over four lanes); zeros past N. Vector n is vector n % nv of group
+// n / nv; a group's hi rows are followed by its lo rows.
 __global__ void btc_prep_kernel(const float* __restrict__ x, int64_t x_nb1, __half* __restrict__ ximg,
-                                __half* __restrict__ simg, float* __restrict__ vscale, int K, int N, int np) {
-    const int n = blockIdx.x;
-    const float* xn = reinterpret_cast<const float*>(reinterpret_cast<const uint8_t*>(x) + n * x_nb1);
-    __shared__ float red[32];
-    __shared__ int e_sh;
+                                __half* __restrict__ simg, float* __restrict__ vscale, int K, int N, int nv, int groups) {
+    const int lane = threadIdx.x & 31;
+    const int n = blockIdx.y * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int b = blockIdx.x;
+    const int np = nv * groups, g = n / nv, l = n - g * nv;
+    if (n >= np) return;
+    float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    if (n < N) {
+        const float* xn = reinterpret_cast<const float*>(reinterpret_cast<const uint8_t*>(x) + n * x_nb1) + 256 * b + 8 * lane;
+        if ((reinterpret_cast<uintptr_t>(xn) & 15) == 0) {
+            const float4 a0 = __ldg(reinterpret_cast<const float4*>(xn));
+            const float4 a1 = __ldg(reinterpret_cast<const float4*>(xn) + 1);
+            v[0] = a0.x, v[1] = a0.y, v[2] = a0.z, v[3] = a0.w, v[4] = a1.x, v[5] = a1.y, v[6] = a1.z, v[7] = a1.w;
+        } else {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) v[i] = __ldg(xn + i);
+        }
+    }
     float mx = 0.f;
-    if (n < N)
-        for (int k = threadIdx.x; k < K; k += blockDim.x) mx = fmaxf(mx, fabsf(xn[k]));
+#pragma unroll
+    for (int i = 0; i < 8; ++i) mx = fmaxf(mx, fabsf(v[i]));
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        float m = 0.f;
-        for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) m = fmaxf(m, red[w]);
-        int E = 0;
-        frexpf(m, &E);  // m < 2^E
-        e_sh = (m > 0.f && isfinite(m)) ? E - 15 : 0;
+    int E = 0;
+    frexpf(mx, &E);  // mx < 2^E
+    const int e = (mx > 0.f && isfinite(mx)) ? E - 15 : 0;
+    uint32_t hw[4], lw[4];
+    double acc = 0.0;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const float s0 = ldexpf(v[2 * i], -e), s1 = ldexpf(v[2 * i + 1], -e);
+        const __half h0 = __float2half_rn(s0), h1 = __float2half_rn(s1);
+        const __half l0 = __float2half_rn(s0 - __half2float(h0)), l1 = __float2half_rn(s1 - __half2float(h1));
+        hw[i] = static_cast<uint32_t>(__half_as_ushort(h0)) | (static_cast<uint32_t>(__half_as_ushort(h1)) << 16);
+        lw[i] = static_cast<uint32_t>(__half_as_ushort(l0)) | (static_cast<uint32_t>(__half_as_ushort(l1)) << 16);
+        acc += static_cast<double>(v[2 * i]) + static_cast<double>(v[2 * i + 1]);
     }
-    __syncthreads();
-    const int e = e_sh;
-    __half* hi = ximg + static_cast<int64_t>(n) * K;
-    __half* lo = ximg + static_cast<int64_t>(np + n) * K;
-    for (int k = threadIdx.x; k < K; k += blockDim.x) {
-        const float v = n < N ? ldexpf(xn[k], -e) : 0.f;
-        const __half h = __float2half_rn(v);
-        hi[k] = h;
-        lo[k] = __float2half_rn(v - __half2float(h));
+    const int64_t k = 256LL * b + 8 * lane;
+    const int64_t hrow = static_cast<int64_t>(g) * 2 * nv + l;
+    *reinterpret_cast<uint4*>(ximg + hrow * K + k) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+    *reinterpret_cast<uint4*>(ximg + (hrow + nv) * K + k) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+    // sub-block lane / 4: the four lanes' partial sums
+    acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+    acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+    __half* row = simg + (static_cast<int64_t>(b) * np + n) * 64;  // 128 bytes
+    if ((lane & 3) == 0) {
+        const double sv = ldexp(acc, -(e + 5));
+        const __half hs = __double2half(sv);
+        row[lane >> 2] = hs;
+        row[8 + (lane >> 2)] = __double2half(sv - static_cast<double>(__half2float(hs)));
+    } else if (lane < 8) {
+        // bytes 32 .. 127 of the row are zero (the mins MMA reads K = 16): lanes
+        // 1, 2, 3, 5, 6, 7 write one 16-byte piece each
+        const int j = lane - 1 - (lane >> 2);  // 0 .. 5
+        reinterpret_cast<uint4*>(row)[2 + j] = make_uint4(0u, 0u, 0u, 0u);
     }
-    // the sums: one 32-element sub-block per thread and round, in order, in double
-    const int nsub = K / 32;
-    for (int sb = threadIdx.x; sb < nsub; sb += blockDim.x) {
-        double acc = 0.0;
-        if (n < N)
-            for (int i = 0; i < 32; ++i) acc += static_cast<double>(xn[32 * sb + i]);
-        const double v = ldexp(acc, -(e + 5));
-        const __half h = __double2half(v);
-        const __half l = __double2half(v - static_cast<double>(__half2float(h)));
-        __half* row = simg + (static_cast<int64_t>(sb / 8) * np + n) * 64;
-        row[sb % 8] = h;
-        row[8 + sb % 8] = l;
-        if (sb % 8 == 0)
-            for (int i = 16; i < 64; ++i) row[i] = __float2half_rn(0.f);
-    }
-    if (threadIdx.x == 0) {
-        vscale[n] = ldexpf(1.f, e);
-        vscale[np + n] = ldexpf(1.f, e + 5);
+    if (lane == 0) {
+        float* vsb = vscale + ((static_cast<int64_t>(b) * groups + g) * 2) * nv + l;
+        vsb[0] = ldexpf(1.f, e);
+        vsb[nv] = ldexpf(1.f, e + 5);
     }
 }
 
@@ -585,15 +644,20 @@ EncodeFn btc_encoder() {
     return fn;
 }
 
-int np_of(const MulMatOp& o) { return (o.N + 15) / 16 * 16; }
+// Vectors per CTA (16 or 32) and vector groups: N <= 32 is one group of N
+// rounded up to 16; N = 33..64 is two groups of 32.
+int nv_of(const MulMatOp& o) { return o.N <= 16 ? 16 : 32; }
+int groups_of(const MulMatOp& o) { return (o.N + nv_of(o) - 1) / nv_of(o); }
+int np_of(const MulMatOp& o) { return nv_of(o) * groups_of(o); }
 size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
 size_t ximg_bytes(const MulMatOp& o) { return align256(static_cast<size_t>(2) * np_of(o) * o.K * 2); }
 size_t simg_bytes(const MulMatOp& o) { return align256(static_cast<size_t>(o.K / 256) * np_of(o) * 128); }
-size_t vscale_bytes(const MulMatOp& o) { return align256(static_cast<size_t>(2) * np_of(o) * 4); }
+size_t vscale_bytes(const MulMatOp& o) { return align256(static_cast<size_t>(o.K / 256) * 2 * np_of(o) * 4); }
+int tiles_of(const MulMatOp& o) { return (o.M + kTM - 1) / kTM * groups_of(o); }
 
 // K splits: about one wave of CTAs (one per SM), at least two blocks per split.
 int plan_splits(const MulMatOp& o, int num_sms) {
-    const int tiles = (o.M + kTM - 1) / kTM, nblk = o.K / 256;
+    const int tiles = tiles_of(o), nblk = o.K / 256;
     int s = num_sms / tiles;
     s = s < kMaxSplits ? s : kMaxSplits;
     s = s < nblk / 2 ? s : nblk / 2;
@@ -601,8 +665,8 @@ int plan_splits(const MulMatOp& o, int num_sms) {
 }
 size_t split_bytes(const MulMatOp& o, int splits) {
     if (splits <= 1) return 0;
-    const size_t tiles = static_cast<size_t>((o.M + kTM - 1) / kTM);
-    return align256(tiles * splits * kMaxNP * kTM * 4) + align256(tiles * 4);
+    const size_t tiles = static_cast<size_t>(tiles_of(o));
+    return align256(tiles * splits * kMaxNV * kTM * 4) + align256(tiles * 4);
 }
 
 }  // namespace
@@ -630,13 +694,14 @@ int launch_batched_tc(const MulMatOp& o, void* workspace, size_t workspace_bytes
     const size_t base = ximg_bytes(o) + simg_bytes(o) + vscale_bytes(o);
     if (base + split_bytes(o, splits) > workspace_bytes) splits = 1;
     if (base > workspace_bytes) return -static_cast<int>(cudaErrorInvalidValue);
-    const int np = np_of(o), nblk = o.K / 256, kb_split = (nblk + splits - 1) / splits;
+    const int nv = nv_of(o), groups = groups_of(o), np = np_of(o), nblk = o.K / 256;
+    const int kb_split = (nblk + splits - 1) / splits;
     splits = (nblk + kb_split - 1) / kb_split;  // no empty split
     uint8_t* ws = static_cast<uint8_t*>(workspace);
     __half* ximg = reinterpret_cast<__half*>(ws);
     __half* simg = reinterpret_cast<__half*>(ws + ximg_bytes(o));
     float* vscale = reinterpret_cast<float*>(ws + ximg_bytes(o) + simg_bytes(o));
-    btc_prep_kernel<<<np, 256, 0, stream>>>(o.x, o.x_nb1, ximg, simg, vscale, o.K, o.N, np);
+    btc_prep_kernel<<<dim3(nblk, np / 8), 256, 0, stream>>>(o.x, o.x_nb1, ximg, simg, vscale, o.K, o.N, nv, groups);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return -static_cast<int>(e);
     BtcArgs P{};
@@ -655,7 +720,7 @@ int launch_batched_tc(const MulMatOp& o, void* workspace, size_t workspace_bytes
     {
         const cuuint64_t dims[2] = {static_cast<cuuint64_t>(o.K), static_cast<cuuint64_t>(2 * np)};
         const cuuint64_t strides[1] = {static_cast<cuuint64_t>(o.K) * 2};
-        const cuuint32_t box[2] = {static_cast<cuuint32_t>(kChunk), static_cast<cuuint32_t>(np)};
+        const cuuint32_t box[2] = {static_cast<cuuint32_t>(kChunk), static_cast<cuuint32_t>(2 * nv)};
         if (enc(&P.xmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, ximg, dims, strides, box, es,
                 CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
@@ -664,11 +729,29 @@ int launch_batched_tc(const MulMatOp& o, void* workspace, size_t workspace_bytes
     {
         const cuuint64_t dims[2] = {64, static_cast<cuuint64_t>(nblk) * np};
         const cuuint64_t strides[1] = {128};
-        const cuuint32_t box[2] = {64, static_cast<cuuint32_t>(np)};
+        const cuuint32_t box[2] = {64, static_cast<cuuint32_t>(nv)};
         if (enc(&P.smap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, simg, dims, strides, box, es,
                 CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
             return -static_cast<int>(cudaErrorInvalidValue);
+    }
+    // TMEM: per issuer the accumulators (an epilogue warp reads 16-column
+    // groups from its first vector, nv / 2 of them: the columns cover the
+    // overhang), then A_min (8 columns each) and the two A stages from a
+    // 32-column boundary
+    {
+        const int nh = nv / 2;
+        const int need = max(3 * nv, 2 * nv + nh + 16);
+        P.accw = (need + 31) / 32 * 32;
+        P.acol0 = (2 * P.accw + 16 + 31) / 32 * 32;
+        if (P.acol0 + 2 * kACols > kTmemCols) return -static_cast<int>(cudaErrorInvalidValue);
+    }
+    // B stages: the shared memory left after the raw and scale slots, within 224 KB
+    {
+        const Smem s0(nv, bb, 0);
+        const int nb = static_cast<int>(((224u << 10) - s0.total()) / s0.b_bytes);
+        P.nstb = nb >= 4 ? 4 : 2;
+        if (nb < 2) return -static_cast<int>(cudaErrorInvalidValue);
     }
     P.vscale = vscale;
     P.y = o.y;
@@ -676,18 +759,18 @@ int launch_batched_tc(const MulMatOp& o, void* workspace, size_t workspace_bytes
     P.M = o.M;
     P.K = o.K;
     P.N = o.N;
-    P.np = np;
+    P.nv = nv;
+    P.groups = groups;
     P.splits = splits;
     P.kb_split = kb_split;
-    const int tiles = (o.M + kTM - 1) / kTM;
-    int launched = 2;
+    const int tiles = tiles_of(o);
     if (splits > 1) {
         P.partial = reinterpret_cast<float*>(ws + base);
-        P.counters = reinterpret_cast<unsigned*>(ws + base + align256(static_cast<size_t>(tiles) * splits * kMaxNP * kTM * 4));
+        P.counters = reinterpret_cast<unsigned*>(ws + base + align256(static_cast<size_t>(tiles) * splits * kMaxNV * kTM * 4));
         e = cudaMemsetAsync(P.counters, 0, static_cast<size_t>(tiles) * 4, stream);
         if (e != cudaSuccess) return -static_cast<int>(e);
     }
-    const size_t smem = Smem(np, bb).total(np);
+    const size_t smem = Smem(nv, bb, P.nstb).total();
     static size_t configured[kMaxDevices][2] = {};
     int dev = 0;
     if ((e = cudaGetDevice(&dev)) != cudaSuccess) return -static_cast<int>(e);
@@ -699,9 +782,9 @@ int launch_batched_tc(const MulMatOp& o, void* workspace, size_t workspace_bytes
         if (e != cudaSuccess) return -static_cast<int>(e);
         configured[dev][ti] = smem;
     }
-    kernel<<<dim3(tiles, 1, splits), kThr, smem, stream>>>(P);
+    kernel<<<dim3((o.M + kTM - 1) / kTM, groups, splits), kThr, smem, stream>>>(P);
     e = cudaGetLastError();
-    return e == cudaSuccess ? launched : -static_cast<int>(e);
+    return e == cudaSuccess ? 2 : -static_cast<int>(e);
 }
 
 unsigned read_and_clear_btc_error() {
