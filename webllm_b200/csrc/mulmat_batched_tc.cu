@@ -64,7 +64,7 @@ constexpr int kMaxNP = 64;    // vectors per launch
 constexpr int kMaxNV = 32;    // vectors per CTA
 constexpr int kChunk = 64;    // K per activation box (one 128-byte swizzle atom of f16)
 constexpr int kMaxStB = 4;    // B stages (blocks of activations), at most
-constexpr int kRaw = 4;       // raw blocks in flight
+constexpr int kMaxRaw = 8;    // raw blocks in flight, at most (8, or 4 where B stages need the room)
 constexpr int kDq = 8;        // dequant warps
 constexpr int kEp = 8;        // epilogue warps
 constexpr int kFirstDq = 3;   // warps: 0 TMA, 1-2 MMA issuers, then dequant, then epilogue
@@ -88,7 +88,7 @@ struct BtcArgs {
     int64_t y_nb1;        // bytes between output vectors
     int32_t M, K, N;
     int32_t nv, groups;   // vectors per CTA, vector groups (grid y)
-    int32_t nstb;         // B stages (2 or 4)
+    int32_t nstb, nraw;   // B stages (2 or 4), raw slots (4 or 8)
     int32_t accw, acol0;  // TMEM columns of one issuer's accumulators; first A column
     int32_t splits, kb_split;
     float* partial;       // [tile][split][kMaxNV][128] (split K)
@@ -139,6 +139,10 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
 }
 __device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+// Adds to the barrier's expected transaction bytes without arriving.
+__device__ __forceinline__ void mbar_expect_tx_only(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.expect_tx.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
 }
 __device__ __forceinline__ void tma_2d(void* dst, const CUtensorMap* tm, int x, int y, uint64_t* bar) {
     asm volatile(
@@ -215,23 +219,24 @@ __device__ __forceinline__ void tmem_ld16x3(uint32_t t0, uint32_t t1, uint32_t t
 // Shared-memory layout (from a 1024-byte aligned base): B stages (four hi+lo
 // activation boxes, then the sums box), raw slots, scale slots, barriers.
 struct Smem {
-    uint32_t box_bytes, s_bytes, b_bytes, raw_bytes, v_bytes, nstb;
-    __host__ __device__ Smem(int nv, int bb, int nstb_) {
+    uint32_t box_bytes, s_bytes, b_bytes, raw_bytes, v_bytes, nstb, nraw;
+    __host__ __device__ Smem(int nv, int bb, int nstb_, int nraw_) {
         box_bytes = static_cast<uint32_t>(2 * nv * 128);  // hi + lo rows of one 64-element chunk
         s_bytes = static_cast<uint32_t>(nv * 128);
         b_bytes = 4 * box_bytes + s_bytes;
         raw_bytes = static_cast<uint32_t>(kTM * bb);
         v_bytes = static_cast<uint32_t>(2 * nv * 4);  // the block's 2 nv scales
         nstb = static_cast<uint32_t>(nstb_);
+        nraw = static_cast<uint32_t>(nraw_);
     }
     __host__ __device__ uint32_t b_off(int s) const { return s * b_bytes; }
     __host__ __device__ uint32_t raw_off(int r) const { return nstb * b_bytes + r * raw_bytes; }
-    __host__ __device__ uint32_t v_off(int r) const { return nstb * b_bytes + kRaw * raw_bytes + r * v_bytes; }
-    __host__ __device__ uint32_t bar_off() const { return nstb * b_bytes + kRaw * (raw_bytes + v_bytes); }
-    // barriers: b_full, b_free [kMaxStB], raw_full, raw_free [kRaw], a_full,
+    __host__ __device__ uint32_t v_off(int r) const { return nstb * b_bytes + nraw * raw_bytes + r * v_bytes; }
+    __host__ __device__ uint32_t bar_off() const { return nstb * b_bytes + nraw * (raw_bytes + v_bytes); }
+    // barriers: b_full, b_free [kMaxStB], raw_full, raw_free [kMaxRaw], a_full,
     // a_free, acc_full, acc_free [2]; then the TMEM base address word and the
     // poison flag
-    static constexpr uint32_t kBars = 2 * kMaxStB + 2 * kRaw + 8;
+    static constexpr uint32_t kBars = 2 * kMaxStB + 2 * kMaxRaw + 8;
     __host__ __device__ uint32_t total() const {
         return bar_off() + 8 * kBars + 16 + 1024;  // + alignment slack
     }
@@ -242,14 +247,14 @@ __global__ void __launch_bounds__(kThr, 1) btc_kernel(const __grid_constant__ Bt
     extern __shared__ __align__(128) uint8_t smem_raw[];
     uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     constexpr int BB = blk_bytes<TYPE>();
-    const int nv = P.nv, nstb = P.nstb;
-    const Smem L(nv, BB, nstb);
+    const int nv = P.nv, nstb = P.nstb, nraw = P.nraw;
+    const Smem L(nv, BB, nstb, nraw);
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L.bar_off());
     uint64_t* b_full = bars;
     uint64_t* b_free = b_full + kMaxStB;
     uint64_t* raw_full = b_free + kMaxStB;
-    uint64_t* raw_free = raw_full + kRaw;
-    uint64_t* a_full = raw_free + kRaw;
+    uint64_t* raw_free = raw_full + kMaxRaw;
+    uint64_t* a_full = raw_free + kMaxRaw;
     uint64_t* a_free = a_full + 2;
     uint64_t* acc_full = a_free + 2;
     uint64_t* acc_free = acc_full + 2;
@@ -269,7 +274,7 @@ __global__ void __launch_bounds__(kThr, 1) btc_kernel(const __grid_constant__ Bt
             mbar_init(&b_full[i], 1);
             mbar_init(&b_free[i], 1);
         }
-        for (int r = 0; r < kRaw; ++r) {
+        for (int r = 0; r < kMaxRaw; ++r) {
             mbar_init(&raw_full[r], 1);
             mbar_init(&raw_free[r], kDq + kEp);
         }
@@ -293,24 +298,37 @@ __global__ void __launch_bounds__(kThr, 1) btc_kernel(const __grid_constant__ Bt
     const uint32_t tmem = *tmem_slot;
 
     const int lgb = nstb == 4 ? 2 : 1;  // log2 of the B stages (2 or 4)
+    const int lgr = nraw == 8 ? 3 : 2;  // log2 of the raw slots (4 or 8)
     if (warp == 0) {
         // ---------------- TMA producer ----------------
         if (lane == 0) {
             asm volatile("prefetch.tensormap [%0];" ::"l"(&P.wmap) : "memory");
             asm volatile("prefetch.tensormap [%0];" ::"l"(&P.xmap) : "memory");
             asm volatile("prefetch.tensormap [%0];" ::"l"(&P.smap) : "memory");
-            int issued = 0;  // blocks whose copies are all in flight
+            // the weights do not depend on the pre-pass: the first raw slots' boxes
+            // go out before the wait for it (their barrier's arrival comes with the
+            // scales, after the wait, so no phase can complete early)
+            const int pre = min(nblk, nraw);
+            for (int b = 0; b < pre; ++b) {
+                mbar_expect_tx_only(&raw_full[b], L.raw_bytes);
+                tma_2d(smem + L.raw_off(b), &P.wmap, (kb0 + b) * (BB / 8), m0, &raw_full[b]);
+            }
+            asm volatile("griddepcontrol.wait;" ::: "memory");
+            int armed = 0;   // blocks whose raw slot copies are all issued and armed
+            int issued = 0;  // blocks whose B stage copies are issued
             for (int b = 0; b < nblk; ++b) {
-                const int r = b & (kRaw - 1), s = b & (nstb - 1), kb = kb0 + b;
-                if (b >= kRaw && !mbar_wait(&raw_free[r], ((b >> 2) - 1) & 1, 1u, poisoned)) break;
-                mbar_expect_tx(&raw_full[r], L.raw_bytes + L.v_bytes);
-                tma_2d(smem + L.raw_off(r), &P.wmap, kb * (BB / 8), m0, &raw_full[r]);
+                const int r = b & (nraw - 1), s = b & (nstb - 1), kb = kb0 + b;
+                if (b >= nraw) {
+                    if (!mbar_wait(&raw_free[r], ((b >> lgr) - 1) & 1, 1u, poisoned)) break;
+                    mbar_expect_tx(&raw_full[r], L.raw_bytes + L.v_bytes);
+                    tma_2d(smem + L.raw_off(r), &P.wmap, kb * (BB / 8), m0, &raw_full[r]);
+                } else {
+                    mbar_expect_tx(&raw_full[r], L.v_bytes);
+                }
                 bulk_copy(smem + L.v_off(r), P.vscale + (static_cast<int64_t>(kb) * P.groups + grp) * 2 * nv, L.v_bytes,
                           &raw_full[r]);
-                if (b >= nstb && !mbar_wait(&b_free[s], ((b >> lgb) - 1) & 1, 1u, poisoned)) {
-                    issued = -(b + 1);  // the raw slot of block b is in flight, its B stage is not
-                    break;
-                }
+                armed = b + 1;
+                if (b >= nstb && !mbar_wait(&b_free[s], ((b >> lgb) - 1) & 1, 1u, poisoned)) break;
                 uint8_t* dst = smem + L.b_off(s);
                 mbar_expect_tx(&b_full[s], L.b_bytes);
 #pragma unroll
@@ -320,12 +338,13 @@ __global__ void __launch_bounds__(kThr, 1) btc_kernel(const __grid_constant__ Bt
                 issued = b + 1;
             }
             // before the CTA exits, the last copy into every slot and stage has
-            // landed (bounded, whatever the poison flag says)
-            const int raw_issued = issued < 0 ? -issued : issued;
-            const int b_issued = issued < 0 ? -issued - 1 : issued;
-            for (int b = max(0, raw_issued - kRaw); b < raw_issued; ++b)
-                if (!mbar_wait_drain(&raw_full[b & (kRaw - 1)], (b >> 2) & 1)) atomicOr(&g_btc_error, 16u);
-            for (int b = max(0, b_issued - nstb); b < b_issued; ++b)
+            // landed (bounded, whatever the poison flag says); a pre-issued slot
+            // that was never armed gets its arrival now
+            for (int b = armed; b < pre; ++b) mbar_arrive(&raw_full[b]);
+            const int raw_issued = max(armed, pre);
+            for (int b = max(0, raw_issued - nraw); b < raw_issued; ++b)
+                if (!mbar_wait_drain(&raw_full[b & (nraw - 1)], (b >> lgr) & 1)) atomicOr(&g_btc_error, 16u);
+            for (int b = max(0, issued - nstb); b < issued; ++b)
                 if (!mbar_wait_drain(&b_full[b & (nstb - 1)], (b >> lgb) & 1)) atomicOr(&g_btc_error, 16u);
         }
     } else if (warp < kFirstDq) {
@@ -379,8 +398,8 @@ __global__ void __launch_bounds__(kThr, 1) btc_kernel(const __grid_constant__ Bt
         const uint32_t sel_b = 0x4440u + 2u + static_cast<uint32_t>(h);  // byte 2 + h
         const __half2 k1024 = __float2half2_rn(1024.f), km1024 = __float2half2_rn(-1024.f);
         for (int b = 0; b < nblk; ++b) {
-            const int rs = b & (kRaw - 1), i = b & 1;
-            if (!mbar_wait(&raw_full[rs], (b >> 2) & 1, 3u, poisoned)) break;
+            const int rs = b & (nraw - 1), i = b & 1;
+            if (!mbar_wait(&raw_full[rs], (b >> lgr) & 1, 3u, poisoned)) break;
             const uint8_t* blk = smem + L.raw_off(rs) + r * BB;
             // scales of this thread's sub-blocks j = 2p + h (p = 0..3), get_scale_min_k4
             // (src/inference/jsep/ops/matmul.ts:408-424) on the bytes of the three scale words
@@ -479,28 +498,26 @@ __global__ void __launch_bounds__(kThr, 1) btc_kernel(const __grid_constant__ Bt
 #pragma unroll
         for (int j = 0; j < 16; ++j) yacc[j] = 0.f;
         for (int b = 0; b < nblk; ++b) {
-            const int i = b & 1, rs = b & (kRaw - 1);
-            if (!mbar_wait(&acc_full[i], (b >> 1) & 1, 4u, poisoned)) break;
-            if (!mbar_wait(&raw_full[rs], (b >> 2) & 1, 4u, poisoned)) break;
-            tc_fence_after();
+            const int i = b & 1, rs = b & (nraw - 1);
+            // the block's d, dmin and scales first (they need only the raw slot)
+            if (!mbar_wait(&raw_full[rs], (b >> lgr) & 1, 4u, poisoned)) break;
             const uint32_t dm = *reinterpret_cast<const uint32_t*>(smem + L.raw_off(rs) + r * BB);
             const float d = f16_bits_to_f32(dm), dmin = f16_bits_to_f32(dm >> 16);
-            const float* vs = reinterpret_cast<const float*>(smem + L.v_off(rs));  // [2][nv]
-            const uint32_t c0 = trow + static_cast<uint32_t>(accw * i + n0);
+            const float* vs = reinterpret_cast<const float*>(smem + L.v_off(rs)) + n0;  // [2][nv] from vector n0
+            if (!mbar_wait(&acc_full[i], (b >> 1) & 1, 4u, poisoned)) break;
+            tc_fence_after();
             float mv[16], lv[16], sv[16];
-            tmem_ld16x3(c0, c0 + nv, c0 + 2 * nv, mv, lv, sv);  // hi part, lo part, mins
-#pragma unroll
-            for (int j = 0; j < 16; ++j)
-                if (j < nh) {
-                    const int n = n0 + j;
-                    yacc[j] = fmaf(mv[j] + lv[j], d * vs[n], fmaf(-sv[j], dmin * vs[nv + n], yacc[j]));
-                }
+            tmem_ld16x3(trow + static_cast<uint32_t>(accw * i + n0), trow + static_cast<uint32_t>(accw * i + nv + n0),
+                        trow + static_cast<uint32_t>(accw * i + 2 * nv + n0), mv, lv, sv);  // hi part, lo part, mins
+            // the accumulators are read: the issuer may start on block b + 2
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) {
-                mbar_arrive(&acc_free[i]);
-                mbar_arrive(&raw_free[rs]);
-            }
+            if (lane == 0) mbar_arrive(&acc_free[i]);
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+                if (j < nh) yacc[j] = fmaf(mv[j] + lv[j], d * vs[j], fmaf(-sv[j], dmin * vs[nv + j], yacc[j]));
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&raw_free[rs]);
         }
         // ---------------- outputs ----------------
         const int row = m0 + r;
@@ -562,9 +579,16 @@ __global__ void __launch_bounds__(kThr, 1) btc_kernel(const __grid_constant__ Bt
 // maximum |x| in [2^14, 2^15) after scaling), the hi / lo f16 parts, and the
 // f16 hi / lo parts of its eight 32-element sums at scale 2^(e + 5) (each sum
 // in double over four lanes); zeros past N. Vector n is vector n % nv of group
-// n / nv; a group's hi rows are followed by its lo rows.
+// n / nv; a group's hi rows are followed by its lo rows. CTA (0, 0) also zeroes
+// the split-K tile counters. The GEMM that follows may start at once (its
+// prologue and first weight loads overlap this kernel; it waits for the
+// image with griddepcontrol.wait).
 __global__ void btc_prep_kernel(const float* __restrict__ x, int64_t x_nb1, __half* __restrict__ ximg,
-                                __half* __restrict__ simg, float* __restrict__ vscale, int K, int N, int nv, int groups) {
+                                __half* __restrict__ simg, float* __restrict__ vscale, int K, int N, int nv, int groups,
+                                unsigned* __restrict__ counters, int ncounters) {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    if (blockIdx.x == 0 && blockIdx.y == 0)
+        for (int t = threadIdx.x; t < ncounters; t += blockDim.x) counters[t] = 0u;
     const int lane = threadIdx.x & 31;
     const int n = blockIdx.y * (blockDim.x >> 5) + (threadIdx.x >> 5);
     const int b = blockIdx.x;
@@ -701,9 +725,7 @@ int launch_batched_tc(const MulMatOp& o, void* workspace, size_t workspace_bytes
     __half* ximg = reinterpret_cast<__half*>(ws);
     __half* simg = reinterpret_cast<__half*>(ws + ximg_bytes(o));
     float* vscale = reinterpret_cast<float*>(ws + ximg_bytes(o) + simg_bytes(o));
-    btc_prep_kernel<<<dim3(nblk, np / 8), 256, 0, stream>>>(o.x, o.x_nb1, ximg, simg, vscale, o.K, o.N, nv, groups);
-    cudaError_t e = cudaGetLastError();
-    if (e != cudaSuccess) return -static_cast<int>(e);
+    cudaError_t e = cudaSuccess;
     BtcArgs P{};
     const EncodeFn enc = btc_encoder();
     const int bb = o.type == kTypeQ5_K ? 176 : 144;
@@ -746,12 +768,21 @@ int launch_batched_tc(const MulMatOp& o, void* workspace, size_t workspace_bytes
         P.acol0 = (2 * P.accw + 16 + 31) / 32 * 32;
         if (P.acol0 + 2 * kACols > kTmemCols) return -static_cast<int>(cudaErrorInvalidValue);
     }
-    // B stages: the shared memory left after the raw and scale slots, within 224 KB
+    // raw slots and B stages within 224 KB: 8 raw slots where 4 B stages still
+    // fit, else 4 raw slots and as many B stages (4 or 2) as fit
     {
-        const Smem s0(nv, bb, 0);
-        const int nb = static_cast<int>(((224u << 10) - s0.total()) / s0.b_bytes);
-        P.nstb = nb >= 4 ? 4 : 2;
+        const auto stages_with = [&](int nraw) {
+            const Smem s0(nv, bb, 0, nraw);
+            return static_cast<int>(((224u << 10) - s0.total()) / s0.b_bytes);
+        };
+        int nb = stages_with(8);
+        P.nraw = 8;
+        if (nb < 4) {
+            nb = stages_with(4);
+            P.nraw = 4;
+        }
         if (nb < 2) return -static_cast<int>(cudaErrorInvalidValue);
+        P.nstb = nb >= 4 ? 4 : 2;
     }
     P.vscale = vscale;
     P.y = o.y;
@@ -767,10 +798,11 @@ int launch_batched_tc(const MulMatOp& o, void* workspace, size_t workspace_bytes
     if (splits > 1) {
         P.partial = reinterpret_cast<float*>(ws + base);
         P.counters = reinterpret_cast<unsigned*>(ws + base + align256(static_cast<size_t>(tiles) * splits * kMaxNV * kTM * 4));
-        e = cudaMemsetAsync(P.counters, 0, static_cast<size_t>(tiles) * 4, stream);
-        if (e != cudaSuccess) return -static_cast<int>(e);
     }
-    const size_t smem = Smem(nv, bb, P.nstb).total();
+    btc_prep_kernel<<<dim3(nblk, np / 8), 256, 0, stream>>>(o.x, o.x_nb1, ximg, simg, vscale, o.K, o.N, nv, groups,
+                                                            P.counters, splits > 1 ? tiles : 0);
+    if ((e = cudaGetLastError()) != cudaSuccess) return -static_cast<int>(e);
+    const size_t smem = Smem(nv, bb, P.nstb, P.nraw).total();
     static size_t configured[kMaxDevices][2] = {};
     int dev = 0;
     if ((e = cudaGetDevice(&dev)) != cudaSuccess) return -static_cast<int>(e);
@@ -782,8 +814,18 @@ int launch_batched_tc(const MulMatOp& o, void* workspace, size_t workspace_bytes
         if (e != cudaSuccess) return -static_cast<int>(e);
         configured[dev][ti] = smem;
     }
-    kernel<<<dim3((o.M + kTM - 1) / kTM, groups, splits), kThr, smem, stream>>>(P);
-    e = cudaGetLastError();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((o.M + kTM - 1) / kTM, groups, splits);
+    cfg.blockDim = dim3(kThr);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&cfg, kernel, P);
+    if (e == cudaSuccess) e = cudaGetLastError();
     return e == cudaSuccess ? 2 : -static_cast<int>(e);
 }
 
