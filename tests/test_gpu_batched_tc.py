@@ -3,7 +3,10 @@ decoding together, N = 5..64, and N = 3-4 where the streaming kernel cannot
 take the shape): both error metrics of the path (max-normalized and
 per-element, 1e-3) against a float64 matmul of the device-dequantized
 weights, on N(0,1) activations and on outlier channels; shapes with partial
-row tiles, split K and K not a multiple of 1024."""
+row tiles, split K and K not a multiple of 1024. Weights of at most 4096 x 4096
+below 16 vectors route to the mma.sync GEMM instead; the shapes above that
+size (5000 x 4352, 4200 x 4608: partial row tiles, K = 17 and 18 blocks) keep
+those N on this kernel."""
 from __future__ import annotations
 
 import zlib
@@ -52,7 +55,8 @@ def _kernels():
 @pytest.mark.parametrize("qtype,M,K", [(jsep.GGML_TYPE_Q4_K, 4096, 4096), (jsep.GGML_TYPE_Q4_K, 14336, 4096),
                                        (jsep.GGML_TYPE_Q4_K, 4096, 14336), (jsep.GGML_TYPE_Q4_K, 1000, 2304),
                                        (jsep.GGML_TYPE_Q5_K, 4096, 4096), (jsep.GGML_TYPE_Q5_K, 333, 3072),
-                                       (jsep.GGML_TYPE_Q4_K, 128, 256)])
+                                       (jsep.GGML_TYPE_Q4_K, 128, 256), (jsep.GGML_TYPE_Q4_K, 5000, 4352),
+                                       (jsep.GGML_TYPE_Q5_K, 4200, 4608)])
 def test_batched_tc_both_metrics(runtime, qtype, M, K, N):
     rng = np.random.default_rng(zlib.crc32(repr((qtype, M, K, N)).encode()))
     x = synth.activations(rng, N, K)

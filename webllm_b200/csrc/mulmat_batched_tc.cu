@@ -118,9 +118,14 @@ __device__ __forceinline__ bool mbar_try(uint64_t* bar, uint32_t parity) {
     return ok != 0;
 }
 // Bounded wait; a timeout poisons the CTA (every later wait returns at once).
+// SLEEP_NS > 0 backs off between polls: warps whose waits are long and off the
+// critical path (the copy warp, the epilogue) then leave the issue slots to
+// the dequantizing warps on the same scheduler.
+template <int SLEEP_NS = 0>
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned code, volatile int* poisoned) {
     for (uint32_t i = 0; i < kSpin; ++i) {
         if (mbar_try(bar, parity)) return true;
+        if (SLEEP_NS > 0) __nanosleep(SLEEP_NS);
         if ((i & 255u) == 255u && *poisoned) return false;
     }
     *poisoned = 1;
@@ -234,9 +239,9 @@ struct Smem {
     __host__ __device__ uint32_t v_off(int r) const { return nstb * b_bytes + nraw * raw_bytes + r * v_bytes; }
     __host__ __device__ uint32_t bar_off() const { return nstb * b_bytes + nraw * (raw_bytes + v_bytes); }
     // barriers: b_full, b_free [kMaxStB], raw_full, raw_free [kMaxRaw], a_full,
-    // a_free, acc_full, acc_free [2]; then the TMEM base address word and the
-    // poison flag
-    static constexpr uint32_t kBars = 2 * kMaxStB + 2 * kMaxRaw + 8;
+    // a_free [4] (A stage i, half f at 2 i + f), acc_full, acc_free [2]; then
+    // the TMEM base address word and the poison flag
+    static constexpr uint32_t kBars = 2 * kMaxStB + 2 * kMaxRaw + 12;
     __host__ __device__ uint32_t total() const {
         return bar_off() + 8 * kBars + 16 + 1024;  // + alignment slack
     }
@@ -255,8 +260,8 @@ __global__ void __launch_bounds__(kThr, 1) btc_kernel(const __grid_constant__ Bt
     uint64_t* raw_full = b_free + kMaxStB;
     uint64_t* raw_free = raw_full + kMaxRaw;
     uint64_t* a_full = raw_free + kMaxRaw;
-    uint64_t* a_free = a_full + 2;
-    uint64_t* acc_full = a_free + 2;
+    uint64_t* a_free = a_full + 4;
+    uint64_t* acc_full = a_free + 4;
     uint64_t* acc_free = acc_full + 2;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_free + 2);
     volatile int* poisoned = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -278,9 +283,11 @@ __global__ void __launch_bounds__(kThr, 1) btc_kernel(const __grid_constant__ Bt
             mbar_init(&raw_full[r], 1);
             mbar_init(&raw_free[r], kDq + kEp);
         }
-        for (int p = 0; p < 2; ++p) {
+        for (int p = 0; p < 4; ++p) {
             mbar_init(&a_full[p], kDq);
             mbar_init(&a_free[p], 1);
+        }
+        for (int p = 0; p < 2; ++p) {
             mbar_init(&acc_full[p], 1);
             mbar_init(&acc_free[p], kEp);
         }
@@ -319,7 +326,7 @@ __global__ void __launch_bounds__(kThr, 1) btc_kernel(const __grid_constant__ Bt
             for (int b = 0; b < nblk; ++b) {
                 const int r = b & (nraw - 1), s = b & (nstb - 1), kb = kb0 + b;
                 if (b >= nraw) {
-                    if (!mbar_wait(&raw_free[r], ((b >> lgr) - 1) & 1, 1u, poisoned)) break;
+                    if (!mbar_wait<64>(&raw_free[r], ((b >> lgr) - 1) & 1, 1u, poisoned)) break;
                     mbar_expect_tx(&raw_full[r], L.raw_bytes + L.v_bytes);
                     tma_2d(smem + L.raw_off(r), &P.wmap, kb * (BB / 8), m0, &raw_full[r]);
                 } else {
@@ -328,7 +335,7 @@ __global__ void __launch_bounds__(kThr, 1) btc_kernel(const __grid_constant__ Bt
                 bulk_copy(smem + L.v_off(r), P.vscale + (static_cast<int64_t>(kb) * P.groups + grp) * 2 * nv, L.v_bytes,
                           &raw_full[r]);
                 armed = b + 1;
-                if (b >= nstb && !mbar_wait(&b_free[s], ((b >> lgb) - 1) & 1, 1u, poisoned)) break;
+                if (b >= nstb && !mbar_wait<64>(&b_free[s], ((b >> lgb) - 1) & 1, 1u, poisoned)) break;
                 uint8_t* dst = smem + L.b_off(s);
                 mbar_expect_tx(&b_full[s], L.b_bytes);
 #pragma unroll
@@ -364,20 +371,35 @@ __global__ void __launch_bounds__(kThr, 1) btc_kernel(const __grid_constant__ Bt
             for (int b = i, u = 0; b < nblk; b += 2, ++u) {  // u: this issuer's block count (its phases)
                 const int s = b & (nstb - 1);
                 if (u >= 1 && !mbar_wait(&acc_free[i], (u - 1) & 1, 2u, poisoned)) break;
-                if (!mbar_wait(&b_full[s], (b >> lgb) & 1, 2u, poisoned) || !mbar_wait(&a_full[i], u & 1, 2u, poisoned))
+                // the A stage comes in two halves (chunks 0-1, 2-3): the MMAs of the
+                // first overlap the dequantization of the second
+                if (!mbar_wait(&b_full[s], (b >> lgb) & 1, 2u, poisoned) ||
+                    !mbar_wait(&a_full[2 * i], u & 1, 2u, poisoned))
                     break;
                 tc_fence_after();
                 const uint64_t bd = bdesc0 + (L.b_off(s) >> 4);
-                // the mins: A_min (K = 16) against the block's sums box
-                umma_f16_ts(dmin, amin, bd + ((4 * L.box_bytes) >> 4), idesc_min, 0u);
+                bool second = true;  // the second half arrived
 #pragma unroll
                 for (int c = 0; c < 4; ++c) {
+                    if (c == 2) {
+                        umma_commit(&a_free[2 * i]);  // the first half is free once these have read it
+                        last_bar = &a_free[2 * i];
+                        last_par = static_cast<uint32_t>(u & 1);
+                        if (!mbar_wait(&a_full[2 * i + 1], u & 1, 2u, poisoned)) {
+                            second = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        // the mins: A_min (K = 16, written with the second half) against the sums box
+                        umma_f16_ts(dmin, amin, bd + ((4 * L.box_bytes) >> 4), idesc_min, 0u);
+                    }
                     const uint64_t bc = bd + ((c * L.box_bytes) >> 4);
 #pragma unroll
                     for (int ks = 0; ks < kChunk / 16; ++ks)  // K = 16 per MMA: 8 A columns, 32 bytes of B rows
                         umma_f16_ts(dmain, a0 + 32 * c + 8 * ks, bc + 2 * ks, idesc_main, (c | ks) ? 1u : 0u);
                 }
-                umma_commit(&a_free[i]);  // A stage, A_min and B stage are free once these have read them
+                if (!second) break;  // the first half's MMAs are tracked by their commit
+                umma_commit(&a_free[2 * i + 1]);  // the second half, A_min and the B stage are read
                 umma_commit(&b_free[s]);
                 umma_commit(&acc_full[i]);
                 last_bar = &acc_full[i];
@@ -424,68 +446,76 @@ __global__ void __launch_bounds__(kThr, 1) btc_kernel(const __grid_constant__ Bt
                     hv[qq][3] = t.w;
                 }
             }
-            // A stage i (and A_min i) is free once issuer i's MMAs of block b - 2 have read it
-            if (b >= 2 && !mbar_wait(&a_free[i], ((b >> 1) - 1) & 1, 3u, poisoned)) break;
-            tc_fence_after();
+            // A stage i, half f (chunks 2f, 2f + 1; A_min with the second half) is
+            // free once issuer i's MMAs of block b - 2 have read it
             const uint32_t acol = static_cast<uint32_t>(P.acol0 + kACols * i + 16 * h);
+            bool stop = false;
 #pragma unroll
-            for (int p = 0; p < 4; ++p) {
-                // A = sc q exactly: (1024 + q) sc - 1024 sc in one f16 FMA (the
-                // exact result, at most 1953, is an f16 integer); sc itself as the
-                // f16 (1024 + sc) - 1024, both halves
-                const uint32_t sbits = 0x64006400u | (scv[p] * 0x00010001u);
-                const __half2 sc2 = __hsub2(*reinterpret_cast<const __half2*>(&sbits), k1024);
-                const __half2 mn2 = __hmul2(sc2, km1024);
+            for (int f = 0; f < 2; ++f) {
+                if (b >= 2 && !mbar_wait(&a_free[2 * i + f], ((b >> 1) - 1) & 1, 3u, poisoned)) {
+                    stop = true;
+                    break;
+                }
+                tc_fence_after();
 #pragma unroll
-                for (int qq = 0; qq < 2; ++qq) {
-                    // bytes 16 qq .. 16 qq + 15 of pair p; this thread's quants are their
-                    // low (h = 0) or high (h = 1) nibbles: elements 64p + 32h + 16qq + l
-                    const uint4 v0 = qv[2 * p + qq];
-                    const uint32_t wv[4] = {v0.x, v0.y, v0.z, v0.w};
-                    uint32_t out[8];  // 16 f16, element order l = 0..15
+                for (int pp = 0; pp < 2; ++pp) {
+                    const int p = 2 * f + pp;
+                    // A = sc q exactly: (1024 + q) sc - 1024 sc in one f16 FMA (the
+                    // exact result, at most 1953, is an f16 integer); sc itself as the
+                    // f16 (1024 + sc) - 1024, both halves
+                    const uint32_t sbits = 0x64006400u | (scv[p] * 0x00010001u);
+                    const __half2 sc2 = __hsub2(*reinterpret_cast<const __half2*>(&sbits), k1024);
+                    const __half2 mn2 = __hmul2(sc2, km1024);
 #pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        uint32_t nib = (wv[j] >> (4 * h)) & 0x0F0F0F0Fu;
-                        if constexpr (TYPE == kTypeQ5_K) nib |= ((hv[qq][j] >> (2 * p + h)) & 0x01010101u) << 4;
-                        // f16 1024 + q (exact) for bytes (0, 1) and (2, 3): 0x64 in each high byte
-                        const uint32_t e01 = __byte_perm(nib, 0x00006464u, 0x5140u);
-                        const uint32_t e23 = __byte_perm(nib, 0x00006464u, 0x5342u);
-                        const __half2 w01 = __hfma2(*reinterpret_cast<const __half2*>(&e01), sc2, mn2);
-                        const __half2 w23 = __hfma2(*reinterpret_cast<const __half2*>(&e23), sc2, mn2);
-                        out[2 * j] = *reinterpret_cast<const uint32_t*>(&w01);
-                        out[2 * j + 1] = *reinterpret_cast<const uint32_t*>(&w23);
+                    for (int qq = 0; qq < 2; ++qq) {
+                        // bytes 16 qq .. 16 qq + 15 of pair p; this thread's quants are their
+                        // low (h = 0) or high (h = 1) nibbles: elements 64p + 32h + 16qq + l
+                        const uint4 v0 = qv[2 * p + qq];
+                        const uint32_t wv[4] = {v0.x, v0.y, v0.z, v0.w};
+                        uint32_t out[8];  // 16 f16, element order l = 0..15
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) {
+                            uint32_t nib = (wv[j] >> (4 * h)) & 0x0F0F0F0Fu;
+                            if constexpr (TYPE == kTypeQ5_K) nib |= ((hv[qq][j] >> (2 * p + h)) & 0x01010101u) << 4;
+                            // f16 1024 + q (exact) for bytes (0, 1) and (2, 3): 0x64 in each high byte
+                            const uint32_t e01 = __byte_perm(nib, 0x00006464u, 0x5140u);
+                            const uint32_t e23 = __byte_perm(nib, 0x00006464u, 0x5342u);
+                            const __half2 w01 = __hfma2(*reinterpret_cast<const __half2*>(&e01), sc2, mn2);
+                            const __half2 w23 = __hfma2(*reinterpret_cast<const __half2*>(&e23), sc2, mn2);
+                            out[2 * j] = *reinterpret_cast<const uint32_t*>(&w01);
+                            out[2 * j + 1] = *reinterpret_cast<const uint32_t*>(&w23);
+                        }
+                        // k = 64p + 32h + 16qq + l of the block: TMEM columns 32p + 16h + 8qq .. +7 of A stage i
+                        tmem_st8(trow + acol + static_cast<uint32_t>(32 * p + 8 * qq), out);
                     }
-                    // k = 64p + 32h + 16qq + l of the block: TMEM columns 32p + 16h + 8qq .. +7 of A stage i
-                    tmem_st8(trow + acol + static_cast<uint32_t>(32 * p + 8 * qq), out);
                 }
-            }
-            if (h == 0) {
-                // A_min of this block: the eight 6-bit mins (get_scale_min_k4), twice,
-                // as f16 pairs (k 0..7 meet the sums' hi parts, 8..15 their lo parts)
-                const uint32_t mlo = hdr.z & 0x3F3F3F3Fu;                                                  // m_0..m_3
-                const uint32_t mhi = ((hdr.w >> 4) & 0x0F0F0F0Fu) | (((hdr.z >> 6) & 0x03030303u) << 4);  // m_4..m_7
-                uint32_t mm[4];
-                const uint32_t mq[2] = {mlo, mhi};
+                if (f == 1 && h == 0) {
+                    // A_min of this block: the eight 6-bit mins (get_scale_min_k4), twice,
+                    // as f16 pairs (k 0..7 meet the sums' hi parts, 8..15 their lo parts)
+                    const uint32_t mlo = hdr.z & 0x3F3F3F3Fu;                                                  // m_0..m_3
+                    const uint32_t mhi = ((hdr.w >> 4) & 0x0F0F0F0Fu) | (((hdr.z >> 6) & 0x03030303u) << 4);  // m_4..m_7
+                    uint32_t mm[4];
+                    const uint32_t mq[2] = {mlo, mhi};
 #pragma unroll
-                for (int t = 0; t < 2; ++t) {
-                    const uint32_t e01 = __byte_perm(mq[t], 0x00006464u, 0x5140u);
-                    const uint32_t e23 = __byte_perm(mq[t], 0x00006464u, 0x5342u);
-                    const __half2 m01 = __hsub2(*reinterpret_cast<const __half2*>(&e01), k1024);
-                    const __half2 m23 = __hsub2(*reinterpret_cast<const __half2*>(&e23), k1024);
-                    mm[2 * t] = *reinterpret_cast<const uint32_t*>(&m01);
-                    mm[2 * t + 1] = *reinterpret_cast<const uint32_t*>(&m23);
+                    for (int t = 0; t < 2; ++t) {
+                        const uint32_t e01 = __byte_perm(mq[t], 0x00006464u, 0x5140u);
+                        const uint32_t e23 = __byte_perm(mq[t], 0x00006464u, 0x5342u);
+                        const __half2 m01 = __hsub2(*reinterpret_cast<const __half2*>(&e01), k1024);
+                        const __half2 m23 = __hsub2(*reinterpret_cast<const __half2*>(&e23), k1024);
+                        mm[2 * t] = *reinterpret_cast<const uint32_t*>(&m01);
+                        mm[2 * t + 1] = *reinterpret_cast<const uint32_t*>(&m23);
+                    }
+                    const uint32_t amin[8] = {mm[0], mm[1], mm[2], mm[3], mm[0], mm[1], mm[2], mm[3]};
+                    tmem_st8(trow + mincol0 + static_cast<uint32_t>(8 * i), amin);
                 }
-                const uint32_t amin[8] = {mm[0], mm[1], mm[2], mm[3], mm[0], mm[1], mm[2], mm[3]};
-                tmem_st8(trow + mincol0 + static_cast<uint32_t>(8 * i), amin);
+                // one wait for the half's stores, then its arrival
+                asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&a_full[2 * i + f]);
             }
-            // one wait for the block's stores, then one arrival
-            asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) {
-                mbar_arrive(&a_full[i]);
-                mbar_arrive(&raw_free[rs]);
-            }
+            if (stop) break;
+            if (lane == 0) mbar_arrive(&raw_free[rs]);
         }
     } else {
         // ---------------- epilogue ----------------
@@ -500,11 +530,11 @@ __global__ void __launch_bounds__(kThr, 1) btc_kernel(const __grid_constant__ Bt
         for (int b = 0; b < nblk; ++b) {
             const int i = b & 1, rs = b & (nraw - 1);
             // the block's d, dmin and scales first (they need only the raw slot)
-            if (!mbar_wait(&raw_full[rs], (b >> lgr) & 1, 4u, poisoned)) break;
+            if (!mbar_wait<64>(&raw_full[rs], (b >> lgr) & 1, 4u, poisoned)) break;
             const uint32_t dm = *reinterpret_cast<const uint32_t*>(smem + L.raw_off(rs) + r * BB);
             const float d = f16_bits_to_f32(dm), dmin = f16_bits_to_f32(dm >> 16);
             const float* vs = reinterpret_cast<const float*>(smem + L.v_off(rs)) + n0;  // [2][nv] from vector n0
-            if (!mbar_wait(&acc_full[i], (b >> 1) & 1, 4u, poisoned)) break;
+            if (!mbar_wait<64>(&acc_full[i], (b >> 1) & 1, 4u, poisoned)) break;
             tc_fence_after();
             float mv[16], lv[16], sv[16];
             tmem_ld16x3(trow + static_cast<uint32_t>(accw * i + n0), trow + static_cast<uint32_t>(accw * i + nv + n0),
@@ -554,14 +584,25 @@ __global__ void __launch_bounds__(kThr, 1) btc_kernel(const __grid_constant__ Bt
             }
             asm volatile("bar.sync 1, %0;" ::"n"(kEp * 32) : "memory");
             if (last) {
+                // thread t sums elements t + 256 k (k < nv / 2) over the splits, in
+                // split order, with each split's loads issued together
                 const float* base = P.partial + static_cast<int64_t>(tile) * P.splits * (kMaxNV * kTM);
-                for (int e = threadIdx.x - 32 * kFirstEp; e < nv * kTM; e += kEp * 32) {
-                    const int n = e / kTM, rr = e - n * kTM;
-                    float acc = 0.f;
-                    for (int z = 0; z < P.splits; ++z) acc += __ldcg(base + z * (kMaxNV * kTM) + e);
-                    if (nbase + n < P.N && m0 + rr < P.M)
+                const int t = threadIdx.x - 32 * kFirstEp, per = nv * kTM / (kEp * 32);
+                float acc[kMaxNV * kTM / (kEp * 32)];
+#pragma unroll
+                for (int k = 0; k < kMaxNV * kTM / (kEp * 32); ++k) acc[k] = 0.f;
+                for (int z = 0; z < P.splits; ++z) {
+                    const float* src = base + z * (kMaxNV * kTM) + t;
+#pragma unroll
+                    for (int k = 0; k < kMaxNV * kTM / (kEp * 32); ++k)
+                        if (k < per) acc[k] += __ldcg(src + kEp * 32 * k);
+                }
+#pragma unroll
+                for (int k = 0; k < kMaxNV * kTM / (kEp * 32); ++k) {
+                    const int e = t + kEp * 32 * k, n = e / kTM, rr = e - n * kTM;
+                    if (k < per && nbase + n < P.N && m0 + rr < P.M)
                         *reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(P.y) + (nbase + n) * P.y_nb1 + 4LL * (m0 + rr)) =
-                            acc;
+                            acc[k];
                 }
             }
         }

@@ -370,9 +370,12 @@ const char* check_mulmat_op(const MulMatOp& op) {
 }
 
 // Q4_K / Q5_K with 5 to 64 vectors (and 3 or 4 where the streaming kernel
-// cannot take them) run on the tcgen05 small-batch GEMM.
+// cannot take them) run on the tcgen05 small-batch GEMM, except small
+// weights (at most 4096 x 4096) below 16 vectors, where the mma.sync GEMM's
+// shorter fixed costs win (13.5 against 15.1 us for Q4_K 4096 x 4096 at N = 8).
 bool use_batched_tc(const MulMatOp& o) {
     if (!batched_tc_supported(o) || o.N < 3) return false;
+    if (o.N < 16 && static_cast<int64_t>(o.M) * o.K <= 4096LL * 4096 && batched_supported(o)) return false;
     return o.N >= 5 || !stream_supported(&o, 1);
 }
 
