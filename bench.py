@@ -320,8 +320,9 @@ class DevArray:
 def batched_measure(dev, reps: int = 10, warmup: int = 3):
     """Several sequences decoding together (N = 1 .. 64) on three weights:
     Gemma-2-2B ffn_up (Q8_0 9216x2304), Llama-3-8B ffn_gate (Q4_K 14336x4096)
-    and ffn_down (Q6_K 4096x14336). N = 1, 2 run the streaming GEMV, N >= 3
-    the integer tensor-core batched GEMM. Distinct weight copies (over 2x the
+    and ffn_down (Q6_K 4096x14336). N = 1, 2 run the streaming GEMV; the
+    Q4_K shape at N >= 8 the tcgen05 small-batch GEMM, the others the integer
+    tensor-core (mma.sync) batched GEMM. Distinct weight copies (over 2x the
     L2) rotate between launches so every launch streams its weights from HBM.
     Returns the JSON object: the Q8_0 shape at the top level, the K-quant
     shapes under "kquant"."""
@@ -334,7 +335,6 @@ def batched_measure(dev, reps: int = 10, warmup: int = 3):
               ("llama-3-8b ffn_gate", jsep.GGML_TYPE_Q4_K, 14336, 4096, 8),
               ("llama-3-8b ffn_down", jsep.GGML_TYPE_Q6_K, 4096, 14336, 6)]
     stream_ptr = jsep.library_stream()
-    lib_stream = torch.cuda.ExternalStream(stream_ptr)
     hbm, _ = measured_peaks()
     out = []
     for name, t, M, K, copies in shapes:
@@ -347,19 +347,29 @@ def batched_measure(dev, reps: int = 10, warmup: int = 3):
             y = torch.empty(N, M, device=dev)
             torch.cuda.synchronize()
 
-            def run(i):
+            def run(i, s):
                 w = ws[i % copies]
-                jsep.mul_mat_device(t, w.data_ptr(), w.shape[1], x.data_ptr(), K, y.data_ptr(), M, M, K, N, stream_ptr)
+                jsep.mul_mat_device(t, w.data_ptr(), w.shape[1], x.data_ptr(), K, y.data_ptr(), M, M, K, N, s)
 
+            # one launch per weight copy, captured as one CUDA graph (no host
+            # time between launches), replayed `reps` times
             for i in range(warmup):
-                run(i)
+                run(i, stream_ptr)
+            torch.cuda.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                cs = torch.cuda.current_stream().cuda_stream
+                for i in range(copies):
+                    run(i, cs)
+            graph.replay()
+            torch.cuda.synchronize()
             ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            with torch.cuda.stream(lib_stream):
-                ev0.record()
-                for i in range(reps * copies):
-                    run(i)
-                ev1.record()
+            ev0.record()
+            for _ in range(reps):
+                graph.replay()
+            ev1.record()
             ev1.synchronize()
+            del graph
             us = ev0.elapsed_time(ev1) * 1e3 / (reps * copies)
             nbytes = synth.algorithmic_bytes(t, M, K, N)
             per.append({"n": N, "us": round(us, 2), "gbs": round(nbytes / (us * 1e-6) / 1e9, 1),
@@ -371,7 +381,9 @@ def batched_measure(dev, reps: int = 10, warmup: int = 3):
                     "per_n": per})
     res = dict(out[0])
     res["kquant"] = out[1:]
-    res["note"] = "N <= 2: streaming GEMV; N >= 3: integer tensor-core batched GEMM (x pre-pass included)"
+    res["note"] = ("N <= 2: streaming GEMV; Q4_K N >= 5 (N >= 16 at 4096x4096 and below): tcgen05 small-batch GEMM; "
+                   "other N >= 3: integer tensor-core batched GEMM (mma.sync); activation pre-passes included; "
+                   "launches timed inside a CUDA graph")
     return res
 
 
