@@ -302,36 +302,37 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
                 if (!mbar_wait_drain(&b_full[q % kStages], (q / kStages) & 1)) atomicOr(&g_prefill_error, 16u);
         }
     } else if (warp == 1) {
-        // ---------------- MMA issuer ----------------
-        int committed = 0;  // chunks whose MMAs were committed
-        for (int q = 0; q < nchunk; ++q) {
-            const int s = q % kStages;
-            const uint32_t par = (q / kStages) & 1;
-            int ok = 1;
-            if (lane == 0) ok = mbar_wait(&b_full[s], par, 2u, poisoned) && mbar_wait(&a_full[s], par, 2u, poisoned);
-            ok = __shfl_sync(0xffffffffu, ok, 0);
-            if (!ok) {
-                // a time-out: the MMAs already issued still write TMEM, which is
-                // freed at the end; wait (bounded) for the last commit, which
-                // tracks all of them
-                if (lane == 0 && committed > 0 &&
-                    !mbar_wait_drain(&st_free[(committed - 1) % kStages], ((committed - 1) / kStages) & 1))
-                    atomicOr(&g_prefill_error, 16u);
-                __syncwarp();
-                break;
-            }
-            tc_fence_after();
-            if (lane == 0) {
-                const uint32_t a0 = tmem + static_cast<uint32_t>(kTileN + s * kACols), b0 = smem_u32(B + s * kBBytes);
+        // ---------------- MMA issuer (one thread) ----------------
+        // The loop runs on lane 0 alone, with the B descriptors advanced from
+        // one base: warp-wide broadcasts and syncs around each chunk's waits
+        // cost the issuing thread as much as the chunk's four MMAs take.
+        if (lane == 0) {
+            int committed = 0;  // chunks whose MMAs were committed
+            const uint64_t bdesc0 = umma_desc_sw128(smem_u32(B));  // + (byte offset >> 4)
+            for (int q = 0; q < nchunk; ++q) {
+                const int s = q % kStages;
+                const uint32_t par = (q / kStages) & 1;
+                if (!mbar_wait(&b_full[s], par, 2u, poisoned) || !mbar_wait(&a_full[s], par, 2u, poisoned)) {
+                    // a time-out: the MMAs already issued still write TMEM, which is
+                    // freed at the end; wait (bounded) for the last commit, which
+                    // tracks all of them
+                    if (committed > 0 &&
+                        !mbar_wait_drain(&st_free[(committed - 1) % kStages], ((committed - 1) / kStages) & 1))
+                        atomicOr(&g_prefill_error, 16u);
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t a0 = tmem + static_cast<uint32_t>(kTileN + s * kACols);
+                const uint64_t bd = bdesc0 + static_cast<uint64_t>((s * kBBytes) >> 4);
 #pragma unroll
                 for (int ks = 0; ks < kChunkK / 16; ++ks)  // K = 16 per MMA: 8 TMEM columns of A, 32 bytes of B's row
-                    umma_f16_ts(tmem, a0 + 8 * ks, umma_desc_sw128(b0 + 32 * ks), (q > 0 || ks > 0) ? 1u : 0u);
+                    umma_f16_ts(tmem, a0 + 8 * ks, bd + 2 * ks, (q > 0 || ks > 0) ? 1u : 0u);
                 umma_commit(&st_free[s]);  // the stage is free once these MMAs have read it
                 if (q == nchunk - 1) umma_commit(acc_full);
+                committed = q + 1;
             }
-            committed = q + 1;
-            __syncwarp();
         }
+        __syncwarp();
     } else {
         // ---------------- dequant (then epilogue) ----------------
         const int quarter = warp & 3;  // TMEM lanes this warp may access
