@@ -217,6 +217,7 @@ __device__ __forceinline__ uint4 q6_load16(const uint8_t* rowp, int c, int q4, u
 template <int TYPE>
 __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_constant__ PrefillArgs P) {
     constexpr int kRawBytes = raw_bytes<TYPE>();
+    constexpr bool kOneWait = TYPE != kTypeQ6_K;  // the MMA thread waits on a_full alone
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     // 1024-byte alignment for the swizzled tiles
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -312,7 +313,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
             for (int q = 0; q < nchunk; ++q) {
                 const int s = q % kStages;
                 const uint32_t par = (q / kStages) & 1;
-                if (!mbar_wait(&b_full[s], par, 2u, poisoned) || !mbar_wait(&a_full[s], par, 2u, poisoned)) {
+                if ((!kOneWait && !mbar_wait(&b_full[s], par, 2u, poisoned)) ||
+                    !mbar_wait(&a_full[s], par, 2u, poisoned)) {  // with kOneWait a_full implies b_full
                     // a time-out: the MMAs already issued still write TMEM, which is
                     // freed at the end; wait (bounded) for the last commit, which
                     // tracks all of them
@@ -398,6 +400,10 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
                     tc_fence_before();
                     __syncwarp();
                     if (lane == 0) {
+                        // the first dequant warp also waits for the chunk's B box, so the
+                        // MMA thread needs one barrier per chunk (Q6_K, whose dequant is
+                        // the slower side, leaves that wait to the MMA thread)
+                        if (kOneWait && dw == 0) mbar_wait(&b_full[s], (q / kStages) & 1, 3u, poisoned);
                         mbar_arrive(&a_full[s]);
                         if (p == 3) mbar_arrive(&raw_free[rs]);
                     }
@@ -439,6 +445,10 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
                     tc_fence_before();
                     __syncwarp();
                     if (lane == 0) {
+                        // the first dequant warp also waits for the chunk's B box, so the
+                        // MMA thread needs one barrier per chunk (Q6_K, whose dequant is
+                        // the slower side, leaves that wait to the MMA thread)
+                        if (kOneWait && dw == 0) mbar_wait(&b_full[s], (q / kStages) & 1, 3u, poisoned);
                         mbar_arrive(&a_full[s]);
                         if (p == 3) mbar_arrive(&raw_free[rs]);
                     }
@@ -479,6 +489,10 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
                     tc_fence_before();
                     __syncwarp();
                     if (lane == 0) {
+                        // the first dequant warp also waits for the chunk's B box, so the
+                        // MMA thread needs one barrier per chunk (Q6_K, whose dequant is
+                        // the slower side, leaves that wait to the MMA thread)
+                        if (kOneWait && dw == 0) mbar_wait(&b_full[s], (q / kStages) & 1, 3u, poisoned);
                         mbar_arrive(&a_full[s]);
                         if (p == 3) mbar_arrive(&raw_free[rs]);
                     }
@@ -533,6 +547,10 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
                     tc_fence_before();
                     __syncwarp();
                     if (lane == 0) {
+                        // the first dequant warp also waits for the chunk's B box, so the
+                        // MMA thread needs one barrier per chunk (Q6_K, whose dequant is
+                        // the slower side, leaves that wait to the MMA thread)
+                        if (kOneWait && dw == 0) mbar_wait(&b_full[s], (q / kStages) & 1, 3u, poisoned);
                         mbar_arrive(&a_full[s]);
                         if (p == 3) mbar_arrive(&raw_free[rs]);
                     }
