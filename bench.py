@@ -234,15 +234,37 @@ def fused_glu_measure(dev, layers: int = 12, reps: int = 20):
 def prefill_measure(dev, reps: int = 10, warmup: int = 3):
     """Llama-3-8B prefill GEMMs (N = 512 tokens, Q4_K): each MUL_MAT is the
     f16 pre-pass plus the tcgen05 GEMM. Two weight copies per shape (156 MB,
-    more than L2) alternate between replays. Returns the JSON object."""
+    more than L2) alternate between launches, which are captured in a CUDA
+    graph (no host time between them). Returns the JSON object."""
     import torch
 
     from webllm_b200 import jsep, synth
 
     N = 512
     stream_ptr = jsep.library_stream()
-    lib_stream = torch.cuda.ExternalStream(stream_ptr)
     gen = torch.Generator(device=dev)
+
+    def graph_us(call) -> float:
+        """Mean device time of call(copy, stream) over `reps` launches that
+        alternate the two weight copies, replayed from one CUDA graph."""
+        for w in range(warmup):
+            call(w & 1, stream_ptr)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            cs = torch.cuda.current_stream().cuda_stream
+            for r in range(reps):
+                call(r & 1, cs)
+        g.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        g.replay()
+        e1.record()
+        e1.synchronize()
+        del g
+        return e0.elapsed_time(e1) * 1e3 / reps
+
     shapes, per = [], []
     for name, t, M, K in synth.LLAMA3_8B_PREFILL:
         gen.manual_seed(zlib.crc32(name.encode()))
@@ -252,23 +274,12 @@ def prefill_measure(dev, reps: int = 10, warmup: int = 3):
         shapes.append((name, t, M, K, ws, x, y))
     torch.cuda.synchronize()
 
-    def run(copy: int, only=None):
-        for i, (name, t, M, K, ws, x, y) in enumerate(shapes):
-            if only is None or i == only:
-                jsep.mul_mat_device(t, ws[copy].data_ptr(), ws[copy].shape[1], x.data_ptr(), K, y.data_ptr(), M, M,
-                                    K, N, stream_ptr)
-
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     for i, (name, t, M, K, ws, x, y) in enumerate(shapes):
-        for w in range(warmup):
-            run(w & 1, i)
-        with torch.cuda.stream(lib_stream):
-            ev0.record()
-            for r in range(reps):
-                run(r & 1, i)
-            ev1.record()
-        ev1.synchronize()
-        ms = ev0.elapsed_time(ev1) / reps
+        def run(copy: int, s, t=t, M=M, K=K, ws=ws, x=x, y=y):
+            jsep.mul_mat_device(t, ws[copy].data_ptr(), ws[copy].shape[1], x.data_ptr(), K, y.data_ptr(), M, M, K,
+                                N, s)
+
+        ms = graph_us(run) / 1e3
         per.append({"shape": f"{M}x{K}", "n": N, "us": round(ms * 1e3, 2),
                     "tflops": round(2.0 * M * N * K / (ms * 1e-3) / 1e12, 1)})
     total_flop = sum(2.0 * M * N * K for (_, _, M, K, _, _, _) in shapes)
@@ -286,19 +297,11 @@ def prefill_measure(dev, reps: int = 10, warmup: int = 3):
         ws = [synth.weights_torch(gen, t, M, K, dev) for _ in range(2)]
         torch.cuda.synchronize()
 
-        def one(copy: int):
+        def one(copy: int, s, t=t, ws=ws):
             jsep.mul_mat_device(t, ws[copy].data_ptr(), ws[copy].shape[1], x.data_ptr(), K, y.data_ptr(), M, M, K, N,
-                                stream_ptr)
+                                s)
 
-        for w in range(warmup):
-            one(w & 1)
-        with torch.cuda.stream(lib_stream):
-            ev0.record()
-            for r in range(reps):
-                one(r & 1)
-            ev1.record()
-        ev1.synchronize()
-        ms = ev0.elapsed_time(ev1) / reps
+        ms = graph_us(one) / 1e3
         per_type.append({"type": tname, "shape": f"{M}x{K}", "n": N, "us": round(ms * 1e3, 2),
                          "tflops": round(2.0 * M * N * K / (ms * 1e-3) / 1e12, 1)})
         del ws

@@ -268,9 +268,25 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
             asm volatile("prefetch.tensormap [%0];" ::"l"(&P.wmap) : "memory");
             asm volatile("prefetch.tensormap [%0];" ::"l"(&P.xmap) : "memory");
             int raw_issued = 0, b_issued = 0;  // copies issued (for the drain below)
+            // the weights do not depend on the f16 pre-pass: the first raw slots
+            // go out before the wait for it (programmatic launch)
+            const int pre = min(nchunk >> 2, kRawSlots);
+            for (int kb = 0; kb < pre; ++kb) {
+                mbar_expect_tx(&raw_full[kb], kRawBytes);
+                const int x = TYPE == kTypeQ6_K ? ((kb0 + kb) * 210) & ~15 : (kb0 + kb) * (raw_row_bytes<TYPE>() / 8);
+                if (TYPE == kTypeQ6_K && P.q6_pairs) {
+                    const int xo = ((kb0 + kb) * 210 + P.w_nb1) & ~15;
+                    tma_2d(raw + kb * kRawBytes, &P.wmap, x, m0 / 2, &raw_full[kb]);
+                    tma_2d(raw + kb * kRawBytes + (kTileM / 2) * kQ6Box, &P.wmap, xo, m0 / 2, &raw_full[kb]);
+                } else {
+                    tma_2d(raw + kb * kRawBytes, &P.wmap, x, m0, &raw_full[kb]);
+                }
+                raw_issued = kb + 1;
+            }
+            asm volatile("griddepcontrol.wait;" ::: "memory");
             for (int q = 0; q < nchunk; ++q) {
                 const int kb = q >> 2, c = q & 3;
-                if (c == 0) {
+                if (c == 0 && kb >= pre) {
                     const int r = kb % kRawSlots;
                     if (kb >= kRawSlots && !mbar_wait(&raw_free[r], ((kb / kRawSlots) - 1) & 1, 1u, poisoned)) break;
                     mbar_expect_tx(&raw_full[r], kRawBytes);
@@ -645,15 +661,25 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
 }
 
 // f32 activations [N][K] (vector stride x_nb1 bytes) -> contiguous f16 [N][K].
-__global__ void x_to_f16_kernel(const float* __restrict__ x, int64_t x_nb1, __half* __restrict__ x16, int K, int N) {
-    const int64_t total4 = static_cast<int64_t>(N) * (K / 4);
-    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total4;
-         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-        const int64_t n = i / (K / 4), k4 = i - n * (K / 4);
-        const float4 v = *reinterpret_cast<const float4*>(reinterpret_cast<const uint8_t*>(x) + n * x_nb1 + 16 * k4);
-        __half2* o = reinterpret_cast<__half2*>(x16 + n * K + 4 * k4);
-        o[0] = __floats2half2_rn(v.x, v.y);
-        o[1] = __floats2half2_rn(v.z, v.w);
+// Vectors blockIdx.y, blockIdx.y + gridDim.y, ..., elements 4 (blockIdx.x
+// blockDim.x + t) .. +3 (and their grid-stride successors). CTA (0, 0) also zeroes the split-K tile counters.
+// The GEMM that follows may start at once: its prologue and first weight
+// boxes overlap this kernel, and it waits for the f16 image with
+// griddepcontrol.wait.
+__global__ void x_to_f16_kernel(const float* __restrict__ x, int64_t x_nb1, __half* __restrict__ x16, int K, int N,
+                                unsigned* __restrict__ counters, int ncounters) {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    if (blockIdx.x == 0 && blockIdx.y == 0)
+        for (int t = threadIdx.x; t < ncounters; t += blockDim.x) counters[t] = 0u;
+    const int k4n = K / 4;
+    for (int n = blockIdx.y; n < N; n += gridDim.y) {
+        const float4* xr = reinterpret_cast<const float4*>(reinterpret_cast<const uint8_t*>(x) + n * x_nb1);
+        __half2* orow = reinterpret_cast<__half2*>(x16 + static_cast<int64_t>(n) * K);
+        for (int k4 = blockIdx.x * blockDim.x + threadIdx.x; k4 < k4n; k4 += gridDim.x * blockDim.x) {
+            const float4 v = xr[k4];
+            orow[2 * k4] = __floats2half2_rn(v.x, v.y);
+            orow[2 * k4 + 1] = __floats2half2_rn(v.z, v.w);
+        }
     }
 }
 
@@ -754,15 +780,6 @@ int launch_prefill(const MulMatOp& o, void* workspace, size_t workspace_bytes, c
     if (x16_bytes(o) + split_bytes(o, splits) > workspace_bytes) splits = 1;
     const int nblk = o.K / 256, kb_split = (nblk + splits - 1) / splits;
     __half* x16 = static_cast<__half*>(workspace);
-    {
-        const int64_t total4 = static_cast<int64_t>(o.N) * (o.K / 4);
-        const int threads = 256;
-        const int64_t want = (total4 + threads - 1) / threads;
-        const int blocks = static_cast<int>(want < 4096 ? want : 4096);
-        x_to_f16_kernel<<<blocks, threads, 0, stream>>>(o.x, o.x_nb1, x16, o.K, o.N);
-        const cudaError_t e = cudaGetLastError();
-        if (e != cudaSuccess) return -static_cast<int>(e);
-    }
     PrefillArgs P{};
     const EncodeFn enc = encoder();
     const bool q6 = o.type == kTypeQ6_K;
@@ -806,11 +823,18 @@ int launch_prefill(const MulMatOp& o, void* workspace, size_t workspace_bytes, c
     P.splits = splits;
     P.kb_split = kb_split;
     int launched = 2;
+    size_t tiles = 0;
     if (splits > 1) {
-        const size_t tiles = static_cast<size_t>((o.M + kTileM - 1) / kTileM) * ((o.N + kTileN - 1) / kTileN);
+        tiles = static_cast<size_t>((o.M + kTileM - 1) / kTileM) * ((o.N + kTileN - 1) / kTileN);
         P.partial = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + x16_bytes(o));
         P.counters = reinterpret_cast<unsigned*>(P.partial + tiles * splits * kTileM * kTileN);
-        const cudaError_t e = cudaMemsetAsync(P.counters, 0, tiles * 4, stream);
+    }
+    {
+        // the f16 activation image (and the split counters), then the GEMM
+        const int threads = 256, per_row = (o.K / 4 + threads - 1) / threads;
+        x_to_f16_kernel<<<dim3(per_row, o.N < 65535 ? o.N : 65535), threads, 0, stream>>>(o.x, o.x_nb1, x16, o.K, o.N, P.counters,
+                                                                    static_cast<int>(tiles));
+        const cudaError_t e = cudaGetLastError();
         if (e != cudaSuccess) return -static_cast<int>(e);
     }
     // the attribute is per device: one flag per device ordinal and kernel
@@ -832,9 +856,18 @@ int launch_prefill(const MulMatOp& o, void* workspace, size_t workspace_bytes, c
         if (e != cudaSuccess) return -static_cast<int>(e);
         configured[dev][ti] = true;
     }
-    const dim3 grid((o.M + kTileM - 1) / kTileM, (o.N + kTileN - 1) / kTileN, splits);
-    kernel<<<grid, kThreads, smem, stream>>>(P);
-    const cudaError_t e = cudaGetLastError();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((o.M + kTileM - 1) / kTileM, (o.N + kTileN - 1) / kTileN, splits);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, P);
+    if (e == cudaSuccess) e = cudaGetLastError();
     return e == cudaSuccess ? launched : -static_cast<int>(e);
 }
 
