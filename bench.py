@@ -292,7 +292,7 @@ def prefill_measure(dev, reps: int = 10, warmup: int = 3):
     y = torch.empty(N, M, device=dev)
     per_type = []
     for tname, t in (("q4_k", jsep.GGML_TYPE_Q4_K), ("q5_k", jsep.GGML_TYPE_Q5_K), ("q6_k", jsep.GGML_TYPE_Q6_K),
-                     ("q8_0", jsep.GGML_TYPE_Q8_0), ("q4_0", jsep.GGML_TYPE_Q4_0)):
+                     ("q8_0", jsep.GGML_TYPE_Q8_0), ("q4_0", jsep.GGML_TYPE_Q4_0), ("iq4_xs", jsep.GGML_TYPE_IQ4_XS)):
         gen.manual_seed(zlib.crc32(tname.encode()))
         ws = [synth.weights_torch(gen, t, M, K, dev) for _ in range(2)]
         torch.cuda.synchronize()

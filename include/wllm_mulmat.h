@@ -270,8 +270,9 @@ int32_t wllm_graph_launch(int32_t graph);
 int32_t wllm_graph_destroy(int32_t graph);
 
 /* Prefill MUL_MAT that allocates nothing: the same arguments and result as
- * wllm_mul_mat for the prefill path (Q4_K, Q5_K, Q8_0 or Q4_0 weights, or Q6_K with
- * rows of a multiple of 16 bytes, or of 8 with M even; N >= 65 vectors, 16-byte
+ * wllm_mul_mat for the prefill path (Q4_K, Q5_K, Q8_0 or Q4_0 weights, IQ4_XS with
+ * K a multiple of 512, or Q6_K with rows of a multiple of 16 bytes, or of 8 with M
+ * even; N >= 65 vectors, 16-byte
  * aligned weights and activations), with the f16 activation workspace
  * in a fixed 16 MiB device array of the library instead of library-allocated
  * memory: N * K * 2 + 256 bytes must fit, otherwise WLLM_STATUS_FAILED with
@@ -288,7 +289,7 @@ int32_t wllm_mul_mat_prefill_static(int32_t src0_type, const void* w, int64_t w_
 /* Device dequantization of n elements (n a multiple of the block size) of
  * raw GGUF blocks to f32. Replaces the libllama oracle shim
  * webllm_dequantize_q4_K (webgpu-bridge.cpp:692-708) on the device, for
- * Q4_K, Q5_K, Q6_K, Q4_0 and Q8_0. Returns -1 on bad arguments. */
+ * Q4_K, Q5_K, Q6_K, Q4_0, Q8_0 and IQ4_XS. Returns -1 on bad arguments. */
 int32_t wllm_dequantize(int32_t type, const void* src, float* dst, int64_t n, void* stream);
 
 /* Library build/version string. */

@@ -154,6 +154,8 @@ def test_prefill_q6k_shapes_vs_torch_fp32(runtime, M, K, N):
     (O.TYPE_Q8_0, 333, 2304, 300),    # Gemma-2-2B hidden: 9 groups; partial tiles
     (O.TYPE_Q4_0, 128, 256, 65),
     (O.TYPE_Q4_0, 260, 2304, 200),
+    (O.TYPE_IQ4_XS, 128, 512, 65),    # two 136-byte blocks: offsets 0 and 8 in their boxes
+    (O.TYPE_IQ4_XS, 200, 2048, 130),  # partial tiles
 ])
 def test_prefill_other_types_matches_oracle(runtime, qtype, M, K, N):
     rng = np.random.default_rng(3000 + qtype + M + K + N)
@@ -167,7 +169,8 @@ def test_prefill_other_types_matches_oracle(runtime, qtype, M, K, N):
 
 @pytest.mark.parametrize("qtype,M,K,N", [(O.TYPE_Q8_0, 9216, 2304, 512), (O.TYPE_Q8_0, 2304, 9216, 256),
                                          (O.TYPE_Q5_K, 14336, 4096, 512), (O.TYPE_Q5_K, 4096, 14336, 200),
-                                         (O.TYPE_Q4_0, 14336, 4096, 512), (O.TYPE_Q4_0, 4096, 14336, 128)])
+                                         (O.TYPE_Q4_0, 14336, 4096, 512), (O.TYPE_Q4_0, 4096, 14336, 128),
+                                         (O.TYPE_IQ4_XS, 14336, 4096, 512), (O.TYPE_IQ4_XS, 4096, 14336, 200)])
 def test_prefill_other_types_shapes_vs_torch_fp32(runtime, qtype, M, K, N):
     """Gemma-2-2B ffn_up / ffn_down (Q8_0) and Llama-3-8B ffn_gate / ffn_down
     (Q5_K, Q4_0) in prefill."""

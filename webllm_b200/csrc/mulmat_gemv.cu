@@ -394,7 +394,7 @@ size_t mulmat_workspace_bytes(const MulMatOp* ops, int n_ops) {
 int launch_mulmat(const MulMatOp* ops, int n_ops, cudaStream_t stream, int num_sms, void* workspace,
                   size_t workspace_bytes) {
     if (n_ops < 1 || n_ops > kMaxOpsPerLaunch) return -static_cast<int>(cudaErrorInvalidValue);
-    // prefill-sized ops (Q4_K, Q5_K, Q8_0, Q4_0, or Q6_K rows the TMA can copy; N >= 65) and small batches (N >= 5, or 3-4 where
+    // prefill-sized ops (Q4_K, Q5_K, Q8_0, Q4_0, IQ4_XS, or Q6_K rows the TMA can copy; N >= 65) and small batches (N >= 5, or 3-4 where
     // the streaming kernel cannot take them) run as tensor-core GEMMs, one
     // launch each; the rest together
     int launched = 0;

@@ -214,10 +214,20 @@ __device__ __forceinline__ uint4 q6_load16(const uint8_t* rowp, int c, int q4, u
                       __funnelshift_r(v[3], v[4], sh));
 }
 
+// The weight box's x coordinate for K block kb: Q6_K (210 B) and IQ4_XS
+// (136 B) blocks are mapped in bytes, from the block's start rounded down to
+// 16; the others in uint64 words, block-aligned.
+template <int TYPE>
+__device__ __forceinline__ int byte_box_x(int kb) {
+    if constexpr (TYPE == kTypeQ6_K) return (kb * 210) & ~15;
+    if constexpr (TYPE == kTypeIQ4_XS) return (kb * 136) & ~15;
+    return kb * (raw_row_bytes<TYPE>() / 8);
+}
+
 template <int TYPE>
 __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_constant__ PrefillArgs P) {
     constexpr int kRawBytes = raw_bytes<TYPE>();
-    constexpr bool kOneWait = TYPE != kTypeQ6_K;  // the MMA thread waits on a_full alone
+    constexpr bool kOneWait = TYPE != kTypeQ6_K && TYPE != kTypeIQ4_XS;  // the MMA thread waits on a_full alone
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     // 1024-byte alignment for the swizzled tiles
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -273,7 +283,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
             const int pre = min(nchunk >> 2, kRawSlots);
             for (int kb = 0; kb < pre; ++kb) {
                 mbar_expect_tx(&raw_full[kb], kRawBytes);
-                const int x = TYPE == kTypeQ6_K ? ((kb0 + kb) * 210) & ~15 : (kb0 + kb) * (raw_row_bytes<TYPE>() / 8);
+                const int x = byte_box_x<TYPE>(kb0 + kb);
                 if (TYPE == kTypeQ6_K && P.q6_pairs) {
                     const int xo = ((kb0 + kb) * 210 + P.w_nb1) & ~15;
                     tma_2d(raw + kb * kRawBytes, &P.wmap, x, m0 / 2, &raw_full[kb]);
@@ -292,7 +302,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
                     mbar_expect_tx(&raw_full[r], kRawBytes);
                     // x: uint64 words per 256 elements (Q4_K 18, Q5_K 22, Q8_0 34);
                     // Q6_K in bytes, the block's start rounded down to 16
-                    const int x = TYPE == kTypeQ6_K ? ((kb0 + kb) * 210) & ~15 : (kb0 + kb) * (raw_row_bytes<TYPE>() / 8);
+                    const int x = byte_box_x<TYPE>(kb0 + kb);
                     if (TYPE == kTypeQ6_K && P.q6_pairs) {
                         const int xo = ((kb0 + kb) * 210 + P.w_nb1) & ~15;
                         tma_2d(raw + r * kRawBytes, &P.wmap, x, m0 / 2, &raw_full[r]);
@@ -420,6 +430,53 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
                         // MMA thread needs one barrier per chunk (Q6_K, whose dequant is
                         // the slower side, leaves that wait to the MMA thread)
                         if (kOneWait && dw == 0) mbar_wait(&b_full[s], (q / kStages) & 1, 3u, poisoned);
+                        mbar_arrive(&a_full[s]);
+                        if (p == 3) mbar_arrive(&raw_free[rs]);
+                    }
+                }
+            } else if constexpr (TYPE == kTypeIQ4_XS) {
+                // IQ4_XS (136 B: f16 d, u16 scales_h, 4 B of 4-bit scales_l, 128 B of
+                // level indices): element 64p + 32h + 16qq + l of the block is sub-block
+                // j = 2p + h, nibble qq of index byte 8 + 16j + l; w = d (ls_j - 32)
+                // level. The block starts o = 136 kb mod 16 (0 or 8) bytes into its
+                // 144-byte box row. The level enters as f16 1024 + (level + 128)
+                // (an unsigned byte), minus 1152: the level exactly, times the f16
+                // d (ls - 32).
+                const uint8_t* rowp = raw + rs * kRawBytes + r * 144;
+                const int o = ((kb0 + kb) * 136) & 15;
+                const float d = __half2float(*reinterpret_cast<const __half*>(rowp + o));
+                const uint32_t shb = *reinterpret_cast<const uint16_t*>(rowp + o + 2);
+                const uint32_t slb = *reinterpret_cast<const uint32_t*>(rowp + o + 4);
+                const int c8 = (o + 8) & 16, q48 = ((o + 8) & 15) >> 2;  // the indices start o + 8 bytes in
+                const __half2 k1152 = __float2half2_rn(1152.f);
+#pragma unroll
+                for (int p = 0; p < 4; ++p, ++q) {
+                    const int s = q % kStages;
+                    if (q >= kStages && !mbar_wait(&st_free[s], ((q / kStages) - 1) & 1, 3u, poisoned)) {
+                        stop = true;
+                        break;
+                    }
+                    const int j = 2 * p + h;
+                    const __half2 ds2 = __float2half2_rn(d * static_cast<float>(iq4xs_scale(shb, slb, j)));
+                    const uint4 v = q6_load16(rowp, 16 * j + c8, q48, 0u);
+                    const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
+                    uint32_t out[8];  // 16 f16, element order l = 0..15
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const uint32_t u = iq4_lut4((wv[i] >> (4 * qq)) & 0x0F0F0F0Fu) ^ 0x80808080u;  // level + 128
+                        const uint32_t e01 = __byte_perm(u, 0x00006464u, 0x5140u);
+                        const uint32_t e23 = __byte_perm(u, 0x00006464u, 0x5342u);
+                        const __half2 q01 = __hsub2(*reinterpret_cast<const __half2*>(&e01), k1152);
+                        const __half2 q23 = __hsub2(*reinterpret_cast<const __half2*>(&e23), k1152);
+                        const __half2 w01 = __hmul2(q01, ds2), w23 = __hmul2(q23, ds2);
+                        out[2 * i] = *reinterpret_cast<const uint32_t*>(&w01);
+                        out[2 * i + 1] = *reinterpret_cast<const uint32_t*>(&w23);
+                    }
+                    tmem_st8(trow + static_cast<uint32_t>(kTileN + s * kACols + 16 * h + 8 * qq), out);
+                    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) {
                         mbar_arrive(&a_full[s]);
                         if (p == 3) mbar_arrive(&raw_free[rs]);
                     }
@@ -738,7 +795,8 @@ bool q6_row_pairs(const MulMatOp& o) {
 
 // Bytes of 256 elements of a row: Q4_K 144, Q5_K 176, Q6_K 210, Q8_0 272, Q4_0 144.
 int block_group_bytes(int type) {
-    return type == kTypeQ6_K ? 210 : (type == kTypeQ5_K ? 176 : (type == kTypeQ8_0 ? 272 : 144));
+    return type == kTypeQ6_K ? 210
+                             : (type == kTypeQ5_K ? 176 : (type == kTypeQ8_0 ? 272 : (type == kTypeIQ4_XS ? 136 : 144)));
 }
 
 size_t x16_bytes(const MulMatOp& o) { return (static_cast<size_t>(o.N) * o.K * 2 + 255) & ~size_t(255); }
@@ -752,7 +810,7 @@ size_t split_bytes(const MulMatOp& o, int splits) {
 
 bool prefill_supported(const MulMatOp& o) {
     if ((o.type != kTypeQ4_K && o.type != kTypeQ5_K && o.type != kTypeQ6_K && o.type != kTypeQ8_0 &&
-         o.type != kTypeQ4_0) ||
+         o.type != kTypeQ4_0 && o.type != kTypeIQ4_XS) ||
         o.N < kPrefillMinN || o.ne2 != 1 || o.ne3 != 1)
         return false;
     if (o.K % 256 != 0 || o.M < 1) return false;
@@ -764,6 +822,7 @@ bool prefill_supported(const MulMatOp& o) {
     if ((reinterpret_cast<uintptr_t>(o.w) & 15) || ((o.w_nb1 & 15) && !pairs)) return false;
     if (o.w_nb1 < row_bytes) return false;
     if (o.type == kTypeQ6_K && row_bytes < kQ6Box) return false;  // the box stays within a row's width
+    if (o.type == kTypeIQ4_XS && row_bytes < 144) return false;
     if ((reinterpret_cast<uintptr_t>(o.x) | static_cast<uintptr_t>(o.x_nb1)) & 15) return false;  // float4 reads
     return encoder() != nullptr;
 }
@@ -782,25 +841,25 @@ int launch_prefill(const MulMatOp& o, void* workspace, size_t workspace_bytes, c
     __half* x16 = static_cast<__half*>(workspace);
     PrefillArgs P{};
     const EncodeFn enc = encoder();
-    const bool q6 = o.type == kTypeQ6_K;
+    const bool q6 = o.type == kTypeQ6_K, iq4 = o.type == kTypeIQ4_XS, bytemap = q6 || iq4;
     {
         // Q4_K / Q5_K / Q8_0 / Q4_0: uint64 words, one 256-element column per
-        // box (18 / 22 / 34 / 18 words); Q6_K: bytes, a
-        // 240-byte box from the block's 16-byte-rounded start (the box's end may
+        // box (18 / 22 / 34 / 18 words); Q6_K and IQ4_XS: bytes, a 240- or
+        // 144-byte box from the block's 16-byte-rounded start (the box's end may
         // pass the row's last block: zeros, never read)
         const cuuint64_t group = static_cast<cuuint64_t>(block_group_bytes(o.type));
         const bool pairs = q6_row_pairs(o);
         // row pairs: [M / 2][2 w_nb1 bytes], the odd row's bytes from w_nb1 on
         const cuuint64_t dims[2] = {pairs ? 2 * static_cast<cuuint64_t>(o.w_nb1)
-                                          : static_cast<cuuint64_t>(o.K / 256) * (q6 ? group : group / 8),
+                                          : static_cast<cuuint64_t>(o.K / 256) * (bytemap ? group : group / 8),
                                     static_cast<cuuint64_t>(pairs ? o.M / 2 : o.M)};
         const cuuint64_t strides[1] = {static_cast<cuuint64_t>(pairs ? 2 * o.w_nb1 : o.w_nb1)};
-        const cuuint32_t box[2] = {q6 ? static_cast<cuuint32_t>(kQ6Box) : static_cast<cuuint32_t>(group / 8),
+        const cuuint32_t box[2] = {q6 ? static_cast<cuuint32_t>(kQ6Box) : (iq4 ? 144u : static_cast<cuuint32_t>(group / 8)),
                                    pairs ? kTileM / 2u : static_cast<cuuint32_t>(kTileM)};
         P.q6_pairs = pairs ? 1 : 0;
         P.w_nb1 = static_cast<int32_t>(o.w_nb1);
         const cuuint32_t es[2] = {1, 1};
-        if (enc(&P.wmap, q6 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, const_cast<uint8_t*>(o.w),
+        if (enc(&P.wmap, bytemap ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, const_cast<uint8_t*>(o.w),
                 dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
             return -static_cast<int>(cudaErrorInvalidValue);
@@ -838,16 +897,21 @@ int launch_prefill(const MulMatOp& o, void* workspace, size_t workspace_bytes, c
         if (e != cudaSuccess) return -static_cast<int>(e);
     }
     // the attribute is per device: one flag per device ordinal and kernel
-    static bool configured[kMaxDevices][5] = {};
+    static bool configured[kMaxDevices][6] = {};
     int dev = 0;
     if (const cudaError_t e = cudaGetDevice(&dev); e != cudaSuccess) return -static_cast<int>(e);
     if (dev < 0 || dev >= kMaxDevices) return -static_cast<int>(cudaErrorInvalidDevice);
-    const int ti = o.type == kTypeQ4_K ? 0 : (o.type == kTypeQ5_K ? 1 : (q6 ? 2 : (o.type == kTypeQ8_0 ? 3 : 4)));
-    void (*const kernels[5])(PrefillArgs) = {prefill_kernel<kTypeQ4_K>, prefill_kernel<kTypeQ5_K>,
+    const int ti = o.type == kTypeQ4_K    ? 0
+                   : o.type == kTypeQ5_K  ? 1
+                   : q6                   ? 2
+                   : o.type == kTypeQ8_0  ? 3
+                   : o.type == kTypeQ4_0  ? 4
+                                          : 5;
+    void (*const kernels[6])(PrefillArgs) = {prefill_kernel<kTypeQ4_K>, prefill_kernel<kTypeQ5_K>,
                                              prefill_kernel<kTypeQ6_K>, prefill_kernel<kTypeQ8_0>,
-                                             prefill_kernel<kTypeQ4_0>};
-    const size_t smems[5] = {smem_bytes<kTypeQ4_K>(), smem_bytes<kTypeQ5_K>(), smem_bytes<kTypeQ6_K>(),
-                             smem_bytes<kTypeQ8_0>(), smem_bytes<kTypeQ4_0>()};
+                                             prefill_kernel<kTypeQ4_0>, prefill_kernel<kTypeIQ4_XS>};
+    const size_t smems[6] = {smem_bytes<kTypeQ4_K>(), smem_bytes<kTypeQ5_K>(), smem_bytes<kTypeQ6_K>(),
+                             smem_bytes<kTypeQ8_0>(), smem_bytes<kTypeQ4_0>(), smem_bytes<kTypeIQ4_XS>()};
     void (*const kernel)(PrefillArgs) = kernels[ti];
     const size_t smem = smems[ti];
     if (!configured[dev][ti]) {

@@ -669,20 +669,6 @@ __device__ __forceinline__ void q6k_item(const uint8_t* pg, const uint8_t* ph, u
     yh = fmaf(dh, fmaf(fmaf(static_cast<float>(a3), 0.0078125f, static_cast<float>(a2) * lf), xf, mf * sh), yh);
 }
 
-// Four IQ4_XS level indices (0..15, one per byte) -> their int8 levels. A
-// byte permute picks from the table's low half (levels 0-7) and another from
-// its high half, by the index's low 3 bits (__byte_perm reads 3 bits per
-// selector nibble); bit 3 of each index, spread over its byte, selects between
-// the two.
-__device__ __forceinline__ uint32_t iq4_lut4(uint32_t idx) {
-    const uint32_t y = idx | (idx >> 4);
-    const uint32_t sel = __byte_perm(y, 0u, 0x4420u) & 0x7777u;  // i0 | i1 << 4 | i2 << 8 | i3 << 12, low 3 bits
-    const uint32_t lo = __byte_perm(kIq4Lv0, kIq4Lv1, sel);
-    const uint32_t hi = __byte_perm(kIq4Lv2, kIq4Lv3, sel);
-    const uint32_t hsel = ((idx >> 3) & 0x01010101u) * 0xFFu;  // 0xFF where the index is 8..15
-    return (hi & hsel) | (lo & ~hsel);
-}
-
 // One IQ4_XS item: 16 rows x one 136-byte block (256 elements), for NP = 1 or
 // 2 vectors. Sub-block j (32 elements) is one MMA on the int8 levels: lane
 // (g, c)'s A fragment for rows g / g+8 is the low nibbles of qs[16j + 4c ..

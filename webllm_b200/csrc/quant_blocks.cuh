@@ -125,6 +125,20 @@ __device__ __forceinline__ int iq4_level(uint32_t i) {
     return static_cast<int8_t>(w & 0xFFu);
 }
 
+// Four IQ4_XS level indices (0..15, one per byte) -> their int8 levels. A
+// byte permute picks from the table's low half (levels 0-7) and another from
+// its high half, by the index's low 3 bits (__byte_perm reads 3 bits per
+// selector nibble); bit 3 of each index, spread over its byte, selects between
+// the two.
+__device__ __forceinline__ uint32_t iq4_lut4(uint32_t idx) {
+    const uint32_t y = idx | (idx >> 4);
+    const uint32_t sel = __byte_perm(y, 0u, 0x4420u) & 0x7777u;  // i0 | i1 << 4 | i2 << 8 | i3 << 12, low 3 bits
+    const uint32_t lo = __byte_perm(kIq4Lv0, kIq4Lv1, sel);
+    const uint32_t hi = __byte_perm(kIq4Lv2, kIq4Lv3, sel);
+    const uint32_t hsel = ((idx >> 3) & 0x01010101u) * 0xFFu;  // 0xFF where the index is 8..15
+    return (hi & hsel) | (lo & ~hsel);
+}
+
 // The 6-bit scale (ls - 32, -32..31) of sub-block j (0..7) of an IQ4_XS block.
 __device__ __forceinline__ int iq4xs_scale(uint32_t scales_h, uint32_t scales_l4, int j) {
     const uint32_t lo = (scales_l4 >> (4 * j)) & 0xFu;  // scales_l[j/2] >> 4(j%2), the four bytes as one word
