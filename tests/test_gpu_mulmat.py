@@ -754,3 +754,32 @@ def test_iq4_xs_through_the_descriptor_seam_vs_oracle(runtime):
         got = run_mul_mat(runtime, t, w, x)
         r = O.mul_mat_f64(t, w, x)
         assert O.rel_error(got, r) <= GEMV_TOL and O.rel_error_elem(got, r) <= GEMV_TOL, (M, K, N)
+
+
+@pytest.mark.parametrize("N", [3, 5, 8, 16, 33, 64])
+@pytest.mark.parametrize("M,K", [(4096, 4096), (1000, 2304), (12288, 4096), (4096, 14336), (33, 256)])
+def test_iq4_xs_batched_vs_torch_fp64(runtime, M, K, N):
+    """IQ4_XS at 3-64 vectors on the integer tensor-core batched GEMM (levels
+    as s8 A fragments, ls - 32 per sub-block; K = 2304's 8-byte aligned rows
+    through the 16-byte copy window; N = 3 with K = 14336, which the streaming
+    kernel leaves to it), against a float64 matmul of the device-dequantized
+    weights, both metrics."""
+    import torch
+
+    dev = torch.device("cuda", 0)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(23 * 2000 + M + K + N)
+    t = jsep.GGML_TYPE_IQ4_XS
+    w = synth.weights_torch(gen, t, M, K, dev)
+    x = torch.randn(N, K, device=dev, generator=gen)
+    y = torch.full((N, M), float("nan"), device=dev)
+    torch.cuda.synchronize()
+    stream = jsep.library_stream()
+    assert jsep.mul_mat_device(t, w.data_ptr(), w.shape[1], x.data_ptr(), K, y.data_ptr(), M, M, K, N,
+                               stream) == jsep.STATUS_OK
+    wf = torch.empty(M, K, device=dev)
+    jsep.dequantize_device(t, w.data_ptr(), wf.data_ptr(), M * K, stream)
+    runtime.jsep_sync()
+    ref = (wf.double() @ x.double().t()).t().cpu().numpy()
+    got = y.double().cpu().numpy()
+    assert O.rel_error(got, ref) <= GEMV_TOL and O.rel_error_elem(got, ref) <= GEMV_TOL

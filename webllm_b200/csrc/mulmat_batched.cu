@@ -71,7 +71,8 @@ __device__ unsigned g_tile_counters[kSlotsB];
 // Shared-memory bytes of one row's chunk (16-byte pieces copied): Q8_0 8 x 34
 // = 272; Q4_0 8 x 18 = 144; Q4_K one 144-byte block; Q5_K one 176-byte block;
 // Q6_K one 210-byte block at any even offset in a 240-byte window (60 words:
-// the 8 rows a warp reads hit 8 bank groups).
+// the 8 rows a warp reads hit 8 bank groups); IQ4_XS one 136-byte block at
+// offset 0 or 8 of a 144-byte window.
 template <int TYPE>
 __host__ __device__ constexpr int row_stride() {
     return TYPE == kTypeQ8_0 ? 272 : (TYPE == kTypeQ6_K ? 240 : (TYPE == kTypeQ5_K ? 176 : 144));
@@ -79,6 +80,10 @@ __host__ __device__ constexpr int row_stride() {
 template <int TYPE>
 __host__ __device__ constexpr int row_pieces() {  // 16-byte pieces copied per row (Q6_K: 14 cover any offset)
     return TYPE == kTypeQ8_0 ? 17 : (TYPE == kTypeQ6_K ? 14 : (TYPE == kTypeQ5_K ? 11 : 9));
+}
+template <int TYPE>
+__host__ __device__ constexpr int window_block() {  // blocks copied through a 16-byte window: their bytes
+    return TYPE == kTypeQ6_K ? 210 : (TYPE == kTypeIQ4_XS ? 136 : 0);
 }
 template <int TYPE>
 __host__ __device__ constexpr int sum_floats() {  // x sub-block sums per vector and chunk (the mins)
@@ -346,11 +351,12 @@ __global__ void __launch_bounds__(kThreadsB, 2) batched_kernel(const __grid_cons
             } else if (TYPE == kTypeQ5_K) {
                 src = row + (k0 / 256) * 176 + 16 * pc;
             } else {
-                // the 16-byte pieces that meet the 210-byte block (none past the
-                // 16-byte boundary after its last byte)
-                const uintptr_t a = reinterpret_cast<uintptr_t>(row + (k0 / 256) * 210);
+                // Q6_K / IQ4_XS: the 16-byte pieces that meet the block (none past
+                // the 16-byte boundary after its last byte)
+                constexpr int WB = window_block<TYPE>();
+                const uintptr_t a = reinterpret_cast<uintptr_t>(row + (k0 / 256) * WB);
                 const uintptr_t ga = a & ~uintptr_t(15);
-                ok = ok && ga + 16 * pc < a + 210;
+                ok = ok && ga + 16 * pc < a + WB;
                 src = reinterpret_cast<const uint8_t*>(ga + 16 * pc);
             }
             cp_async16(sw + r * RS + 16 * pc, ok ? src : P.w, ok);
@@ -544,6 +550,45 @@ __global__ void __launch_bounds__(kThreadsB, 2) batched_kernel(const __grid_cons
                     acc[o][2 + e] += fmaf(dh * af[o][2 + e], f, -oh);
                 }
             }
+        } else if (TYPE == kTypeIQ4_XS) {
+            // IQ4_XS: sub-block j's A fragment for rows g / g+8 is the levels of the
+            // low nibbles of index bytes 16j + 4c .. + 3 (k = 4c ..) and of their high
+            // nibbles (k = 16 + 4c ..); times ls_j - 32 in f32, then d / s per block
+            const uintptr_t boff = static_cast<uintptr_t>((ch0 + ch) * 136);
+            const uint8_t* pg = rg + ((rowg_addr + boff) & 15);
+            const uint8_t* ph = rh + ((rowh_addr + boff) & 15);
+            const uint32_t shg = *reinterpret_cast<const uint16_t*>(pg + 2), slg = *reinterpret_cast<const uint32_t*>(pg + 4);
+            const uint32_t shh = *reinterpret_cast<const uint16_t*>(ph + 2), slh = *reinterpret_cast<const uint32_t*>(ph + 4);
+            float af[NO][4];  // the block's scaled sub-block sums
+#pragma unroll
+            for (int o = 0; o < NO; ++o) af[o][0] = af[o][1] = af[o][2] = af[o][3] = 0.f;
+#pragma unroll 2
+            for (int j = 0; j < 8; ++j) {
+                const uint32_t wg = *reinterpret_cast<const uint32_t*>(pg + 8 + 16 * j + 4 * c);
+                const uint32_t wh = *reinterpret_cast<const uint32_t*>(ph + 8 + 16 * j + 4 * c);
+                const uint32_t A0 = iq4_lut4(wg & 0x0F0F0F0Fu), A1 = iq4_lut4(wh & 0x0F0F0F0Fu);
+                const uint32_t A2 = iq4_lut4((wg >> 4) & 0x0F0F0F0Fu), A3 = iq4_lut4((wh >> 4) & 0x0F0F0F0Fu);
+                const float scj = static_cast<float>(iq4xs_scale(shg, slg, j));
+                const float shj = static_cast<float>(iq4xs_scale(shh, slh, j));
+#pragma unroll
+                for (int o = 0; o < NO; ++o) {
+                    float v[4];
+                    mma_limbs<false>(v, A0, A1, A2, A3, xb01 + o * OCT + 32 * j, xb2 + o * OCT + 32 * j);
+                    af[o][0] = fmaf(scj, v[0], af[o][0]);
+                    af[o][1] = fmaf(scj, v[1], af[o][1]);
+                    af[o][2] = fmaf(shj, v[2], af[o][2]);
+                    af[o][3] = fmaf(shj, v[3], af[o][3]);
+                }
+            }
+            const float dg = f16_bits_to_f32(*reinterpret_cast<const uint16_t*>(pg));
+            const float dh = f16_bits_to_f32(*reinterpret_cast<const uint16_t*>(ph));
+#pragma unroll
+            for (int o = 0; o < NO; ++o) {
+                acc[o][0] = fmaf(dg * af[o][0], is[o][0], acc[o][0]);
+                acc[o][1] = fmaf(dg * af[o][1], is[o][1], acc[o][1]);
+                acc[o][2] = fmaf(dh * af[o][2], is[o][0], acc[o][2]);
+                acc[o][3] = fmaf(dh * af[o][3], is[o][1], acc[o][3]);
+            }
         } else {
             // Q6_K: the block of row g / g+8 at its offset in the 16-byte window
             const uintptr_t boff = static_cast<uintptr_t>((ch0 + ch) * 210);
@@ -729,12 +774,13 @@ cudaError_t launch_type(int nv, const BatchedArgs& P, dim3 grid, cudaStream_t st
 
 bool batched_supported(const MulMatOp& o) {
     if (o.type != kTypeQ8_0 && o.type != kTypeQ4_K && o.type != kTypeQ6_K && o.type != kTypeQ5_K &&
-        o.type != kTypeQ4_0)
+        o.type != kTypeQ4_0 && o.type != kTypeIQ4_XS)
         return false;
     if (o.N < 3 || o.ne2 != 1 || o.ne3 != 1) return false;
     if (o.K % 256 != 0 || o.M < 1) return false;
     const uintptr_t wa = reinterpret_cast<uintptr_t>(o.w) | static_cast<uintptr_t>(o.w_nb1);
-    if (o.type == kTypeQ6_K ? (wa & 1) : (wa & 15)) return false;  // 16-byte copies (Q6_K: 2-byte loads)
+    // 16-byte copies (Q6_K: 2-byte loads; IQ4_XS: 4-byte loads from 8-byte aligned blocks)
+    if (o.type == kTypeQ6_K ? (wa & 1) : (o.type == kTypeIQ4_XS ? (wa & 7) : (wa & 15))) return false;
     if ((reinterpret_cast<uintptr_t>(o.x) | static_cast<uintptr_t>(o.x_nb1)) & 15) return false;  // float4 reads
     return true;
 }
@@ -793,6 +839,7 @@ int launch_batched(const MulMatOp& o, void* workspace, size_t workspace_bytes, c
         case kTypeQ4_K: e = launch_type<kTypeQ4_K>(nv, P, grid, stream); break;
         case kTypeQ5_K: e = launch_type<kTypeQ5_K>(nv, P, grid, stream); break;
         case kTypeQ4_0: e = launch_type<kTypeQ4_0>(nv, P, grid, stream); break;
+        case kTypeIQ4_XS: e = launch_type<kTypeIQ4_XS>(nv, P, grid, stream); break;
         default: e = launch_type<kTypeQ6_K>(nv, P, grid, stream); break;
     }
     return e == cudaSuccess ? 2 : -static_cast<int>(e);
