@@ -36,12 +36,14 @@
 // library workspace: N x K x 2 bytes, read by every row tile from L2.
 //
 // Split K: grids far below two CTAs per SM (few row tiles) or with long K run
-// S splits of the K blocks per tile (grid z). Each split stores its f32 tile
-// in workspace; the tile's last split (a per-tile counter) sums the S tiles in
-// split order, so results do not depend on timing.
+// S splits of the K blocks per tile (grid z, one cluster per tile). Each split
+// stores its f32 tile in workspace; after a cluster barrier each split sums
+// its slice of the tile's columns over the S tiles in split order, so results
+// do not depend on timing and the reduction runs on S SMs.
 //
 // Every mbarrier wait is bounded; on timeout the CTA records an error code
 // (read by wllm_sync), stops issuing work, and still releases its TMEM.
+#include <algorithm>
 #include <cuda.h>
 #include <cuda_fp16.h>
 #include <stdint.h>
@@ -89,9 +91,11 @@ struct PrefillArgs {
     float* y;
     int64_t y_nb1;      // bytes between output vectors
     int32_t M, K, N;
-    // split-K (splits > 1): CTA z of a tile covers K blocks [z kb_split, (z+1) kb_split),
-    // writes its f32 tile to partial[tile][z][col][row], and the tile's last CTA
-    // (counted in counters[tile], zero at launch) sums the splits in order
+    // split-K (splits > 1): CTA z of a tile covers K blocks [z kb_split, (z+1) kb_split)
+    // and writes its f32 tile to partial[tile][z][col][row]; the tile's splits
+    // are one cluster, and after a cluster barrier CTA z sums slice z of the
+    // tile's columns over the splits in order. counters[tile] (zeroed by the
+    // pre-pass) marks a tile one of whose splits gave up waiting
     int32_t splits, kb_split;
     // Q6_K rows of 8 mod 16 bytes (K = 3072: 2520 B): the map is over row
     // pairs (2 w_nb1 bytes, a legal stride), and each block takes two boxes of
@@ -655,62 +659,57 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
                 }
             }
         }
-        if (P.splits > 1) {
-            // the tile's last split sums all of them in split order (deterministic)
-            __shared__ int last;
-            asm volatile("bar.sync 1, %0;" ::"n"(kDqWarps * 32) : "memory");
-            if (threadIdx.x == 64) {
-                // the count's low 16 bits are splits done, the high ones splits
-                // that gave up waiting (their partial tiles were not written):
-                // then nobody sums the tile, and wllm_sync reports the error
-                __threadfence();  // this CTA's partial tile before the count
-                const unsigned add = 1u + (*poisoned ? 0x10000u : 0u);
-                const unsigned old = atomicAdd(P.counters + tile, add);
-                last = (old & 0xFFFFu) == static_cast<unsigned>(P.splits - 1);
-                if (last) {
-                    if ((old + add) >> 16) last = 0;
-                    P.counters[tile] = 0u;
-                    __threadfence();  // the other splits' partial tiles after the count
-                }
-            }
-            asm volatile("bar.sync 1, %0;" ::"n"(kDqWarps * 32) : "memory");
-            if (last) {
-                // thread t sums rows 4 (t % 32) .. +3 of columns t / 32 + 16 j (j < 16):
-                // 16 independent float4 loads per split in flight
-                const int t = threadIdx.x - 64, r4 = 4 * (t & 31), cb = t >> 5;
-                static_assert(kDqWarps * 32 / 32 * 16 == kTileN, "reduction covers the tile's columns");
-                const float4* base =
-                    reinterpret_cast<const float4*>(P.partial + static_cast<int64_t>(tile) * P.splits * (kTileM * kTileN));
-                float4 acc[16];
-#pragma unroll
-                for (int j = 0; j < 16; ++j) acc[j] = make_float4(0.f, 0.f, 0.f, 0.f);
-                for (int z = 0; z < P.splits; ++z) {
-                    float4 v[16];
-#pragma unroll
-                    for (int j = 0; j < 16; ++j) v[j] = __ldcg(base + (z * kTileN + cb + 16 * j) * (kTileM / 4) + (r4 >> 2));
-#pragma unroll
-                    for (int j = 0; j < 16; ++j) {
-                        acc[j].x += v[j].x;
-                        acc[j].y += v[j].y;
-                        acc[j].z += v[j].z;
-                        acc[j].w += v[j].w;
-                    }
-                }
-#pragma unroll
-                for (int j = 0; j < 16; ++j) {
-                    const int n = n0 + cb + 16 * j, r = m0 + r4;
-                    if (n >= P.N) continue;
-                    float* yn = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(P.y) + n * P.y_nb1);
-                    const float a[4] = {acc[j].x, acc[j].y, acc[j].z, acc[j].w};
-#pragma unroll
-                    for (int i = 0; i < 4; ++i)
-                        if (r + i < P.M) yn[r + i] = a[i];
-                }
-            }
-        }
+        // a split that gave up waiting did not write its partial tile: it marks
+        // the tile (the marks are zeroed by the pre-pass), and nobody sums it
+        if (P.splits > 1 && dw == 0 && lane == 0 && *poisoned) atomicOr(P.counters + blockIdx.y * gridDim.x + blockIdx.x, 1u);
     }
     tc_fence_before();
     __syncthreads();
+    if (P.splits > 1) {
+        // The S splits of a tile are one cluster (grid z): after the cluster
+        // barrier every partial tile is written, and each split sums its own
+        // slice of the tile's columns over the S partial tiles, in split order
+        // (deterministic), so the reduction runs on S SMs at once.
+        asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+        const int tile = blockIdx.y * gridDim.x + blockIdx.x;
+        if (warp >= 2 && __ldcg(P.counters + tile) == 0u) {
+            // thread t sums rows 4 (t % 32) .. +3 of slice columns t / 32 + 16 j
+            const int t = threadIdx.x - 64, r4 = 4 * (t & 31), cb = t >> 5;
+            const int w = (kTileN + P.splits - 1) / P.splits, c0 = blockIdx.z * w, c1 = min(kTileN, c0 + w);
+            const float4* base =
+                reinterpret_cast<const float4*>(P.partial + static_cast<int64_t>(tile) * P.splits * (kTileM * kTileN));
+            constexpr int kJ = kTileN / 2 / 16;  // slice columns per thread at S >= 2
+            float4 acc[kJ];
+#pragma unroll
+            for (int j = 0; j < kJ; ++j) acc[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int z = 0; z < P.splits; ++z) {
+                float4 v[kJ];
+#pragma unroll
+                for (int j = 0; j < kJ; ++j) {
+                    const int col = c0 + cb + 16 * j;
+                    v[j] = col < c1 ? __ldcg(base + (z * kTileN + col) * (kTileM / 4) + (r4 >> 2))
+                                    : make_float4(0.f, 0.f, 0.f, 0.f);
+                }
+#pragma unroll
+                for (int j = 0; j < kJ; ++j) {
+                    acc[j].x += v[j].x;
+                    acc[j].y += v[j].y;
+                    acc[j].z += v[j].z;
+                    acc[j].w += v[j].w;
+                }
+            }
+#pragma unroll
+            for (int j = 0; j < kJ; ++j) {
+                const int col = c0 + cb + 16 * j, n = n0 + col, r = m0 + r4;
+                if (col >= c1 || n >= P.N) continue;
+                float* yn = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(P.y) + n * P.y_nb1);
+                const float av[4] = {acc[j].x, acc[j].y, acc[j].z, acc[j].w};
+#pragma unroll
+                for (int i = 0; i < 4; ++i)
+                    if (r + i < P.M) yn[r + i] = av[i];
+            }
+        }
+    }
     if (warp == 1) {
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
@@ -779,6 +778,9 @@ int plan_splits(const MulMatOp& o) {
         const int kb = (nblk + S - 1) / S;
         if (S > 1 && (nblk + kb - 1) / kb < S) continue;  // a split would be empty
         const int waves = (tiles * S + kSlots - 1) / kSlots;
+        // a split costs its partial tile's write and its slice's reduction, and
+        // clusters of many splits place less freely (S = 8 measured slower than
+        // S = 4 at 1024 x 4096 with this term at 1.3)
         const double cost = static_cast<double>(waves) * kb + (S > 1 ? 0.65 * S : 0.0);
         if (cost < best_cost - 1e-9) {
             best_cost = cost;
@@ -890,8 +892,12 @@ int launch_prefill(const MulMatOp& o, void* workspace, size_t workspace_bytes, c
     }
     {
         // the f16 activation image (and the split counters), then the GEMM
+        // at most about four CTAs per SM, so that every CTA of the pre-pass is
+        // running (and has released the GEMM) at once: the GEMM's launch waits
+        // for all of them to execute griddepcontrol.launch_dependents
         const int threads = 256, per_row = (o.K / 4 + threads - 1) / threads;
-        x_to_f16_kernel<<<dim3(per_row, o.N < 65535 ? o.N : 65535), threads, 0, stream>>>(o.x, o.x_nb1, x16, o.K, o.N, P.counters,
+        const int rows = std::max(1, std::min(o.N, 4 * kSlots / per_row));
+        x_to_f16_kernel<<<dim3(per_row, rows), threads, 0, stream>>>(o.x, o.x_nb1, x16, o.K, o.N, P.counters,
                                                                     static_cast<int>(tiles));
         const cudaError_t e = cudaGetLastError();
         if (e != cudaSuccess) return -static_cast<int>(e);
@@ -925,11 +931,16 @@ int launch_prefill(const MulMatOp& o, void* workspace, size_t workspace_bytes, c
     cfg.blockDim = dim3(kThreads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
+    // a tile's splits are one cluster, for the barrier before their reduction
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = 1;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = static_cast<unsigned>(splits);
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = splits > 1 ? 2 : 1;
     cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, P);
     if (e == cudaSuccess) e = cudaGetLastError();
     return e == cudaSuccess ? launched : -static_cast<int>(e);
