@@ -337,14 +337,19 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
         // The loop runs on lane 0 alone, with the B descriptors advanced from
         // one base: warp-wide broadcasts and syncs around each chunk's waits
         // cost the issuing thread as much as the chunk's four MMAs take.
+        // Chunks go in pairs (q, q + 1; nchunk is a multiple of 4): one wait on
+        // chunk q + 1's A barrier covers both, since every dequant warp arrives
+        // for q before q + 1 (and with kOneWait the first one waited for each
+        // chunk's B box before arriving).
         if (lane == 0) {
             int committed = 0;  // chunks whose MMAs were committed
             const uint64_t bdesc0 = umma_desc_sw128(smem_u32(B));  // + (byte offset >> 4)
-            for (int q = 0; q < nchunk; ++q) {
-                const int s = q % kStages;
+            for (int q = 0; q < nchunk; q += 2) {
+                const int s0 = q % kStages;  // chunk q + 1 is in stage s0 + 1 of the same round
                 const uint32_t par = (q / kStages) & 1;
-                if ((!kOneWait && !mbar_wait(&b_full[s], par, 2u, poisoned)) ||
-                    !mbar_wait(&a_full[s], par, 2u, poisoned)) {  // with kOneWait a_full implies b_full
+                if ((!kOneWait &&
+                     (!mbar_wait(&b_full[s0], par, 2u, poisoned) || !mbar_wait(&b_full[s0 + 1], par, 2u, poisoned))) ||
+                    !mbar_wait(&a_full[s0 + 1], par, 2u, poisoned)) {
                     // a time-out: the MMAs already issued still write TMEM, which is
                     // freed at the end; wait (bounded) for the last commit, which
                     // tracks all of them
@@ -354,14 +359,18 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
                     break;
                 }
                 tc_fence_after();
-                const uint32_t a0 = tmem + static_cast<uint32_t>(kTileN + s * kACols);
-                const uint64_t bd = bdesc0 + static_cast<uint64_t>((s * kBBytes) >> 4);
 #pragma unroll
-                for (int ks = 0; ks < kChunkK / 16; ++ks)  // K = 16 per MMA: 8 TMEM columns of A, 32 bytes of B's row
-                    umma_f16_ts(tmem, a0 + 8 * ks, bd + 2 * ks, (q > 0 || ks > 0) ? 1u : 0u);
-                umma_commit(&st_free[s]);  // the stage is free once these MMAs have read it
-                if (q == nchunk - 1) umma_commit(acc_full);
-                committed = q + 1;
+                for (int c2 = 0; c2 < 2; ++c2) {
+                    const int s = s0 + c2;
+                    const uint32_t a0 = tmem + static_cast<uint32_t>(kTileN + s * kACols);
+                    const uint64_t bd = bdesc0 + static_cast<uint64_t>((s * kBBytes) >> 4);
+#pragma unroll
+                    for (int ks = 0; ks < kChunkK / 16; ++ks)  // K = 16 per MMA: 8 TMEM columns of A, 32 bytes of B's row
+                        umma_f16_ts(tmem, a0 + 8 * ks, bd + 2 * ks, (q + c2 > 0 || ks > 0) ? 1u : 0u);
+                    umma_commit(&st_free[s]);  // the stage is free once these MMAs have read it
+                }
+                if (q + 2 == nchunk) umma_commit(acc_full);
+                committed = q + 2;
             }
         }
         __syncwarp();
