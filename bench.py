@@ -62,6 +62,10 @@ _MODEL = "qwen3-8b"
 # DRAM bytes (read + write) of one Llama-3.2-3B layer's four GEMV launches
 # from an ncu capture; its algorithmic bytes are 64,139,264 per layer.
 NCU_DRAM_BYTES_PER_LAYER_LLAMA32 = 64_314_496
+# The same for Qwen3-8B: one layer's four launches (algorithmic 108,830,720
+# bytes) and the 151936x4096 Q6_K output projection (algorithmic 511,129,088).
+NCU_DRAM_BYTES_PER_LAYER_QWEN3 = 108_935_168
+NCU_DRAM_BYTES_OUTPUT_QWEN3 = 511_432_448
 FALLBACK_HBM_GBS = 6650.0
 
 
@@ -865,6 +869,8 @@ def run_b200(args, rank: int, world: int, local_rank: int):
         traffic = None
         if world == 1 and _MODEL == "llama-3.2-3b":
             traffic = NCU_DRAM_BYTES_PER_LAYER_LLAMA32 * layers
+        elif world == 1 and _MODEL == "qwen3-8b":
+            traffic = NCU_DRAM_BYTES_PER_LAYER_QWEN3 * layers + (NCU_DRAM_BYTES_OUTPUT_QWEN3 if WORKLOADS[_MODEL][2] else 0)
         line = {
             "metric": METRIC, "value": round(gbs, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(dev_ms, 4), "higher_is_better": True,
