@@ -1,8 +1,11 @@
 """GPU parity tests of the prefill path: Q4_K, Q5_K, Q6_K, Q8_0 and Q4_0 MUL_MAT with
 N > 64 vectors runs as a tcgen05 tensor-core GEMM (f16 dequantized weights and
 activations, f32 accumulation). Q6_K takes it when its rows are a multiple of
-16 bytes (K a multiple of 2048), as the tensor-memory copies need, or of 8
-bytes with M even (K = 3072: rows copied in pairs).
+16 bytes (K a multiple of 2048), as the tensor-memory copies need, or an even
+number of bytes with M a multiple of the row group that makes a multiple of
+16: K = 3072 rows (2520 B) in pairs, K = 3584 (2940 B) in fours, K = 2304
+(1890 B) in eights. IQ4_XS rows of 8 mod 16 bytes (an odd number of blocks)
+go in pairs.
 
 Bar: max relative error <= 2e-2 (rel = max|y - r| / max|r|) against
  - the oracle's f64 dequant-then-dot (small and ragged shapes), and
@@ -122,10 +125,12 @@ def test_prefill_q6k_matches_oracle(runtime, M, K, N):
     assert O.rel_error(y, r) <= PREFILL_TOL
 
 
-@pytest.mark.parametrize("M,K,N", [(4096, 14336, 512), (1024, 4096, 512), (3072, 8192, 200), (14336, 4096, 77)])
+@pytest.mark.parametrize("M,K,N", [(4096, 14336, 512), (1024, 4096, 512), (3072, 8192, 200), (14336, 4096, 77),
+                                   (9216, 2304, 512), (2304, 2304, 300)])
 def test_prefill_q6k_shapes_vs_torch_fp32(runtime, M, K, N):
     """Q6_K projections of Q4_K_M models in prefill: Llama-3-8B ffn_down and
-    attn_v (512 tokens), Llama-3.2-3B ffn_down, and a wide one at a short N."""
+    attn_v (512 tokens), Llama-3.2-3B ffn_down, a wide one at a short N, and
+    Gemma-2-2B ffn_up and attn_q (1890-byte rows, copied in eights)."""
     import torch
 
     dev = torch.device("cuda", 0)
@@ -156,6 +161,8 @@ def test_prefill_q6k_shapes_vs_torch_fp32(runtime, M, K, N):
     (O.TYPE_Q4_0, 260, 2304, 200),
     (O.TYPE_IQ4_XS, 128, 512, 65),    # two 136-byte blocks: offsets 0 and 8 in their boxes
     (O.TYPE_IQ4_XS, 200, 2048, 130),  # partial tiles
+    (O.TYPE_IQ4_XS, 256, 2304, 65),   # 1224-byte rows (8 mod 16): copied in pairs
+    (O.TYPE_IQ4_XS, 130, 768, 70),    # 408-byte rows in pairs; partial row tile
 ])
 def test_prefill_other_types_matches_oracle(runtime, qtype, M, K, N):
     rng = np.random.default_rng(3000 + qtype + M + K + N)
@@ -170,7 +177,8 @@ def test_prefill_other_types_matches_oracle(runtime, qtype, M, K, N):
 @pytest.mark.parametrize("qtype,M,K,N", [(O.TYPE_Q8_0, 9216, 2304, 512), (O.TYPE_Q8_0, 2304, 9216, 256),
                                          (O.TYPE_Q5_K, 14336, 4096, 512), (O.TYPE_Q5_K, 4096, 14336, 200),
                                          (O.TYPE_Q4_0, 14336, 4096, 512), (O.TYPE_Q4_0, 4096, 14336, 128),
-                                         (O.TYPE_IQ4_XS, 14336, 4096, 512), (O.TYPE_IQ4_XS, 4096, 14336, 200)])
+                                         (O.TYPE_IQ4_XS, 14336, 4096, 512), (O.TYPE_IQ4_XS, 4096, 14336, 200),
+                                         (O.TYPE_IQ4_XS, 9216, 2304, 512)])
 def test_prefill_other_types_shapes_vs_torch_fp32(runtime, qtype, M, K, N):
     """Gemma-2-2B ffn_up / ffn_down (Q8_0) and Llama-3-8B ffn_gate / ffn_down
     (Q5_K, Q4_0) in prefill."""
@@ -199,8 +207,11 @@ def test_prefill_other_types_shapes_vs_torch_fp32(runtime, qtype, M, K, N):
     (1024, 3072, 65),    # Llama-3.2-3B attn_v: 2520-byte rows, copied as pairs
     (1000, 3072, 130),   # partial row tile (M even)
     (3072, 1024, 300),   # 840-byte rows
+    (256, 2304, 65),     # Gemma-2-2B hidden: 1890-byte rows, copied in eights
+    (1000, 2304, 130),   # partial row tile (M a multiple of 8)
+    (520, 3584, 100),    # 2940-byte rows, copied in fours; partial row tile
 ])
-def test_prefill_q6k_row_pairs_matches_oracle(runtime, M, K, N):
+def test_prefill_q6k_row_groups_matches_oracle(runtime, M, K, N):
     rng = np.random.default_rng(4000 + M + K + N)
     w = synth.weights(rng, O.TYPE_Q6_K, M, K)
     x = synth.activations(rng, N, K)
@@ -210,11 +221,12 @@ def test_prefill_q6k_row_pairs_matches_oracle(runtime, M, K, N):
     assert O.rel_error(y, O.mul_mat_f64(O.TYPE_Q6_K, w, x)) <= PREFILL_TOL
 
 
-def test_prefill_q6k_odd_rows_take_the_batched_gemm(runtime):
-    """M odd with 2520-byte rows: no row pairs, so the batched GEMM runs it, at
-    the GEMV bar."""
-    rng = np.random.default_rng(4100)
-    M, K, N = 333, 3072, 70
+@pytest.mark.parametrize("M,K", [(333, 3072), (1002, 2304)])
+def test_prefill_q6k_ragged_row_groups_take_the_batched_gemm(runtime, M, K):
+    """M not a multiple of the row group (2520-byte rows in pairs, 1890-byte
+    rows in eights): the batched GEMM runs it, at the GEMV bar."""
+    rng = np.random.default_rng(4100 + M)
+    N = 70
     w = synth.weights(rng, O.TYPE_Q6_K, M, K)
     x = synth.activations(rng, N, K)
     y = run_mul_mat(runtime, O.TYPE_Q6_K, w, x)

@@ -85,8 +85,8 @@ constexpr uint32_t kSpinLimit = 1u << 26;
 
 struct PrefillArgs {
     CUtensorMap wmap;   // weights: Q4_K [M rows][row_bytes / 8] uint64, box 18 x 128 (one block column);
-                        // Q6_K [M rows][row_bytes] uint8, box 240 x 128 (rows of 8 mod 16
-                        // bytes: [M / 2 row pairs][2 w_nb1] uint8, box 240 x 64)
+                        // Q6_K [M rows][row_bytes] uint8, box 240 x 128 (rows grouped by
+                        // G = 2, 4, 8: [M / G][G w_nb1] uint8, box 240 x 128 / G)
     CUtensorMap xmap;   // f16 activations: [N][K], box 64 x 128, 128-byte swizzle
     float* y;
     int64_t y_nb1;      // bytes between output vectors
@@ -97,10 +97,12 @@ struct PrefillArgs {
     // tile's columns over the splits in order. counters[tile] (zeroed by the
     // pre-pass) marks a tile one of whose splits gave up waiting
     int32_t splits, kb_split;
-    // Q6_K rows of 8 mod 16 bytes (K = 3072: 2520 B): the map is over row
-    // pairs (2 w_nb1 bytes, a legal stride), and each block takes two boxes of
-    // 64 pairs, the even rows' bytes and the odd rows' (w_nb1 further on)
-    int32_t q6_pairs;
+    // byte-mapped rows (Q6_K, IQ4_XS) whose stride is not a multiple of 16
+    // bytes (Q6_K K = 3072: 2520 B, K = 2304: 1890 B): the map is over groups
+    // of G = 2^row_lg rows (G w_nb1 bytes, a legal stride), and each block
+    // takes G boxes of 128 / G groups, box j from the block's start in row j
+    // of the group; 0 for rows 16-byte apart
+    int32_t row_lg;
     int32_t w_nb1;
     float* partial;
     unsigned* counters;
@@ -228,6 +230,36 @@ __device__ __forceinline__ int byte_box_x(int kb) {
     return kb * (raw_row_bytes<TYPE>() / 8);
 }
 
+// Bytes of one block column (256 elements) of a byte-mapped row.
+template <int TYPE>
+__host__ __device__ constexpr int byte_blk_bytes() { return TYPE == kTypeQ6_K ? 210 : 136; }
+
+// Copies K block kb of the tile's 128 rows from row m0 into a raw slot. Row
+// r of the tile lands in box row (r mod G) (128 / G) + r / G of the slot.
+template <int TYPE>
+__device__ __forceinline__ void issue_raw(uint8_t* dst, const PrefillArgs& P, int kb, int m0, uint64_t* bar) {
+    if constexpr (TYPE == kTypeQ6_K || TYPE == kTypeIQ4_XS) {
+        const int lg = P.row_lg;
+        for (int j = 0; j < (1 << lg); ++j)
+            tma_2d(dst + j * (kTileM >> lg) * raw_row_bytes<TYPE>(), &P.wmap,
+                   (kb * byte_blk_bytes<TYPE>() + j * P.w_nb1) & ~15, m0 >> lg, bar);
+    } else {
+        tma_2d(dst, &P.wmap, byte_box_x<TYPE>(kb), m0, bar);
+    }
+}
+
+// A byte-mapped row's place in a raw slot (box row) and its block's offset
+// in that box row (0..15).
+template <int TYPE>
+__device__ __forceinline__ int byte_row_slot(const PrefillArgs& P, int r) {
+    const int j = r & ((1 << P.row_lg) - 1);
+    return j * (kTileM >> P.row_lg) + (r >> P.row_lg);
+}
+template <int TYPE>
+__device__ __forceinline__ int byte_row_off(const PrefillArgs& P, int kb, int r) {
+    return (kb * byte_blk_bytes<TYPE>() + (r & ((1 << P.row_lg) - 1)) * P.w_nb1) & 15;
+}
+
 template <int TYPE>
 __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_constant__ PrefillArgs P) {
     constexpr int kRawBytes = raw_bytes<TYPE>();
@@ -287,14 +319,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
             const int pre = min(nchunk >> 2, kRawSlots);
             for (int kb = 0; kb < pre; ++kb) {
                 mbar_expect_tx(&raw_full[kb], kRawBytes);
-                const int x = byte_box_x<TYPE>(kb0 + kb);
-                if (TYPE == kTypeQ6_K && P.q6_pairs) {
-                    const int xo = ((kb0 + kb) * 210 + P.w_nb1) & ~15;
-                    tma_2d(raw + kb * kRawBytes, &P.wmap, x, m0 / 2, &raw_full[kb]);
-                    tma_2d(raw + kb * kRawBytes + (kTileM / 2) * kQ6Box, &P.wmap, xo, m0 / 2, &raw_full[kb]);
-                } else {
-                    tma_2d(raw + kb * kRawBytes, &P.wmap, x, m0, &raw_full[kb]);
-                }
+                issue_raw<TYPE>(raw + kb * kRawBytes, P, kb0 + kb, m0, &raw_full[kb]);
                 raw_issued = kb + 1;
             }
             asm volatile("griddepcontrol.wait;" ::: "memory");
@@ -304,16 +329,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
                     const int r = kb % kRawSlots;
                     if (kb >= kRawSlots && !mbar_wait(&raw_free[r], ((kb / kRawSlots) - 1) & 1, 1u, poisoned)) break;
                     mbar_expect_tx(&raw_full[r], kRawBytes);
-                    // x: uint64 words per 256 elements (Q4_K 18, Q5_K 22, Q8_0 34);
-                    // Q6_K in bytes, the block's start rounded down to 16
-                    const int x = byte_box_x<TYPE>(kb0 + kb);
-                    if (TYPE == kTypeQ6_K && P.q6_pairs) {
-                        const int xo = ((kb0 + kb) * 210 + P.w_nb1) & ~15;
-                        tma_2d(raw + r * kRawBytes, &P.wmap, x, m0 / 2, &raw_full[r]);
-                        tma_2d(raw + r * kRawBytes + (kTileM / 2) * kQ6Box, &P.wmap, xo, m0 / 2, &raw_full[r]);
-                    } else {
-                        tma_2d(raw + r * kRawBytes, &P.wmap, x, m0, &raw_full[r]);
-                    }
+                    issue_raw<TYPE>(raw + r * kRawBytes, P, kb0 + kb, m0, &raw_full[r]);
                     raw_issued = kb + 1;
                 }
                 const int s = q % kStages;
@@ -395,12 +411,10 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
                 // j = 2 (p%2) + h: ql byte 64 (p/2) + 32 h + 16 qq + l (high nibble when
                 // p is odd), qh byte 128 + 32 (p/2) + 16 qq + l shifted by 2 j, scale
                 // 192 + 8 (p/2) + 2 j + qq; w = d sc (q - 32)
-                // row pairs: odd rows are in the second box, w_nb1 bytes on (their
-                // offset differs from the even rows': per thread, not per warp)
-                const bool odd = P.q6_pairs && (r & 1);
-                const int o = ((kb0 + kb) * 210 + (odd ? P.w_nb1 : 0)) & 15;
-                const uint8_t* rowp =
-                    raw + rs * kRawBytes + (P.q6_pairs ? (odd ? kTileM / 2 : 0) + (r >> 1) : r) * kQ6Box;
+                // grouped rows: the offset depends on the row's place in its group
+                // (per thread, not per warp)
+                const int o = byte_row_off<TYPE>(P, kb0 + kb, r);
+                const uint8_t* rowp = raw + rs * kRawBytes + byte_row_slot<TYPE>(P, r) * kQ6Box;
                 const int q4 = o >> 2;
                 const uint32_t sh = 8u * static_cast<uint32_t>(o & 3);
                 const float d = __half2float(*reinterpret_cast<const __half*>(rowp + o + 208));
@@ -455,8 +469,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
                 // 144-byte box row. The level enters as f16 1024 + (level + 128)
                 // (an unsigned byte), minus 1152: the level exactly, times the f16
                 // d (ls - 32).
-                const uint8_t* rowp = raw + rs * kRawBytes + r * 144;
-                const int o = ((kb0 + kb) * 136) & 15;
+                const uint8_t* rowp = raw + rs * kRawBytes + byte_row_slot<TYPE>(P, r) * 144;
+                const int o = byte_row_off<TYPE>(P, kb0 + kb, r);
                 const float d = __half2float(*reinterpret_cast<const __half*>(rowp + o));
                 const uint32_t shb = *reinterpret_cast<const uint16_t*>(rowp + o + 2);
                 const uint32_t slb = *reinterpret_cast<const uint32_t*>(rowp + o + 4);
@@ -799,9 +813,19 @@ int plan_splits(const MulMatOp& o) {
     return best;
 }
 
-// Whether a Q6_K op's rows are copied as pairs: 8 mod 16 bytes apart, M even.
-bool q6_row_pairs(const MulMatOp& o) {
-    return o.type == kTypeQ6_K && (o.w_nb1 & 15) == 8 && o.M % 2 == 0 && o.w_nb1 < (int64_t(1) << 30);
+// log2 of the row group a byte-mapped op's rows are copied in: 0 for rows a
+// multiple of 16 bytes apart; Q6_K / IQ4_XS rows 8 mod 16 bytes apart in
+// pairs; Q6_K rows 4 or 12 mod 16 apart in fours, 2 mod 4 in eights (G w_nb1
+// a multiple of 16); M a multiple of G; -1 where no group fits. (An IQ4_XS
+// block must start at most 8 bytes into its 144-byte box row.)
+int row_group_lg(const MulMatOp& o) {
+    const int m = static_cast<int>(o.w_nb1 & 15);
+    if (m == 0) return 0;
+    if (o.w_nb1 >= (int64_t(1) << 26)) return -1;
+    int lg = -1;
+    if (o.type == kTypeQ6_K && !(m & 1)) lg = m == 8 ? 1 : ((m & 3) == 0 ? 2 : 3);
+    if (o.type == kTypeIQ4_XS && m == 8) lg = 1;
+    return lg > 0 && o.M % (1 << lg) == 0 ? lg : -1;
 }
 
 // Bytes of 256 elements of a row: Q4_K 144, Q5_K 176, Q6_K 210, Q8_0 272, Q4_0 144.
@@ -826,11 +850,10 @@ bool prefill_supported(const MulMatOp& o) {
         return false;
     if (o.K % 256 != 0 || o.M < 1) return false;
     const int64_t row_bytes = static_cast<int64_t>(o.K / 256) * block_group_bytes(o.type);
-    // TMA rows: 16-byte aligned base and row stride. Q6_K also takes rows of 8
-    // mod 16 bytes (K = 1024 (mod 2048), unpadded) as row pairs when M is even;
-    // other Q6_K shapes take the batched GEMM
-    const bool pairs = q6_row_pairs(o);
-    if ((reinterpret_cast<uintptr_t>(o.w) & 15) || ((o.w_nb1 & 15) && !pairs)) return false;
+    // TMA rows: 16-byte aligned base and row stride, or (Q6_K, IQ4_XS) rows of
+    // an even stride in groups of 2, 4 or 8 (Q6_K K = 1024 (mod 2048) in pairs,
+    // K = 256 (mod 512) in eights, unpadded) when M is a multiple of the group
+    if ((reinterpret_cast<uintptr_t>(o.w) & 15) || row_group_lg(o) < 0) return false;
     if (o.w_nb1 < row_bytes) return false;
     if (o.type == kTypeQ6_K && row_bytes < kQ6Box) return false;  // the box stays within a row's width
     if (o.type == kTypeIQ4_XS && row_bytes < 144) return false;
@@ -859,15 +882,15 @@ int launch_prefill(const MulMatOp& o, void* workspace, size_t workspace_bytes, c
         // 144-byte box from the block's 16-byte-rounded start (the box's end may
         // pass the row's last block: zeros, never read)
         const cuuint64_t group = static_cast<cuuint64_t>(block_group_bytes(o.type));
-        const bool pairs = q6_row_pairs(o);
-        // row pairs: [M / 2][2 w_nb1 bytes], the odd row's bytes from w_nb1 on
-        const cuuint64_t dims[2] = {pairs ? 2 * static_cast<cuuint64_t>(o.w_nb1)
-                                          : static_cast<cuuint64_t>(o.K / 256) * (bytemap ? group : group / 8),
-                                    static_cast<cuuint64_t>(pairs ? o.M / 2 : o.M)};
-        const cuuint64_t strides[1] = {static_cast<cuuint64_t>(pairs ? 2 * o.w_nb1 : o.w_nb1)};
+        const int lg = row_group_lg(o);
+        // row groups: [M / G][G w_nb1 bytes], row j of a group from j w_nb1 on
+        const cuuint64_t dims[2] = {lg ? static_cast<cuuint64_t>(o.w_nb1) << lg
+                                       : static_cast<cuuint64_t>(o.K / 256) * (bytemap ? group : group / 8),
+                                    static_cast<cuuint64_t>(o.M >> lg)};
+        const cuuint64_t strides[1] = {static_cast<cuuint64_t>(o.w_nb1) << lg};
         const cuuint32_t box[2] = {q6 ? static_cast<cuuint32_t>(kQ6Box) : (iq4 ? 144u : static_cast<cuuint32_t>(group / 8)),
-                                   pairs ? kTileM / 2u : static_cast<cuuint32_t>(kTileM)};
-        P.q6_pairs = pairs ? 1 : 0;
+                                   static_cast<cuuint32_t>(kTileM >> lg)};
+        P.row_lg = lg;
         P.w_nb1 = static_cast<int32_t>(o.w_nb1);
         const cuuint32_t es[2] = {1, 1};
         if (enc(&P.wmap, bytemap ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, const_cast<uint8_t*>(o.w),
