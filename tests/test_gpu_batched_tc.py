@@ -1,12 +1,15 @@
-"""The tcgen05 small-batch GEMM (Q4_K and Q5_K weights, several sequences
-decoding together, N = 5..64, and N = 3-4 where the streaming kernel cannot
-take the shape): both error metrics of the path (max-normalized and
-per-element, 1e-3) against a float64 matmul of the device-dequantized
+"""The tcgen05 small-batch GEMM (Q4_K, Q5_K and Q8_0 weights, several
+sequences decoding together, N = 5..64, and N = 3-4 where the streaming
+kernel cannot take the shape): both error metrics of the path (max-normalized
+and per-element, 1e-3) against a float64 matmul of the device-dequantized
 weights, on N(0,1) activations and on outlier channels; shapes with partial
 row tiles, split K and K not a multiple of 1024. Weights of at most 4096 x 4096
 below 16 vectors route to the mma.sync GEMM instead; the shapes above that
 size (5000 x 4352, 4200 x 4608: partial row tiles, K = 17 and 18 blocks) keep
-those N on this kernel."""
+those N on this kernel. Q8_0 goes in as two exact f16 weight planes (d q
+rounded to f16, and the remainder) and takes this kernel above 16 vectors
+(the integer mma.sync GEMM below); a test drives its scales through the f16
+subnormal range and up to 2^8."""
 from __future__ import annotations
 
 import zlib
@@ -51,12 +54,14 @@ def _kernels():
     return c.kernels_launched
 
 
-@pytest.mark.parametrize("N", [5, 8, 16, 33, 64])
+@pytest.mark.parametrize("N", [5, 8, 16, 17, 33, 64])
 @pytest.mark.parametrize("qtype,M,K", [(jsep.GGML_TYPE_Q4_K, 4096, 4096), (jsep.GGML_TYPE_Q4_K, 14336, 4096),
                                        (jsep.GGML_TYPE_Q4_K, 4096, 14336), (jsep.GGML_TYPE_Q4_K, 1000, 2304),
                                        (jsep.GGML_TYPE_Q5_K, 4096, 4096), (jsep.GGML_TYPE_Q5_K, 333, 3072),
                                        (jsep.GGML_TYPE_Q4_K, 128, 256), (jsep.GGML_TYPE_Q4_K, 5000, 4352),
-                                       (jsep.GGML_TYPE_Q5_K, 4200, 4608)])
+                                       (jsep.GGML_TYPE_Q5_K, 4200, 4608), (jsep.GGML_TYPE_Q8_0, 9216, 2304),
+                                       (jsep.GGML_TYPE_Q8_0, 2304, 9216), (jsep.GGML_TYPE_Q8_0, 5000, 4352),
+                                       (jsep.GGML_TYPE_Q8_0, 128, 256)])
 def test_batched_tc_both_metrics(runtime, qtype, M, K, N):
     rng = np.random.default_rng(zlib.crc32(repr((qtype, M, K, N)).encode()))
     x = synth.activations(rng, N, K)
@@ -92,3 +97,39 @@ def test_batched_tc_tiny_and_huge_activations(runtime):
     for n in (0, 1, 2, 4):
         a, b = O.rel_error(y[n], r[n]), O.rel_error_elem(y[n], r[n])
         assert a <= TOL and b <= TOL, (n, a, b)
+
+
+@pytest.mark.parametrize("N", [24, 40])
+def test_batched_tc_q8_0_scale_range(runtime, N):
+    """Q8_0 blocks whose f16 scale d is subnormal (down to 2^-24), tiny, normal
+    or large (up to 2^8), mixed within rows: hi = f16(d q) and lo = d q - hi
+    stay exact, so the result meets both metrics whatever d is."""
+    import torch
+
+    M, K = 5000, 4352
+    rng = np.random.default_rng(77 + N)
+    w = synth.weights(rng, jsep.GGML_TYPE_Q8_0, M, K)
+    blocks = w.reshape(M, K // 32, 34)
+    exps = rng.integers(-24, 9, size=(M, K // 32)).astype(np.float64)
+    mant = rng.uniform(1.0, 2.0, size=(M, K // 32))
+    d = np.ldexp(mant, exps.astype(np.int64)).astype(np.float16)  # subnormals where 2^e < 2^-14
+    blocks[:, :, 0:2] = d.view(np.uint8).reshape(M, K // 32, 2)
+    x = synth.activations(rng, N, K)
+    dev = torch.device("cuda", 0)
+    wt = torch.from_numpy(w).to(dev)
+    xt = torch.from_numpy(x).to(dev)
+    y = torch.full((N, M), float("nan"), device=dev)
+    torch.cuda.synchronize()
+    stream = jsep.library_stream()
+    k0 = _kernels()
+    assert jsep.mul_mat_device(jsep.GGML_TYPE_Q8_0, wt.data_ptr(), wt.shape[1], xt.data_ptr(), K, y.data_ptr(), M, M,
+                               K, N, stream) == jsep.STATUS_OK, jsep.last_error()
+    assert _kernels() - k0 == 2
+    wf = torch.empty(M, K, device=dev)
+    jsep.dequantize_device(jsep.GGML_TYPE_Q8_0, wt.data_ptr(), wf.data_ptr(), M * K, stream)
+    runtime.jsep_sync()
+    r = (wf.double() @ xt.double().t()).t().cpu().numpy()
+    yy = y.double().cpu().numpy()
+    assert np.all(np.isfinite(yy))
+    a, b = O.rel_error(yy, r), O.rel_error_elem(yy, r)
+    assert a <= TOL and b <= TOL, (a, b)

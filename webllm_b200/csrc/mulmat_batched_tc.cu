@@ -1,6 +1,7 @@
-// Small-batch quantized MUL_MAT on tcgen05 tensor cores for Q4_K and Q5_K
-// weights (several sequences decoding together: N up to 64 vectors), exact to
-// about 2^-22 of every activation element, like the integer decode kernels.
+// Small-batch quantized MUL_MAT on tcgen05 tensor cores for Q4_K, Q5_K and
+// Q8_0 weights (several sequences decoding together: N up to 64 vectors),
+// exact to about 2^-22 of every activation element, like the integer decode
+// kernels.
 //
 //   y[m + M n] = sum_k W[m, k] x[k + K n]   (ggml MUL_MAT, matmul.ts:10-17)
 //
@@ -21,6 +22,15 @@
 //    sums split the same way (scale 2^(e + 5)), one MMA per block.
 // A pre-pass (btc_prep_kernel, one warp per vector and block) writes the
 // activation image, the sums image and the scales into workspace.
+//
+// Q8_0 (ggml's dequantize_row_q8_0: w = d q per 32-element block) has no
+// integer form that fits f16: d is an f16 of 11 significant bits, so d q has
+// up to 18. It goes in as two exact weight planes, hi = f16(d q) and
+// lo = d q - hi (one f16 FMA; the residual has at most 7 significant bits
+// on hi's grid, never below f16's smallest subnormal, so it is exact), each
+// against the same activations: the accumulator gets sum (hi + lo) x, and the
+// epilogue scales it by 2^e only. Chunk by chunk (64 K), both planes of a
+// chunk share one half of the A stage.
 //
 // One thread issues a tcgen05.mma in about 50 cycles and waits on an mbarrier
 // in about 150, whatever the MMA's N (16 to 128), so at these sizes the issue
@@ -95,9 +105,15 @@ struct BtcArgs {
     unsigned* counters;   // [tile] (split K, zero at launch)
 };
 
+// Bytes per row of one 256-element block: Q4_K 144, Q5_K 176, Q8_0 272 (8 blocks).
 template <int TYPE>
 __host__ __device__ constexpr int blk_bytes() {
-    return TYPE == kTypeQ5_K ? 176 : 144;
+    return TYPE == kTypeQ5_K ? 176 : (TYPE == kTypeQ8_0 ? 272 : 144);
+}
+// Q8_0 weights go in as two f16 planes (no mins, no sums box).
+template <int TYPE>
+__host__ __device__ constexpr bool two_planes() {
+    return TYPE == kTypeQ8_0;
 }
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -219,15 +235,31 @@ __device__ __forceinline__ void tmem_ld16x3(uint32_t t0, uint32_t t1, uint32_t t
         v2[i] = __uint_as_float(r[32 + i]);
     }
 }
+__device__ __forceinline__ void tmem_ld16x2(uint32_t t0, uint32_t t1, float (&v0)[16], float (&v1)[16]) {
+    uint32_t r[32];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%32];\n\t"
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%33];\n\t"
+        "tcgen05.wait::ld.sync.aligned;"
+        : WLLM_R16(0), WLLM_R16(16)
+        : "r"(t0), "r"(t1)
+        : "memory");
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+        v0[i] = __uint_as_float(r[i]);
+        v1[i] = __uint_as_float(r[16 + i]);
+    }
+}
 #undef WLLM_R16
 
 // Shared-memory layout (from a 1024-byte aligned base): B stages (four hi+lo
-// activation boxes, then the sums box), raw slots, scale slots, barriers.
+// activation boxes, then the sums box unless the type has no mins), raw
+// slots, scale slots, barriers.
 struct Smem {
     uint32_t box_bytes, s_bytes, b_bytes, raw_bytes, v_bytes, nstb, nraw;
-    __host__ __device__ Smem(int nv, int bb, int nstb_, int nraw_) {
+    __host__ __device__ Smem(int nv, int bb, int nstb_, int nraw_, bool sums) {
         box_bytes = static_cast<uint32_t>(2 * nv * 128);  // hi + lo rows of one 64-element chunk
-        s_bytes = static_cast<uint32_t>(nv * 128);
+        s_bytes = sums ? static_cast<uint32_t>(nv * 128) : 0u;
         b_bytes = 4 * box_bytes + s_bytes;
         raw_bytes = static_cast<uint32_t>(kTM * bb);
         v_bytes = static_cast<uint32_t>(2 * nv * 4);  // the block's 2 nv scales
@@ -247,13 +279,63 @@ struct Smem {
     }
 };
 
+// Both f16 planes of Q8_0 block J of a row (272 bytes: eight 34-byte blocks,
+// an f16 d then 32 int8 quants): hi = f16(d q) and lo = d q - hi, exact
+// (ggml's dequantize_row_q8_0, w = d q), elements 16 qq .. 16 qq + 15 in
+// hw[qq] / lw[qq], f16 pairs in element order. The quants start a = 34 J + 2
+// bytes into the row; they are read as 16-byte words from a rounded down to
+// 16 (conflict-free at the 272-byte row stride) and shifted into place.
+template <int J>
+__device__ __forceinline__ void q8_block_planes(const uint8_t* row, uint32_t (&hw)[2][8], uint32_t (&lw)[2][8]) {
+    constexpr int a = 34 * J + 2, w0 = a & ~15, sh = a & 15;  // sh even: 0 .. 14
+    uint32_t win[12];
+#pragma unroll
+    for (int t = 0; t < 3; ++t) {
+        uint4 v = make_uint4(0u, 0u, 0u, 0u);
+        if (t < 2 || sh > 0) v = *reinterpret_cast<const uint4*>(row + w0 + 16 * t);
+        win[4 * t] = v.x;
+        win[4 * t + 1] = v.y;
+        win[4 * t + 2] = v.z;
+        win[4 * t + 3] = v.w;
+    }
+    const __half2 d2 = __half2half2(*reinterpret_cast<const __half*>(row + 34 * J));
+    const __half2 k1152 = __float2half2_rn(1152.f);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+        constexpr int q4 = sh >> 2;
+        const uint32_t w = (sh & 3) ? __funnelshift_r(win[q4 + k], win[q4 + k + 1], 16) : win[q4 + k];
+        // f16 1024 + (q + 128) for bytes (0, 1) and (2, 3), minus 1152: q exactly
+        const uint32_t u = w ^ 0x80808080u;
+        const uint32_t e01 = __byte_perm(u, 0x00006464u, 0x5140u), e23 = __byte_perm(u, 0x00006464u, 0x5342u);
+        const __half2 q01 = __hsub2(*reinterpret_cast<const __half2*>(&e01), k1152);
+        const __half2 q23 = __hsub2(*reinterpret_cast<const __half2*>(&e23), k1152);
+        const __half2 h01 = __hmul2(q01, d2), h23 = __hmul2(q23, d2);
+        const __half2 l01 = __hfma2(q01, d2, __hneg2(h01)), l23 = __hfma2(q23, d2, __hneg2(h23));
+        hw[k >> 2][2 * (k & 3)] = *reinterpret_cast<const uint32_t*>(&h01);
+        hw[k >> 2][2 * (k & 3) + 1] = *reinterpret_cast<const uint32_t*>(&h23);
+        lw[k >> 2][2 * (k & 3)] = *reinterpret_cast<const uint32_t*>(&l01);
+        lw[k >> 2][2 * (k & 3) + 1] = *reinterpret_cast<const uint32_t*>(&l23);
+    }
+}
+// Block 2 f + H of the row (this warp's block of chunk f).
+template <int H>
+__device__ __forceinline__ void q8_chunk_planes(const uint8_t* row, int f, uint32_t (&hw)[2][8], uint32_t (&lw)[2][8]) {
+    switch (f) {
+        case 0: q8_block_planes<H>(row, hw, lw); break;
+        case 1: q8_block_planes<2 + H>(row, hw, lw); break;
+        case 2: q8_block_planes<4 + H>(row, hw, lw); break;
+        default: q8_block_planes<6 + H>(row, hw, lw); break;
+    }
+}
+
 template <int TYPE>
 __global__ void __launch_bounds__(kThr, 1) btc_kernel(const __grid_constant__ BtcArgs P) {
     extern __shared__ __align__(128) uint8_t smem_raw[];
     uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     constexpr int BB = blk_bytes<TYPE>();
+    constexpr bool TWO = two_planes<TYPE>();
     const int nv = P.nv, nstb = P.nstb, nraw = P.nraw;
-    const Smem L(nv, BB, nstb, nraw);
+    const Smem L(nv, BB, nstb, nraw, !TWO);
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L.bar_off());
     uint64_t* b_full = bars;
     uint64_t* b_free = b_full + kMaxStB;
@@ -311,7 +393,7 @@ __global__ void __launch_bounds__(kThr, 1) btc_kernel(const __grid_constant__ Bt
         if (lane == 0) {
             asm volatile("prefetch.tensormap [%0];" ::"l"(&P.wmap) : "memory");
             asm volatile("prefetch.tensormap [%0];" ::"l"(&P.xmap) : "memory");
-            asm volatile("prefetch.tensormap [%0];" ::"l"(&P.smap) : "memory");
+            if (!TWO) asm volatile("prefetch.tensormap [%0];" ::"l"(&P.smap) : "memory");
             // the weights do not depend on the pre-pass: the first raw slots' boxes
             // go out before the wait for it (their barrier's arrival comes with the
             // scales, after the wait, so no phase can complete early)
@@ -341,7 +423,7 @@ __global__ void __launch_bounds__(kThr, 1) btc_kernel(const __grid_constant__ Bt
 #pragma unroll
                 for (int c = 0; c < 4; ++c)
                     tma_2d(dst + c * L.box_bytes, &P.xmap, kb * 256 + kChunk * c, grp * 2 * nv, &b_full[s]);
-                tma_2d(dst + 4 * L.box_bytes, &P.smap, 0, kb * P.groups * nv + grp * nv, &b_full[s]);
+                if (!TWO) tma_2d(dst + 4 * L.box_bytes, &P.smap, 0, kb * P.groups * nv + grp * nv, &b_full[s]);
                 issued = b + 1;
             }
             // before the CTA exits, the last copy into every slot and stage has
@@ -368,42 +450,78 @@ __global__ void __launch_bounds__(kThr, 1) btc_kernel(const __grid_constant__ Bt
             const uint32_t idesc_main =
                 (1u << 4) | (static_cast<uint32_t>((2 * nv) >> 3) << 17) | (static_cast<uint32_t>(kTM >> 4) << 24);
             const uint32_t idesc_min = (1u << 4) | (static_cast<uint32_t>(nv >> 3) << 17) | (static_cast<uint32_t>(kTM >> 4) << 24);
-            for (int b = i, u = 0; b < nblk; b += 2, ++u) {  // u: this issuer's block count (its phases)
-                const int s = b & (nstb - 1);
-                if (u >= 1 && !mbar_wait(&acc_free[i], (u - 1) & 1, 2u, poisoned)) break;
-                // the A stage comes in two halves (chunks 0-1, 2-3): the MMAs of the
-                // first overlap the dequantization of the second
-                if (!mbar_wait(&b_full[s], (b >> lgb) & 1, 2u, poisoned) ||
-                    !mbar_wait(&a_full[2 * i], u & 1, 2u, poisoned))
-                    break;
-                tc_fence_after();
-                const uint64_t bd = bdesc0 + (L.b_off(s) >> 4);
-                bool second = true;  // the second half arrived
+            if constexpr (TWO) {
+                // chunk f (64 K) of the block: both planes in half f & 1 of A stage i
+                // (hi at columns 0..31, lo at 32..63), use 2 u + f / 2 of that half
+                for (int b = i, u = 0; b < nblk; b += 2, ++u) {
+                    const int s = b & (nstb - 1);
+                    if (u >= 1 && !mbar_wait(&acc_free[i], (u - 1) & 1, 2u, poisoned)) break;
+                    if (!mbar_wait(&b_full[s], (b >> lgb) & 1, 2u, poisoned)) break;
+                    const uint64_t bd = bdesc0 + (L.b_off(s) >> 4);
+                    bool all = true;  // every chunk arrived
 #pragma unroll
-                for (int c = 0; c < 4; ++c) {
-                    if (c == 2) {
-                        umma_commit(&a_free[2 * i]);  // the first half is free once these have read it
-                        last_bar = &a_free[2 * i];
-                        last_par = static_cast<uint32_t>(u & 1);
-                        if (!mbar_wait(&a_full[2 * i + 1], u & 1, 2u, poisoned)) {
-                            second = false;
+                    for (int f = 0; f < 4; ++f) {
+                        const uint32_t use = static_cast<uint32_t>(2 * u + (f >> 1));
+                        if (!mbar_wait(&a_full[2 * i + (f & 1)], use & 1, 2u, poisoned)) {
+                            all = false;
                             break;
                         }
                         tc_fence_after();
-                        // the mins: A_min (K = 16, written with the second half) against the sums box
-                        umma_f16_ts(dmin, amin, bd + ((4 * L.box_bytes) >> 4), idesc_min, 0u);
-                    }
-                    const uint64_t bc = bd + ((c * L.box_bytes) >> 4);
+                        const uint64_t bc = bd + ((f * L.box_bytes) >> 4);
+                        const uint32_t ah = a0 + static_cast<uint32_t>(64 * (f & 1));
 #pragma unroll
-                    for (int ks = 0; ks < kChunk / 16; ++ks)  // K = 16 per MMA: 8 A columns, 32 bytes of B rows
-                        umma_f16_ts(dmain, a0 + 32 * c + 8 * ks, bc + 2 * ks, idesc_main, (c | ks) ? 1u : 0u);
+                        for (int ks = 0; ks < kChunk / 16; ++ks) {
+                            umma_f16_ts(dmain, ah + 8 * ks, bc + 2 * ks, idesc_main, (f | ks) ? 1u : 0u);
+                            umma_f16_ts(dmain, ah + 32 + 8 * ks, bc + 2 * ks, idesc_main, 1u);
+                        }
+                        umma_commit(&a_free[2 * i + (f & 1)]);
+                        last_bar = &a_free[2 * i + (f & 1)];
+                        last_par = use & 1;
+                    }
+                    if (!all) break;
+                    umma_commit(&b_free[s]);
+                    umma_commit(&acc_full[i]);
+                    last_bar = &acc_full[i];
+                    last_par = static_cast<uint32_t>(u & 1);
                 }
-                if (!second) break;  // the first half's MMAs are tracked by their commit
-                umma_commit(&a_free[2 * i + 1]);  // the second half, A_min and the B stage are read
-                umma_commit(&b_free[s]);
-                umma_commit(&acc_full[i]);
-                last_bar = &acc_full[i];
-                last_par = static_cast<uint32_t>(u & 1);
+            } else {
+                for (int b = i, u = 0; b < nblk; b += 2, ++u) {  // u: this issuer's block count (its phases)
+                    const int s = b & (nstb - 1);
+                    if (u >= 1 && !mbar_wait(&acc_free[i], (u - 1) & 1, 2u, poisoned)) break;
+                    // the A stage comes in two halves (chunks 0-1, 2-3): the MMAs of the
+                    // first overlap the dequantization of the second
+                    if (!mbar_wait(&b_full[s], (b >> lgb) & 1, 2u, poisoned) ||
+                        !mbar_wait(&a_full[2 * i], u & 1, 2u, poisoned))
+                        break;
+                    tc_fence_after();
+                    const uint64_t bd = bdesc0 + (L.b_off(s) >> 4);
+                    bool second = true;  // the second half arrived
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) {
+                        if (c == 2) {
+                            umma_commit(&a_free[2 * i]);  // the first half is free once these have read it
+                            last_bar = &a_free[2 * i];
+                            last_par = static_cast<uint32_t>(u & 1);
+                            if (!mbar_wait(&a_full[2 * i + 1], u & 1, 2u, poisoned)) {
+                                second = false;
+                                break;
+                            }
+                            tc_fence_after();
+                            // the mins: A_min (K = 16, written with the second half) against the sums box
+                            umma_f16_ts(dmin, amin, bd + ((4 * L.box_bytes) >> 4), idesc_min, 0u);
+                        }
+                        const uint64_t bc = bd + ((c * L.box_bytes) >> 4);
+#pragma unroll
+                        for (int ks = 0; ks < kChunk / 16; ++ks)  // K = 16 per MMA: 8 A columns, 32 bytes of B rows
+                            umma_f16_ts(dmain, a0 + 32 * c + 8 * ks, bc + 2 * ks, idesc_main, (c | ks) ? 1u : 0u);
+                    }
+                    if (!second) break;  // the first half's MMAs are tracked by their commit
+                    umma_commit(&a_free[2 * i + 1]);  // the second half, A_min and the B stage are read
+                    umma_commit(&b_free[s]);
+                    umma_commit(&acc_full[i]);
+                    last_bar = &acc_full[i];
+                    last_par = static_cast<uint32_t>(u & 1);
+                }
             }
             // a time-out: the MMAs already issued still write TMEM, which is freed
             // at the end; wait (bounded) for the last commit
@@ -419,103 +537,141 @@ __global__ void __launch_bounds__(kThr, 1) btc_kernel(const __grid_constant__ Bt
         const uint32_t sel_a = 0x4440u + static_cast<uint32_t>(h);      // byte h, zero-extended
         const uint32_t sel_b = 0x4440u + 2u + static_cast<uint32_t>(h);  // byte 2 + h
         const __half2 k1024 = __float2half2_rn(1024.f), km1024 = __float2half2_rn(-1024.f);
-        for (int b = 0; b < nblk; ++b) {
-            const int rs = b & (nraw - 1), i = b & 1;
-            if (!mbar_wait(&raw_full[rs], (b >> lgr) & 1, 3u, poisoned)) break;
-            const uint8_t* blk = smem + L.raw_off(rs) + r * BB;
-            // scales of this thread's sub-blocks j = 2p + h (p = 0..3), get_scale_min_k4
-            // (src/inference/jsep/ops/matmul.ts:408-424) on the bytes of the three scale words
-            const uint4 hdr = *reinterpret_cast<const uint4*>(blk);
-            const uint32_t w1a = __byte_perm(hdr.y, 0u, sel_a), w1b = __byte_perm(hdr.y, 0u, sel_b);
-            const uint32_t w3a = __byte_perm(hdr.w, 0u, sel_a), w3b = __byte_perm(hdr.w, 0u, sel_b);
-            const uint32_t scv[4] = {w1a & 63u, w1b & 63u, (w3a & 15u) | ((w1a >> 6) << 4),
-                                     (w3b & 15u) | ((w1b >> 6) << 4)};
-            // the block's quants (and Q5_K high bits), read before the stage wait
-            const uint4* qs = reinterpret_cast<const uint4*>(blk + (TYPE == kTypeQ5_K ? 48 : 16));
-            uint4 qv[8];
+        if constexpr (TWO) {
+            // Q8_0: chunk f is the row's Q8_0 blocks 2f and 2f + 1, this warp's
+            // 2f + h; both planes go to half f & 1 of A stage i (use 2 (b / 2) +
+            // f / 2 of it), hi at columns 16h .. 16h + 15, lo 32 further on
+            for (int b = 0; b < nblk; ++b) {
+                const int rs = b & (nraw - 1), i = b & 1;
+                if (!mbar_wait(&raw_full[rs], (b >> lgr) & 1, 3u, poisoned)) break;
+                const uint8_t* row = smem + L.raw_off(rs) + r * BB;
+                bool stop = false;
 #pragma unroll
-            for (int j = 0; j < 8; ++j) qv[j] = qs[j];
-            uint32_t hv[2][4] = {{0u, 0u, 0u, 0u}, {0u, 0u, 0u, 0u}};
-            if constexpr (TYPE == kTypeQ5_K) {
-#pragma unroll
-                for (int qq = 0; qq < 2; ++qq) {
-                    const uint4 t = *reinterpret_cast<const uint4*>(blk + 16 + 16 * qq);
-                    hv[qq][0] = t.x;
-                    hv[qq][1] = t.y;
-                    hv[qq][2] = t.z;
-                    hv[qq][3] = t.w;
-                }
-            }
-            // A stage i, half f (chunks 2f, 2f + 1; A_min with the second half) is
-            // free once issuer i's MMAs of block b - 2 have read it
-            const uint32_t acol = static_cast<uint32_t>(P.acol0 + kACols * i + 16 * h);
-            bool stop = false;
-#pragma unroll
-            for (int f = 0; f < 2; ++f) {
-                if (b >= 2 && !mbar_wait(&a_free[2 * i + f], ((b >> 1) - 1) & 1, 3u, poisoned)) {
-                    stop = true;
-                    break;
-                }
-                tc_fence_after();
-#pragma unroll
-                for (int pp = 0; pp < 2; ++pp) {
-                    const int p = 2 * f + pp;
-                    // A = sc q exactly: (1024 + q) sc - 1024 sc in one f16 FMA (the
-                    // exact result, at most 1953, is an f16 integer); sc itself as the
-                    // f16 (1024 + sc) - 1024, both halves
-                    const uint32_t sbits = 0x64006400u | (scv[p] * 0x00010001u);
-                    const __half2 sc2 = __hsub2(*reinterpret_cast<const __half2*>(&sbits), k1024);
-                    const __half2 mn2 = __hmul2(sc2, km1024);
+                for (int f = 0; f < 4; ++f) {
+                    uint32_t hw[2][8], lw[2][8];
+                    if (h == 0)
+                        q8_chunk_planes<0>(row, f, hw, lw);
+                    else
+                        q8_chunk_planes<1>(row, f, hw, lw);
+                    const uint32_t use = static_cast<uint32_t>(2 * (b >> 1) + (f >> 1));
+                    if (use >= 1 && !mbar_wait(&a_free[2 * i + (f & 1)], (use - 1) & 1, 3u, poisoned)) {
+                        stop = true;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t acol = static_cast<uint32_t>(P.acol0 + kACols * i + 64 * (f & 1) + 16 * h);
 #pragma unroll
                     for (int qq = 0; qq < 2; ++qq) {
-                        // bytes 16 qq .. 16 qq + 15 of pair p; this thread's quants are their
-                        // low (h = 0) or high (h = 1) nibbles: elements 64p + 32h + 16qq + l
-                        const uint4 v0 = qv[2 * p + qq];
-                        const uint32_t wv[4] = {v0.x, v0.y, v0.z, v0.w};
-                        uint32_t out[8];  // 16 f16, element order l = 0..15
-#pragma unroll
-                        for (int j = 0; j < 4; ++j) {
-                            uint32_t nib = (wv[j] >> (4 * h)) & 0x0F0F0F0Fu;
-                            if constexpr (TYPE == kTypeQ5_K) nib |= ((hv[qq][j] >> (2 * p + h)) & 0x01010101u) << 4;
-                            // f16 1024 + q (exact) for bytes (0, 1) and (2, 3): 0x64 in each high byte
-                            const uint32_t e01 = __byte_perm(nib, 0x00006464u, 0x5140u);
-                            const uint32_t e23 = __byte_perm(nib, 0x00006464u, 0x5342u);
-                            const __half2 w01 = __hfma2(*reinterpret_cast<const __half2*>(&e01), sc2, mn2);
-                            const __half2 w23 = __hfma2(*reinterpret_cast<const __half2*>(&e23), sc2, mn2);
-                            out[2 * j] = *reinterpret_cast<const uint32_t*>(&w01);
-                            out[2 * j + 1] = *reinterpret_cast<const uint32_t*>(&w23);
-                        }
-                        // k = 64p + 32h + 16qq + l of the block: TMEM columns 32p + 16h + 8qq .. +7 of A stage i
-                        tmem_st8(trow + acol + static_cast<uint32_t>(32 * p + 8 * qq), out);
+                        tmem_st8(trow + acol + static_cast<uint32_t>(8 * qq), hw[qq]);
+                        tmem_st8(trow + acol + static_cast<uint32_t>(32 + 8 * qq), lw[qq]);
                     }
+                    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&a_full[2 * i + (f & 1)]);
                 }
-                if (f == 1 && h == 0) {
-                    // A_min of this block: the eight 6-bit mins (get_scale_min_k4), twice,
-                    // as f16 pairs (k 0..7 meet the sums' hi parts, 8..15 their lo parts)
-                    const uint32_t mlo = hdr.z & 0x3F3F3F3Fu;                                                  // m_0..m_3
-                    const uint32_t mhi = ((hdr.w >> 4) & 0x0F0F0F0Fu) | (((hdr.z >> 6) & 0x03030303u) << 4);  // m_4..m_7
-                    uint32_t mm[4];
-                    const uint32_t mq[2] = {mlo, mhi};
-#pragma unroll
-                    for (int t = 0; t < 2; ++t) {
-                        const uint32_t e01 = __byte_perm(mq[t], 0x00006464u, 0x5140u);
-                        const uint32_t e23 = __byte_perm(mq[t], 0x00006464u, 0x5342u);
-                        const __half2 m01 = __hsub2(*reinterpret_cast<const __half2*>(&e01), k1024);
-                        const __half2 m23 = __hsub2(*reinterpret_cast<const __half2*>(&e23), k1024);
-                        mm[2 * t] = *reinterpret_cast<const uint32_t*>(&m01);
-                        mm[2 * t + 1] = *reinterpret_cast<const uint32_t*>(&m23);
-                    }
-                    const uint32_t amin[8] = {mm[0], mm[1], mm[2], mm[3], mm[0], mm[1], mm[2], mm[3]};
-                    tmem_st8(trow + mincol0 + static_cast<uint32_t>(8 * i), amin);
-                }
-                // one wait for the half's stores, then its arrival
-                asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&a_full[2 * i + f]);
+                if (stop) break;
+                if (lane == 0) mbar_arrive(&raw_free[rs]);
             }
-            if (stop) break;
-            if (lane == 0) mbar_arrive(&raw_free[rs]);
+        } else {
+            for (int b = 0; b < nblk; ++b) {
+                const int rs = b & (nraw - 1), i = b & 1;
+                if (!mbar_wait(&raw_full[rs], (b >> lgr) & 1, 3u, poisoned)) break;
+                const uint8_t* blk = smem + L.raw_off(rs) + r * BB;
+                // scales of this thread's sub-blocks j = 2p + h (p = 0..3), get_scale_min_k4
+                // (src/inference/jsep/ops/matmul.ts:408-424) on the bytes of the three scale words
+                const uint4 hdr = *reinterpret_cast<const uint4*>(blk);
+                const uint32_t w1a = __byte_perm(hdr.y, 0u, sel_a), w1b = __byte_perm(hdr.y, 0u, sel_b);
+                const uint32_t w3a = __byte_perm(hdr.w, 0u, sel_a), w3b = __byte_perm(hdr.w, 0u, sel_b);
+                const uint32_t scv[4] = {w1a & 63u, w1b & 63u, (w3a & 15u) | ((w1a >> 6) << 4),
+                                         (w3b & 15u) | ((w1b >> 6) << 4)};
+                // the block's quants (and Q5_K high bits), read before the stage wait
+                const uint4* qs = reinterpret_cast<const uint4*>(blk + (TYPE == kTypeQ5_K ? 48 : 16));
+                uint4 qv[8];
+#pragma unroll
+                for (int j = 0; j < 8; ++j) qv[j] = qs[j];
+                uint32_t hv[2][4] = {{0u, 0u, 0u, 0u}, {0u, 0u, 0u, 0u}};
+                if constexpr (TYPE == kTypeQ5_K) {
+#pragma unroll
+                    for (int qq = 0; qq < 2; ++qq) {
+                        const uint4 t = *reinterpret_cast<const uint4*>(blk + 16 + 16 * qq);
+                        hv[qq][0] = t.x;
+                        hv[qq][1] = t.y;
+                        hv[qq][2] = t.z;
+                        hv[qq][3] = t.w;
+                    }
+                }
+                // A stage i, half f (chunks 2f, 2f + 1; A_min with the second half) is
+                // free once issuer i's MMAs of block b - 2 have read it
+                const uint32_t acol = static_cast<uint32_t>(P.acol0 + kACols * i + 16 * h);
+                bool stop = false;
+#pragma unroll
+                for (int f = 0; f < 2; ++f) {
+                    if (b >= 2 && !mbar_wait(&a_free[2 * i + f], ((b >> 1) - 1) & 1, 3u, poisoned)) {
+                        stop = true;
+                        break;
+                    }
+                    tc_fence_after();
+#pragma unroll
+                    for (int pp = 0; pp < 2; ++pp) {
+                        const int p = 2 * f + pp;
+                        // A = sc q exactly: (1024 + q) sc - 1024 sc in one f16 FMA (the
+                        // exact result, at most 1953, is an f16 integer); sc itself as the
+                        // f16 (1024 + sc) - 1024, both halves
+                        const uint32_t sbits = 0x64006400u | (scv[p] * 0x00010001u);
+                        const __half2 sc2 = __hsub2(*reinterpret_cast<const __half2*>(&sbits), k1024);
+                        const __half2 mn2 = __hmul2(sc2, km1024);
+#pragma unroll
+                        for (int qq = 0; qq < 2; ++qq) {
+                            // bytes 16 qq .. 16 qq + 15 of pair p; this thread's quants are their
+                            // low (h = 0) or high (h = 1) nibbles: elements 64p + 32h + 16qq + l
+                            const uint4 v0 = qv[2 * p + qq];
+                            const uint32_t wv[4] = {v0.x, v0.y, v0.z, v0.w};
+                            uint32_t out[8];  // 16 f16, element order l = 0..15
+#pragma unroll
+                            for (int j = 0; j < 4; ++j) {
+                                uint32_t nib = (wv[j] >> (4 * h)) & 0x0F0F0F0Fu;
+                                if constexpr (TYPE == kTypeQ5_K) nib |= ((hv[qq][j] >> (2 * p + h)) & 0x01010101u) << 4;
+                                // f16 1024 + q (exact) for bytes (0, 1) and (2, 3): 0x64 in each high byte
+                                const uint32_t e01 = __byte_perm(nib, 0x00006464u, 0x5140u);
+                                const uint32_t e23 = __byte_perm(nib, 0x00006464u, 0x5342u);
+                                const __half2 w01 = __hfma2(*reinterpret_cast<const __half2*>(&e01), sc2, mn2);
+                                const __half2 w23 = __hfma2(*reinterpret_cast<const __half2*>(&e23), sc2, mn2);
+                                out[2 * j] = *reinterpret_cast<const uint32_t*>(&w01);
+                                out[2 * j + 1] = *reinterpret_cast<const uint32_t*>(&w23);
+                            }
+                            // k = 64p + 32h + 16qq + l of the block: TMEM columns 32p + 16h + 8qq .. +7 of A stage i
+                            tmem_st8(trow + acol + static_cast<uint32_t>(32 * p + 8 * qq), out);
+                        }
+                    }
+                    if (f == 1 && h == 0) {
+                        // A_min of this block: the eight 6-bit mins (get_scale_min_k4), twice,
+                        // as f16 pairs (k 0..7 meet the sums' hi parts, 8..15 their lo parts)
+                        const uint32_t mlo = hdr.z & 0x3F3F3F3Fu;                                                  // m_0..m_3
+                        const uint32_t mhi = ((hdr.w >> 4) & 0x0F0F0F0Fu) | (((hdr.z >> 6) & 0x03030303u) << 4);  // m_4..m_7
+                        uint32_t mm[4];
+                        const uint32_t mq[2] = {mlo, mhi};
+#pragma unroll
+                        for (int t = 0; t < 2; ++t) {
+                            const uint32_t e01 = __byte_perm(mq[t], 0x00006464u, 0x5140u);
+                            const uint32_t e23 = __byte_perm(mq[t], 0x00006464u, 0x5342u);
+                            const __half2 m01 = __hsub2(*reinterpret_cast<const __half2*>(&e01), k1024);
+                            const __half2 m23 = __hsub2(*reinterpret_cast<const __half2*>(&e23), k1024);
+                            mm[2 * t] = *reinterpret_cast<const uint32_t*>(&m01);
+                            mm[2 * t + 1] = *reinterpret_cast<const uint32_t*>(&m23);
+                        }
+                        const uint32_t amin[8] = {mm[0], mm[1], mm[2], mm[3], mm[0], mm[1], mm[2], mm[3]};
+                        tmem_st8(trow + mincol0 + static_cast<uint32_t>(8 * i), amin);
+                    }
+                    // one wait for the half's stores, then its arrival
+                    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&a_full[2 * i + f]);
+                }
+                if (stop) break;
+                if (lane == 0) mbar_arrive(&raw_free[rs]);
+            }
         }
     } else {
         // ---------------- epilogue ----------------
@@ -529,23 +685,37 @@ __global__ void __launch_bounds__(kThr, 1) btc_kernel(const __grid_constant__ Bt
         for (int j = 0; j < 16; ++j) yacc[j] = 0.f;
         for (int b = 0; b < nblk; ++b) {
             const int i = b & 1, rs = b & (nraw - 1);
-            // the block's d, dmin and scales first (they need only the raw slot)
+            // the block's d, dmin and scales first (they need only the raw slot);
+            // Q8_0's d is inside its weight planes
             if (!mbar_wait<64>(&raw_full[rs], (b >> lgr) & 1, 4u, poisoned)) break;
-            const uint32_t dm = *reinterpret_cast<const uint32_t*>(smem + L.raw_off(rs) + r * BB);
-            const float d = f16_bits_to_f32(dm), dmin = f16_bits_to_f32(dm >> 16);
+            float d = 1.f, dmin = 0.f;
+            if constexpr (!TWO) {
+                const uint32_t dm = *reinterpret_cast<const uint32_t*>(smem + L.raw_off(rs) + r * BB);
+                d = f16_bits_to_f32(dm);
+                dmin = f16_bits_to_f32(dm >> 16);
+            }
             const float* vs = reinterpret_cast<const float*>(smem + L.v_off(rs)) + n0;  // [2][nv] from vector n0
             if (!mbar_wait<64>(&acc_full[i], (b >> 1) & 1, 4u, poisoned)) break;
             tc_fence_after();
             float mv[16], lv[16], sv[16];
-            tmem_ld16x3(trow + static_cast<uint32_t>(accw * i + n0), trow + static_cast<uint32_t>(accw * i + nv + n0),
-                        trow + static_cast<uint32_t>(accw * i + 2 * nv + n0), mv, lv, sv);  // hi part, lo part, mins
+            if constexpr (TWO)
+                tmem_ld16x2(trow + static_cast<uint32_t>(accw * i + n0), trow + static_cast<uint32_t>(accw * i + nv + n0),
+                            mv, lv);  // hi part, lo part
+            else
+                tmem_ld16x3(trow + static_cast<uint32_t>(accw * i + n0), trow + static_cast<uint32_t>(accw * i + nv + n0),
+                            trow + static_cast<uint32_t>(accw * i + 2 * nv + n0), mv, lv, sv);  // hi part, lo part, mins
             // the accumulators are read: the issuer may start on block b + 2
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&acc_free[i]);
 #pragma unroll
-            for (int j = 0; j < 16; ++j)
-                if (j < nh) yacc[j] = fmaf(mv[j] + lv[j], d * vs[j], fmaf(-sv[j], dmin * vs[nv + j], yacc[j]));
+            for (int j = 0; j < 16; ++j) {
+                if (j >= nh) continue;
+                if constexpr (TWO)
+                    yacc[j] = fmaf(mv[j] + lv[j], vs[j], yacc[j]);
+                else
+                    yacc[j] = fmaf(mv[j] + lv[j], d * vs[j], fmaf(-sv[j], dmin * vs[nv + j], yacc[j]));
+            }
             __syncwarp();
             if (lane == 0) mbar_arrive(&raw_free[rs]);
         }
@@ -734,15 +904,17 @@ size_t split_bytes(const MulMatOp& o, int splits) {
     return align256(tiles * splits * kMaxNV * kTM * 4) + align256(tiles * 4);
 }
 
+int host_blk_bytes(int type) { return type == kTypeQ5_K ? 176 : (type == kTypeQ8_0 ? 272 : 144); }
+
 }  // namespace
 
 bool batched_tc_supported(const MulMatOp& o) {
-    if (o.type != kTypeQ4_K && o.type != kTypeQ5_K) return false;
+    if (o.type != kTypeQ4_K && o.type != kTypeQ5_K && o.type != kTypeQ8_0) return false;
     if (o.N < 1 || o.N > kMaxNP || o.ne2 != 1 || o.ne3 != 1) return false;
     if (o.K % 256 != 0 || o.M < 1) return false;
     // TMA rows: 16-byte aligned base and row stride
     if ((reinterpret_cast<uintptr_t>(o.w) | static_cast<uintptr_t>(o.w_nb1)) & 15) return false;
-    if (o.w_nb1 < static_cast<int64_t>(o.K / 256) * (o.type == kTypeQ5_K ? 176 : 144)) return false;
+    if (o.w_nb1 < static_cast<int64_t>(o.K / 256) * host_blk_bytes(o.type)) return false;
     if ((reinterpret_cast<uintptr_t>(o.x) | static_cast<uintptr_t>(o.x_nb1)) & 3) return false;
     return btc_encoder() != nullptr;
 }
@@ -769,7 +941,8 @@ int launch_batched_tc(const MulMatOp& o, void* workspace, size_t workspace_bytes
     cudaError_t e = cudaSuccess;
     BtcArgs P{};
     const EncodeFn enc = btc_encoder();
-    const int bb = o.type == kTypeQ5_K ? 176 : 144;
+    const int bb = host_blk_bytes(o.type);
+    const bool two = o.type == kTypeQ8_0;  // two weight planes, no mins
     const cuuint32_t es[2] = {1, 1};
     {
         const cuuint64_t dims[2] = {static_cast<cuuint64_t>(nblk) * (bb / 8), static_cast<cuuint64_t>(o.M)};
@@ -800,21 +973,21 @@ int launch_batched_tc(const MulMatOp& o, void* workspace, size_t workspace_bytes
     }
     // TMEM: per issuer the accumulators (an epilogue warp reads 16-column
     // groups from its first vector, nv / 2 of them: the columns cover the
-    // overhang), then A_min (8 columns each) and the two A stages from a
-    // 32-column boundary
+    // overhang; no mins columns for two-plane types), then A_min (8 columns
+    // each, K-quants) and the two A stages from a 32-column boundary
     {
         const int nh = nv / 2;
-        const int need = max(3 * nv, 2 * nv + nh + 16);
+        const int need = two ? max(2 * nv, nv + nh + 16) : max(3 * nv, 2 * nv + nh + 16);
         P.accw = (need + 31) / 32 * 32;
-        P.acol0 = (2 * P.accw + 16 + 31) / 32 * 32;
+        P.acol0 = (2 * P.accw + (two ? 0 : 16) + 31) / 32 * 32;
         if (P.acol0 + 2 * kACols > kTmemCols) return -static_cast<int>(cudaErrorInvalidValue);
     }
     // raw slots and B stages within 224 KB: 8 raw slots where 4 B stages still
     // fit, else 4 raw slots and as many B stages (4 or 2) as fit
     {
         const auto stages_with = [&](int nraw) {
-            const Smem s0(nv, bb, 0, nraw);
-            return static_cast<int>(((224u << 10) - s0.total()) / s0.b_bytes);
+            const Smem s0(nv, bb, 0, nraw, !two);
+            return (static_cast<int>(224u << 10) - static_cast<int>(s0.total())) / static_cast<int>(s0.b_bytes);
         };
         int nb = stages_with(8);
         P.nraw = 8;
@@ -843,13 +1016,14 @@ int launch_batched_tc(const MulMatOp& o, void* workspace, size_t workspace_bytes
     btc_prep_kernel<<<dim3(nblk, np / 8), 256, 0, stream>>>(o.x, o.x_nb1, ximg, simg, vscale, o.K, o.N, nv, groups,
                                                             P.counters, splits > 1 ? tiles : 0);
     if ((e = cudaGetLastError()) != cudaSuccess) return -static_cast<int>(e);
-    const size_t smem = Smem(nv, bb, P.nstb, P.nraw).total();
-    static size_t configured[kMaxDevices][2] = {};
+    const size_t smem = Smem(nv, bb, P.nstb, P.nraw, !two).total();
+    static size_t configured[kMaxDevices][3] = {};
     int dev = 0;
     if ((e = cudaGetDevice(&dev)) != cudaSuccess) return -static_cast<int>(e);
     if (dev < 0 || dev >= kMaxDevices) return -static_cast<int>(cudaErrorInvalidDevice);
-    const int ti = o.type == kTypeQ5_K ? 1 : 0;
-    void (*const kernel)(BtcArgs) = ti ? btc_kernel<kTypeQ5_K> : btc_kernel<kTypeQ4_K>;
+    const int ti = o.type == kTypeQ5_K ? 1 : (two ? 2 : 0);
+    void (*const kernel)(BtcArgs) =
+        ti == 1 ? btc_kernel<kTypeQ5_K> : (ti == 2 ? btc_kernel<kTypeQ8_0> : btc_kernel<kTypeQ4_K>);
     if (configured[dev][ti] < smem) {
         e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
         if (e != cudaSuccess) return -static_cast<int>(e);
