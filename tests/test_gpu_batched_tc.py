@@ -9,7 +9,10 @@ size (5000 x 4352, 4200 x 4608: partial row tiles, K = 17 and 18 blocks) keep
 those N on this kernel. Q8_0 goes in as two exact f16 weight planes (d q
 rounded to f16, and the remainder) and takes this kernel above 16 vectors
 (the integer mma.sync GEMM below); a test drives its scales through the f16
-subnormal range and up to 2^8."""
+subnormal range and up to 2^8. Q6_K (rows a multiple of 16 bytes: K a
+multiple of 2048) goes in as two planes of sc (q - 32), which reaches 4096,
+also above 16 vectors; a test sets its int8 scales to the extremes -128 and
+127 (at N = 8 on the mma.sync GEMM, at 24 and 40 here)."""
 from __future__ import annotations
 
 import zlib
@@ -61,7 +64,9 @@ def _kernels():
                                        (jsep.GGML_TYPE_Q4_K, 128, 256), (jsep.GGML_TYPE_Q4_K, 5000, 4352),
                                        (jsep.GGML_TYPE_Q5_K, 4200, 4608), (jsep.GGML_TYPE_Q8_0, 9216, 2304),
                                        (jsep.GGML_TYPE_Q8_0, 2304, 9216), (jsep.GGML_TYPE_Q8_0, 5000, 4352),
-                                       (jsep.GGML_TYPE_Q8_0, 128, 256)])
+                                       (jsep.GGML_TYPE_Q8_0, 128, 256), (jsep.GGML_TYPE_Q6_K, 4096, 14336),
+                                       (jsep.GGML_TYPE_Q6_K, 14336, 4096), (jsep.GGML_TYPE_Q6_K, 1000, 2048),
+                                       (jsep.GGML_TYPE_Q6_K, 5000, 6144)])
 def test_batched_tc_both_metrics(runtime, qtype, M, K, N):
     rng = np.random.default_rng(zlib.crc32(repr((qtype, M, K, N)).encode()))
     x = synth.activations(rng, N, K)
@@ -127,6 +132,41 @@ def test_batched_tc_q8_0_scale_range(runtime, N):
     assert _kernels() - k0 == 2
     wf = torch.empty(M, K, device=dev)
     jsep.dequantize_device(jsep.GGML_TYPE_Q8_0, wt.data_ptr(), wf.data_ptr(), M * K, stream)
+    runtime.jsep_sync()
+    r = (wf.double() @ xt.double().t()).t().cpu().numpy()
+    yy = y.double().cpu().numpy()
+    assert np.all(np.isfinite(yy))
+    a, b = O.rel_error(yy, r), O.rel_error_elem(yy, r)
+    assert a <= TOL and b <= TOL, (a, b)
+
+
+@pytest.mark.parametrize("N", [8, 24, 40])
+def test_batched_tc_q6_k_extreme_scales(runtime, N):
+    """Q6_K sub-block scales of -128 and 127 beside small ones: sc (q - 32)
+    then reaches 4096 in magnitude, where f16 holds only even integers, and the
+    second weight plane carries the odd remainder."""
+    import torch
+
+    M, K = 4096, 6144
+    rng = np.random.default_rng(99 + N)
+    w = synth.weights(rng, jsep.GGML_TYPE_Q6_K, M, K)
+    blocks = w.reshape(M, K // 256, 210)
+    choice = rng.integers(0, 3, size=(M, K // 256, 16))
+    sc = np.where(choice == 0, -128, np.where(choice == 1, 127, rng.integers(-5, 6, size=choice.shape)))
+    blocks[:, :, 192:208] = sc.astype(np.int8).view(np.uint8)
+    x = synth.activations(rng, N, K)
+    dev = torch.device("cuda", 0)
+    wt = torch.from_numpy(w).to(dev)
+    xt = torch.from_numpy(x).to(dev)
+    y = torch.full((N, M), float("nan"), device=dev)
+    torch.cuda.synchronize()
+    stream = jsep.library_stream()
+    k0 = _kernels()
+    assert jsep.mul_mat_device(jsep.GGML_TYPE_Q6_K, wt.data_ptr(), wt.shape[1], xt.data_ptr(), K, y.data_ptr(), M, M,
+                               K, N, stream) == jsep.STATUS_OK, jsep.last_error()
+    assert _kernels() - k0 == 2
+    wf = torch.empty(M, K, device=dev)
+    jsep.dequantize_device(jsep.GGML_TYPE_Q6_K, wt.data_ptr(), wf.data_ptr(), M * K, stream)
     runtime.jsep_sync()
     r = (wf.double() @ xt.double().t()).t().cpu().numpy()
     yy = y.double().cpu().numpy()

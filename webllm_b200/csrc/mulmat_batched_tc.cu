@@ -1,5 +1,5 @@
-// Small-batch quantized MUL_MAT on tcgen05 tensor cores for Q4_K, Q5_K and
-// Q8_0 weights (several sequences decoding together: N up to 64 vectors),
+// Small-batch quantized MUL_MAT on tcgen05 tensor cores for Q4_K, Q5_K, Q6_K
+// and Q8_0 weights (several sequences decoding together: N up to 64 vectors),
 // exact to about 2^-22 of every activation element, like the integer decode
 // kernels.
 //
@@ -30,7 +30,10 @@
 // on hi's grid, never below f16's smallest subnormal, so it is exact), each
 // against the same activations: the accumulator gets sum (hi + lo) x, and the
 // epilogue scales it by 2^e only. Chunk by chunk (64 K), both planes of a
-// chunk share one half of the A stage.
+// chunk share one half of the A stage. Q6_K (w = d sc (q - 32), int8 sc per
+// 16 elements) takes the same two planes for A = sc (q - 32), which reaches
+// 4096 in magnitude where f16 holds only even integers (lo is 0 or +-1), with
+// d applied per block in the epilogue.
 //
 // One thread issues a tcgen05.mma in about 50 cycles and waits on an mbarrier
 // in about 150, whatever the MMA's N (16 to 128), so at these sizes the issue
@@ -105,15 +108,24 @@ struct BtcArgs {
     unsigned* counters;   // [tile] (split K, zero at launch)
 };
 
-// Bytes per row of one 256-element block: Q4_K 144, Q5_K 176, Q8_0 272 (8 blocks).
+// Bytes per row of one 256-element block in a raw slot: Q4_K 144, Q5_K 176,
+// Q8_0 272 (8 blocks), Q6_K 240 (the 210-byte block from its start rounded
+// down to 16: at most 14 + 210 bytes, a 16-byte multiple).
 template <int TYPE>
 __host__ __device__ constexpr int blk_bytes() {
-    return TYPE == kTypeQ5_K ? 176 : (TYPE == kTypeQ8_0 ? 272 : 144);
+    return TYPE == kTypeQ5_K ? 176 : (TYPE == kTypeQ8_0 ? 272 : (TYPE == kTypeQ6_K ? 240 : 144));
 }
-// Q8_0 weights go in as two f16 planes (no mins, no sums box).
+// Q8_0 and Q6_K weights go in as two f16 planes (no mins, no sums box).
 template <int TYPE>
 __host__ __device__ constexpr bool two_planes() {
-    return TYPE == kTypeQ8_0;
+    return TYPE == kTypeQ8_0 || TYPE == kTypeQ6_K;
+}
+// The weight box's x coordinate for K block kb: Q6_K rows are mapped in bytes
+// (the block's start rounded down to 16), the others in uint64 words.
+template <int TYPE>
+__device__ __forceinline__ int raw_box_x(int kb) {
+    if constexpr (TYPE == kTypeQ6_K) return (kb * 210) & ~15;
+    return kb * (blk_bytes<TYPE>() / 8);
 }
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -328,6 +340,64 @@ __device__ __forceinline__ void q8_chunk_planes(const uint8_t* row, int f, uint3
     }
 }
 
+// 16 bytes at byte o + c of a Q6_K box row (c a multiple of 16, o the block's
+// offset: even, the same for every row of the block), from the two aligned
+// 16-byte words at c: a word select by o / 4 (q4), then a funnel shift by
+// 8 (o % 4) bits (sh).
+__device__ __forceinline__ uint4 q6_load16(const uint8_t* row, int c, int q4, uint32_t sh) {
+    const uint4* a = reinterpret_cast<const uint4*>(row + c);
+    const uint4 lo = a[0], hi = (q4 | sh) ? a[1] : lo;  // an aligned piece needs no second word
+    const uint32_t w[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
+    uint32_t v[5];
+#pragma unroll
+    for (int i = 0; i < 5; ++i) v[i] = q4 == 0 ? w[i] : (q4 == 1 ? w[i + 1] : (q4 == 2 ? w[i + 2] : w[i + 3]));
+    return make_uint4(__funnelshift_r(v[0], v[1], sh), __funnelshift_r(v[1], v[2], sh), __funnelshift_r(v[2], v[3], sh),
+                      __funnelshift_r(v[3], v[4], sh));
+}
+
+// Both f16 planes of chunk f (64 elements) of a Q6_K block, this warp's half
+// h (ggml's dequantize_row_q6_K layout): element 64f + 32h + 16qq + l is in
+// half n = f / 2 of the block, j = 2 (f % 2) + h: ql byte 64n + 32h + 16qq + l
+// (its high nibble when f is odd), qh byte 128 + 32n + 16qq + l shifted by
+// 2j, int8 scale 192 + 8n + 2j + qq; w = d sc (q - 32). A = sc (q - 32)
+// reaches 4096 in magnitude, one bit past f16's exact integers, so it goes in
+// as hi = f16(A) and lo = A - hi (0 or +-1); d is applied per block when the
+// accumulator is read. ql and qh serve both chunks of a half: loaded when f
+// is even. o: the block's offset in its 240-byte box row (q4 = o / 4,
+// sh = 8 (o % 4)).
+__device__ __forceinline__ void q6_chunk_planes(const uint8_t* row, int f, int h, int o, int q4, uint32_t sh,
+                                                uint4 (&ql)[2], uint4 (&qh)[2], uint32_t (&hw)[2][8],
+                                                uint32_t (&lw)[2][8]) {
+    const int n = f >> 1, t = f & 1, j = 2 * t + h;
+    if (t == 0) {
+#pragma unroll
+        for (int qq = 0; qq < 2; ++qq) {
+            ql[qq] = q6_load16(row, 64 * n + 32 * h + 16 * qq, q4, sh);
+            qh[qq] = q6_load16(row, 128 + 32 * n + 16 * qq, q4, sh);
+        }
+    }
+    const __half2 k1056 = __float2half2_rn(1056.f);
+#pragma unroll
+    for (int qq = 0; qq < 2; ++qq) {
+        const __half2 sc2 = __half2half2(__int2half_rn(static_cast<int8_t>(row[o + 192 + 8 * n + 2 * j + qq])));
+        const uint32_t lq[4] = {ql[qq].x, ql[qq].y, ql[qq].z, ql[qq].w}, hq[4] = {qh[qq].x, qh[qq].y, qh[qq].z, qh[qq].w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const uint32_t qv = ((lq[i] >> (4 * t)) & 0x0F0F0F0Fu) | (((hq[i] >> (2 * j)) & 0x03030303u) << 4);
+            // f16 1024 + q (exact, q < 64), minus 1056: q - 32 exactly
+            const uint32_t e01 = __byte_perm(qv, 0x00006464u, 0x5140u), e23 = __byte_perm(qv, 0x00006464u, 0x5342u);
+            const __half2 v01 = __hsub2(*reinterpret_cast<const __half2*>(&e01), k1056);
+            const __half2 v23 = __hsub2(*reinterpret_cast<const __half2*>(&e23), k1056);
+            const __half2 h01 = __hmul2(v01, sc2), h23 = __hmul2(v23, sc2);
+            const __half2 l01 = __hfma2(v01, sc2, __hneg2(h01)), l23 = __hfma2(v23, sc2, __hneg2(h23));
+            hw[qq][2 * i] = *reinterpret_cast<const uint32_t*>(&h01);
+            hw[qq][2 * i + 1] = *reinterpret_cast<const uint32_t*>(&h23);
+            lw[qq][2 * i] = *reinterpret_cast<const uint32_t*>(&l01);
+            lw[qq][2 * i + 1] = *reinterpret_cast<const uint32_t*>(&l23);
+        }
+    }
+}
+
 template <int TYPE>
 __global__ void __launch_bounds__(kThr, 1) btc_kernel(const __grid_constant__ BtcArgs P) {
     extern __shared__ __align__(128) uint8_t smem_raw[];
@@ -400,7 +470,7 @@ __global__ void __launch_bounds__(kThr, 1) btc_kernel(const __grid_constant__ Bt
             const int pre = min(nblk, nraw);
             for (int b = 0; b < pre; ++b) {
                 mbar_expect_tx_only(&raw_full[b], L.raw_bytes);
-                tma_2d(smem + L.raw_off(b), &P.wmap, (kb0 + b) * (BB / 8), m0, &raw_full[b]);
+                tma_2d(smem + L.raw_off(b), &P.wmap, raw_box_x<TYPE>(kb0 + b), m0, &raw_full[b]);
             }
             asm volatile("griddepcontrol.wait;" ::: "memory");
             int armed = 0;   // blocks whose raw slot copies are all issued and armed
@@ -410,7 +480,7 @@ __global__ void __launch_bounds__(kThr, 1) btc_kernel(const __grid_constant__ Bt
                 if (b >= nraw) {
                     if (!mbar_wait<64>(&raw_free[r], ((b >> lgr) - 1) & 1, 1u, poisoned)) break;
                     mbar_expect_tx(&raw_full[r], L.raw_bytes + L.v_bytes);
-                    tma_2d(smem + L.raw_off(r), &P.wmap, kb * (BB / 8), m0, &raw_full[r]);
+                    tma_2d(smem + L.raw_off(r), &P.wmap, raw_box_x<TYPE>(kb), m0, &raw_full[r]);
                 } else {
                     mbar_expect_tx(&raw_full[r], L.v_bytes);
                 }
@@ -538,18 +608,26 @@ __global__ void __launch_bounds__(kThr, 1) btc_kernel(const __grid_constant__ Bt
         const uint32_t sel_b = 0x4440u + 2u + static_cast<uint32_t>(h);  // byte 2 + h
         const __half2 k1024 = __float2half2_rn(1024.f), km1024 = __float2half2_rn(-1024.f);
         if constexpr (TWO) {
-            // Q8_0: chunk f is the row's Q8_0 blocks 2f and 2f + 1, this warp's
-            // 2f + h; both planes go to half f & 1 of A stage i (use 2 (b / 2) +
-            // f / 2 of it), hi at columns 16h .. 16h + 15, lo 32 further on
+            // two planes per chunk f (64 K): Q8_0's blocks 2f and 2f + 1 (this
+            // warp's 2f + h), Q6_K's elements 64f + 32h .. +31; both planes go to
+            // half f & 1 of A stage i (use 2 (b / 2) + f / 2 of it), hi at columns
+            // 16h .. 16h + 15, lo 32 further on
             for (int b = 0; b < nblk; ++b) {
                 const int rs = b & (nraw - 1), i = b & 1;
                 if (!mbar_wait(&raw_full[rs], (b >> lgr) & 1, 3u, poisoned)) break;
                 const uint8_t* row = smem + L.raw_off(rs) + r * BB;
+                // Q6_K: the block starts o = 210 kb mod 16 bytes into its box row
+                const int o = TYPE == kTypeQ6_K ? ((kb0 + b) * 210) & 15 : 0;
+                const int q4 = o >> 2;
+                const uint32_t sh = 8u * static_cast<uint32_t>(o & 3);
+                uint4 ql[2], qh[2];
                 bool stop = false;
 #pragma unroll
                 for (int f = 0; f < 4; ++f) {
                     uint32_t hw[2][8], lw[2][8];
-                    if (h == 0)
+                    if constexpr (TYPE == kTypeQ6_K)
+                        q6_chunk_planes(row, f, h, o, q4, sh, ql, qh, hw, lw);
+                    else if (h == 0)
                         q8_chunk_planes<0>(row, f, hw, lw);
                     else
                         q8_chunk_planes<1>(row, f, hw, lw);
@@ -686,10 +764,13 @@ __global__ void __launch_bounds__(kThr, 1) btc_kernel(const __grid_constant__ Bt
         for (int b = 0; b < nblk; ++b) {
             const int i = b & 1, rs = b & (nraw - 1);
             // the block's d, dmin and scales first (they need only the raw slot);
-            // Q8_0's d is inside its weight planes
+            // Q8_0's d is inside its weight planes, Q6_K's at byte 208 of the block
             if (!mbar_wait<64>(&raw_full[rs], (b >> lgr) & 1, 4u, poisoned)) break;
             float d = 1.f, dmin = 0.f;
-            if constexpr (!TWO) {
+            if constexpr (TYPE == kTypeQ6_K) {
+                const int o = ((kb0 + b) * 210) & 15;
+                d = __half2float(*reinterpret_cast<const __half*>(smem + L.raw_off(rs) + r * BB + o + 208));
+            } else if constexpr (!TWO) {
                 const uint32_t dm = *reinterpret_cast<const uint32_t*>(smem + L.raw_off(rs) + r * BB);
                 d = f16_bits_to_f32(dm);
                 dmin = f16_bits_to_f32(dm >> 16);
@@ -712,7 +793,7 @@ __global__ void __launch_bounds__(kThr, 1) btc_kernel(const __grid_constant__ Bt
             for (int j = 0; j < 16; ++j) {
                 if (j >= nh) continue;
                 if constexpr (TWO)
-                    yacc[j] = fmaf(mv[j] + lv[j], vs[j], yacc[j]);
+                    yacc[j] = fmaf(mv[j] + lv[j], d * vs[j], yacc[j]);
                 else
                     yacc[j] = fmaf(mv[j] + lv[j], d * vs[j], fmaf(-sv[j], dmin * vs[nv + j], yacc[j]));
             }
@@ -904,17 +985,22 @@ size_t split_bytes(const MulMatOp& o, int splits) {
     return align256(tiles * splits * kMaxNV * kTM * 4) + align256(tiles * 4);
 }
 
-int host_blk_bytes(int type) { return type == kTypeQ5_K ? 176 : (type == kTypeQ8_0 ? 272 : 144); }
+// Bytes per row of one 256-element block in a raw slot, and in the weights.
+int host_blk_bytes(int type) {
+    return type == kTypeQ5_K ? 176 : (type == kTypeQ8_0 ? 272 : (type == kTypeQ6_K ? 240 : 144));
+}
+int row_blk_bytes(int type) { return type == kTypeQ6_K ? 210 : host_blk_bytes(type); }
 
 }  // namespace
 
 bool batched_tc_supported(const MulMatOp& o) {
-    if (o.type != kTypeQ4_K && o.type != kTypeQ5_K && o.type != kTypeQ8_0) return false;
+    if (o.type != kTypeQ4_K && o.type != kTypeQ5_K && o.type != kTypeQ8_0 && o.type != kTypeQ6_K) return false;
     if (o.N < 1 || o.N > kMaxNP || o.ne2 != 1 || o.ne3 != 1) return false;
     if (o.K % 256 != 0 || o.M < 1) return false;
     // TMA rows: 16-byte aligned base and row stride
     if ((reinterpret_cast<uintptr_t>(o.w) | static_cast<uintptr_t>(o.w_nb1)) & 15) return false;
-    if (o.w_nb1 < static_cast<int64_t>(o.K / 256) * host_blk_bytes(o.type)) return false;
+    if (o.w_nb1 < static_cast<int64_t>(o.K / 256) * row_blk_bytes(o.type)) return false;
+    if (o.type == kTypeQ6_K && o.K < 512) return false;  // the 240-byte box stays within a row's width
     if ((reinterpret_cast<uintptr_t>(o.x) | static_cast<uintptr_t>(o.x_nb1)) & 3) return false;
     return btc_encoder() != nullptr;
 }
@@ -942,13 +1028,16 @@ int launch_batched_tc(const MulMatOp& o, void* workspace, size_t workspace_bytes
     BtcArgs P{};
     const EncodeFn enc = btc_encoder();
     const int bb = host_blk_bytes(o.type);
-    const bool two = o.type == kTypeQ8_0;  // two weight planes, no mins
+    const bool two = o.type == kTypeQ8_0 || o.type == kTypeQ6_K;  // two weight planes, no mins
+    const bool q6 = o.type == kTypeQ6_K;  // rows mapped in bytes, 240-byte boxes
     const cuuint32_t es[2] = {1, 1};
     {
-        const cuuint64_t dims[2] = {static_cast<cuuint64_t>(nblk) * (bb / 8), static_cast<cuuint64_t>(o.M)};
+        const cuuint64_t dims[2] = {q6 ? static_cast<cuuint64_t>(nblk) * 210 : static_cast<cuuint64_t>(nblk) * (bb / 8),
+                                    static_cast<cuuint64_t>(o.M)};
         const cuuint64_t strides[1] = {static_cast<cuuint64_t>(o.w_nb1)};
-        const cuuint32_t box[2] = {static_cast<cuuint32_t>(bb / 8), static_cast<cuuint32_t>(kTM)};
-        if (enc(&P.wmap, CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, const_cast<uint8_t*>(o.w), dims, strides, box, es,
+        const cuuint32_t box[2] = {static_cast<cuuint32_t>(q6 ? bb : bb / 8), static_cast<cuuint32_t>(kTM)};
+        if (enc(&P.wmap, q6 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, const_cast<uint8_t*>(o.w),
+                dims, strides, box, es,
                 CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
             return -static_cast<int>(cudaErrorInvalidValue);
@@ -1017,13 +1106,14 @@ int launch_batched_tc(const MulMatOp& o, void* workspace, size_t workspace_bytes
                                                             P.counters, splits > 1 ? tiles : 0);
     if ((e = cudaGetLastError()) != cudaSuccess) return -static_cast<int>(e);
     const size_t smem = Smem(nv, bb, P.nstb, P.nraw, !two).total();
-    static size_t configured[kMaxDevices][3] = {};
+    static size_t configured[kMaxDevices][4] = {};
     int dev = 0;
     if ((e = cudaGetDevice(&dev)) != cudaSuccess) return -static_cast<int>(e);
     if (dev < 0 || dev >= kMaxDevices) return -static_cast<int>(cudaErrorInvalidDevice);
-    const int ti = o.type == kTypeQ5_K ? 1 : (two ? 2 : 0);
+    const int ti = o.type == kTypeQ5_K ? 1 : (o.type == kTypeQ8_0 ? 2 : (q6 ? 3 : 0));
     void (*const kernel)(BtcArgs) =
-        ti == 1 ? btc_kernel<kTypeQ5_K> : (ti == 2 ? btc_kernel<kTypeQ8_0> : btc_kernel<kTypeQ4_K>);
+        ti == 1 ? btc_kernel<kTypeQ5_K>
+                : (ti == 2 ? btc_kernel<kTypeQ8_0> : (ti == 3 ? btc_kernel<kTypeQ6_K> : btc_kernel<kTypeQ4_K>));
     if (configured[dev][ti] < smem) {
         e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
         if (e != cudaSuccess) return -static_cast<int>(e);
