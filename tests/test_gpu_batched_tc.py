@@ -11,8 +11,8 @@ rounded to f16, and the remainder) and takes this kernel above 16 vectors
 (the integer mma.sync GEMM below); a test drives its scales through the f16
 subnormal range and up to 2^8. Q6_K (rows a multiple of 16 bytes: K a
 multiple of 2048) goes in as two planes of sc (q - 32), which reaches 4096,
-also above 16 vectors; a test sets its int8 scales to the extremes -128 and
-127 (at N = 8 on the mma.sync GEMM, at 24 and 40 here)."""
+with the Q4_K routing (below 4096 x 4096 only above 16 vectors); a test sets
+its int8 scales to the extremes -128 and 127."""
 from __future__ import annotations
 
 import zlib

@@ -340,19 +340,35 @@ __device__ __forceinline__ void q8_chunk_planes(const uint8_t* row, int f, uint3
     }
 }
 
-// 16 bytes at byte o + c of a Q6_K box row (c a multiple of 16, o the block's
-// offset: even, the same for every row of the block), from the two aligned
-// 16-byte words at c: a word select by o / 4 (q4), then a funnel shift by
-// 8 (o % 4) bits (sh).
-__device__ __forceinline__ uint4 q6_load16(const uint8_t* row, int c, int q4, uint32_t sh) {
+// 16 bytes at byte O + c of a Q6_K box row (c a multiple of 16, O the block's
+// offset, even, known at compile time): from the aligned 16-byte words at c,
+// the words from O / 4 on, funnel-shifted by 8 (O % 4) bits.
+template <int O>
+__device__ __forceinline__ uint4 q6_load16(const uint8_t* row, int c) {
+    constexpr int q4 = O >> 2;
+    constexpr uint32_t sh = 8u * (O & 3);
     const uint4* a = reinterpret_cast<const uint4*>(row + c);
-    const uint4 lo = a[0], hi = (q4 | sh) ? a[1] : lo;  // an aligned piece needs no second word
-    const uint32_t w[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
-    uint32_t v[5];
+    const uint4 lo = a[0];
+    if constexpr (O == 0) {
+        return lo;
+    } else {
+        const uint4 hi = a[1];
+        const uint32_t w[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
+        if constexpr (sh == 0)
+            return make_uint4(w[q4], w[q4 + 1], w[q4 + 2], w[q4 + 3]);
+        else
+            return make_uint4(__funnelshift_r(w[q4], w[q4 + 1], sh), __funnelshift_r(w[q4 + 1], w[q4 + 2], sh),
+                              __funnelshift_r(w[q4 + 2], w[q4 + 3], sh), __funnelshift_r(w[q4 + 3], w[q4 + 4], sh));
+    }
+}
+// This thread's ql and qh bytes of half n of a Q6_K block at offset O.
+template <int O>
+__device__ __forceinline__ void q6_half_loads(const uint8_t* row, int n, int h, uint4 (&ql)[2], uint4 (&qh)[2]) {
 #pragma unroll
-    for (int i = 0; i < 5; ++i) v[i] = q4 == 0 ? w[i] : (q4 == 1 ? w[i + 1] : (q4 == 2 ? w[i + 2] : w[i + 3]));
-    return make_uint4(__funnelshift_r(v[0], v[1], sh), __funnelshift_r(v[1], v[2], sh), __funnelshift_r(v[2], v[3], sh),
-                      __funnelshift_r(v[3], v[4], sh));
+    for (int qq = 0; qq < 2; ++qq) {
+        ql[qq] = q6_load16<O>(row, 64 * n + 32 * h + 16 * qq);
+        qh[qq] = q6_load16<O>(row, 128 + 32 * n + 16 * qq);
+    }
 }
 
 // Both f16 planes of chunk f (64 elements) of a Q6_K block, this warp's half
@@ -363,17 +379,21 @@ __device__ __forceinline__ uint4 q6_load16(const uint8_t* row, int c, int q4, ui
 // reaches 4096 in magnitude, one bit past f16's exact integers, so it goes in
 // as hi = f16(A) and lo = A - hi (0 or +-1); d is applied per block when the
 // accumulator is read. ql and qh serve both chunks of a half: loaded when f
-// is even. o: the block's offset in its 240-byte box row (q4 = o / 4,
-// sh = 8 (o % 4)).
-__device__ __forceinline__ void q6_chunk_planes(const uint8_t* row, int f, int h, int o, int q4, uint32_t sh,
-                                                uint4 (&ql)[2], uint4 (&qh)[2], uint32_t (&hw)[2][8],
-                                                uint32_t (&lw)[2][8]) {
+// is even. o: the block's offset in its 240-byte box row (2 kb mod 16, the
+// same for every row: one uniform branch to the loads for that offset).
+__device__ __forceinline__ void q6_chunk_planes(const uint8_t* row, int f, int h, int o, uint4 (&ql)[2],
+                                                uint4 (&qh)[2], uint32_t (&hw)[2][8], uint32_t (&lw)[2][8]) {
     const int n = f >> 1, t = f & 1, j = 2 * t + h;
     if (t == 0) {
-#pragma unroll
-        for (int qq = 0; qq < 2; ++qq) {
-            ql[qq] = q6_load16(row, 64 * n + 32 * h + 16 * qq, q4, sh);
-            qh[qq] = q6_load16(row, 128 + 32 * n + 16 * qq, q4, sh);
+        switch (o) {
+            case 0: q6_half_loads<0>(row, n, h, ql, qh); break;
+            case 2: q6_half_loads<2>(row, n, h, ql, qh); break;
+            case 4: q6_half_loads<4>(row, n, h, ql, qh); break;
+            case 6: q6_half_loads<6>(row, n, h, ql, qh); break;
+            case 8: q6_half_loads<8>(row, n, h, ql, qh); break;
+            case 10: q6_half_loads<10>(row, n, h, ql, qh); break;
+            case 12: q6_half_loads<12>(row, n, h, ql, qh); break;
+            default: q6_half_loads<14>(row, n, h, ql, qh); break;
         }
     }
     const __half2 k1056 = __float2half2_rn(1056.f);
@@ -618,15 +638,13 @@ __global__ void __launch_bounds__(kThr, 1) btc_kernel(const __grid_constant__ Bt
                 const uint8_t* row = smem + L.raw_off(rs) + r * BB;
                 // Q6_K: the block starts o = 210 kb mod 16 bytes into its box row
                 const int o = TYPE == kTypeQ6_K ? ((kb0 + b) * 210) & 15 : 0;
-                const int q4 = o >> 2;
-                const uint32_t sh = 8u * static_cast<uint32_t>(o & 3);
                 uint4 ql[2], qh[2];
                 bool stop = false;
 #pragma unroll
                 for (int f = 0; f < 4; ++f) {
                     uint32_t hw[2][8], lw[2][8];
                     if constexpr (TYPE == kTypeQ6_K)
-                        q6_chunk_planes(row, f, h, o, q4, sh, ql, qh, hw, lw);
+                        q6_chunk_planes(row, f, h, o, ql, qh, hw, lw);
                     else if (h == 0)
                         q8_chunk_planes<0>(row, f, hw, lw);
                     else
