@@ -328,8 +328,9 @@ def batched_measure(dev, reps: int = 10, warmup: int = 3):
     """Several sequences decoding together (N = 1 .. 64) on three weights:
     Gemma-2-2B ffn_up (Q8_0 9216x2304), Llama-3-8B ffn_gate (Q4_K 14336x4096)
     and ffn_down (Q6_K 4096x14336). N = 1, 2 run the streaming GEMV; the
-    Q4_K shape at N >= 8 the tcgen05 small-batch GEMM, the others the integer
-    tensor-core (mma.sync) batched GEMM. Distinct weight copies (over 2x the
+    K-quant shapes at N >= 8 and the Q8_0 shape above 16 vectors the tcgen05
+    small-batch GEMM, the Q8_0 shape at N = 8, 16 the integer tensor-core
+    (mma.sync) batched GEMM. Distinct weight copies (over 2x the
     L2) rotate between launches so every launch streams its weights from HBM.
     Returns the JSON object: the Q8_0 shape at the top level, the K-quant
     shapes under "kquant"."""
@@ -388,9 +389,9 @@ def batched_measure(dev, reps: int = 10, warmup: int = 3):
                     "per_n": per})
     res = dict(out[0])
     res["kquant"] = out[1:]
-    res["note"] = ("N <= 2: streaming GEMV; Q4_K N >= 5 (N >= 16 at 4096x4096 and below): tcgen05 small-batch GEMM; "
-                   "other N >= 3: integer tensor-core batched GEMM (mma.sync); activation pre-passes included; "
-                   "launches timed inside a CUDA graph")
+    res["note"] = ("N <= 2: streaming GEMV; Q4_K/Q6_K N >= 5 (N >= 16 at 4096x4096 and below) and Q8_0 N > 16: "
+                   "tcgen05 small-batch GEMM; Q8_0 N = 3..16: integer tensor-core batched GEMM (mma.sync); "
+                   "activation pre-passes included; launches timed inside a CUDA graph")
     return res
 
 
