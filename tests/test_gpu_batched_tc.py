@@ -12,7 +12,9 @@ rounded to f16, and the remainder) and takes this kernel above 16 vectors
 subnormal range and up to 2^8. Q6_K (rows a multiple of 16 bytes: K a
 multiple of 2048) goes in as two planes of sc (q - 32), which reaches 4096,
 with the Q4_K routing (below 4096 x 4096 only above 16 vectors); a test sets
-its int8 scales to the extremes -128 and 127."""
+its int8 scales to the extremes -128 and 127. Above 32 vectors both two-plane
+types run their two vector groups in one CTA (N = 33, 40, 64 here, with and
+without split K)."""
 from __future__ import annotations
 
 import zlib

@@ -41,7 +41,10 @@
 // rate. The kernel is laid out for that:
 //
 // CTA: 128 rows x nv vectors (nv = 16 or 32; N > 32 runs two vector groups as
-// grid y). Per block everything moves as one unit:
+// grid y, except the two-plane types, whose CTA then takes both groups: its
+// issuer i MMAs group i of every block from the one dequantized A stage, into
+// two accumulators of its own by block parity). Per block everything moves as
+// one unit:
 //  - warp 0 (TMA): the 128 rows' raw blocks and the block's scales into a raw
 //    slot (4 slots); the block's four hi+lo activation boxes (64 x 2 nv,
 //    128-byte swizzle) and its sums box into a B stage (2 or 4 stages);
@@ -74,7 +77,8 @@ namespace {
 
 constexpr int kTM = 128;      // rows of W per CTA (TMEM lanes)
 constexpr int kMaxNP = 64;    // vectors per launch
-constexpr int kMaxNV = 32;    // vectors per CTA
+constexpr int kMaxNV = 32;    // vectors per vector group
+constexpr int kMaxVPC = 64;   // vectors per CTA (two groups in a wide CTA)
 constexpr int kChunk = 64;    // K per activation box (one 128-byte swizzle atom of f16)
 constexpr int kMaxStB = 4;    // B stages (blocks of activations), at most
 constexpr int kMaxRaw = 8;    // raw blocks in flight, at most (8, or 4 where B stages need the room)
@@ -100,11 +104,12 @@ struct BtcArgs {
     float* y;
     int64_t y_nb1;        // bytes between output vectors
     int32_t M, K, N;
-    int32_t nv, groups;   // vectors per CTA, vector groups (grid y)
+    int32_t nv, groups;   // vectors per group, vector groups (grid y, or both in one wide CTA)
+    int32_t wide;         // two-plane types above 32 vectors: one CTA, issuer i takes group i of every block
     int32_t nstb, nraw;   // B stages (2 or 4), raw slots (4 or 8)
     int32_t accw, acol0;  // TMEM columns of one issuer's accumulators; first A column
     int32_t splits, kb_split;
-    float* partial;       // [tile][split][kMaxNV][128] (split K)
+    float* partial;       // [tile][split][kMaxVPC][128] (split K)
     unsigned* counters;   // [tile] (split K, zero at launch)
 };
 
@@ -263,18 +268,35 @@ __device__ __forceinline__ void tmem_ld16x2(uint32_t t0, uint32_t t1, float (&v0
     }
 }
 #undef WLLM_R16
+// 8 f32 columns at each of two column addresses, one wait.
+__device__ __forceinline__ void tmem_ld8x2(uint32_t t0, uint32_t t1, float (&v0)[8], float (&v1)[8]) {
+    uint32_t r[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%16];\n\t"
+        "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%8,%9,%10,%11,%12,%13,%14,%15}, [%17];\n\t"
+        "tcgen05.wait::ld.sync.aligned;"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+          "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(t0), "r"(t1)
+        : "memory");
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        v0[i] = __uint_as_float(r[i]);
+        v1[i] = __uint_as_float(r[8 + i]);
+    }
+}
 
 // Shared-memory layout (from a 1024-byte aligned base): B stages (four hi+lo
 // activation boxes, then the sums box unless the type has no mins), raw
 // slots, scale slots, barriers.
 struct Smem {
     uint32_t box_bytes, s_bytes, b_bytes, raw_bytes, v_bytes, nstb, nraw;
-    __host__ __device__ Smem(int nv, int bb, int nstb_, int nraw_, bool sums) {
+    __host__ __device__ Smem(int nv, int bb, int nstb_, int nraw_, bool sums, bool wide) {
         box_bytes = static_cast<uint32_t>(2 * nv * 128);  // hi + lo rows of one 64-element chunk
         s_bytes = sums ? static_cast<uint32_t>(nv * 128) : 0u;
-        b_bytes = 4 * box_bytes + s_bytes;
+        b_bytes = (wide ? 8u : 4u) * box_bytes + s_bytes;  // wide: chunk c of group g at box 2c + g
         raw_bytes = static_cast<uint32_t>(kTM * bb);
-        v_bytes = static_cast<uint32_t>(2 * nv * 4);  // the block's 2 nv scales
+        v_bytes = static_cast<uint32_t>((wide ? 2 : 1) * 2 * nv * 4);  // the block's 2 nv scales per group
         nstb = static_cast<uint32_t>(nstb_);
         nraw = static_cast<uint32_t>(nraw_);
     }
@@ -283,9 +305,10 @@ struct Smem {
     __host__ __device__ uint32_t v_off(int r) const { return nstb * b_bytes + nraw * raw_bytes + r * v_bytes; }
     __host__ __device__ uint32_t bar_off() const { return nstb * b_bytes + nraw * (raw_bytes + v_bytes); }
     // barriers: b_full, b_free [kMaxStB], raw_full, raw_free [kMaxRaw], a_full,
-    // a_free [4] (A stage i, half f at 2 i + f), acc_full, acc_free [2]; then
-    // the TMEM base address word and the poison flag
-    static constexpr uint32_t kBars = 2 * kMaxStB + 2 * kMaxRaw + 12;
+    // a_free [4] (A stage i, half f at 2 i + f), acc_full, acc_free [4] (issuer
+    // i's accumulator, wide: 2 i + block parity); then the TMEM base address
+    // word and the poison flag
+    static constexpr uint32_t kBars = 2 * kMaxStB + 2 * kMaxRaw + 16;
     __host__ __device__ uint32_t total() const {
         return bar_off() + 8 * kBars + 16 + 1024;  // + alignment slack
     }
@@ -418,14 +441,17 @@ __device__ __forceinline__ void q6_chunk_planes(const uint8_t* row, int f, int h
     }
 }
 
-template <int TYPE>
+// WIDE (two-plane types above 32 vectors, P.wide set): both vector groups in
+// one CTA, a separate instantiation so the others carry none of its code.
+template <int TYPE, bool WIDE>
 __global__ void __launch_bounds__(kThr, 1) btc_kernel(const __grid_constant__ BtcArgs P) {
     extern __shared__ __align__(128) uint8_t smem_raw[];
     uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     constexpr int BB = blk_bytes<TYPE>();
     constexpr bool TWO = two_planes<TYPE>();
     const int nv = P.nv, nstb = P.nstb, nraw = P.nraw;
-    const Smem L(nv, BB, nstb, nraw, !TWO);
+    constexpr bool wide = TWO && WIDE;
+    const Smem L(nv, BB, nstb, nraw, !TWO, wide);
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L.bar_off());
     uint64_t* b_full = bars;
     uint64_t* b_free = b_full + kMaxStB;
@@ -434,8 +460,8 @@ __global__ void __launch_bounds__(kThr, 1) btc_kernel(const __grid_constant__ Bt
     uint64_t* a_full = raw_free + kMaxRaw;
     uint64_t* a_free = a_full + 4;
     uint64_t* acc_full = a_free + 4;
-    uint64_t* acc_free = acc_full + 2;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_free + 2);
+    uint64_t* acc_free = acc_full + 4;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_free + 4);
     volatile int* poisoned = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -449,7 +475,7 @@ __global__ void __launch_bounds__(kThr, 1) btc_kernel(const __grid_constant__ Bt
     if (threadIdx.x == 0) {
         for (int i = 0; i < kMaxStB; ++i) {
             mbar_init(&b_full[i], 1);
-            mbar_init(&b_free[i], 1);
+            mbar_init(&b_free[i], wide ? 2 : 1);  // wide: both issuers read every stage
         }
         for (int r = 0; r < kMaxRaw; ++r) {
             mbar_init(&raw_full[r], 1);
@@ -457,11 +483,11 @@ __global__ void __launch_bounds__(kThr, 1) btc_kernel(const __grid_constant__ Bt
         }
         for (int p = 0; p < 4; ++p) {
             mbar_init(&a_full[p], kDq);
-            mbar_init(&a_free[p], 1);
+            mbar_init(&a_free[p], wide ? 2 : 1);
         }
-        for (int p = 0; p < 2; ++p) {
+        for (int p = 0; p < 4; ++p) {
             mbar_init(&acc_full[p], 1);
-            mbar_init(&acc_free[p], kEp);
+            mbar_init(&acc_free[p], wide ? kEp / 2 : kEp);  // wide: the four epilogue warps of the group
         }
         *poisoned = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -477,7 +503,7 @@ __global__ void __launch_bounds__(kThr, 1) btc_kernel(const __grid_constant__ Bt
     const uint32_t tmem = *tmem_slot;
 
     const int lgb = nstb == 4 ? 2 : 1;  // log2 of the B stages (2 or 4)
-    const int lgr = nraw == 8 ? 3 : 2;  // log2 of the raw slots (4 or 8)
+    const int lgr = nraw == 8 ? 3 : (nraw == 4 ? 2 : 1);  // log2 of the raw slots (2, 4 or 8)
     if (warp == 0) {
         // ---------------- TMA producer ----------------
         if (lane == 0) {
@@ -505,14 +531,20 @@ __global__ void __launch_bounds__(kThr, 1) btc_kernel(const __grid_constant__ Bt
                     mbar_expect_tx(&raw_full[r], L.v_bytes);
                 }
                 bulk_copy(smem + L.v_off(r), P.vscale + (static_cast<int64_t>(kb) * P.groups + grp) * 2 * nv, L.v_bytes,
-                          &raw_full[r]);
+                          &raw_full[r]);  // wide: both groups' scales (grp = 0)
                 armed = b + 1;
                 if (b >= nstb && !mbar_wait<64>(&b_free[s], ((b >> lgb) - 1) & 1, 1u, poisoned)) break;
                 uint8_t* dst = smem + L.b_off(s);
                 mbar_expect_tx(&b_full[s], L.b_bytes);
+                if constexpr (wide) {
 #pragma unroll
-                for (int c = 0; c < 4; ++c)
-                    tma_2d(dst + c * L.box_bytes, &P.xmap, kb * 256 + kChunk * c, grp * 2 * nv, &b_full[s]);
+                    for (int c = 0; c < 8; ++c)
+                        tma_2d(dst + c * L.box_bytes, &P.xmap, kb * 256 + kChunk * (c >> 1), (c & 1) * 2 * nv, &b_full[s]);
+                } else {
+#pragma unroll
+                    for (int c = 0; c < 4; ++c)
+                        tma_2d(dst + c * L.box_bytes, &P.xmap, kb * 256 + kChunk * c, grp * 2 * nv, &b_full[s]);
+                }
                 if (!TWO) tma_2d(dst + 4 * L.box_bytes, &P.smap, 0, kb * P.groups * nv + grp * nv, &b_full[s]);
                 issued = b + 1;
             }
@@ -541,6 +573,45 @@ __global__ void __launch_bounds__(kThr, 1) btc_kernel(const __grid_constant__ Bt
                 (1u << 4) | (static_cast<uint32_t>((2 * nv) >> 3) << 17) | (static_cast<uint32_t>(kTM >> 4) << 24);
             const uint32_t idesc_min = (1u << 4) | (static_cast<uint32_t>(nv >> 3) << 17) | (static_cast<uint32_t>(kTM >> 4) << 24);
             if constexpr (TWO) {
+              if constexpr (wide) {
+                // every block, vector group i, into accumulator 2 i + (b & 1); the
+                // block's A stage (b & 1) and B stage are shared with the other
+                // issuer, whose commits the barriers also count
+                for (int b = 0; b < nblk; ++b) {
+                    const int s = b & (nstb - 1), q = b & 1, ai = 2 * i + q;
+                    const uint32_t u = static_cast<uint32_t>(b >> 1);  // uses of this accumulator and A stage
+                    const uint32_t dw = tmem + static_cast<uint32_t>(accw * ai);
+                    if (b >= 2 && !mbar_wait(&acc_free[ai], (u - 1) & 1, 2u, poisoned)) break;
+                    if (!mbar_wait(&b_full[s], (b >> lgb) & 1, 2u, poisoned)) break;
+                    const uint64_t bd = bdesc0 + (L.b_off(s) >> 4);
+                    const uint32_t aq = tmem + static_cast<uint32_t>(P.acol0 + kACols * q);
+                    bool all = true;  // every chunk arrived
+#pragma unroll
+                    for (int f = 0; f < 4; ++f) {
+                        const uint32_t use = 2 * u + static_cast<uint32_t>(f >> 1);
+                        if (!mbar_wait(&a_full[2 * q + (f & 1)], use & 1, 2u, poisoned)) {
+                            all = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        const uint64_t bc = bd + (((2 * f + i) * L.box_bytes) >> 4);
+                        const uint32_t ah = aq + static_cast<uint32_t>(64 * (f & 1));
+#pragma unroll
+                        for (int ks = 0; ks < kChunk / 16; ++ks) {
+                            umma_f16_ts(dw, ah + 8 * ks, bc + 2 * ks, idesc_main, (f | ks) ? 1u : 0u);
+                            umma_f16_ts(dw, ah + 32 + 8 * ks, bc + 2 * ks, idesc_main, 1u);
+                        }
+                        umma_commit(&a_free[2 * q + (f & 1)]);
+                    }
+                    // (after a time-out, the accumulator's barrier, counted once, still
+                    // tracks every MMA issued for the drain below)
+                    if (all) umma_commit(&b_free[s]);
+                    umma_commit(&acc_full[ai]);
+                    last_bar = &acc_full[ai];
+                    last_par = u & 1;
+                    if (!all) break;
+                }
+              } else {
                 // chunk f (64 K) of the block: both planes in half f & 1 of A stage i
                 // (hi at columns 0..31, lo at 32..63), use 2 u + f / 2 of that half
                 for (int b = i, u = 0; b < nblk; b += 2, ++u) {
@@ -574,6 +645,7 @@ __global__ void __launch_bounds__(kThr, 1) btc_kernel(const __grid_constant__ Bt
                     last_bar = &acc_full[i];
                     last_par = static_cast<uint32_t>(u & 1);
                 }
+              }
             } else {
                 for (int b = i, u = 0; b < nblk; b += 2, ++u) {  // u: this issuer's block count (its phases)
                     const int s = b & (nstb - 1);
@@ -772,106 +844,197 @@ __global__ void __launch_bounds__(kThr, 1) btc_kernel(const __grid_constant__ Bt
     } else {
         // ---------------- epilogue ----------------
         const int quarter = warp & 3;
-        const int ep = (warp - kFirstEp) >> 2;  // half of the group's vectors
         const int r = 32 * quarter + lane;
         const uint32_t trow = tmem + (static_cast<uint32_t>(32 * quarter) << 16);
-        const int nh = nv / 2, n0 = ep * nh;  // this warp's vectors (8 or 16)
-        float yacc[16];
+        if constexpr (TWO) {
+          if constexpr (wide) {
+            // wide: the four warps of group g = (warp - kFirstEp) / 4 read issuer
+            // g's accumulator of every block, all 32 of the group's vectors
+            const int g = (warp - kFirstEp) >> 2;
+            float ya[32];
 #pragma unroll
-        for (int j = 0; j < 16; ++j) yacc[j] = 0.f;
-        for (int b = 0; b < nblk; ++b) {
-            const int i = b & 1, rs = b & (nraw - 1);
-            // the block's d, dmin and scales first (they need only the raw slot);
-            // Q8_0's d is inside its weight planes, Q6_K's at byte 208 of the block
-            if (!mbar_wait<64>(&raw_full[rs], (b >> lgr) & 1, 4u, poisoned)) break;
-            float d = 1.f, dmin = 0.f;
-            if constexpr (TYPE == kTypeQ6_K) {
-                const int o = ((kb0 + b) * 210) & 15;
-                d = __half2float(*reinterpret_cast<const __half*>(smem + L.raw_off(rs) + r * BB + o + 208));
-            } else if constexpr (!TWO) {
-                const uint32_t dm = *reinterpret_cast<const uint32_t*>(smem + L.raw_off(rs) + r * BB);
-                d = f16_bits_to_f32(dm);
-                dmin = f16_bits_to_f32(dm >> 16);
-            }
-            const float* vs = reinterpret_cast<const float*>(smem + L.v_off(rs)) + n0;  // [2][nv] from vector n0
-            if (!mbar_wait<64>(&acc_full[i], (b >> 1) & 1, 4u, poisoned)) break;
-            tc_fence_after();
-            float mv[16], lv[16], sv[16];
-            if constexpr (TWO)
-                tmem_ld16x2(trow + static_cast<uint32_t>(accw * i + n0), trow + static_cast<uint32_t>(accw * i + nv + n0),
-                            mv, lv);  // hi part, lo part
-            else
-                tmem_ld16x3(trow + static_cast<uint32_t>(accw * i + n0), trow + static_cast<uint32_t>(accw * i + nv + n0),
-                            trow + static_cast<uint32_t>(accw * i + 2 * nv + n0), mv, lv, sv);  // hi part, lo part, mins
-            // the accumulators are read: the issuer may start on block b + 2
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&acc_free[i]);
+            for (int j = 0; j < 32; ++j) ya[j] = 0.f;
+            for (int b = 0; b < nblk; ++b) {
+                const int rs = b & (nraw - 1), ai = 2 * g + (b & 1);
+                if (!mbar_wait<64>(&raw_full[rs], (b >> lgr) & 1, 4u, poisoned)) break;
+                float d = 1.f;
+                if constexpr (TYPE == kTypeQ6_K) {
+                    const int o = ((kb0 + b) * 210) & 15;
+                    d = __half2float(*reinterpret_cast<const __half*>(smem + L.raw_off(rs) + r * BB + o + 208));
+                }
+                const float* vs = reinterpret_cast<const float*>(smem + L.v_off(rs)) + g * 2 * nv;  // group g's scales
+                if (!mbar_wait<64>(&acc_full[ai], (b >> 1) & 1, 4u, poisoned)) break;
+                tc_fence_after();
 #pragma unroll
-            for (int j = 0; j < 16; ++j) {
-                if (j >= nh) continue;
-                if constexpr (TWO)
-                    yacc[j] = fmaf(mv[j] + lv[j], d * vs[j], yacc[j]);
-                else
-                    yacc[j] = fmaf(mv[j] + lv[j], d * vs[j], fmaf(-sv[j], dmin * vs[nv + j], yacc[j]));
+                for (int hh = 0; hh < 4; ++hh) {  // 8 vectors at a time (registers)
+                    float mv[8], lv[8];
+                    tmem_ld8x2(trow + static_cast<uint32_t>(accw * ai + 8 * hh),
+                               trow + static_cast<uint32_t>(accw * ai + nv + 8 * hh), mv, lv);  // hi part, lo part
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) ya[8 * hh + j] = fmaf(mv[j] + lv[j], d * vs[8 * hh + j], ya[8 * hh + j]);
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&acc_free[ai]);
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&raw_free[rs]);
             }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&raw_free[rs]);
+            const int row = m0 + r, tile = blockIdx.x;
+            if (P.splits == 1) {
+                if (row < P.M) {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        const int n = 32 * g + j;
+                        if (n < P.N)
+                            *reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(P.y) + n * P.y_nb1 + 4LL * row) = ya[j];
+                    }
+                }
+            } else {
+                float* ptile = P.partial + (static_cast<int64_t>(tile) * P.splits + blockIdx.z) * (kMaxVPC * kTM);
+#pragma unroll
+                for (int j = 0; j < 32; ++j) ptile[(32 * g + j) * kTM + r] = ya[j];
+                // the tile's last split sums all of them in split order, as below
+                __shared__ int last_w;
+                asm volatile("bar.sync 1, %0;" ::"n"(kEp * 32) : "memory");
+                if (threadIdx.x == 32 * kFirstEp) {
+                    __threadfence();
+                    const unsigned add = 1u + (*poisoned ? 0x10000u : 0u);
+                    const unsigned old = atomicAdd(P.counters + tile, add);
+                    last_w = (old & 0xFFFFu) == static_cast<unsigned>(P.splits - 1);
+                    if (last_w) {
+                        if ((old + add) >> 16) last_w = 0;
+                        P.counters[tile] = 0u;
+                        __threadfence();
+                    }
+                }
+                asm volatile("bar.sync 1, %0;" ::"n"(kEp * 32) : "memory");
+                if (last_w) {
+                    // thread t sums elements t + 256 k (k < 32: 64 vectors) over the
+                    // splits, 16 at a time
+                    const float* base = P.partial + static_cast<int64_t>(tile) * P.splits * (kMaxVPC * kTM);
+                    const int t = threadIdx.x - 32 * kFirstEp;
+#pragma unroll 1
+                    for (int part = 0; part < 2; ++part) {
+                        float acc[16];
+#pragma unroll
+                        for (int k = 0; k < 16; ++k) acc[k] = 0.f;
+                        for (int z = 0; z < P.splits; ++z) {
+                            const float* src = base + z * (kMaxVPC * kTM) + t + kEp * 32 * 16 * part;
+#pragma unroll
+                            for (int k = 0; k < 16; ++k) acc[k] += __ldcg(src + kEp * 32 * k);
+                        }
+#pragma unroll
+                        for (int k = 0; k < 16; ++k) {
+                            const int e = t + kEp * 32 * (16 * part + k), n = e / kTM, rr = e - n * kTM;
+                            if (n < P.N && m0 + rr < P.M)
+                                *reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(P.y) + n * P.y_nb1 + 4LL * (m0 + rr)) =
+                                    acc[k];
+                        }
+                    }
+                }
+            }
+          }
         }
-        // ---------------- outputs ----------------
-        const int row = m0 + r;
-        const int nbase = grp * nv;  // first vector of this group
-        const int tile = blockIdx.y * gridDim.x + blockIdx.x;
-        if (P.splits == 1) {
-            if (row < P.M) {
+        if constexpr (!wide) {
+            const int ep = (warp - kFirstEp) >> 2;  // half of the group's vectors
+            const int nh = nv / 2, n0 = ep * nh;  // this warp's vectors (8 or 16)
+            float yacc[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) yacc[j] = 0.f;
+            for (int b = 0; b < nblk; ++b) {
+                const int i = b & 1, rs = b & (nraw - 1);
+                // the block's d, dmin and scales first (they need only the raw slot);
+                // Q8_0's d is inside its weight planes, Q6_K's at byte 208 of the block
+                if (!mbar_wait<64>(&raw_full[rs], (b >> lgr) & 1, 4u, poisoned)) break;
+                float d = 1.f, dmin = 0.f;
+                if constexpr (TYPE == kTypeQ6_K) {
+                    const int o = ((kb0 + b) * 210) & 15;
+                    d = __half2float(*reinterpret_cast<const __half*>(smem + L.raw_off(rs) + r * BB + o + 208));
+                } else if constexpr (!TWO) {
+                    const uint32_t dm = *reinterpret_cast<const uint32_t*>(smem + L.raw_off(rs) + r * BB);
+                    d = f16_bits_to_f32(dm);
+                    dmin = f16_bits_to_f32(dm >> 16);
+                }
+                const float* vs = reinterpret_cast<const float*>(smem + L.v_off(rs)) + n0;  // [2][nv] from vector n0
+                if (!mbar_wait<64>(&acc_full[i], (b >> 1) & 1, 4u, poisoned)) break;
+                tc_fence_after();
+                float mv[16], lv[16], sv[16];
+                if constexpr (TWO)
+                    tmem_ld16x2(trow + static_cast<uint32_t>(accw * i + n0), trow + static_cast<uint32_t>(accw * i + nv + n0),
+                                mv, lv);  // hi part, lo part
+                else
+                    tmem_ld16x3(trow + static_cast<uint32_t>(accw * i + n0), trow + static_cast<uint32_t>(accw * i + nv + n0),
+                                trow + static_cast<uint32_t>(accw * i + 2 * nv + n0), mv, lv, sv);  // hi part, lo part, mins
+                // the accumulators are read: the issuer may start on block b + 2
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&acc_free[i]);
 #pragma unroll
                 for (int j = 0; j < 16; ++j) {
-                    const int n = nbase + n0 + j;
-                    if (j < nh && n < P.N)
-                        *reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(P.y) + n * P.y_nb1 + 4LL * row) = yacc[j];
+                    if (j >= nh) continue;
+                    if constexpr (TWO)
+                        yacc[j] = fmaf(mv[j] + lv[j], d * vs[j], yacc[j]);
+                    else
+                        yacc[j] = fmaf(mv[j] + lv[j], d * vs[j], fmaf(-sv[j], dmin * vs[nv + j], yacc[j]));
                 }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&raw_free[rs]);
             }
-        } else {
-            float* ptile = P.partial + (static_cast<int64_t>(tile) * P.splits + blockIdx.z) * (kMaxNV * kTM);
+            // ---------------- outputs ----------------
+            const int row = m0 + r;
+            const int nbase = grp * nv;  // first vector of this group
+            const int tile = blockIdx.y * gridDim.x + blockIdx.x;
+            if (P.splits == 1) {
+                if (row < P.M) {
 #pragma unroll
-            for (int j = 0; j < 16; ++j)
-                if (j < nh) ptile[(n0 + j) * kTM + r] = yacc[j];
-            // the tile's last split sums all of them in split order (deterministic);
-            // a split that gave up waiting counts in the high half and nobody sums
-            __shared__ int last;
-            asm volatile("bar.sync 1, %0;" ::"n"(kEp * 32) : "memory");
-            if (threadIdx.x == 32 * kFirstEp) {
-                __threadfence();
-                const unsigned add = 1u + (*poisoned ? 0x10000u : 0u);
-                const unsigned old = atomicAdd(P.counters + tile, add);
-                last = (old & 0xFFFFu) == static_cast<unsigned>(P.splits - 1);
-                if (last) {
-                    if ((old + add) >> 16) last = 0;
-                    P.counters[tile] = 0u;
+                    for (int j = 0; j < 16; ++j) {
+                        const int n = nbase + n0 + j;
+                        if (j < nh && n < P.N)
+                            *reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(P.y) + n * P.y_nb1 + 4LL * row) = yacc[j];
+                    }
+                }
+            } else {
+                float* ptile = P.partial + (static_cast<int64_t>(tile) * P.splits + blockIdx.z) * (kMaxVPC * kTM);
+#pragma unroll
+                for (int j = 0; j < 16; ++j)
+                    if (j < nh) ptile[(n0 + j) * kTM + r] = yacc[j];
+                // the tile's last split sums all of them in split order (deterministic);
+                // a split that gave up waiting counts in the high half and nobody sums
+                __shared__ int last;
+                asm volatile("bar.sync 1, %0;" ::"n"(kEp * 32) : "memory");
+                if (threadIdx.x == 32 * kFirstEp) {
                     __threadfence();
+                    const unsigned add = 1u + (*poisoned ? 0x10000u : 0u);
+                    const unsigned old = atomicAdd(P.counters + tile, add);
+                    last = (old & 0xFFFFu) == static_cast<unsigned>(P.splits - 1);
+                    if (last) {
+                        if ((old + add) >> 16) last = 0;
+                        P.counters[tile] = 0u;
+                        __threadfence();
+                    }
                 }
-            }
-            asm volatile("bar.sync 1, %0;" ::"n"(kEp * 32) : "memory");
-            if (last) {
-                // thread t sums elements t + 256 k (k < nv / 2) over the splits, in
-                // split order, with each split's loads issued together
-                const float* base = P.partial + static_cast<int64_t>(tile) * P.splits * (kMaxNV * kTM);
-                const int t = threadIdx.x - 32 * kFirstEp, per = nv * kTM / (kEp * 32);
-                float acc[kMaxNV * kTM / (kEp * 32)];
+                asm volatile("bar.sync 1, %0;" ::"n"(kEp * 32) : "memory");
+                if (last) {
+                    // thread t sums elements t + 256 k (k < nv / 2) over the splits, in
+                    // split order, with each split's loads issued together
+                    const float* base = P.partial + static_cast<int64_t>(tile) * P.splits * (kMaxVPC * kTM);
+                    const int t = threadIdx.x - 32 * kFirstEp, per = nv * kTM / (kEp * 32);
+                    float acc[kMaxNV * kTM / (kEp * 32)];
 #pragma unroll
-                for (int k = 0; k < kMaxNV * kTM / (kEp * 32); ++k) acc[k] = 0.f;
-                for (int z = 0; z < P.splits; ++z) {
-                    const float* src = base + z * (kMaxNV * kTM) + t;
+                    for (int k = 0; k < kMaxNV * kTM / (kEp * 32); ++k) acc[k] = 0.f;
+                    for (int z = 0; z < P.splits; ++z) {
+                        const float* src = base + z * (kMaxVPC * kTM) + t;
 #pragma unroll
-                    for (int k = 0; k < kMaxNV * kTM / (kEp * 32); ++k)
-                        if (k < per) acc[k] += __ldcg(src + kEp * 32 * k);
-                }
+                        for (int k = 0; k < kMaxNV * kTM / (kEp * 32); ++k)
+                            if (k < per) acc[k] += __ldcg(src + kEp * 32 * k);
+                    }
 #pragma unroll
-                for (int k = 0; k < kMaxNV * kTM / (kEp * 32); ++k) {
-                    const int e = t + kEp * 32 * k, n = e / kTM, rr = e - n * kTM;
-                    if (k < per && nbase + n < P.N && m0 + rr < P.M)
-                        *reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(P.y) + (nbase + n) * P.y_nb1 + 4LL * (m0 + rr)) =
-                            acc[k];
+                    for (int k = 0; k < kMaxNV * kTM / (kEp * 32); ++k) {
+                        const int e = t + kEp * 32 * k, n = e / kTM, rr = e - n * kTM;
+                        if (k < per && nbase + n < P.N && m0 + rr < P.M)
+                            *reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(P.y) + (nbase + n) * P.y_nb1 + 4LL * (m0 + rr)) =
+                                acc[k];
+                    }
                 }
             }
         }
@@ -987,7 +1150,10 @@ size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
 size_t ximg_bytes(const MulMatOp& o) { return align256(static_cast<size_t>(2) * np_of(o) * o.K * 2); }
 size_t simg_bytes(const MulMatOp& o) { return align256(static_cast<size_t>(o.K / 256) * np_of(o) * 128); }
 size_t vscale_bytes(const MulMatOp& o) { return align256(static_cast<size_t>(o.K / 256) * 2 * np_of(o) * 4); }
-int tiles_of(const MulMatOp& o) { return (o.M + kTM - 1) / kTM * groups_of(o); }
+// Two-plane types (Q8_0, Q6_K) above 32 vectors run both vector groups in one
+// CTA: its two MMA issuers take one group each of every block.
+bool wide_of(const MulMatOp& o) { return (o.type == kTypeQ8_0 || o.type == kTypeQ6_K) && groups_of(o) == 2; }
+int tiles_of(const MulMatOp& o) { return (o.M + kTM - 1) / kTM * (wide_of(o) ? 1 : groups_of(o)); }
 
 // K splits: about one wave of CTAs (one per SM), at least two blocks per split.
 int plan_splits(const MulMatOp& o, int num_sms) {
@@ -1000,7 +1166,7 @@ int plan_splits(const MulMatOp& o, int num_sms) {
 size_t split_bytes(const MulMatOp& o, int splits) {
     if (splits <= 1) return 0;
     const size_t tiles = static_cast<size_t>(tiles_of(o));
-    return align256(tiles * splits * kMaxNV * kTM * 4) + align256(tiles * 4);
+    return align256(tiles * splits * kMaxVPC * kTM * 4) + align256(tiles * 4);
 }
 
 // Bytes per row of one 256-element block in a raw slot, and in the weights.
@@ -1080,20 +1246,24 @@ int launch_batched_tc(const MulMatOp& o, void* workspace, size_t workspace_bytes
     }
     // TMEM: per issuer the accumulators (an epilogue warp reads 16-column
     // groups from its first vector, nv / 2 of them: the columns cover the
-    // overhang; no mins columns for two-plane types), then A_min (8 columns
-    // each, K-quants) and the two A stages from a 32-column boundary
+    // overhang; no mins columns for two-plane types; wide: two per issuer),
+    // then A_min (8 columns each, K-quants) and the two A stages from a
+    // 32-column boundary
+    const bool wide = wide_of(o);
+    P.wide = wide ? 1 : 0;
     {
         const int nh = nv / 2;
         const int need = two ? max(2 * nv, nv + nh + 16) : max(3 * nv, 2 * nv + nh + 16);
         P.accw = (need + 31) / 32 * 32;
-        P.acol0 = (2 * P.accw + (two ? 0 : 16) + 31) / 32 * 32;
+        P.acol0 = ((wide ? 4 : 2) * P.accw + (two ? 0 : 16) + 31) / 32 * 32;
         if (P.acol0 + 2 * kACols > kTmemCols) return -static_cast<int>(cudaErrorInvalidValue);
     }
     // raw slots and B stages within 224 KB: 8 raw slots where 4 B stages still
-    // fit, else 4 raw slots and as many B stages (4 or 2) as fit
+    // fit, else 4 raw slots and as many B stages (4 or 2) as fit (wide, whose
+    // B stages hold both groups: 2 raw slots where 4 leave room for one)
     {
         const auto stages_with = [&](int nraw) {
-            const Smem s0(nv, bb, 0, nraw, !two);
+            const Smem s0(nv, bb, 0, nraw, !two, wide);
             return (static_cast<int>(224u << 10) - static_cast<int>(s0.total())) / static_cast<int>(s0.b_bytes);
         };
         int nb = stages_with(8);
@@ -1101,6 +1271,10 @@ int launch_batched_tc(const MulMatOp& o, void* workspace, size_t workspace_bytes
         if (nb < 4) {
             nb = stages_with(4);
             P.nraw = 4;
+        }
+        if (nb < 2 && wide) {
+            nb = stages_with(2);
+            P.nraw = 2;
         }
         if (nb < 2) return -static_cast<int>(cudaErrorInvalidValue);
         P.nstb = nb >= 4 ? 4 : 2;
@@ -1118,27 +1292,30 @@ int launch_batched_tc(const MulMatOp& o, void* workspace, size_t workspace_bytes
     const int tiles = tiles_of(o);
     if (splits > 1) {
         P.partial = reinterpret_cast<float*>(ws + base);
-        P.counters = reinterpret_cast<unsigned*>(ws + base + align256(static_cast<size_t>(tiles) * splits * kMaxNV * kTM * 4));
+        P.counters = reinterpret_cast<unsigned*>(ws + base + align256(static_cast<size_t>(tiles) * splits * kMaxVPC * kTM * 4));
     }
     btc_prep_kernel<<<dim3(nblk, np / 8), 256, 0, stream>>>(o.x, o.x_nb1, ximg, simg, vscale, o.K, o.N, nv, groups,
                                                             P.counters, splits > 1 ? tiles : 0);
     if ((e = cudaGetLastError()) != cudaSuccess) return -static_cast<int>(e);
-    const size_t smem = Smem(nv, bb, P.nstb, P.nraw, !two).total();
-    static size_t configured[kMaxDevices][4] = {};
+    const size_t smem = Smem(nv, bb, P.nstb, P.nraw, !two, wide).total();
+    static size_t configured[kMaxDevices][6] = {};
     int dev = 0;
     if ((e = cudaGetDevice(&dev)) != cudaSuccess) return -static_cast<int>(e);
     if (dev < 0 || dev >= kMaxDevices) return -static_cast<int>(cudaErrorInvalidDevice);
-    const int ti = o.type == kTypeQ5_K ? 1 : (o.type == kTypeQ8_0 ? 2 : (q6 ? 3 : 0));
-    void (*const kernel)(BtcArgs) =
-        ti == 1 ? btc_kernel<kTypeQ5_K>
-                : (ti == 2 ? btc_kernel<kTypeQ8_0> : (ti == 3 ? btc_kernel<kTypeQ6_K> : btc_kernel<kTypeQ4_K>));
+    const int ti = o.type == kTypeQ5_K ? 1 : (o.type == kTypeQ8_0 ? (wide ? 4 : 2) : (q6 ? (wide ? 5 : 3) : 0));
+    void (*const kernel)(BtcArgs) = ti == 1   ? btc_kernel<kTypeQ5_K, false>
+                                    : ti == 2 ? btc_kernel<kTypeQ8_0, false>
+                                    : ti == 3 ? btc_kernel<kTypeQ6_K, false>
+                                    : ti == 4 ? btc_kernel<kTypeQ8_0, true>
+                                    : ti == 5 ? btc_kernel<kTypeQ6_K, true>
+                                              : btc_kernel<kTypeQ4_K, false>;
     if (configured[dev][ti] < smem) {
         e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
         if (e != cudaSuccess) return -static_cast<int>(e);
         configured[dev][ti] = smem;
     }
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((o.M + kTM - 1) / kTM, groups, splits);
+    cfg.gridDim = dim3((o.M + kTM - 1) / kTM, wide ? 1 : groups, splits);
     cfg.blockDim = dim3(kThr);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
