@@ -12,9 +12,10 @@ rounded to f16, and the remainder) and takes this kernel above 16 vectors
 subnormal range and up to 2^8. Q6_K (rows a multiple of 16 bytes: K a
 multiple of 2048) goes in as two planes of sc (q - 32), which reaches 4096,
 with the Q4_K routing (below 4096 x 4096 only above 16 vectors); a test sets
-its int8 scales to the extremes -128 and 127. Above 32 vectors both two-plane
-types run their two vector groups in one CTA (N = 33, 40, 64 here, with and
-without split K)."""
+its int8 scales to the extremes -128 and 127. IQ4_XS (K a multiple of 512)
+takes the same two planes for (ls - 32) level, up to 4064 in magnitude,
+above 16 vectors. Above 32 vectors the two-plane types run their two vector
+groups in one CTA (N = 33, 40, 64 here, with and without split K)."""
 from __future__ import annotations
 
 import zlib
@@ -68,7 +69,9 @@ def _kernels():
                                        (jsep.GGML_TYPE_Q8_0, 2304, 9216), (jsep.GGML_TYPE_Q8_0, 5000, 4352),
                                        (jsep.GGML_TYPE_Q8_0, 128, 256), (jsep.GGML_TYPE_Q6_K, 4096, 14336),
                                        (jsep.GGML_TYPE_Q6_K, 14336, 4096), (jsep.GGML_TYPE_Q6_K, 1000, 2048),
-                                       (jsep.GGML_TYPE_Q6_K, 5000, 6144)])
+                                       (jsep.GGML_TYPE_Q6_K, 5000, 6144), (jsep.GGML_TYPE_IQ4_XS, 14336, 4096),
+                                       (jsep.GGML_TYPE_IQ4_XS, 4096, 14336), (jsep.GGML_TYPE_IQ4_XS, 1000, 2048),
+                                       (jsep.GGML_TYPE_IQ4_XS, 4200, 4608)])
 def test_batched_tc_both_metrics(runtime, qtype, M, K, N):
     rng = np.random.default_rng(zlib.crc32(repr((qtype, M, K, N)).encode()))
     x = synth.activations(rng, N, K)

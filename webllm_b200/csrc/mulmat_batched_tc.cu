@@ -1,7 +1,7 @@
-// Small-batch quantized MUL_MAT on tcgen05 tensor cores for Q4_K, Q5_K, Q6_K
-// and Q8_0 weights (several sequences decoding together: N up to 64 vectors),
-// exact to about 2^-22 of every activation element, like the integer decode
-// kernels.
+// Small-batch quantized MUL_MAT on tcgen05 tensor cores for Q4_K, Q5_K, Q6_K,
+// Q8_0 and IQ4_XS weights (several sequences decoding together: N up to 64
+// vectors), exact to about 2^-22 of every activation element, like the
+// integer decode kernels.
 //
 //   y[m + M n] = sum_k W[m, k] x[k + K n]   (ggml MUL_MAT, matmul.ts:10-17)
 //
@@ -33,7 +33,8 @@
 // chunk share one half of the A stage. Q6_K (w = d sc (q - 32), int8 sc per
 // 16 elements) takes the same two planes for A = sc (q - 32), which reaches
 // 4096 in magnitude where f16 holds only even integers (lo is 0 or +-1), with
-// d applied per block in the epilogue.
+// d applied per block in the epilogue; IQ4_XS likewise for A = (ls - 32)
+// level (up to 4064).
 //
 // One thread issues a tcgen05.mma in about 50 cycles and waits on an mbarrier
 // in about 150, whatever the MMA's N (16 to 128), so at these sizes the issue
@@ -115,21 +116,27 @@ struct BtcArgs {
 
 // Bytes per row of one 256-element block in a raw slot: Q4_K 144, Q5_K 176,
 // Q8_0 272 (8 blocks), Q6_K 240 (the 210-byte block from its start rounded
-// down to 16: at most 14 + 210 bytes, a 16-byte multiple).
+// down to 16: at most 14 + 210 bytes, a 16-byte multiple), IQ4_XS 144 (the
+// 136-byte block at offset 0 or 8).
 template <int TYPE>
 __host__ __device__ constexpr int blk_bytes() {
     return TYPE == kTypeQ5_K ? 176 : (TYPE == kTypeQ8_0 ? 272 : (TYPE == kTypeQ6_K ? 240 : 144));
 }
-// Q8_0 and Q6_K weights go in as two f16 planes (no mins, no sums box).
+// Q8_0, Q6_K and IQ4_XS weights go in as two f16 planes (no mins, no sums box).
 template <int TYPE>
 __host__ __device__ constexpr bool two_planes() {
-    return TYPE == kTypeQ8_0 || TYPE == kTypeQ6_K;
+    return TYPE == kTypeQ8_0 || TYPE == kTypeQ6_K || TYPE == kTypeIQ4_XS;
 }
-// The weight box's x coordinate for K block kb: Q6_K rows are mapped in bytes
-// (the block's start rounded down to 16), the others in uint64 words.
+// Q6_K and IQ4_XS rows are mapped in bytes: the bytes of one block.
+template <int TYPE>
+__host__ __device__ constexpr int row_blk_bytes() {
+    return TYPE == kTypeQ6_K ? 210 : 136;
+}
+// The weight box's x coordinate for K block kb: byte-mapped rows from the
+// block's start rounded down to 16, the others in uint64 words.
 template <int TYPE>
 __device__ __forceinline__ int raw_box_x(int kb) {
-    if constexpr (TYPE == kTypeQ6_K) return (kb * 210) & ~15;
+    if constexpr (TYPE == kTypeQ6_K || TYPE == kTypeIQ4_XS) return (kb * row_blk_bytes<TYPE>()) & ~15;
     return kb * (blk_bytes<TYPE>() / 8);
 }
 
@@ -443,6 +450,40 @@ __device__ __forceinline__ void q6_chunk_planes(const uint8_t* row, int f, int h
 
 // WIDE (two-plane types above 32 vectors, P.wide set): both vector groups in
 // one CTA, a separate instantiation so the others carry none of its code.
+// Both f16 planes of chunk f of an IQ4_XS block (136 B: f16 d, u16 scales_h,
+// 4 B of 4-bit scales_l, 128 B of level indices), this warp's sub-block
+// j = 2f + h: its 16 index bytes at o + 8 + 16j hold elements 0..15 (low
+// nibbles) and 16..31 (high); w = d (ls_j - 32) level (dequantize_row_iq4_xs).
+// A = (ls_j - 32) level reaches 32 * 127 = 4064, past f16's exact integers,
+// so hi = f16(A) and lo = A - hi; d is applied per block in the epilogue. The
+// level comes from the 16-entry table as f16 1024 + (level + 128), minus 1152.
+// o (0 or 8) is the block's offset in its 144-byte box row, the same for
+// every row.
+__device__ __forceinline__ void iq4_chunk_planes(const uint8_t* row, int f, int h, int o, uint32_t shb, uint32_t slb,
+                                                 uint32_t (&hw)[2][8], uint32_t (&lw)[2][8]) {
+    const int j = 2 * f + h;
+    const uint4 v = o == 0 ? q6_load16<8>(row, 16 * j) : q6_load16<0>(row, 16 + 16 * j);
+    const __half2 s2 = __half2half2(__int2half_rn(iq4xs_scale(shb, slb, j)));
+    const __half2 k1152 = __float2half2_rn(1152.f);
+    const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int qq = 0; qq < 2; ++qq) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const uint32_t u = iq4_lut4((wv[i] >> (4 * qq)) & 0x0F0F0F0Fu) ^ 0x80808080u;  // level + 128
+            const uint32_t e01 = __byte_perm(u, 0x00006464u, 0x5140u), e23 = __byte_perm(u, 0x00006464u, 0x5342u);
+            const __half2 v01 = __hsub2(*reinterpret_cast<const __half2*>(&e01), k1152);
+            const __half2 v23 = __hsub2(*reinterpret_cast<const __half2*>(&e23), k1152);
+            const __half2 h01 = __hmul2(v01, s2), h23 = __hmul2(v23, s2);
+            const __half2 l01 = __hfma2(v01, s2, __hneg2(h01)), l23 = __hfma2(v23, s2, __hneg2(h23));
+            hw[qq][2 * i] = *reinterpret_cast<const uint32_t*>(&h01);
+            hw[qq][2 * i + 1] = *reinterpret_cast<const uint32_t*>(&h23);
+            lw[qq][2 * i] = *reinterpret_cast<const uint32_t*>(&l01);
+            lw[qq][2 * i + 1] = *reinterpret_cast<const uint32_t*>(&l23);
+        }
+    }
+}
+
 template <int TYPE, bool WIDE>
 __global__ void __launch_bounds__(kThr, 1) btc_kernel(const __grid_constant__ BtcArgs P) {
     extern __shared__ __align__(128) uint8_t smem_raw[];
@@ -708,15 +749,23 @@ __global__ void __launch_bounds__(kThr, 1) btc_kernel(const __grid_constant__ Bt
                 const int rs = b & (nraw - 1), i = b & 1;
                 if (!mbar_wait(&raw_full[rs], (b >> lgr) & 1, 3u, poisoned)) break;
                 const uint8_t* row = smem + L.raw_off(rs) + r * BB;
-                // Q6_K: the block starts o = 210 kb mod 16 bytes into its box row
-                const int o = TYPE == kTypeQ6_K ? ((kb0 + b) * 210) & 15 : 0;
+                // Q6_K / IQ4_XS: the block starts o = 210 kb (136 kb) mod 16 bytes
+                // into its box row
+                const int o = (TYPE == kTypeQ6_K || TYPE == kTypeIQ4_XS) ? ((kb0 + b) * row_blk_bytes<TYPE>()) & 15 : 0;
                 uint4 ql[2], qh[2];
+                uint32_t shb = 0u, slb = 0u;  // IQ4_XS: scales_h, scales_l
+                if constexpr (TYPE == kTypeIQ4_XS) {
+                    shb = *reinterpret_cast<const uint16_t*>(row + o + 2);
+                    slb = *reinterpret_cast<const uint32_t*>(row + o + 4);
+                }
                 bool stop = false;
 #pragma unroll
                 for (int f = 0; f < 4; ++f) {
                     uint32_t hw[2][8], lw[2][8];
                     if constexpr (TYPE == kTypeQ6_K)
                         q6_chunk_planes(row, f, h, o, ql, qh, hw, lw);
+                    else if constexpr (TYPE == kTypeIQ4_XS)
+                        iq4_chunk_planes(row, f, h, o, shb, slb, hw, lw);
                     else if (h == 0)
                         q8_chunk_planes<0>(row, f, hw, lw);
                     else
@@ -858,9 +907,10 @@ __global__ void __launch_bounds__(kThr, 1) btc_kernel(const __grid_constant__ Bt
                 const int rs = b & (nraw - 1), ai = 2 * g + (b & 1);
                 if (!mbar_wait<64>(&raw_full[rs], (b >> lgr) & 1, 4u, poisoned)) break;
                 float d = 1.f;
-                if constexpr (TYPE == kTypeQ6_K) {
-                    const int o = ((kb0 + b) * 210) & 15;
-                    d = __half2float(*reinterpret_cast<const __half*>(smem + L.raw_off(rs) + r * BB + o + 208));
+                if constexpr (TYPE == kTypeQ6_K || TYPE == kTypeIQ4_XS) {
+                    const int o = ((kb0 + b) * row_blk_bytes<TYPE>()) & 15;
+                    d = __half2float(*reinterpret_cast<const __half*>(smem + L.raw_off(rs) + r * BB + o +
+                                                                     (TYPE == kTypeQ6_K ? 208 : 0)));
                 }
                 const float* vs = reinterpret_cast<const float*>(smem + L.v_off(rs)) + g * 2 * nv;  // group g's scales
                 if (!mbar_wait<64>(&acc_full[ai], (b >> 1) & 1, 4u, poisoned)) break;
@@ -944,12 +994,14 @@ __global__ void __launch_bounds__(kThr, 1) btc_kernel(const __grid_constant__ Bt
             for (int b = 0; b < nblk; ++b) {
                 const int i = b & 1, rs = b & (nraw - 1);
                 // the block's d, dmin and scales first (they need only the raw slot);
-                // Q8_0's d is inside its weight planes, Q6_K's at byte 208 of the block
+                // Q8_0's d is inside its weight planes, Q6_K's at byte 208 of the
+                // block, IQ4_XS's at byte 0
                 if (!mbar_wait<64>(&raw_full[rs], (b >> lgr) & 1, 4u, poisoned)) break;
                 float d = 1.f, dmin = 0.f;
-                if constexpr (TYPE == kTypeQ6_K) {
-                    const int o = ((kb0 + b) * 210) & 15;
-                    d = __half2float(*reinterpret_cast<const __half*>(smem + L.raw_off(rs) + r * BB + o + 208));
+                if constexpr (TYPE == kTypeQ6_K || TYPE == kTypeIQ4_XS) {
+                    const int o = ((kb0 + b) * row_blk_bytes<TYPE>()) & 15;
+                    d = __half2float(*reinterpret_cast<const __half*>(smem + L.raw_off(rs) + r * BB + o +
+                                                                     (TYPE == kTypeQ6_K ? 208 : 0)));
                 } else if constexpr (!TWO) {
                     const uint32_t dm = *reinterpret_cast<const uint32_t*>(smem + L.raw_off(rs) + r * BB);
                     d = f16_bits_to_f32(dm);
@@ -1150,9 +1202,10 @@ size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
 size_t ximg_bytes(const MulMatOp& o) { return align256(static_cast<size_t>(2) * np_of(o) * o.K * 2); }
 size_t simg_bytes(const MulMatOp& o) { return align256(static_cast<size_t>(o.K / 256) * np_of(o) * 128); }
 size_t vscale_bytes(const MulMatOp& o) { return align256(static_cast<size_t>(o.K / 256) * 2 * np_of(o) * 4); }
-// Two-plane types (Q8_0, Q6_K) above 32 vectors run both vector groups in one
+// Two-plane types (Q8_0, Q6_K, IQ4_XS) above 32 vectors run both vector groups in one
 // CTA: its two MMA issuers take one group each of every block.
-bool wide_of(const MulMatOp& o) { return (o.type == kTypeQ8_0 || o.type == kTypeQ6_K) && groups_of(o) == 2; }
+bool two_of(const MulMatOp& o) { return o.type == kTypeQ8_0 || o.type == kTypeQ6_K || o.type == kTypeIQ4_XS; }
+bool wide_of(const MulMatOp& o) { return two_of(o) && groups_of(o) == 2; }
 int tiles_of(const MulMatOp& o) { return (o.M + kTM - 1) / kTM * (wide_of(o) ? 1 : groups_of(o)); }
 
 // K splits: about one wave of CTAs (one per SM), at least two blocks per split.
@@ -1173,18 +1226,23 @@ size_t split_bytes(const MulMatOp& o, int splits) {
 int host_blk_bytes(int type) {
     return type == kTypeQ5_K ? 176 : (type == kTypeQ8_0 ? 272 : (type == kTypeQ6_K ? 240 : 144));
 }
-int row_blk_bytes(int type) { return type == kTypeQ6_K ? 210 : host_blk_bytes(type); }
+int host_row_blk_bytes(int type) {
+    return type == kTypeQ6_K ? 210 : (type == kTypeIQ4_XS ? 136 : host_blk_bytes(type));
+}
 
 }  // namespace
 
 bool batched_tc_supported(const MulMatOp& o) {
-    if (o.type != kTypeQ4_K && o.type != kTypeQ5_K && o.type != kTypeQ8_0 && o.type != kTypeQ6_K) return false;
+    if (o.type != kTypeQ4_K && o.type != kTypeQ5_K && o.type != kTypeQ8_0 && o.type != kTypeQ6_K &&
+        o.type != kTypeIQ4_XS)
+        return false;
     if (o.N < 1 || o.N > kMaxNP || o.ne2 != 1 || o.ne3 != 1) return false;
     if (o.K % 256 != 0 || o.M < 1) return false;
     // TMA rows: 16-byte aligned base and row stride
     if ((reinterpret_cast<uintptr_t>(o.w) | static_cast<uintptr_t>(o.w_nb1)) & 15) return false;
-    if (o.w_nb1 < static_cast<int64_t>(o.K / 256) * row_blk_bytes(o.type)) return false;
-    if (o.type == kTypeQ6_K && o.K < 512) return false;  // the 240-byte box stays within a row's width
+    if (o.w_nb1 < static_cast<int64_t>(o.K / 256) * host_row_blk_bytes(o.type)) return false;
+    // the 240- or 144-byte box stays within a row's width
+    if ((o.type == kTypeQ6_K || o.type == kTypeIQ4_XS) && o.K < 512) return false;
     if ((reinterpret_cast<uintptr_t>(o.x) | static_cast<uintptr_t>(o.x_nb1)) & 3) return false;
     return btc_encoder() != nullptr;
 }
@@ -1212,15 +1270,17 @@ int launch_batched_tc(const MulMatOp& o, void* workspace, size_t workspace_bytes
     BtcArgs P{};
     const EncodeFn enc = btc_encoder();
     const int bb = host_blk_bytes(o.type);
-    const bool two = o.type == kTypeQ8_0 || o.type == kTypeQ6_K;  // two weight planes, no mins
-    const bool q6 = o.type == kTypeQ6_K;  // rows mapped in bytes, 240-byte boxes
+    const bool two = two_of(o);  // two weight planes, no mins
+    const bool q6 = o.type == kTypeQ6_K, iq4 = o.type == kTypeIQ4_XS;
+    const bool bytemap = q6 || iq4;  // rows mapped in bytes, 240- or 144-byte boxes
     const cuuint32_t es[2] = {1, 1};
     {
-        const cuuint64_t dims[2] = {q6 ? static_cast<cuuint64_t>(nblk) * 210 : static_cast<cuuint64_t>(nblk) * (bb / 8),
+        const cuuint64_t dims[2] = {bytemap ? static_cast<cuuint64_t>(nblk) * host_row_blk_bytes(o.type)
+                                            : static_cast<cuuint64_t>(nblk) * (bb / 8),
                                     static_cast<cuuint64_t>(o.M)};
         const cuuint64_t strides[1] = {static_cast<cuuint64_t>(o.w_nb1)};
-        const cuuint32_t box[2] = {static_cast<cuuint32_t>(q6 ? bb : bb / 8), static_cast<cuuint32_t>(kTM)};
-        if (enc(&P.wmap, q6 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, const_cast<uint8_t*>(o.w),
+        const cuuint32_t box[2] = {static_cast<cuuint32_t>(bytemap ? bb : bb / 8), static_cast<cuuint32_t>(kTM)};
+        if (enc(&P.wmap, bytemap ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, const_cast<uint8_t*>(o.w),
                 dims, strides, box, es,
                 CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
@@ -1298,16 +1358,22 @@ int launch_batched_tc(const MulMatOp& o, void* workspace, size_t workspace_bytes
                                                             P.counters, splits > 1 ? tiles : 0);
     if ((e = cudaGetLastError()) != cudaSuccess) return -static_cast<int>(e);
     const size_t smem = Smem(nv, bb, P.nstb, P.nraw, !two, wide).total();
-    static size_t configured[kMaxDevices][6] = {};
+    static size_t configured[kMaxDevices][8] = {};
     int dev = 0;
     if ((e = cudaGetDevice(&dev)) != cudaSuccess) return -static_cast<int>(e);
     if (dev < 0 || dev >= kMaxDevices) return -static_cast<int>(cudaErrorInvalidDevice);
-    const int ti = o.type == kTypeQ5_K ? 1 : (o.type == kTypeQ8_0 ? (wide ? 4 : 2) : (q6 ? (wide ? 5 : 3) : 0));
+    const int ti = o.type == kTypeQ5_K   ? 1
+                   : o.type == kTypeQ8_0 ? (wide ? 4 : 2)
+                   : q6                  ? (wide ? 5 : 3)
+                   : iq4                 ? (wide ? 7 : 6)
+                                         : 0;
     void (*const kernel)(BtcArgs) = ti == 1   ? btc_kernel<kTypeQ5_K, false>
                                     : ti == 2 ? btc_kernel<kTypeQ8_0, false>
                                     : ti == 3 ? btc_kernel<kTypeQ6_K, false>
                                     : ti == 4 ? btc_kernel<kTypeQ8_0, true>
                                     : ti == 5 ? btc_kernel<kTypeQ6_K, true>
+                                    : ti == 6 ? btc_kernel<kTypeIQ4_XS, false>
+                                    : ti == 7 ? btc_kernel<kTypeIQ4_XS, true>
                                               : btc_kernel<kTypeQ4_K, false>;
     if (configured[dev][ti] < smem) {
         e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));

@@ -370,15 +370,18 @@ const char* check_mulmat_op(const MulMatOp& op) {
 }
 
 // Q4_K / Q5_K / Q6_K with 5 to 64 vectors (and 3 or 4 where the streaming
-// kernel cannot take them) and Q8_0 above 16 vectors run on the tcgen05
+// kernel cannot take them), Q8_0 and IQ4_XS above 16 vectors run on the tcgen05
 // small-batch GEMM, except small weights (at most 4096 x 4096) below 16
 // vectors, where the mma.sync GEMM's shorter fixed costs win (13.5 against
 // 15.1 us for Q4_K 4096 x 4096 at N = 8).
 bool use_batched_tc(const MulMatOp& o) {
     if (!batched_tc_supported(o) || o.N < 3) return false;
-    // Q8_0's two weight planes cost the tcgen05 GEMM twice a Q4_K dequantization:
-    // the integer mma.sync GEMM, which needs none, is faster up to 16 vectors
-    if (o.type == kTypeQ8_0) return o.N > 16 || (!batched_supported(o) && (o.N >= 5 || !stream_supported(&o, 1)));
+    // Q8_0's and IQ4_XS's two weight planes (and IQ4_XS's level table) cost the
+    // tcgen05 GEMM two to three times a Q4_K dequantization: the integer mma.sync
+    // GEMM, which needs none, is faster up to 16 vectors (IQ4_XS 14336 x 4096 at
+    // N = 8: 32.9 against 43.6 us; at N = 32: 54.6 against 47.2)
+    if (o.type == kTypeQ8_0 || o.type == kTypeIQ4_XS)
+        return o.N > 16 || (!batched_supported(o) && (o.N >= 5 || !stream_supported(&o, 1)));
     // Q6_K (also two planes) below 4096 x 4096 keeps the mma.sync GEMM through 16
     // vectors (1024 x 4096 at N = 16: 12.9 against 16.3 us)
     if (o.type == kTypeQ6_K && o.N <= 16 && static_cast<int64_t>(o.M) * o.K < 4096LL * 4096 && batched_supported(o))
