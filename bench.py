@@ -325,12 +325,12 @@ class DevArray:
 
 
 def batched_measure(dev, reps: int = 10, warmup: int = 3):
-    """Several sequences decoding together (N = 1 .. 64) on three weights:
+    """Several sequences decoding together (N = 1 .. 64) on four weights:
     Gemma-2-2B ffn_up (Q8_0 9216x2304), Llama-3-8B ffn_gate (Q4_K 14336x4096)
-    and ffn_down (Q6_K 4096x14336). N = 1, 2 run the streaming GEMV; the
-    K-quant shapes at N >= 8 and the Q8_0 shape above 16 vectors the tcgen05
-    small-batch GEMM, the Q8_0 shape at N = 8, 16 the integer tensor-core
-    (mma.sync) batched GEMM. Distinct weight copies (over 2x the
+    and ffn_down (Q6_K 4096x14336), and ffn_gate as IQ4_XS. N = 1, 2 run the
+    streaming GEMV; the K-quant shapes at N >= 8 and the Q8_0 and IQ4_XS shapes
+    above 16 vectors the tcgen05 small-batch GEMM, those two at N = 8, 16 the
+    integer tensor-core (mma.sync) batched GEMM. Distinct weight copies (over 2x the
     L2) rotate between launches so every launch streams its weights from HBM.
     Returns the JSON object: the Q8_0 shape at the top level, the K-quant
     shapes under "kquant"."""
@@ -341,7 +341,8 @@ def batched_measure(dev, reps: int = 10, warmup: int = 3):
     gname, gt, gM, gK = synth.GEMMA2_2B_SHAPES[0]
     shapes = [(f"gemma-2-2b {gname}", gt, gM, gK, 24),
               ("llama-3-8b ffn_gate", jsep.GGML_TYPE_Q4_K, 14336, 4096, 8),
-              ("llama-3-8b ffn_down", jsep.GGML_TYPE_Q6_K, 4096, 14336, 6)]
+              ("llama-3-8b ffn_down", jsep.GGML_TYPE_Q6_K, 4096, 14336, 6),
+              ("llama-3-8b ffn_gate", jsep.GGML_TYPE_IQ4_XS, 14336, 4096, 8)]
     stream_ptr = jsep.library_stream()
     hbm, _ = measured_peaks()
     out = []
@@ -384,13 +385,14 @@ def batched_measure(dev, reps: int = 10, warmup: int = 3):
                         "hbm_frac": round(nbytes / (us * 1e-6) / 1e9 / hbm, 4),
                         "tflops": round(2.0 * M * K * N / (us * 1e-6) / 1e12, 2)})
         del ws
-        tname = {jsep.GGML_TYPE_Q8_0: "Q8_0", jsep.GGML_TYPE_Q4_K: "Q4_K", jsep.GGML_TYPE_Q6_K: "Q6_K"}[t]
+        tname = {jsep.GGML_TYPE_Q8_0: "Q8_0", jsep.GGML_TYPE_Q4_K: "Q4_K", jsep.GGML_TYPE_Q6_K: "Q6_K",
+                 jsep.GGML_TYPE_IQ4_XS: "IQ4_XS"}[t]
         out.append({"workload": f"{name} {tname} {M}x{K}, N sequences decoding together", "unit": "GB/s",
                     "per_n": per})
     res = dict(out[0])
     res["kquant"] = out[1:]
-    res["note"] = ("N <= 2: streaming GEMV; Q4_K/Q6_K N >= 5 (N >= 16 at 4096x4096 and below) and Q8_0 N > 16: "
-                   "tcgen05 small-batch GEMM; Q8_0 N = 3..16: integer tensor-core batched GEMM (mma.sync); "
+    res["note"] = ("N <= 2: streaming GEMV; Q4_K/Q6_K N >= 5 (N >= 16 at 4096x4096 and below), Q8_0/IQ4_XS N > 16: "
+                   "tcgen05 small-batch GEMM; Q8_0/IQ4_XS N = 3..16: integer tensor-core batched GEMM (mma.sync); "
                    "activation pre-passes included; launches timed inside a CUDA graph")
     return res
 
