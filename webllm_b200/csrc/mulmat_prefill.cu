@@ -741,23 +741,37 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
 
 // f32 activations [N][K] (vector stride x_nb1 bytes) -> contiguous f16 [N][K].
 // Vectors blockIdx.y, blockIdx.y + gridDim.y, ..., elements 4 (blockIdx.x
-// blockDim.x + t) .. +3 (and their grid-stride successors). CTA (0, 0) also zeroes the split-K tile counters.
-// The GEMM that follows may start at once: its prologue and first weight
-// boxes overlap this kernel, and it waits for the f16 image with
-// griddepcontrol.wait.
+// blockDim.x + t) .. +3 (and their grid-stride successors); a thread loads
+// eight vectors' float4s before it converts and stores them, so enough loads
+// are in flight to stream at the HBM rate (one at a time it ran at about half
+// of it). CTA (0, 0) also zeroes the split-K tile counters. The GEMM that
+// follows may start at once: its prologue and first weight boxes overlap this
+// kernel, and it waits for the f16 image with griddepcontrol.wait.
 __global__ void x_to_f16_kernel(const float* __restrict__ x, int64_t x_nb1, __half* __restrict__ x16, int K, int N,
                                 unsigned* __restrict__ counters, int ncounters) {
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     if (blockIdx.x == 0 && blockIdx.y == 0)
         for (int t = threadIdx.x; t < ncounters; t += blockDim.x) counters[t] = 0u;
+    constexpr int kRows = 8;
     const int k4n = K / 4;
-    for (int n = blockIdx.y; n < N; n += gridDim.y) {
-        const float4* xr = reinterpret_cast<const float4*>(reinterpret_cast<const uint8_t*>(x) + n * x_nb1);
-        __half2* orow = reinterpret_cast<__half2*>(x16 + static_cast<int64_t>(n) * K);
-        for (int k4 = blockIdx.x * blockDim.x + threadIdx.x; k4 < k4n; k4 += gridDim.x * blockDim.x) {
-            const float4 v = xr[k4];
-            orow[2 * k4] = __floats2half2_rn(v.x, v.y);
-            orow[2 * k4 + 1] = __floats2half2_rn(v.z, v.w);
+    for (int k4 = blockIdx.x * blockDim.x + threadIdx.x; k4 < k4n; k4 += gridDim.x * blockDim.x) {
+        for (int n0 = blockIdx.y; n0 < N; n0 += kRows * gridDim.y) {
+            float4 v[kRows];
+#pragma unroll
+            for (int i = 0; i < kRows; ++i) {
+                const int n = n0 + i * gridDim.y;
+                if (n < N)
+                    v[i] = reinterpret_cast<const float4*>(reinterpret_cast<const uint8_t*>(x) + n * x_nb1)[k4];
+            }
+#pragma unroll
+            for (int i = 0; i < kRows; ++i) {
+                const int n = n0 + i * gridDim.y;
+                if (n < N) {
+                    __half2* orow = reinterpret_cast<__half2*>(x16 + static_cast<int64_t>(n) * K);
+                    orow[2 * k4] = __floats2half2_rn(v[i].x, v[i].y);
+                    orow[2 * k4 + 1] = __floats2half2_rn(v[i].z, v[i].w);
+                }
+            }
         }
     }
 }
