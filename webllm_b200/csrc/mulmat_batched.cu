@@ -566,8 +566,9 @@ __global__ void __launch_bounds__(kThreadsB, 2) batched_kernel(const __grid_cons
             for (int j = 0; j < 8; ++j) {
                 const uint32_t wg = *reinterpret_cast<const uint32_t*>(pg + 8 + 16 * j + 4 * c);
                 const uint32_t wh = *reinterpret_cast<const uint32_t*>(ph + 8 + 16 * j + 4 * c);
-                const uint32_t A0 = iq4_lut4(wg & 0x0F0F0F0Fu), A1 = iq4_lut4(wh & 0x0F0F0F0Fu);
-                const uint32_t A2 = iq4_lut4((wg >> 4) & 0x0F0F0F0Fu), A3 = iq4_lut4((wh >> 4) & 0x0F0F0F0Fu);
+                uint32_t A0, A1, A2, A3;  // levels: rows g / g+8, low / high nibbles
+                iq4_lut8(wg, A0, A2);
+                iq4_lut8(wh, A1, A3);
                 const float scj = static_cast<float>(iq4xs_scale(shg, slg, j));
                 const float shj = static_cast<float>(iq4xs_scale(shh, slh, j));
 #pragma unroll

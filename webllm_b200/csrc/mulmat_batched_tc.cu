@@ -466,11 +466,14 @@ __device__ __forceinline__ void iq4_chunk_planes(const uint8_t* row, int f, int 
     const __half2 s2 = __half2half2(__int2half_rn(iq4xs_scale(shb, slb, j)));
     const __half2 k1152 = __float2half2_rn(1152.f);
     const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
+    uint32_t lv[2][4];  // levels of the low (qq = 0) and high nibbles
+#pragma unroll
+    for (int i = 0; i < 4; ++i) iq4_lut8(wv[i], lv[0][i], lv[1][i]);
 #pragma unroll
     for (int qq = 0; qq < 2; ++qq) {
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-            const uint32_t u = iq4_lut4((wv[i] >> (4 * qq)) & 0x0F0F0F0Fu) ^ 0x80808080u;  // level + 128
+            const uint32_t u = lv[qq][i] ^ 0x80808080u;  // level + 128
             const uint32_t e01 = __byte_perm(u, 0x00006464u, 0x5140u), e23 = __byte_perm(u, 0x00006464u, 0x5342u);
             const __half2 v01 = __hsub2(*reinterpret_cast<const __half2*>(&e01), k1152);
             const __half2 v23 = __hsub2(*reinterpret_cast<const __half2*>(&e23), k1152);

@@ -694,8 +694,10 @@ __device__ __forceinline__ void iq4xs_item(const uint8_t* pg, const uint8_t* ph,
         for (int h = 0; h < 2; ++h) {
             const int j = 2 * p + h;
             const uint32_t wg = lds_u32_any(pg + 8 + 16 * j + 4 * c), wh = lds_u32_any(ph + 8 + 16 * j + 4 * c);
-            imma_s8s8_acc(D[j / NS], iq4_lut4(wg & 0x0F0F0F0Fu), iq4_lut4(wh & 0x0F0F0F0Fu),
-                          iq4_lut4((wg >> 4) & 0x0F0F0F0Fu), iq4_lut4((wh >> 4) & 0x0F0F0F0Fu), x[2 * h],
+            uint32_t gl, gh, hl, hh;  // levels: rows g / g+8, low / high nibbles
+            iq4_lut8(wg, gl, gh);
+            iq4_lut8(wh, hl, hh);
+            imma_s8s8_acc(D[j / NS], gl, hl, gh, hh, x[2 * h],
                           x[2 * h + 1]);
         }
     }
