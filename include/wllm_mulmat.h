@@ -270,9 +270,10 @@ int32_t wllm_graph_launch(int32_t graph);
 int32_t wllm_graph_destroy(int32_t graph);
 
 /* Prefill MUL_MAT that allocates nothing: the same arguments and result as
- * wllm_mul_mat for the prefill path (Q4_K, Q5_K, Q8_0 or Q4_0 weights, IQ4_XS with
- * K a multiple of 512, or Q6_K with rows of a multiple of 16 bytes, or of 8 with M
- * even; N >= 65 vectors, 16-byte
+ * wllm_mul_mat for the prefill path (Q4_K, Q5_K, Q8_0 or Q4_0 weights; Q6_K or
+ * IQ4_XS with rows of a multiple of 16 bytes, or of an even number of bytes with
+ * M a multiple of the 2, 4 or 8 rows that make a multiple of 16 (IQ4_XS: pairs
+ * only); N >= 65 vectors, 16-byte
  * aligned weights and activations), with the f16 activation workspace
  * in a fixed 16 MiB device array of the library instead of library-allocated
  * memory: N * K * 2 + 256 bytes must fit, otherwise WLLM_STATUS_FAILED with

@@ -806,7 +806,8 @@ int32_t wllm_mul_mat_prefill_static(int32_t src0_type, const void* w, int64_t w_
     if (const char* why = wllm::check_mulmat_op(m)) return fail(s, "wllm_mul_mat_prefill_static: %s", why);
     if (!wllm::prefill_supported(m))
         return fail(s,
-                    "wllm_mul_mat_prefill_static: only the prefill path (Q4_K, Q5_K, Q8_0, Q4_0, IQ4_XS, or Q6_K with 16-byte or, at even M, 8-byte multiple rows; "
+                    "wllm_mul_mat_prefill_static: only the prefill path (Q4_K, Q5_K, Q8_0, Q4_0; Q6_K / IQ4_XS rows of a 16-byte "
+                    "multiple, or of an even number of bytes with M a multiple of the 2, 4 or 8 rows that make one; "
                     "N >= %d, 16-byte aligned rows and activations) is available here",
                     wllm::kPrefillMinN);
     const size_t need = wllm::prefill_min_workspace_bytes(m);
